@@ -1,0 +1,141 @@
+/*
+ * lucid_b200 — C ABI of the B200 (sm_100a) LUCID attention kernels.
+ *
+ * LUCID attention computes  O = softmax(s Q K^T + causal) X,  X = P^-1 V,
+ * P = tril(exp(s K^ K^T - 1/s)),  K^ = RMSNorm(K) (no affine),  s = D^-1/2.
+ *
+ * Conventions shared by every entry point
+ *   - All tensors are device pointers to bf16 unless stated otherwise.
+ *   - "Strided" tensors are 4-D [B, H, N, D] views given by element strides
+ *     (sb, sh, sn); the innermost (D) stride is 1.  Strides and base
+ *     addresses must be multiples of 8 elements (16 bytes).
+ *   - "Internal" tensors are contiguous [B, H, Npad, D] (or [B, H, Npad])
+ *     buffers with Npad = lucid_padded_len(N); the library owns their
+ *     contents, the caller owns their memory.
+ *   - D must be 128 (the tensor-core head dimension of this build).
+ *   - Hq must be a multiple of Hkv (grouped-query attention).
+ *   - Every call is asynchronous on `stream` (a cudaStream_t, 0 = legacy
+ *     default stream), performs no host synchronisation and allocates no
+ *     memory.  Scratch memory comes from the caller's `workspace`, whose
+ *     size is given by the matching *_workspace_bytes function.
+ *   - Return value: LUCID_OK, or one of the error codes below; nothing is
+ *     launched when an error is returned.
+ *   - The kernels record run-time failures (a bounded wait that timed out)
+ *     in a status word inside the workspace; lucid_workspace_status_offset
+ *     gives its byte offset for callers that want to read it back.
+ */
+#ifndef LUCID_B200_H_
+#define LUCID_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LUCID_OK 0
+#define LUCID_ERR_SHAPE 1       /* unsupported B/H/N/D combination */
+#define LUCID_ERR_ALIGN 2       /* pointer or stride not 16-byte aligned */
+#define LUCID_ERR_WORKSPACE 3   /* workspace missing or too small */
+#define LUCID_ERR_TENSORMAP 4   /* TMA descriptor creation failed */
+#define LUCID_ERR_LAUNCH 5      /* CUDA launch error */
+
+/* Library version, e.g. 100 for 0.1.0. */
+int lucid_version(void);
+
+/* Rows of the internal buffers: N rounded up to a multiple of 128. */
+int lucid_padded_len(int N);
+
+/* Byte offset of the int32 run-time status word inside every workspace. */
+size_t lucid_workspace_status_offset(void);
+
+/*
+ * Solve forward: X = P^-1 V.
+ * Replaces LucidAttention.get_v_prime (modeling_lucid.py:551-574: dense
+ * branch, k_norm + einsum + exp + torch.linalg.solve_triangular) and the
+ * blockwise Lucid_Tril_Solver.forward (modeling_lucid.py:285-312).
+ * In : k, v strided [B,H,N,D]; scale = s; eps = RMSNorm epsilon.
+ * Out: x    internal bf16 [B,H,Npad,D]   solved values
+ *      khat internal bf16 [B,H,Npad,D]   RMS-normalised keys   (saved)
+ *      u    bf16 [B,H,Npad/128,128,128]  diagonal-block inverses (saved)
+ *      rstd, dinv internal fp32 [B,H,Npad]                         (saved)
+ */
+size_t lucid_solve_fwd_workspace_bytes(int B, int H, int N, int D);
+int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps,
+                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                    const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                    void* x, void* khat, void* u, float* rstd, float* dinv,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Attention forward: O = softmax(scale Q K^T + causal) X.
+ * Replaces LucidAttention.eager_lucid_attention_forward
+ * (modeling_lucid.py:505-549; SDPA with repeat_kv, is_causal=True).
+ * In : q strided [B,Hq,N,D]; k strided [B,Hkv,N,D] (raw keys);
+ *      x internal bf16 [B,Hkv,Npad,D].
+ * Out: o strided [B,Hq,N,D] (pass the strides of the caller's output, e.g.
+ *      the [B,N,Hq,D] layout the reference returns); lse internal fp32
+ *      [B,Hq,Npad] (log2 domain, saved for the backward).
+ */
+size_t lucid_attn_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
+int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
+                   const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                   const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                   const void* x,
+                   void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                   float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Attention backward (autograd of eager_lucid_attention_forward).
+ * In : q, k, o, dout strided; x internal; lse from lucid_attn_fwd.
+ * Out: dq strided bf16 [B,Hq,N,D];
+ *      dk_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dK through Q K^T)
+ *      dx_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dX)
+ */
+size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
+int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale,
+                   const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                   const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                   const void* x,
+                   const void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                   const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn,
+                   const float* lse,
+                   void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn,
+                   float* dk_f32, float* dx_f32,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Solve backward: dV = P^-T dX and dK through P and RMSNorm.
+ * Replaces Lucid_Tril_Solver.backward (modeling_lucid.py:314-382) and the
+ * autograd of the dense branch (modeling_lucid.py:566-570).
+ * In : k strided (raw keys); x, khat, u, rstd, dinv from lucid_solve_fwd;
+ *      dx_f32 internal fp32 [B,H,Npad,D]; dk_add optional internal fp32
+ *      [B,H,Npad,D] added to dK (e.g. dk_f32 of lucid_attn_bwd), may be NULL.
+ * Out: dk, dv strided bf16 [B,H,N,D].
+ */
+size_t lucid_solve_bwd_workspace_bytes(int B, int H, int N, int D);
+int lucid_solve_bwd(int B, int H, int N, int D, float scale,
+                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                    const void* x, const void* khat, const void* u,
+                    const float* rstd, const float* dinv,
+                    const float* dx_f32, const float* dk_add,
+                    void* dk, int64_t dk_sb, int64_t dk_sh, int64_t dk_sn,
+                    void* dv, int64_t dv_sb, int64_t dv_sh, int64_t dv_sn,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Tensor-core self test: D = op(A) op(B) for one 128x128x128 bf16 tile,
+ * A and B row-major [128][128] bf16, D row-major fp32.  a_mn / b_mn select
+ * the operand majorness (0: A is used as is / B^T; 1: A^T / B), i.e.
+ *   (0,0) D = A B^T   (0,1) D = A B   (1,0) D = A^T B^T   (1,1) D = A^T B.
+ * `via_tma` loads the operands with TMA instead of thread stores.
+ */
+int lucid_selftest_umma(const void* a, const void* b, float* d, int a_mn, int b_mn,
+                        int via_tma, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUCID_B200_H_ */

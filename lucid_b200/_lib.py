@@ -1,0 +1,81 @@
+"""ctypes binding of liblucid_b200.so (the C ABI in include/lucid_b200.h).
+
+The shared library is built in-tree by ``python -m lucid_b200.build``.  There
+is no fallback: if the library is missing or fails to load, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblucid_b200.so")
+
+LUCID_OK = 0
+ERRORS = {
+    1: "unsupported shape (head_dim must be 128, Hq a multiple of Hkv)",
+    2: "pointer or stride not 16-byte aligned",
+    3: "workspace missing or too small",
+    4: "TMA descriptor creation failed",
+    5: "CUDA launch error",
+}
+
+c_int, c_float, c_size_t, c_void_p, c_int64 = (
+    ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64)
+c_float_p = ctypes.POINTER(ctypes.c_float)
+
+S3 = [c_int64] * 3  # (sb, sh, sn) element strides
+
+# name -> (restype, argtypes); every symbol declared in include/lucid_b200.h
+SIGNATURES = {
+    "lucid_version": (c_int, []),
+    "lucid_padded_len": (c_int, [c_int]),
+    "lucid_workspace_status_offset": (c_size_t, []),
+    "lucid_solve_fwd_workspace_bytes": (c_size_t, [c_int] * 4),
+    "lucid_solve_fwd": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3
+                        + [c_void_p] * 5 + [c_void_p, c_size_t, c_void_p]),
+    "lucid_attn_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_attn_fwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
+                       + [c_void_p] + S3 + [c_void_p] + [c_void_p, c_size_t, c_void_p]),
+    "lucid_attn_bwd_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_attn_bwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
+                       + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p] + [c_void_p] + S3
+                       + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),
+    "lucid_solve_bwd_workspace_bytes": (c_size_t, [c_int] * 4),
+    "lucid_solve_bwd": (c_int, [c_int] * 4 + [c_float] + [c_void_p] + S3 + [c_void_p] * 5
+                        + [c_void_p, c_void_p] + [c_void_p] + S3 + [c_void_p] + S3
+                        + [c_void_p, c_size_t, c_void_p]),
+    "lucid_selftest_umma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class LucidError(RuntimeError):
+    pass
+
+
+def load(path: str | None = None):
+    """Load (once) and return the ctypes handle of liblucid_b200.so."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise LucidError(
+                f"{p} not found: build it with `python -m lucid_b200.build` (no CPU fallback exists)")
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != LUCID_OK:
+        raise LucidError(f"{what} failed: {ERRORS.get(rc, rc)}")

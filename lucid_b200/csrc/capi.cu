@@ -1,0 +1,372 @@
+// extern "C" entry points of liblucid_b200.so (declared in
+// include/lucid_b200.h): argument checks, workspace carving, TMA descriptor
+// creation and the launch sequence of each stage.
+#include "../../include/lucid_b200.h"
+#include "lucid_common.cuh"
+#include "tmap.h"
+
+namespace lb {
+cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
+cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
+                       const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
+cudaError_t launch_bwd(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2,
+                       const CUtensorMap& tB1, const CUtensorMap& tB2, const CUtensorMap& tU,
+                       const BwdArgs& a, cudaStream_t st);
+cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
+                         long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
+                         long long d_sn, float* delta, cudaStream_t st);
+cudaError_t launch_f32_to_bf16(int B, int H, int N, int Npad, float scale, const float* src, bf16* dst,
+                               long long sb, long long sh, long long sn, cudaStream_t st);
+cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const bf16* k, long long k_sb,
+                                  long long k_sh, long long k_sn, const float* rstd, const float* dinv,
+                                  const bf16* x, const bf16* dv_int, const float* dk_col,
+                                  const float* dk_row, const float* dk_add, bf16* dk, long long dk_sb,
+                                  long long dk_sh, long long dk_sn, bf16* dv, long long dv_sb,
+                                  long long dv_sh, long long dv_sn, cudaStream_t st);
+}  // namespace lb
+
+using namespace lb;
+
+namespace {
+
+constexpr size_t kStatusRegion = 256;
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+int npad_of(int N) { return ((N + 127) / 128) * 128; }
+int nb_of(int N) { return (N + 127) / 128; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool strides_ok(int64_t a, int64_t b, int64_t c) { return (a % 8 == 0) && (b % 8 == 0) && (c % 8 == 0); }
+
+bool shape_ok(int B, int Hq, int Hkv, int N, int D) {
+  return B >= 0 && Hq >= 0 && Hkv >= 0 && N >= 0 && D == kHeadDim &&
+         (Hkv == 0 || Hq % Hkv == 0) && (Hkv > 0 || Hq == 0) && N <= (1 << 30);
+}
+bool empty_problem(int B, int Hq, int Hkv, int N) { return B == 0 || Hq == 0 || Hkv == 0 || N == 0; }
+
+int to_status(cudaError_t e) { return e == cudaSuccess ? LUCID_OK : LUCID_ERR_LAUNCH; }
+
+// Internal contiguous [B][H][Npad][128] bf16 tensor map.
+bool tmap_internal(CUtensorMap* m, const void* p, int B, int H, int Npad) {
+  return make_tmap_bf16(m, p, kHeadDim, Npad, H, B, kHeadDim, (long long)Npad * kHeadDim,
+                        (long long)H * Npad * kHeadDim);
+}
+// Caller's strided [B][H][N][128] bf16 tensor map.
+bool tmap_strided(CUtensorMap* m, const void* p, int B, int H, int N, int64_t sb, int64_t sh, int64_t sn) {
+  return make_tmap_bf16(m, p, kHeadDim, N, H, B, sn, sh, sb);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lucid_version(void) { return 100; }
+int lucid_padded_len(int N) { return npad_of(N); }
+size_t lucid_workspace_status_offset(void) { return 0; }
+
+// ---------------------------------------------------------------------------
+// solve forward
+// ---------------------------------------------------------------------------
+size_t lucid_solve_fwd_workspace_bytes(int B, int H, int N, int D) {
+  (void)D;
+  return kStatusRegion + align256((size_t)B * H * nb_of(N) * sizeof(int));
+}
+
+int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const void* k, int64_t k_sb,
+                    int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                    void* x, void* khat, void* u, float* rstd, float* dinv, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  if (!aligned16(k) || !aligned16(v) || !aligned16(x) || !aligned16(khat) || !aligned16(u) ||
+      !aligned16(rstd) || !aligned16(dinv) || !strides_ok(k_sb, k_sh, k_sn) ||
+      !strides_ok(v_sb, v_sh, v_sn))
+    return LUCID_ERR_ALIGN;
+  if (!workspace || workspace_bytes < lucid_solve_fwd_workspace_bytes(B, H, N, D))
+    return LUCID_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int NB = nb_of(N), Npad = npad_of(N);
+  int* status = reinterpret_cast<int*>(workspace);
+  int* flags = reinterpret_cast<int*>(static_cast<char*>(workspace) + kStatusRegion);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, lucid_solve_fwd_workspace_bytes(B, H, N, D), st);
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+
+  PrepArgs pa{};
+  pa.B = B; pa.H = H; pa.N = N; pa.NB = NB; pa.Npad = Npad;
+  pa.s = scale; pa.eps = eps;
+  pa.k = static_cast<const bf16*>(k); pa.k_sb = k_sb; pa.k_sh = k_sh; pa.k_sn = k_sn;
+  pa.khat = static_cast<bf16*>(khat); pa.rstd = rstd; pa.dinv = dinv; pa.u = static_cast<bf16*>(u);
+  e = launch_prep(pa, st);
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+
+  CUtensorMap tK, tX, tU;
+  if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
+      !tmap_internal(&tU, u, B, H, Npad))
+    return LUCID_ERR_TENSORMAP;
+  FwdArgs fa{};
+  fa.B = B; fa.Hq = H; fa.Hkv = H; fa.N = N; fa.NB = NB; fa.Npad = Npad;
+  fa.scale = scale;
+  fa.dinv = dinv;
+  fa.v = static_cast<const bf16*>(v); fa.v_sb = v_sb; fa.v_sh = v_sh; fa.v_sn = v_sn;
+  fa.x = static_cast<bf16*>(x);
+  fa.flags = flags;
+  fa.status = status;
+  return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
+}
+
+// ---------------------------------------------------------------------------
+// attention forward
+// ---------------------------------------------------------------------------
+size_t lucid_attn_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
+  (void)B; (void)Hq; (void)Hkv; (void)N; (void)D;
+  return kStatusRegion;
+}
+
+int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
+                   int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                   const void* x, void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, Hq, Hkv, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(o) || !aligned16(lse) ||
+      !strides_ok(q_sb, q_sh, q_sn) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn))
+    return LUCID_ERR_ALIGN;
+  if (!workspace || workspace_bytes < lucid_attn_fwd_workspace_bytes(B, Hq, Hkv, N, D))
+    return LUCID_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int NB = nb_of(N), Npad = npad_of(N);
+  int* status = reinterpret_cast<int*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, kStatusRegion, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  CUtensorMap tQ, tK, tX;
+  if (!tmap_strided(&tQ, q, B, Hq, N, q_sb, q_sh, q_sn) || !tmap_strided(&tK, k, B, Hkv, N, k_sb, k_sh, k_sn) ||
+      !tmap_internal(&tX, x, B, Hkv, Npad))
+    return LUCID_ERR_TENSORMAP;
+  FwdArgs fa{};
+  fa.B = B; fa.Hq = Hq; fa.Hkv = Hkv; fa.N = N; fa.NB = NB; fa.Npad = Npad;
+  fa.scale = scale;
+  fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
+  fa.lse = lse;
+  fa.status = status;
+  return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
+}
+
+// ---------------------------------------------------------------------------
+// attention backward
+// ---------------------------------------------------------------------------
+size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
+  (void)Hkv; (void)D;
+  const size_t rows = (size_t)B * Hq * npad_of(N);
+  return kStatusRegion + align256(rows * sizeof(float)) + align256(rows * kHeadDim * sizeof(float));
+}
+
+int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
+                   int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                   const void* x, const void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                   const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, const float* lse,
+                   void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn, float* dk_f32, float* dx_f32,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, Hq, Hkv, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(o) || !aligned16(dout) ||
+      !aligned16(lse) || !aligned16(dq) || !aligned16(dk_f32) || !aligned16(dx_f32) ||
+      !strides_ok(q_sb, q_sh, q_sn) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn) ||
+      !strides_ok(do_sb, do_sh, do_sn) || !strides_ok(dq_sb, dq_sh, dq_sn))
+    return LUCID_ERR_ALIGN;
+  if (!workspace || workspace_bytes < lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D))
+    return LUCID_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int NB = nb_of(N), Npad = npad_of(N);
+  const size_t rows = (size_t)B * Hq * Npad;
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  float* delta = reinterpret_cast<float*>(ws + kStatusRegion);
+  float* dq_acc = reinterpret_cast<float*>(ws + kStatusRegion + align256(rows * sizeof(float)));
+  if (cudaMemsetAsync(ws, 0, kStatusRegion, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  if (cudaMemsetAsync(dq_acc, 0, rows * kHeadDim * sizeof(float), st) != cudaSuccess)
+    return LUCID_ERR_LAUNCH;
+  cudaError_t e = launch_delta(B, Hq, N, Npad, static_cast<const bf16*>(o), o_sb, o_sh, o_sn,
+                               static_cast<const bf16*>(dout), do_sb, do_sh, do_sn, delta, st);
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+  CUtensorMap tK, tX, tQ, tDO;
+  if (!tmap_strided(&tK, k, B, Hkv, N, k_sb, k_sh, k_sn) || !tmap_internal(&tX, x, B, Hkv, Npad) ||
+      !tmap_strided(&tQ, q, B, Hq, N, q_sb, q_sh, q_sn) ||
+      !tmap_strided(&tDO, dout, B, Hq, N, do_sb, do_sh, do_sn))
+    return LUCID_ERR_TENSORMAP;
+  BwdArgs ba{};
+  ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
+  ba.scale = scale;
+  ba.lse = lse; ba.delta = delta;
+  ba.dx = dx_f32; ba.dk_col = dk_f32; ba.d_row = dq_acc;
+  ba.status = status;
+  e = launch_bwd(false, tK, tX, tQ, tDO, tX, ba, st);
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+  return to_status(launch_f32_to_bf16(B, Hq, N, Npad, scale, dq_acc, static_cast<bf16*>(dq), dq_sb, dq_sh,
+                                      dq_sn, st));
+}
+
+// ---------------------------------------------------------------------------
+// solve backward
+// ---------------------------------------------------------------------------
+size_t lucid_solve_bwd_workspace_bytes(int B, int H, int N, int D) {
+  (void)D;
+  const size_t rows = (size_t)B * H * npad_of(N);
+  return kStatusRegion + align256((size_t)B * H * nb_of(N) * sizeof(int)) +
+         align256(rows * kHeadDim * sizeof(bf16)) + 2 * align256(rows * kHeadDim * sizeof(float));
+}
+
+int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int64_t k_sb, int64_t k_sh,
+                    int64_t k_sn, const void* x, const void* khat, const void* u, const float* rstd,
+                    const float* dinv, const float* dx_f32, const float* dk_add, void* dk, int64_t dk_sb,
+                    int64_t dk_sh, int64_t dk_sn, void* dv, int64_t dv_sb, int64_t dv_sh, int64_t dv_sn,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  if (!aligned16(k) || !aligned16(x) || !aligned16(khat) || !aligned16(u) || !aligned16(rstd) ||
+      !aligned16(dinv) || !aligned16(dx_f32) || (dk_add && !aligned16(dk_add)) || !aligned16(dk) ||
+      !aligned16(dv) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(dk_sb, dk_sh, dk_sn) ||
+      !strides_ok(dv_sb, dv_sh, dv_sn))
+    return LUCID_ERR_ALIGN;
+  if (!workspace || workspace_bytes < lucid_solve_bwd_workspace_bytes(B, H, N, D))
+    return LUCID_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int NB = nb_of(N), Npad = npad_of(N);
+  const size_t rows = (size_t)B * H * Npad;
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  size_t off = kStatusRegion;
+  int* flags = reinterpret_cast<int*>(ws + off);
+  off += align256((size_t)B * H * NB * sizeof(int));
+  bf16* dv_int = reinterpret_cast<bf16*>(ws + off);
+  off += align256(rows * kHeadDim * sizeof(bf16));
+  float* dk_col = reinterpret_cast<float*>(ws + off);
+  off += align256(rows * kHeadDim * sizeof(float));
+  float* dk_row = reinterpret_cast<float*>(ws + off);
+  // status + flags, and the atomic row accumulator start at zero
+  if (cudaMemsetAsync(ws, 0, kStatusRegion + align256((size_t)B * H * NB * sizeof(int)), st) != cudaSuccess)
+    return LUCID_ERR_LAUNCH;
+  if (cudaMemsetAsync(dk_row, 0, rows * kHeadDim * sizeof(float), st) != cudaSuccess)
+    return LUCID_ERR_LAUNCH;
+  CUtensorMap tK, tX, tDV, tU;
+  if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
+      !tmap_internal(&tDV, dv_int, B, H, Npad) || !tmap_internal(&tU, u, B, H, Npad))
+    return LUCID_ERR_TENSORMAP;
+  BwdArgs ba{};
+  ba.B = B; ba.Hq = H; ba.Hkv = H; ba.N = N; ba.NB = NB; ba.Npad = Npad;
+  ba.scale = scale;
+  ba.dk_col = dk_col; ba.d_row = dk_row;
+  ba.dinv = dinv; ba.dx_in = dx_f32; ba.dv = dv_int;
+  ba.flags = flags;
+  ba.status = status;
+  cudaError_t e = launch_bwd(true, tK, tX, tK, tDV, tU, ba, st);
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+  return to_status(launch_solve_finalize(
+      B, H, N, Npad, scale, static_cast<const bf16*>(k), k_sb, k_sh, k_sn, rstd, dinv,
+      static_cast<const bf16*>(x), dv_int, dk_col, dk_row, dk_add, static_cast<bf16*>(dk), dk_sb, dk_sh,
+      dk_sn, static_cast<bf16*>(dv), dv_sb, dv_sh, dv_sn, st));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// tensor-core self test
+// ---------------------------------------------------------------------------
+namespace lb {
+
+__global__ void __launch_bounds__(128, 1)
+    umma_selftest_kernel(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+                         const bf16* a, const bf16* b, float* d, int a_mn, int b_mn, int via_tma,
+                         int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - raw);
+  const uint32_t sA = sbase, sB = sbase + 32768;
+  const uint32_t bar_tma = sbase + 65536, bar_mma = bar_tma + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 65536 + 16);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + 65536 + 20);
+  const Abort ab{abort_cta, status};
+  const int r = threadIdx.x, warp = r >> 5;
+  if (r == 0) {
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  if (via_tma) {
+    if (r == 0) {
+      mbar_arrive_expect_tx(bar_tma, 65536);
+      tma_load_tile(sA, &tA, bar_tma, 0, 0, 0);
+      tma_load_tile(sB, &tB, bar_tma, 0, 0, 0);
+    }
+    ok = mbar_wait(bar_tma, 0, ab);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float va[32], vb[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        ld_bf16x8(a + r * 128 + q * 32 + c * 8, va + c * 8);
+        ld_bf16x8(b + r * 128 + q * 32 + c * 8, vb + c * 8);
+      }
+      tile_store_row32(sA, r, q, va);
+      tile_store_row32(sB, r, q, vb);
+    }
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (r == 0 && ok) {
+    tc_fence_after();
+    umma_tile(tmem, sA, a_mn != 0, sB, b_mn != 0, 0u);
+    umma_commit(bar_mma);
+  }
+  ok = ok && mbar_wait(bar_mma, 0, ab);
+  ok = __all_sync(0xffffffffu, ok);
+  if (ok) {
+    tc_fence_after();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + 32u * q, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) d[r * 128 + q * 32 + e] = v[e];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+}  // namespace lb
+
+extern "C" int lucid_selftest_umma(const void* a, const void* b, float* d, int a_mn, int b_mn, int via_tma,
+                                   void* stream) {
+  if (!aligned16(a) || !aligned16(b) || !aligned16(d)) return LUCID_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  CUtensorMap tA, tB;
+  if (!make_tmap_bf16(&tA, a, 128, 128, 1, 1, 128, 128 * 128, 128 * 128) ||
+      !make_tmap_bf16(&tB, b, 128, 128, 1, 1, 128, 128 * 128, 128 * 128))
+    return LUCID_ERR_TENSORMAP;
+  // status word lives right after D (caller allocates 128*128 + 4 floats)
+  int* status = reinterpret_cast<int*>(d + 128 * 128);
+  const int smem = 65536 + 64 + 1024;
+  if (cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return LUCID_ERR_LAUNCH;
+  umma_selftest_kernel<<<1, 128, smem, st>>>(tA, tB, static_cast<const bf16*>(a), static_cast<const bf16*>(b),
+                                             d, a_mn, b_mn, via_tma, status);
+  return cudaGetLastError() == cudaSuccess ? LUCID_OK : LUCID_ERR_LAUNCH;
+}

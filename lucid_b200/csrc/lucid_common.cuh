@@ -1,0 +1,61 @@
+// Shared definitions of the LUCID kernels: problem geometry, argument
+// structs, and the workspace layout contract between forward and backward.
+#pragma once
+#include "sm100.cuh"
+
+namespace lb {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kBlock = 128;      // rows per block (queries / keys / solve rows)
+constexpr int kHeadDim = 128;    // head dimension handled by the tensor-core kernels
+constexpr int kTileBytes = kBlock * kHeadDim * 2;  // 32 KB bf16 tile
+
+// Row statistics + diagonal-block inverse (CUDA cores).
+struct PrepArgs {
+  int B, H, N, NB, Npad;     // H = key/value heads
+  float s, eps;              // s = D^-1/2, eps = RMSNorm epsilon
+  const bf16* k;             // raw keys, element strides below
+  long long k_sb, k_sh, k_sn;
+  bf16* khat;                // [B][H][Npad][128]  RMS-normalised keys (bf16)
+  float* rstd;               // [B*H][Npad]
+  float* dinv;               // [B*H][Npad]        1 / P_rr
+  bf16* u;                   // [B*H][NB][128][128] (I + L~)^-1 - I per diagonal block
+};
+
+// Forward tile engine (solve or attention).
+struct FwdArgs {
+  int B, Hq, Hkv, N, NB, Npad;
+  float scale;               // s (solve) or softmax scale (attention)
+  // solve
+  const float* dinv;
+  const bf16* v;
+  long long v_sb, v_sh, v_sn;
+  bf16* x;                   // [B][Hkv][Npad][128]
+  int* flags;                // [B*Hkv][NB], zero before launch, 1 = X block ready
+  // attention
+  bf16* o;
+  long long o_sb, o_sh, o_sn;
+  float* lse;                // [B*Hq][Npad], log2 domain
+  int* status;
+};
+
+// Backward tile engine (attention backward or transposed solve).
+struct BwdArgs {
+  int B, Hq, Hkv, N, NB, Npad;
+  float scale;
+  // attention backward
+  const float* lse;          // [B*Hq][Npad] log2 domain
+  const float* delta;        // [B*Hq][Npad]  rowsum(dO * O)
+  float* dx;                 // [B][Hkv][Npad][128] fp32 (column-local, plain stores)
+  float* dk_col;             // [B][Hkv][Npad][128] fp32 dK (attention) or dK^ (solve), column part
+  float* d_row;              // fp32 atomic target: dQ [B][Hq][Npad][128] or dK^ rows [B][Hkv][Npad][128]
+  // solve backward
+  const float* dinv;
+  const float* dx_in;        // dX from the attention backward (fp32)
+  bf16* dv;                  // [B][Hkv][Npad][128] bf16 (MMA operand + output source)
+  int* flags;                // [B*Hkv][NB], zero before launch
+  int* status;
+};
+
+}  // namespace lb

@@ -1,0 +1,177 @@
+// Row statistics and diagonal-block inverses of the LUCID preconditioner.
+//
+// For every (batch, kv-head) and every 128-row block i this kernel produces
+//   rstd_r = (mean_d K_r^2 + eps)^-1/2           (RMSNorm without affine,
+//                                                  modeling_lucid.py:409,564)
+//   khat_r = K_r * rstd_r                          (bf16 copy, GEMM operand)
+//   d_r    = P_rr = exp(s * rstd_r^2 |K_r|^2 - 1/s)  computed from the exact
+//            fp32 row statistics, so the cancellation s*|k^|^2 - 1/s ~ 0 never
+//            goes through a bf16 product          (modeling_lucid.py:566-569)
+//   U_i    = (I + L~_i)^-1 - I,  L~_i = D_i^-1 * strictly-lower(P_ii)
+// so that the diagonal solve of block i becomes  X_i = Y + U_i Y  with
+// Y = D_i^-1 R_i (forward) and  dV_i = D_i^-1 (R + U_i^T R) (backward).
+// P_ii's strictly-lower entries are exp(s k^_r.k^_c - 1/s) from fp32 k^.
+//
+// The inverse is a blocked forward substitution over 16x16 sub-blocks in
+// fp32 shared memory.
+#include "lucid_common.cuh"
+
+namespace lb {
+
+constexpr int kLD = 129;  // padded fp32 row stride (bank-conflict free columns)
+
+__global__ void __launch_bounds__(256) lucid_prep_kernel(PrepArgs p) {
+  extern __shared__ float sm[];
+  float* kf = sm;                 // [128][kLD] fp32 k^ rows; reused as Z
+  float* lt = kf + 128 * kLD;     // [128][kLD] L~ (strictly lower)
+  float* dd = lt + 128 * kLD;     // [128] d_r
+  float* tt = dd + 128;           // [8][16][16] temporaries
+
+  const int ib = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float s = p.s, inv_s = 1.0f / p.s;
+
+  // ---- 1. row statistics -------------------------------------------------
+  for (int rr = warp; rr < 128; rr += 8) {
+    const int row = ib * 128 + rr;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (row < p.N) {
+      const bf16* src = p.k + (long long)b * p.k_sb + (long long)h * p.k_sh +
+                        (long long)row * p.k_sn + lane * 4;
+      const uint2 u = *reinterpret_cast<const uint2*>(src);
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const float2 f0 = __bfloat1622float2(hh[0]), f1 = __bfloat1622float2(hh[1]);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    }
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const bool valid = row < p.N;
+    const float r = valid ? 1.0f / sqrtf(ss * (1.0f / kHeadDim) + p.eps) : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) kf[rr * kLD + lane * 4 + e] = v[e] * r;
+    uint2 outv;
+    outv.x = pack_bf16(v[0] * r, v[1] * r);
+    outv.y = pack_bf16(v[2] * r, v[3] * r);
+    *reinterpret_cast<uint2*>(p.khat + ((long long)bh * p.Npad + row) * kHeadDim + lane * 4) = outv;
+    if (lane == 0) {
+      const float g = r * r * ss;  // |k^_r|^2 exactly in fp32
+      const float d = valid ? expf(s * g - inv_s) : 1.0f;
+      dd[rr] = d;
+      p.rstd[(long long)bh * p.Npad + row] = r;
+      p.dinv[(long long)bh * p.Npad + row] = 1.0f / d;
+    }
+  }
+  __syncthreads();
+
+  // ---- 2. L~ = D^-1 strictly-lower(exp(s k^ k^T - 1/s)) ------------------
+  {
+    const int tr = tid >> 4, tc = tid & 15;  // 8x8 output block (tr, tc)
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    if (tc <= tr) {
+      for (int kk = 0; kk < kHeadDim; ++kk) {
+        float a[8], bb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = kf[(tr * 8 + i) * kLD + kk];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bb[j] = kf[(tc * 8 + j) * kLD + kk];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = tr * 8 + i;
+      const bool rv = (ib * 128 + r) < p.N;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = tc * 8 + j;
+        float val = 0.f;
+        if (c < r && rv) val = expf(s * acc[i][j] - inv_s) / dd[r];
+        lt[r * kLD + c] = val;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 3. Z = (I + L~)^-1, blocked forward substitution -----------------
+  float* z = kf;
+  // zero the strictly-upper 16x16 blocks
+  for (int e = tid; e < 128 * 128; e += 256) {
+    const int r = e >> 7, c = e & 127;
+    if ((c >> 4) > (r >> 4)) z[r * kLD + c] = 0.f;
+  }
+  // diagonal 16x16 blocks: warp I, lane c owns column c
+  if (lane < 16) {
+    const int I = warp, c = lane;
+    float zc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float a = (r == c) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < r; ++m) a -= lt[(I * 16 + r) * kLD + I * 16 + m] * zc[m];
+      zc[r] = a;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) z[(I * 16 + r) * kLD + I * 16 + c] = zc[r];
+  }
+  __syncthreads();
+  {
+    const int r = tid >> 4, c = tid & 15;
+    for (int I = 1; I < 8; ++I) {
+      for (int J = 0; J < I; ++J) {
+        float a = 0.f;
+        for (int col = J * 16; col < I * 16; ++col)
+          a = fmaf(lt[(I * 16 + r) * kLD + col], z[col * kLD + J * 16 + c], a);
+        tt[J * 256 + r * 16 + c] = a;
+      }
+      __syncthreads();
+      for (int J = 0; J < I; ++J) {
+        float a = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          a = fmaf(z[(I * 16 + r) * kLD + I * 16 + m], tt[J * 256 + m * 16 + c], a);
+        z[(I * 16 + r) * kLD + J * 16 + c] = -a;
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---- 4. U = Z - I as bf16 ------------------------------------------------
+  {
+    const int r = tid >> 1, half = tid & 1;
+    bf16* dst = p.u + (((long long)bh * p.NB + ib) * 128 + r) * 128 + half * 64;
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = half * 64 + c8 * 8 + e;
+        v[e] = z[r * kLD + c] - (r == c ? 1.f : 0.f);
+      }
+      st_bf16x8(dst + c8 * 8, v);
+    }
+  }
+}
+
+size_t prep_smem_bytes() { return (size_t)(2 * 128 * kLD + 128 + 8 * 256) * sizeof(float); }
+
+cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st) {
+  const size_t smem = prep_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(lucid_prep_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.NB, a.B * a.H);
+  lucid_prep_kernel<<<grid, 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace lb

@@ -1,0 +1,226 @@
+"""Torch-facing LUCID ops on the B200 kernels.
+
+Stages (each a thin wrapper over one C-ABI entry point, see
+include/lucid_b200.h):
+
+  solve_fwd   X = P^-1 V                      modeling_lucid.py:551-574
+  attn_fwd    O = softmax(s Q K^T + causal) X  modeling_lucid.py:505-549
+  attn_bwd    dQ, dK(attention), dX
+  solve_bwd   dV = P^-T dX, dK through P and RMSNorm  modeling_lucid.py:314-382
+
+Autograd functions:
+
+  LucidSolveFunction      drop-in for get_v_prime's "exp_k_norm" branch
+  LucidAttnFunction       drop-in for eager_lucid_attention_forward
+  LucidAttentionFunction  the fused op (solve + attention), dX stays fp32
+
+All tensors are [B, H, N, D] (any strides with a unit innermost stride);
+the attention output is returned as [B, N, Hq, D] like the reference
+(modeling_lucid.py:546).  There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
+    "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
+    "lucid_attention", "padded_len",
+]
+
+
+def padded_len(n: int) -> int:
+    return ((n + 127) // 128) * 128
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _prep(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: LUCID B200 kernels need CUDA tensors (no CPU fallback)")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name}: expected bfloat16, got {t.dtype}")
+    if t.dim() != 4:
+        raise ValueError(f"{name}: expected a 4-D [B, H, N, D] tensor, got shape {tuple(t.shape)}")
+    ok = t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+    return t if ok else t.contiguous()
+
+
+def _s3(t: torch.Tensor):
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# ---------------------------------------------------------------------------
+# stages
+# ---------------------------------------------------------------------------
+def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float):
+    """X = P^-1 V.  Returns (x_int, khat, u, rstd, dinv); x_int is
+    [B, H, Npad, D] (rows >= N are padding)."""
+    lib = _lib.load()
+    k = _prep(k, "key")
+    v = _prep(v, "value")
+    B, H, N, D = k.shape
+    if v.shape != k.shape:
+        raise ValueError(f"key {tuple(k.shape)} and value {tuple(v.shape)} must match")
+    Np = padded_len(N)
+    dev = k.device
+    x = torch.empty(B, H, Np, D, dtype=torch.bfloat16, device=dev)
+    khat = torch.empty(B, H, Np, D, dtype=torch.bfloat16, device=dev)
+    u = torch.empty(B, H, Np, 128, dtype=torch.bfloat16, device=dev)
+    rstd = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
+    dinv = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
+    ws = _ws(lib.lucid_solve_fwd_workspace_bytes(B, H, N, D), dev)
+    rc = lib.lucid_solve_fwd(B, H, N, D, float(scale), float(eps), k.data_ptr(), *_s3(k),
+                             v.data_ptr(), *_s3(v), x.data_ptr(), khat.data_ptr(), u.data_ptr(),
+                             rstd.data_ptr(), dinv.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_solve_fwd")
+    return x, khat, u, rstd, dinv
+
+
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float):
+    """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,D], lse)."""
+    lib = _lib.load()
+    q = _prep(q, "query")
+    k = _prep(k, "key")
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    Np = padded_len(N)
+    if k.shape != (B, Hkv, N, D) or x_int.shape != (B, Hkv, Np, D) or not x_int.is_contiguous():
+        raise ValueError("attn_fwd: inconsistent shapes")
+    dev = q.device
+    o = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=dev)
+    ot = o.transpose(1, 2)
+    lse = torch.empty(B, Hq, Np, dtype=torch.float32, device=dev)
+    ws = _ws(lib.lucid_attn_fwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
+    rc = lib.lucid_attn_fwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
+                            *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), lse.data_ptr(),
+                            ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_attn_fwd")
+    return o, lse
+
+
+def attn_bwd(q, k, x_int, o, do, lse, scale: float):
+    """Backward of attn_fwd.  o, do are [B,N,Hq,D].  Returns
+    (dq [B,Hq,N,D] bf16, dk_f32 [B,Hkv,Npad,D], dx_f32 [B,Hkv,Npad,D])."""
+    lib = _lib.load()
+    q = _prep(q, "query")
+    k = _prep(k, "key")
+    ot = _prep(o.transpose(1, 2), "attn_output")
+    dot = _prep(do.transpose(1, 2), "grad_output")
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    Np = padded_len(N)
+    dev = q.device
+    dq = torch.empty(B, Hq, N, D, dtype=torch.bfloat16, device=dev)
+    dk = torch.empty(B, Hkv, Np, D, dtype=torch.float32, device=dev)
+    dx = torch.empty(B, Hkv, Np, D, dtype=torch.float32, device=dev)
+    ws = _ws(lib.lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
+    rc = lib.lucid_attn_bwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
+                            *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), dot.data_ptr(),
+                            *_s3(dot), lse.data_ptr(), dq.data_ptr(), *_s3(dq), dk.data_ptr(),
+                            dx.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_attn_bwd")
+    return dq, dk, dx
+
+
+def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None):
+    """Backward of solve_fwd.  Returns (dk, dv) bf16 [B,H,N,D]."""
+    lib = _lib.load()
+    k = _prep(k, "key")
+    B, H, N, D = k.shape
+    dev = k.device
+    dk = torch.empty(B, H, N, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty(B, H, N, D, dtype=torch.bfloat16, device=dev)
+    ws = _ws(lib.lucid_solve_bwd_workspace_bytes(B, H, N, D), dev)
+    rc = lib.lucid_solve_bwd(B, H, N, D, float(scale), k.data_ptr(), *_s3(k), x_int.data_ptr(),
+                             khat.data_ptr(), u.data_ptr(), rstd.data_ptr(), dinv.data_ptr(),
+                             dx_f32.data_ptr(), dk_add.data_ptr() if dk_add is not None else None,
+                             dk.data_ptr(), *_s3(dk), dv.data_ptr(), *_s3(dv), ws.data_ptr(), ws.numel(),
+                             _stream())
+    _lib.check(rc, "lucid_solve_bwd")
+    return dk, dv
+
+
+# ---------------------------------------------------------------------------
+# autograd
+# ---------------------------------------------------------------------------
+class LucidSolveFunction(torch.autograd.Function):
+    """X = P^-1 V (get_v_prime, exp_k_norm branch).  Returns X [B,H,N,D]."""
+
+    @staticmethod
+    def forward(ctx, key, value, scaling: float, eps: float):
+        k = _prep(key, "key")
+        x, khat, u, rstd, dinv = solve_fwd(k, value, scaling, eps)
+        ctx.save_for_backward(k, x, khat, u, rstd, dinv)
+        ctx.scaling = scaling
+        return x[:, :, : k.shape[2]]
+
+    @staticmethod
+    def backward(ctx, gx):
+        k, x, khat, u, rstd, dinv = ctx.saved_tensors
+        B, H, N, D = k.shape
+        dx = torch.zeros(B, H, x.shape[2], D, dtype=torch.float32, device=k.device)
+        dx[:, :, :N] = gx.float()
+        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, ctx.scaling)
+        return dk, dv, None, None
+
+
+class LucidAttnFunction(torch.autograd.Function):
+    """O = softmax(s Q K^T + causal) X (eager_lucid_attention_forward).
+    Returns O as [B, N, Hq, D]."""
+
+    @staticmethod
+    def forward(ctx, query, key, v_prime, scaling: float):
+        B, Hkv, N, D = key.shape
+        x = torch.zeros(B, Hkv, padded_len(N), D, dtype=torch.bfloat16, device=key.device)
+        x[:, :, :N] = v_prime
+        o, lse = attn_fwd(query, key, x, scaling)
+        ctx.save_for_backward(query, key, x, o, lse)
+        ctx.scaling = scaling
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, x, o, lse = ctx.saved_tensors
+        N = k.shape[2]
+        dq, dk, dx = attn_bwd(q, k, x, o, do, lse, ctx.scaling)
+        return dq, dk[:, :, :N].to(torch.bfloat16), dx[:, :, :N].to(torch.bfloat16), None
+
+
+class LucidAttentionFunction(torch.autograd.Function):
+    """Fused LUCID attention: O = softmax(s Q K^T + causal) P^-1 V, returned
+    as [B, N, Hq, D]; q [B,Hq,N,D], k, v [B,Hkv,N,D]."""
+
+    @staticmethod
+    def forward(ctx, query, key, value, scaling: float, eps: float):
+        k = _prep(key, "key")
+        q = _prep(query, "query")
+        x, khat, u, rstd, dinv = solve_fwd(k, value, scaling, eps)
+        o, lse = attn_fwd(q, k, x, scaling)
+        ctx.save_for_backward(q, k, x, khat, u, rstd, dinv, o, lse)
+        ctx.scaling = scaling
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, x, khat, u, rstd, dinv, o, lse = ctx.saved_tensors
+        s = ctx.scaling
+        dq, dk_attn, dx = attn_bwd(q, k, x, o, do, lse, s)
+        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, s, dk_add=dk_attn)
+        return dq, dk, dv, None, None
+
+
+def lucid_attention(query, key, value, scaling: float | None = None, eps: float = 1e-5):
+    """Fused LUCID attention.  query [B,Hq,N,D], key/value [B,Hkv,N,D]
+    (bf16, CUDA).  Returns O [B, N, Hq, D]."""
+    if scaling is None:
+        scaling = query.shape[-1] ** -0.5
+    return LucidAttentionFunction.apply(query, key, value, float(scaling), float(eps))

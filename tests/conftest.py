@@ -1,0 +1,43 @@
+import glob
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU (sm_100a)")
+
+
+def from_bf16_bits(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def load_golden(name: str) -> dict:
+    """Fixture produced by tests/golden/make_golden.py from the reference.
+    Inputs (q, k, v, do) are exact bf16 values, returned as float64."""
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        d = {k: z[k] for k in z.files}
+    for nm in ("q", "k", "v", "do"):
+        if f"{nm}_bf16" in d:
+            d[nm] = from_bf16_bits(d.pop(f"{nm}_bf16")).astype(np.float64)
+    return d
+
+
+ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                    if not os.path.basename(p).startswith("blockwise"))
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)

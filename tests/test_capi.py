@@ -1,0 +1,92 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol
+declared in include/lucid_b200.h, and the host-only helpers behave."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "lucid_b200.h")
+
+
+def declared_symbols():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(lucid_[a-z0-9_]+)\s*\(", txt)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from lucid_b200 import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        from lucid_b200 import build
+        build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_stage_entry_points():
+    syms = declared_symbols()
+    for s in ("lucid_solve_fwd", "lucid_attn_fwd", "lucid_attn_bwd", "lucid_solve_bwd"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+
+
+def test_binding_covers_every_declared_symbol():
+    from lucid_b200 import _lib
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_host_helpers(lib):
+    assert lib.lucid_version() >= 100
+    assert lib.lucid_padded_len(1) == 128
+    assert lib.lucid_padded_len(128) == 128
+    assert lib.lucid_padded_len(130) == 256
+    assert lib.lucid_workspace_status_offset() == 0
+    B, H, N, D = 2, 4, 1000, 128
+    ws_f = lib.lucid_solve_fwd_workspace_bytes(B, H, N, D)
+    assert ws_f >= 256 + B * H * 8 * 4
+    ws_b = lib.lucid_solve_bwd_workspace_bytes(B, H, N, D)
+    assert ws_b >= B * H * 1024 * 128 * (2 + 4 + 4)
+    assert lib.lucid_attn_bwd_workspace_bytes(B, 8, H, N, D) >= B * 8 * 1024 * 128 * 4
+
+
+def test_argument_errors_without_launch(lib):
+    """Bad shapes / alignment / workspace are rejected before any CUDA call."""
+    from lucid_b200 import _lib as L
+    null = None
+    # D != 128
+    rc = lib.lucid_solve_fwd(1, 1, 128, 64, 0.125, 1e-5, 16, 64, 64, 64, 16, 64, 64, 64,
+                             16, 16, 16, 16, 16, 16, 4096, null)
+    assert rc == 1
+    # misaligned pointer
+    rc = lib.lucid_solve_fwd(1, 1, 128, 128, 0.088, 1e-5, 18, 128, 128, 128, 16, 128, 128, 128,
+                             16, 16, 16, 16, 16, 16, 4096, null)
+    assert rc == 2
+    # workspace too small
+    rc = lib.lucid_solve_fwd(1, 1, 128, 128, 0.088, 1e-5, 16, 128, 128, 128, 16, 128, 128, 128,
+                             16, 16, 16, 16, 16, 16, 8, null)
+    assert rc == 3
+    # Hq not a multiple of Hkv
+    rc = lib.lucid_attn_fwd(1, 3, 2, 128, 128, 0.088, 16, 128, 128, 128, 16, 128, 128, 128, 16,
+                            16, 128, 128, 128, 16, 16, 4096, null)
+    assert rc == 1
+    # empty problems are a no-op
+    rc = lib.lucid_solve_fwd(1, 1, 0, 128, 0.088, 1e-5, 16, 128, 128, 128, 16, 128, 128, 128,
+                             16, 16, 16, 16, 16, 16, 4096, null)
+    assert rc == 0
+    with pytest.raises(L.LucidError):
+        L.check(3, "x")
+
+
+def test_ops_refuse_cpu_tensors():
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import lucid_attention
+    q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        lucid_attention(q, q, q)

@@ -1,0 +1,204 @@
+"""GPU parity tests: the sm_100a kernels (through the C ABI) against the CPU
+oracle and the reference's golden fixtures.
+
+Tolerance (bf16): max |ours - ref| <= 1e-2 + 2^-8 |ref|, i.e. 1e-2 absolute
+beyond the half-ulp rounding of the bf16 output itself; the reference value
+is the float64 restatement of modeling_lucid.py on the same (bf16-exact)
+inputs.  Worst-case errors are also reported so drift is visible.
+"""
+import numpy as np
+import pytest
+
+from conftest import ATTN_CASES, load_golden
+from oracle import lucid_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2
+RTOL_BF16 = 2.0 ** -8
+
+
+def _t(a, dev, dtype=None):
+    import torch
+    return torch.as_tensor(np.ascontiguousarray(a)).to(device=dev, dtype=dtype or torch.bfloat16)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def assert_bf16_close(ours, ref, what):
+    err = np.abs(ours - ref)
+    bound = ATOL + RTOL_BF16 * np.abs(ref)
+    worst = float(np.max(err - bound))
+    assert np.all(np.isfinite(ours)), f"{what}: non-finite values"
+    assert worst <= 0, f"{what}: max excess {worst:.3e} (max abs err {float(err.max()):.3e})"
+    return float(err.max())
+
+
+def _rand_inputs(seed, B, Hq, Hkv, N, D=128, keys="iid", q_scale=1.0):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, Hq, N, D)) * q_scale
+    if keys == "iid":
+        k = rng.standard_normal((B, Hkv, N, D))
+    else:
+        k = 0.6 * rng.standard_normal((B, Hkv, 1, D)) + 0.8 * rng.standard_normal((B, Hkv, N, D))
+    v = rng.standard_normal((B, Hkv, N, D))
+    do = rng.standard_normal((B, N, Hq, D))
+    import torch
+    rnd = lambda a: torch.as_tensor(a).to(torch.bfloat16).double().numpy()
+    return [rnd(a) for a in (q, k, v, do)]
+
+
+# ---------------------------------------------------------------------------
+# tensor-core primitive
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("via_tma", [0, 1])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_umma_tile_selftest(cuda_device, a_mn, b_mn, via_tma):
+    import torch
+    from lucid_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cpu").manual_seed(0)
+    a = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    b = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    da, db = a.to(cuda_device), b.to(cuda_device)
+    d = torch.zeros(128 * 128 + 4, dtype=torch.float32, device=cuda_device)
+    rc = lib.lucid_selftest_umma(da.data_ptr(), db.data_ptr(), d.data_ptr(), a_mn, b_mn, via_tma,
+                                 torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    af, bf = a.float(), b.float()
+    A = af.t() if a_mn else af
+    Bm = bf if b_mn else bf.t()
+    ref = A @ Bm
+    got = d[: 128 * 128].view(128, 128).cpu()
+    assert d[128 * 128:].view(torch.int32)[0].item() == 0
+    torch.testing.assert_close(got, ref, atol=1e-3, rtol=1e-3)
+
+
+# ---------------------------------------------------------------------------
+# solve forward
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("B,H,N,keys", [(1, 1, 128, "iid"), (1, 2, 130, "iid"), (2, 3, 512, "iid"),
+                                        (1, 2, 1000, "corr"), (1, 1, 2048, "iid")])
+def test_solve_fwd_matches_oracle(cuda_device, B, H, N, keys):
+    from lucid_b200 import solve_fwd
+    _, k, v, _ = _rand_inputs(10 + N, B, H, H, N, keys=keys)
+    s = 128 ** -0.5
+    x, khat, u, rstd, dinv = solve_fwd(_t(k, cuda_device), _t(v, cuda_device), s, 1e-5)
+    ref = orc.solve(k, v, s, 1e-5)
+    kh, r = orc.rms_norm(k, 1e-5)
+    np.testing.assert_allclose(_np(rstd)[..., :N], r[..., 0], rtol=1e-5)
+    assert_bf16_close(_np(khat)[:, :, :N], kh, "khat")
+    assert_bf16_close(_np(x)[:, :, :N], ref, "X")
+    assert np.all(np.isfinite(_np(x)))
+
+
+def test_solve_fwd_diag_block_inverse(cuda_device):
+    """U = (I + L~)^-1 - I of every diagonal block, against numpy."""
+    from lucid_b200 import solve_fwd
+    _, k, v, _ = _rand_inputs(3, 1, 1, 1, 256, keys="corr")
+    s = 128 ** -0.5
+    _, _, u, _, dinv = solve_fwd(_t(k, cuda_device), _t(v, cuda_device), s, 1e-5)
+    p = orc.build_p(k, s, 1e-5)[0, 0]
+    un = _np(u)[0, 0]
+    for i in range(2):
+        blk = p[i * 128:(i + 1) * 128, i * 128:(i + 1) * 128]
+        d = np.diag(blk)
+        lt = np.tril(blk, -1) / d[:, None]
+        want = np.linalg.inv(np.eye(128) + lt) - np.eye(128)
+        np.testing.assert_allclose(un[i * 128:(i + 1) * 128], want, atol=2e-3)
+        np.testing.assert_allclose(_np(dinv)[0, 0, i * 128:(i + 1) * 128], 1.0 / d, rtol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+# full op against the reference's own outputs
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", [c for c in ATTN_CASES if c.endswith("d128")])
+def test_fused_matches_reference_fixture(cuda_device, case):
+    import torch
+    from lucid_b200 import lucid_attention
+    g = load_golden(case)
+    q = _t(g["q"], cuda_device).requires_grad_(True)
+    k = _t(g["k"], cuda_device).requires_grad_(True)
+    v = _t(g["v"], cuda_device).requires_grad_(True)
+    o = lucid_attention(q, k, v, float(g["scale"]), float(g["eps"]))
+    o.backward(_t(g["do"], cuda_device))
+    torch.cuda.synchronize()
+    assert_bf16_close(_np(o), g["o"], f"{case} O")
+    assert_bf16_close(_np(q.grad), g["dq"], f"{case} dQ")
+    assert_bf16_close(_np(k.grad), g["dk"], f"{case} dK")
+    assert_bf16_close(_np(v.grad), g["dv"], f"{case} dV")
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,keys,qs", [
+    (1, 2, 2, 384, "iid", 1.0),
+    (2, 4, 2, 300, "iid", 128 ** -0.5),
+    (1, 1, 1, 1024, "corr", 1.0),
+    (1, 8, 1, 256, "iid", 1.0),
+])
+def test_fused_fwd_bwd_matches_oracle(cuda_device, B, Hq, Hkv, N, keys, qs):
+    import torch
+    from lucid_b200 import lucid_attention
+    q_, k_, v_, do_ = _rand_inputs(100 + N, B, Hq, Hkv, N, keys=keys, q_scale=qs)
+    s = 128 ** -0.5
+    q = _t(q_, cuda_device).requires_grad_(True)
+    k = _t(k_, cuda_device).requires_grad_(True)
+    v = _t(v_, cuda_device).requires_grad_(True)
+    o = lucid_attention(q, k, v, s)
+    o.backward(_t(do_, cuda_device))
+    torch.cuda.synchronize()
+    o_ref, dq_ref, dk_ref, dv_ref = orc.lucid_fwd_bwd(q_, k_, v_, do_, s)
+    assert_bf16_close(_np(o), o_ref, "O")
+    assert_bf16_close(_np(q.grad), dq_ref, "dQ")
+    assert_bf16_close(_np(k.grad), dk_ref, "dK")
+    assert_bf16_close(_np(v.grad), dv_ref, "dV")
+
+
+def test_separate_functions_compose(cuda_device):
+    """get_v_prime (LucidSolveFunction) followed by the attention function
+    (LucidAttnFunction) gives the same result as the fused op."""
+    import torch
+    from lucid_b200 import LucidAttnFunction, LucidSolveFunction
+    q_, k_, v_, do_ = _rand_inputs(7, 1, 2, 2, 200)
+    s = 128 ** -0.5
+    q = _t(q_, cuda_device).requires_grad_(True)
+    k = _t(k_, cuda_device).requires_grad_(True)
+    v = _t(v_, cuda_device).requires_grad_(True)
+    x = LucidSolveFunction.apply(k, v, s, 1e-5)
+    o = LucidAttnFunction.apply(q, k, x, s)
+    o.backward(_t(do_, cuda_device))
+    torch.cuda.synchronize()
+    o_ref, dq_ref, dk_ref, dv_ref = orc.lucid_fwd_bwd(q_, k_, v_, do_, s)
+    assert_bf16_close(_np(o), o_ref, "O")
+    assert_bf16_close(_np(q.grad), dq_ref, "dQ")
+    # dX crosses the autograd boundary in bf16 here: allow one more rounding
+    assert_bf16_close(_np(k.grad), dk_ref, "dK")
+    assert_bf16_close(_np(v.grad), dv_ref, "dV")
+
+
+def test_forward_is_deterministic(cuda_device):
+    import torch
+    from lucid_b200 import lucid_attention
+    q_, k_, v_, _ = _rand_inputs(5, 1, 4, 4, 640)
+    q, k, v = (_t(a, cuda_device) for a in (q_, k_, v_))
+    o1 = lucid_attention(q, k, v)
+    o2 = lucid_attention(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+
+
+def test_strided_bnhd_inputs(cuda_device):
+    """Q/K/V as transposed views of [B, N, H, D] projections (the layout
+    LucidAttention.forward produces, modeling_lucid.py:433-435)."""
+    import torch
+    from lucid_b200 import lucid_attention
+    q_, k_, v_, do_ = _rand_inputs(9, 2, 2, 2, 256)
+    mk = lambda a: _t(np.ascontiguousarray(np.swapaxes(a, 1, 2)), cuda_device).transpose(1, 2)
+    q, k, v = mk(q_), mk(k_), mk(v_)
+    assert not q.is_contiguous()
+    o = lucid_attention(q, k, v)
+    torch.cuda.synchronize()
+    o_ref, _ = orc.lucid_fwd(q_, k_, v_, 128 ** -0.5)
+    assert_bf16_close(_np(o), o_ref, "O")
