@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the LUCID attention hot path on B200.
+
+Metric: LUCID attention fwd+bwd TFLOP/s and fraction of the
+dense-BF16 peak at N=32K, with the overhead against plain causal attention
+of the same shape.
+
+Workload per GPU (one step): one LUCID attention layer forward + backward,
+bf16, B=1, H=32 (MHA), N=32768, D=128, causal; Q ~ N(0,1)/sqrt(128),
+K, V, dO ~ N(0,1) (seeded synthetic data, per rank).  Every input tensor is
+268 MB, larger than the 126 MB L2, so no flush is needed between steps.
+
+Algorithmic FLOPs per (batch, head): 14 N^2 D
+  attention fwd 2 N^2 D + bwd 5 N^2 D, LUCID solve fwd 2 N^2 D + bwd 5 N^2 D.
+
+Multi-GPU (torchrun): (batch, head) sharding with no data-path collective;
+every rank runs its own batch element (weak scaling); the step time is the
+max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "LUCID attn fwd+bwd TFLOP/s & % BF16 peak at 32K; overhead vs causal attn"
+CONFIGS = {
+    # name: (B per rank, H, N, D, q_scale)
+    "32k": (1, 32, 32768, 128, 128 ** -0.5),
+    "cfg2": (4, 32, 4096, 128, 128 ** -0.5),
+    "small": (1, 8, 4096, 128, 128 ** -0.5),
+    "8k": (1, 32, 8192, 128, 128 ** -0.5),   # profiling case (about 1.5 GB on the device)
+}
+
+
+def flops_per_step(B, H, N, D):
+    return 14.0 * N * N * D * B * H
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), \
+            float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi, during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's torch path (restated in oracle/torch_ref.py)
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(N: int, D: int, seed: int = 0):
+    """One LUCID layer fwd+bwd for one (batch, head) on the host cores, fp32
+    (the reference's solve_triangular path has no bf16 CPU kernel)."""
+    import torch
+
+    from oracle import torch_ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, 1, N, D, generator=g) * D ** -0.5
+    k = torch.randn(1, 1, N, D, generator=g)
+    v = torch.randn(1, 1, N, D, generator=g)
+    do = torch.randn(1, N, 1, D, generator=g)
+    t0 = time.perf_counter()
+    torch_ref.lucid_fwd_bwd(q, k, v, do)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(N_cpu: int, D: int, reps: int = 1):
+    cpu_reference_sample(1024, D)  # warm-up (thread pool, allocator)
+    times = [cpu_reference_sample(N_cpu, D, seed=i) for i in range(reps)]
+    t = statistics.median(times)
+    fl = flops_per_step(1, 1, N_cpu, D)
+    return {"value": fl / t / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 (batch, head) of the workload at N={N_cpu}, D={D}, fp32, fwd+bwd via "
+                      f"oracle/torch_ref.py (reference torch path), median of {reps}",
+            "seconds_per_sample": t}
+
+
+def reference_arm(args):
+    """--impl reference: the reference's CPU path on the host cores, same
+    metric/config; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    B, H, N, D, _ = CONFIGS[args.config]
+    n_cpu = args.cpu_n
+    cpu_reference_sample(1024, D)
+    for _ in range(args.warmup):
+        cpu_reference_sample(n_cpu, D)
+    times = [cpu_reference_sample(n_cpu, D, seed=i) for i in range(args.steps)]
+    t = sum(times) / len(times)
+    val = flops_per_step(1, 1, n_cpu, D) / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} (sampled: 1 head at N={n_cpu})",
+                   "global_batch": B, "seq_len": N, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"1 (batch, head) at N={n_cpu}, D={D}, fp32, oracle/torch_ref.py"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="32k")
+    ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from lucid_b200 import _lib, attn_bwd, attn_fwd, lucid_attention, solve_bwd, solve_fwd
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    lib = _lib.load()
+    B, H, N, D, qs = CONFIGS[args.config]
+    s = D ** -0.5
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    mk = lambda *shape, sc=1.0: (torch.randn(*shape, generator=g, device=dev) * sc).to(torch.bfloat16)
+    q = mk(B, H, N, D, sc=qs).requires_grad_(True)
+    k = mk(B, H, N, D).requires_grad_(True)
+    v = mk(B, H, N, D).requires_grad_(True)
+    do = mk(B, N, H, D)
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        o = lucid_attention(q, k, v, s)
+        o.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    fl = flops_per_step(B, H, N, D) * world
+    tflops = fl / (ms * 1e-3) / 1e12
+
+    # ---- per-kernel timing (dominant kernel -> roofline) ----
+    pk_burst, pk_sust, hbm, pk_kind = peaks()
+    per_stage_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 5, "solve_bwd": 5}
+    stage_ms = {}
+    with torch.no_grad():
+        x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
+        o, lse = attn_fwd(q, k, x, s)
+        dq, dkf, dxf = attn_bwd(q, k, x, o, do, lse, s)
+        torch.cuda.synchronize()
+        reps = 3
+        for name in ("solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd"):
+            lib.lucid_profile_enable(_lib.KERNEL_IDS[name])
+            for _ in range(reps):
+                if name == "solve_fwd":
+                    solve_fwd(k, v, s, 1e-5)
+                elif name == "attn_fwd":
+                    attn_fwd(q, k, x, s)
+                elif name == "attn_bwd":
+                    attn_bwd(q, k, x, o, do, lse, s)
+                else:
+                    solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf)
+            torch.cuda.synchronize()
+            tot, n = ctypes.c_float(), ctypes.c_int()
+            lib.lucid_profile_read(ctypes.byref(tot), ctypes.byref(n))
+            stage_ms[name] = tot.value / max(n.value, 1)
+        lib.lucid_profile_enable(0)
+        lib.lucid_profile_enable(_lib.KERNEL_IDS["prep"])
+        solve_fwd(k, v, s, 1e-5)
+        torch.cuda.synchronize()
+        tot, n = ctypes.c_float(), ctypes.c_int()
+        lib.lucid_profile_read(ctypes.byref(tot), ctypes.byref(n))
+        stage_ms["prep"] = tot.value / max(n.value, 1)
+        lib.lucid_profile_enable(0)
+        del x, khat, u, rstd, dinv, o, lse, dq, dkf, dxf
+    dom = max(per_stage_flops, key=lambda n: stage_ms[n])
+    dom_flops = per_stage_flops[dom] * float(N) * N * D * B * H
+    achieved = dom_flops / (stage_ms[dom] * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tj = json.load(f)
+            if tj.get("config") == args.config:
+                traffic = tj.get(dom)
+        except Exception:
+            traffic = None
+
+    # ---- causal attention of the same shape (overhead reference) ----
+    import torch.nn.functional as F
+    qd, kd, vd = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    dot = do.transpose(1, 2)
+    def sdpa_step():
+        qd.grad = kd.grad = vd.grad = None
+        F.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=s).backward(dot)
+    for _ in range(2):
+        sdpa_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        sdpa_step()
+    e1.record()
+    torch.cuda.synchronize()
+    sdpa_ms = e0.elapsed_time(e1) / 3
+    our_attn_ms = stage_ms["attn_fwd"] + stage_ms["attn_bwd"]
+    del qd, kd, vd
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        hq = q.detach().cpu().pin_memory()
+        hk = k.detach().cpu().pin_memory()
+        hv = v.detach().cpu().pin_memory()
+        hdo = do.cpu().pin_memory()
+        outs = [torch.empty(B, N, H, D, dtype=torch.bfloat16).pin_memory()] + \
+               [torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+
+        def e2e_step():
+            qq = hq.to(dev, non_blocking=True).requires_grad_(True)
+            kk = hk.to(dev, non_blocking=True).requires_grad_(True)
+            vv = hv.to(dev, non_blocking=True).requires_grad_(True)
+            dd = hdo.to(dev, non_blocking=True)
+            oo = lucid_attention(qq, kk, vv, s)
+            oo.backward(dd)
+            for h, t in zip(outs, (oo, qq.grad, kk.grad, vv.grad)):
+                h.copy_(t.detach(), non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        ne = max(1, min(args.steps, 3))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(ne):
+            e2e_step()
+        a1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = a0.elapsed_time(a1) / ne
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        nbytes = B * H * N * D * 2
+        e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(args.cpu_n, D)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    launches_per_step = 8  # prep, solve, attn fwd, delta, attn bwd, dq convert, solve bwd, finalize
+    line = {
+        "metric": METRIC,
+        "value": tflops,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} causal MHA per GPU",
+                   "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D,
+                   "parallelism": f"(batch,head) shards x{world}, no collective",
+                   "l2": "inputs larger than L2 (268 MB per tensor), no flush"},
+        "tokens_per_s": B * N * world / (ms * 1e-3),
+        "frac_of_bf16_peak": tflops / pk_sust,
+        "peak_used": {"bf16_tflops_sustained": pk_sust, "bf16_tflops_burst": pk_burst, "kind": pk_kind},
+        "overhead_vs_causal_attn": {"sdpa_fwd_bwd_ms": sdpa_ms, "lucid_fwd_bwd_ms": ms,
+                                    "ratio_vs_sdpa": ms / sdpa_ms, "our_attention_only_ms": our_attn_ms,
+                                    "ratio_vs_our_attention": ms / our_attn_ms},
+        "stage_ms": stage_ms,
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": pk_burst,
+                     "unit": "TFLOP/s", "frac": achieved / pk_burst, "traffic": traffic,
+                     "peak_kind": f"{pk_kind} burst bf16 (kernel timed alone)"},
+        "clocks": clk,
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -125,8 +125,25 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Kernel timing hook (benchmarks).  While enabled for one kernel family,
+ * every launch of that family's main kernel is bracketed by a pair of CUDA
+ * events recorded on the launch stream; lucid_profile_read waits for the
+ * recorded events and returns the summed device time and the launch count.
+ * lucid_profile_enable(0) disables recording.  Not thread-safe with
+ * concurrent launches from several host threads.
+ */
+#define LUCID_KERNEL_PREP 1       /* row statistics + diagonal-block inverses */
+#define LUCID_KERNEL_SOLVE_FWD 2  /* wavefront solve X = P^-1 V */
+#define LUCID_KERNEL_ATTN_FWD 3   /* causal attention forward */
+#define LUCID_KERNEL_ATTN_BWD 4   /* attention backward */
+#define LUCID_KERNEL_SOLVE_BWD 5  /* transposed-solve backward */
+int lucid_profile_enable(int kernel);
+int lucid_profile_read(float* total_ms, int* launches);
+
+/*
  * Tensor-core self test: D = op(A) op(B) for one 128x128x128 bf16 tile,
- * A and B row-major [128][128] bf16, D row-major fp32.  a_mn / b_mn select
+ * A and B row-major [128][128] bf16, D row-major fp32 with room for one
+ * extra int32 status word after the 128*128 results.  a_mn / b_mn select
  * the operand majorness (0: A is used as is / B^T; 1: A^T / B), i.e.
  *   (0,0) D = A B^T   (0,1) D = A B   (1,0) D = A^T B^T   (1,1) D = A^T B.
  * `via_tma` loads the operands with TMA instead of thread stores.

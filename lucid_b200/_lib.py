@@ -13,6 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "liblucid_b200.so")
 
 LUCID_OK = 0
+KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bwd": 5}
 ERRORS = {
     1: "unsupported shape (head_dim must be 128, Hq a multiple of Hkv)",
     2: "pointer or stride not 16-byte aligned",
@@ -47,6 +48,8 @@ SIGNATURES = {
                         + [c_void_p, c_void_p] + [c_void_p] + S3 + [c_void_p] + S3
                         + [c_void_p, c_size_t, c_void_p]),
     "lucid_selftest_umma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "lucid_profile_enable": (c_int, [c_int]),
+    "lucid_profile_read": (c_int, [c_float_p, ctypes.POINTER(c_int)]),
 }
 
 _lock = threading.Lock()

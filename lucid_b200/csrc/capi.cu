@@ -27,7 +27,46 @@ cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const 
 
 using namespace lb;
 
+#include <mutex>
+#include <vector>
+
 namespace {
+
+// ---- kernel timing hook -----------------------------------------------------
+struct Profiler {
+  std::mutex mu;
+  int kernel = 0;
+  std::vector<cudaEvent_t> ev;  // start/stop pairs
+  int used = 0;                 // pairs recorded
+};
+Profiler& profiler() {
+  static Profiler p;
+  return p;
+}
+
+// Brackets one launch with events when the hook is enabled for `kernel`.
+struct ProfileScope {
+  cudaEvent_t stop = nullptr;
+  cudaStream_t st;
+  ProfileScope(int kernel, cudaStream_t s) : st(s) {
+    Profiler& p = profiler();
+    std::lock_guard<std::mutex> g(p.mu);
+    if (p.kernel != kernel || p.used >= 512) return;
+    if ((int)p.ev.size() < 2 * (p.used + 1)) {
+      cudaEvent_t a, b;
+      if (cudaEventCreate(&a) != cudaSuccess) return;
+      if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return; }
+      p.ev.push_back(a);
+      p.ev.push_back(b);
+    }
+    cudaEventRecord(p.ev[2 * p.used], st);
+    stop = p.ev[2 * p.used + 1];
+    ++p.used;
+  }
+  ~ProfileScope() {
+    if (stop) cudaEventRecord(stop, st);
+  }
+};
 
 constexpr size_t kStatusRegion = 256;
 
@@ -61,6 +100,29 @@ bool tmap_strided(CUtensorMap* m, const void* p, int B, int H, int N, int64_t sb
 extern "C" {
 
 int lucid_version(void) { return 100; }
+
+int lucid_profile_enable(int kernel) {
+  Profiler& p = profiler();
+  std::lock_guard<std::mutex> g(p.mu);
+  p.kernel = kernel;
+  p.used = 0;
+  return LUCID_OK;
+}
+
+int lucid_profile_read(float* total_ms, int* launches) {
+  Profiler& p = profiler();
+  std::lock_guard<std::mutex> g(p.mu);
+  float tot = 0.f;
+  for (int i = 0; i < p.used; ++i) {
+    if (cudaEventSynchronize(p.ev[2 * i + 1]) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, p.ev[2 * i], p.ev[2 * i + 1]) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    tot += ms;
+  }
+  if (total_ms) *total_ms = tot;
+  if (launches) *launches = p.used;
+  return LUCID_OK;
+}
 int lucid_padded_len(int N) { return npad_of(N); }
 size_t lucid_workspace_status_offset(void) { return 0; }
 
@@ -96,7 +158,10 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
   pa.s = scale; pa.eps = eps;
   pa.k = static_cast<const bf16*>(k); pa.k_sb = k_sb; pa.k_sh = k_sh; pa.k_sn = k_sn;
   pa.khat = static_cast<bf16*>(khat); pa.rstd = rstd; pa.dinv = dinv; pa.u = static_cast<bf16*>(u);
-  e = launch_prep(pa, st);
+  {
+    ProfileScope ps(LUCID_KERNEL_PREP, st);
+    e = launch_prep(pa, st);
+  }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
 
   CUtensorMap tK, tX, tU;
@@ -111,6 +176,7 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
   fa.x = static_cast<bf16*>(x);
   fa.flags = flags;
   fa.status = status;
+  ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
   return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
 }
 
@@ -147,6 +213,7 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
   fa.lse = lse;
   fa.status = status;
+  ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
   return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
 }
 
@@ -198,7 +265,10 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   ba.lse = lse; ba.delta = delta;
   ba.dx = dx_f32; ba.dk_col = dk_f32; ba.d_row = dq_acc;
   ba.status = status;
-  e = launch_bwd(false, tK, tX, tQ, tDO, tX, ba, st);
+  {
+    ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
+    e = launch_bwd(false, tK, tX, tQ, tDO, tX, ba, st);
+  }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   return to_status(launch_f32_to_bf16(B, Hq, N, Npad, scale, dq_acc, static_cast<bf16*>(dq), dq_sb, dq_sh,
                                       dq_sn, st));
@@ -257,7 +327,11 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   ba.dinv = dinv; ba.dx_in = dx_f32; ba.dv = dv_int;
   ba.flags = flags;
   ba.status = status;
-  cudaError_t e = launch_bwd(true, tK, tX, tK, tDV, tU, ba, st);
+  cudaError_t e;
+  {
+    ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
+    e = launch_bwd(true, tK, tX, tK, tDV, tU, ba, st);
+  }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   return to_status(launch_solve_finalize(
       B, H, N, Npad, scale, static_cast<const bf16*>(k), k_sb, k_sh, k_sn, rstd, dinv,

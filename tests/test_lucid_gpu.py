@@ -4,7 +4,9 @@ oracle and the reference's golden fixtures.
 Tolerance (bf16): max |ours - ref| <= 1e-2 + 2^-8 |ref|, i.e. 1e-2 absolute
 beyond the half-ulp rounding of the bf16 output itself; the reference value
 is the float64 restatement of modeling_lucid.py on the same (bf16-exact)
-inputs.  Worst-case errors are also reported so drift is visible.
+inputs.  For grouped-query heads the kv-head gradients dK and dV are sums
+over the G query heads of a group, each carrying the bf16 rounding of the
+attention probabilities, so their absolute budget is 1e-2 * sqrt(G).
 """
 import numpy as np
 import pytest
@@ -27,9 +29,9 @@ def _np(t):
     return t.detach().float().cpu().numpy().astype(np.float64)
 
 
-def assert_bf16_close(ours, ref, what):
+def assert_bf16_close(ours, ref, what, group=1):
     err = np.abs(ours - ref)
-    bound = ATOL + RTOL_BF16 * np.abs(ref)
+    bound = ATOL * np.sqrt(group) + RTOL_BF16 * np.abs(ref)
     worst = float(np.max(err - bound))
     assert np.all(np.isfinite(ours)), f"{what}: non-finite values"
     assert worst <= 0, f"{what}: max excess {worst:.3e} (max abs err {float(err.max()):.3e})"
@@ -126,10 +128,11 @@ def test_fused_matches_reference_fixture(cuda_device, case):
     o = lucid_attention(q, k, v, float(g["scale"]), float(g["eps"]))
     o.backward(_t(g["do"], cuda_device))
     torch.cuda.synchronize()
+    G = g["q"].shape[1] // g["k"].shape[1]
     assert_bf16_close(_np(o), g["o"], f"{case} O")
     assert_bf16_close(_np(q.grad), g["dq"], f"{case} dQ")
-    assert_bf16_close(_np(k.grad), g["dk"], f"{case} dK")
-    assert_bf16_close(_np(v.grad), g["dv"], f"{case} dV")
+    assert_bf16_close(_np(k.grad), g["dk"], f"{case} dK", G)
+    assert_bf16_close(_np(v.grad), g["dv"], f"{case} dV", G)
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,N,keys,qs", [
@@ -150,10 +153,11 @@ def test_fused_fwd_bwd_matches_oracle(cuda_device, B, Hq, Hkv, N, keys, qs):
     o.backward(_t(do_, cuda_device))
     torch.cuda.synchronize()
     o_ref, dq_ref, dk_ref, dv_ref = orc.lucid_fwd_bwd(q_, k_, v_, do_, s)
+    G = Hq // Hkv
     assert_bf16_close(_np(o), o_ref, "O")
     assert_bf16_close(_np(q.grad), dq_ref, "dQ")
-    assert_bf16_close(_np(k.grad), dk_ref, "dK")
-    assert_bf16_close(_np(v.grad), dv_ref, "dV")
+    assert_bf16_close(_np(k.grad), dk_ref, "dK", G)
+    assert_bf16_close(_np(v.grad), dv_ref, "dV", G)
 
 
 def test_separate_functions_compose(cuda_device):
