@@ -243,42 +243,45 @@ def main(argv=None):
     tflops = fl / (ms * 1e-3) / 1e12
 
     # ---- per-kernel timing (dominant kernel -> roofline) ----
+    # algorithmic GEMM work of each kernel in units of N^2 D per (batch, head)
+    # (causal: each GEMM over the lower triangle is N^2 D flops); the row
+    # passes recompute S and dP, which is executed but not algorithmic work.
     pk_burst, pk_sust, hbm, pk_kind = peaks()
-    per_stage_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 5, "solve_bwd": 5}
+    per_stage_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": 1,
+                       "solve_bwd": 4, "solve_bwd_row": 1}
+    executed_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": 3,
+                      "solve_bwd": 4, "solve_bwd_row": 3}
     stage_ms = {}
     with torch.no_grad():
         x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
         o, lse = attn_fwd(q, k, x, s)
         dq, dkf, dxf = attn_bwd(q, k, x, o, do, lse, s)
         torch.cuda.synchronize()
-        reps = 3
-        for name in ("solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd"):
+        runs = {
+            "prep": lambda: solve_fwd(k, v, s, 1e-5),
+            "solve_fwd": lambda: solve_fwd(k, v, s, 1e-5),
+            "attn_fwd": lambda: attn_fwd(q, k, x, s),
+            "attn_bwd": lambda: attn_bwd(q, k, x, o, do, lse, s),
+            "attn_bwd_row": lambda: attn_bwd(q, k, x, o, do, lse, s),
+            "solve_bwd": lambda: solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf),
+            "solve_bwd_row": lambda: solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf),
+        }
+        for name, fn in runs.items():
             lib.lucid_profile_enable(_lib.KERNEL_IDS[name])
-            for _ in range(reps):
-                if name == "solve_fwd":
-                    solve_fwd(k, v, s, 1e-5)
-                elif name == "attn_fwd":
-                    attn_fwd(q, k, x, s)
-                elif name == "attn_bwd":
-                    attn_bwd(q, k, x, o, do, lse, s)
-                else:
-                    solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf)
+            for _ in range(3):
+                fn()
             torch.cuda.synchronize()
             tot, n = ctypes.c_float(), ctypes.c_int()
             lib.lucid_profile_read(ctypes.byref(tot), ctypes.byref(n))
             stage_ms[name] = tot.value / max(n.value, 1)
         lib.lucid_profile_enable(0)
-        lib.lucid_profile_enable(_lib.KERNEL_IDS["prep"])
-        solve_fwd(k, v, s, 1e-5)
-        torch.cuda.synchronize()
-        tot, n = ctypes.c_float(), ctypes.c_int()
-        lib.lucid_profile_read(ctypes.byref(tot), ctypes.byref(n))
-        stage_ms["prep"] = tot.value / max(n.value, 1)
-        lib.lucid_profile_enable(0)
         del x, khat, u, rstd, dinv, o, lse, dq, dkf, dxf
+    unit_flops = float(N) * N * D * B * H
+    stage_tflops = {n: {"alg": per_stage_flops[n] * unit_flops / (stage_ms[n] * 1e-3) / 1e12,
+                        "executed": executed_flops[n] * unit_flops / (stage_ms[n] * 1e-3) / 1e12}
+                    for n in per_stage_flops}
     dom = max(per_stage_flops, key=lambda n: stage_ms[n])
-    dom_flops = per_stage_flops[dom] * float(N) * N * D * B * H
-    achieved = dom_flops / (stage_ms[dom] * 1e-3) / 1e12
+    achieved = stage_tflops[dom]["alg"]
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -307,7 +310,7 @@ def main(argv=None):
     e1.record()
     torch.cuda.synchronize()
     sdpa_ms = e0.elapsed_time(e1) / 3
-    our_attn_ms = stage_ms["attn_fwd"] + stage_ms["attn_bwd"]
+    our_attn_ms = stage_ms["attn_fwd"] + stage_ms["attn_bwd"] + stage_ms["attn_bwd_row"]
     del qd, kd, vd
 
     # ---- end to end through the public API with host buffers ----
@@ -359,7 +362,8 @@ def main(argv=None):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    launches_per_step = 8  # prep, solve, attn fwd, delta, attn bwd, dq convert, solve bwd, finalize
+    # prep, solve, attn fwd, delta, attn bwd col + row, solve bwd col + row, finalize
+    launches_per_step = 9
     line = {
         "metric": METRIC,
         "value": tflops,
@@ -384,6 +388,7 @@ def main(argv=None):
                                     "ratio_vs_sdpa": ms / sdpa_ms, "our_attention_only_ms": our_attn_ms,
                                     "ratio_vs_our_attention": ms / our_attn_ms},
         "stage_ms": stage_ms,
+        "stage_tflops": stage_tflops,
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": pk_burst,
                      "unit": "TFLOP/s", "frac": achieved / pk_burst, "traffic": traffic,
                      "peak_kind": f"{pk_kind} burst bf16 (kernel timed alone)"},

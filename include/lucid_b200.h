@@ -135,8 +135,10 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale,
 #define LUCID_KERNEL_PREP 1       /* row statistics + diagonal-block inverses */
 #define LUCID_KERNEL_SOLVE_FWD 2  /* wavefront solve X = P^-1 V */
 #define LUCID_KERNEL_ATTN_FWD 3   /* causal attention forward */
-#define LUCID_KERNEL_ATTN_BWD 4   /* attention backward */
-#define LUCID_KERNEL_SOLVE_BWD 5  /* transposed-solve backward */
+#define LUCID_KERNEL_ATTN_BWD 4       /* attention backward, column pass (dK, dX) */
+#define LUCID_KERNEL_SOLVE_BWD 5      /* transposed-solve wavefront (dV, dK^ columns) */
+#define LUCID_KERNEL_ATTN_BWD_ROW 6   /* attention backward, row pass (dQ) */
+#define LUCID_KERNEL_SOLVE_BWD_ROW 7  /* solve backward, row pass (dK^ rows) */
 int lucid_profile_enable(int kernel);
 int lucid_profile_read(float* total_ms, int* launches);
 
@@ -146,7 +148,8 @@ int lucid_profile_read(float* total_ms, int* launches);
  * extra int32 status word after the 128*128 results.  a_mn / b_mn select
  * the operand majorness (0: A is used as is / B^T; 1: A^T / B), i.e.
  *   (0,0) D = A B^T   (0,1) D = A B   (1,0) D = A^T B^T   (1,1) D = A^T B.
- * `via_tma` loads the operands with TMA instead of thread stores.
+ * via_tma: 0 = operands written by threads, 1 = loaded with TMA,
+ * 2 = as 1 but A is staged in tensor memory (the TS form of the MMA).
  */
 int lucid_selftest_umma(const void* a, const void* b, float* d, int a_mn, int b_mn,
                         int via_tma, void* stream);

@@ -13,7 +13,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "liblucid_b200.so")
 
 LUCID_OK = 0
-KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bwd": 5}
+KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bwd": 5, "attn_bwd_row": 6,
+              "solve_bwd_row": 7}
 ERRORS = {
     1: "unsupported shape (head_dim must be 128, Hq a multiple of Hkv)",
     2: "pointer or stride not 16-byte aligned",

@@ -1,7 +1,7 @@
 // extern "C" entry points of liblucid_b200.so (declared in
 // include/lucid_b200.h): argument checks, workspace carving, TMA descriptor
 // creation and the launch sequence of each stage.
-#include "../../include/lucid_b200.h"
+#include "lucid_b200.h"
 #include "lucid_common.cuh"
 #include "tmap.h"
 
@@ -9,14 +9,13 @@ namespace lb {
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
-cudaError_t launch_bwd(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2,
-                       const CUtensorMap& tB1, const CUtensorMap& tB2, const CUtensorMap& tU,
-                       const BwdArgs& a, cudaStream_t st);
+cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a, cudaStream_t st);
+cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
+                           const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st);
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
                          long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
                          long long d_sn, float* delta, cudaStream_t st);
-cudaError_t launch_f32_to_bf16(int B, int H, int N, int Npad, float scale, const float* src, bf16* dst,
-                               long long sb, long long sh, long long sn, cudaStream_t st);
 cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const bf16* k, long long k_sb,
                                   long long k_sh, long long k_sn, const float* rstd, const float* dinv,
                                   const bf16* x, const bf16* dv_int, const float* dk_col,
@@ -223,7 +222,7 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
 size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
   (void)Hkv; (void)D;
   const size_t rows = (size_t)B * Hq * npad_of(N);
-  return kStatusRegion + align256(rows * sizeof(float)) + align256(rows * kHeadDim * sizeof(float));
+  return kStatusRegion + align256(rows * sizeof(float));
 }
 
 int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
@@ -243,14 +242,10 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
     return LUCID_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int NB = nb_of(N), Npad = npad_of(N);
-  const size_t rows = (size_t)B * Hq * Npad;
   char* ws = static_cast<char*>(workspace);
   int* status = reinterpret_cast<int*>(ws);
   float* delta = reinterpret_cast<float*>(ws + kStatusRegion);
-  float* dq_acc = reinterpret_cast<float*>(ws + kStatusRegion + align256(rows * sizeof(float)));
   if (cudaMemsetAsync(ws, 0, kStatusRegion, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
-  if (cudaMemsetAsync(dq_acc, 0, rows * kHeadDim * sizeof(float), st) != cudaSuccess)
-    return LUCID_ERR_LAUNCH;
   cudaError_t e = launch_delta(B, Hq, N, Npad, static_cast<const bf16*>(o), o_sb, o_sh, o_sn,
                                static_cast<const bf16*>(dout), do_sb, do_sh, do_sn, delta, st);
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
@@ -263,15 +258,16 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
   ba.lse = lse; ba.delta = delta;
-  ba.dx = dx_f32; ba.dk_col = dk_f32; ba.d_row = dq_acc;
+  ba.dx = dx_f32; ba.dk_col = dk_f32;
+  ba.dq = static_cast<bf16*>(dq); ba.dq_sb = dq_sb; ba.dq_sh = dq_sh; ba.dq_sn = dq_sn;
   ba.status = status;
   {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
-    e = launch_bwd(false, tK, tX, tQ, tDO, tX, ba, st);
+    e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
-  return to_status(launch_f32_to_bf16(B, Hq, N, Npad, scale, dq_acc, static_cast<bf16*>(dq), dq_sb, dq_sh,
-                                      dq_sn, st));
+  ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
+  return to_status(launch_bwd_row(false, tQ, tDO, tK, tX, ba, st));
 }
 
 // ---------------------------------------------------------------------------
@@ -311,10 +307,8 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   float* dk_col = reinterpret_cast<float*>(ws + off);
   off += align256(rows * kHeadDim * sizeof(float));
   float* dk_row = reinterpret_cast<float*>(ws + off);
-  // status + flags, and the atomic row accumulator start at zero
+  // status word and the dependency flags start at zero
   if (cudaMemsetAsync(ws, 0, kStatusRegion + align256((size_t)B * H * NB * sizeof(int)), st) != cudaSuccess)
-    return LUCID_ERR_LAUNCH;
-  if (cudaMemsetAsync(dk_row, 0, rows * kHeadDim * sizeof(float), st) != cudaSuccess)
     return LUCID_ERR_LAUNCH;
   CUtensorMap tK, tX, tDV, tU;
   if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
@@ -323,14 +317,19 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   BwdArgs ba{};
   ba.B = B; ba.Hq = H; ba.Hkv = H; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
-  ba.dk_col = dk_col; ba.d_row = dk_row;
+  ba.dk_col = dk_col; ba.dk_row = dk_row;
   ba.dinv = dinv; ba.dx_in = dx_f32; ba.dv = dv_int;
   ba.flags = flags;
   ba.status = status;
   cudaError_t e;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    e = launch_bwd(true, tK, tX, tK, tDV, tU, ba, st);
+    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st);
+  }
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+  {
+    ProfileScope ps(LUCID_KERNEL_SOLVE_BWD_ROW, st);
+    e = launch_bwd_row(true, tK, tDV, tK, tX, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   return to_status(launch_solve_finalize(
@@ -367,7 +366,7 @@ __global__ void __launch_bounds__(128, 1)
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_alloc(smem_u32(tmem_slot), 256);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -375,7 +374,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
-  if (via_tma) {
+  if (via_tma == 1 || via_tma == 2) {
     if (r == 0) {
       mbar_arrive_expect_tx(bar_tma, 65536);
       tma_load_tile(sA, &tA, bar_tma, 0, 0, 0);
@@ -396,10 +395,34 @@ __global__ void __launch_bounds__(128, 1)
     }
     fence_proxy_async_smem();
   }
+  // mode 2: A goes to TMEM columns [128, 256) in the split-half packed
+  // layout (row elements [64h, 64h+64) packed into columns 128 + 64h + [0, 32))
+  if (via_tma == 2) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float va[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ld_bf16x8(a + r * 128 + h * 64 + q * 32 + c * 8, va + c * 8);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(va[2 * e], va[2 * e + 1]);
+        tmem_st16(tmem + ((uint32_t)(warp * 32) << 16) + 128u + 64u * h + 16u * q, pk);
+      }
+    }
+    tmem_st_wait();
+    tc_fence_before();
+  }
   __syncthreads();
   if (r == 0 && ok) {
     tc_fence_after();
-    umma_tile(tmem, sA, a_mn != 0, sB, b_mn != 0, 0u);
+    if (via_tma == 2) {
+      umma_tile_ts(tmem, [&](int kk) { return tmem + 128u + 64u * (kk >> 2) + 8u * (kk & 3); }, sB,
+                   b_mn != 0, 0u);
+    } else {
+      umma_tile(tmem, sA, a_mn != 0, sB, b_mn != 0, 0u);
+    }
     umma_commit(bar_mma);
   }
   ok = ok && mbar_wait(bar_mma, 0, ab);
@@ -420,7 +443,7 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 

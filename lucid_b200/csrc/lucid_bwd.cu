@@ -1,47 +1,36 @@
-// Backward tile engine: one persistent, warp-specialised tcgen05 kernel
-// template for the two column-oriented loops of the LUCID backward.
+// Backward tile engines of LUCID attention: two persistent, warp-specialised
+// tcgen05 kernels per backward, a column pass and a row pass, with no
+// atomics anywhere.
 //
-//   ATTN  (backward of modeling_lucid.py:505-549, O = softmax(s Q K^T) X)
-//     column = key block i of kv head hk; tiles = (query head g of the
-//     group, query block j >= i).  With A1 = K_i, A2 = X_i, B1 = Q_j,
-//     B2 = dO_j:
-//       S^T = A1 B1^T, P = exp2(S^T s log2e - lse_j)      (causal mask)
-//       dP^T = A2 B2^T, dS = P (dP^T - delta_j)
-//       dX_i += P B2 ;  dK_i += dS B1 ;  dQ_j += dS^T A1 (fp32 atomics)
+// Attention backward (of O = softmax(s Q K^T + causal) X, modeling_lucid.py:505-549)
+//   column pass, key block i of kv head hk, tiles = (query head g, block j >= i):
+//     S^T = K_i Q_j^T, P = exp2(S^T s log2e - lse_j) (causal),  dP^T = X_i dO_j^T,
+//     dS = P (dP^T - delta_j);   dX_i += P dO_j,   dK_i += s dS Q_j
+//   row pass, query block j of head hq, tiles = key blocks i <= j:
+//     S = Q_j K_i^T, P = exp2(S s log2e - lse), dP = dO_j X_i^T,
+//     dS = P (dP - delta);       dQ_j += s dS K_i
 //
-//   SOLVE (backward of X = P^-1 V, modeling_lucid.py:314-382)
-//     column = block i; tiles j = NB-1 .. i+1 (waiting for dV_j); with
-//     A1 = K^_i, A2 = X_i, B1 = K^_j, B2 = dV_j:
-//       E = exp(s A1 B1^T - 1/s),  D = A2 B2^T,  dG^T = -s E o D
-//       acc_i += E B2 ;  dK^_i += dG^T B1 ;  dK^_j += dG A1 (fp32 atomics)
-//     then the diagonal block:
-//       R = dX_i - acc_i ;  dV_i = D_i^-1 (R + U_i^T R)   (publish flag)
-//       dG_ii (strictly lower) and  dK^_i += dG_ii^T K^_i + dG_ii K^_i.
-//     The diagonal entries P_rr are handled exactly in fp32 by the
-//     finalize kernel.
+// Solve backward (of X = P^-1 V, modeling_lucid.py:314-382)
+//   column pass = the transposed (back-substitution) solve, a wavefront over
+//   column blocks i = NB-1 .. 0 that waits for every dV_j (j > i):
+//     E = exp(s K^_i K^_j^T - 1/s),  D = X_i dV_j^T,  dG^T = -s E o D
+//     acc_i += E dV_j,  dK^col_i += dG^T K^_j
+//     then R = dX_i - acc_i,  dV_i = D_i^-1 (R + U_i^T R)  (published), and the
+//     strictly-lower part of the diagonal block: dK^col_i += dG_ii^T K^_i + dG_ii K^_i
+//   row pass (after all dV are final), row block j, tiles i < j:
+//     E = exp(s K^_j K^_i^T - 1/s),  D = dV_j X_i^T,  dG = -s E o D,  dK^row_j += dG K^_i
+//   The diagonal entries P_rr enter exactly in fp32 in the finalize kernel.
 //
-// Warp roles as in the forward: warps 0-3 epilogue (thread = tile row),
-// warp 4 TMA producer, warp 5 MMA issuer.  TMEM: S/T 0, dP 128, acc1 256,
-// acc2 384.
+// Both passes: warps 0-7 are the epilogue (warp w reads TMEM lanes of
+// sub-partition w%4 = tile rows 32(w%4).., column half w/4), warp 8 issues
+// TMA, warp 9 issues tcgen05.mma.  P and dS return to tensor memory as packed
+// bf16 and feed the next GEMMs as the A operand (TS form); the next tile's
+// S / dP GEMMs are issued while the epilogue of the current tile runs.
 #include "lucid_common.cuh"
 
 #include <algorithm>
 
 namespace lb {
-
-namespace bwd {
-constexpr int kThreads = 192;
-constexpr uint32_t kOffA1 = 0, kOffA2 = 32768, kOffB1 = 65536, kOffB2 = 98304;
-constexpr uint32_t kOffP = 131072, kOffDS = 163840, kOffVec = 196608;  // vec: lse[128], delta[128]
-constexpr uint32_t kOffBar = kOffVec + 1024;
-enum {
-  A_FULL = 0, A_EMPTY, KV_FULL, KV_EMPTY, SD_FULL, DP_FREE, PD_FULL, PD_FREE, T_FULL, T_FREE,
-  ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR
-};
-constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16 + 1024;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
-}  // namespace bwd
 
 // Phase bookkeeping for one mbarrier as seen by one role.
 struct Ph {
@@ -55,41 +44,77 @@ __device__ __forceinline__ bool warp_wait_b(uint32_t bar, uint32_t parity, const
   return __all_sync(0xffffffffu, ok);
 }
 
+// Packed bf16 operands written back into a 128-column TMEM region by the
+// epilogue.  Warp half h owns columns [64h, 64h+64); its 32-column chunk q
+// ([64h+32q, +32)) holds the packed values of tile columns [64h+32q, +32) in
+// its first 16 columns and a second operand in the next 16.  Every warp
+// writes only columns it has already read, so no cross-warp ordering is
+// needed.  K-slice kk (16 tile columns) of the first operand:
+__device__ __forceinline__ uint32_t packed_kslice(uint32_t region, int kk) {
+  return region + 64u * (uint32_t)(kk >> 2) + 32u * (uint32_t)((kk >> 1) & 1) + 8u * (uint32_t)(kk & 1);
+}
+
+constexpr int kBwdEpiWarps = 8;
+constexpr int kBwdEpiThreads = kBwdEpiWarps * 32;
+constexpr int kBwdThreads = kBwdEpiThreads + 64;
+constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1;
+
+// ===========================================================================
+// column pass
+// ===========================================================================
+namespace bwdc {
+constexpr uint32_t kOffA1 = 0, kOffA2 = 32768;
+constexpr uint32_t kOffStage = 65536;        // stage s: B1 at +s*65536, B2 at +32768
+constexpr uint32_t kOffDS = 196608;          // R / dV / dG^T tile of the diagonal steps
+constexpr uint32_t kOffVec = 229376;         // stage s: lse[128], delta[128] at +s*1024
+constexpr uint32_t kOffBar = kOffVec + 2048;
+enum {
+  A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_READ, PD_FULL, DS_FREE,
+  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR
+};
+constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
+}  // namespace bwdc
+
 template <bool SOLVE>
-__global__ void __launch_bounds__(bwd::kThreads, 1)
-    lucid_bwd_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
-                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
-                     const __grid_constant__ CUtensorMap tmU, BwdArgs p) {
-  using namespace bwd;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = (raw + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (sbase - raw);
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    lucid_bwd_col_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
+                         const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                         const __grid_constant__ CUtensorMap tmU, BwdArgs p) {
+  using namespace bwdc;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
-  const float* svec = reinterpret_cast<const float*>(smem + kOffVec);
-  const Abort ab{abort_cta, p.status};
-  const uint32_t sA1 = sbase + kOffA1, sA2 = sbase + kOffA2, sB1 = sbase + kOffB1,
-                 sB2 = sbase + kOffB2, sP = sbase + kOffP, sDS = sbase + kOffDS;
+  const Abort ab{abort_cta, p.status, SOLVE ? kTagBwdColSolve : kTagBwdColAttn};
+  const uint32_t sA1 = sbase + kOffA1, sA2 = sbase + kOffA2, sDS = sbase + kOffDS;
+  auto sB1 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u; };
+  auto sB2 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u + 32768u; };
 
   const int warp = warp_id(), lane = lane_id();
-  if (threadIdx.x == 128) {
+  if ((sbase & 1023u) != 0) {  // the tile layout needs a 1024-byte aligned window
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | ((SOLVE ? 1 : 0) << 20));
+    return;
+  }
+  if (threadIdx.x == kBwdWarpTma * 32) {
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
-    mbar_init(bar(KV_FULL), 1);
-    mbar_init(bar(KV_EMPTY), 1);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(bar(KV_FULL0 + s2), 1);
+      mbar_init(bar(KV_EMPTY0 + s2), 1);
+    }
     mbar_init(bar(SD_FULL), 1);
-    mbar_init(bar(DP_FREE), 128);
-    mbar_init(bar(PD_FULL), 128);
-    mbar_init(bar(PD_FREE), 1);
+    mbar_init(bar(DP_READ), kBwdEpiThreads);
+    mbar_init(bar(PD_FULL), kBwdEpiThreads);
+    mbar_init(bar(DS_FREE), 1);
     mbar_init(bar(T_FULL), 1);
-    mbar_init(bar(T_FREE), 128);
+    mbar_init(bar(S_FREE), kBwdEpiThreads);
     mbar_init(bar(ACC_FULL), 1);
     mbar_init(bar(ACC2_FULL), 1);
-    mbar_init(bar(ACC_FREE), 128);
-    mbar_init(bar(EPI_DONE), 128);
+    mbar_init(bar(ACC_FREE), kBwdEpiThreads);
+    mbar_init(bar(EPI_DONE), kBwdEpiThreads);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -99,8 +124,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     tma_prefetch_desc(&tmB2);
     if (SOLVE) tma_prefetch_desc(&tmU);
   }
-  if (warp == 5) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+  if (warp == kBwdWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -117,9 +142,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     b = bh / p.Hkv;
     hk = bh % p.Hkv;
   };
-  // number of off-diagonal (solve) / all (attention) tiles of column i
   auto ntiles = [&](int i) { return SOLVE ? (p.NB - 1 - i) : G * (p.NB - i); };
-  // tile t of column i -> (query head offset g, row block j)
   auto tile_at = [&](int i, int t, int& g, int& j) {
     if (SOLVE) {
       g = 0;
@@ -131,12 +154,12 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     }
   };
 
-  if (warp == 4) {
+  if (warp == kBwdWarpTma) {
     // ======================= TMA producer =======================
     if (lane == 0) {
-      Ph a_empty, kv_empty;
-      int last_a = -1, last_kv = -1;
-      uint32_t n_a = 0, n_kv = 0;
+      Ph a_empty;
+      uint32_t n_kv = 0, n_a = 0;
+      int last_a = -1, last_kv[2] = {-1, -1};
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         int i, b, hk;
@@ -147,68 +170,93 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         tma_load_tile(sA1, &tmA1, bar(A_FULL), i * 128, hk, b);
         tma_load_tile(sA2, &tmA2, bar(A_FULL), i * 128, hk, b);
         const int T = ntiles(i);
-        for (int t = 0; t < T; ++t) {
-          int g, j;
-          tile_at(i, t, g, j);
-          if (SOLVE) {
-            if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + j], 1, ab)) { ok = false; break; }
-            fence_proxy_async_global();
-          }
-          if (!mbar_wait(bar(KV_EMPTY), kv_empty.empty(), ab)) { ok = false; break; }
-          last_kv = n_kv++ & 1;
-          if (SOLVE) {
-            mbar_arrive_expect_tx(bar(KV_FULL), 65536);
-            tma_load_tile(sB1, &tmB1, bar(KV_FULL), j * 128, hk, b);
-            tma_load_tile(sB2, &tmB2, bar(KV_FULL), j * 128, hk, b);
+        for (int t = 0; t < T + (SOLVE ? 1 : 0); ++t, ++n_kv) {
+          const int st = n_kv & 1;
+          const uint32_t use = n_kv >> 1;
+          if (t < T) {
+            int g, j;
+            tile_at(i, t, g, j);
+            if (SOLVE) {
+              if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + j], 1, ab)) { ok = false; break; }
+              fence_proxy_async_global();
+            }
+            if (!mbar_wait(bar(KV_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+            last_kv[st] = use & 1;
+            if (SOLVE) {
+              mbar_arrive_expect_tx(bar(KV_FULL0 + st), 65536);
+              tma_load_tile(sB1(st), &tmB1, bar(KV_FULL0 + st), j * 128, hk, b);
+              tma_load_tile(sB2(st), &tmB2, bar(KV_FULL0 + st), j * 128, hk, b);
+            } else {
+              const int hq = hk * G + g;
+              const long long voff = ((long long)b * p.Hq + hq) * p.Npad + (long long)j * 128;
+              mbar_arrive_expect_tx(bar(KV_FULL0 + st), 65536 + 1024);
+              tma_load_tile(sB1(st), &tmB1, bar(KV_FULL0 + st), j * 128, hq, b);
+              tma_load_tile(sB2(st), &tmB2, bar(KV_FULL0 + st), j * 128, hq, b);
+              bulk_load(sbase + kOffVec + (uint32_t)st * 1024u, p.lse + voff, 512, bar(KV_FULL0 + st));
+              bulk_load(sbase + kOffVec + (uint32_t)st * 1024u + 512u, p.delta + voff, 512,
+                        bar(KV_FULL0 + st));
+            }
           } else {
-            const int hq = hk * G + g;
-            const long long voff = ((long long)b * p.Hq + hq) * p.Npad + (long long)j * 128;
-            mbar_arrive_expect_tx(bar(KV_FULL), 65536 + 1024);
-            tma_load_tile(sB1, &tmB1, bar(KV_FULL), j * 128, hq, b);
-            tma_load_tile(sB2, &tmB2, bar(KV_FULL), j * 128, hq, b);
-            bulk_load(sbase + kOffVec, p.lse + voff, 512, bar(KV_FULL));
-            bulk_load(sbase + kOffVec + 512, p.delta + voff, 512, bar(KV_FULL));
+            // solve: diagonal-block inverse U_i into the stage's B1 slot
+            if (!mbar_wait(bar(KV_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+            last_kv[st] = use & 1;
+            mbar_arrive_expect_tx(bar(KV_FULL0 + st), 32768);
+            tma_load_tile(sB1(st), &tmU, bar(KV_FULL0 + st), i * 128, hk, b);
           }
-        }
-        if (!ok) break;
-        if (SOLVE) {
-          if (!mbar_wait(bar(KV_EMPTY), kv_empty.empty(), ab)) break;
-          last_kv = n_kv++ & 1;
-          mbar_arrive_expect_tx(bar(KV_FULL), 32768);
-          tma_load_tile(sB1, &tmU, bar(KV_FULL), i * 128, hk, b);
         }
       }
       if (last_a >= 0) mbar_wait_timed(bar(A_FULL), (uint32_t)last_a, kDrainNs);
-      if (last_kv >= 0) mbar_wait_timed(bar(KV_FULL), (uint32_t)last_kv, kDrainNs);
+      for (int s2 = 0; s2 < 2; ++s2)
+        if (last_kv[s2] >= 0) mbar_wait_timed(bar(KV_FULL0 + s2), (uint32_t)last_kv[s2], kDrainNs);
     }
-  } else if (warp == 5) {
+  } else if (warp == kBwdWarpMma) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      Ph a_full, kv_full, t_free, dp_free, pd_full, acc_free;
+      Ph a_full, dp_read, pd_full, acc_free, s_free;
+      uint32_t n_kv = 0;
+      bool pending_dp_read = false;  // a dP read whose release the next dP write must await
+      bool first_item = true;
+      const uint32_t tS = tmem + kTmS, tDP = tmem + kTmDP;
+      auto issue_sd = [&](int st) {
+        umma_tile(tDP, sA2, false, sB2(st), false, 0u);  // dP = A2 B2^T
+        umma_tile(tS, sA1, false, sB1(st), false, 0u);   // S  = A1 B1^T
+        umma_commit(bar(SD_FULL));
+      };
       for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
         int i, b, hk;
         decode(idx, i, b, hk);
         const int T = ntiles(i);
         if (!mbar_wait(bar(A_FULL), a_full.full(), ab)) break;
+        // solve: the previous item's diagonal steps read S / dP last
+        // (S_FREE completes in D3 and D5 of every solve item; waits consume them in order)
+        if (SOLVE && !first_item && !mbar_wait(bar(S_FREE), s_free.full(), ab)) break;
+        first_item = false;
         bool ok = true;
-        for (int t = 0; t < T; ++t) {
-          if (!mbar_wait(bar(KV_FULL), kv_full.full(), ab) ||
-              !mbar_wait(bar(T_FREE), t_free.empty(), ab) ||
-              !mbar_wait(bar(DP_FREE), dp_free.empty(), ab)) { ok = false; break; }
+        if (T > 0) {
+          const int st = n_kv & 1;
+          if (!mbar_wait(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) break;
+          if (pending_dp_read && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) break;
           tc_fence_after();
-          umma_tile(tmem + kTmS, sA1, false, sB1, false, 0u);   // S  = A1 B1^T
-          umma_tile(tmem + kTmDP, sA2, false, sB2, false, 0u);  // dP = A2 B2^T
-          umma_commit(bar(SD_FULL));
+          issue_sd(st);
+          pending_dp_read = true;
+        }
+        for (int t = 0; t < T; ++t, ++n_kv) {
+          const int st = n_kv & 1;
           if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) { ok = false; break; }
           if (t == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
           tc_fence_after();
           const uint32_t acc = t > 0 ? 1u : 0u;
-          umma_tile(tmem + kTmAcc1, sP, false, sB2, true, acc);   // acc1 += P B2
-          umma_tile(tmem + kTmAcc2, sDS, false, sB1, true, acc);  // acc2 += dS B1
-          umma_commit(bar(KV_EMPTY));
-          umma_tile(tmem + kTmS, sDS, true, sA1, true, 0u);       // T = dS^T A1
-          umma_commit(bar(T_FULL));
-          umma_commit(bar(PD_FREE));
+          // acc1 += P B2, acc2 += dS B1 (P, dS packed in the S region)
+          umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk); }, sB2(st), true, acc);
+          umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tS, kk) + 16u; }, sB1(st), true, acc);
+          umma_commit(bar(KV_EMPTY0 + st));
+          if (t + 1 < T) {
+            const int st2 = (n_kv + 1) & 1;
+            if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab) ||
+                !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
+            tc_fence_after();
+            issue_sd(st2);
+          }
         }
         if (!ok) break;
         umma_commit(bar(ACC_FULL));
@@ -217,31 +265,32 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           continue;
         }
         // ---- diagonal block of the transposed solve ----
-        // D2: T' = U^T R
-        if (!mbar_wait(bar(KV_FULL), kv_full.full(), ab) ||
-            !mbar_wait(bar(PD_FULL), pd_full.full(), ab) ||
-            !mbar_wait(bar(T_FREE), t_free.empty(), ab)) break;
+        const int st = n_kv & 1;
+        const uint32_t use = n_kv >> 1;
+        ++n_kv;
+        // D2: T' = U^T R   (S region; its last readers were G3/G4 or the previous item)
+        if (!mbar_wait(bar(KV_FULL0 + st), use & 1, ab) || !mbar_wait(bar(PD_FULL), pd_full.full(), ab)) break;
         tc_fence_after();
-        umma_tile(tmem + kTmS, sB1, true, sP, true, 0u);
+        umma_tile(tS, sB1(st), true, sDS, true, 0u);
         umma_commit(bar(T_FULL));
-        umma_commit(bar(PD_FREE));
-        umma_commit(bar(KV_EMPTY));
+        umma_commit(bar(DS_FREE));
+        umma_commit(bar(KV_EMPTY0 + st));
         // D4: S' = K^_i K^_i^T ; D' = X_i dV_i^T
-        if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab) ||
-            !mbar_wait(bar(T_FREE), t_free.empty(), ab) ||
-            !mbar_wait(bar(DP_FREE), dp_free.empty(), ab)) break;
+        if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab) || !mbar_wait(bar(S_FREE), s_free.full(), ab)) break;
+        if (pending_dp_read && T > 0 && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) break;
+        pending_dp_read = false;
         tc_fence_after();
-        umma_tile(tmem + kTmS, sA1, false, sA1, false, 0u);
-        umma_tile(tmem + kTmDP, sA2, false, sDS, false, 0u);
+        umma_tile(tS, sA1, false, sA1, false, 0u);
+        umma_tile(tDP, sA2, false, sDS, false, 0u);
         umma_commit(bar(SD_FULL));
-        umma_commit(bar(PD_FREE));
+        umma_commit(bar(DS_FREE));
         // D6: acc2 += dG^T K^_i + dG K^_i
         if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) break;
         if (T == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) break;
         tc_fence_after();
-        umma_tile(tmem + kTmAcc2, sP, false, sA1, true, T > 0 ? 1u : 0u);
-        umma_tile(tmem + kTmAcc2, sP, true, sA1, true, 1u);
-        umma_commit(bar(PD_FREE));
+        umma_tile(tmem + kTmAcc2, sDS, false, sA1, true, T > 0 ? 1u : 0u);
+        umma_tile(tmem + kTmAcc2, sDS, true, sA1, true, 1u);
+        umma_commit(bar(DS_FREE));
         umma_commit(bar(A_EMPTY));
         umma_commit(bar(ACC2_FULL));
       }
@@ -249,86 +298,91 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
   } else {
-    // ======================= epilogue warps 0-3 =======================
-    const int r = threadIdx.x;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // ======================= epilogue warps 0-7 =======================
+    const int sp = warp & 3, h = warp >> 2;
+    const int r = sp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    const uint32_t c0 = 64u * (uint32_t)h;
     const float kLog2e = 1.4426950408889634f;
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
-    Ph kv_full, sd_full, pd_free, t_full, acc_full, acc2_full;
-    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+    Ph sd_full, ds_free, t_full, acc_full, acc2_full;
+    uint32_t n_kv = 0, item = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
       int i, b, hk;
       decode(idx, i, b, hk);
       const int T = ntiles(i);
       const long long bhk = (long long)b * p.Hkv + hk;
-      const int row_i = i * 128 + r;  // this thread's row of column block i
+      const int row_i = i * 128 + r;
       bool ok = true;
-      for (int t = 0; t < T; ++t) {
+      for (int t = 0; t < T; ++t, ++n_kv) {
         int g, j;
         tile_at(i, t, g, j);
-        if (!SOLVE && !warp_wait_b(bar(KV_FULL), kv_full.full(), ab)) { ok = false; break; }
-        if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab) ||
-            !warp_wait_b(bar(PD_FREE), pd_free.empty(), ab)) { ok = false; break; }
+        const int st = n_kv & 1;
+        if (!SOLVE && !warp_wait_b(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) { ok = false; break; }
+        if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
+        float dv[2][32];
+        tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
+        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(DP_READ));
+        const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
+        const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
+                                : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float sv[32], dv[32];
-          tmem_ld32(tmem + lane_base + kTmS + 32u * q, sv);
-          tmem_ld32(tmem + lane_base + kTmDP + 32u * q, dv);
+        for (int q = 0; q < 2; ++q) {
+          float sv[32];
+          tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, sv);
           tmem_ld_wait();
+          const int cb = (int)c0 + 32 * q;
+          uint32_t pk[16], dk[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int c = q * 32 + e;      // column within the tile (query / key of block j)
-            const int colg = j * 128 + c;  // global column
-            float pe, ds;
+          for (int e = 0; e < 32; e += 2) {
+            const int c = cb + e;
+            float2 arg, pe, ds;
             if (SOLVE) {
-              pe = (colg < p.N) ? fast_exp2(fmaf(sv[e], c1, -c2)) : 0.f;
-              ds = -p.scale * pe * dv[e];
+              arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+              pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+              if (!full) {
+                if (j * 128 + c >= p.N) pe.x = 0.f;
+                if (j * 128 + c + 1 >= p.N) pe.y = 0.f;
+              }
+              ds = mul2(pe, mul2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-p.scale, -p.scale)));
             } else {
-              const bool valid = (colg < p.N) && (row_i < p.N) && (colg >= row_i);
-              pe = valid ? fast_exp2(fmaf(sv[e], c1, -svec[c])) : 0.f;
-              ds = pe * (dv[e] - svec[128 + c]);
+              const float2 ls = *reinterpret_cast<const float2*>(vec + c);
+              const float2 dl = *reinterpret_cast<const float2*>(vec + 128 + c);
+              arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-ls.x, -ls.y));
+              pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+              if (!full) {
+                const int q0 = j * 128 + c;
+                if (!(q0 < p.N && row_i < p.N && q0 >= row_i)) pe.x = 0.f;
+                if (!(q0 + 1 < p.N && row_i < p.N && q0 + 1 >= row_i)) pe.y = 0.f;
+              }
+              ds = mul2(pe, add2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-dl.x, -dl.y)));
             }
-            sv[e] = pe;
-            dv[e] = ds;
+            pk[e >> 1] = pack_bf16(pe.x, pe.y);
+            dk[e >> 1] = pack_bf16(ds.x, ds.y);
           }
-          tile_store_row32(sP, r, q, sv);
-          tile_store_row32(sDS, r, q, dv);
+          tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
+          tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q + 16u, dk);
         }
+        tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(DP_FREE));
-        fence_proxy_async_smem();
         mbar_arrive(bar(PD_FULL));
-        // T rows -> fp32 atomics
-        if (!warp_wait_b(bar(T_FULL), t_full.full(), ab)) { ok = false; break; }
-        tc_fence_after();
-        const long long drow =
-            SOLVE ? (bhk * p.Npad + (long long)j * 128 + r)
-                  : (((long long)b * p.Hq + hk * G + g) * p.Npad + (long long)j * 128 + r);
-        float4* dst = reinterpret_cast<float4*>(p.d_row + drow * kHeadDim);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float tv[32];
-          tmem_ld32(tmem + lane_base + kTmS + 32u * q, tv);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            atomicAdd(dst + q * 8 + c, make_float4(tv[4 * c], tv[4 * c + 1], tv[4 * c + 2], tv[4 * c + 3]));
-        }
-        tc_fence_before();
-        mbar_arrive(bar(T_FREE));
       }
       if (!ok) break;
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
       tc_fence_after();
       if (!SOLVE) {
-        float* dxr = p.dx + (bhk * p.Npad + row_i) * kHeadDim;
-        float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim;
+        float* dxr = p.dx + (bhk * p.Npad + row_i) * kHeadDim + c0;
+        float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
           float a1[32], a2[32];
-          tmem_ld32(tmem + lane_base + kTmAcc1 + 32u * q, a1);
-          tmem_ld32(tmem + lane_base + kTmAcc2 + 32u * q, a2);
+          tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
+          tmem_ld32(tmem + lane_base + kTmAcc2 + c0 + 32u * q, a2);
           tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -343,15 +397,16 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         mbar_arrive(bar(ACC_FREE));
         continue;
       }
+      ++n_kv;  // the U_i load
       // ---------------- solve: diagonal block ----------------
-      // D1: R = dX_i - acc1 -> P buffer (bf16), kept in fp32 registers
-      float rr[4][32];
-      const float* dxr = p.dx_in + (bhk * p.Npad + row_i) * kHeadDim;
+      // D1: R = dX_i - acc1 (this warp's column half), staged as bf16 for U^T R
+      float rr[2][32];
+      const float* dxr = p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float a1[32];
         if (T > 0) {
-          tmem_ld32(tmem + lane_base + kTmAcc1 + 32u * q, a1);
+          tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -366,73 +421,70 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           rr[q][4 * c + 3] = x4.w - a1[4 * c + 3];
         }
       }
-      if (!warp_wait_b(bar(PD_FREE), pd_free.empty(), ab)) break;
+      if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) break;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tile_store_row32(sP, r, q, rr[q]);
+      for (int q = 0; q < 2; ++q) tile_store_row32(sDS, r, 2 * h + q, rr[q]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar(PD_FULL));
-      // D3: dV_i = D^-1 (R + U^T R) -> global bf16 + dS buffer; publish
-      if (!warp_wait_b(bar(T_FULL), t_full.full(), ab) ||
-          !warp_wait_b(bar(PD_FREE), pd_free.empty(), ab)) break;
+      // D3: dV_i = D^-1 (R + U^T R) -> global bf16 and the smem tile; publish
+      if (!warp_wait_b(bar(T_FULL), t_full.full(), ab) || !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab))
+        break;
       tc_fence_after();
       const float di = p.dinv[bhk * p.Npad + row_i];
-      bf16* dvr = p.dv + (bhk * p.Npad + row_i) * kHeadDim;
+      bf16* dvr = p.dv + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float tv[32];
-        tmem_ld32(tmem + lane_base + kTmS + 32u * q, tv);
+        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, tv);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e) tv[e] = (rr[q][e] + tv[e]) * di;
 #pragma unroll
         for (int c = 0; c < 4; ++c) st_bf16x8(dvr + q * 32 + c * 8, tv + c * 8);
-        tile_store_row32(sDS, r, q, tv);
+        tile_store_row32(sDS, r, 2 * h + q, tv);
       }
       tc_fence_before();
-      mbar_arrive(bar(T_FREE));
+      mbar_arrive(bar(S_FREE));
       fence_proxy_async_smem();
       mbar_arrive(bar(PD_FULL));
       fence_proxy_async_global();
       __threadfence();
       mbar_arrive(bar(EPI_DONE));
-      if (r == 0) {
-        const uint32_t ph = (uint32_t)((idx - (int)blockIdx.x) / (int)gridDim.x) & 1u;
-        if (mbar_wait(bar(EPI_DONE), ph, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+      if (threadIdx.x == 0) {
+        if (mbar_wait(bar(EPI_DONE), item & 1, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
       }
       __syncwarp();
-      // D5: dG^T of the strictly-lower part of P_ii -> P buffer
-      if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab) ||
-          !warp_wait_b(bar(PD_FREE), pd_free.empty(), ab)) break;
+      // D5: dG^T of the strictly-lower part of P_ii -> smem tile
+      if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab) || !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab))
+        break;
       tc_fence_after();
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float sv[32], dv[32];
-        tmem_ld32(tmem + lane_base + kTmS + 32u * q, sv);
-        tmem_ld32(tmem + lane_base + kTmDP + 32u * q, dv);
+        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, sv);
+        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u * q, dv);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const int c = q * 32 + e;
-          const int colg = i * 128 + c;
-          const bool valid = (c > r) && (colg < p.N);
+          const int c = (int)c0 + 32 * q + e;
+          const bool valid = (c > r) && (i * 128 + c < p.N);
           sv[e] = valid ? -p.scale * fast_exp2(fmaf(sv[e], c1, -c2)) * dv[e] : 0.f;
         }
-        tile_store_row32(sP, r, q, sv);
+        tile_store_row32(sDS, r, 2 * h + q, sv);
       }
       tc_fence_before();
-      mbar_arrive(bar(T_FREE));
-      mbar_arrive(bar(DP_FREE));
+      mbar_arrive(bar(S_FREE));
       fence_proxy_async_smem();
       mbar_arrive(bar(PD_FULL));
       // D7: column part of dK^_i
       if (!warp_wait_b(bar(ACC2_FULL), acc2_full.full(), ab)) break;
       tc_fence_after();
-      float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim;
+      float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float a2[32];
-        tmem_ld32(tmem + lane_base + kTmAcc2 + 32u * q, a2);
+        tmem_ld32(tmem + lane_base + kTmAcc2 + c0 + 32u * q, a2);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 8; ++c)
@@ -446,10 +498,283 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kBwdWarpMma) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// row pass
+// ===========================================================================
+namespace bwdr {
+constexpr uint32_t kOffA1 = 0, kOffA2 = 32768;
+constexpr uint32_t kOffStage = 65536;        // stage s: B1 at +s*65536, B2 at +32768
+constexpr uint32_t kOffBar = kOffStage + 2 * 65536;
+enum { A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_READ, PD_FULL,
+       ACC_FULL, ACC_FREE, DRAIN, NBAR };
+constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmS0 = 0, kTmS1 = 128, kTmDP = 256, kTmAcc = 384;
+}  // namespace bwdr
+
+template <bool SOLVE>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    lucid_bwd_row_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
+                         const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                         BwdArgs p) {
+  using namespace bwdr;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + kOffBar;
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, SOLVE ? kTagBwdRowSolve : kTagBwdRowAttn};
+  const uint32_t sA1 = sbase + kOffA1, sA2 = sbase + kOffA2;
+  auto sB1 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u; };
+  auto sB2 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u + 32768u; };
+
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | ((SOLVE ? 1 : 0) << 20));
+    return;
+  }
+  if (threadIdx.x == kBwdWarpTma * 32) {
+    mbar_init(bar(A_FULL), 1);
+    mbar_init(bar(A_EMPTY), 1);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(bar(KV_FULL0 + s2), 1);
+      mbar_init(bar(KV_EMPTY0 + s2), 1);
+    }
+    mbar_init(bar(SD_FULL), 1);
+    mbar_init(bar(DP_READ), kBwdEpiThreads);
+    mbar_init(bar(PD_FULL), kBwdEpiThreads);
+    mbar_init(bar(ACC_FULL), 1);
+    mbar_init(bar(ACC_FREE), kBwdEpiThreads);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA1);
+    tma_prefetch_desc(&tmA2);
+    tma_prefetch_desc(&tmB1);
+    tma_prefetch_desc(&tmB2);
+  }
+  if (warp == kBwdWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // items: (row block j, head); longest rows first for balance
+  const int BH = SOLVE ? p.B * p.Hkv : p.B * p.Hq;
+  const int G = p.Hq / p.Hkv;
+  const int total = p.NB * BH;
+  auto decode = [&](int idx, int& j, int& b, int& ha, int& hk) {
+    j = p.NB - 1 - idx / BH;
+    const int bh = idx % BH;
+    if (SOLVE) {
+      b = bh / p.Hkv;
+      hk = bh % p.Hkv;
+      ha = hk;
+    } else {
+      b = bh / p.Hq;
+      ha = bh % p.Hq;
+      hk = ha / G;
+    }
+  };
+  auto ntiles = [&](int j) { return SOLVE ? j : j + 1; };  // key blocks i < j (solve) / i <= j
+
+  if (warp == kBwdWarpTma) {
+    if (lane == 0) {
+      Ph a_empty;
+      uint32_t n_kv = 0, n_a = 0;
+      int last_a = -1, last_kv[2] = {-1, -1};
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int j, b, ha, hk;
+        decode(idx, j, b, ha, hk);
+        if (!mbar_wait(bar(A_EMPTY), a_empty.empty(), ab)) break;
+        last_a = n_a++ & 1;
+        mbar_arrive_expect_tx(bar(A_FULL), 65536);
+        tma_load_tile(sA1, &tmA1, bar(A_FULL), j * 128, ha, b);
+        tma_load_tile(sA2, &tmA2, bar(A_FULL), j * 128, ha, b);
+        const int T = ntiles(j);
+        for (int t = 0; t < T; ++t, ++n_kv) {
+          const int st = n_kv & 1;
+          const uint32_t use = n_kv >> 1;
+          if (!mbar_wait(bar(KV_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+          last_kv[st] = use & 1;
+          mbar_arrive_expect_tx(bar(KV_FULL0 + st), 65536);
+          tma_load_tile(sB1(st), &tmB1, bar(KV_FULL0 + st), t * 128, hk, b);
+          tma_load_tile(sB2(st), &tmB2, bar(KV_FULL0 + st), t * 128, hk, b);
+        }
+      }
+      if (last_a >= 0) mbar_wait_timed(bar(A_FULL), (uint32_t)last_a, kDrainNs);
+      for (int s2 = 0; s2 < 2; ++s2)
+        if (last_kv[s2] >= 0) mbar_wait_timed(bar(KV_FULL0 + s2), (uint32_t)last_kv[s2], kDrainNs);
+    }
+  } else if (warp == kBwdWarpMma) {
+    if (lane == 0) {
+      Ph a_full, dp_read, pd_full, acc_free;
+      uint32_t n_kv = 0, n_s = 0;
+      bool pending_dp_read = false;
+      const uint32_t tDP = tmem + kTmDP;
+      auto tS = [&](uint32_t n) { return tmem + ((n & 1) ? kTmS1 : kTmS0); };
+      for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+        int j, b, ha, hk;
+        decode(idx, j, b, ha, hk);
+        const int T = ntiles(j);
+        if (!mbar_wait(bar(A_FULL), a_full.full(), ab)) break;
+        bool ok = true;
+        for (int t = 0; t <= T; ++t) {
+          if (t < T) {
+            // S(t) = A1 B1^T into S[n_s % 2]; dP(t) = A2 B2^T (after dP(t-1) was read)
+            const int st = (n_kv + t) & 1;
+            if (!mbar_wait(bar(KV_FULL0 + st), ((n_kv + t) >> 1) & 1, ab)) { ok = false; break; }
+            if (pending_dp_read && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
+            tc_fence_after();
+            umma_tile(tS(n_s + t), sA1, false, sB1(st), false, 0u);
+            umma_tile(tDP, sA2, false, sB2(st), false, 0u);
+            umma_commit(bar(SD_FULL));
+            pending_dp_read = true;
+          }
+          if (t >= 1) {
+            // acc += dS(t-1) B1(t-1), dS packed in S[(n_s + t - 1) % 2]
+            const int tt = t - 1;
+            const int st = (n_kv + tt) & 1;
+            if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) { ok = false; break; }
+            if (tt == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sreg = tS(n_s + tt);
+            umma_tile_ts(tmem + kTmAcc, [&](int kk) { return packed_kslice(sreg, kk); }, sB1(st), true,
+                         tt > 0 ? 1u : 0u);
+            umma_commit(bar(KV_EMPTY0 + st));
+          }
+        }
+        if (!ok) break;
+        n_kv += T;
+        n_s += T;
+        if (T == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) break;
+        umma_commit(bar(ACC_FULL));
+        umma_commit(bar(A_EMPTY));
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    const int sp = warp & 3, h = warp >> 2;
+    const int r = sp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    const uint32_t c0 = 64u * (uint32_t)h;
+    const float kLog2e = 1.4426950408889634f;
+    const float c1 = p.scale * kLog2e;
+    const float c2 = kLog2e / p.scale;
+    Ph sd_full, acc_full;
+    uint32_t n_s = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      int j, b, ha, hk;
+      decode(idx, j, b, ha, hk);
+      const int T = ntiles(j);
+      const int row = j * 128 + r;
+      const long long bha = (long long)b * (SOLVE ? p.Hkv : p.Hq) + ha;
+      float lse_r = 0.f, dl_r = 0.f;
+      if (!SOLVE) {
+        lse_r = p.lse[bha * p.Npad + row];
+        dl_r = p.delta[bha * p.Npad + row];
+      }
+      bool ok = true;
+      for (int t = 0; t < T; ++t, ++n_s) {
+        const int i = t;  // key block
+        if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
+        tc_fence_after();
+        float dv[2][32];
+        tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
+        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(DP_READ));
+        const uint32_t sreg = tmem + lane_base + ((n_s & 1) ? kTmS1 : kTmS0);
+        const bool full = SOLVE ? true : (i < j && (j + 1) * 128 <= p.N);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float sv[32];
+          tmem_ld32(sreg + c0 + 32u * q, sv);
+          tmem_ld_wait();
+          const int cb = (int)c0 + 32 * q;
+          uint32_t dk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float2 ds;
+            if (SOLVE) {
+              const float2 arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+              const float2 pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+              ds = mul2(pe, mul2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-p.scale, -p.scale)));
+            } else {
+              const float2 arg =
+                  fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-lse_r, -lse_r));
+              float2 pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+              if (!full) {
+                const int k0 = i * 128 + cb + e;  // key index
+                if (!(k0 <= row && k0 < p.N && row < p.N)) pe.x = 0.f;
+                if (!(k0 + 1 <= row && k0 + 1 < p.N && row < p.N)) pe.y = 0.f;
+              }
+              ds = mul2(pe, add2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-dl_r, -dl_r)));
+            }
+            dk[e >> 1] = pack_bf16(ds.x, ds.y);
+          }
+          tmem_st16(sreg + c0 + 32u * q, dk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(PD_FULL));
+      }
+      if (!ok) break;
+      if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
+      tc_fence_after();
+      float av[2][32];
+      if (T > 0) {
+        tmem_ld32(tmem + lane_base + kTmAcc + c0, av[0]);
+        tmem_ld32(tmem + lane_base + kTmAcc + c0 + 32u, av[1]);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) av[q][e] = 0.f;
+      }
+      tc_fence_before();
+      mbar_arrive(bar(ACC_FREE));
+      if (SOLVE) {
+        float* dst = p.dk_row + (bha * p.Npad + row) * kHeadDim + c0;
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            reinterpret_cast<float4*>(dst)[q * 8 + c] =
+                make_float4(av[q][4 * c], av[q][4 * c + 1], av[q][4 * c + 2], av[q][4 * c + 3]);
+      } else if (row < p.N) {
+        bf16* dst = p.dq + (long long)b * p.dq_sb + (long long)ha * p.dq_sh + (long long)row * p.dq_sn + c0;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) av[q][e] *= p.scale;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) st_bf16x8(dst + q * 32 + c * 8, av[q] + c * 8);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kBwdWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -488,26 +813,6 @@ __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
   if (lane == 0) delta[gw] = acc;
-}
-
-// dst (bf16, strided [B,H,N,128]) = scale * src (fp32 [B,H,Npad,128])
-__global__ void lucid_f32_to_bf16_kernel(int B, int H, int N, int Npad, float scale, const float* src,
-                                         bf16* dst, long long sb, long long sh, long long sn) {
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // one 8-element chunk
-  const long long total = (long long)B * H * N * 16;
-  if (t >= total) return;
-  const int c8 = (int)(t & 15);
-  const long long rowg = t >> 4;
-  const int row = (int)(rowg % N);
-  const long long bh = rowg / N;
-  const int b = (int)(bh / H), h = (int)(bh % H);
-  const float* s = src + ((bh * Npad + row) * kHeadDim) + c8 * 8;
-  float v[8];
-  const float4 x0 = reinterpret_cast<const float4*>(s)[0];
-  const float4 x1 = reinterpret_cast<const float4*>(s)[1];
-  v[0] = x0.x * scale; v[1] = x0.y * scale; v[2] = x0.z * scale; v[3] = x0.w * scale;
-  v[4] = x1.x * scale; v[5] = x1.y * scale; v[6] = x1.z * scale; v[7] = x1.w * scale;
-  st_bf16x8(dst + b * sb + h * sh + (long long)row * sn + c8 * 8, v);
 }
 
 // Solve backward finalize, one warp per row (row < N):
@@ -587,23 +892,39 @@ static int bwd_num_sms() {
   return n > 0 ? n : 148;
 }
 
-cudaError_t launch_bwd(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2,
-                       const CUtensorMap& tB1, const CUtensorMap& tB2, const CUtensorMap& tU,
-                       const BwdArgs& a, cudaStream_t st) {
+template <typename K>
+static cudaError_t set_smem(K kernel, uint32_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a, cudaStream_t st) {
   const int total = a.NB * a.B * a.Hkv;
   if (total == 0) return cudaSuccess;
   const int grid = std::min(total, bwd_num_sms());
   cudaError_t e;
   if (solve) {
-    e = cudaFuncSetAttribute(lucid_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)bwd::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    lucid_bwd_kernel<true><<<grid, bwd::kThreads, bwd::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
+    if ((e = set_smem(lucid_bwd_col_kernel<true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_col_kernel<true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
   } else {
-    e = cudaFuncSetAttribute(lucid_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)bwd::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    lucid_bwd_kernel<false><<<grid, bwd::kThreads, bwd::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
+    if ((e = set_smem(lucid_bwd_col_kernel<false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_col_kernel<false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
+                           const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st) {
+  const int total = a.NB * a.B * (solve ? a.Hkv : a.Hq);
+  if (total == 0) return cudaSuccess;
+  const int grid = std::min(total, bwd_num_sms());
+  cudaError_t e;
+  if (solve) {
+    if ((e = set_smem(lucid_bwd_row_kernel<true>, bwdr::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_row_kernel<true><<<grid, kBwdThreads, bwdr::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, a);
+  } else {
+    if ((e = set_smem(lucid_bwd_row_kernel<false>, bwdr::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_row_kernel<false><<<grid, kBwdThreads, bwdr::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, a);
   }
   return cudaGetLastError();
 }
@@ -616,15 +937,6 @@ cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long lon
   const int blocks = (int)((warps + 7) / 8);
   lucid_delta_kernel<<<blocks, 256, 0, st>>>(B, Hq, N, Npad, o, o_sb, o_sh, o_sn, dout, d_sb, d_sh,
                                              d_sn, delta);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_f32_to_bf16(int B, int H, int N, int Npad, float scale, const float* src, bf16* dst,
-                               long long sb, long long sh, long long sn, cudaStream_t st) {
-  const long long total = (long long)B * H * N * 16;
-  if (total == 0) return cudaSuccess;
-  const int blocks = (int)((total + 255) / 256);
-  lucid_f32_to_bf16_kernel<<<blocks, 256, 0, st>>>(B, H, N, Npad, scale, src, dst, sb, sh, sn);
   return cudaGetLastError();
 }
 

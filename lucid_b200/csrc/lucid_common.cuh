@@ -40,16 +40,18 @@ struct FwdArgs {
   int* status;
 };
 
-// Backward tile engine (attention backward or transposed solve).
+// Backward tile engines (column pass and row pass; attention or solve).
 struct BwdArgs {
   int B, Hq, Hkv, N, NB, Npad;
   float scale;
   // attention backward
   const float* lse;          // [B*Hq][Npad] log2 domain
   const float* delta;        // [B*Hq][Npad]  rowsum(dO * O)
-  float* dx;                 // [B][Hkv][Npad][128] fp32 (column-local, plain stores)
-  float* dk_col;             // [B][Hkv][Npad][128] fp32 dK (attention) or dK^ (solve), column part
-  float* d_row;              // fp32 atomic target: dQ [B][Hq][Npad][128] or dK^ rows [B][Hkv][Npad][128]
+  float* dx;                 // column pass: dL/dX  [B][Hkv][Npad][128] fp32
+  float* dk_col;             // column pass: dK (attention) or dK^ column part (solve), fp32
+  bf16* dq;                  // row pass (attention): dQ, strided [B,Hq,N,128]
+  long long dq_sb, dq_sh, dq_sn;
+  float* dk_row;             // row pass (solve): dK^ row part [B][Hkv][Npad][128] fp32
   // solve backward
   const float* dinv;
   const float* dx_in;        // dX from the attention backward (fp32)

@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
-  const Abort ab{abort_cta, p.status};
+  const Abort ab{abort_cta, p.status, SOLVE ? kTagFwdSolve : kTagFwdAttn};
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 128) {

@@ -24,11 +24,17 @@ namespace lb {
 // ---------------------------------------------------------------------------
 // Status codes written to the per-launch status word.
 // ---------------------------------------------------------------------------
+// bits 0-7: code; bits 8-19: shared-memory offset of the barrier / 8 (mbarrier
+// timeouts); bits 20-27: kernel tag.
 enum : int {
   kStatusOk = 0,
   kStatusTimeoutMbar = 1,   // an mbarrier wait exceeded its time limit
   kStatusTimeoutFlag = 2,   // a cross-CTA dependency flag never arrived
+  kStatusMisaligned = 3,    // dynamic shared memory window not 1024-byte aligned
 };
+// kernel tags
+enum : int { kTagFwdSolve = 1, kTagFwdAttn = 2, kTagBwdColAttn = 3, kTagBwdColSolve = 4,
+             kTagBwdRowAttn = 5, kTagBwdRowSolve = 6, kTagSelftest = 7 };
 
 // Wall-clock bound for any spin wait inside a kernel.  A correct launch never
 // comes close (the longest legitimate wait is one work item, milliseconds);
@@ -80,11 +86,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 struct Abort {
   volatile int* cta;   // shared
   int* status;         // global
+  int tag = 0;         // kernel tag recorded with a failure
 };
 
-__device__ __forceinline__ void raise_abort(const Abort& ab, int code) {
+__device__ __forceinline__ void raise_abort(const Abort& ab, int code, uint32_t where = 0) {
   *ab.cta = 1;
-  atomicCAS(ab.status, 0, code);
+  atomicCAS(ab.status, 0, code | (int)((where & 0xFFFu) << 8) | (ab.tag << 20));
 }
 
 // Wait for phase `parity` of `bar`.  Returns false if the wait timed out or
@@ -96,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const A
     if (mbar_try_wait(bar, parity)) return true;
     if (*ab.cta) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      raise_abort(ab, kStatusTimeoutMbar);
+      raise_abort(ab, kStatusTimeoutMbar, (bar & 0x7FFFu) >> 3);
       return false;
     }
   }
@@ -174,6 +181,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Bulk tensor reduce-add (fp32) of a shared-memory box into global memory,
+// tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until the shared-memory sources of all committed bulk groups were read
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// wait until all committed bulk groups completed (global writes included)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Load one [128 x 128] bf16 tile (two 64-column boxes) whose rows start at
 // `row0` of matrix (c2, c3).  Box k of the tile lands at dst + k*16 KB.
 __device__ __forceinline__ void tma_load_tile(uint32_t dst, const CUtensorMap* m, uint32_t bar,
@@ -212,6 +236,18 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A is M x K bf16 packed two per 32-bit
+// TMEM column (element 2c in the low half of column c), lanes = rows.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -258,6 +294,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
 }
+// 32 lanes x 16 columns store (packed bf16 pairs as 32-bit words).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -314,6 +360,19 @@ __device__ __forceinline__ void umma_tile(uint32_t d_tmem, uint32_t a_tile, bool
   }
 }
 
+// The 8 K-slices of a 128x128x128 product whose A operand lives in TMEM.
+// a_tmem(kk) gives the TMEM address of K-slice kk (8 columns of packed bf16).
+template <typename AddrFn>
+__device__ __forceinline__ void umma_tile_ts(uint32_t d_tmem, AddrFn a_tmem, uint32_t b_tile, bool b_mn,
+                                             uint32_t accumulate_first) {
+  const uint32_t idesc = idesc_bf16(128, 128, false, b_mn);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t bd = b_mn ? desc_mnmajor(b_tile, kk) : desc_kmajor(b_tile, kk);
+    umma_ts(d_tmem, a_tmem(kk), bd, idesc, (kk > 0) ? 1u : accumulate_first);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Swizzled tile writes from registers (one thread owns one tile row)
 // ---------------------------------------------------------------------------
@@ -344,6 +403,41 @@ __device__ __forceinline__ void tile_store_row32(uint32_t tile, int r, int q, co
                  pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
                  pack_bf16(v[8 * c + 6], v[8 * c + 7]));
   }
+}
+
+// Fire-and-forget fp32 vector reduction into global memory (no return value,
+// so the issuing thread never waits for the L2 round trip).
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions).
+union F2 {
+  float2 f;
+  unsigned long long u;
+};
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  F2 x{a}, y{b}, z{c}, d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.u) : "l"(x.u), "l"(y.u), "l"(z.u));
+  return d.f;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  F2 x{a}, y{b}, d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(x.u), "l"(y.u));
+  return d.f;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  F2 x{a}, y{b}, d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.u) : "l"(x.u), "l"(y.u));
+  return d.f;
+}
+
+// Write 16 packed bf16 pairs (tile columns [32*q, 32*q+32) of row r).
+__device__ __forceinline__ void tile_store_row32_packed(uint32_t tile, int r, int q, const uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    st_shared_v4(tile + tile_chunk_off(r, q * 4 + c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -45,4 +45,19 @@ inline bool make_tmap_bf16(CUtensorMap* m, const void* ptr, int cols, int rows, 
   return r == CUDA_SUCCESS;
 }
 
+// fp32 [rows][128] matrix, box = 32 columns (128 bytes) x 128 rows,
+// 128-byte swizzle: the target of the bulk reduce-adds of the backward.
+inline bool make_tmap_f32_rows(CUtensorMap* m, const void* ptr, long long rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {128 * 4};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace lb

@@ -55,9 +55,11 @@ def _rand_inputs(seed, B, Hq, Hkv, N, D=128, keys="iid", q_scale=1.0):
 # ---------------------------------------------------------------------------
 # tensor-core primitive
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("via_tma", [0, 1])
+@pytest.mark.parametrize("via_tma", [0, 1, 2])
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_umma_tile_selftest(cuda_device, a_mn, b_mn, via_tma):
+    if via_tma == 2 and a_mn:
+        pytest.skip("A from TMEM is always K-major")
     import torch
     from lucid_b200 import _lib
     lib = _lib.load()
@@ -206,3 +208,73 @@ def test_strided_bnhd_inputs(cuda_device):
     torch.cuda.synchronize()
     o_ref, _ = orc.lucid_fwd(q_, k_, v_, 128 ** -0.5)
     assert_bf16_close(_np(o), o_ref, "O")
+
+
+# ---------------------------------------------------------------------------
+# stage-level checks (each backward pass against the oracle in isolation)
+# ---------------------------------------------------------------------------
+def _attn_bwd_oracle(q, k, x, do, s):
+    """dQ, dK, dX of sum(O * dO), O = softmax(s Q K^T + causal) X (float64)."""
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    g = Hq // Hkv
+    kr, xr = np.repeat(k, g, axis=1), np.repeat(x, g, axis=1)
+    sc = np.einsum("bhld,bhsd->bhls", q, kr) * s
+    sc = np.where(np.tril(np.ones((N, N), dtype=bool)), sc, -np.inf)
+    a = np.exp(sc - sc.max(-1, keepdims=True))
+    a /= a.sum(-1, keepdims=True)
+    dot = np.swapaxes(do, 1, 2)
+    da = dot @ np.swapaxes(xr, -1, -2)
+    ds = a * (da - np.sum(da * a, -1, keepdims=True))
+    dq = s * ds @ kr
+    dk = (s * np.swapaxes(ds, -1, -2) @ q).reshape(B, Hkv, g, N, D).sum(2)
+    dx = (np.swapaxes(a, -1, -2) @ dot).reshape(B, Hkv, g, N, D).sum(2)
+    return dq, dk, dx
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,keys", [(1, 1, 1, 256, "corr"), (1, 2, 1, 384, "iid"),
+                                             (1, 2, 2, 300, "corr")])
+def test_attn_bwd_stage(cuda_device, B, Hq, Hkv, N, keys):
+    import torch
+    from lucid_b200 import attn_bwd, attn_fwd, padded_len
+    q_, k_, v_, do_ = _rand_inputs(300 + N, B, Hq, Hkv, N, keys=keys)
+    s = 128 ** -0.5
+    x_ = torch.as_tensor(orc.solve(k_, v_, s, 1e-5)).to(torch.bfloat16).double().numpy()
+    xp = np.zeros((B, Hkv, padded_len(N), 128))
+    xp[:, :, :N] = x_
+    q, k, do = _t(q_, cuda_device), _t(k_, cuda_device), _t(do_, cuda_device)
+    x = _t(xp, cuda_device)
+    o, lse = attn_fwd(q, k, x, s)
+    dq, dk, dx = attn_bwd(q, k, x, o, do, lse, s)
+    torch.cuda.synchronize()
+    dq_r, dk_r, dx_r = _attn_bwd_oracle(q_, k_, x_, do_, s)
+    G = Hq // Hkv
+    assert_bf16_close(_np(dq), dq_r, "dQ")
+    assert_bf16_close(_np(dk)[:, :, :N], dk_r, "dK(attn)", G)
+    assert_bf16_close(_np(dx)[:, :, :N], dx_r, "dX", G)
+
+
+@pytest.mark.parametrize("B,H,N,keys", [(1, 1, 256, "corr"), (1, 2, 384, "corr"), (2, 1, 200, "iid")])
+def test_solve_bwd_stage(cuda_device, B, H, N, keys):
+    """dV = P^-T dX and dK through P and RMSNorm, given dX (fp32)."""
+    import torch
+    from lucid_b200 import padded_len, solve_bwd, solve_fwd
+    _, k_, v_, _ = _rand_inputs(400 + N, B, H, H, N, keys=keys)
+    s = 128 ** -0.5
+    rng = np.random.default_rng(N)
+    dx_ = rng.standard_normal((B, H, N, 128))
+    k, v = _t(k_, cuda_device), _t(v_, cuda_device)
+    x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
+    dxp = torch.zeros(B, H, padded_len(N), 128, dtype=torch.float32, device=cuda_device)
+    dxp[:, :, :N] = torch.as_tensor(dx_, dtype=torch.float32, device=cuda_device)
+    dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dxp, s)
+    torch.cuda.synchronize()
+    p = orc.build_p(k_, s, 1e-5)
+    xo = orc.solve(k_, v_, s, 1e-5)
+    dv_r = np.linalg.solve(np.swapaxes(p, -1, -2), dx_)
+    kh, r = orc.rms_norm(k_, 1e-5)
+    dg = s * p * (-np.tril(dv_r @ np.swapaxes(xo, -1, -2)))
+    dkh = dg @ kh + np.swapaxes(dg, -1, -2) @ kh
+    dk_r = r * (dkh - np.sum(kh * dkh, -1, keepdims=True) / 128 * kh)
+    assert_bf16_close(_np(dv), dv_r, "dV")
+    assert_bf16_close(_np(dk), dk_r, "dK(solve)")
