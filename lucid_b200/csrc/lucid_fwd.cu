@@ -5,20 +5,25 @@
 //     X = P^-1 V,  P = tril(exp(s K^K^T - 1/s))
 //     Row block i:  R_i = V_i - sum_{j<i} exp(s K^_i K^_j^T - 1/s) X_j
 //                   Y   = D_i^-1 R_i ;  X_i = Y + U_i Y
-//     Blocks are processed as a wavefront: work item (i, head) waits on a
-//     global flag for every X_j (j < i) it consumes and publishes X_i.
+//     Blocks are processed as a wavefront: a work item waits on a global flag
+//     for every X_j it consumes and publishes its own X_i.
 //
 //   ATTN   (modeling_lucid.py:505-549)
-//     O = softmax(scale Q K^T + causal) X   (raw K, X from SOLVE), with the
-//     row log-sum-exp kept for the backward.  Grouped-query heads index
-//     kv head = q head / (Hq / Hkv)  (repeat_kv, modeling_lucid.py:523-524).
+//     O = softmax(scale Q K^T + causal) X   (raw K, X from SOLVE), keeping the
+//     row log-sum-exp for the backward.  Grouped-query heads index kv head =
+//     q head / (Hq / Hkv)  (repeat_kv, modeling_lucid.py:523-524).
 //
-// Warp roles (192 threads): warps 0-3 own one tile row each thread (the 128
-// TMEM lanes), warp 4 issues TMA, warp 5 issues tcgen05.mma.  Per tile j:
-//   S   = A_i B_j^T            (TMEM, double-buffered)
-//   P   = f(S)   -> bf16 smem  (epilogue warps)
-//   acc = acc + P C_j          (TMEM accumulator)
-// with A = K^ (solve) or Q (attention), B = K^ or K, C = X.
+// A work item is a PAIR of consecutive row blocks (i0 = 2p, i1 = 2p+1) of one
+// head: both rows share every K / X tile load, which halves the L2->SM
+// traffic per FLOP.  Warp roles (320 threads): warpgroup 0 (warps 0-3) owns
+// row block 0 and warpgroup 1 (warps 4-7) row block 1, one TMEM lane = one
+// row per thread; in warpgroup 2, warp 8 issues TMA and warp 9 issues
+// tcgen05.mma (registers are shifted to the epilogue warpgroups).  TMEM:
+// S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).  Per tile j:
+//   S_k = A_k B_j^T  ->  P_k = f(S_k) written back over S_k as packed bf16
+//   O_k += P_k C_j   (A operand from tensor memory)
+// issued in the order PV0(j), S0(j+1), PV1(j), S1(j+1) so that each
+// warpgroup's epilogue overlaps the other row's GEMMs.
 #include "lucid_common.cuh"
 
 #include <algorithm>
@@ -26,20 +31,22 @@
 namespace lb {
 
 namespace fwd {
-constexpr int kThreads = 192;
-// shared-memory map (bytes from the 1024-aligned base)
-constexpr uint32_t kOffA = 0;
-constexpr uint32_t kOffStage = 32768;        // stage s: B tile at +s*65536, C tile at +32768
-constexpr uint32_t kOffP = 32768 + 2 * 65536;  // P / Y buffers: 2 x 32 KB
-constexpr uint32_t kOffBar = kOffP + 2 * 32768;
+constexpr int kEpiThreads = 256;
+constexpr int kThreads = kEpiThreads + 128;  // + one warpgroup: TMA warp, MMA warp, 2 idle warps
+constexpr int kWarpTma = 8, kWarpMma = 9;
+// register split: 384 threads x 168 at launch >= 2 x 128 x 208 + 128 x 88
+constexpr int kRegsEpi = 208, kRegsCtl = 88;
+constexpr uint32_t kOffQ = 0;                 // row block k: A operand (Q / K^) or Y, at +k*32 KB
+constexpr uint32_t kOffK = 65536;             // 3 stages of B tiles (K / K^ / U)
+constexpr uint32_t kOffX = kOffK + 3 * 32768; // 2 stages of C tiles (X)
+constexpr uint32_t kOffBar = kOffX + 2 * 32768;
 enum {
-  A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL0, S_FULL1,
-  S_FREE0, S_FREE1, P_FULL0, P_FULL1, P_FREE0, P_FREE1, ACC_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR
+  Q_FULL = 0, Q_EMPTY, K_FULL0, K_EMPTY0 = K_FULL0 + 3, X_FULL0 = K_EMPTY0 + 3, X_EMPTY0 = X_FULL0 + 2,
+  S_FULL0 = X_EMPTY0 + 2, P_FULL0 = S_FULL0 + 2, O_DONE0 = P_FULL0 + 2, O_FREE0 = O_DONE0 + 2,
+  Y_FULL0 = O_FREE0 + 2, EPI_DONE0 = Y_FULL0 + 2, DRAIN = EPI_DONE0 + 2, NBAR
 };
-constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16 + 1024;  // + alignment slack
-// TMEM columns
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS0 = 0, kTmemAcc = 256;
+constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmS0 = 0, kTmO0 = 256;
 }  // namespace fwd
 
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
@@ -53,31 +60,39 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmU,
                      FwdArgs p) {
   using namespace fwd;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = (raw + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (sbase - raw);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
   const Abort ab{abort_cta, p.status, SOLVE ? kTagFwdSolve : kTagFwdAttn};
+  auto sQ = [&](int k) { return sbase + kOffQ + (uint32_t)k * 32768u; };
+  auto sK = [&](uint32_t idx) { return sbase + kOffK + (idx % 3u) * 32768u; };
+  auto sX = [&](uint32_t idx) { return sbase + kOffX + (idx & 1u) * 32768u; };
 
   const int warp = warp_id(), lane = lane_id();
-  if (threadIdx.x == 128) {
-    mbar_init(bar(A_FULL), 1);
-    mbar_init(bar(A_EMPTY), 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(KV_FULL0 + s), 1);
-      mbar_init(bar(KV_EMPTY0 + s), 1);
-      mbar_init(bar(S_FULL0 + s), 1);
-      mbar_init(bar(S_FREE0 + s), 128);
-      mbar_init(bar(P_FULL0 + s), 128);
-      mbar_init(bar(P_FREE0 + s), 1);
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
+    return;
+  }
+  if (threadIdx.x == kWarpTma * 32) {
+    mbar_init(bar(Q_FULL), 1);
+    mbar_init(bar(Q_EMPTY), 1);
+    for (int s2 = 0; s2 < 3; ++s2) {
+      mbar_init(bar(K_FULL0 + s2), 1);
+      mbar_init(bar(K_EMPTY0 + s2), 1);
     }
-    mbar_init(bar(ACC_FULL), 1);
-    mbar_init(bar(ACC_FREE), 128);
-    mbar_init(bar(EPI_DONE), 128);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(bar(X_FULL0 + s2), 1);
+      mbar_init(bar(X_EMPTY0 + s2), 1);
+      mbar_init(bar(S_FULL0 + s2), 1);
+      mbar_init(bar(P_FULL0 + s2), 128);
+      mbar_init(bar(O_DONE0 + s2), 1);
+      mbar_init(bar(O_FREE0 + s2), 128);
+      mbar_init(bar(Y_FULL0 + s2), 128);
+      mbar_init(bar(EPI_DONE0 + s2), 128);
+    }
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -86,8 +101,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     tma_prefetch_desc(&tmC);
     if (SOLVE) tma_prefetch_desc(&tmU);
   }
-  if (warp == 5) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+  if (warp == kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -97,169 +112,230 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 
   const int BHk = p.B * p.Hkv, BHq = p.B * p.Hq;
   const int G = p.Hq / p.Hkv;
-  const int total = SOLVE ? p.NB * BHk : p.NB * BHq;
+  const int NP = (p.NB + 1) / 2;
+  const int total = SOLVE ? NP * BHk : NP * BHq;
 
-  // Decode a work item.  Solve: increasing block index (wavefront order).
-  // Attention: longest rows first.
-  auto decode = [&](int idx, int& i, int& b, int& ha, int& hk) {
+  // Work item -> (pair pp, batch b, A-operand head ha, kv head hk).
+  // Solve: increasing pair index (wavefront).  Attention: longest pairs first.
+  auto decode = [&](int idx, int& pp, int& b, int& ha, int& hk) {
     if (SOLVE) {
-      i = idx / BHk;
+      pp = idx / BHk;
       const int bh = idx % BHk;
       b = bh / p.Hkv;
       hk = bh % p.Hkv;
       ha = hk;
     } else {
-      i = p.NB - 1 - idx / BHq;
+      pp = NP - 1 - idx / BHq;
       const int bh = idx % BHq;
       b = bh / p.Hq;
       ha = bh % p.Hq;
       hk = ha / G;
     }
   };
+  // Streaming tiles of row k: attention row block i has tiles j = 0..i;
+  // the solve streams the shared tiles j < 2pp (row 1's tile 2pp is part of
+  // its tail).
+  auto nrow = [&](int pp, int k) -> int {
+    const bool r1 = (2 * pp + 1) < p.NB;
+    if (k == 1 && !r1) return 0;
+    return SOLVE ? 2 * pp : 2 * pp + 1 + k;
+  };
 
-  if (warp == 4) {
+  if (warp >= kWarpTma) {
+  regs_dec<kRegsCtl>();
+  if (warp == kWarpTma) {
     // ======================= TMA producer =======================
     if (lane == 0) {
-      uint32_t g = 0, it = 0;
-      int last_a = -1, last_kv[2] = {-1, -1};  // parity of the newest load per barrier
-      for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++it) {
-        int i, b, ha, hk;
-        decode(idx, i, b, ha, hk);
-        const int T = SOLVE ? i : i + 1;
-        if (!mbar_wait(bar(A_EMPTY), (it & 1) ^ 1, ab)) break;
-        last_a = it & 1;
-        mbar_arrive_expect_tx(bar(A_FULL), 32768);
-        tma_load_tile(sbase + kOffA, &tmA, bar(A_FULL), i * 128, ha, b);
-        bool ok = true;
-        for (int t = 0; t < T && ok; ++t, ++g) {
-          const int st = g & 1;
-          const uint32_t ph = (g >> 1) & 1;
-          if (SOLVE) {
-            if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + t], 1, ab)) { ok = false; break; }
-            fence_proxy_async_global();
-          }
-          if (!mbar_wait(bar(KV_EMPTY0 + st), ph ^ 1, ab)) { ok = false; break; }
-          last_kv[st] = (int)ph;
-          mbar_arrive_expect_tx(bar(KV_FULL0 + st), 65536);
-          const uint32_t dst = sbase + kOffStage + (uint32_t)st * 65536u;
-          tma_load_tile(dst, &tmB, bar(KV_FULL0 + st), t * 128, hk, b);
-          tma_load_tile(dst + 32768, &tmC, bar(KV_FULL0 + st), t * 128, hk, b);
-        }
-        if (!ok) break;
-        if (SOLVE) {
-          const int st = g & 1;
-          const uint32_t ph = (g >> 1) & 1;
-          if (!mbar_wait(bar(KV_EMPTY0 + st), ph ^ 1, ab)) break;
-          last_kv[st] = (int)ph;
-          mbar_arrive_expect_tx(bar(KV_FULL0 + st), 32768);
-          tma_load_tile(sbase + kOffStage + (uint32_t)st * 65536u, &tmU, bar(KV_FULL0 + st),
-                        i * 128, hk, b);
-          ++g;
-        }
-      }
-      // never leave with a TMA write into shared memory still in flight
-      if (last_a >= 0) mbar_wait_timed(bar(A_FULL), (uint32_t)last_a, kDrainNs);
-      for (int s2 = 0; s2 < 2; ++s2)
-        if (last_kv[s2] >= 0) mbar_wait_timed(bar(KV_FULL0 + s2), (uint32_t)last_kv[s2], kDrainNs);
-    }
-  } else if (warp == 5) {
-    // ======================= MMA issuer =======================
-    if (lane == 0) {
-      uint32_t g = 0, it = 0;
+      uint32_t kidx = 0, xidx = 0, item = 0;
+      int last_q = -1, last_k[3] = {-1, -1, -1}, last_x[2] = {-1, -1};
       bool ok = true;
-      auto issue_pv = [&](uint32_t gg, int t) -> bool {
-        const int st = gg & 1;
-        const uint32_t ph = (gg >> 1) & 1;
-        if (!mbar_wait(bar(P_FULL0 + st), ph, ab)) return false;
-        if (t == 0 && !mbar_wait(bar(ACC_FREE), (it & 1) ^ 1, ab)) return false;
-        tc_fence_after();
-        umma_tile(tmem + kTmemAcc, sbase + kOffP + (uint32_t)st * 32768u, false,
-                  sbase + kOffStage + (uint32_t)st * 65536u + 32768u, true, t > 0 ? 1u : 0u);
-        umma_commit(bar(P_FREE0 + st));
-        umma_commit(bar(KV_EMPTY0 + st));
+      auto loadK = [&](const CUtensorMap* m, int row, int h2, int b2) -> bool {
+        const uint32_t st = kidx % 3u, use = kidx / 3u;
+        if (!mbar_wait(bar(K_EMPTY0 + st), (use & 1) ^ 1, ab)) return false;
+        last_k[st] = use & 1;
+        mbar_arrive_expect_tx(bar(K_FULL0 + st), 32768);
+        tma_load_tile(sK(kidx), m, bar(K_FULL0 + st), row, h2, b2);
+        ++kidx;
         return true;
       };
-      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
-        int i, b, ha, hk;
-        decode(idx, i, b, ha, hk);
-        const int T = SOLVE ? i : i + 1;
-        if (!mbar_wait(bar(A_FULL), it & 1, ab)) break;
-        tc_fence_after();
-        for (int t = 0; t < T; ++t) {
-          const uint32_t gg = g + t;
-          const int st = gg & 1;
-          const uint32_t ph = (gg >> 1) & 1;
-          if (!mbar_wait(bar(KV_FULL0 + st), ph, ab) || !mbar_wait(bar(S_FREE0 + st), ph ^ 1, ab)) {
-            ok = false;
-            break;
+      auto loadX = [&](int row, int h2, int b2) -> bool {
+        const uint32_t st = xidx & 1u, use = xidx >> 1;
+        if (!mbar_wait(bar(X_EMPTY0 + st), (use & 1) ^ 1, ab)) return false;
+        last_x[st] = use & 1;
+        mbar_arrive_expect_tx(bar(X_FULL0 + st), 32768);
+        tma_load_tile(sX(xidx), &tmC, bar(X_FULL0 + st), row, h2, b2);
+        ++xidx;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++item) {
+        int pp, b, ha, hk;
+        decode(idx, pp, b, ha, hk);
+        const int i0 = 2 * pp;
+        const bool r1 = i0 + 1 < p.NB;
+        if (!mbar_wait(bar(Q_EMPTY), (item & 1) ^ 1, ab)) break;
+        last_q = item & 1;
+        mbar_arrive_expect_tx(bar(Q_FULL), r1 ? 65536 : 32768);
+        tma_load_tile(sQ(0), &tmA, bar(Q_FULL), i0 * 128, ha, b);
+        if (r1) tma_load_tile(sQ(1), &tmA, bar(Q_FULL), (i0 + 1) * 128, ha, b);
+        const int nt = nrow(pp, 0) > nrow(pp, 1) ? nrow(pp, 0) : nrow(pp, 1);
+        for (int j = 0; j < nt; ++j) {
+          if (!loadK(&tmB, j * 128, hk, b)) { ok = false; break; }
+          if (SOLVE) {
+            if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + j], 1, ab)) { ok = false; break; }
+            fence_proxy_async_global();
           }
-          tc_fence_after();
-          umma_tile(tmem + kTmemS0 + (uint32_t)st * 128u, sbase + kOffA, false,
-                    sbase + kOffStage + (uint32_t)st * 65536u, false, 0u);
-          umma_commit(bar(S_FULL0 + st));
-          if (t == T - 1) umma_commit(bar(A_EMPTY));
-          if (t >= 1 && !issue_pv(gg - 1, t - 1)) { ok = false; break; }
+          if (!loadX(j * 128, hk, b)) { ok = false; break; }
         }
-        if (!ok) break;
-        if (T >= 1) {
-          if (!issue_pv(g + T - 1, T - 1)) break;
-        } else {
-          if (!mbar_wait(bar(ACC_FREE), (it & 1) ^ 1, ab)) break;
-          umma_commit(bar(A_EMPTY));
-        }
-        umma_commit(bar(ACC_FULL));
-        g += T;
-        if (SOLVE) {
-          // diagonal block: T = U_i * Y  (U from the stage's B slot, Y from the P buffer)
-          const int st = g & 1;
-          const uint32_t ph = (g >> 1) & 1;
-          if (!mbar_wait(bar(KV_FULL0 + st), ph, ab) || !mbar_wait(bar(S_FREE0 + st), ph ^ 1, ab) ||
-              !mbar_wait(bar(P_FULL0 + st), ph, ab))
-            break;
-          tc_fence_after();
-          umma_tile(tmem + kTmemS0 + (uint32_t)st * 128u, sbase + kOffStage + (uint32_t)st * 65536u,
-                    false, sbase + kOffP + (uint32_t)st * 32768u, true, 0u);
-          umma_commit(bar(S_FULL0 + st));
-          umma_commit(bar(KV_EMPTY0 + st));
-          umma_commit(bar(P_FREE0 + st));
-          ++g;
+        if (!ok || !SOLVE) continue;
+        // solve tail: K^_{2pp} for row 1, U_i0, U_i1, then X_{2pp} (made by row 0 of this item)
+        if (r1 && !loadK(&tmB, i0 * 128, hk, b)) break;
+        if (!loadK(&tmU, i0 * 128, hk, b)) break;
+        if (r1 && !loadK(&tmU, (i0 + 1) * 128, hk, b)) break;
+        if (r1) {
+          if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + i0], 1, ab)) break;
+          fence_proxy_async_global();
+          if (!loadX(i0 * 128, hk, b)) break;
         }
       }
-      // drain: no MMA may be in flight when TMEM is released
+      if (last_q >= 0) mbar_wait_timed(bar(Q_FULL), (uint32_t)last_q, kDrainNs);
+      for (int s2 = 0; s2 < 3; ++s2)
+        if (last_k[s2] >= 0) mbar_wait_timed(bar(K_FULL0 + s2), (uint32_t)last_k[s2], kDrainNs);
+      for (int s2 = 0; s2 < 2; ++s2)
+        if (last_x[s2] >= 0) mbar_wait_timed(bar(X_FULL0 + s2), (uint32_t)last_x[s2], kDrainNs);
+    }
+  } else if (warp == kWarpMma) {
+    // ======================= MMA issuer =======================
+    if (lane == 0) {
+      uint32_t kidx = 0, xidx = 0, item = 0;
+      uint32_t n_pfull[2] = {0, 0}, n_ofree[2] = {0, 0}, n_yfull[2] = {0, 0};
+      auto waitK = [&](uint32_t idx) { return mbar_wait(bar(K_FULL0 + idx % 3u), (idx / 3u) & 1, ab); };
+      auto waitX = [&](uint32_t idx) { return mbar_wait(bar(X_FULL0 + (idx & 1u)), (idx >> 1) & 1, ab); };
+      auto tS = [&](int k) { return tmem + kTmS0 + 128u * (uint32_t)k; };
+      auto tO = [&](int k) { return tmem + kTmO0 + 128u * (uint32_t)k; };
+      auto issue_s = [&](int k, uint32_t kslot) {
+        umma_tile(tS(k), sQ(k), false, sK(kslot), false, 0u);
+        umma_commit(bar(S_FULL0 + k));
+      };
+      // PV_k of streaming tile t (x slot xs); first_pv: overwrite O_k
+      auto issue_pv = [&](int k, uint32_t xs, bool first_pv) -> bool {
+        if (!mbar_wait(bar(P_FULL0 + k), (n_pfull[k]++) & 1, ab)) return false;
+        if (first_pv && !mbar_wait(bar(O_FREE0 + k), ((n_ofree[k]++) & 1) ^ 1, ab)) return false;
+        tc_fence_after();
+        const uint32_t sreg = tS(k);
+        umma_tile_ts(tO(k), [&](int kk) { return sreg + 8u * (uint32_t)kk; }, sX(xs), true, first_pv ? 0u : 1u);
+        umma_commit(bar(O_DONE0 + k));
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+        int pp, b, ha, hk;
+        decode(idx, pp, b, ha, hk);
+        const int i0 = 2 * pp;
+        const bool r1 = i0 + 1 < p.NB;
+        const int n0 = nrow(pp, 0), n1 = nrow(pp, 1), nt = n0 > n1 ? n0 : n1;
+        if (!mbar_wait(bar(Q_FULL), item & 1, ab)) break;
+        tc_fence_after();
+        bool ok = true;
+        const uint32_t kb = kidx, xb = xidx;
+        // S for the first tile of each row
+        if (nt > 0) {
+          if (!waitK(kb)) break;
+          tc_fence_after();
+          if (n0 > 0) issue_s(0, kb);
+          if (n1 > 0) issue_s(1, kb);
+          umma_commit(bar(K_EMPTY0 + kb % 3u));
+        }
+        for (int t = 0; t < nt && ok; ++t) {
+          const uint32_t xs = xb + t;
+          if (!waitX(xs)) { ok = false; break; }
+          const bool has_next = t + 1 < nt;
+          if (has_next && !waitK(kb + t + 1)) { ok = false; break; }
+          if (t < n0) {
+            if (!issue_pv(0, xs, t == 0)) { ok = false; break; }
+            if (t + 1 < n0) issue_s(0, kb + t + 1);
+          }
+          if (t < n1) {
+            if (!issue_pv(1, xs, t == 0)) { ok = false; break; }
+            if (t + 1 < n1) issue_s(1, kb + t + 1);
+          }
+          umma_commit(bar(X_EMPTY0 + (xs & 1u)));
+          if (has_next) umma_commit(bar(K_EMPTY0 + (kb + t + 1) % 3u));
+        }
+        if (!ok) break;
+        kidx = kb + nt;
+        xidx = xb + nt;
+        if (SOLVE) {
+          // tail: S1(2pp), DIAG0, PV1(2pp), DIAG1
+          if (r1) {
+            if (!waitK(kidx)) break;
+            tc_fence_after();
+            issue_s(1, kidx);
+            umma_commit(bar(K_EMPTY0 + kidx % 3u));
+            ++kidx;
+          }
+          // DIAG0: T0 = U_i0 Y0  (Y0 in row 0's A buffer)
+          if (!waitK(kidx) || !mbar_wait(bar(Y_FULL0), (n_yfull[0]++) & 1, ab)) break;
+          tc_fence_after();
+          umma_tile(tS(0), sK(kidx), false, sQ(0), true, 0u);
+          umma_commit(bar(S_FULL0));
+          umma_commit(bar(K_EMPTY0 + kidx % 3u));
+          ++kidx;
+          if (r1) {
+            if (!waitX(xidx) || !issue_pv(1, xidx, n1 == 0)) break;
+            umma_commit(bar(X_EMPTY0 + (xidx & 1u)));
+            ++xidx;
+            if (!waitK(kidx) || !mbar_wait(bar(Y_FULL0 + 1), (n_yfull[1]++) & 1, ab)) break;
+            tc_fence_after();
+            umma_tile(tS(1), sK(kidx), false, sQ(1), true, 0u);
+            umma_commit(bar(S_FULL0 + 1));
+            umma_commit(bar(K_EMPTY0 + kidx % 3u));
+            ++kidx;
+          }
+        }
+        umma_commit(bar(Q_EMPTY));
+      }
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
+  }
   } else {
-    // ======================= epilogue warps 0-3 =======================
-    const int r = threadIdx.x;  // tile row == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    regs_inc<kRegsEpi>();
+    // ======================= epilogue warpgroups =======================
+    const int k = warp >> 2;            // row block of the pair owned by this warpgroup
+    const int sp = warp & 3;            // TMEM sub-partition
+    const int r = sp * 32 + lane;       // tile row == TMEM lane
+    const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    const uint32_t tSk = tmem + lane_base + fwd::kTmS0 + 128u * (uint32_t)k;
+    const uint32_t tOk = tmem + lane_base + fwd::kTmO0 + 128u * (uint32_t)k;
+    const int wg_thread0 = k * 128;     // publishes this warpgroup's flags
     const float kLog2e = 1.4426950408889634f;
-    const float c1 = p.scale * kLog2e;               // S -> log2 domain
-    const float c2 = kLog2e / p.scale;               // 1/s in log2 domain (solve)
-    uint32_t g = 0, it = 0;
-    for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++it) {
-      int i, b, ha, hk;
-      decode(idx, i, b, ha, hk);
-      const int T = SOLVE ? i : i + 1;
+    const float c1 = p.scale * kLog2e;
+    const float c2 = kLog2e / p.scale;
+    uint32_t n_sfull = 0, n_p = 0, n_epi = 0, item = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+      int pp, b, ha, hk;
+      decode(idx, pp, b, ha, hk);
+      const int i = 2 * pp + k;         // this warpgroup's row block
+      if (i >= p.NB) continue;
+      const int nk = nrow(pp, k) + ((SOLVE && k == 1) ? 1 : 0);  // solve row 1 adds tile 2pp
+      const int row = i * 128 + r;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int t = 0; t < T; ++t, ++g) {
-        const int st = g & 1;
-        const uint32_t ph = (g >> 1) & 1;
-        if (!warp_wait(bar(S_FULL0 + st), ph, ab)) { ok = false; break; }
+      for (int t = 0; t < nk; ++t, ++n_p) {
+        if (!warp_wait(bar(S_FULL0 + k), (n_sfull++) & 1, ab)) { ok = false; break; }
         tc_fence_after();
         float sv[4][32];
-        const uint32_t ts = tmem + lane_base + kTmemS0 + (uint32_t)st * 128u;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(ts + 32u * q, sv[q]);
+        for (int q = 0; q < 4; ++q) tmem_ld32(tSk + 32u * q, sv[q]);
         tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(bar(S_FREE0 + st));
         if (SOLVE) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sv[q][e] = fast_exp2(fmaf(sv[q][e], c1, -c2));
+            for (int e = 0; e < 32; e += 2) {
+              const float2 a = fma2(make_float2(sv[q][e], sv[q][e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+              sv[q][e] = fast_exp2(a.x);
+              sv[q][e + 1] = fast_exp2(a.y);
+            }
         } else {
           const bool diag = (t == i);
           float mx = -INFINITY;
@@ -283,19 +359,17 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
             m_run = mx;
           }
           if (__any_sync(0xffffffffu, need)) {
-            // acc must be stable: wait for the previous tile's P*C product
-            const uint32_t gp = g - 1;
-            if (!warp_wait(bar(P_FREE0 + (gp & 1)), (gp >> 1) & 1, ab)) { ok = false; break; }
+            // O_k must be stable: wait for the PV of the previous tile
+            if (!warp_wait(bar(O_DONE0 + k), (n_p - 1) & 1, ab)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t ta = tmem + lane_base + kTmemAcc;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               float av[32];
-              tmem_ld32(ta + 32u * q, av);
+              tmem_ld32(tOk + 32u * q, av);
               tmem_ld_wait();
 #pragma unroll
               for (int e = 0; e < 32; ++e) av[e] *= alpha;
-              tmem_st32(ta + 32u * q, av);
+              tmem_st32(tOk + 32u * q, av);
             }
             tmem_st_wait();
           }
@@ -304,93 +378,44 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float pe = fast_exp2(sv[q][e] - m_run);
-              sv[q][e] = pe;
-              sum += pe;
+            for (int e = 0; e < 32; e += 2) {
+              const float2 a = add2(make_float2(sv[q][e], sv[q][e + 1]), make_float2(-m_run, -m_run));
+              sv[q][e] = fast_exp2(a.x);
+              sv[q][e + 1] = fast_exp2(a.y);
+              sum += sv[q][e] + sv[q][e + 1];
             }
           l_run += sum;
         }
-        if (!warp_wait(bar(P_FREE0 + st), ph ^ 1, ab)) { ok = false; break; }
-        const uint32_t pbuf = sbase + kOffP + (uint32_t)st * 32768u;
+        // P back into tensor memory over S_k (this lane's own columns)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tile_store_row32(pbuf, r, q, sv[q]);
-        fence_proxy_async_smem();
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(sv[q][2 * e], sv[q][2 * e + 1]);
+          tmem_st16(tSk + 16u * q, pk);
+        }
+        tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(P_FULL0 + st));
+        mbar_arrive(bar(P_FULL0 + k));
       }
       if (!ok) break;
-      if (!warp_wait(bar(ACC_FULL), it & 1, ab)) break;
-      tc_fence_after();
+      // O_k is final once the PV of the last tile of this row is done
       float acc[4][32];
-      const uint32_t ta = tmem + lane_base + kTmemAcc;
-      if (T > 0) {
+      if (nk > 0) {
+        if (!warp_wait(bar(O_DONE0 + k), (n_p - 1) & 1, ab)) break;
+        tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(ta + 32u * q, acc[q]);
+        for (int q = 0; q < 4; ++q) tmem_ld32(tOk + 32u * q, acc[q]);
         tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(O_FREE0 + k));
       } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[q][e] = 0.f;
       }
-      tc_fence_before();
-      mbar_arrive(bar(ACC_FREE));
-      const int row = i * 128 + r;
-      if (SOLVE) {
-        // Y = D^-1 (V - acc), kept in fp32 registers and staged as bf16 for U*Y
-        const long long bhk = (long long)b * p.Hkv + hk;
-        const float di = p.dinv[bhk * p.Npad + row];
-        const bf16* vrow = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh + (long long)row * p.v_sn;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float vv[8];
-            if (row < p.N) {
-              ld_bf16x8(vrow + q * 32 + c * 8, vv);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) vv[e] = 0.f;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[q][c * 8 + e] = (vv[e] - acc[q][c * 8 + e]) * di;
-          }
-        }
-        const int st = g & 1;
-        const uint32_t ph = (g >> 1) & 1;
-        if (!warp_wait(bar(P_FREE0 + st), ph ^ 1, ab)) break;
-        const uint32_t pbuf = sbase + kOffP + (uint32_t)st * 32768u;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tile_store_row32(pbuf, r, q, acc[q]);
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(bar(P_FULL0 + st));
-        if (!warp_wait(bar(S_FULL0 + st), ph, ab)) break;
-        tc_fence_after();
-        bf16* xrow = p.x + (bhk * p.Npad + row) * kHeadDim;
-        const uint32_t ts = tmem + lane_base + kTmemS0 + (uint32_t)st * 128u;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float tv[32];
-          tmem_ld32(ts + 32u * q, tv);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) tv[e] += acc[q][e];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) st_bf16x8(xrow + q * 32 + c * 8, tv + c * 8);
-        }
-        tc_fence_before();
-        mbar_arrive(bar(S_FREE0 + st));
-        ++g;
-        fence_proxy_async_global();
-        __threadfence();
-        mbar_arrive(bar(EPI_DONE));
-        if (r == 0) {
-          if (mbar_wait(bar(EPI_DONE), it & 1, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
-        }
-        __syncwarp();
-      } else {
+      if (!SOLVE) {
         const float inv_l = 1.f / l_run;
         if (row < p.N) {
           bf16* orow = p.o + (long long)b * p.o_sb + (long long)ha * p.o_sh + (long long)row * p.o_sn;
@@ -403,17 +428,65 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
           }
         }
         p.lse[((long long)b * p.Hq + ha) * p.Npad + row] = m_run + __log2f(l_run);
+        continue;
       }
+      // ---- solve: diagonal block.  Y = D^-1 (V - acc) -> A buffer of this row ----
+      const long long bhk = (long long)b * p.Hkv + hk;
+      const float di = p.dinv[bhk * p.Npad + row];
+      const bf16* vrow = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh + (long long)row * p.v_sn;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float vv[8];
+          if (row < p.N) {
+            ld_bf16x8(vrow + q * 32 + c * 8, vv);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vv[e] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[q][c * 8 + e] = (vv[e] - acc[q][c * 8 + e]) * di;
+        }
+      }
+      // the A buffer may still be in flight from TMA when this row had no tiles
+      if (!warp_wait(bar(Q_FULL), item & 1, ab)) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tile_store_row32(sQ(k), r, q, acc[q]);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(Y_FULL0 + k));
+      if (!warp_wait(bar(S_FULL0 + k), (n_sfull++) & 1, ab)) break;
+      tc_fence_after();
+      bf16* xrow = p.x + (bhk * p.Npad + row) * kHeadDim;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float tv[32];
+        tmem_ld32(tSk + 32u * q, tv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) tv[e] += acc[q][e];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) st_bf16x8(xrow + q * 32 + c * 8, tv + c * 8);
+      }
+      tc_fence_before();
+      fence_proxy_async_global();
+      __threadfence();
+      mbar_arrive(bar(EPI_DONE0 + k));
+      if ((int)threadIdx.x == wg_thread0) {
+        if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+      }
+      ++n_epi;
+      __syncwarp();
     }
   }
 
   // ---- teardown: every role is done (or aborted); release TMEM ----
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -430,7 +503,8 @@ static int num_sms() {
 
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st) {
-  const int total = solve ? a.NB * a.B * a.Hkv : a.NB * a.B * a.Hq;
+  const int pairs = (a.NB + 1) / 2;
+  const int total = solve ? pairs * a.B * a.Hkv : pairs * a.B * a.Hq;
   if (total == 0) return cudaSuccess;
   const int grid = std::min(total, num_sms());
   cudaError_t e;

@@ -52,6 +52,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+// Re-balance registers between warpgroups (all threads of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 
 // ---------------------------------------------------------------------------
