@@ -22,8 +22,9 @@
 //   The diagonal entries P_rr enter exactly in fp32 in the finalize kernel.
 //
 // Both passes: warps 0-7 are the epilogue (warp w reads TMEM lanes of
-// sub-partition w%4 = tile rows 32(w%4).., column half w/4), warp 8 issues
-// TMA, warp 9 issues tcgen05.mma.  P and dS return to tensor memory as packed
+// sub-partition w%4 = tile rows 32(w%4).., column half w/4); in the control
+// warpgroup warp 8 issues TMA and warp 9 issues tcgen05.mma (registers are
+// shifted from the control warpgroup to the epilogue).  P and dS return to tensor memory as packed
 // bf16 and feed the next GEMMs as the A operand (TS form); the next tile's
 // S / dP GEMMs are issued while the epilogue of the current tile runs.
 #include "lucid_common.cuh"
@@ -56,8 +57,10 @@ __device__ __forceinline__ uint32_t packed_kslice(uint32_t region, int kk) {
 
 constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdEpiThreads = kBwdEpiWarps * 32;
-constexpr int kBwdThreads = kBwdEpiThreads + 64;
+constexpr int kBwdThreads = kBwdEpiThreads + 128;  // + control warpgroup (TMA, MMA, 2 idle warps)
 constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1;
+// register split: 384 x 168 at launch >= 256 x 192 + 128 x 120
+constexpr int kBwdRegsEpi = 192, kBwdRegsCtl = 120;
 
 // ===========================================================================
 // column pass
@@ -154,6 +157,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   };
 
+  if (warp >= kBwdWarpTma) {
+  regs_dec<kBwdRegsCtl>();
   if (warp == kBwdWarpTma) {
     // ======================= TMA producer =======================
     if (lane == 0) {
@@ -217,11 +222,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool pending_dp_read = false;  // a dP read whose release the next dP write must await
       bool first_item = true;
       const uint32_t tS = tmem + kTmS, tDP = tmem + kTmDP;
-      auto issue_sd = [&](int st) {
-        umma_tile(tDP, sA2, false, sB2(st), false, 0u);  // dP = A2 B2^T
-        umma_tile(tS, sA1, false, sB1(st), false, 0u);   // S  = A1 B1^T
-        umma_commit(bar(SD_FULL));
-      };
       for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
         int i, b, hk;
         decode(idx, i, b, hk);
@@ -232,16 +232,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (SOLVE && !first_item && !mbar_wait(bar(S_FREE), s_free.full(), ab)) break;
         first_item = false;
         bool ok = true;
+        // tile t: dP(t) = A2 B2^T is issued as soon as dP(t-1) was read by the
+        // epilogue (P / dS live in the S region); S(t) = A1 B1^T after the
+        // GEMMs that read P(t-1) / dS(t-1).
         if (T > 0) {
           const int st = n_kv & 1;
           if (!mbar_wait(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) break;
           if (pending_dp_read && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) break;
           tc_fence_after();
-          issue_sd(st);
+          umma_tile(tDP, sA2, false, sB2(st), false, 0u);
+          umma_tile(tS, sA1, false, sB1(st), false, 0u);
+          umma_commit(bar(SD_FULL));
           pending_dp_read = true;
         }
         for (int t = 0; t < T; ++t, ++n_kv) {
           const int st = n_kv & 1;
+          const int st2 = (n_kv + 1) & 1;
+          const bool has_next = t + 1 < T;
+          if (has_next) {
+            if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab) ||
+                !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
+            tc_fence_after();
+            umma_tile(tDP, sA2, false, sB2(st2), false, 0u);  // dP(t+1)
+          }
           if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) { ok = false; break; }
           if (t == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
           tc_fence_after();
@@ -250,12 +263,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk); }, sB2(st), true, acc);
           umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tS, kk) + 16u; }, sB1(st), true, acc);
           umma_commit(bar(KV_EMPTY0 + st));
-          if (t + 1 < T) {
-            const int st2 = (n_kv + 1) & 1;
-            if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab) ||
-                !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
-            tc_fence_after();
-            issue_sd(st2);
+          if (has_next) {
+            umma_tile(tS, sA1, false, sB1(st2), false, 0u);    // S(t+1)
+            umma_commit(bar(SD_FULL));
           }
         }
         if (!ok) break;
@@ -297,7 +307,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
+  }
   } else {
+    regs_inc<kBwdRegsEpi>();
     // ======================= epilogue warps 0-7 =======================
     const int sp = warp & 3, h = warp >> 2;
     const int r = sp * 32 + lane;
@@ -322,9 +334,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!SOLVE && !warp_wait_b(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) { ok = false; break; }
         if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
-        float dv[2][32];
+        float dv[2][32], sv[2][32];
         tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
         tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        tmem_ld32(tmem + lane_base + kTmS + c0, sv[0]);
+        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u, sv[1]);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar(DP_READ));
@@ -333,37 +347,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                 : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          float sv[32];
-          tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, sv);
-          tmem_ld_wait();
           const int cb = (int)c0 + 32 * q;
           uint32_t pk[16], dk[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int c = cb + e;
-            float2 arg, pe, ds;
-            if (SOLVE) {
-              arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
-              pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
-              if (!full) {
-                if (j * 128 + c >= p.N) pe.x = 0.f;
-                if (j * 128 + c + 1 >= p.N) pe.y = 0.f;
-              }
-              ds = mul2(pe, mul2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-p.scale, -p.scale)));
-            } else {
-              const float2 ls = *reinterpret_cast<const float2*>(vec + c);
-              const float2 dl = *reinterpret_cast<const float2*>(vec + 128 + c);
-              arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-ls.x, -ls.y));
-              pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
-              if (!full) {
-                const int q0 = j * 128 + c;
-                if (!(q0 < p.N && row_i < p.N && q0 >= row_i)) pe.x = 0.f;
-                if (!(q0 + 1 < p.N && row_i < p.N && q0 + 1 >= row_i)) pe.y = 0.f;
-              }
-              ds = mul2(pe, add2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-dl.x, -dl.y)));
+          for (int e = 0; e < 32; e += 4) {
+            float4 ls4, dl4;
+            if (!SOLVE) {
+              ls4 = *reinterpret_cast<const float4*>(vec + cb + e);
+              dl4 = *reinterpret_cast<const float4*>(vec + 128 + cb + e);
             }
-            pk[e >> 1] = pack_bf16(pe.x, pe.y);
-            dk[e >> 1] = pack_bf16(ds.x, ds.y);
+#pragma unroll
+            for (int hh = 0; hh < 4; hh += 2) {
+              const int c = cb + e + hh;
+              float2 arg, pe, ds;
+              if (SOLVE) {
+                arg = fma2(make_float2(sv[q][e + hh], sv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+                if (!full) {
+                  if (j * 128 + c >= p.N) pe.x = 0.f;
+                  if (j * 128 + c + 1 >= p.N) pe.y = 0.f;
+                }
+                ds = mul2(pe, mul2(make_float2(dv[q][e + hh], dv[q][e + hh + 1]), make_float2(-p.scale, -p.scale)));
+              } else {
+                const float2 ls = hh == 0 ? make_float2(ls4.x, ls4.y) : make_float2(ls4.z, ls4.w);
+                const float2 dl = hh == 0 ? make_float2(dl4.x, dl4.y) : make_float2(dl4.z, dl4.w);
+                arg = fma2(make_float2(sv[q][e + hh], sv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-ls.x, -ls.y));
+                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+                if (!full) {
+                  const int q0 = j * 128 + c;
+                  if (!(q0 < p.N && row_i < p.N && q0 >= row_i)) pe.x = 0.f;
+                  if (!(q0 + 1 < p.N && row_i < p.N && q0 + 1 >= row_i)) pe.y = 0.f;
+                }
+                ds = mul2(pe, add2(make_float2(dv[q][e + hh], dv[q][e + hh + 1]), make_float2(-dl.x, -dl.y)));
+              }
+              pk[(e + hh) >> 1] = pack_bf16(pe.x, pe.y);
+              dk[(e + hh) >> 1] = pack_bf16(ds.x, ds.y);
+            }
           }
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q + 16u, dk);
@@ -510,10 +529,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ===========================================================================
 namespace bwdr {
 constexpr uint32_t kOffA1 = 0, kOffA2 = 32768;
-constexpr uint32_t kOffStage = 65536;        // stage s: B1 at +s*65536, B2 at +32768
-constexpr uint32_t kOffBar = kOffStage + 2 * 65536;
-enum { A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_READ, PD_FULL,
-       ACC_FULL, ACC_FREE, DRAIN, NBAR };
+constexpr uint32_t kOffK = 65536;             // 3-deep ring of B1 tiles (K / K^)
+constexpr uint32_t kOffX = kOffK + 3 * 32768;  // 2-deep ring of B2 tiles (X)
+constexpr uint32_t kOffBar = kOffX + 2 * 32768;
+enum { A_FULL = 0, A_EMPTY, K_FULL0, K_EMPTY0 = K_FULL0 + 3, X_FULL0 = K_EMPTY0 + 3, X_EMPTY0 = X_FULL0 + 2,
+       SD_FULL = X_EMPTY0 + 2, DP_READ, PD_FULL, ACC_FULL, ACC_FREE, DRAIN, NBAR };
 constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS0 = 0, kTmS1 = 128, kTmDP = 256, kTmAcc = 384;
 }  // namespace bwdr
@@ -532,8 +552,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
   const Abort ab{abort_cta, p.status, SOLVE ? kTagBwdRowSolve : kTagBwdRowAttn};
   const uint32_t sA1 = sbase + kOffA1, sA2 = sbase + kOffA2;
-  auto sB1 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u; };
-  auto sB2 = [&](int st) { return sbase + kOffStage + (uint32_t)st * 65536u + 32768u; };
+  auto sK = [&](uint32_t idx) { return sbase + kOffK + (idx % 3u) * 32768u; };
+  auto sX = [&](uint32_t idx) { return sbase + kOffX + (idx & 1u) * 32768u; };
 
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {
@@ -543,9 +563,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == kBwdWarpTma * 32) {
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
+    for (int s2 = 0; s2 < 3; ++s2) {
+      mbar_init(bar(K_FULL0 + s2), 1);
+      mbar_init(bar(K_EMPTY0 + s2), 1);
+    }
     for (int s2 = 0; s2 < 2; ++s2) {
-      mbar_init(bar(KV_FULL0 + s2), 1);
-      mbar_init(bar(KV_EMPTY0 + s2), 1);
+      mbar_init(bar(X_FULL0 + s2), 1);
+      mbar_init(bar(X_EMPTY0 + s2), 1);
     }
     mbar_init(bar(SD_FULL), 1);
     mbar_init(bar(DP_READ), kBwdEpiThreads);
@@ -588,11 +612,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   };
   auto ntiles = [&](int j) { return SOLVE ? j : j + 1; };  // key blocks i < j (solve) / i <= j
 
+  if (warp >= kBwdWarpTma) {
+  regs_dec<kBwdRegsCtl>();
   if (warp == kBwdWarpTma) {
     if (lane == 0) {
       Ph a_empty;
-      uint32_t n_kv = 0, n_a = 0;
-      int last_a = -1, last_kv[2] = {-1, -1};
+      uint32_t kidx = 0, xidx = 0, n_a = 0;
+      int last_a = -1, last_k[3] = {-1, -1, -1}, last_x[2] = {-1, -1};
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         int j, b, ha, hk;
@@ -603,24 +629,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_tile(sA1, &tmA1, bar(A_FULL), j * 128, ha, b);
         tma_load_tile(sA2, &tmA2, bar(A_FULL), j * 128, ha, b);
         const int T = ntiles(j);
-        for (int t = 0; t < T; ++t, ++n_kv) {
-          const int st = n_kv & 1;
-          const uint32_t use = n_kv >> 1;
-          if (!mbar_wait(bar(KV_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
-          last_kv[st] = use & 1;
-          mbar_arrive_expect_tx(bar(KV_FULL0 + st), 65536);
-          tma_load_tile(sB1(st), &tmB1, bar(KV_FULL0 + st), t * 128, hk, b);
-          tma_load_tile(sB2(st), &tmB2, bar(KV_FULL0 + st), t * 128, hk, b);
+        for (int t = 0; t < T; ++t) {
+          {
+            const uint32_t st = kidx % 3u, use = kidx / 3u;
+            if (!mbar_wait(bar(K_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+            last_k[st] = use & 1;
+            mbar_arrive_expect_tx(bar(K_FULL0 + st), 32768);
+            tma_load_tile(sK(kidx), &tmB1, bar(K_FULL0 + st), t * 128, hk, b);
+            ++kidx;
+          }
+          {
+            const uint32_t st = xidx & 1u, use = xidx >> 1;
+            if (!mbar_wait(bar(X_EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+            last_x[st] = use & 1;
+            mbar_arrive_expect_tx(bar(X_FULL0 + st), 32768);
+            tma_load_tile(sX(xidx), &tmB2, bar(X_FULL0 + st), t * 128, hk, b);
+            ++xidx;
+          }
         }
       }
       if (last_a >= 0) mbar_wait_timed(bar(A_FULL), (uint32_t)last_a, kDrainNs);
+      for (int s2 = 0; s2 < 3; ++s2)
+        if (last_k[s2] >= 0) mbar_wait_timed(bar(K_FULL0 + s2), (uint32_t)last_k[s2], kDrainNs);
       for (int s2 = 0; s2 < 2; ++s2)
-        if (last_kv[s2] >= 0) mbar_wait_timed(bar(KV_FULL0 + s2), (uint32_t)last_kv[s2], kDrainNs);
+        if (last_x[s2] >= 0) mbar_wait_timed(bar(X_FULL0 + s2), (uint32_t)last_x[s2], kDrainNs);
     }
   } else if (warp == kBwdWarpMma) {
     if (lane == 0) {
       Ph a_full, dp_read, pd_full, acc_free;
-      uint32_t n_kv = 0, n_s = 0;
+      uint32_t kidx = 0, xidx = 0, n_s = 0;
       bool pending_dp_read = false;
       const uint32_t tDP = tmem + kTmDP;
       auto tS = [&](uint32_t n) { return tmem + ((n & 1) ? kTmS1 : kTmS0); };
@@ -632,31 +669,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bool ok = true;
         for (int t = 0; t <= T; ++t) {
           if (t < T) {
-            // S(t) = A1 B1^T into S[n_s % 2]; dP(t) = A2 B2^T (after dP(t-1) was read)
-            const int st = (n_kv + t) & 1;
-            if (!mbar_wait(bar(KV_FULL0 + st), ((n_kv + t) >> 1) & 1, ab)) { ok = false; break; }
+            // S(t) = A1 K_t^T into S[n_s % 2]; dP(t) = A2 X_t^T (after dP(t-1) was read)
+            const uint32_t ki = kidx + t, xi = xidx + t;
+            if (!mbar_wait(bar(K_FULL0 + ki % 3u), (ki / 3u) & 1, ab) ||
+                !mbar_wait(bar(X_FULL0 + (xi & 1u)), (xi >> 1) & 1, ab)) { ok = false; break; }
             if (pending_dp_read && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
             tc_fence_after();
-            umma_tile(tS(n_s + t), sA1, false, sB1(st), false, 0u);
-            umma_tile(tDP, sA2, false, sB2(st), false, 0u);
+            umma_tile(tS(n_s + t), sA1, false, sK(ki), false, 0u);
+            umma_tile(tDP, sA2, false, sX(xi), false, 0u);
             umma_commit(bar(SD_FULL));
+            umma_commit(bar(X_EMPTY0 + (xi & 1u)));
             pending_dp_read = true;
           }
           if (t >= 1) {
-            // acc += dS(t-1) B1(t-1), dS packed in S[(n_s + t - 1) % 2]
+            // acc += dS(t-1) K_{t-1}, dS packed in S[(n_s + t - 1) % 2]
             const int tt = t - 1;
-            const int st = (n_kv + tt) & 1;
+            const uint32_t ki = kidx + tt;
             if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) { ok = false; break; }
             if (tt == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sreg = tS(n_s + tt);
-            umma_tile_ts(tmem + kTmAcc, [&](int kk) { return packed_kslice(sreg, kk); }, sB1(st), true,
+            umma_tile_ts(tmem + kTmAcc, [&](int kk) { return packed_kslice(sreg, kk); }, sK(ki), true,
                          tt > 0 ? 1u : 0u);
-            umma_commit(bar(KV_EMPTY0 + st));
+            umma_commit(bar(K_EMPTY0 + ki % 3u));
           }
         }
         if (!ok) break;
-        n_kv += T;
+        kidx += T;
+        xidx += T;
         n_s += T;
         if (T == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) break;
         umma_commit(bar(ACC_FULL));
@@ -665,7 +705,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
+  }
   } else {
+    regs_inc<kBwdRegsEpi>();
     const int sp = warp & 3, h = warp >> 2;
     const int r = sp * 32 + lane;
     const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
@@ -691,19 +733,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int i = t;  // key block
         if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
-        float dv[2][32];
+        const uint32_t sreg = tmem + lane_base + ((n_s & 1) ? kTmS1 : kTmS0);
+        float dv[2][32], svv[2][32];
         tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
         tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        tmem_ld32(sreg + c0, svv[0]);
+        tmem_ld32(sreg + c0 + 32u, svv[1]);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar(DP_READ));
-        const uint32_t sreg = tmem + lane_base + ((n_s & 1) ? kTmS1 : kTmS0);
         const bool full = SOLVE ? true : (i < j && (j + 1) * 128 <= p.N);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          float sv[32];
-          tmem_ld32(sreg + c0 + 32u * q, sv);
-          tmem_ld_wait();
+          const float (&sv)[32] = svv[q];
           const int cb = (int)c0 + 32 * q;
           uint32_t dk[16];
 #pragma unroll
