@@ -40,6 +40,7 @@ extern "C" {
 #define LUCID_ERR_WORKSPACE 3   /* workspace missing or too small */
 #define LUCID_ERR_TENSORMAP 4   /* TMA descriptor creation failed */
 #define LUCID_ERR_LAUNCH 5      /* CUDA launch error */
+#define LUCID_ERR_TOO_LARGE 6   /* problem exceeds a fixed-size internal buffer */
 
 /* Library version, e.g. 100 for 0.1.0. */
 int lucid_version(void);
@@ -67,6 +68,30 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps,
                     const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
                     void* x, void* khat, void* u, float* rstd, float* dinv,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Solve forward that allocates nothing and takes no workspace.
+ * No counterpart in the reference: it exists for callers that cannot call
+ * cudaMalloc, e.g. a plugin hosted by an engine that owns all device memory
+ * and forbids allocations after start-up, or a code path that cannot afford
+ * the implicit device synchronisation of an allocation.
+ * Same arguments and results as lucid_solve_fwd minus the workspace.  Its
+ * scratch (the per-block dependency flags and the status word) is a fixed
+ * static device array of LUCID_NOALLOC_SCRATCH_BYTES bytes that every GPU
+ * loading the library holds until the process exits:
+ *   - B * H * ceil(N / 128) must not exceed LUCID_NOALLOC_MAX_BLOCKS, else the
+ *     call returns LUCID_ERR_TOO_LARGE and launches nothing;
+ *   - the first call on each device looks up the array's device address, so
+ *     make that first call before any stream capture;
+ *   - every call clears and reuses the same array: calls whose execution
+ *     overlaps on the GPU (e.g. on two streams) race, so serialise them.
+ */
+#define LUCID_NOALLOC_MAX_BLOCKS 16384
+#define LUCID_NOALLOC_SCRATCH_BYTES (256 + 4 * LUCID_NOALLOC_MAX_BLOCKS)
+int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps,
+                            const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                            const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                            void* x, void* khat, void* u, float* rstd, float* dinv, void* stream);
 
 /*
  * Attention forward: O = softmax(scale Q K^T + causal) X.

@@ -21,6 +21,7 @@ ERRORS = {
     3: "workspace missing or too small",
     4: "TMA descriptor creation failed",
     5: "CUDA launch error",
+    6: "problem exceeds a fixed-size internal buffer",
 }
 
 c_int, c_float, c_size_t, c_void_p, c_int64 = (
@@ -37,6 +38,8 @@ SIGNATURES = {
     "lucid_solve_fwd_workspace_bytes": (c_size_t, [c_int] * 4),
     "lucid_solve_fwd": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3
                         + [c_void_p] * 5 + [c_void_p, c_size_t, c_void_p]),
+    "lucid_solve_fwd_noalloc": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3
+                                + [c_void_p] * 5 + [c_void_p]),
     "lucid_attn_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_fwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
                        + [c_void_p] + S3 + [c_void_p] + [c_void_p, c_size_t, c_void_p]),

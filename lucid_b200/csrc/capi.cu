@@ -341,6 +341,46 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// solve forward without a workspace (static scratch)
+// ---------------------------------------------------------------------------
+// Scratch of lucid_solve_fwd_noalloc: status word region + dependency flags.
+// Host code must not pass this symbol to a kernel (on the host it names a
+// host-side stand-in); its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LUCID_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+// Device address of g_noalloc_scratch for the current device, looked up once
+// per device.  Returns nullptr if the lookup fails.
+void* noalloc_scratch_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  static std::mutex mu;
+  static void* ptrs[64] = {};
+  std::lock_guard<std::mutex> g(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+}  // namespace
+
+extern "C" int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps, const void* k,
+                                       int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb,
+                                       int64_t v_sh, int64_t v_sn, void* x, void* khat, void* u, float* rstd,
+                                       float* dinv, void* stream) {
+  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  if ((long long)B * H * nb_of(N) > LUCID_NOALLOC_MAX_BLOCKS) return LUCID_ERR_TOO_LARGE;
+  void* ws = noalloc_scratch_ptr();
+  if (!ws) return LUCID_ERR_LAUNCH;
+  // lucid_solve_fwd clears the status word and the flags before its launches
+  return lucid_solve_fwd(B, H, N, D, scale, eps, k, k_sb, k_sh, k_sn, v, v_sb, v_sh, v_sn, x, khat, u, rstd,
+                         dinv, ws, LUCID_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------
 // tensor-core self test
 // ---------------------------------------------------------------------------
 namespace lb {
