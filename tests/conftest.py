@@ -32,7 +32,20 @@ def load_golden(name: str) -> dict:
 
 
 ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                    if not os.path.basename(p).startswith("blockwise"))
+                    if not os.path.basename(p).startswith(("blockwise", "path_")))
+PATH_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "path_*.npz")))
+
+
+def load_path_golden(name: str) -> dict:
+    """LUCID-Path fixture from tests/golden/make_path_golden.py (the reference
+    Triton op, float32).  Inputs are exact bf16 values, returned as float64."""
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        d = {k: z[k] for k in z.files}
+    for nm in ("q", "k", "v", "w", "beta", "do"):
+        if f"{nm}_bf16" in d:
+            d[nm] = from_bf16_bits(d.pop(f"{nm}_bf16")).astype(np.float64)
+    d.setdefault("q", None)
+    return d
 
 
 @pytest.fixture(scope="session")
