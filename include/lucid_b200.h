@@ -150,6 +150,59 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * LUCID-Path forward: O = (I + L)^-1 V with the Householder-path scores
+ *   L = stril(exp(scale * A - 1/scale)),  A_rc = q_r^T (H_r ... H_{c+1}) k_c,
+ *   H_t = I - beta_t w_t w_t^T.
+ * Replaces parallel_lucid_path_attention / ParallelLUCIDPathAttentionFunction
+ * .forward (lucid_path/triton_code/parallel.py:27-76, :180-241) together with
+ * the kernels it launches: chunk_scaled_dot_kkt_fwd + solve_tril (:40-51),
+ * triangular_solve_fwd_kernel (triangular_solve_fwd.py:14-225) and
+ * mini_triangular_solve (mini_tril_solve.py:9-81).
+ * Layout is the reference's BTHD: k, v, w are [B, T, H, D] and q, o are
+ * [B, T, HQ, D], each given by element strides (sb, st, sh) with unit
+ * innermost stride; beta is [B, T, H] (bf16, or fp32 when beta_fp32 != 0)
+ * with strides (sb, st, sh).  q may be NULL, meaning q = k (then HQ == H).
+ * The workspace (lucid_path_fwd_workspace_bytes) holds the state the
+ * backward reads: keep it unchanged until lucid_path_bwd has run.
+ */
+size_t lucid_path_fwd_workspace_bytes(int B, int T, int H, int HQ, int D);
+int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
+                   const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                   const void* k, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                   const void* v, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                   const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
+                   const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
+                   void* o, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * LUCID-Path backward.  Replaces ParallelLUCIDPathAttentionFunction.backward
+ * (parallel.py:78-177) and its kernels: triangular_solve_bwd_dv_kernel
+ * (triangular_solve_bwd_dv_reuse.py:17-205), the prepare / cumprod / transform_q
+ * / inter / intra / preprocess kernels and the GQA reduction (:165-171).
+ * In : q, k, w, beta as for lucid_path_fwd (q NULL when the forward used q = k);
+ *      dout [B, T, HQ, D]; fwd_workspace = the forward's workspace.
+ * Out: dk, dv, dw [B, T, H, D] and dbeta [B, T, H] (bf16, fp32 when
+ *      dbeta_fp32 != 0), dq [B, T, HQ, D] when q was given.  With q = k the
+ *      query gradient is added into dk (the reference returns both and
+ *      autograd sums them into k.grad).
+ */
+size_t lucid_path_bwd_workspace_bytes(int B, int T, int H, int HQ, int D);
+int lucid_path_bwd(int B, int T, int H, int HQ, int D, float scale,
+                   const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                   const void* k, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                   const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
+                   const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
+                   const void* dout, int64_t do_sb, int64_t do_st, int64_t do_sh,
+                   const void* fwd_workspace, size_t fwd_workspace_bytes,
+                   void* dq, int64_t dq_sb, int64_t dq_st, int64_t dq_sh,
+                   void* dk, int64_t dk_sb, int64_t dk_st, int64_t dk_sh,
+                   void* dv, int64_t dv_sb, int64_t dv_st, int64_t dv_sh,
+                   void* dw, int64_t dw_sb, int64_t dw_st, int64_t dw_sh,
+                   void* dbeta, int dbeta_fp32, int64_t db_sb, int64_t db_st, int64_t db_sh,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Kernel timing hook (benchmarks).  While enabled for one kernel family,
  * every launch of that family's main kernel is bracketed by a pair of CUDA
  * events recorded on the launch stream; lucid_profile_read waits for the
@@ -164,6 +217,12 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale,
 #define LUCID_KERNEL_SOLVE_BWD 5      /* transposed-solve wavefront (dV, dK^ columns) */
 #define LUCID_KERNEL_ATTN_BWD_ROW 6   /* attention backward, row pass (dQ) */
 #define LUCID_KERNEL_SOLVE_BWD_ROW 7  /* solve backward, row pass (dK^ rows) */
+#define LUCID_KERNEL_PATH_BLOCK 8     /* LUCID-Path per-block kernels (UT transform, diagonal blocks, their backward) */
+#define LUCID_KERNEL_PATH_SCORES 9    /* LUCID-Path off-diagonal path scores */
+#define LUCID_KERNEL_PATH_SOLVE 10    /* LUCID-Path wavefront solve O = (I + L)^-1 V */
+#define LUCID_KERNEL_PATH_SOLVE_T 11  /* LUCID-Path transposed solve dV = (I + L)^-T dO */
+#define LUCID_KERNEL_PATH_ROW 12      /* LUCID-Path backward row pass (dA, dQ~ chain) */
+#define LUCID_KERNEL_PATH_COL 13      /* LUCID-Path backward column pass (dK_new, dW, dW2) */
 int lucid_profile_enable(int kernel);
 int lucid_profile_read(float* total_ms, int* launches);
 

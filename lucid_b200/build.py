@@ -19,8 +19,9 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "liblucid_b200.so")
 
-SOURCES = ["lucid_prep.cu", "lucid_fwd.cu", "lucid_bwd.cu", "capi.cu"]
-HEADERS = ["sm100.cuh", "lucid_common.cuh", "tmap.h"]
+SOURCES = ["lucid_prep.cu", "lucid_fwd.cu", "lucid_bwd.cu", "capi.cu", "path_block.cu", "path_kernels.cu",
+           "path_capi.cu"]
+HEADERS = ["sm100.cuh", "lucid_common.cuh", "tmap.h", "path_common.cuh", "profile.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,0 +1,966 @@
+// O(N^2) kernels of LUCID-Path (lucid_path/triton_code/), all persistent,
+// warp-specialised tcgen05 kernels on [128 x 128] bf16 tiles (320 threads:
+// warps 0-7 epilogue, warp 8 TMA producer, warp 9 MMA issuer; epilogue warp
+// w reads TMEM lanes 32*(w%4).. and columns 64*(w/4)..).
+//
+//   path_scores_kernel  off-diagonal path scores (triangular_solve_fwd.py:177-209).
+//       Row block i walks j = i-1 .. 0 carrying Q~ (fp32 in registers):
+//         S = Q~ K_new_j^T -> L_ij = exp(s S - 1/s) (bf16 tile to HBM)
+//         Q~ <- Q~ - (Q~ W_j^T) W2_j               (two MMAs, -S2 staged in TMEM)
+//       The bf16 operand copy of every Q~ is also stored (TMA) for the backward.
+//   path_solve_kernel<false>  O = (I + L)^-1 V, block forward substitution as a
+//       wavefront over flags (triangular_solve_fwd.py:160-221):
+//         R_i = V_i - sum_{j<i} L_ij O_j,  O_i = R_i + U_i R_i,  U_i = (I + L_ii)^-1 - I
+//   path_solve_kernel<true>   dV = (I + L)^-T dO, the transposed wavefront
+//       (triangular_solve_bwd_dv_reuse.py:17-205):
+//         R_j = dO_j - sum_{i>j} L_ij^T dV_i,  dV_j = R_j + U_j^T R_j
+//   path_row_kernel     row pass of the backward, row block i, j = 0 .. i:
+//         dA_ij = -s L_ij o (dV_i O_j^T)                  (stored for the column pass)
+//         dQ~^{(j)} = dQ~^{(j-1)} - (dQ~^{(j-1)} W2_j^T) W_j + dA_ij K_new_j
+//       giving dQ_new_i = dQ~^{(i-1)} and the snapshots dQ~_i^{(j-1)}
+//       (the work of parallel_path_bwd_inter_dqh.py / parallel_path_bwd_intra.py).
+//   path_col_kernel     column pass, column block j, i = j+1 .. NB-1:
+//         dK_new_j = sum_i dA_ij^T Q~_i^{(j)},   Phi_j = sum_i Q~_i^{(j)T} dQ~_i^{(j-1)}
+//         dW2_j = -W_j Phi_j,  dW_j = -W2_j Phi_j^T
+//       (parallel_path_bwd_inter_dkv.py, cumprod_householder_bwd.py: Phi_j is
+//       the gradient of the block transform G_j = I - W_j^T W2_j).
+// Every spin wait is bounded (mbar_wait / wait_flag_geq); a timeout records
+// the status word and unwinds.
+#include "path_common.cuh"
+
+#include <algorithm>
+
+namespace lb {
+
+namespace pk {
+constexpr int kThreads = 320;
+constexpr int kEpi = 256;
+constexpr int kWarpTma = 8, kWarpMma = 9;
+}  // namespace pk
+
+__device__ __forceinline__ bool pwarp_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
+  const bool ok = mbar_wait(bar, parity, ab);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v));
+  tmem_ld32(taddr + 32u, *reinterpret_cast<float(*)[32]>(v + 32));
+  tmem_ld_wait();
+}
+// Rewrite 64 fp32 values (one thread's half row) as 32 packed bf16 columns
+// starting at taddr (the first column of the half), optionally negated.
+__device__ __forceinline__ void tmem_st_packed64(uint32_t taddr, const float (&v)[64], float sign) {
+  uint32_t pk0[16], pk1[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    pk0[e] = pack_bf16(sign * v[2 * e], sign * v[2 * e + 1]);
+    pk1[e] = pack_bf16(sign * v[32 + 2 * e], sign * v[32 + 2 * e + 1]);
+  }
+  tmem_st16(taddr, pk0);
+  tmem_st16(taddr + 16u, pk1);
+}
+__device__ __forceinline__ void tile_store_row64(uint32_t tile, int r, int hf, const float (&v)[64]) {
+  tile_store_row32(tile, r, 2 * hf, *reinterpret_cast<const float(*)[32]>(v));
+  tile_store_row32(tile, r, 2 * hf + 1, *reinterpret_cast<const float(*)[32]>(v + 32));
+}
+__device__ __forceinline__ void st_f32x64(float* p, const float (&v)[64]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e)
+    reinterpret_cast<float4*>(p)[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+}
+__device__ __forceinline__ void st_bf16x64(bf16* p, const float (&v)[64]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) st_bf16x8(p + 8 * e, v + 8 * e);
+}
+__device__ __forceinline__ void ld_bf16x64(const bf16* p, float (&v)[64]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ld_bf16x8(p + 8 * e, v + 8 * e);
+}
+
+// Producer-side ring of 32 KB tiles.
+template <int R>
+struct TileRing {
+  uint32_t base, full0, empty0;
+  uint32_t n = 0;
+  int last[R];
+  __device__ void init(uint32_t b, uint32_t f0, uint32_t e0) {
+    base = b; full0 = f0; empty0 = e0; n = 0;
+#pragma unroll
+    for (int s = 0; s < R; ++s) last[s] = -1;
+  }
+  __device__ uint32_t slot(uint32_t idx) const { return base + (idx % R) * 32768u; }
+  __device__ bool load(const CUtensorMap* m, int row, int c2, int c3, const Abort& ab) {
+    const uint32_t st = n % R, use = n / R;
+    if (!mbar_wait(empty0 + 8u * st, (use & 1) ^ 1, ab)) return false;
+    last[st] = (int)(use & 1);
+    mbar_arrive_expect_tx(full0 + 8u * st, 32768);
+    tma_load_tile(slot(n), m, full0 + 8u * st, row, c2, c3);
+    ++n;
+    return true;
+  }
+  __device__ void drain() {
+#pragma unroll
+    for (int s = 0; s < R; ++s)
+      if (last[s] >= 0) mbar_wait_timed(full0 + 8u * s, (uint32_t)last[s], kDrainNs);
+  }
+};
+
+// ===========================================================================
+// path_scores_kernel
+// ===========================================================================
+namespace psc {
+constexpr int kRing = 4;
+constexpr uint32_t kOffQ = 0, kOffRing = 32768, kOffBar = kOffRing + kRing * 32768;
+enum { RF0 = 0, RE0 = RF0 + kRing, QOP_FULL = RE0 + kRing, QFREE, QWRITTEN, SS_FULL, NS2_FULL, D_FULL, DRAIN, NBAR };
+constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmS = 0, kTmS2 = 128;
+}  // namespace psc
+
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    path_scores_kernel(const __grid_constant__ CUtensorMap tmKn, const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmQs,
+                       PathScoresArgs p) {
+  using namespace psc;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagPathScores};
+  const uint32_t sQ = sbase + kOffQ;
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagPathScores << 20));
+    return;
+  }
+  if (threadIdx.x == pk::kWarpTma * 32) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(RF0 + s), 1);
+      mbar_init(bar(RE0 + s), 1);
+    }
+    mbar_init(bar(QOP_FULL), 1);
+    mbar_init(bar(QFREE), 1);
+    mbar_init(bar(QWRITTEN), pk::kEpi);
+    mbar_init(bar(SS_FULL), 1);
+    mbar_init(bar(NS2_FULL), pk::kEpi);
+    mbar_init(bar(D_FULL), 1);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmKn);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmW2);
+    tma_prefetch_desc(&tmQs);
+  }
+  if (warp == pk::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BHQ = p.B * p.HQ;
+  const int total = (p.NB - 1) * BHQ;
+  const long long Npad = (long long)p.NB * 128;
+  auto decode = [&](int idx, int& i, int& bhq, int& b, int& h, int& bhk) {
+    i = p.NB - 1 - idx / BHQ;
+    bhq = idx % BHQ;
+    b = bhq / p.HQ;
+    h = (bhq % p.HQ) / p.G;
+    bhk = b * p.H + h;
+  };
+
+  if (warp == pk::kWarpTma) {
+    if (lane == 0) {
+      TileRing<kRing> ring;
+      ring.init(sbase + kOffRing, bar(RF0), bar(RE0));
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int i, bhq, b, h, bhk;
+        decode(idx, i, bhq, b, h, bhk);
+        for (int j = i - 1; j >= 0 && ok; --j) {
+          ok = ring.load(&tmKn, j * 128, bhk, 0, ab);
+          if (ok && j > 0) ok = ring.load(&tmW, j * 128, h, b, ab) && ring.load(&tmW2, j * 128, bhk, 0, ab);
+        }
+      }
+      ring.drain();
+    }
+  } else if (warp == pk::kWarpMma) {
+    if (lane == 0) {
+      uint32_t rc = 0, n_q = 0, n_ns2 = 0;
+      auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
+      auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
+      auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int i, bhq, b, h, bhk;
+        decode(idx, i, bhq, b, h, bhk);
+        for (int j = i - 1; j >= 0; --j) {
+          if (!mbar_wait(bar(QOP_FULL), (n_q++) & 1, ab)) { ok = false; break; }
+          const uint32_t sK = rc++;
+          if (!ring_wait(sK)) { ok = false; break; }
+          uint32_t sW = 0;
+          if (j > 0) {
+            sW = rc++;
+            if (!ring_wait(sW)) { ok = false; break; }
+          }
+          tc_fence_after();
+          umma_tile(tmem + kTmS, sQ, false, ring_slot(sK), false, 0u);
+          if (j > 0) umma_tile(tmem + kTmS2, sQ, false, ring_slot(sW), false, 0u);
+          umma_commit(bar(SS_FULL));
+          ring_free(sK);
+          if (j == 0) break;
+          ring_free(sW);
+          if (!mbar_wait(bar(NS2_FULL), (n_ns2++) & 1, ab)) { ok = false; break; }
+          const uint32_t sW2 = rc++;
+          if (!ring_wait(sW2)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t s2 = tmem + kTmS2;
+          umma_tile_ts(tmem + kTmS, [&](int kk) { return packed_half_kslice(s2, kk); }, ring_slot(sW2), true, 0u);
+          umma_commit(bar(D_FULL));
+          ring_free(sW2);
+        }
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t tS = tmem + lane_base + kTmS + 64u * hf;
+    const uint32_t tS2 = tmem + lane_base + kTmS2 + 64u * hf;
+    const float c1 = p.s * 1.4426950408889634f, c2 = 1.4426950408889634f / p.s;
+    uint32_t n_ss = 0, n_d = 0, n_qf = 0, n_qw = 0;
+    // Publish the bf16 copy of Q~ as the next MMA operand and as snapshot `pair`.
+    auto write_qop = [&](const float (&q)[64], long long pair, int bhq) -> bool {
+      if (threadIdx.x == 0) {
+        bulk_wait_read_all();
+        mbar_arrive(bar(QFREE));
+      }
+      __syncwarp();
+      if (!pwarp_wait(bar(QFREE), (n_qf++) & 1, ab)) return false;
+      tile_store_row64(sQ, r, hf, q);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(QWRITTEN));
+      if (threadIdx.x == 0) {
+        if (mbar_wait(bar(QWRITTEN), n_qw & 1, ab)) {
+          tma_store_tile(&tmQs, sQ, (int)(pair * 128), bhq, 0);
+          bulk_commit();
+          mbar_arrive(bar(QOP_FULL));
+        }
+      }
+      ++n_qw;
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+      int i, bhq, b, h, bhk;
+      decode(idx, i, bhq, b, h, bhk);
+      float q[64];
+      {
+        const float4* src = reinterpret_cast<const float4*>(p.qn + (((long long)bhq * Npad) + i * 128 + r) * 128 + hf * 64);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float4 f = src[e];
+          q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
+        }
+      }
+      if (!write_qop(q, path_pair(i, i - 1), bhq)) break;
+      for (int j = i - 1; j >= 0; --j) {
+        if (!pwarp_wait(bar(SS_FULL), (n_ss++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        float sv[64];
+        tmem_ld64(tS, sv);
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const float2 a = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+          sv[e] = fast_exp2(a.x);
+          sv[e + 1] = fast_exp2(a.y);
+        }
+        st_bf16x64(p.L + ((((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128 + hf * 64), sv);
+        if (j == 0) break;
+        tmem_ld64(tS2, sv);
+        tmem_st_packed64(tS2, sv, -1.f);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(NS2_FULL));
+        if (!pwarp_wait(bar(D_FULL), (n_d++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        tmem_ld64(tS, sv);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) q[e] += sv[e];
+        tc_fence_before();
+        if (!write_qop(q, path_pair(i, j - 1), bhq)) { ok = false; break; }
+      }
+    }
+    if (threadIdx.x == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == pk::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ===========================================================================
+// path_solve_kernel<TR>
+// ===========================================================================
+namespace psv {
+constexpr int kRing = 4;
+constexpr uint32_t kOffY = 0, kOffRing = 32768, kOffBar = kOffRing + kRing * 32768;
+enum { RF0 = 0, RE0 = RF0 + kRing, ACC_FULL = RE0 + kRing, Y_FULL, T_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR };
+constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmAcc = 0, kTmT = 128;
+}  // namespace psv
+
+template <bool TR>
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    path_solve_kernel(const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmX,
+                      const __grid_constant__ CUtensorMap tmU, PathSolveArgs p) {
+  using namespace psv;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, TR ? kTagPathSolveT : kTagPathSolve};
+  const uint32_t sY = sbase + kOffY;
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
+    return;
+  }
+  if (threadIdx.x == pk::kWarpTma * 32) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(RF0 + s), 1);
+      mbar_init(bar(RE0 + s), 1);
+    }
+    mbar_init(bar(ACC_FULL), 1);
+    mbar_init(bar(Y_FULL), pk::kEpi);
+    mbar_init(bar(T_FULL), 1);
+    mbar_init(bar(ACC_FREE), pk::kEpi);
+    mbar_init(bar(EPI_DONE), pk::kEpi);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmL);
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmU);
+  }
+  if (warp == pk::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BHQ = p.B * p.HQ;
+  const int total = p.NB * BHQ;
+  const long long Npad = (long long)p.NB * 128;
+  // item -> (block, head); the forward walks blocks upwards, the transposed solve downwards
+  auto decode = [&](int idx, int& blk, int& bhq, int& ndeps) {
+    blk = TR ? p.NB - 1 - idx / BHQ : idx / BHQ;
+    bhq = idx % BHQ;
+    ndeps = TR ? p.NB - 1 - blk : blk;
+  };
+  auto dep_block = [&](int blk, int d) { return TR ? blk + 1 + d : d; };
+  auto pair_of = [&](int blk, int db) { return TR ? path_pair(db, blk) : path_pair(blk, db); };
+
+  if (warp == pk::kWarpTma) {
+    if (lane == 0) {
+      TileRing<kRing> ring;
+      ring.init(sbase + kOffRing, bar(RF0), bar(RE0));
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int blk, bhq, nd;
+        decode(idx, blk, bhq, nd);
+        for (int d = 0; d < nd && ok; ++d) {
+          const int db = dep_block(blk, d);
+          if (!wait_flag_geq(&p.flags[(long long)bhq * p.NB + db], 1, ab)) { ok = false; break; }
+          fence_proxy_async_global();
+          ok = ring.load(&tmL, (int)(pair_of(blk, db) * 128), bhq, 0, ab) && ring.load(&tmX, db * 128, bhq, 0, ab);
+        }
+        if (ok) ok = ring.load(&tmU, blk * 128, bhq, 0, ab);
+      }
+      ring.drain();
+    }
+  } else if (warp == pk::kWarpMma) {
+    if (lane == 0) {
+      uint32_t rc = 0, n_free = 0, n_y = 0;
+      auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
+      auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
+      auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+        int blk, bhq, nd;
+        decode(idx, blk, bhq, nd);
+        if (!mbar_wait(bar(ACC_FREE), ((n_free++) & 1) ^ 1, ab)) break;
+        bool ok = true;
+        for (int d = 0; d < nd; ++d) {
+          const uint32_t sL = rc++, sX = rc++;
+          if (!ring_wait(sL) || !ring_wait(sX)) { ok = false; break; }
+          tc_fence_after();
+          umma_tile(tmem + kTmAcc, ring_slot(sL), TR, ring_slot(sX), true, d > 0 ? 1u : 0u);
+          ring_free(sL);
+          ring_free(sX);
+        }
+        if (!ok) break;
+        umma_commit(bar(ACC_FULL));
+        const uint32_t sU = rc++;
+        if (!ring_wait(sU) || !mbar_wait(bar(Y_FULL), (n_y++) & 1, ab)) break;
+        tc_fence_after();
+        umma_tile(tmem + kTmT, ring_slot(sU), TR, sY, true, 0u);
+        umma_commit(bar(T_FULL));
+        ring_free(sU);
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t tAcc = tmem + lane_base + kTmAcc + 64u * hf;
+    const uint32_t tT = tmem + lane_base + kTmT + 64u * hf;
+    uint32_t n_acc = 0, n_t = 0, n_epi = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      int blk, bhq, nd;
+      decode(idx, blk, bhq, nd);
+      const int b = bhq / p.HQ, hq = bhq % p.HQ, h = hq / p.G;
+      if (!pwarp_wait(bar(ACC_FULL), (n_acc++) & 1, ab)) break;
+      tc_fence_after();
+      float R[64];
+      if (nd > 0) {
+        tmem_ld64(tAcc, R);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) R[e] = 0.f;
+      }
+      const long long t = (long long)blk * 128 + r;
+      if (t < p.T) {
+        float rhs[64];
+        const bf16* src = p.rhs + (long long)b * p.r_sb + (long long)(TR ? hq : h) * p.r_sh + t * p.r_st + hf * 64;
+        ld_bf16x64(src, rhs);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) R[e] = rhs[e] - R[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) R[e] = -R[e];
+      }
+      tile_store_row64(sY, r, hf, R);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(Y_FULL));
+      if (!pwarp_wait(bar(T_FULL), (n_t++) & 1, ab)) break;
+      tc_fence_after();
+      float X[64];
+      tmem_ld64(tT, X);
+#pragma unroll
+      for (int e = 0; e < 64; ++e) X[e] += R[e];
+      tc_fence_before();
+      mbar_arrive(bar(ACC_FREE));
+      st_bf16x64(p.xbuf + (((long long)bhq * Npad) + t) * 128 + hf * 64, X);
+      if (!TR && p.out != nullptr && t < p.T)
+        st_bf16x64(p.out + (long long)b * p.o_sb + (long long)hq * p.o_sh + t * p.o_st + hf * 64, X);
+      fence_proxy_async_global();
+      __threadfence();
+      mbar_arrive(bar(EPI_DONE));
+      if (threadIdx.x == 0) {
+        if (mbar_wait(bar(EPI_DONE), n_epi & 1, ab)) st_release_gpu(&p.flags[(long long)bhq * p.NB + blk], 1);
+      }
+      ++n_epi;
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == pk::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ===========================================================================
+// path_row_kernel
+// ===========================================================================
+namespace prw {
+constexpr int kRing = 4;
+constexpr uint32_t kOffDV = 0, kOffDOP = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
+enum { RF0 = 0, RE0 = RF0 + kRing, DV_FULL = RE0 + kRing, DV_EMPTY, PS_FULL, PK_FULL, D_FULL, DOP_FULL, QFREE,
+       QWRITTEN, DRAIN, NBAR };
+constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmP = 0, kTmS3 = 128, kTmD = 256;
+}  // namespace prw
+
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    path_row_kernel(const __grid_constant__ CUtensorMap tmDV, const __grid_constant__ CUtensorMap tmO,
+                    const __grid_constant__ CUtensorMap tmKn, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmDs,
+                    PathRowArgs p) {
+  using namespace prw;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagPathRow};
+  const uint32_t sDV = sbase + kOffDV, sDOP = sbase + kOffDOP;
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagPathRow << 20));
+    return;
+  }
+  if (threadIdx.x == pk::kWarpTma * 32) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(RF0 + s), 1);
+      mbar_init(bar(RE0 + s), 1);
+    }
+    mbar_init(bar(DV_FULL), 1);
+    mbar_init(bar(DV_EMPTY), 1);
+    mbar_init(bar(PS_FULL), 1);
+    mbar_init(bar(PK_FULL), pk::kEpi);
+    mbar_init(bar(D_FULL), 1);
+    mbar_init(bar(DOP_FULL), 1);
+    mbar_init(bar(QFREE), 1);
+    mbar_init(bar(QWRITTEN), pk::kEpi);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmDV);
+    tma_prefetch_desc(&tmO);
+    tma_prefetch_desc(&tmKn);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmW2);
+    tma_prefetch_desc(&tmDs);
+  }
+  if (warp == pk::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BHQ = p.B * p.HQ;
+  const int total = p.NB * BHQ;
+  const long long Npad = (long long)p.NB * 128;
+  auto decode = [&](int idx, int& i, int& bhq, int& b, int& h, int& bhk) {
+    i = p.NB - 1 - idx / BHQ;
+    bhq = idx % BHQ;
+    b = bhq / p.HQ;
+    h = (bhq % p.HQ) / p.G;
+    bhk = b * p.H + h;
+  };
+
+  if (warp == pk::kWarpTma) {
+    if (lane == 0) {
+      TileRing<kRing> ring;
+      ring.init(sbase + kOffRing, bar(RF0), bar(RE0));
+      bool ok = true;
+      uint32_t it = 0;
+      int last_dv = -1;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
+        int i, bhq, b, h, bhk;
+        decode(idx, i, bhq, b, h, bhk);
+        if (!mbar_wait(bar(DV_EMPTY), (it & 1) ^ 1, ab)) break;
+        last_dv = (int)(it & 1);
+        mbar_arrive_expect_tx(bar(DV_FULL), 32768);
+        tma_load_tile(sDV, &tmDV, bar(DV_FULL), i * 128, bhq, 0);
+        for (int j = 0; j <= i && ok; ++j) {
+          ok = ring.load(&tmO, j * 128, bhq, 0, ab);
+          if (ok && j >= 1 && j < i) ok = ring.load(&tmW2, j * 128, bhk, 0, ab);
+          if (ok && j < i) ok = ring.load(&tmKn, j * 128, bhk, 0, ab);
+          if (ok && j >= 1 && j < i) ok = ring.load(&tmW, j * 128, h, b, ab);
+        }
+      }
+      if (last_dv >= 0) mbar_wait_timed(bar(DV_FULL), (uint32_t)last_dv, kDrainNs);
+      ring.drain();
+    }
+  } else if (warp == pk::kWarpMma) {
+    if (lane == 0) {
+      uint32_t rc = 0, n_pk = 0, n_dop = 0, it = 0;
+      auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
+      auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
+      auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
+        int i, bhq, b, h, bhk;
+        decode(idx, i, bhq, b, h, bhk);
+        if (!mbar_wait(bar(DV_FULL), it & 1, ab)) break;
+        for (int j = 0; j <= i; ++j) {
+          const bool has_s3 = (j >= 1 && j < i);
+          const uint32_t sO = rc++;
+          if (!ring_wait(sO)) { ok = false; break; }
+          uint32_t sW2 = 0;
+          if (has_s3) {
+            if (!mbar_wait(bar(DOP_FULL), (n_dop++) & 1, ab)) { ok = false; break; }
+            sW2 = rc++;
+            if (!ring_wait(sW2)) { ok = false; break; }
+          }
+          tc_fence_after();
+          umma_tile(tmem + kTmP, sDV, false, ring_slot(sO), false, 0u);
+          if (has_s3) umma_tile(tmem + kTmS3, sDOP, false, ring_slot(sW2), false, 0u);
+          umma_commit(bar(PS_FULL));
+          ring_free(sO);
+          if (has_s3) ring_free(sW2);
+          if (!mbar_wait(bar(PK_FULL), (n_pk++) & 1, ab)) { ok = false; break; }
+          if (j < i) {
+            const uint32_t sK = rc++;
+            if (!ring_wait(sK)) { ok = false; break; }
+            uint32_t sW = 0;
+            if (j >= 1) {
+              sW = rc++;
+              if (!ring_wait(sW)) { ok = false; break; }
+            }
+            tc_fence_after();
+            const uint32_t tp = tmem + kTmP, ts3 = tmem + kTmS3;
+            umma_tile_ts(tmem + kTmD, [&](int kk) { return packed_half_kslice(tp, kk); }, ring_slot(sK), true, 0u);
+            if (j >= 1)
+              umma_tile_ts(tmem + kTmD, [&](int kk) { return packed_half_kslice(ts3, kk); }, ring_slot(sW), true, 1u);
+            umma_commit(bar(D_FULL));
+            ring_free(sK);
+            if (j >= 1) ring_free(sW);
+          }
+        }
+        umma_commit(bar(DV_EMPTY));
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t tP = tmem + lane_base + kTmP + 64u * hf;
+    const uint32_t tS3 = tmem + lane_base + kTmS3 + 64u * hf;
+    const uint32_t tD = tmem + lane_base + kTmD + 64u * hf;
+    uint32_t n_ps = 0, n_d = 0, n_qf = 0, n_qw = 0;
+    auto write_dop = [&](const float (&q)[64], long long pair, int bhq) -> bool {
+      if (threadIdx.x == 0) {
+        bulk_wait_read_all();
+        mbar_arrive(bar(QFREE));
+      }
+      __syncwarp();
+      if (!pwarp_wait(bar(QFREE), (n_qf++) & 1, ab)) return false;
+      tile_store_row64(sDOP, r, hf, q);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(QWRITTEN));
+      if (threadIdx.x == 0) {
+        if (mbar_wait(bar(QWRITTEN), n_qw & 1, ab)) {
+          tma_store_tile(&tmDs, sDOP, (int)(pair * 128), bhq, 0);
+          bulk_commit();
+          mbar_arrive(bar(DOP_FULL));
+        }
+      }
+      ++n_qw;
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+      int i, bhq, b, h, bhk;
+      decode(idx, i, bhq, b, h, bhk);
+      float dq[64];
+#pragma unroll
+      for (int e = 0; e < 64; ++e) dq[e] = 0.f;
+      for (int j = 0; j <= i; ++j) {
+        if (!pwarp_wait(bar(PS_FULL), (n_ps++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        float pv[64], lv[64];
+        tmem_ld64(tP, pv);
+        const long long toff = (j < i) ? ((((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128 + hf * 64)
+                                       : ((((long long)bhq * p.NB + i) * 128 + r) * 128 + hf * 64);
+        ld_bf16x64((j < i ? p.L : p.Ld) + toff, lv);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          float v = -p.s * lv[e] * pv[e];
+          if (j == i && hf * 64 + e >= r) v = 0.f;
+          pv[e] = v;
+        }
+        st_bf16x64((j < i ? p.dA : p.dAd) + toff, pv);
+        if (j < i) tmem_st_packed64(tP, pv, 1.f);
+        if (j >= 1 && j < i) {
+          tmem_ld64(tS3, lv);
+          tmem_st_packed64(tS3, lv, -1.f);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(PK_FULL));
+        if (j < i) {
+          if (!pwarp_wait(bar(D_FULL), (n_d++) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          tmem_ld64(tD, pv);
+#pragma unroll
+          for (int e = 0; e < 64; ++e) dq[e] += pv[e];
+          tc_fence_before();
+          if (j + 1 < i && !write_dop(dq, path_pair(i, j + 1), bhq)) { ok = false; break; }
+        }
+      }
+      if (!ok) break;
+      st_f32x64(p.dqn + (((long long)bhq * Npad) + i * 128 + r) * 128 + hf * 64, dq);
+    }
+    if (threadIdx.x == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == pk::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// path_col_kernel
+// ===========================================================================
+namespace pcl {
+constexpr int kRing = 5;
+constexpr uint32_t kOffHi = 0, kOffLo = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
+enum { RF0 = 0, RE0 = RF0 + kRing, ACC_FULL = RE0 + kRing, PHI_FULL, W_FULL, ACC_FREE, DRAIN, NBAR };
+constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmA1 = 0, kTmA2 = 128, kTmW2 = 256, kTmW = 384;
+}  // namespace pcl
+
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    path_col_kernel(const __grid_constant__ CUtensorMap tmDA, const __grid_constant__ CUtensorMap tmQs,
+                    const __grid_constant__ CUtensorMap tmDs, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmW2, PathColArgs p) {
+  using namespace pcl;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagPathCol};
+  const uint32_t sHi = sbase + kOffHi, sLo = sbase + kOffLo;
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagPathCol << 20));
+    return;
+  }
+  if (threadIdx.x == pk::kWarpTma * 32) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(RF0 + s), 1);
+      mbar_init(bar(RE0 + s), 1);
+    }
+    mbar_init(bar(ACC_FULL), 1);
+    mbar_init(bar(PHI_FULL), pk::kEpi);
+    mbar_init(bar(W_FULL), 1);
+    mbar_init(bar(ACC_FREE), pk::kEpi);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmDA);
+    tma_prefetch_desc(&tmQs);
+    tma_prefetch_desc(&tmDs);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmW2);
+  }
+  if (warp == pk::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BHQ = p.B * p.HQ;
+  const int total = p.NB * BHQ;
+  const long long Npad = (long long)p.NB * 128;
+  auto decode = [&](int idx, int& j, int& bhq, int& b, int& h, int& bhk, int& steps) {
+    j = idx / BHQ;
+    bhq = idx % BHQ;
+    b = bhq / p.HQ;
+    h = (bhq % p.HQ) / p.G;
+    bhk = b * p.H + h;
+    steps = p.NB - 1 - j;
+  };
+
+  if (warp == pk::kWarpTma) {
+    if (lane == 0) {
+      TileRing<kRing> ring;
+      ring.init(sbase + kOffRing, bar(RF0), bar(RE0));
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int j, bhq, b, h, bhk, steps;
+        decode(idx, j, bhq, b, h, bhk, steps);
+        if (steps == 0) continue;
+        for (int i = j + 1; i < p.NB && ok; ++i) {
+          const int row = (int)(path_pair(i, j) * 128);
+          ok = ring.load(&tmDA, row, bhq, 0, ab) && ring.load(&tmQs, row, bhq, 0, ab);
+          if (ok && j >= 1) ok = ring.load(&tmDs, row, bhq, 0, ab);
+        }
+        if (ok && j >= 1) ok = ring.load(&tmW, j * 128, h, b, ab) && ring.load(&tmW2, j * 128, bhk, 0, ab);
+      }
+      ring.drain();
+    }
+  } else if (warp == pk::kWarpMma) {
+    if (lane == 0) {
+      uint32_t rc = 0, n_act = 0, n_phi = 0;
+      auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
+      auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
+      auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int j, bhq, b, h, bhk, steps;
+        decode(idx, j, bhq, b, h, bhk, steps);
+        if (steps == 0) continue;
+        if (!mbar_wait(bar(ACC_FREE), ((n_act++) & 1) ^ 1, ab)) break;
+        for (int s = 0; s < steps; ++s) {
+          const uint32_t sA = rc++, sQ = rc++;
+          if (!ring_wait(sA) || !ring_wait(sQ)) { ok = false; break; }
+          uint32_t sD = 0;
+          if (j >= 1) {
+            sD = rc++;
+            if (!ring_wait(sD)) { ok = false; break; }
+          }
+          tc_fence_after();
+          umma_tile(tmem + kTmA1, ring_slot(sA), true, ring_slot(sQ), true, s > 0 ? 1u : 0u);
+          if (j >= 1) umma_tile(tmem + kTmA2, ring_slot(sQ), true, ring_slot(sD), true, s > 0 ? 1u : 0u);
+          ring_free(sA);
+          ring_free(sQ);
+          if (j >= 1) ring_free(sD);
+        }
+        if (!ok) break;
+        umma_commit(bar(ACC_FULL));
+        if (j >= 1) {
+          const uint32_t sW = rc++, sW2 = rc++;
+          if (!ring_wait(sW) || !ring_wait(sW2)) break;
+          if (!mbar_wait(bar(PHI_FULL), (n_phi++) & 1, ab)) break;
+          tc_fence_after();
+          umma_tile(tmem + kTmW2, ring_slot(sW), false, sHi, true, 0u);
+          umma_tile(tmem + kTmW2, ring_slot(sW), false, sLo, true, 1u);
+          umma_tile(tmem + kTmW, ring_slot(sW2), false, sHi, false, 0u);
+          umma_tile(tmem + kTmW, ring_slot(sW2), false, sLo, false, 1u);
+          umma_commit(bar(W_FULL));
+          ring_free(sW);
+          ring_free(sW2);
+        }
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t t1 = tmem + lane_base + kTmA1 + 64u * hf;
+    const uint32_t t2 = tmem + lane_base + kTmA2 + 64u * hf;
+    const uint32_t tw2 = tmem + lane_base + kTmW2 + 64u * hf;
+    const uint32_t tw = tmem + lane_base + kTmW + 64u * hf;
+    uint32_t n_acc = 0, n_w = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      int j, bhq, b, h, bhk, steps;
+      decode(idx, j, bhq, b, h, bhk, steps);
+      const long long off = (((long long)bhq * Npad) + j * 128 + r) * 128 + hf * 64;
+      float v[64];
+      if (steps == 0 || j == 0) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = 0.f;
+        st_f32x64(p.dw2 + off, v);
+        st_f32x64(p.dw + off, v);
+        if (steps == 0) {
+          st_f32x64(p.dkn + off, v);
+          continue;
+        }
+      }
+      if (!pwarp_wait(bar(ACC_FULL), (n_acc++) & 1, ab)) break;
+      tc_fence_after();
+      tmem_ld64(t1, v);
+      st_f32x64(p.dkn + off, v);
+      if (j >= 1) {
+        float hi[64];
+        tmem_ld64(t2, v);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          hi[e] = __bfloat162float(__float2bfloat16(v[e]));
+          v[e] -= hi[e];
+        }
+        tile_store_row64(sHi, r, hf, hi);
+        tile_store_row64(sLo, r, hf, v);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(PHI_FULL));
+        if (!pwarp_wait(bar(W_FULL), (n_w++) & 1, ab)) break;
+        tc_fence_after();
+        tmem_ld64(tw2, v);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = -v[e];
+        st_f32x64(p.dw2 + off, v);
+        tmem_ld64(tw, v);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = -v[e];
+        st_f32x64(p.dw + off, v);
+      }
+      tc_fence_before();
+      mbar_arrive(bar(ACC_FREE));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == pk::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------
+static int path_num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <typename K, typename... Args>
+static cudaError_t launch_persistent(K kernel, uint32_t smem, int total, cudaStream_t st, Args... args) {
+  if (total <= 0) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(total, path_num_sms());
+  kernel<<<grid, pk::kThreads, smem, st>>>(args...);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_path_scores(const CUtensorMap& tmKn, const CUtensorMap& tmW, const CUtensorMap& tmW2,
+                               const CUtensorMap& tmQs, const PathScoresArgs& a, cudaStream_t st) {
+  return launch_persistent(path_scores_kernel, psc::kSmem, (a.NB - 1) * a.B * a.HQ, st, tmKn, tmW, tmW2, tmQs, a);
+}
+
+cudaError_t launch_path_solve(bool transposed, const CUtensorMap& tmL, const CUtensorMap& tmX, const CUtensorMap& tmU,
+                              const PathSolveArgs& a, cudaStream_t st) {
+  const int total = a.NB * a.B * a.HQ;
+  if (transposed) return launch_persistent(path_solve_kernel<true>, psv::kSmem, total, st, tmL, tmX, tmU, a);
+  return launch_persistent(path_solve_kernel<false>, psv::kSmem, total, st, tmL, tmX, tmU, a);
+}
+
+cudaError_t launch_path_row(const CUtensorMap& tmDV, const CUtensorMap& tmO, const CUtensorMap& tmKn,
+                            const CUtensorMap& tmW, const CUtensorMap& tmW2, const CUtensorMap& tmDs,
+                            const PathRowArgs& a, cudaStream_t st) {
+  return launch_persistent(path_row_kernel, prw::kSmem, a.NB * a.B * a.HQ, st, tmDV, tmO, tmKn, tmW, tmW2, tmDs, a);
+}
+
+cudaError_t launch_path_col(const CUtensorMap& tmDA, const CUtensorMap& tmQs, const CUtensorMap& tmDs,
+                            const CUtensorMap& tmW, const CUtensorMap& tmW2, const PathColArgs& a, cudaStream_t st) {
+  return launch_persistent(path_col_kernel, pcl::kSmem, a.NB * a.B * a.HQ, st, tmDA, tmQs, tmDs, tmW, tmW2, a);
+}
+
+}  // namespace lb

@@ -1,0 +1,175 @@
+"""LUCID-Path on the B200 kernels: the drop-in for
+``parallel_lucid_path_attention`` (lucid_path/triton_code/parallel.py:180-241).
+
+    o, k_cache = parallel_lucid_path_attention(k, v, w, beta, q=None, g=None,
+                                               scale=None, cu_seqlens=None,
+                                               use_cache=False)
+
+solves (I + L) O = V with L = stril(exp(scale * A - 1/scale)) and the
+Householder-path scores A_rc = q_r^T (H_r ... H_{c+1}) k_c,
+H_t = I - beta_t w_t w_t^T.  Layout is the reference's BTHD: k, v, w
+[B, T, H, K], beta [B, T, H], q [B, T, HQ, K] (defaults to k), o [B, T, HQ, V].
+
+The forward and backward are the C-ABI entry points lucid_path_fwd /
+lucid_path_bwd (include/lucid_b200.h); the forward's workspace is the state
+saved for the backward.  There is no CPU path: CPU tensors raise.
+
+Differences from the reference, all raising instead of computing something
+else: head_dim must be 128 (the reference accepts 16/32/64/128, parallel.py:230);
+``g`` must be None (the reference asserts the same, :235); ``use_cache=True``
+(the decode-time key cache of prepare_k_cache.py) is not built yet.
+``cu_seqlens`` (packed variable-length batches, B == 1) runs one call per
+sequence.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = ["parallel_lucid_path_attention", "ParallelLUCIDPathAttentionFunction", "path_fwd", "path_bwd"]
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _prep(t: torch.Tensor, name: str, ndim: int = 4) -> torch.Tensor:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: LUCID B200 kernels need CUDA tensors (no CPU fallback)")
+    if t.dim() != ndim:
+        raise ValueError(f"{name}: expected a {ndim}-D tensor, got shape {tuple(t.shape)}")
+    if ndim == 4:
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name}: expected bfloat16, got {t.dtype}")
+        ok = t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+        return t if ok else t.contiguous()
+    if t.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"{name}: expected bfloat16 or float32, got {t.dtype}")
+    return t
+
+
+def _s3(t: torch.Tensor):
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def path_fwd(k, v, w, beta, q=None, scale=None):
+    """Forward stage.  Returns (o [B,T,HQ,V], state); ``state`` is the
+    forward workspace the backward reads."""
+    lib = _lib.load()
+    k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
+    beta = _prep(beta, "beta", 3)
+    B, T, H, K = k.shape
+    if K != 128 or v.shape[-1] != 128:
+        raise NotImplementedError("LUCID-Path B200 kernels support head_dim 128 only")
+    if w.shape != k.shape or v.shape[:3] != k.shape[:3] or tuple(beta.shape) != (B, T, H):
+        raise ValueError("k, v, w must be [B, T, H, 128] and beta [B, T, H]")
+    if q is not None:
+        q = _prep(q, "q")
+        if q.shape[0] != B or q.shape[1] != T or q.shape[3] != K or q.shape[2] % H != 0:
+            raise ValueError("q must be [B, T, HQ, 128] with HQ a multiple of H")
+    HQ = q.shape[2] if q is not None else H
+    s = float(K ** -0.5 if scale is None else scale)
+    dev = k.device
+    o = torch.empty(B, T, HQ, v.shape[-1], dtype=v.dtype, device=dev)
+    ws = _ws(lib.lucid_path_fwd_workspace_bytes(B, T, H, HQ, K), dev)
+    qp, qs = (q.data_ptr(), _s3(q)) if q is not None else (None, (0, 0, 0))
+    rc = lib.lucid_path_fwd(B, T, H, HQ, K, s, qp, *qs, k.data_ptr(), *_s3(k), v.data_ptr(), *_s3(v),
+                            w.data_ptr(), *_s3(w), beta.data_ptr(), int(beta.dtype == torch.float32), *beta.stride(),
+                            o.data_ptr(), *_s3(o), ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_path_fwd")
+    return o, ws
+
+
+def path_bwd(state, do, k, w, beta, q=None, scale=None):
+    """Backward stage.  Returns (dq or None, dk, dv, dw, dbeta); with q None
+    the query gradient is folded into dk (q = k)."""
+    lib = _lib.load()
+    k, w, do = _prep(k, "k"), _prep(w, "w"), _prep(do, "do")
+    beta = _prep(beta, "beta", 3)
+    B, T, H, K = k.shape
+    HQ = q.shape[2] if q is not None else H
+    s = float(K ** -0.5 if scale is None else scale)
+    dev = k.device
+    dk = torch.empty(B, T, H, K, dtype=k.dtype, device=dev)
+    dv = torch.empty(B, T, H, K, dtype=k.dtype, device=dev)
+    dw = torch.empty(B, T, H, K, dtype=w.dtype, device=dev)
+    dbeta = torch.empty(B, T, H, dtype=beta.dtype, device=dev)
+    dq = None
+    if q is not None:
+        q = _prep(q, "q")
+        dq = torch.empty(B, T, HQ, K, dtype=q.dtype, device=dev)
+    ws = _ws(lib.lucid_path_bwd_workspace_bytes(B, T, H, HQ, K), dev)
+    qp, qs = (q.data_ptr(), _s3(q)) if q is not None else (None, (0, 0, 0))
+    dqp, dqs = (dq.data_ptr(), _s3(dq)) if dq is not None else (None, (0, 0, 0))
+    rc = lib.lucid_path_bwd(B, T, H, HQ, K, s, qp, *qs, k.data_ptr(), *_s3(k), w.data_ptr(), *_s3(w),
+                            beta.data_ptr(), int(beta.dtype == torch.float32), *beta.stride(),
+                            do.data_ptr(), *_s3(do), state.data_ptr(), state.numel(),
+                            dqp, *dqs, dk.data_ptr(), *_s3(dk), dv.data_ptr(), *_s3(dv), dw.data_ptr(), *_s3(dw),
+                            dbeta.data_ptr(), int(dbeta.dtype == torch.float32), *dbeta.stride(),
+                            ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_path_bwd")
+    return dq, dk, dv, dw, dbeta
+
+
+class ParallelLUCIDPathAttentionFunction(torch.autograd.Function):
+    """Autograd mirror of parallel.py:27-177 (same positional arguments)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, w, beta, g, scale, cu_seqlens, use_cache=False):
+        if g is not None:
+            raise NotImplementedError("g is not supported (the reference asserts g is None)")
+        q_given = q is not None and q is not k
+        o, state = path_fwd(k, v, w, beta, q=q if q_given else None, scale=scale)
+        ctx.save_for_backward(q if q_given else None, k, w, beta, state)
+        ctx.q_given = q_given
+        ctx.q_is_k = q is k
+        ctx.scale = scale
+        return o, None
+
+    @staticmethod
+    def backward(ctx, do, dk_cache):
+        q, k, w, beta, state = ctx.saved_tensors
+        dq, dk, dv, dw, dbeta = path_bwd(state, do, k, w, beta, q=q, scale=ctx.scale)
+        if ctx.q_is_k:
+            # q and k are the same tensor: the reference returns dq and dk
+            # separately and autograd sums them; dk already holds the sum.
+            return None, dk, dv, dw, dbeta, None, None, None, None
+        return dq, dk, dv, dw, dbeta, None, None, None, None
+
+
+def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_seqlens=None, use_cache=False):
+    """Drop-in for lucid_path/triton_code/parallel.py:180-241; returns (o, k_cache)."""
+    if use_cache:
+        raise NotImplementedError("use_cache=True (prepare_k_cache) is not implemented")
+    if q is None:
+        q = k
+    if scale is None:
+        scale = k.shape[-1] ** -0.5
+    if q.shape[-1] != k.shape[-1]:
+        raise ValueError("q, k should have the same head_dim.")
+    if k.shape != w.shape:
+        raise ValueError("k, w should have the same shape.")
+    if beta.shape[:3] != k.shape[:3]:
+        raise ValueError("beta should have the same number of heads as k")
+    if g is not None:
+        raise NotImplementedError("g is not supported")
+    if q.shape[-2] % k.shape[-2] != 0:
+        raise ValueError("the number of query heads should be divisible by the number of key heads")
+    if cu_seqlens is None:
+        return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, False)
+    if k.shape[0] != 1:
+        raise ValueError("cu_seqlens requires a packed batch of size 1")
+    bounds = [int(x) for x in cu_seqlens.tolist()]
+    outs = []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        qa = q[:, a:b] if q is not k else None
+        ka = k[:, a:b]
+        o, _ = ParallelLUCIDPathAttentionFunction.apply(qa if qa is not None else ka, ka, v[:, a:b], w[:, a:b],
+                                                        beta[:, a:b], None, float(scale), None, False)
+        outs.append(o)
+    return torch.cat(outs, dim=1), None

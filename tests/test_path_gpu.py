@@ -1,0 +1,141 @@
+"""LUCID-Path on the B200 kernels against the reference and the oracle.
+
+Reference: the fixtures of tests/golden/make_path_golden.py (the reference's
+Triton op in float32).  Oracle: oracle/path_oracle.py (float64).  The kernels
+compute in bf16 with fp32 accumulation, so the bars are:
+
+  o:          max |o - ref| <= 1e-2 (the op's bf16 tolerance) + 2^-8 |ref|
+  gradients:  max |g - ref| <= 2e-2 * max |ref|   (the gradients of the
+              default-scale fixtures are ~1e-3 in magnitude, so an absolute
+              1e-2 bar would be vacuous; the bar is relative to their scale)
+"""
+import numpy as np
+import pytest
+
+from conftest import PATH_CASES, load_path_golden
+
+pytestmark = pytest.mark.gpu
+
+GRADS = ("dq", "dk", "dv", "dw", "dbeta")
+
+
+def _to(torch, a, dev, dtype=None):
+    return torch.tensor(a, dtype=torch.float32).to(dev, dtype or torch.bfloat16)
+
+
+def _run(torch, d, dev, scale=None, backward=True):
+    from lucid_b200.path import parallel_lucid_path_attention
+    k = _to(torch, d["k"], dev).requires_grad_(backward)
+    v = _to(torch, d["v"], dev).requires_grad_(backward)
+    w = _to(torch, d["w"], dev).requires_grad_(backward)
+    beta = _to(torch, d["beta"], dev).requires_grad_(backward)
+    q = _to(torch, d["q"], dev).requires_grad_(backward) if d.get("q") is not None else None
+    o, kc = parallel_lucid_path_attention(k, v, w, beta, q=q, scale=scale)
+    assert kc is None
+    out = {"o": o.float().cpu().numpy()}
+    if backward:
+        o.backward(_to(torch, d["do"], dev))
+        torch.cuda.synchronize()
+        out.update(dk=k.grad.float().cpu().numpy(), dv=v.grad.float().cpu().numpy(),
+                   dw=w.grad.float().cpu().numpy(), dbeta=beta.grad.float().cpu().numpy())
+        if q is not None:
+            out["dq"] = q.grad.float().cpu().numpy()
+    return out
+
+
+def _check(got, ref, label):
+    o, ro = got["o"], ref["o"]
+    assert np.all(np.isfinite(o)), label
+    err = np.abs(o - ro) - (1e-2 + 2.0 ** -8 * np.abs(ro))
+    assert err.max() <= 0, f"{label} o: max err {np.abs(o - ro).max():.3e}"
+    for nm in GRADS:
+        if nm not in ref or nm not in got:
+            continue
+        g, r = got[nm], ref[nm]
+        assert np.all(np.isfinite(g)), f"{label} {nm}"
+        rel = np.abs(g - r).max() / max(np.abs(r).max(), 1e-30)
+        assert rel <= 2e-2, f"{label} {nm}: max err {np.abs(g - r).max():.3e} (rel {rel:.3e})"
+
+
+@pytest.mark.parametrize("name", [c for c in PATH_CASES if "k128" in c])
+def test_path_matches_reference_fixture(cuda_device, name):
+    torch = pytest.importorskip("torch")
+    d = load_path_golden(name)
+    got = _run(torch, d, cuda_device)
+    _check(got, d, name)
+
+
+@pytest.mark.parametrize("B,T,H,HQ,with_q,scale", [
+    (1, 300, 1, 1, False, 0.15),     # ragged T, large path scores
+    (2, 256, 2, 2, False, 0.15),     # two batches, two heads
+    (1, 260, 1, 2, True, 0.15),      # grouped query heads with explicit q
+    (1, 128, 1, 1, False, 0.15),     # a single block (diagonal only)
+    (1, 77, 2, 2, False, None),      # shorter than one block, default scale
+])
+def test_path_matches_oracle(cuda_device, B, T, H, HQ, with_q, scale):
+    torch = pytest.importorskip("torch")
+    from oracle.path_oracle import make_path_inputs, path_fwd_bwd_torch
+    d = make_path_inputs(100 + T + HQ, B, T, H, 128, HQ, with_q)
+    o, dq, dk, dv, dw, db = path_fwd_bwd_torch(d["k"], d["v"], d["w"], d["beta"], d["do"], q=d["q"], scale=scale)
+    ref = dict(o=o, dk=dk, dv=dv, dw=dw, dbeta=db)
+    if dq is not None:
+        ref["dq"] = dq
+    got = _run(torch, d, cuda_device, scale=scale)
+    _check(got, ref, f"B{B} T{T} H{H} HQ{HQ}")
+
+
+def test_path_forward_long_sequence_matches_oracle(cuda_device):
+    """16 row blocks: the wavefront solve and the score chain over many blocks."""
+    torch = pytest.importorskip("torch")
+    from oracle.path_oracle import make_path_inputs, path_fwd
+    d = make_path_inputs(5, 1, 2048, 1, 128)
+    ref, _ = path_fwd(d["k"], d["v"], d["w"], d["beta"], scale=0.15)
+    got = _run(torch, d, cuda_device, scale=0.15, backward=False)
+    _check(got, {"o": ref}, "T2048")
+
+
+def test_path_solve_is_linear_in_v(cuda_device):
+    """O = (I + L)^-1 V is linear in V at the benchmark's block count."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200.path import parallel_lucid_path_attention
+    g = torch.Generator(device="cpu").manual_seed(3)
+    B, T, H = 1, 4096, 2
+    k = torch.randn(B, T, H, 128, generator=g)
+    w = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g), dim=-1)
+    beta = 2 * torch.sigmoid(torch.randn(B, T, H, generator=g))
+    v1 = torch.randn(B, T, H, 128, generator=g)
+    v2 = torch.randn(B, T, H, 128, generator=g)
+    dev = cuda_device
+    k, w, beta = (t.to(dev, torch.bfloat16) for t in (k, w, beta))
+    with torch.no_grad():
+        o1, _ = parallel_lucid_path_attention(k, v1.to(dev, torch.bfloat16), w, beta, scale=0.15)
+        o2, _ = parallel_lucid_path_attention(k, v2.to(dev, torch.bfloat16), w, beta, scale=0.15)
+        o12, _ = parallel_lucid_path_attention(k, (v1 + v2).to(dev, torch.bfloat16), w, beta, scale=0.15)
+    diff = (o12.float() - o1.float() - o2.float()).abs().max().item()
+    assert diff < 5e-2, diff
+    assert torch.isfinite(o12).all()
+
+
+def test_path_deterministic(cuda_device):
+    torch = pytest.importorskip("torch")
+    from oracle.path_oracle import make_path_inputs
+    d = make_path_inputs(9, 1, 384, 1, 128)
+    a = _run(torch, d, cuda_device, scale=0.15)
+    b = _run(torch, d, cuda_device, scale=0.15)
+    for nm in ("o", "dk", "dv", "dw", "dbeta"):
+        np.testing.assert_array_equal(a[nm], b[nm])
+
+
+def test_path_varlen_matches_separate_sequences(cuda_device):
+    torch = pytest.importorskip("torch")
+    from lucid_b200.path import parallel_lucid_path_attention
+    from oracle.path_oracle import make_path_inputs
+    d = make_path_inputs(21, 1, 400, 1, 128)
+    dev = cuda_device
+    k, v, w, beta = (_to(torch, d[n], dev) for n in ("k", "v", "w", "beta"))
+    cu = torch.tensor([0, 150, 400], dtype=torch.int32, device=dev)
+    with torch.no_grad():
+        o, _ = parallel_lucid_path_attention(k, v, w, beta, cu_seqlens=cu, scale=0.15)
+        o_a, _ = parallel_lucid_path_attention(k[:, :150], v[:, :150], w[:, :150], beta[:, :150], scale=0.15)
+        o_b, _ = parallel_lucid_path_attention(k[:, 150:], v[:, 150:], w[:, 150:], beta[:, 150:], scale=0.15)
+    torch.testing.assert_close(o, torch.cat([o_a, o_b], 1), rtol=0, atol=0)
