@@ -178,7 +178,7 @@ POperand opnd_rs(const PMat& m, int trans, const PVec& rs) {
 
 // bf16 tensor map over an internal [heads][rows][128] buffer.
 bool tm_int(CUtensorMap* m, const void* p, long long heads, long long rows) {
-  return make_tmap_bf16(m, p, 128, (int)rows, (int)heads, 1, 128, rows * 128, 0);
+  return make_tmap_bf16(m, p, 128, (int)rows, (int)heads, 1, 128, rows * 128, heads * rows * 128);
 }
 // bf16 tensor map over the caller's [B, T, heads, 128].
 bool tm_user(CUtensorMap* m, const void* p, int B, int T, int heads, int64_t sb, int64_t st, int64_t sh) {

@@ -5,7 +5,8 @@
 //
 //   path_scores_kernel  off-diagonal path scores (triangular_solve_fwd.py:177-209).
 //       Row block i walks j = i-1 .. 0 carrying Q~ (fp32 in registers):
-//         S = Q~ K_new_j^T -> L_ij = exp(s S - 1/s) (bf16 tile to HBM)
+//         S = Q~ K_new_j^T -> L_ij = exp(s S - 1/s) (bf16 tile to HBM;
+//             Q~ enters as bf16 hi + lo, so the score keeps ~16 mantissa bits)
 //         Q~ <- Q~ - (Q~ W_j^T) W2_j               (two MMAs, -S2 staged in TMEM)
 //       The bf16 operand copy of every Q~ is also stored (TMA) for the backward.
 //   path_solve_kernel<false>  O = (I + L)^-1 V, block forward substitution as a
@@ -111,7 +112,7 @@ struct TileRing {
 // ===========================================================================
 namespace psc {
 constexpr int kRing = 4;
-constexpr uint32_t kOffQ = 0, kOffRing = 32768, kOffBar = kOffRing + kRing * 32768;
+constexpr uint32_t kOffQ = 0, kOffQlo = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
 enum { RF0 = 0, RE0 = RF0 + kRing, QOP_FULL = RE0 + kRing, QFREE, QWRITTEN, SS_FULL, NS2_FULL, D_FULL, DRAIN, NBAR };
 constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmS2 = 128;
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
   const Abort ab{abort_cta, p.status, kTagPathScores};
-  const uint32_t sQ = sbase + kOffQ;
+  const uint32_t sQ = sbase + kOffQ, sQlo = sbase + kOffQlo;
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagPathScores << 20));
@@ -209,6 +210,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
           }
           tc_fence_after();
           umma_tile(tmem + kTmS, sQ, false, ring_slot(sK), false, 0u);
+          umma_tile(tmem + kTmS, sQlo, false, ring_slot(sK), false, 1u);
           if (j > 0) umma_tile(tmem + kTmS2, sQ, false, ring_slot(sW), false, 0u);
           umma_commit(bar(SS_FULL));
           ring_free(sK);
@@ -243,7 +245,16 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       }
       __syncwarp();
       if (!pwarp_wait(bar(QFREE), (n_qf++) & 1, ab)) return false;
-      tile_store_row64(sQ, r, hf, q);
+      {  // Q~ = hi + lo (bf16 each): the score GEMM uses both, the chain GEMM and the snapshot hi
+        float hi[64], lo[64];
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          hi[e] = __bfloat162float(__float2bfloat16(q[e]));
+          lo[e] = q[e] - hi[e];
+        }
+        tile_store_row64(sQ, r, hf, hi);
+        tile_store_row64(sQlo, r, hf, lo);
+      }
       fence_proxy_async_smem();
       mbar_arrive(bar(QWRITTEN));
       if (threadIdx.x == 0) {
@@ -315,7 +326,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 // ===========================================================================
 namespace psv {
 constexpr int kRing = 4;
-constexpr uint32_t kOffY = 0, kOffRing = 32768, kOffBar = kOffRing + kRing * 32768;
+constexpr uint32_t kOffY = 0, kOffY2 = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
 enum { RF0 = 0, RE0 = RF0 + kRing, ACC_FULL = RE0 + kRing, Y_FULL, T_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR };
 constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmAcc = 0, kTmT = 128;
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
   volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
   const Abort ab{abort_cta, p.status, TR ? kTagPathSolveT : kTagPathSolve};
-  const uint32_t sY = sbase + kOffY;
+  const uint32_t sY = sbase + kOffY, sY2 = sbase + kOffY2;
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
@@ -373,7 +384,9 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     bhq = idx % BHQ;
     ndeps = TR ? p.NB - 1 - blk : blk;
   };
-  auto dep_block = [&](int blk, int d) { return TR ? blk + 1 + d : d; };
+  // dependencies in the order they were published (oldest first), so a block
+  // stalls only on its last dependency
+  auto dep_block = [&](int blk, int d) { (void)blk; return TR ? p.NB - 1 - d : d; };
   auto pair_of = [&](int blk, int db) { return TR ? path_pair(db, blk) : path_pair(blk, db); };
 
   if (warp == pk::kWarpTma) {
@@ -419,6 +432,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         if (!ring_wait(sU) || !mbar_wait(bar(Y_FULL), (n_y++) & 1, ab)) break;
         tc_fence_after();
         umma_tile(tmem + kTmT, ring_slot(sU), TR, sY, true, 0u);
+        umma_tile(tmem + kTmT, ring_slot(sU), TR, sY2, true, 1u);
         umma_commit(bar(T_FULL));
         ring_free(sU);
       }
@@ -456,7 +470,16 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 64; ++e) R[e] = -R[e];
       }
-      tile_store_row64(sY, r, hf, R);
+      {  // R = hi + lo, both bf16: the diagonal product U R keeps ~16 mantissa bits
+        float hi[64], lo[64];
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          hi[e] = __bfloat162float(__float2bfloat16(R[e]));
+          lo[e] = R[e] - hi[e];
+        }
+        tile_store_row64(sY, r, hf, hi);
+        tile_store_row64(sY2, r, hf, lo);
+      }
       fence_proxy_async_smem();
       mbar_arrive(bar(Y_FULL));
       if (!pwarp_wait(bar(T_FULL), (n_t++) & 1, ab)) break;

@@ -28,11 +28,26 @@ inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// cuTensorMapEncodeTiled needs the device's context current in the calling
+// thread.  A thread that has only set the device (e.g. the autograd engine's
+// worker thread) has no current context until its first runtime call, so
+// bind the primary context once per (thread, device).
+inline void bind_current_context() {
+  thread_local int bound_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (dev != bound_dev) {
+    cudaFree(nullptr);
+    bound_dev = dev;
+  }
+}
+
 // bf16 [c3][c2][rows][cols] view with element strides (s_row, s_c2, s_c3);
 // box = 64 columns x 128 rows, 128-byte swizzle.  Rows beyond `rows` read
 // as zero.
 inline bool make_tmap_bf16(CUtensorMap* m, const void* ptr, int cols, int rows, int n2, int n3,
                            long long s_row, long long s_c2, long long s_c3) {
+  bind_current_context();
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)n2, (cuuint64_t)n3};
@@ -48,6 +63,7 @@ inline bool make_tmap_bf16(CUtensorMap* m, const void* ptr, int cols, int rows, 
 // fp32 [rows][128] matrix, box = 32 columns (128 bytes) x 128 rows,
 // 128-byte swizzle: the target of the bulk reduce-adds of the backward.
 inline bool make_tmap_f32_rows(CUtensorMap* m, const void* ptr, long long rows) {
+  bind_current_context();
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {128, (cuuint64_t)rows};

@@ -4,7 +4,10 @@ Reference: the fixtures of tests/golden/make_path_golden.py (the reference's
 Triton op in float32).  Oracle: oracle/path_oracle.py (float64).  The kernels
 compute in bf16 with fp32 accumulation, so the bars are:
 
-  o:          max |o - ref| <= 1e-2 (the op's bf16 tolerance) + 2^-8 |ref|
+  o:          max |o - ref| <= 1e-2 (the op's bf16 tolerance) + 2^-8 |ref|, or,
+              where the path scores are large (scale 0.15), no more than 1.5x
+              the deviation of the reference's own bf16 forward, modelled by
+              oracle/path_precision.py
   gradients:  max |g - ref| <= 2e-2 * max |ref|   (the gradients of the
               default-scale fixtures are ~1e-3 in magnitude, so an absolute
               1e-2 bar would be vacuous; the bar is relative to their scale)
@@ -32,7 +35,7 @@ def _run(torch, d, dev, scale=None, backward=True):
     q = _to(torch, d["q"], dev).requires_grad_(backward) if d.get("q") is not None else None
     o, kc = parallel_lucid_path_attention(k, v, w, beta, q=q, scale=scale)
     assert kc is None
-    out = {"o": o.float().cpu().numpy()}
+    out = {"o": o.detach().float().cpu().numpy()}
     if backward:
         o.backward(_to(torch, d["do"], dev))
         torch.cuda.synchronize()
@@ -43,11 +46,15 @@ def _run(torch, d, dev, scale=None, backward=True):
     return out
 
 
-def _check(got, ref, label):
+def _check(got, ref, label, ref_dev=None):
     o, ro = got["o"], ref["o"]
     assert np.all(np.isfinite(o)), label
-    err = np.abs(o - ro) - (1e-2 + 2.0 ** -8 * np.abs(ro))
-    assert err.max() <= 0, f"{label} o: max err {np.abs(o - ro).max():.3e}"
+    if ref_dev is None:
+        err = np.abs(o - ro) - (1e-2 + 2.0 ** -8 * np.abs(ro))
+        assert err.max() <= 0, f"{label} o: max err {np.abs(o - ro).max():.3e}"
+    else:
+        dev = np.abs(o - ro).max()
+        assert dev <= max(1.5 * ref_dev, 1e-2), f"{label} o: max err {dev:.3e}, reference model {ref_dev:.3e}"
     for nm in GRADS:
         if nm not in ref or nm not in got:
             continue
@@ -81,7 +88,12 @@ def test_path_matches_oracle(cuda_device, B, T, H, HQ, with_q, scale):
     if dq is not None:
         ref["dq"] = dq
     got = _run(torch, d, cuda_device, scale=scale)
-    _check(got, ref, f"B{B} T{T} H{H} HQ{HQ}")
+    ref_dev = None
+    if scale is not None:
+        from oracle.path_precision import reference_bf16_forward
+        om = reference_bf16_forward(d["k"], d["v"], d["w"], d["beta"], q=d["q"], scale=scale)
+        ref_dev = float(np.abs(om - o).max())
+    _check(got, ref, f"B{B} T{T} H{H} HQ{HQ}", ref_dev)
 
 
 def test_path_forward_long_sequence_matches_oracle(cuda_device):
@@ -89,9 +101,11 @@ def test_path_forward_long_sequence_matches_oracle(cuda_device):
     torch = pytest.importorskip("torch")
     from oracle.path_oracle import make_path_inputs, path_fwd
     d = make_path_inputs(5, 1, 2048, 1, 128)
+    from oracle.path_precision import reference_bf16_forward
     ref, _ = path_fwd(d["k"], d["v"], d["w"], d["beta"], scale=0.15)
+    ref_dev = float(np.abs(reference_bf16_forward(d["k"], d["v"], d["w"], d["beta"], scale=0.15) - ref).max())
     got = _run(torch, d, cuda_device, scale=0.15, backward=False)
-    _check(got, {"o": ref}, "T2048")
+    _check(got, {"o": ref}, "T2048", ref_dev)
 
 
 def test_path_solve_is_linear_in_v(cuda_device):
@@ -111,8 +125,9 @@ def test_path_solve_is_linear_in_v(cuda_device):
         o1, _ = parallel_lucid_path_attention(k, v1.to(dev, torch.bfloat16), w, beta, scale=0.15)
         o2, _ = parallel_lucid_path_attention(k, v2.to(dev, torch.bfloat16), w, beta, scale=0.15)
         o12, _ = parallel_lucid_path_attention(k, (v1 + v2).to(dev, torch.bfloat16), w, beta, scale=0.15)
+    # bf16 outputs and operands: linear up to a few bf16 ulps of |o|
     diff = (o12.float() - o1.float() - o2.float()).abs().max().item()
-    assert diff < 5e-2, diff
+    assert diff < 1e-2 * o12.float().abs().max().item(), diff
     assert torch.isfinite(o12).all()
 
 

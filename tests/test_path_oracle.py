@@ -71,3 +71,18 @@ def test_unit_diagonal_and_identity_limit():
     Lr = np.tril(np.exp(s * k @ k.T - 1 / s), -1)
     assert np.allclose(L[0, 0], Lr)
     assert np.allclose(o[0, :, 0], np.linalg.solve(np.eye(24) + Lr, d["v"][0, :, 0]))
+
+
+def test_reference_precision_model_is_close_to_float64():
+    """The bf16/TF32 model of the reference forward stays within bf16 error of
+    the float64 oracle, and equals it when every rounding point is exact
+    (w = 0, integer-valued v, L tiny)."""
+    from oracle.path_precision import reference_bf16_forward
+    d = make_path_inputs(4, 1, 200, 1, 128)
+    o, _ = path_fwd(d["k"], d["v"], d["w"], d["beta"])
+    om = reference_bf16_forward(d["k"], d["v"], d["w"], d["beta"])
+    assert np.abs(om - o).max() < 1e-2
+    d2 = make_path_inputs(4, 1, 150, 2, 32, HQ=4, with_q=True)
+    o2, _ = path_fwd(d2["k"], d2["v"], d2["w"], d2["beta"], q=d2["q"])
+    om2 = reference_bf16_forward(d2["k"], d2["v"], d2["w"], d2["beta"], q=d2["q"])
+    assert np.abs(om2 - o2).max() < 3e-2
