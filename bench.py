@@ -18,6 +18,11 @@ every rank runs its own batch element (weak scaling); the step time is the
 max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--config path measures the LUCID-Path op instead (
+parallel_lucid_path_attention fwd+bwd, B=2, H=16, T=16384, K=V=128, bf16,
+q = k; k, v ~ N(0,1), w ~ N(0,1) L2-normalised, beta = 2 sigmoid(N(0,1)),
+dO ~ N(0,1)), with the algorithmic count 14 T^2 K per (batch, head).
 """
 from __future__ import annotations
 
@@ -79,9 +84,20 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: begin the timed region only once
+        # it has written its first sample (short regions would see none)
+        t0 = time.time()
+        while time.time() - t0 < 5.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -147,6 +163,8 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.config == "path":
+        return path_reference_arm(args)
     B, H, N, D, _ = CONFIGS[args.config]
     n_cpu = args.cpu_n
     cpu_reference_sample(1024, D)
@@ -170,6 +188,210 @@ def reference_arm(args):
 
 
 # ---------------------------------------------------------------------------
+# LUCID-Path
+# ---------------------------------------------------------------------------
+PATH_METRIC = "LUCID-Path fwd+bwd TFLOP/s (parallel_lucid_path_attention, B2 H16 T16384 K128)"
+PATH_CONFIG = (2, 16, 16384, 128)   # B per rank, H, T, K
+
+
+def path_cpu_sample(T: int, seed: int = 0):
+    """Seconds for one (batch, head) of the LUCID-Path fwd+bwd at length T on
+    the host: the float64 block restatement of the reference algorithm
+    (oracle/path_oracle.py, blocks of 64 like the reference)."""
+    from oracle.path_oracle import make_path_inputs, path_bwd_blockwise
+    d = make_path_inputs(seed, 1, T, 1, 128)
+    t0 = time.perf_counter()
+    path_bwd_blockwise(d["k"], d["v"], d["w"], d["beta"], d["do"], bt=64)
+    return time.perf_counter() - t0
+
+
+def path_reference_arm(args):
+    B, H, T, K = PATH_CONFIG
+    n_cpu = min(args.cpu_n, 4096)
+    path_cpu_sample(256)
+    for _ in range(args.warmup):
+        path_cpu_sample(n_cpu)
+    times = [path_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
+    t = sum(times) / len(times)
+    val = 14.0 * n_cpu * n_cpu * K / t / 1e12
+    line = {
+        "impl": "reference", "metric": PATH_METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"LUCID-Path fwd+bwd B{B} H{H} T{T} K{K} (sampled: 1 head at T={n_cpu})",
+                   "global_batch": B, "seq_len": T, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"1 (batch, head) at T={n_cpu}, float64 numpy, oracle/path_oracle.py"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_path(args, torch, dist, dev, world, rank, local, barrier):
+    import ctypes as ct
+    from lucid_b200 import _lib
+    from lucid_b200.path import parallel_lucid_path_attention, path_bwd, path_fwd
+    lib = _lib.load()
+    B, H, T, K = PATH_CONFIG
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    k = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
+    v = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
+    w = torch.nn.functional.normalize(torch.randn(B, T, H, K, generator=g, device=dev), dim=-1).bfloat16()
+    w.requires_grad_(True)
+    beta = (2 * torch.sigmoid(torch.randn(B, T, H, generator=g, device=dev))).bfloat16().requires_grad_(True)
+    do = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16()
+
+    def step():
+        k.grad = v.grad = w.grad = beta.grad = None
+        o, _ = parallel_lucid_path_attention(k, v, w, beta)
+        o.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    fl = 14.0 * T * T * K * B * H * world
+    tflops = fl / (ms * 1e-3) / 1e12
+
+    # ---- per kernel family (profile hook), dominant kernel -> roofline ----
+    pk_burst, pk_sust, hbm, pk_kind = peaks()
+    stage_ms, stage_n = {}, {}
+    names = ["path_block", "path_scores", "path_solve", "path_solve_t", "path_row", "path_col"]
+    with torch.no_grad():
+        kd, vd, wd, bd = (t.detach() for t in (k, v, w, beta))
+        for name in names:
+            lib.lucid_profile_enable(_lib.KERNEL_IDS[name])
+            for _ in range(2):
+                o, st = path_fwd(kd, vd, wd, bd)
+                path_bwd(st, do, kd, wd, bd)
+                del o, st
+            torch.cuda.synchronize()
+            tot, n = ct.c_float(), ct.c_int()
+            lib.lucid_profile_read(ct.byref(tot), ct.byref(n))
+            stage_ms[name] = tot.value / 2
+            stage_n[name] = n.value // 2
+        lib.lucid_profile_enable(0)
+    # algorithmic bytes / flops of each O(T^2) kernel per (batch, head): one 128x128
+    # bf16 tile is 32 KiB, one 128^3 tile GEMM is 2*128^3 flops
+    NB = T // 128
+    pairs = NB * (NB - 1) // 2 * B * H
+    tile_b, tile_f = 128 * 128 * 2, 2.0 * 128 ** 3
+    alg = {  # (bytes that must cross HBM, tensor flops)
+        "path_scores": (2 * pairs * tile_b, 4 * pairs * tile_f),     # write L and Q~; S hi+lo, S2, update
+        "path_solve": (pairs * tile_b, pairs * tile_f),               # read L; L O
+        "path_solve_t": (pairs * tile_b, pairs * tile_f),
+        "path_row": (3 * pairs * tile_b, 4 * pairs * tile_f),         # read L, write dA and dQ~; 4 GEMMs
+        "path_col": (3 * pairs * tile_b, 2 * pairs * tile_f),         # read dA, Q~, dQ~; 2 GEMMs
+    }
+    stage = {}
+    for n_, (by, fl_) in alg.items():
+        sec = stage_ms[n_] * 1e-3
+        stage[n_] = {"ms": stage_ms[n_], "gbs": by / sec / 1e9, "hbm_frac": by / sec / 1e9 / hbm,
+                     "tflops": fl_ / sec / 1e12, "tensor_frac": fl_ / sec / 1e12 / pk_burst}
+    dom = max(alg, key=lambda n_: stage_ms[n_])
+    bound = "hbm" if stage[dom]["hbm_frac"] >= stage[dom]["tensor_frac"] else "tensor"
+    if bound == "hbm":
+        roof = {"bound": "hbm", "kernel": dom, "achieved": stage[dom]["gbs"], "peak": hbm, "unit": "GB/s",
+                "frac": stage[dom]["hbm_frac"], "peak_kind": f"{pk_kind} HBM copy bandwidth"}
+    else:
+        roof = {"bound": "tensor", "kernel": dom, "achieved": stage[dom]["tflops"], "peak": pk_burst,
+                "unit": "TFLOP/s", "frac": stage[dom]["tensor_frac"], "peak_kind": f"{pk_kind} burst bf16"}
+    roof["traffic"] = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tj = json.load(f)
+            if tj.get("config") == "path":
+                roof["traffic"] = tj.get(dom)
+        except Exception:
+            pass
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        hk, hv, hw, hb, hdo = (t.detach().cpu().pin_memory() for t in (k, v, w, beta, do))
+        outs = [torch.empty_like(hk).pin_memory() for _ in range(4)] + [torch.empty_like(hb).pin_memory()]
+
+        def e2e_step():
+            kk, vv, ww, bb = (h.to(dev, non_blocking=True).requires_grad_(True) for h in (hk, hv, hw, hb))
+            dd = hdo.to(dev, non_blocking=True)
+            oo, _ = parallel_lucid_path_attention(kk, vv, ww, bb)
+            oo.backward(dd)
+            for h, t in zip(outs, (oo, kk.grad, vv.grad, ww.grad, bb.grad)):
+                h.copy_(t.detach(), non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ne = max(1, min(args.steps, 3))
+        a0.record()
+        for _ in range(ne):
+            e2e_step()
+        a1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = a0.elapsed_time(a1) / ne
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        nb4 = B * T * H * K * 2
+        e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": 4 * nb4 + B * T * H * 2, "d2h_bytes_per_step": 4 * nb4 + B * T * H * 2}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n_cpu = min(args.cpu_n, 4096)
+        path_cpu_sample(256)
+        tc = min(path_cpu_sample(n_cpu, seed=i) for i in range(2))
+        cpu = {"value": 14.0 * n_cpu * n_cpu * K / tc / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": f"1 (batch, head) at T={n_cpu}, float64 numpy block restatement "
+                                         f"(oracle/path_oracle.py), best of 2",
+               "seconds_per_sample": tc}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    # the hook brackets the dbeta row-dot and the three gradient packs as one scope
+    launches = sum(stage_n.values()) - 1 + 4
+    line = {
+        "metric": PATH_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"LUCID-Path fwd+bwd B{B} H{H} T{T} K{K} per GPU, q = k",
+                   "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": K,
+                   "parallelism": f"(batch,head) shards x{world}, no collective",
+                   "l2": "inputs and path tiles larger than L2, no flush"},
+        "tokens_per_s": B * T * world / (ms * 1e-3),
+        "frac_of_bf16_peak": tflops / pk_sust,
+        "stage": stage, "stage_ms": stage_ms, "roofline": roof, "clocks": clk,
+        "gpu_launches": launches * args.steps, "e2e": e2e, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def main(argv=None):
@@ -178,7 +400,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="32k")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path"], default="32k")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -204,6 +426,8 @@ def main(argv=None):
         if world > 1:
             dist.barrier()
 
+    if args.config == "path":
+        return bench_path(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
     B, H, N, D, qs = CONFIGS[args.config]
     s = D ** -0.5
