@@ -36,7 +36,7 @@ from __future__ import annotations
 import numpy as np
 
 __all__ = ["path_scores", "path_fwd", "path_fwd_blockwise", "path_bwd_blockwise", "path_fwd_bwd_torch",
-           "make_path_inputs"]
+           "make_path_inputs", "path_attention_fwd"]
 
 
 def make_path_inputs(seed: int, B: int, T: int, H: int, K: int, HQ: int | None = None, with_q: bool = False):
@@ -85,6 +85,33 @@ def path_scores(q, k, w, beta):
                 X[:r] -= beta[b, r, h] * np.outer(X[:r] @ wr, wr)
                 A[b, hq, r, :r] = X[:r] @ q[b, r, hq]
     return A
+
+
+def path_attention_fwd(k, v, w, beta, q=None, scale=None):
+    """PaTH softmax attention forward (parallel_path_fwd.py:13-124 with the diagonal
+    blocks of intra_chunk_preprocess_fwd.py:13-121):
+        O_r = sum_{c <= r} softmax_c(s A_rc) v_c,  A_rc = q_r^T (H_r ... H_{c+1}) k_c
+    (A_rr = q_r . k_r).  Returns (o [B,T,HQ,V], lse [B,T,HQ]) with lse the
+    log2-sum-exp of s A log2(e) over the row, as the reference stores L_new."""
+    q = k if q is None else q
+    B, T, HQ, K = q.shape
+    _, H, G = _heads(q, k)
+    s = K ** -0.5 if scale is None else scale
+    A = path_scores(q, k, w, beta)
+    o = np.zeros((B, T, HQ, v.shape[-1]))
+    lse = np.zeros((B, T, HQ))
+    for b in range(B):
+        for hq in range(HQ):
+            h = hq // G
+            Ab = A[b, hq].copy()
+            Ab[np.arange(T), np.arange(T)] = np.einsum("td,td->t", q[b, :, hq], k[b, :, h])
+            z = np.where(np.tril(np.ones((T, T), dtype=bool)), s * Ab * np.log2(np.e), -np.inf)
+            m = z.max(axis=1, keepdims=True)
+            p = np.exp2(z - m)
+            l = p.sum(axis=1, keepdims=True)
+            o[b, :, hq] = (p / l) @ v[b, :, h]
+            lse[b, :, hq] = (np.log2(l) + m)[:, 0]
+    return o, lse
 
 
 def _unit_lower_solve(L, R):

@@ -32,8 +32,9 @@ def load_golden(name: str) -> dict:
 
 
 ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                    if not os.path.basename(p).startswith(("blockwise", "path_")))
+                    if not os.path.basename(p).startswith(("blockwise", "path")))
 PATH_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "path_*.npz")))
+PATH_ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "pathattn_*.npz")))
 
 
 def load_path_golden(name: str) -> dict:

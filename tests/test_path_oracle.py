@@ -9,9 +9,9 @@ ragged sequence lengths and grouped query heads."""
 import numpy as np
 import pytest
 
-from conftest import PATH_CASES, load_path_golden
-from oracle.path_oracle import (make_path_inputs, path_bwd_blockwise, path_fwd, path_fwd_blockwise,
-                                path_fwd_bwd_torch)
+from conftest import PATH_ATTN_CASES, PATH_CASES, load_path_golden
+from oracle.path_oracle import (make_path_inputs, path_attention_fwd, path_bwd_blockwise, path_fwd,
+                                path_fwd_blockwise, path_fwd_bwd_torch)
 
 GRADS = ("dq", "dk", "dv", "dw", "dbeta")
 
@@ -86,3 +86,13 @@ def test_reference_precision_model_is_close_to_float64():
     o2, _ = path_fwd(d2["k"], d2["v"], d2["w"], d2["beta"], q=d2["q"])
     om2 = reference_bf16_forward(d2["k"], d2["v"], d2["w"], d2["beta"], q=d2["q"])
     assert np.abs(om2 - o2).max() < 3e-2
+
+
+@pytest.mark.parametrize("name", PATH_ATTN_CASES)
+def test_path_attention_oracle_matches_reference_fixture(name):
+    """PaTH softmax attention (intra_chunk_preprocess_fwd + parallel_path_fwd of the
+    reference, float32 in the Triton interpreter) against the dense float64 oracle."""
+    d = load_path_golden(name)
+    o, lse = path_attention_fwd(d["k"], d["v"], d["w"], d["beta"], q=d["q"])
+    assert _rel(o, d["o"]) < 1e-6
+    assert np.max(np.abs(lse - d["lse"])) < 1e-4
