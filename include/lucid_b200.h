@@ -203,6 +203,27 @@ int lucid_path_bwd(int B, int T, int H, int HQ, int D, float scale,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * PaTH softmax attention forward:
+ *   o_r = sum_{c <= r} softmax_c(scale * A_rc) v_c,  A_rc = q_r^T (H_r ... H_{c+1}) k_c,
+ *   lse_r = log2 sum_c exp2(scale * log2(e) * A_rc)   (log2 domain, as the reference's L).
+ * Replaces the composition intra_chunk_preprocess_fwd_fn (intra_chunk_preprocess_fwd.py:124-168,
+ * diagonal blocks) + parallel_path_fwd_fn (parallel_path_fwd.py:127-170, off-diagonal blocks
+ * with online softmax), with the UT transform of parallel.py:40-51.  The reference has no
+ * backward for this op.  Layout as lucid_path_fwd; lse is [B, T, HQ] fp32 with element
+ * strides (sb, st, sh).
+ */
+size_t lucid_path_attn_fwd_workspace_bytes(int B, int T, int H, int HQ, int D);
+int lucid_path_attn_fwd(int B, int T, int H, int HQ, int D, float scale,
+                        const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                        const void* k, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                        const void* v, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                        const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
+                        const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
+                        void* o, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                        float* lse, int64_t l_sb, int64_t l_st, int64_t l_sh,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Kernel timing hook (benchmarks).  While enabled for one kernel family,
  * every launch of that family's main kernel is bracketed by a pair of CUDA
  * events recorded on the launch stream; lucid_profile_read waits for the
@@ -223,6 +244,7 @@ int lucid_path_bwd(int B, int T, int H, int HQ, int D, float scale,
 #define LUCID_KERNEL_PATH_SOLVE_T 11  /* LUCID-Path transposed solve dV = (I + L)^-T dO */
 #define LUCID_KERNEL_PATH_ROW 12      /* LUCID-Path backward row pass (dA, dQ~ chain) */
 #define LUCID_KERNEL_PATH_COL 13      /* LUCID-Path backward column pass (dK_new, dW, dW2) */
+#define LUCID_KERNEL_PATH_ATTN 14     /* PaTH softmax attention forward */
 int lucid_profile_enable(int kernel);
 int lucid_profile_read(float* total_ms, int* launches);
 

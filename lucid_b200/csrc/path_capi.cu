@@ -24,6 +24,8 @@ cudaError_t launch_path_solve(bool transposed, const CUtensorMap& tmL, const CUt
 cudaError_t launch_path_row(const CUtensorMap& tmDV, const CUtensorMap& tmO, const CUtensorMap& tmKn,
                             const CUtensorMap& tmW, const CUtensorMap& tmW2, const CUtensorMap& tmDs,
                             const PathRowArgs& a, cudaStream_t st);
+cudaError_t launch_path_attn(const CUtensorMap& tmKn, const CUtensorMap& tmW, const CUtensorMap& tmW2,
+                             const CUtensorMap& tmV, const PathAttnArgs& a, cudaStream_t st);
 cudaError_t launch_path_col(const CUtensorMap& tmDA, const CUtensorMap& tmQs, const CUtensorMap& tmDs,
                             const CUtensorMap& tmW, const CUtensorMap& tmW2, const PathColArgs& a, cudaStream_t st);
 }  // namespace lb
@@ -123,6 +125,25 @@ struct BwdLayout {
   }
 };
 
+// PaTH attention forward: the per-block prep of the solve plus the raw diagonal scores.
+struct AttnLayout {
+  size_t status, Tm, WbK, TB, Kn, W2, QW, Qn, Ad, M, total;
+  explicit AttnLayout(const Dims& d) {
+    Carver c;
+    status = c.take(256);
+    Tm = c.take(d.blocks_k() * 4);
+    WbK = c.take(d.blocks_k() * 2);
+    TB = c.take(d.blocks_k() * 2);
+    Kn = c.take(d.blocks_k() * 2);
+    W2 = c.take(d.blocks_k() * 2);
+    QW = c.take(d.blocks_q() * 2);
+    Qn = c.take(d.blocks_q() * 4);
+    Ad = c.take(d.blocks_q() * 4);
+    M = c.take(d.blocks_k() * 4);
+    total = c.off;
+  }
+};
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool st8(int64_t a, int64_t b, int64_t c) { return (a % 8 == 0) && (b % 8 == 0) && (c % 8 == 0); }
 
@@ -185,6 +206,15 @@ bool tm_user(CUtensorMap* m, const void* p, int B, int T, int heads, int64_t sb,
   return make_tmap_bf16(m, p, 128, T, heads, B, st, sh, sb);
 }
 
+struct PrepIn {
+  const void *q, *k, *w, *beta;
+  int64_t q_sb, q_st, q_sh, k_sb, k_st, k_sh, w_sb, w_st, w_sh, be_sb, be_st, be_sh;
+  int beta_fp32;
+};
+struct PrepOut {
+  void *M, *Tm, *WbK, *TB, *Kn, *W2, *QW, *Qn;
+};
+
 struct Launcher {
   cudaStream_t st;
   int* status;
@@ -208,6 +238,85 @@ struct Launcher {
     err = launch_path_triinv(a, st);
   }
 };
+
+// UT transform, W2, K_new, QW, Q_new of every 128-row block (triangular_solve_fwd.py:118-148).
+void launch_prep_fwd(Launcher& Lc, const Dims& d, const PrepIn& in, const PrepOut& out) {
+  const int H = d.H, HQ = d.HQ, G = d.G, T = d.T;
+  const long long Np = d.Np;
+  const PMat Wk = ubuf(in.w, in.w_sb, in.w_st, in.w_sh, T, 1), Wq = ubuf(in.w, in.w_sb, in.w_st, in.w_sh, T, G);
+  const PMat Kk = ubuf(in.k, in.k_sb, in.k_st, in.k_sh, T, 1);
+  const PMat Qq = ubuf(in.q, in.q_sb, in.q_st, in.q_sh, T, 1);
+  const PVec bet = uvec(in.beta, in.beta_fp32, in.be_sb, in.be_st, in.be_sh, T, 1);
+  const PMat Mk = ibuf(out.M, true, H, Np, 1);
+  const PMat Tk = ibuf(out.Tm, true, H, Np, 1);
+  const PMat WbKk = ibuf(out.WbK, false, H, Np, 1);
+  const PMat TBk = ibuf(out.TB, false, H, Np, 1);
+  const PMat W2k = ibuf(out.W2, false, H, Np, 1), W2q = ibuf(out.W2, false, H, Np, G);
+  const PMat QWq = ibuf(out.QW, false, HQ, Np, 1);
+  {  // M = stril(diag(beta) W W^T)
+    BGemmArgs a;
+    a.A[0] = opnd(Wk);
+    a.B[0] = opnd(Wk, 1);
+    a.orsc = bet;
+    a.out_mask = kMaskStril;
+    a.O = Mk;
+    Lc.gemm(a, H);
+  }
+  {  // T = (I + M)^-1
+    TriInvArgs a;
+    a.M = Mk;
+    a.Z = Tk;
+    Lc.inv(a, H);
+  }
+  {  // W2 = T diag(beta) W
+    BGemmArgs a;
+    a.A[0] = opnd(Tk);
+    a.B[0] = opnd_rs(Wk, 0, bet);
+    a.O = W2k;
+    Lc.gemm(a, H);
+  }
+  {  // WbK = stril(diag(beta) W K^T)
+    BGemmArgs a;
+    a.A[0] = opnd_rs(Wk, 0, bet);
+    a.B[0] = opnd(Kk, 1);
+    a.out_mask = kMaskStril;
+    a.O = WbKk;
+    Lc.gemm(a, H);
+  }
+  {  // TB = T WbK
+    BGemmArgs a;
+    a.A[0] = opnd(Tk);
+    a.B[0] = opnd(WbKk);
+    a.O = TBk;
+    Lc.gemm(a, H);
+  }
+  {  // K_new = K - TB^T W
+    BGemmArgs a;
+    a.A[0] = opnd(TBk, 1, -1.f);
+    a.B[0] = opnd(Wk);
+    a.nc = 1;
+    a.C[0] = Kk;
+    a.O = ibuf(out.Kn, false, H, Np, 1);
+    Lc.gemm(a, H);
+  }
+  {  // QW = tril(Q W^T)
+    BGemmArgs a;
+    a.A[0] = opnd(Qq);
+    a.B[0] = opnd(Wq, 1);
+    a.out_mask = kMaskTril;
+    a.O = QWq;
+    Lc.gemm(a, HQ);
+  }
+  {  // Q_new = Q - QW W2
+    BGemmArgs a;
+    a.A[0] = opnd(QWq, 0, -1.f);
+    a.B[0] = opnd(W2q);
+    a.nc = 1;
+    a.C[0] = Qq;
+    a.O = ibuf(out.Qn, true, HQ, Np, 1);
+    Lc.gemm(a, HQ);
+  }
+}
 
 bool path_shape_ok(int B, int T, int H, int HQ, int D) {
   return B >= 0 && T >= 0 && H >= 0 && HQ >= 0 && D == kHeadDim && (H == 0 ? HQ == 0 : HQ % H == 0) &&
@@ -269,83 +378,16 @@ int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
 
   if (cudaMemsetAsync(ws, 0, lay.Tm, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
 
-  const PMat Wk = ubuf(w, w_sb, w_st, w_sh, T, 1), Wq = ubuf(w, w_sb, w_st, w_sh, T, G);
-  const PMat Kk = ubuf(k, k_sb, k_st, k_sh, T, 1), Kq = ubuf(k, k_sb, k_st, k_sh, T, G);
+  const PMat Kq = ubuf(k, k_sb, k_st, k_sh, T, G);
   const PMat Qq = ubuf(q, q_sb, q_st, q_sh, T, 1);
-  const PVec bet = uvec(beta, beta_fp32, be_sb, be_st, be_sh, T, 1);
-  const PMat Mk = ibuf(P(lay.M), true, H, Np, 1), Mq = ibuf(P(lay.M), true, HQ, Np, 1);
-  const PMat Tk = ibuf(P(lay.Tm), true, H, Np, 1);
-  const PMat WbKk = ibuf(P(lay.WbK), false, H, Np, 1);
-  const PMat TBk = ibuf(P(lay.TB), false, H, Np, 1), TBq = ibuf(P(lay.TB), false, H, Np, G);
-  const PMat Knk = ibuf(P(lay.Kn), false, H, Np, 1);
-  const PMat W2k = ibuf(P(lay.W2), false, H, Np, 1), W2q = ibuf(P(lay.W2), false, H, Np, G);
+  const PMat Mq = ibuf(P(lay.M), true, HQ, Np, 1);
+  const PMat TBq = ibuf(P(lay.TB), false, H, Np, G);
   const PMat QWq = ibuf(P(lay.QW), false, HQ, Np, 1);
-  const PMat Qnq = ibuf(P(lay.Qn), true, HQ, Np, 1);
 
   Launcher Lc{st, status, B, d.NB};
-  {  // M = stril(diag(beta) W W^T)
-    BGemmArgs a;
-    a.A[0] = opnd(Wk);
-    a.B[0] = opnd(Wk, 1);
-    a.orsc = bet;
-    a.out_mask = kMaskStril;
-    a.O = Mk;
-    Lc.gemm(a, H);
-  }
-  {  // T = (I + M)^-1
-    TriInvArgs a;
-    a.M = Mk;
-    a.Z = Tk;
-    Lc.inv(a, H);
-  }
-  {  // W2 = T diag(beta) W
-    BGemmArgs a;
-    a.A[0] = opnd(Tk);
-    a.B[0] = opnd_rs(Wk, 0, bet);
-    a.O = W2k;
-    Lc.gemm(a, H);
-  }
-  {  // WbK = stril(diag(beta) W K^T)
-    BGemmArgs a;
-    a.A[0] = opnd_rs(Wk, 0, bet);
-    a.B[0] = opnd(Kk, 1);
-    a.out_mask = kMaskStril;
-    a.O = WbKk;
-    Lc.gemm(a, H);
-  }
-  {  // TB = T WbK
-    BGemmArgs a;
-    a.A[0] = opnd(Tk);
-    a.B[0] = opnd(WbKk);
-    a.O = TBk;
-    Lc.gemm(a, H);
-  }
-  {  // K_new = K - TB^T W
-    BGemmArgs a;
-    a.A[0] = opnd(TBk, 1, -1.f);
-    a.B[0] = opnd(Wk);
-    a.nc = 1;
-    a.C[0] = Kk;
-    a.O = Knk;
-    Lc.gemm(a, H);
-  }
-  {  // QW = tril(Q W^T)
-    BGemmArgs a;
-    a.A[0] = opnd(Qq);
-    a.B[0] = opnd(Wq, 1);
-    a.out_mask = kMaskTril;
-    a.O = QWq;
-    Lc.gemm(a, HQ);
-  }
-  {  // Q_new = Q - QW W2
-    BGemmArgs a;
-    a.A[0] = opnd(QWq, 0, -1.f);
-    a.B[0] = opnd(W2q);
-    a.nc = 1;
-    a.C[0] = Qq;
-    a.O = Qnq;
-    Lc.gemm(a, HQ);
-  }
+  launch_prep_fwd(Lc, d, PrepIn{q, k, w, beta, q_sb, q_st, q_sh, k_sb, k_st, k_sh, w_sb, w_st, w_sh, be_sb, be_st,
+                                be_sh, beta_fp32},
+                  PrepOut{P(lay.M), P(lay.Tm), P(lay.WbK), P(lay.TB), P(lay.Kn), P(lay.W2), P(lay.QW), P(lay.Qn)});
   {  // L_ii = stril(exp(s (Q K^T - QW TB) - 1/s))   (fp32 into M)
     BGemmArgs a;
     a.nprod = 2;
@@ -655,6 +697,66 @@ int lucid_path_bwd(int B, int T, int H, int HQ, int D, float scale,
       e = launch_path_pack((bf16*)dw, dw_sb, dw_st, dw_sh, P(bl.dWfin), 1, 1, nullptr, 1, 1, B, H, T, (int)Np, st);
     if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
+  return LUCID_OK;
+}
+
+size_t lucid_path_attn_fwd_workspace_bytes(int B, int T, int H, int HQ, int D) {
+  (void)D;
+  return AttnLayout(Dims(B, T, H, HQ)).total;
+}
+
+int lucid_path_attn_fwd(int B, int T, int H, int HQ, int D, float scale,
+                        const void* q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                        const void* k, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                        const void* v, int64_t v_sb, int64_t v_st, int64_t v_sh,
+                        const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
+                        const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
+                        void* o, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                        float* lse, int64_t l_sb, int64_t l_st, int64_t l_sh,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!path_shape_ok(B, T, H, HQ, D)) return LUCID_ERR_SHAPE;
+  if (q == nullptr) {
+    if (HQ != H) return LUCID_ERR_SHAPE;
+    q = k; q_sb = k_sb; q_st = k_st; q_sh = k_sh;
+  }
+  if (B == 0 || T == 0 || H == 0) return LUCID_OK;
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(w) || !al16(o) || lse == nullptr || !st8(q_sb, q_st, q_sh) ||
+      !st8(k_sb, k_st, k_sh) || !st8(v_sb, v_st, v_sh) || !st8(w_sb, w_st, w_sh) || !st8(o_sb, o_st, o_sh))
+    return LUCID_ERR_ALIGN;
+  const Dims d(B, T, H, HQ);
+  const AttnLayout lay(d);
+  if (workspace == nullptr || workspace_bytes < lay.total || !al16(workspace)) return LUCID_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(ws + lay.status);
+  auto P = [&](size_t off) { return static_cast<void*>(ws + off); };
+  const long long Np = d.Np;
+  CUtensorMap tmKn, tmW, tmW2, tmV;
+  if (!(tm_int(&tmKn, P(lay.Kn), d.BHK, Np) && tm_user(&tmW, w, B, T, H, w_sb, w_st, w_sh) &&
+        tm_int(&tmW2, P(lay.W2), d.BHK, Np) && tm_user(&tmV, v, B, T, H, v_sb, v_st, v_sh)))
+    return LUCID_ERR_TENSORMAP;
+  if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  Launcher Lc{st, status, B, d.NB};
+  launch_prep_fwd(Lc, d, PrepIn{q, k, w, beta, q_sb, q_st, q_sh, k_sb, k_st, k_sh, w_sb, w_st, w_sh, be_sb, be_st,
+                                be_sh, beta_fp32},
+                  PrepOut{P(lay.M), P(lay.Tm), P(lay.WbK), P(lay.TB), P(lay.Kn), P(lay.W2), P(lay.QW), P(lay.Qn)});
+  {  // raw diagonal-block scores A_ii = tril(Q K^T - QW TB)
+    BGemmArgs a;
+    a.nprod = 2;
+    a.A[0] = opnd(ubuf(q, q_sb, q_st, q_sh, T, 1));
+    a.B[0] = opnd(ubuf(k, k_sb, k_st, k_sh, T, d.G), 1);
+    a.A[1] = opnd(ibuf(P(lay.QW), false, HQ, Np, 1), 0, -1.f);
+    a.B[1] = opnd(ibuf(P(lay.TB), false, H, Np, d.G));
+    a.out_mask = kMaskTril;
+    a.O = ibuf(P(lay.Ad), true, HQ, Np, 1);
+    Lc.gemm(a, HQ);
+  }
+  if (Lc.err != cudaSuccess) return LUCID_ERR_LAUNCH;
+  PathAttnArgs a{B, HQ, H, d.G, T, d.NB, scale, reinterpret_cast<const float*>(P(lay.Qn)),
+                 reinterpret_cast<const float*>(P(lay.Ad)), reinterpret_cast<bf16*>(o), o_sb, o_st, o_sh, lse,
+                 l_sb, l_st, l_sh, status};
+  ProfileScope ps(LUCID_KERNEL_PATH_ATTN, st);
+  if (launch_path_attn(tmKn, tmW, tmW2, tmV, a, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   return LUCID_OK;
 }
 

@@ -122,6 +122,19 @@ struct PathColArgs {
   int* status;
 };
 
+struct PathAttnArgs {
+  int B, HQ, H, G, T, NB;
+  float s;
+  const float* qn;      // [B*HQ][Npad][128] fp32 Q_new
+  const float* ad;      // [B*HQ][NB][128][128] fp32 diagonal-block scores (tril, raw)
+  bf16* o;              // caller's [B, T, HQ, V]
+  long long o_sb, o_st, o_sh;
+  float* lse;           // caller's [B, T, HQ] (log2 domain)
+  long long l_sb, l_st, l_sh;
+  int* status;
+};
+
+enum : int { kTagPathAttn = 14 };
 enum : int { kTagPathGemm = 8, kTagPathScores = 9, kTagPathSolve = 10, kTagPathSolveT = 11,
              kTagPathRow = 12, kTagPathCol = 13 };
 

@@ -986,4 +986,353 @@ cudaError_t launch_path_col(const CUtensorMap& tmDA, const CUtensorMap& tmQs, co
   return launch_persistent(path_col_kernel, pcl::kSmem, a.NB * a.B * a.HQ, st, tmDA, tmQs, tmDs, tmW, tmW2, a);
 }
 
+// ===========================================================================
+// path_attn_kernel: PaTH softmax attention forward
+// (parallel_path_fwd.py:13-124 + the diagonal blocks of intra_chunk_preprocess_fwd.py)
+//   O_r = sum_{c<=r} softmax_c(s A_rc) v_c, lse_r = log2 sum_c exp2(s A_rc log2 e)
+// Row block i: the diagonal block's scores come from the prep (raw A_ii, fp32);
+// then j = i-1 .. 0 along the query chain:
+//   S = Q~ K_new_j^T (Q~ as bf16 hi + lo), online softmax, O += P V_j,
+//   Q~ += (-(Q~ W_j^T)) W2_j accumulated by the tensor core in TMEM.
+// Warps 0-3 run the softmax (one row per thread), warps 4-7 the query chain.
+// ===========================================================================
+namespace pat {
+constexpr int kRing = 4;
+constexpr uint32_t kOffQ = 0, kOffQlo = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
+enum { RF0 = 0, RE0 = RF0 + kRing, QOP_FULL = RE0 + kRing, QOP_FREE, S_FULL, S2_FULL, NS2_FULL, QD_FULL, P_FULL,
+       O_DONE, O_FREE, DRAIN, NBAR };
+constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
+constexpr uint32_t kTmS = 0, kTmS2 = 128, kTmQ = 256, kTmO = 384;
+constexpr int kHalf = 128;  // threads per warpgroup
+}  // namespace pat
+
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    path_attn_kernel(const __grid_constant__ CUtensorMap tmKn, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ CUtensorMap tmV,
+                     PathAttnArgs p) {
+  using namespace pat;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagPathAttn};
+  const uint32_t sQ = sbase + kOffQ, sQlo = sbase + kOffQlo;
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagPathAttn << 20));
+    return;
+  }
+  if (threadIdx.x == pk::kWarpTma * 32) {
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(RF0 + s), 1);
+      mbar_init(bar(RE0 + s), 1);
+    }
+    mbar_init(bar(QOP_FULL), kHalf);
+    mbar_init(bar(QOP_FREE), 1);
+    mbar_init(bar(S_FULL), 1);
+    mbar_init(bar(S2_FULL), 1);
+    mbar_init(bar(NS2_FULL), kHalf);
+    mbar_init(bar(QD_FULL), 1);
+    mbar_init(bar(P_FULL), kHalf);
+    mbar_init(bar(O_DONE), 1);
+    mbar_init(bar(O_FREE), kHalf);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmKn);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmW2);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == pk::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BHQ = p.B * p.HQ;
+  const int total = p.NB * BHQ;
+  const long long Npad = (long long)p.NB * 128;
+  auto decode = [&](int idx, int& i, int& bhq, int& b, int& hq, int& h, int& bhk) {
+    i = p.NB - 1 - idx / BHQ;
+    bhq = idx % BHQ;
+    b = bhq / p.HQ;
+    hq = bhq % p.HQ;
+    h = hq / p.G;
+    bhk = b * p.H + h;
+  };
+
+  if (warp == pk::kWarpTma) {
+    if (lane == 0) {
+      TileRing<kRing> ring;
+      ring.init(sbase + kOffRing, bar(RF0), bar(RE0));
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int i, bhq, b, hq, h, bhk;
+        decode(idx, i, bhq, b, hq, h, bhk);
+        ok = ring.load(&tmV, i * 128, h, b, ab);
+        for (int j = i - 1; j >= 0 && ok; --j) {
+          ok = ring.load(&tmKn, j * 128, bhk, 0, ab);
+          if (ok && j > 0) ok = ring.load(&tmW, j * 128, h, b, ab);
+          if (ok) ok = ring.load(&tmV, j * 128, h, b, ab);
+          if (ok && j > 0) ok = ring.load(&tmW2, j * 128, bhk, 0, ab);
+        }
+      }
+      ring.drain();
+    }
+  } else if (warp == pk::kWarpMma) {
+    if (lane == 0) {
+      uint32_t rc = 0, n_q = 0, n_ns2 = 0, n_p = 0, n_item = 0;
+      auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
+      auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
+      auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      const uint32_t tS = tmem + kTmS, tS2 = tmem + kTmS2;
+      auto pv = [&](uint32_t sv, uint32_t acc) -> bool {
+        if (!mbar_wait(bar(P_FULL), (n_p++) & 1, ab) || !ring_wait(sv)) return false;
+        tc_fence_after();
+        umma_tile_ts(tmem + kTmO, [&](int kk) { return tS + 8u * (uint32_t)kk; }, ring_slot(sv), true, acc);
+        umma_commit(bar(O_DONE));
+        ring_free(sv);
+        return true;
+      };
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++n_item) {
+        int i, bhq, b, hq, h, bhk;
+        decode(idx, i, bhq, b, hq, h, bhk);
+        if (!mbar_wait(bar(O_FREE), (n_item & 1) ^ 1, ab)) break;
+        if (!pv(rc++, 0u)) break;                        // diagonal block
+        for (int j = i - 1; j >= 0; --j) {
+          if (!mbar_wait(bar(QOP_FULL), (n_q++) & 1, ab)) { ok = false; break; }
+          const uint32_t sK = rc++;
+          if (!ring_wait(sK)) { ok = false; break; }
+          uint32_t sW = 0;
+          if (j > 0) {
+            sW = rc++;
+            if (!ring_wait(sW)) { ok = false; break; }
+          }
+          tc_fence_after();
+          if (j > 0) {
+            umma_tile(tS2, sQ, false, ring_slot(sW), false, 0u);
+            umma_commit(bar(S2_FULL));
+          }
+          umma_tile(tS, sQ, false, ring_slot(sK), false, 0u);
+          umma_tile(tS, sQlo, false, ring_slot(sK), false, 1u);
+          umma_commit(bar(S_FULL));
+          if (j == 0) umma_commit(bar(QOP_FREE));
+          ring_free(sK);
+          if (j > 0) ring_free(sW);
+          const uint32_t sV = rc++;
+          if (j > 0) {
+            if (!mbar_wait(bar(NS2_FULL), (n_ns2++) & 1, ab)) { ok = false; break; }
+            const uint32_t sW2 = rc++;
+            if (!ring_wait(sW2)) { ok = false; break; }
+            tc_fence_after();
+            // -S2 was packed by full rows: K-slice kk at column 8 kk
+            umma_tile_ts(tmem + kTmQ, [&](int kk) { return tS2 + 8u * (uint32_t)kk; }, ring_slot(sW2), true, 1u);
+            umma_commit(bar(QD_FULL));
+            ring_free(sW2);
+          }
+          if (!pv(sV, 1u)) { ok = false; break; }
+        }
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else if (warp < 4) {
+    // ---------------- softmax warpgroup ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_base + kTmS, tO = tmem + lane_base + kTmO;
+    const float sm = p.s * 1.4426950408889634f;
+    uint32_t n_s = 0, n_pv = 0;
+    auto store_p = [&](float (&v)[32], int c) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
+      tmem_st16(tS + 16u * (uint32_t)c, pk);
+    };
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      int i, bhq, b, hq, h, bhk;
+      decode(idx, i, bhq, b, hq, h, bhk);
+      float m_run, l_run = 0.f;
+      bool ok = true;
+      {  // diagonal block from the prep's raw scores (causal within the block)
+        const float* arow = p.ad + (((long long)bhq * p.NB + i) * 128 + r) * 128;
+        float mx = -INFINITY;
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e <= r) mx = fmaxf(mx, arow[c * 32 + e] * sm);
+        }
+        m_run = mx;
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            v[e] = (c * 32 + e <= r) ? fast_exp2(arow[c * 32 + e] * sm - m_run) : 0.f;
+            l_run += v[e];
+          }
+          store_p(v, c);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(P_FULL));
+        ++n_pv;
+      }
+      for (int j = i - 1; j >= 0; --j) {
+        if (!pwarp_wait(bar(S_FULL), (n_s++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        float mx = -INFINITY;
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS + 32u * c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e] * sm);
+        }
+        // lazy rescale: every P V issued so far has completed (S of this step was
+        // issued after the last one), so O can be rescaled in place
+        if (__any_sync(0xffffffffu, mx > m_run + 8.f)) {
+          const float mn = fmaxf(m_run, mx);
+          const float alpha = fast_exp2(m_run - mn);
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(tO + 32u * c, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+            tmem_st32(tO + 32u * c, ov);
+          }
+          tmem_st_wait();
+          l_run *= alpha;
+          m_run = mn;
+        }
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS + 32u * c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            v[e] = fast_exp2(fmaf(v[e], sm, -m_run));
+            l_run += v[e];
+          }
+          store_p(v, c);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(P_FULL));
+        ++n_pv;
+      }
+      if (!ok) break;
+      if (!pwarp_wait(bar(O_DONE), (n_pv - 1) & 1, ab)) break;
+      tc_fence_after();
+      const long long t = (long long)i * 128 + r;
+      const float inv_l = 1.f / l_run;
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tO + 32u * c, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] *= inv_l;
+        if (t < p.T) {
+          bf16* dst = p.o + (long long)b * p.o_sb + t * p.o_st + (long long)hq * p.o_sh + c * 32;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) st_bf16x8(dst + 8 * e, ov + 8 * e);
+        }
+      }
+      if (t < p.T) p.lse[(long long)b * p.l_sb + t * p.l_st + (long long)hq * p.l_sh] = m_run + __log2f(l_run);
+      tc_fence_before();
+      mbar_arrive(bar(O_FREE));
+    }
+  } else {
+    // ---------------- query-chain warpgroup ----------------
+    const int wq = warp - 4;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS2 = tmem + lane_base + kTmS2, tQ = tmem + lane_base + kTmQ;
+    uint32_t n_s2 = 0, n_qd = 0, n_free = 0;
+    bool first = true;
+    // bf16 hi / lo operand copies of Q~ (read from registers or TMEM in 32-column chunks)
+    auto write_op = [&](int c, const float (&v)[32]) {
+      float hi[32], lo[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        hi[e] = __bfloat162float(__float2bfloat16(v[e]));
+        lo[e] = v[e] - hi[e];
+      }
+      tile_store_row32(sQ, r, c, hi);
+      tile_store_row32(sQlo, r, c, lo);
+    };
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      int i, bhq, b, hq, h, bhk;
+      decode(idx, i, bhq, b, hq, h, bhk);
+      if (i == 0) continue;
+      bool ok = true;
+      // the previous item's last score GEMM has finished reading the operand tiles
+      if (!first && !pwarp_wait(bar(QOP_FREE), (n_free++) & 1, ab)) break;
+      first = false;
+      {
+        const float* src = p.qn + (((long long)bhq * Npad) + i * 128 + r) * 128;
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = src[c * 32 + e];
+          tmem_st32(tQ + 32u * c, v);
+          write_op(c, v);
+        }
+        tmem_st_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(QOP_FULL));
+      }
+      for (int j = i - 1; j >= 1; --j) {
+        if (!pwarp_wait(bar(S2_FULL), (n_s2++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS2 + 32u * c, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(-v[2 * e], -v[2 * e + 1]);
+          // packed columns of chunk c go to [16c, 16c+16): inside chunks already read
+          tmem_st16(tS2 + 16u * (uint32_t)c, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(NS2_FULL));
+        if (!pwarp_wait(bar(QD_FULL), (n_qd++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tQ + 32u * c, v);
+          tmem_ld_wait();
+          write_op(c, v);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(QOP_FULL));
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == pk::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+cudaError_t launch_path_attn(const CUtensorMap& tmKn, const CUtensorMap& tmW, const CUtensorMap& tmW2,
+                             const CUtensorMap& tmV, const PathAttnArgs& a, cudaStream_t st) {
+  return launch_persistent(path_attn_kernel, pat::kSmem, a.NB * a.B * a.HQ, st, tmKn, tmW, tmW2, tmV, a);
+}
+
 }  // namespace lb

@@ -27,7 +27,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["parallel_lucid_path_attention", "ParallelLUCIDPathAttentionFunction", "path_fwd", "path_bwd"]
+__all__ = ["parallel_lucid_path_attention", "ParallelLUCIDPathAttentionFunction", "path_fwd", "path_bwd",
+           "parallel_path_attention_fwd"]
 
 
 def _stream() -> int:
@@ -173,3 +174,37 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
                                                         beta[:, a:b], None, float(scale), None, False)
         outs.append(o)
     return torch.cat(outs, dim=1), None
+
+
+def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):
+    """PaTH softmax attention forward: o [B,T,HQ,V] and the log2-sum-exp lse
+    [B,T,HQ] (float32), the outputs of the reference's
+    intra_chunk_preprocess_fwd_fn + parallel_path_fwd_fn
+    (intra_chunk_preprocess_fwd.py:124-168, parallel_path_fwd.py:127-170).
+    ``q`` may be None (q = k).  Forward only: the reference has no backward
+    kernels for this op."""
+    lib = _lib.load()
+    k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
+    beta = _prep(beta, "beta", 3)
+    B, T, H, K = k.shape
+    if K != 128 or v.shape[-1] != 128:
+        raise NotImplementedError("PaTH attention B200 kernels support head_dim 128 only")
+    if w.shape != k.shape or v.shape[:3] != k.shape[:3] or tuple(beta.shape) != (B, T, H):
+        raise ValueError("k, v, w must be [B, T, H, 128] and beta [B, T, H]")
+    if q is not None:
+        q = _prep(q, "q")
+        if q.shape[0] != B or q.shape[1] != T or q.shape[3] != K or q.shape[2] % H != 0:
+            raise ValueError("q must be [B, T, HQ, 128] with HQ a multiple of H")
+    HQ = q.shape[2] if q is not None else H
+    s = float(K ** -0.5 if scale is None else scale)
+    dev = k.device
+    o = torch.empty(B, T, HQ, v.shape[-1], dtype=v.dtype, device=dev)
+    lse = torch.empty(B, T, HQ, dtype=torch.float32, device=dev)
+    ws = _ws(lib.lucid_path_attn_fwd_workspace_bytes(B, T, H, HQ, K), dev)
+    qp, qs = (q.data_ptr(), _s3(q)) if q is not None else (None, (0, 0, 0))
+    rc = lib.lucid_path_attn_fwd(B, T, H, HQ, K, s, qp, *qs, k.data_ptr(), *_s3(k), v.data_ptr(), *_s3(v),
+                                 w.data_ptr(), *_s3(w), beta.data_ptr(), int(beta.dtype == torch.float32),
+                                 *beta.stride(), o.data_ptr(), *_s3(o), lse.data_ptr(), *lse.stride(),
+                                 ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_path_attn_fwd")
+    return o, lse

@@ -1,4 +1,5 @@
-"""Precision model of the reference LUCID-Path forward — TEST INFRASTRUCTURE ONLY.
+"""Precision models of the reference LUCID-Path forward and PaTH attention
+forward — TEST INFRASTRUCTURE ONLY.
 
 The reference's own bf16 deviation cannot be measured by running it here
 (its Triton kernels return NaN in bf16 under the CPU interpreter, and the
@@ -22,7 +23,7 @@ from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["reference_bf16_forward"]
+__all__ = ["reference_bf16_forward", "reference_bf16_attention"]
 
 
 def _bf16(x):
@@ -93,4 +94,66 @@ def reference_bf16_forward(k, v, w, beta, q=None, scale=None, bt=64):
                     X[r] = X[r] - (Ld[r, :r].astype(np.float64) @ X[:r].astype(np.float64)).astype(np.float32)
                 O.append(_bf16(X))
                 o[b, i * bt:i * bt + X.shape[0], hq] = O[-1]
+    return o
+
+
+def reference_bf16_attention(k, v, w, beta, q=None, scale=None, bt=64):
+    """o [B, T, HQ, V] of the reference's PaTH softmax attention forward from bf16
+    inputs: intra_chunk_preprocess_fwd.py:71-121 (diagonal blocks: A from bf16
+    dots, q_new / k_new / w2 stored bf16) then parallel_path_fwd.py:87-124
+    (off-diagonal blocks: tl.dot(q.to(bf16), k) :91, p.to(bf16) @ v :104,
+    tl.dot(q.to(bf16), w1) and s2.to(bf16) @ w2 for the query chain :105-106,
+    with the query itself kept in fp32 :37-38)."""
+    q = k if q is None else q
+    B, T, HQ, K = q.shape
+    H = k.shape[2]
+    G = HQ // H
+    s = np.float32(K ** -0.5 if scale is None else scale)
+    sm = np.float32(s * 1.44269504)
+    nt = (T + bt - 1) // bt
+    o = np.zeros((B, T, HQ, v.shape[-1]), dtype=np.float32)
+    for b in range(B):
+        for hq in range(HQ):
+            h = hq // G
+            qn, kn, w2, wv, vv, od, ld, md = [], [], [], [], [], [], [], []
+            for i in range(nt):
+                sl = slice(i * bt, min(T, (i + 1) * bt))
+                n = sl.stop - sl.start
+                bq = q[b, sl, hq].astype(np.float32)
+                bk = k[b, sl, h].astype(np.float32)
+                bw = w[b, sl, h].astype(np.float32)
+                bb = beta[b, sl, h].astype(np.float32)
+                A = np.tril(_dot(bw, bw.T), -1) * bb[:, None]
+                Tm = _bf16(np.linalg.inv(np.eye(n) + A.astype(np.float64)))
+                wb = _bf16(bw * bb[:, None])
+                qw = _bf16(np.tril(_dot(bq, bw.T)))
+                qwT = _bf16(_dot(qw, Tm))
+                wbk = _bf16(np.tril(_dot(wb, bk.T), -1))
+                Ad = _dot(bq, bk.T) - _dot(qwT, wbk)
+                z = np.where(np.tril(np.ones((n, n), dtype=bool)), Ad * sm, -np.inf).astype(np.float32)
+                m = z.max(axis=1)
+                pz = np.exp2(z - m[:, None]).astype(np.float32)
+                od.append(_dot(_bf16(pz), v[b, sl, h].astype(np.float32)))   # p.to(bf16) @ v (:115)
+                ld.append(pz.sum(axis=1))
+                md.append(m)
+                qn.append(bq - _dot(qwT, wb))
+                w2.append(_bf16(_dot(Tm, wb)))
+                kn.append(_bf16(bk - _dot(_bf16(_dot(Tm, wbk)).T, bw)))
+                wv.append(bw)
+                vv.append(v[b, sl, h].astype(np.float32))
+            for i in range(nt):
+                bq = qn[i].copy()
+                bo, bl, bm = od[i].copy(), ld[i].copy(), md[i].copy()
+                for j in range(i - 1, -1, -1):
+                    z = _dot(_bf16(bq), kn[j].T) * sm
+                    mn = np.maximum(bm, z.max(axis=1))
+                    alpha = np.exp2(bm - mn)
+                    pz = np.exp2(z - mn[:, None]).astype(np.float32)
+                    bo = bo * alpha[:, None]
+                    bl = bl * alpha + pz.sum(axis=1)
+                    bm = mn
+                    bo = bo + _dot(_bf16(pz), vv[j])
+                    s2 = _dot(_bf16(bq), wv[j].T)
+                    bq = bq - _dot(_bf16(s2), w2[j])
+                o[b, i * bt:i * bt + bo.shape[0], hq] = _bf16(bo / bl[:, None])
     return o

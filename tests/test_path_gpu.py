@@ -15,7 +15,7 @@ compute in bf16 with fp32 accumulation, so the bars are:
 import numpy as np
 import pytest
 
-from conftest import PATH_CASES, load_path_golden
+from conftest import PATH_ATTN_CASES, PATH_CASES, load_path_golden
 
 pytestmark = pytest.mark.gpu
 
@@ -154,3 +154,44 @@ def test_path_varlen_matches_separate_sequences(cuda_device):
         o_a, _ = parallel_lucid_path_attention(k[:, :150], v[:, :150], w[:, :150], beta[:, :150], scale=0.15)
         o_b, _ = parallel_lucid_path_attention(k[:, 150:], v[:, 150:], w[:, 150:], beta[:, 150:], scale=0.15)
     torch.testing.assert_close(o, torch.cat([o_a, o_b], 1), rtol=0, atol=0)
+
+
+def _attn(torch, d, dev, scale=None):
+    from lucid_b200.path import parallel_path_attention_fwd
+    k, v, w, beta = (_to(torch, d[n], dev) for n in ("k", "v", "w", "beta"))
+    q = _to(torch, d["q"], dev) if d.get("q") is not None else None
+    o, lse = parallel_path_attention_fwd(q, k, v, w, beta, scale=scale)
+    torch.cuda.synchronize()
+    return o.float().cpu().numpy(), lse.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", PATH_ATTN_CASES)
+def test_path_attention_matches_reference_fixture(cuda_device, name):
+    torch = pytest.importorskip("torch")
+    d = load_path_golden(name)
+    o, lse = _attn(torch, d, cuda_device)
+    assert np.all(np.isfinite(o)) and np.all(np.isfinite(lse))
+    err = np.abs(o - d["o"]) - (1e-2 + 2.0 ** -8 * np.abs(d["o"]))
+    assert err.max() <= 0, np.abs(o - d["o"]).max()
+    assert np.abs(lse - d["lse"]).max() < 2e-2
+
+
+@pytest.mark.parametrize("B,T,H,HQ,with_q,scale", [(1, 1000, 1, 1, False, None), (2, 300, 2, 4, True, 0.2),
+                                                     (1, 64, 1, 1, False, None)])
+def test_path_attention_matches_oracle(cuda_device, B, T, H, HQ, with_q, scale):
+    """Many blocks (T = 1000: 8 blocks, rescaling of the running maximum), GQA with an
+    explicit q and sharper scores, a sequence shorter than one block.  Bar: 1e-2, or
+    1.5x the deviation of the reference's own bf16 kernels (oracle/path_precision.py)
+    where that is larger."""
+    torch = pytest.importorskip("torch")
+    from oracle.path_oracle import make_path_inputs, path_attention_fwd
+    from oracle.path_precision import reference_bf16_attention
+    d = make_path_inputs(40 + T, B, T, H, 128, HQ, with_q)
+    ro, rl = path_attention_fwd(d["k"], d["v"], d["w"], d["beta"], q=d["q"], scale=scale)
+    ref_dev = float(np.abs(reference_bf16_attention(d["k"], d["v"], d["w"], d["beta"], q=d["q"],
+                                                    scale=scale) - ro).max())
+    o, lse = _attn(torch, d, cuda_device, scale=scale)
+    dev = float(np.abs(o - ro).max())
+    assert np.all(np.isfinite(o))
+    assert dev <= max(1.5 * ref_dev, 1e-2), (dev, ref_dev)
+    assert np.abs(lse - rl).max() < 2e-2
