@@ -279,7 +279,7 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
         for name in names:
             lib.lucid_profile_enable(_lib.KERNEL_IDS[name])
             for _ in range(2):
-                o, st = path_fwd(kd, vd, wd, bd)
+                o, st, _ = path_fwd(kd, vd, wd, bd)
                 path_bwd(st, do, kd, wd, bd)
                 del o, st
             torch.cuda.synchronize()

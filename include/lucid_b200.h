@@ -94,6 +94,39 @@ int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps,
                             void* x, void* khat, void* u, float* rstd, float* dinv, void* stream);
 
 /*
+ * Decode step of the solve: x_new = v_new - exp(scale k^_new K^_cache^T - 1/scale) X_cache.
+ * Replaces LucidAttention.get_new_v_prime (modeling_lucid.py:576-598) with the
+ * reference's cache convention (raw keys and solved values, :479-481); as in the
+ * reference the Ln new tokens do not see one another and the diagonal P_rr is not
+ * divided out.  k^ = RMSNorm(k) without affine (eps), computed on the fly for the
+ * cache.  All tensors bf16 [B, H, L, D] strided (sb, sh, sn), strides multiples of
+ * 4 elements; k_new / v_new / x_new have L = Ln, k_cache / x_cache L = Nc.
+ */
+size_t lucid_decode_workspace_bytes(int B, int H, int Ln, int Nc, int D);
+int lucid_decode_update(int B, int H, int Ln, int Nc, int D, float scale, float eps,
+                        const void* k_new, int64_t kn_sb, int64_t kn_sh, int64_t kn_sn,
+                        const void* v_new, int64_t vn_sb, int64_t vn_sh, int64_t vn_sn,
+                        const void* k_cache, int64_t kc_sb, int64_t kc_sh, int64_t kc_sn,
+                        const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
+                        void* x_new, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Decode attention: o = softmax(scale q K_cache^T + causal) X_cache for Ln new
+ * queries at positions Nc - Ln .. Nc - 1 of a cache that already holds them
+ * (eager_lucid_attention_forward, modeling_lucid.py:505-549, after the cache
+ * update of :479-481).  q [B, Hq, Ln, D], caches [B, Hkv, Nc, D], o [B, Hq, Ln, D]
+ * (pass the strides of a [B, Ln, Hq, D] tensor for the reference's layout).
+ */
+size_t lucid_decode_attn_workspace_bytes(int B, int Hq, int Ln, int Nc, int D);
+int lucid_decode_attn(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale,
+                      const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                      const void* k_cache, int64_t kc_sb, int64_t kc_sh, int64_t kc_sn,
+                      const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
+                      void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Attention forward: O = softmax(scale Q K^T + causal) X.
  * Replaces LucidAttention.eager_lucid_attention_forward
  * (modeling_lucid.py:505-549; SDPA with repeat_kv, is_causal=True).
@@ -164,6 +197,9 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale,
  * with strides (sb, st, sh).  q may be NULL, meaning q = k (then HQ == H).
  * The workspace (lucid_path_fwd_workspace_bytes) holds the state the
  * backward reads: keep it unchanged until lucid_path_bwd has run.
+ * k_cache (may be NULL; [B, T, H, D] bf16 strided) receives the decode-time
+ * keys of use_cache=True, k_cache_c = (H_{T-1} ... H_{c+1}) k_c
+ * (prepare_k_cache.py:8-74).
  */
 size_t lucid_path_fwd_workspace_bytes(int B, int T, int H, int HQ, int D);
 int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
@@ -173,6 +209,7 @@ int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
                    const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
                    const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
                    void* o, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                   void* k_cache, int64_t kc_sb, int64_t kc_st, int64_t kc_sh,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
@@ -245,6 +282,7 @@ int lucid_path_attn_fwd(int B, int T, int H, int HQ, int D, float scale,
 #define LUCID_KERNEL_PATH_ROW 12      /* LUCID-Path backward row pass (dA, dQ~ chain) */
 #define LUCID_KERNEL_PATH_COL 13      /* LUCID-Path backward column pass (dK_new, dW, dW2) */
 #define LUCID_KERNEL_PATH_ATTN 14     /* PaTH softmax attention forward */
+#define LUCID_KERNEL_DECODE 15        /* LUCID decode step (get_new_v_prime) */
 int lucid_profile_enable(int kernel);
 int lucid_profile_read(float* total_ms, int* launches);
 

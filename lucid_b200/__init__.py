@@ -11,6 +11,8 @@ from .ops import (  # noqa: F401
     LucidSolveFunction,
     attn_bwd,
     attn_fwd,
+    decode_attention,
+    decode_update,
     lucid_attention,
     padded_len,
     solve_bwd,

@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "liblucid_b200.so")
 LUCID_OK = 0
 KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bwd": 5, "attn_bwd_row": 6,
               "solve_bwd_row": 7, "path_block": 8, "path_scores": 9, "path_solve": 10, "path_solve_t": 11,
-              "path_row": 12, "path_col": 13, "path_attn": 14}
+              "path_row": 12, "path_col": 13, "path_attn": 14, "decode": 15}
 ERRORS = {
     1: "unsupported shape (head_dim must be 128, Hq a multiple of Hkv)",
     2: "pointer or stride not 16-byte aligned",
@@ -54,7 +54,7 @@ SIGNATURES = {
                         + [c_void_p, c_size_t, c_void_p]),
     "lucid_path_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_path_fwd": (c_int, [c_int] * 5 + [c_float] + ([c_void_p] + S3) * 4 + [c_void_p, c_int] + S3
-                       + [c_void_p] + S3 + [c_void_p, c_size_t, c_void_p]),
+                       + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_size_t, c_void_p]),
     "lucid_path_bwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_path_bwd": (c_int, [c_int] * 5 + [c_float] + ([c_void_p] + S3) * 3 + [c_void_p, c_int] + S3
                        + [c_void_p] + S3 + [c_void_p, c_size_t] + ([c_void_p] + S3) * 4 + [c_void_p, c_int] + S3
@@ -62,6 +62,11 @@ SIGNATURES = {
     "lucid_path_attn_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_path_attn_fwd": (c_int, [c_int] * 5 + [c_float] + ([c_void_p] + S3) * 4 + [c_void_p, c_int] + S3
                             + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_size_t, c_void_p]),
+    "lucid_decode_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_decode_update": (c_int, [c_int] * 5 + [c_float, c_float] + ([c_void_p] + S3) * 5
+                            + [c_void_p, c_size_t, c_void_p]),
+    "lucid_decode_attn_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_decode_attn": (c_int, [c_int] * 6 + [c_float] + ([c_void_p] + S3) * 4 + [c_void_p, c_size_t, c_void_p]),
     "lucid_selftest_umma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "lucid_profile_enable": (c_int, [c_int]),
     "lucid_profile_read": (c_int, [c_float_p, ctypes.POINTER(c_int)]),

@@ -20,7 +20,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "liblucid_b200.so")
 
 SOURCES = ["lucid_prep.cu", "lucid_fwd.cu", "lucid_bwd.cu", "capi.cu", "path_block.cu", "path_kernels.cu",
-           "path_capi.cu"]
+           "path_capi.cu", "lucid_decode.cu", "decode_capi.cu"]
 HEADERS = ["sm100.cuh", "lucid_common.cuh", "tmap.h", "path_common.cuh", "profile.h"]
 
 NVCC_FLAGS = [

@@ -60,4 +60,17 @@ struct BwdArgs {
   int* status;
 };
 
+// Decode step (get_new_v_prime) and decode attention: one pass over the caches.
+struct DecodeArgs {
+  int B, H, Ln, Nc, nsplit, rows_per_split;
+  float s, eps;
+  const bf16* kn; long long kn_sb, kn_sh, kn_st;   // new keys    [B,H,Ln,D] (attention: queries [B,Hq,Ln,D])
+  const bf16* vn; long long vn_sb, vn_sh, vn_st;   // new values  [B,H,Ln,D]
+  const bf16* kc; long long kc_sb, kc_sh, kc_st;   // cached keys [B,H,Nc,D]
+  const bf16* xc; long long xc_sb, xc_sh, xc_st;   // cached solved values [B,H,Nc,D]
+  bf16* out; long long o_sb, o_sh, o_st;
+  float* part;                                     // per-split partial sums
+  int Hq;                                          // attention: query heads (H = kv heads)
+};
+
 }  // namespace lb

@@ -119,6 +119,10 @@ __global__ void __launch_bounds__(pblk::kThreads) path_bgemm_kernel(const __grid
       const POperand& op = side == 0 ? a.A[p] : a.B[p];
       float v[64];
       pmat_load64(op.m, b, h, blk, r, c0, v);
+      if (op.lo) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] -= __bfloat162float(__float2bfloat16(v[e]));
+      }
       float sc = op.scale;
       if (op.rsc.ptr != nullptr) sc *= pvec_at(op.rsc, b, h, t);
 #pragma unroll
@@ -341,6 +345,12 @@ __global__ void path_pack_kernel(bf16* out, long long o_sb, long long o_st, long
   st_bf16x8(out + (long long)b * o_sb + (long long)t * o_st + (long long)h * o_sh + c8 * 8, acc);
 }
 
+// Identity matrices in an fp32 [heads][128][128] buffer (one 128x128 matrix per CTA).
+__global__ void path_eye_kernel(float* out, long long head_stride) {
+  float* m = out + (long long)blockIdx.x * head_stride;
+  for (int e = threadIdx.x; e < 128 * 128; e += blockDim.x) m[e] = ((e >> 7) == (e & 127)) ? 1.f : 0.f;
+}
+
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
@@ -351,6 +361,12 @@ cudaError_t launch_path_bgemm(const BGemmArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(path_bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(3 * 2 * 32768 + 64));
   if (e != cudaSuccess) return e;
   path_bgemm_kernel<<<(unsigned)n, pblk::kThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_path_eye(float* out, long long heads, long long head_stride, cudaStream_t st) {
+  if (heads == 0) return cudaSuccess;
+  path_eye_kernel<<<(unsigned)heads, 256, 0, st>>>(out, head_stride);
   return cudaGetLastError();
 }
 

@@ -9,6 +9,7 @@
 namespace lb {
 cudaError_t launch_path_bgemm(const BGemmArgs& a, cudaStream_t st);
 cudaError_t launch_path_triinv(const TriInvArgs& a, cudaStream_t st);
+cudaError_t launch_path_eye(float* out, long long heads, long long head_stride, cudaStream_t st);
 cudaError_t launch_path_gsum(float* out, const float* x0, const float* x1, long long heads_out, long long per_head,
                              int G, cudaStream_t st);
 cudaError_t launch_path_rowdot(const float* X, int Npad, const bf16* w, long long w_sb, long long w_st, long long w_sh,
@@ -83,8 +84,10 @@ struct FwdLayout {
     L = c.take(d.pairs_q() * 2);
     Qs = c.take(d.pairs_q() * 2);
     M = c.take((d.BHQ > d.BHK ? d.blocks_q() : d.blocks_k()) * 4);
+    X = c.take((size_t)d.BHK * kTile * 4);
     total = c.off;
   }
+  size_t X;
 };
 
 struct BwdLayout {
@@ -189,6 +192,12 @@ POperand opnd(const PMat& m, int trans = 0, float scale = 1.f, int mask = kMaskN
   o.trans = trans;
   o.scale = scale;
   o.mask = mask;
+  return o;
+}
+// The bf16 rounding residual of an fp32 operand (paired with opnd(m) it gives ~16 bits).
+POperand opnd_lo(const PMat& m, int trans = 0, float scale = 1.f) {
+  POperand o = opnd(m, trans, scale);
+  o.lo = 1;
   return o;
 }
 POperand opnd_rs(const PMat& m, int trans, const PVec& rs) {
@@ -344,6 +353,7 @@ int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
                    const void* w, int64_t w_sb, int64_t w_st, int64_t w_sh,
                    const void* beta, int beta_fp32, int64_t be_sb, int64_t be_st, int64_t be_sh,
                    void* o, int64_t o_sb, int64_t o_st, int64_t o_sh,
+                   void* k_cache, int64_t kc_sb, int64_t kc_st, int64_t kc_sh,
                    void* workspace, size_t workspace_bytes, void* stream) {
   if (!path_shape_ok(B, T, H, HQ, D)) return LUCID_ERR_SHAPE;
   if (q == nullptr) {
@@ -352,7 +362,8 @@ int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
   }
   if (B == 0 || T == 0 || H == 0) return LUCID_OK;
   if (!al16(q) || !al16(k) || !al16(v) || !al16(w) || !al16(o) || !st8(q_sb, q_st, q_sh) ||
-      !st8(k_sb, k_st, k_sh) || !st8(v_sb, v_st, v_sh) || !st8(w_sb, w_st, w_sh) || !st8(o_sb, o_st, o_sh))
+      !st8(k_sb, k_st, k_sh) || !st8(v_sb, v_st, v_sh) || !st8(w_sb, w_st, w_sh) || !st8(o_sb, o_st, o_sh) ||
+      (k_cache != nullptr && (!al16(k_cache) || !st8(kc_sb, kc_st, kc_sh))))
     return LUCID_ERR_ALIGN;
   const Dims d(B, T, H, HQ);
   if (d.NPAIR * 128 >= (1LL << 31)) return LUCID_ERR_TOO_LARGE;
@@ -422,6 +433,60 @@ int lucid_path_fwd(int B, int T, int H, int HQ, int D, float scale,
                     reinterpret_cast<int*>(P(lay.flags)), status};
     ProfileScope ps(LUCID_KERNEL_PATH_SOLVE, st);
     if (launch_path_solve(false, tmL, tmO, tmU, a, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  }
+  if (k_cache != nullptr) {
+    // Decode-time keys (prepare_k_cache.py:8-49): every key transformed by all later
+    // Householders, k_cache_c = (H_{T-1} ... H_{c+1}) k_c.  Per block j:
+    //   K_cache_j = K_new_j P_j,  P_{NB-1} = I,  P_j = G_{j+1}^T P_{j+1} = P_{j+1} - W2_{j+1}^T (W_{j+1} P_{j+1})
+    // with the suffix products P_j (fp32, [B*H][NB][128][128]) in the M scratch.
+    const int NB = d.NB;
+    float* Pbuf = reinterpret_cast<float*>(P(lay.M));
+    if (launch_path_eye(Pbuf + (size_t)(NB - 1) * kTile, d.BHK, (long long)NB * kTile, st) != cudaSuccess)
+      return LUCID_ERR_LAUNCH;
+    Launcher Lk{st, status, B, 1};
+    for (int j = NB - 2; j >= 0; --j) {
+      const PMat Pn = ibuf(Pbuf + (size_t)(j + 1) * kTile, true, H, Np, 1);
+      const PMat Pj = ibuf(Pbuf + (size_t)j * kTile, true, H, Np, 1);
+      PMat Wn = ubuf(static_cast<const bf16*>(w) + (int64_t)(j + 1) * 128 * w_st, w_sb, w_st, w_sh, T - (j + 1) * 128, 1);
+      const PMat W2n = ibuf(static_cast<bf16*>(P(lay.W2)) + (size_t)(j + 1) * kTile, false, H, Np, 1);
+      const PMat Xk = ibuf(P(lay.X), true, H, 128, 1);
+      // fp32 products enter the tensor core as bf16 hi + lo, so the products keep
+      // ~16 mantissa bits along the chain
+      {  // X = W_{j+1} P_{j+1}
+        BGemmArgs a;
+        a.nprod = 2;
+        a.A[0] = opnd(Wn);
+        a.B[0] = opnd(Pn);
+        a.A[1] = opnd(Wn);
+        a.B[1] = opnd_lo(Pn);
+        a.O = Xk;
+        Lk.gemm(a, H);
+      }
+      {  // P_j = P_{j+1} - W2_{j+1}^T X
+        BGemmArgs a;
+        a.nprod = 2;
+        a.A[0] = opnd(W2n, 1, -1.f);
+        a.B[0] = opnd(Xk);
+        a.A[1] = opnd(W2n, 1, -1.f);
+        a.B[1] = opnd_lo(Xk);
+        a.nc = 1;
+        a.C[0] = Pn;
+        a.O = Pj;
+        Lk.gemm(a, H);
+      }
+    }
+    {  // K_cache = K_new P   (all blocks)
+      BGemmArgs a;
+      a.nprod = 2;
+      a.A[0] = opnd(ibuf(P(lay.Kn), false, H, Np, 1));
+      a.B[0] = opnd(ibuf(Pbuf, true, H, Np, 1));
+      a.A[1] = opnd(ibuf(P(lay.Kn), false, H, Np, 1));
+      a.B[1] = opnd_lo(ibuf(Pbuf, true, H, Np, 1));
+      PMat out = ubuf(k_cache, kc_sb, kc_st, kc_sh, T, 1);
+      a.O = out;
+      Lc.gemm(a, H);
+    }
+    if (Lk.err != cudaSuccess || Lc.err != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
   return LUCID_OK;
 }

@@ -56,6 +56,7 @@ struct POperand {
   int mask = kMaskNone; // mask of the stored matrix (row r, column c)
   float scale = 1.f;
   PVec rsc;             // optional scale of every stored row
+  int lo = 0;           // use the bf16 rounding residual v - bf16(v) of the stored values
 };
 
 // C = out_mask(epi( rsc_out .* sum_p op(A_p) op(B_p)  +  sum_c beta_c rsc_c .* C_c ))

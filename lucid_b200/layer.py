@@ -10,17 +10,27 @@ runs on the B200 kernels of lucid_b200.ops.
 imported reference module (its ``LucidAttention`` class) to the B200
 kernels, leaving everything else of the reference model untouched.
 
-Scope of the training / prefill path (past_seq_len == 0); incremental
-decoding (get_new_v_prime, :576-598) raises NotImplementedError.
+Training / prefill (past_seq_len == 0) and incremental decoding
+(get_new_v_prime, :576-598, then attention over the cache) are both covered;
+the cache keeps raw keys and solved values like the reference (:479-481).
 """
 from __future__ import annotations
 
 import torch
 from torch import nn
 
-from .ops import LucidAttentionFunction, LucidAttnFunction, LucidSolveFunction
+from .ops import LucidAttentionFunction, LucidAttnFunction, LucidSolveFunction, decode_attention, decode_update
 
-__all__ = ["LucidAttention", "patch_reference", "get_v_prime", "eager_lucid_attention_forward"]
+__all__ = ["LucidAttention", "patch_reference", "get_v_prime", "get_new_v_prime", "eager_lucid_attention_forward"]
+
+
+def _cache_layer(past_key_value, layer_idx):
+    """(keys, values) of one layer of a transformers cache (old key_cache /
+    value_cache lists or the layered Cache of transformers 5)."""
+    if hasattr(past_key_value, "key_cache"):
+        return past_key_value.key_cache[layer_idx], past_key_value.value_cache[layer_idx]
+    layer = past_key_value.layers[layer_idx]
+    return layer.keys, layer.values
 
 
 def get_v_prime(self, key: torch.Tensor, value: torch.Tensor, scaling: float,
@@ -37,11 +47,28 @@ def get_v_prime(self, key: torch.Tensor, value: torch.Tensor, scaling: float,
     return LucidSolveFunction.apply(key, value, float(scaling), float(eps))
 
 
+def get_new_v_prime(self, key: torch.Tensor, value: torch.Tensor, attention_mask: torch.Tensor | None,
+                    scaling: float, past_key_value) -> torch.Tensor:
+    """Decode step (modeling_lucid.py:576-598): x_new = value -
+    exp(s k_norm(key) k_norm(K_cache)^T - 1/s) X_cache, one pass over the cache on
+    the B200 (cached keys normalised on the fly)."""
+    which = getattr(self, "which_rmsnorm", "exp_k_norm")
+    if which != "exp_k_norm":
+        raise NotImplementedError(f"{which} not implemented")
+    eps = self.k_norm.eps if getattr(self.k_norm, "eps", None) is not None else 1e-5
+    k_cache, x_cache = _cache_layer(past_key_value, self.layer_idx)
+    return decode_update(key, value, k_cache, x_cache, float(scaling), float(eps))
+
+
 def eager_lucid_attention_forward(self, query: torch.Tensor, key: torch.Tensor, v_prime: torch.Tensor,
                                   scaling: float, attention_mask: torch.Tensor | None = None, **kwargs):
     """softmax(scaling Q K^T + causal) repeat_kv(X), returned as
     (O [B, N, Hq, D], None) like modeling_lucid.py:505-549.  Grouped-query
-    heads are handled natively (no repeat_kv copy)."""
+    heads are handled natively (no repeat_kv copy).  With fewer queries than
+    keys (decoding against a cache) the queries sit at the end of the key
+    sequence, as the reference's causal mask places them (:600-618)."""
+    if query.shape[-2] != key.shape[-2]:
+        return decode_attention(query, key, v_prime, float(scaling)), None
     return LucidAttnFunction.apply(query, key, v_prime, float(scaling)), None
 
 
@@ -70,6 +97,7 @@ class LucidAttention(nn.Module):
         self.o_proj = nn.Linear(config.num_attention_heads * self.head_dim, config.hidden_size, bias=bias)
 
     get_v_prime = get_v_prime
+    get_new_v_prime = get_new_v_prime
     eager_lucid_attention_forward = eager_lucid_attention_forward
 
     def create_causal_mask(self, query, key, past_seq_len: int, attention_mask=None):
@@ -86,10 +114,10 @@ class LucidAttention(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
                 past_key_value=None, cache_position=None, **kwargs):
-        """Training / prefill forward (modeling_lucid.py:421-503 with
-        past_seq_len == 0): projections, fused LUCID attention, o_proj."""
-        if past_key_value is not None and past_key_value.get_seq_length(self.layer_idx) > 0:
-            raise NotImplementedError("incremental decoding (get_new_v_prime) is not implemented")
+        """modeling_lucid.py:421-503: projections, LUCID attention, o_proj.  Without
+        a cache (training) the fused op runs; with a cache the prefill solves X,
+        decoding steps use get_new_v_prime, and the cache is updated with raw keys
+        and solved values before the attention, as in the reference."""
         if self.use_rope:
             raise NotImplementedError("use_rope=True is not supported by this layer")
         input_shape = hidden_states.shape[:-1]
@@ -97,15 +125,26 @@ class LucidAttention(nn.Module):
         q = self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
         k = self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
         v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        o = LucidAttentionFunction.apply(q, k, v, float(self.scaling), float(self.k_norm.eps or 1e-5))
+        if past_key_value is None or self.training:
+            o = LucidAttentionFunction.apply(q, k, v, float(self.scaling), float(self.k_norm.eps or 1e-5))
+        else:
+            past = past_key_value.get_seq_length(self.layer_idx)
+            if past == 0:
+                x = self.get_v_prime(k, v, self.scaling, None)
+            else:
+                x = self.get_new_v_prime(k, v, None, self.scaling, past_key_value)
+            k_all, x_all = past_key_value.update(k, x, self.layer_idx,
+                                                 {"cache_position": cache_position})
+            o, _ = self.eager_lucid_attention_forward(q, k_all, x_all, self.scaling, None)
         o = o.reshape(*input_shape, -1).contiguous()
         return self.o_proj(o), None
 
 
 def patch_reference(module) -> None:
-    """Rebind ``module.LucidAttention.get_v_prime`` and
+    """Rebind ``module.LucidAttention.get_v_prime``, ``.get_new_v_prime`` and
     ``.eager_lucid_attention_forward`` (an imported modeling_lucid module)
     to the B200 kernels."""
     cls = module.LucidAttention
     cls.get_v_prime = get_v_prime
+    cls.get_new_v_prime = get_new_v_prime
     cls.eager_lucid_attention_forward = eager_lucid_attention_forward

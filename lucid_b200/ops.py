@@ -27,7 +27,7 @@ from . import _lib
 __all__ = [
     "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
     "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
-    "lucid_attention", "padded_len",
+    "lucid_attention", "padded_len", "decode_update", "decode_attention",
 ]
 
 
@@ -224,3 +224,56 @@ def lucid_attention(query, key, value, scaling: float | None = None, eps: float 
     if scaling is None:
         scaling = query.shape[-1] ** -0.5
     return LucidAttentionFunction.apply(query, key, value, float(scaling), float(eps))
+
+
+# ---------------------------------------------------------------------------
+# decode (inference with a key / solved-value cache)
+# ---------------------------------------------------------------------------
+def _prep_dec(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: LUCID B200 kernels need CUDA tensors (no CPU fallback)")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name}: expected bfloat16, got {t.dtype}")
+    ok = t.stride(-1) == 1 and all(s % 4 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 8 == 0
+    return t if ok else t.contiguous()
+
+
+def decode_update(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor, x_cache: torch.Tensor,
+                  scale: float, eps: float = 1e-5) -> torch.Tensor:
+    """get_new_v_prime (modeling_lucid.py:576-598): x_new = value -
+    exp(s k^ K^_cache^T - 1/s) X_cache, key/value [B,H,Ln,128], caches
+    [B,H,Nc,128] (raw keys, solved values).  Returns x_new [B,H,Ln,128]."""
+    lib = _lib.load()
+    key, value = _prep_dec(key, "key"), _prep_dec(value, "value")
+    key_cache, x_cache = _prep_dec(key_cache, "key_cache"), _prep_dec(x_cache, "value_cache")
+    B, H, Ln, D = key.shape
+    Nc = key_cache.shape[2]
+    out = torch.empty(B, H, Ln, D, dtype=torch.bfloat16, device=key.device)
+    ws = _ws(lib.lucid_decode_workspace_bytes(B, H, Ln, Nc, D), key.device)
+    rc = lib.lucid_decode_update(B, H, Ln, Nc, D, float(scale), float(eps), key.data_ptr(), *_s3(key),
+                                 value.data_ptr(), *_s3(value), key_cache.data_ptr(), *_s3(key_cache),
+                                 x_cache.data_ptr(), *_s3(x_cache), out.data_ptr(), *_s3(out),
+                                 ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_decode_update")
+    return out
+
+
+def decode_attention(query: torch.Tensor, key_cache: torch.Tensor, x_cache: torch.Tensor,
+                     scale: float) -> torch.Tensor:
+    """softmax(s Q K^T + causal) X for Ln new queries at the end of the cache
+    (eager_lucid_attention_forward during decoding).  query [B,Hq,Ln,128],
+    caches [B,Hkv,Nc,128] already holding the new tokens.  Returns O as
+    [B, Ln, Hq, 128] like the reference (modeling_lucid.py:546)."""
+    lib = _lib.load()
+    query = _prep_dec(query, "query")
+    key_cache, x_cache = _prep_dec(key_cache, "key_cache"), _prep_dec(x_cache, "value_cache")
+    B, Hq, Ln, D = query.shape
+    Hkv, Nc = key_cache.shape[1], key_cache.shape[2]
+    o = torch.empty(B, Ln, Hq, D, dtype=torch.bfloat16, device=query.device)
+    ov = o.transpose(1, 2)
+    ws = _ws(lib.lucid_decode_attn_workspace_bytes(B, Hq, Ln, Nc, D), query.device)
+    rc = lib.lucid_decode_attn(B, Hq, Hkv, Ln, Nc, D, float(scale), query.data_ptr(), *_s3(query),
+                               key_cache.data_ptr(), *_s3(key_cache), x_cache.data_ptr(), *_s3(x_cache),
+                               ov.data_ptr(), *_s3(ov), ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_decode_attn")
+    return o

@@ -16,8 +16,7 @@ saved for the backward.  There is no CPU path: CPU tensors raise.
 
 Differences from the reference, all raising instead of computing something
 else: head_dim must be 128 (the reference accepts 16/32/64/128, parallel.py:230);
-``g`` must be None (the reference asserts the same, :235); ``use_cache=True``
-(the decode-time key cache of prepare_k_cache.py) is not built yet.
+``g`` must be None (the reference asserts the same, :235).
 ``cu_seqlens`` (packed variable-length batches, B == 1) runs one call per
 sequence.
 """
@@ -58,9 +57,10 @@ def _ws(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
-def path_fwd(k, v, w, beta, q=None, scale=None):
-    """Forward stage.  Returns (o [B,T,HQ,V], state); ``state`` is the
-    forward workspace the backward reads."""
+def path_fwd(k, v, w, beta, q=None, scale=None, use_cache=False):
+    """Forward stage.  Returns (o [B,T,HQ,V], state, k_cache); ``state`` is the
+    forward workspace the backward reads; ``k_cache`` ([B,T,H,K], the keys
+    transformed by every later Householder, prepare_k_cache.py) or None."""
     lib = _lib.load()
     k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
     beta = _prep(beta, "beta", 3)
@@ -77,13 +77,15 @@ def path_fwd(k, v, w, beta, q=None, scale=None):
     s = float(K ** -0.5 if scale is None else scale)
     dev = k.device
     o = torch.empty(B, T, HQ, v.shape[-1], dtype=v.dtype, device=dev)
+    kc = torch.empty(B, T, H, K, dtype=k.dtype, device=dev) if use_cache else None
+    kcp, kcs = (kc.data_ptr(), _s3(kc)) if kc is not None else (None, (0, 0, 0))
     ws = _ws(lib.lucid_path_fwd_workspace_bytes(B, T, H, HQ, K), dev)
     qp, qs = (q.data_ptr(), _s3(q)) if q is not None else (None, (0, 0, 0))
     rc = lib.lucid_path_fwd(B, T, H, HQ, K, s, qp, *qs, k.data_ptr(), *_s3(k), v.data_ptr(), *_s3(v),
                             w.data_ptr(), *_s3(w), beta.data_ptr(), int(beta.dtype == torch.float32), *beta.stride(),
-                            o.data_ptr(), *_s3(o), ws.data_ptr(), ws.numel(), _stream())
+                            o.data_ptr(), *_s3(o), kcp, *kcs, ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_path_fwd")
-    return o, ws
+    return o, ws, kc
 
 
 def path_bwd(state, do, k, w, beta, q=None, scale=None):
@@ -125,12 +127,14 @@ class ParallelLUCIDPathAttentionFunction(torch.autograd.Function):
         if g is not None:
             raise NotImplementedError("g is not supported (the reference asserts g is None)")
         q_given = q is not None and q is not k
-        o, state = path_fwd(k, v, w, beta, q=q if q_given else None, scale=scale)
+        o, state, kc = path_fwd(k, v, w, beta, q=q if q_given else None, scale=scale, use_cache=use_cache)
         ctx.save_for_backward(q if q_given else None, k, w, beta, state)
         ctx.q_given = q_given
         ctx.q_is_k = q is k
         ctx.scale = scale
-        return o, None
+        if kc is not None:
+            ctx.mark_non_differentiable(kc)
+        return o, kc
 
     @staticmethod
     def backward(ctx, do, dk_cache):
@@ -144,9 +148,10 @@ class ParallelLUCIDPathAttentionFunction(torch.autograd.Function):
 
 
 def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_seqlens=None, use_cache=False):
-    """Drop-in for lucid_path/triton_code/parallel.py:180-241; returns (o, k_cache)."""
-    if use_cache:
-        raise NotImplementedError("use_cache=True (prepare_k_cache) is not implemented")
+    """Drop-in for lucid_path/triton_code/parallel.py:180-241; returns (o, k_cache).
+    k_cache is None unless use_cache (then the keys transformed by every later
+    Householder, prepare_k_cache.py:8-74; no gradient flows through it, as in
+    the reference, whose backward ignores dk_new)."""
     if q is None:
         q = k
     if scale is None:
@@ -162,18 +167,19 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
     if q.shape[-2] % k.shape[-2] != 0:
         raise ValueError("the number of query heads should be divisible by the number of key heads")
     if cu_seqlens is None:
-        return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, False)
+        return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, bool(use_cache))
     if k.shape[0] != 1:
         raise ValueError("cu_seqlens requires a packed batch of size 1")
     bounds = [int(x) for x in cu_seqlens.tolist()]
-    outs = []
+    outs, caches = [], []
     for a, b in zip(bounds[:-1], bounds[1:]):
         qa = q[:, a:b] if q is not k else None
         ka = k[:, a:b]
-        o, _ = ParallelLUCIDPathAttentionFunction.apply(qa if qa is not None else ka, ka, v[:, a:b], w[:, a:b],
-                                                        beta[:, a:b], None, float(scale), None, False)
+        o, kc = ParallelLUCIDPathAttentionFunction.apply(qa if qa is not None else ka, ka, v[:, a:b], w[:, a:b],
+                                                         beta[:, a:b], None, float(scale), None, bool(use_cache))
         outs.append(o)
-    return torch.cat(outs, dim=1), None
+        caches.append(kc)
+    return torch.cat(outs, dim=1), (torch.cat(caches, dim=1) if use_cache else None)
 
 
 def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):

@@ -36,7 +36,7 @@ from __future__ import annotations
 import numpy as np
 
 __all__ = ["path_scores", "path_fwd", "path_fwd_blockwise", "path_bwd_blockwise", "path_fwd_bwd_torch",
-           "make_path_inputs", "path_attention_fwd"]
+           "make_path_inputs", "path_attention_fwd", "path_k_cache"]
 
 
 def make_path_inputs(seed: int, B: int, T: int, H: int, K: int, HQ: int | None = None, with_q: bool = False):
@@ -85,6 +85,21 @@ def path_scores(q, k, w, beta):
                 X[:r] -= beta[b, r, h] * np.outer(X[:r] @ wr, wr)
                 A[b, hq, r, :r] = X[:r] @ q[b, r, hq]
     return A
+
+
+def path_k_cache(k, w, beta):
+    """Decode-time keys of use_cache=True (prepare_k_cache.py:8-49): every key
+    transformed by all later Householders, k_cache_c = (H_{T-1} ... H_{c+1}) k_c."""
+    B, T, H, K = k.shape
+    out = np.zeros_like(k)
+    for b in range(B):
+        for h in range(H):
+            X = k[b, :, h, :].copy()
+            for r in range(1, T):
+                wr = w[b, r, h]
+                X[:r] -= beta[b, r, h] * np.outer(X[:r] @ wr, wr)
+            out[b, :, h] = X
+    return out
 
 
 def path_attention_fwd(k, v, w, beta, q=None, scale=None):

@@ -23,7 +23,7 @@ from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["reference_bf16_forward", "reference_bf16_attention"]
+__all__ = ["reference_bf16_forward", "reference_bf16_attention", "reference_bf16_k_cache"]
 
 
 def _bf16(x):
@@ -157,3 +157,36 @@ def reference_bf16_attention(k, v, w, beta, q=None, scale=None, bt=64):
                     bq = bq - _dot(_bf16(s2), w2[j])
                 o[b, i * bt:i * bt + bo.shape[0], hq] = _bf16(bo / bl[:, None])
     return o
+
+
+def reference_bf16_k_cache(k, w, beta, bt=64):
+    """k_cache [B, T, H, K] of use_cache=True as the reference computes it:
+    k_new and w2 from triangular_solve_fwd (stored bf16, :141-148), then
+    prepare_k_cache.py:36-47 with the key in fp32 and the products on bf16
+    operands (b_k.to(w2.dtype), b_A.to(w1.dtype)), stored bf16."""
+    B, T, H, K = k.shape
+    nt = (T + bt - 1) // bt
+    out = np.zeros(k.shape, dtype=np.float32)
+    for b in range(B):
+        for h in range(H):
+            kn, w2, wv = [], [], []
+            for i in range(nt):
+                sl = slice(i * bt, min(T, (i + 1) * bt))
+                n = sl.stop - sl.start
+                bk = k[b, sl, h].astype(np.float32)
+                bw = w[b, sl, h].astype(np.float32)
+                bb = beta[b, sl, h].astype(np.float32)
+                A = np.tril(_dot(bw, bw.T), -1) * bb[:, None]
+                Tm = _bf16(np.linalg.inv(np.eye(n) + A.astype(np.float64)))
+                wb = _bf16(bw * bb[:, None])
+                wbk = _bf16(np.tril(_dot(wb, bk.T), -1))
+                w2.append(_bf16(_dot(Tm, wb)))
+                kn.append(_bf16(bk - _dot(_bf16(_dot(Tm, wbk)).T, bw)))
+                wv.append(bw)
+            for i in range(nt):
+                bk = kn[i].copy()
+                for j in range(i + 1, nt):
+                    bA = _dot(_bf16(bk), w2[j].T)
+                    bk = bk - _dot(_bf16(bA), wv[j])
+                out[b, i * bt:i * bt + bk.shape[0], h] = _bf16(bk)
+    return out

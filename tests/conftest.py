@@ -32,8 +32,21 @@ def load_golden(name: str) -> dict:
 
 
 ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                    if not os.path.basename(p).startswith(("blockwise", "path")))
+                    if not os.path.basename(p).startswith(("blockwise", "path", "decode")))
 PATH_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "path_*.npz")))
+DECODE_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "decode_*.npz")))
+
+
+def load_decode_golden(name: str) -> dict:
+    """Decode fixture from tests/golden/make_golden.py (the reference's
+    get_new_v_prime in float64).  Inputs are exact bf16 values."""
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        d = {k: z[k] for k in z.files}
+    for nm in ("k_cache", "x_cache", "k_new", "v_new"):
+        d[nm] = from_bf16_bits(d.pop(f"{nm}_bf16")).astype(np.float64)
+    return d
+
+
 PATH_ATTN_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "pathattn_*.npz")))
 
 

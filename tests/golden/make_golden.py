@@ -13,7 +13,10 @@ Inputs are rounded to bf16-representable values (stored as float32) so the
 same fixture drives the bf16 GPU kernels.  The reference checkout is only
 needed to regenerate; the fixtures themselves are committed.
 
-Usage:  python tests/golden/make_golden.py /path/to/LUCID
+It also stores ``decode_*.npz``: LucidAttention.get_new_v_prime
+(modeling_lucid.py:576-598) for one decode step against a key / value cache.
+
+Usage:  python tests/golden/make_golden.py /path/to/LUCID [--decode-only]
 """
 from __future__ import annotations
 
@@ -97,6 +100,31 @@ def blockwise_case(mod, k, v, dx, bs: int, eps: float = 1e-5):
                 dv=vv.grad.numpy(), dx=dx.numpy(), scale=np.float64(scale), bs=np.int64(bs))
 
 
+def decode_case(mod, B: int, H: int, Nc: int, Ln: int, D: int, seed: int, eps: float = 1e-5):
+    """LucidAttention.get_new_v_prime (modeling_lucid.py:576-598): one decode step
+    against a cache of raw keys and solved values (the cache convention of :479-481)."""
+    from transformers import LlamaConfig
+    cfg = LlamaConfig(hidden_size=H * D, num_attention_heads=H, num_key_value_heads=H, head_dim=D,
+                      rms_norm_eps=eps, attention_bias=False)
+    cfg.use_rope = False
+    att = mod.LucidAttention(cfg, 0).double()
+    g = torch.Generator().manual_seed(seed)
+    kc = bf16_round(torch.randn(B, H, Nc, D, generator=g, dtype=torch.float64))
+    xc = bf16_round(torch.randn(B, H, Nc, D, generator=g, dtype=torch.float64))
+    kn = bf16_round(torch.randn(B, H, Ln, D, generator=g, dtype=torch.float64))
+    vn = bf16_round(torch.randn(B, H, Ln, D, generator=g, dtype=torch.float64))
+
+    class Cache:  # the two attributes get_new_v_prime reads
+        key_cache = [kc]
+        value_cache = [xc]
+
+    with torch.no_grad():
+        x = att.get_new_v_prime(kn, vn, None, att.scaling, past_key_value=Cache())
+    return dict(x_new=x.numpy().astype(np.float32), k_cache_bf16=bf16_bits(kc.numpy()),
+                x_cache_bf16=bf16_bits(xc.numpy()), k_new_bf16=bf16_bits(kn.numpy()),
+                v_new_bf16=bf16_bits(vn.numpy()), scale=np.float64(att.scaling), eps=np.float64(eps))
+
+
 def f32(d):
     return {kk: (vv.astype(np.float32) if isinstance(vv, np.ndarray) and vv.dtype == np.float64 else vv)
             for kk, vv in d.items()}
@@ -120,6 +148,13 @@ CASES = [
 ]
 
 
+DECODE_CASES = {
+    # name: (B, H, cache length, new tokens, D, seed)
+    "decode_d128": (1, 2, 300, 1, 128, 11),
+    "decode_multi_d128": (2, 1, 777, 3, 128, 12),
+}
+
+
 def main(argv):
     root = argv[1] if len(argv) > 1 else os.environ.get("LUCID_REFERENCE", "")
     if not root or not os.path.exists(os.path.join(root, "modeling_lucid.py")):
@@ -127,6 +162,11 @@ def main(argv):
         return 2
     torch.manual_seed(0)
     mod = load_reference(root)
+    for name, (B, H, Nc, Ln, D, seed) in DECODE_CASES.items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **decode_case(mod, B, H, Nc, Ln, D, seed))
+        print("wrote", name)
+    if "--decode-only" in argv:
+        return 0
     for name, seed, B, Hq, Hkv, N, D, keys, qs in CASES:
         q, k, v, do = make_inputs(seed, B, Hq, Hkv, N, D, keys, qs)
         out = reference_case(mod, q, k, v, do)

@@ -3,8 +3,9 @@
 Runs the reference's own Triton op ``parallel_lucid_path_attention``
 (lucid_path/triton_code/parallel.py:180-241 of saisuryadv/LUCID) in float32
 under Triton's CPU interpreter (TRITON_INTERPRET=1), forward and backward,
-and stores inputs (as bf16 bit patterns) and outputs (float32) in
-``path_*.npz`` next to this script.
+and stores inputs (as bf16 bit patterns) and outputs (float32, including the
+decode-time key cache of use_cache=True, prepare_k_cache.py) in ``path_*.npz``
+next to this script.
 
 The op imports its kernels as the package ``fla.ops.lucid_path`` (the
 flash-linear-attention fork it was written for); this script registers the
@@ -95,10 +96,10 @@ def main(root: str):
         d = make_path_inputs(seed, B, T, H, K, HQ, with_q)
         t = {n: (torch.tensor(d[n], dtype=torch.float32, requires_grad=n != "do") if d[n] is not None else None)
              for n in d}
-        o, _ = op(t["k"], t["v"], t["w"], t["beta"], q=t["q"])
+        o, kc = op(t["k"], t["v"], t["w"], t["beta"], q=t["q"], use_cache=True)
         o.backward(t["do"])
         out = dict(o=o.detach().numpy(), dk=t["k"].grad.numpy(), dv=t["v"].grad.numpy(),
-                   dw=t["w"].grad.numpy(), dbeta=t["beta"].grad.numpy())
+                   dw=t["w"].grad.numpy(), dbeta=t["beta"].grad.numpy(), k_cache=kc.detach().numpy())
         if with_q:
             out["dq"] = t["q"].grad.numpy()
         arrs = {f"{n}_bf16": bf16_bits(d[n]) for n in ("q", "k", "v", "w", "beta", "do") if d[n] is not None}

@@ -1,0 +1,118 @@
+"""Decoding on the B200 kernels: get_new_v_prime (modeling_lucid.py:576-598)
+against the reference's own outputs, decode attention against the oracle, the
+LucidAttention mirror stepping through a cache, and the LUCID-Path decode-time
+key cache (prepare_k_cache.py) against the reference's Triton op."""
+import numpy as np
+import pytest
+
+from conftest import DECODE_CASES, PATH_CASES, load_decode_golden, load_path_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(torch, a, dev):
+    return torch.tensor(a, dtype=torch.float32).to(dev, torch.bfloat16)
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_decode_update_matches_reference_fixture(cuda_device, name):
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import decode_update
+    d = load_decode_golden(name)
+    t = {n: _bf(torch, d[n], cuda_device) for n in ("k_new", "v_new", "k_cache", "x_cache")}
+    x = decode_update(t["k_new"], t["v_new"], t["k_cache"], t["x_cache"], float(d["scale"]), float(d["eps"]))
+    x = x.float().cpu().numpy()
+    err = np.abs(x - d["x_new"]) - (1e-2 + 2.0 ** -8 * np.abs(d["x_new"]))
+    assert err.max() <= 0, np.abs(x - d["x_new"]).max()
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Ln,Nc", [(1, 4, 2, 1, 1000), (2, 2, 2, 3, 300), (1, 8, 1, 1, 5000)])
+def test_decode_attention_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc):
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import decode_attention
+    from oracle.lucid_oracle import decode_attention as ref_attn
+    g = np.random.default_rng(Nc + Ln)
+    bf = lambda a: (torch.tensor(a, dtype=torch.float32).bfloat16().double().numpy())
+    q = bf(g.standard_normal((B, Hq, Ln, 128)))
+    kc = bf(g.standard_normal((B, Hkv, Nc, 128)))
+    xc = bf(g.standard_normal((B, Hkv, Nc, 128)))
+    s = 128 ** -0.5
+    ref = ref_attn(q, kc, xc, s)
+    o = decode_attention(*(_bf(torch, a, cuda_device) for a in (q, kc, xc)), s).float().cpu().numpy()
+    assert o.shape == ref.shape
+    err = np.abs(o - ref) - (1e-2 + 2.0 ** -8 * np.abs(ref))
+    assert err.max() <= 0, np.abs(o - ref).max()
+
+
+def test_layer_prefill_then_decode_matches_ops(cuda_device):
+    """LucidAttention with a cache: prefill fills (raw keys, solved values) and
+    a decode step equals decode_update + decode_attention on that cache."""
+    torch = pytest.importorskip("torch")
+    from transformers import DynamicCache, LlamaConfig
+    from lucid_b200 import decode_attention, decode_update, solve_fwd
+    from lucid_b200.layer import LucidAttention
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                      rms_norm_eps=1e-5)
+    layer = LucidAttention(cfg, 0).to(cuda_device, torch.bfloat16).eval()
+    T = 200
+    h = torch.randn(1, T + 1, 512, device=cuda_device, dtype=torch.bfloat16)
+    cache = DynamicCache()
+    with torch.no_grad():
+        layer(h[:, :T], past_key_value=cache)
+        out, _ = layer(h[:, T:], past_key_value=cache)
+        kc, xc = (cache.layers[0].keys, cache.layers[0].values) if hasattr(cache, "layers") else \
+            (cache.key_cache[0], cache.value_cache[0])
+        assert kc.shape[2] == T + 1 and xc.shape[2] == T + 1
+        # prefill part of the cache holds the solved values
+        k_pre = layer.k_proj(h[:, :T]).view(1, T, 2, 128).transpose(1, 2)
+        v_pre = layer.v_proj(h[:, :T]).view(1, T, 2, 128).transpose(1, 2)
+        x_pre = solve_fwd(k_pre, v_pre, layer.scaling, 1e-5)[0][:, :, :T]
+        torch.testing.assert_close(xc[:, :, :T], x_pre, rtol=0, atol=0)
+        # decode step = decode_update + decode_attention on the cache
+        k1 = layer.k_proj(h[:, T:]).view(1, 1, 2, 128).transpose(1, 2)
+        v1 = layer.v_proj(h[:, T:]).view(1, 1, 2, 128).transpose(1, 2)
+        x1 = decode_update(k1, v1, kc[:, :, :T], xc[:, :, :T], layer.scaling, 1e-5)
+        torch.testing.assert_close(xc[:, :, T:], x1, rtol=0, atol=0)
+        q1 = layer.q_proj(h[:, T:]).view(1, 1, 4, 128).transpose(1, 2)
+        o1 = decode_attention(q1, kc, xc, layer.scaling)
+        ref = layer.o_proj(o1.reshape(1, 1, -1))
+        torch.testing.assert_close(out, ref, rtol=0, atol=0)
+        assert torch.isfinite(out).all()
+
+
+def _kc_bar(d_k, d_w, d_beta, ref):
+    """1e-2, or 1.5x the deviation of the reference's own bf16 key cache
+    (oracle/path_precision.py: k_new and the output are bf16 there too)."""
+    from oracle.path_precision import reference_bf16_k_cache
+    return max(1e-2, 1.5 * float(np.abs(reference_bf16_k_cache(d_k, d_w, d_beta) - ref).max()))
+
+
+@pytest.mark.parametrize("name", [c for c in PATH_CASES if "k128" in c])
+def test_path_key_cache_matches_reference_fixture(cuda_device, name):
+    torch = pytest.importorskip("torch")
+    from lucid_b200.path import parallel_lucid_path_attention
+    d = load_path_golden(name)
+    bar = _kc_bar(d["k"], d["w"], d["beta"], d["k_cache"])
+    k, v, w, beta = (_bf(torch, d[n], cuda_device) for n in ("k", "v", "w", "beta"))
+    q = _bf(torch, d["q"], cuda_device) if d.get("q") is not None else None
+    with torch.no_grad():
+        o, kc = parallel_lucid_path_attention(k, v, w, beta, q=q, use_cache=True)
+    kc = kc.float().cpu().numpy()
+    assert np.abs(kc - d["k_cache"]).max() <= bar, (np.abs(kc - d["k_cache"]).max(), bar)
+
+
+def test_path_key_cache_long_sequence(cuda_device):
+    """12 blocks of suffix products against the float64 oracle."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200.path import parallel_lucid_path_attention
+    from oracle.path_oracle import make_path_inputs, path_k_cache
+    d = make_path_inputs(8, 1, 1500, 1, 128)
+    ref = path_k_cache(d["k"], d["w"], d["beta"])
+    k, v, w, beta = (_bf(torch, d[n], cuda_device) for n in ("k", "v", "w", "beta"))
+    with torch.no_grad():
+        _, kc = parallel_lucid_path_attention(k, v, w, beta, use_cache=True)
+    kc = kc.float().cpu().numpy()
+    assert np.all(np.isfinite(kc))
+    bar = _kc_bar(d["k"], d["w"], d["beta"], ref)
+    assert np.abs(kc - ref).max() <= bar, (np.abs(kc - ref).max(), bar)

@@ -4,7 +4,7 @@ modeling_lucid.py).  CPU only."""
 import numpy as np
 import pytest
 
-from conftest import ATTN_CASES, load_golden
+from conftest import DECODE_CASES, load_decode_golden, ATTN_CASES, load_golden
 from oracle import lucid_oracle as orc
 
 
@@ -79,3 +79,12 @@ def test_oracle_stress_conditioning():
     assert np.all(np.isfinite(p))
     assert off.sum(axis=1).max() > 0.05
     assert np.all(np.abs(np.diag(p) - 1.0) < 1e-3)
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_decode_oracle_matches_reference_fixture(name):
+    """get_new_v_prime (modeling_lucid.py:576-598) of the reference against the oracle."""
+    from oracle.lucid_oracle import decode_update
+    d = load_decode_golden(name)
+    x = decode_update(d["k_new"], d["v_new"], d["k_cache"], d["x_cache"], float(d["scale"]), float(d["eps"]))
+    assert np.max(np.abs(x - d["x_new"])) < 1e-5
