@@ -261,6 +261,38 @@ int lucid_path_attn_fwd(int B, int T, int H, int HQ, int D, float scale,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Context-parallel building blocks (one process per GPU, each owning a contiguous
+ * chunk of the sequence; no counterpart in the reference, which runs long
+ * sequences on one GPU).  Buffers are full-length ([B, H, N, D] / internal
+ * [B, H, Npad, D]); a rank fills the rows it owns and the chunks it receives.
+ *   lucid_cp_prep       prep of row blocks [blk_lo, blk_hi): khat_only = 1 computes
+ *                       rstd and k^ only (received chunks), 0 also the diagonal
+ *                       inverses (own chunk)
+ *   lucid_cp_publish    mark row blocks [blk_lo, blk_hi) of BH (batch, head) rows of a
+ *                       [BH][NB] flag array as solved (received chunks)
+ *   lucid_cp_solve_fwd  the solve of row blocks [blk_lo, blk_hi) given every earlier
+ *                       block published; flags / status are the caller's, zeroed
+ *                       except for the published blocks
+ *   lucid_cp_attn_fwd   the attention of query row blocks [blk_lo, blk_hi) over all
+ *                       keys up to them
+ * blk_lo must be even and blk_hi even or NB (whole pairs of 128-row blocks); the
+ * kernels touch no row outside [0, 128 blk_hi) and write only rows of [blk_lo, blk_hi).
+ * max_ctas caps the persistent grids (0 = one CTA per SM) so that NCCL kernels keep
+ * SMs to run on.  The kernels never wait on anything another launch produces.
+ */
+int lucid_cp_prep(int B, int H, int N, int D, float scale, float eps, int blk_lo, int blk_hi, int khat_only,
+                  const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, void* khat, void* u, float* rstd,
+                  float* dinv, void* stream);
+int lucid_cp_publish(int* flags, int BH, int NB, int blk_lo, int blk_hi, void* stream);
+int lucid_cp_solve_fwd(int B, int H, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
+                       const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn, void* x,
+                       const void* khat, const void* u, const float* dinv, int* flags, int* status, void* stream);
+int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
+                      const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                      const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x,
+                      void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse, int* status, void* stream);
+
+/*
  * Kernel timing hook (benchmarks).  While enabled for one kernel family,
  * every launch of that family's main kernel is bracketed by a pair of CUDA
  * events recorded on the launch stream; lucid_profile_read waits for the

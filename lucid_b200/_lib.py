@@ -67,6 +67,13 @@ SIGNATURES = {
                             + [c_void_p, c_size_t, c_void_p]),
     "lucid_decode_attn_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_decode_attn": (c_int, [c_int] * 6 + [c_float] + ([c_void_p] + S3) * 4 + [c_void_p, c_size_t, c_void_p]),
+    "lucid_cp_prep": (c_int, [c_int] * 4 + [c_float, c_float] + [c_int] * 3 + [c_void_p] + S3
+                      + [c_void_p] * 4 + [c_void_p]),
+    "lucid_cp_publish": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "lucid_cp_solve_fwd": (c_int, [c_int] * 4 + [c_float, c_int, c_int, c_int] + [c_void_p] + S3
+                           + [c_void_p] * 6 + [c_void_p]),
+    "lucid_cp_attn_fwd": (c_int, [c_int] * 5 + [c_float, c_int, c_int, c_int] + [c_void_p] + S3 + [c_void_p] + S3
+                          + [c_void_p] + [c_void_p] + S3 + [c_void_p, c_void_p, c_void_p]),
     "lucid_selftest_umma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "lucid_profile_enable": (c_int, [c_int]),
     "lucid_profile_read": (c_int, [c_float_p, ctypes.POINTER(c_int)]),

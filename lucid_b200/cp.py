@@ -1,0 +1,214 @@
+"""Context-parallel LUCID attention forward for long sequences (the 128K
+configuration): one process per GPU, each rank owning a contiguous chunk of
+C = N / world tokens of every (batch, head).
+
+The reference runs long sequences on one GPU (the blockwise solver of
+modeling_lucid.py:285-312 under gradient checkpointing); this module spreads
+one sequence over the GPUs of a node:
+
+  X = P^-1 V is a forward substitution, so chunk r needs the solved values
+  X_j and the keys K_j of every earlier chunk j < r:
+    R_r = V_r - sum_{j<r} exp(s K^_r K^_j^T - 1/s) X_j ,  X_r = P_rr^-1 R_r
+  and the attention of chunk r's queries needs K_j and X_j of every j <= r.
+
+Protocol (all point-to-point NCCL send/recv, no collective):
+  1. every rank sends its raw keys to every later rank (they are an input,
+     so this starts at once); a receiver normalises them (k^ only);
+  2. the kv heads are split into head groups; for each group g in order,
+     rank r waits for X_j(g) of every j < r, marks those row blocks solved
+     (the wavefront solve's per-block flags), solves its own row blocks,
+     sends its X_r(g) to every later rank and runs the attention of its own
+     queries for the group.  Rank r solves group g while rank r-1 already
+     works on group g+1, so the serial chain across ranks is pipelined over
+     the head groups.
+  Kernels never wait on another launch: every dependency is a stream-ordered
+  NCCL receive, and the persistent kernels leave `reserve_sms` SMs free so
+  the NCCL kernels of the other groups run alongside.
+
+Forward only: the backward of the context-parallel chain is not built (the
+single-GPU op `lucid_attention` has the full backward).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+__all__ = ["cp_lucid_attention_forward", "ChunkProtocol", "KernelBackend"]
+
+
+class ChunkProtocol:
+    """The message schedule of the forward chain, independent of how the
+    chunks are computed (``backend``) and of the process group's device."""
+
+    def __init__(self, backend, group=None):
+        self.be = backend
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def _peer(self, r):
+        return dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    def run(self, q, k, v):
+        be, r, W = self.be, self.rank, self.world
+        be.set_local(q, k)
+        # 1. raw keys flow to every later rank
+        reqs, kbuf = [], {}
+        for j in range(r):
+            kbuf[j] = be.empty_chunk(heads=be.H)
+            reqs.append(dist.irecv(kbuf[j], src=self._peer(j), group=self.group))
+        ksend = be.own_keys()
+        sends = [dist.isend(ksend, dst=self._peer(j), group=self.group) for j in range(r + 1, W)]
+        for rq in reqs:
+            rq.wait()
+        for j in range(r):
+            be.store_keys(j, kbuf[j])
+        be.prep()
+        # 2. solved values, pipelined over head groups
+        xbuf, xreq = {}, {}
+        for g in range(be.G):
+            for j in range(r):
+                xbuf[g, j] = be.empty_chunk(heads=be.Hg)
+                xreq[g, j] = dist.irecv(xbuf[g, j], src=self._peer(j), group=self.group)
+        for g in range(be.G):
+            for j in range(r):
+                xreq[g, j].wait()
+                be.store_values(g, j, xbuf[g, j])
+            be.solve(g, v)
+            xs = be.own_values(g)
+            sends += [dist.isend(xs, dst=self._peer(j), group=self.group) for j in range(r + 1, W)]
+            be.attend(g)
+        for s in sends:
+            s.wait()
+        return be.finish()
+
+
+class KernelBackend:
+    """The chunk computations on the B200 kernels (C ABI lucid_cp_*)."""
+
+    def __init__(self, B, H, Hq, N, D, scale, eps, rank, world, head_groups, device, reserve_sms=8):
+        if D != 128:
+            raise NotImplementedError("head_dim must be 128")
+        if N % world or (N // world) % 256:
+            raise ValueError("the sequence must split into chunks of a multiple of 256 tokens per rank")
+        if H % head_groups or Hq % H:
+            raise ValueError("head_groups must divide the kv heads and Hq must be a multiple of H")
+        self.lib = _lib.load()
+        self.B, self.H, self.Hq, self.N, self.D = B, H, Hq, N, D
+        self.s, self.eps = float(scale), float(eps)
+        self.r, self.W = rank, world
+        self.G, self.Hg, self.Gq = head_groups, H // head_groups, Hq // H
+        self.C = N // world
+        self.NB = N // 128
+        self.blk_lo = rank * (self.C // 128)
+        self.blk_hi = self.blk_lo + self.C // 128
+        self.row0 = rank * self.C
+        self.dev = device
+        n_sm = torch.cuda.get_device_properties(device).multi_processor_count
+        self.max_ctas = max(1, n_sm - reserve_sms) if world > 1 else 0
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.Kf = torch.zeros(B, H, N, D, **bf)
+        self.Qf = torch.zeros(B, Hq, N, D, **bf)
+        self.khat = [torch.zeros(B, self.Hg, N, D, **bf) for _ in range(self.G)]
+        self.x = [torch.zeros(B, self.Hg, N, D, **bf) for _ in range(self.G)]
+        self.u = [torch.zeros(B, self.Hg, N, 128, **bf) for _ in range(self.G)]
+        f32 = dict(dtype=torch.float32, device=device)
+        self.rstd = [torch.zeros(B, self.Hg, N, **f32) for _ in range(self.G)]
+        self.dinv = [torch.zeros(B, self.Hg, N, **f32) for _ in range(self.G)]
+        self.lse = [torch.zeros(B, self.Hg * self.Gq, N, **f32) for _ in range(self.G)]
+        self.flags = [torch.zeros(B * self.Hg * self.NB, dtype=torch.int32, device=device) for _ in range(self.G)]
+        self.status = torch.zeros(64, dtype=torch.int32, device=device)
+        self.o = torch.empty(B, self.C, Hq, D, **bf)
+
+    # ---- helpers ----
+    def _st(self):
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def _rows(self, j):
+        return slice(j * self.C, (j + 1) * self.C)
+
+    def empty_chunk(self, heads):
+        return torch.empty(self.B, heads, self.C, self.D, dtype=torch.bfloat16, device=self.dev)
+
+    def _hs(self, g):
+        return slice(g * self.Hg, (g + 1) * self.Hg)
+
+    # ---- protocol steps ----
+    def set_local(self, q, k):
+        self.Kf[:, :, self._rows(self.r)] = k
+        self.Qf[:, :, self._rows(self.r)] = q
+
+    def own_keys(self):
+        return self.Kf[:, :, self._rows(self.r)].contiguous()
+
+    def store_keys(self, j, buf):
+        self.Kf[:, :, self._rows(j)] = buf
+
+    def prep(self):
+        lib, nb_own = self.lib, self.C // 128
+        for g in range(self.G):
+            kv = self.Kf[:, self._hs(g)]
+            args = (kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2), self.khat[g].data_ptr(),
+                    self.u[g].data_ptr(), self.rstd[g].data_ptr(), self.dinv[g].data_ptr(), self._st())
+            _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, 0, self.blk_lo, 1,
+                                         *args), "lucid_cp_prep")
+            _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, self.blk_lo,
+                                         self.blk_lo + nb_own, 0, *args), "lucid_cp_prep")
+
+    def store_values(self, g, j, buf):
+        self.x[g][:, :, self._rows(j)] = buf
+        nb = self.C // 128
+        _lib.check(self.lib.lucid_cp_publish(self.flags[g].data_ptr(), self.B * self.Hg, self.NB, j * nb,
+                                             (j + 1) * nb, self._st()), "lucid_cp_publish")
+
+    def solve(self, g, v):
+        vg = v[:, self._hs(g)]
+        if vg.stride(-1) != 1:
+            vg = vg.contiguous()
+        # the kernel indexes V by global row: shift the pointer back by this rank's first row
+        vptr = vg.data_ptr() - self.row0 * vg.stride(2) * vg.element_size()
+        _lib.check(self.lib.lucid_cp_solve_fwd(self.B, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi,
+                                               self.max_ctas,
+                                               vptr, vg.stride(0), vg.stride(1), vg.stride(2), self.x[g].data_ptr(),
+                                               self.khat[g].data_ptr(), self.u[g].data_ptr(),
+                                               self.dinv[g].data_ptr(), self.flags[g].data_ptr(),
+                                               self.status.data_ptr(), self._st()), "lucid_cp_solve_fwd")
+        self._vg = vg  # keep a contiguous copy alive until the kernel has run
+
+    def own_values(self, g):
+        return self.x[g][:, :, self._rows(self.r)].contiguous()
+
+    def attend(self, g):
+        hq = slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
+        qg, kg = self.Qf[:, hq], self.Kf[:, self._hs(g)]
+        og = self.o[:, :, hq].transpose(1, 2)   # [B, Hq_g, C, D] view of [B, C, Hq, D]
+        optr = og.data_ptr() - self.row0 * og.stride(2) * og.element_size()
+        _lib.check(self.lib.lucid_cp_attn_fwd(self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, self.blk_lo,
+                                              self.blk_hi, self.max_ctas, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
+                                              kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2),
+                                              self.x[g].data_ptr(), optr, og.stride(0), og.stride(1), og.stride(2),
+                                              self.lse[g].data_ptr(), self.status.data_ptr(), self._st()),
+                   "lucid_cp_attn_fwd")
+
+    def finish(self):
+        st = int(self.status[0].item())
+        if st != 0:
+            raise _lib.LucidError(f"context-parallel kernels reported status {st:#x} (a bounded wait timed out)")
+        return self.o
+
+
+def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_groups=4, reserve_sms=8):
+    """LUCID attention forward over a sequence split across the ranks of ``group``.
+
+    Each rank passes its own chunk: q [B, Hq, C, D], k, v [B, H, C, D] (bf16,
+    CUDA), the chunks of rank r being rows [r C, (r+1) C) of the sequence.
+    Returns this rank's rows of O as [B, C, Hq, D] (the layout of
+    eager_lucid_attention_forward, modeling_lucid.py:546)."""
+    W, r = dist.get_world_size(group), dist.get_rank(group)
+    B, Hq, C, D = q.shape
+    H = k.shape[1]
+    s = D ** -0.5 if scale is None else scale
+    be = KernelBackend(B, H, Hq, C * W, D, s, eps, r, W, head_groups, q.device, reserve_sms)
+    return ChunkProtocol(be, group).run(q, k, v)

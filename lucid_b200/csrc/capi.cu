@@ -331,6 +331,109 @@ void* noalloc_scratch_ptr() {
 }
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// context-parallel building blocks
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void fill_flags_kernel(int* flags, int NB, int lo, int hi) {
+  const int bh = blockIdx.x;
+  for (int b = lo + threadIdx.x; b < hi; b += blockDim.x) flags[(long long)bh * NB + b] = 1;
+}
+}  // namespace
+
+extern "C" int lucid_cp_publish(int* flags, int BH, int NB, int blk_lo, int blk_hi, void* stream) {
+  if (BH < 0 || NB < 0 || blk_lo < 0 || blk_hi > NB || blk_lo > blk_hi) return LUCID_ERR_SHAPE;
+  if (BH == 0 || blk_lo == blk_hi) return LUCID_OK;
+  fill_flags_kernel<<<BH, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, NB, blk_lo, blk_hi);
+  return to_status(cudaGetLastError());
+}
+
+extern "C" int lucid_cp_prep(int B, int H, int N, int D, float scale, float eps, int blk_lo, int blk_hi,
+                             int khat_only, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, void* khat,
+                             void* u, float* rstd, float* dinv, void* stream) {
+  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
+  const int NB = nb_of(N);
+  if (blk_lo < 0 || blk_hi > NB || blk_lo > blk_hi) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N) || blk_lo == blk_hi) return LUCID_OK;
+  if (!aligned16(k) || !aligned16(khat) || !aligned16(u) || !aligned16(rstd) || !aligned16(dinv) ||
+      !strides_ok(k_sb, k_sh, k_sn))
+    return LUCID_ERR_ALIGN;
+  PrepArgs pa{};
+  pa.B = B; pa.H = H; pa.N = N; pa.NB = NB; pa.Npad = npad_of(N);
+  pa.s = scale; pa.eps = eps;
+  pa.k = static_cast<const bf16*>(k); pa.k_sb = k_sb; pa.k_sh = k_sh; pa.k_sn = k_sn;
+  pa.khat = static_cast<bf16*>(khat); pa.rstd = rstd; pa.dinv = dinv; pa.u = static_cast<bf16*>(u);
+  pa.blk0 = blk_lo; pa.blk1 = blk_hi; pa.khat_only = khat_only;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ProfileScope ps(LUCID_KERNEL_PREP, st);
+  return to_status(launch_prep(pa, st));
+}
+
+// Row blocks [blk_lo, blk_hi) with blk_lo even and blk_hi even or NB: whole pairs.
+bool cp_range_ok(int N, int blk_lo, int blk_hi) {
+  const int NB = nb_of(N);
+  return blk_lo >= 0 && !(blk_lo & 1) && blk_hi <= NB && blk_lo < blk_hi && (!(blk_hi & 1) || blk_hi == NB);
+}
+
+extern "C" int lucid_cp_solve_fwd(int B, int H, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
+                                  const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn, void* x,
+                                  const void* khat, const void* u, const float* dinv, int* flags, int* status,
+                                  void* stream) {
+  if (!shape_ok(B, H, H, N, D) || !cp_range_ok(N, blk_lo, blk_hi)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  if (!aligned16(x) || !aligned16(khat) || !aligned16(u) || !aligned16(dinv) || !strides_ok(v_sb, v_sh, v_sn) ||
+      flags == nullptr || status == nullptr)
+    return LUCID_ERR_ALIGN;
+  const int NB = nb_of(N), Npad = npad_of(N);
+  CUtensorMap tK, tX, tU;
+  if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
+      !tmap_internal(&tU, u, B, H, Npad))
+    return LUCID_ERR_TENSORMAP;
+  FwdArgs fa{};
+  fa.B = B; fa.Hq = H; fa.Hkv = H; fa.N = N; fa.NB = NB; fa.Npad = Npad;
+  fa.scale = scale;
+  fa.dinv = dinv;
+  fa.v = static_cast<const bf16*>(v); fa.v_sb = v_sb; fa.v_sh = v_sh; fa.v_sn = v_sn;
+  fa.x = static_cast<bf16*>(x);
+  fa.flags = flags;
+  fa.status = status;
+  fa.pp0 = blk_lo / 2;
+  fa.pp1 = (blk_hi + 1) / 2;
+  fa.max_ctas = max_ctas;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
+  return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
+}
+
+extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi,
+                                 int max_ctas,
+                                 const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn, const void* k,
+                                 int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x, void* o, int64_t o_sb,
+                                 int64_t o_sh, int64_t o_sn, float* lse, int* status, void* stream) {
+  if (!shape_ok(B, Hq, Hkv, N, D) || !cp_range_ok(N, blk_lo, blk_hi)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(lse) || !strides_ok(q_sb, q_sh, q_sn) ||
+      !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn) || status == nullptr)
+    return LUCID_ERR_ALIGN;
+  const int NB = nb_of(N), Npad = npad_of(N);
+  CUtensorMap tQ, tK, tX;
+  if (!tmap_strided(&tQ, q, B, Hq, N, q_sb, q_sh, q_sn) || !tmap_strided(&tK, k, B, Hkv, N, k_sb, k_sh, k_sn) ||
+      !tmap_internal(&tX, x, B, Hkv, Npad))
+    return LUCID_ERR_TENSORMAP;
+  FwdArgs fa{};
+  fa.B = B; fa.Hq = Hq; fa.Hkv = Hkv; fa.N = N; fa.NB = NB; fa.Npad = Npad;
+  fa.scale = scale;
+  fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
+  fa.lse = lse;
+  fa.status = status;
+  fa.pp0 = blk_lo / 2;
+  fa.pp1 = (blk_hi + 1) / 2;
+  fa.max_ctas = max_ctas;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
+  return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
+}
+
 extern "C" int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps, const void* k,
                                        int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb,
                                        int64_t v_sh, int64_t v_sn, void* x, void* khat, void* u, float* rstd,

@@ -21,6 +21,9 @@ struct PrepArgs {
   float* rstd;               // [B*H][Npad]
   float* dinv;               // [B*H][Npad]        1 / P_rr
   bf16* u;                   // [B*H][NB][128][128] (I + L~)^-1 - I per diagonal block
+  // block range [blk0, blk1) (blk1 == 0: NB); khat_only: row statistics and k^ only
+  // (blocks whose solve runs elsewhere, e.g. another rank's chunk of the sequence)
+  int blk0 = 0, blk1 = 0, khat_only = 0;
 };
 
 // Forward tile engine (solve or attention).
@@ -38,6 +41,10 @@ struct FwdArgs {
   long long o_sb, o_sh, o_sn;
   float* lse;                // [B*Hq][Npad], log2 domain
   int* status;
+  // row-block pairs [pp0, pp1) processed (pp1 == 0: all; earlier blocks are solved
+  // elsewhere and their flags already set) and an optional cap on the persistent
+  // grid (0: #SMs)
+  int pp0 = 0, pp1 = 0, max_ctas = 0;
 };
 
 // Backward tile engines (column pass and row pass; attention or solve).

@@ -113,19 +113,20 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   const int BHk = p.B * p.Hkv, BHq = p.B * p.Hq;
   const int G = p.Hq / p.Hkv;
   const int NP = (p.NB + 1) / 2;
-  const int total = SOLVE ? NP * BHk : NP * BHq;
+  const int NPe = p.pp1 > 0 ? p.pp1 : NP;  // one past the last pair processed
+  const int total = SOLVE ? (NPe - p.pp0) * BHk : (NPe - p.pp0) * BHq;
 
   // Work item -> (pair pp, batch b, A-operand head ha, kv head hk).
   // Solve: increasing pair index (wavefront).  Attention: longest pairs first.
   auto decode = [&](int idx, int& pp, int& b, int& ha, int& hk) {
     if (SOLVE) {
-      pp = idx / BHk;
+      pp = p.pp0 + idx / BHk;
       const int bh = idx % BHk;
       b = bh / p.Hkv;
       hk = bh % p.Hkv;
       ha = hk;
     } else {
-      pp = NP - 1 - idx / BHq;
+      pp = NPe - 1 - idx / BHq;
       const int bh = idx % BHq;
       b = bh / p.Hq;
       ha = bh % p.Hq;
@@ -503,10 +504,10 @@ static int num_sms() {
 
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st) {
-  const int pairs = (a.NB + 1) / 2;
+  const int pairs = (a.pp1 > 0 ? a.pp1 : (a.NB + 1) / 2) - a.pp0;
   const int total = solve ? pairs * a.B * a.Hkv : pairs * a.B * a.Hq;
-  if (total == 0) return cudaSuccess;
-  const int grid = std::min(total, num_sms());
+  if (total <= 0) return cudaSuccess;
+  const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, num_sms()) : num_sms());
   cudaError_t e;
   if (solve) {
     e = cudaFuncSetAttribute(lucid_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

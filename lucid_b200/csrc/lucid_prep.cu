@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(256) lucid_prep_kernel(PrepArgs p) {
   float* dd = lt + 128 * kLD;     // [128] d_r
   float* tt = dd + 128;           // [8][16][16] temporaries
 
-  const int ib = blockIdx.x;
+  const int ib = p.blk0 + blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(256) lucid_prep_kernel(PrepArgs p) {
     }
   }
   __syncthreads();
+  if (p.khat_only) return;
 
   // ---- 2. L~ = D^-1 strictly-lower(exp(s k^ k^T - 1/s)) ------------------
   {
@@ -169,7 +170,9 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(lucid_prep_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(a.NB, a.B * a.H);
+  const int blk1 = a.blk1 > 0 ? a.blk1 : a.NB;
+  if (blk1 <= a.blk0 || a.B * a.H == 0) return cudaSuccess;
+  dim3 grid(blk1 - a.blk0, a.B * a.H);
   lucid_prep_kernel<<<grid, 256, smem, st>>>(a);
   return cudaGetLastError();
 }

@@ -1,0 +1,90 @@
+"""The context-parallel chunk protocol (lucid_b200/cp.py) on CPU gloo ranks.
+
+Each rank runs ChunkProtocol with the float64 CPU backend; the gathered
+outputs must equal the single-process oracle on the whole sequence.  Failure
+handling: a rank that dies before sending makes its successor's receive fail
+with an error instead of hanging."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+SEQ = dict(B=1, Hq=4, H=2, N=384, D=16)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(5)
+    B, Hq, H, N, D = (SEQ[k] for k in ("B", "Hq", "H", "N", "D"))
+    q = torch.randn(B, Hq, N, D, generator=g, dtype=torch.float64)
+    k = 0.6 * torch.randn(B, H, 1, D, generator=g, dtype=torch.float64) + 0.8 * torch.randn(B, H, N, D, generator=g,
+                                                                                            dtype=torch.float64)
+    v = torch.randn(B, H, N, D, generator=g, dtype=torch.float64)
+    return q, k, v
+
+
+def _worker(rank, world, port, groups, mode, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from datetime import timedelta
+    from cp_cpu_backend import CpuBackend
+    from lucid_b200.cp import ChunkProtocol
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    q, k, v = _inputs()
+    C = SEQ["N"] // world
+    rows = slice(rank * C, (rank + 1) * C)
+    be = CpuBackend(SEQ["B"], SEQ["H"], SEQ["Hq"], SEQ["N"], SEQ["D"], SEQ["D"] ** -0.5, 1e-5, rank, world, groups)
+    try:
+        if mode == "die" and rank == 0:
+            os._exit(0)   # leaves without sending anything
+        o = ChunkProtocol(be).run(q[:, :, rows], k[:, :, rows], v[:, :, rows])
+        np.save(os.path.join(out_dir, f"o{rank}.npy"), o.numpy())
+    except Exception as e:  # noqa: BLE001 - the failure test inspects it
+        with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as f:
+            f.write(repr(e))
+    finally:
+        if not (mode == "die"):
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,groups", [(2, 1), (3, 2)])
+def test_cp_protocol_matches_oracle(tmp_path, world, groups):
+    from oracle.lucid_oracle import lucid_fwd
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, groups, "ok", str(tmp_path)), nprocs=world, start_method="spawn")
+    for r in range(world):
+        assert not (tmp_path / f"err{r}.txt").exists(), (tmp_path / f"err{r}.txt").read_text()
+    o = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=1)
+    q, k, v = _inputs()
+    ref = lucid_fwd(q.numpy(), k.numpy(), v.numpy(), SEQ["D"] ** -0.5, 1e-5)[0]
+    np.testing.assert_allclose(o, ref, rtol=1e-10, atol=1e-10)
+
+
+def test_cp_protocol_reports_a_dead_peer(tmp_path):
+    port = _free_port()
+    ctx = mp.start_processes(_worker, args=(2, port, 1, "die", str(tmp_path)), nprocs=2, start_method="spawn",
+                             join=False)
+    # rank 0 exits at once; rank 1's receive must end with an error (the process
+    # group timeout is 10 s), not hang
+    import time
+    deadline = time.time() + 120
+    while any(p.is_alive() for p in ctx.processes) and time.time() < deadline:
+        time.sleep(0.5)
+    hung = [p for p in ctx.processes if p.is_alive()]
+    for p in hung:
+        p.kill()
+    assert not hung, "a rank hung after its peer died"
+    assert (tmp_path / "err1.txt").exists()
