@@ -165,6 +165,8 @@ def reference_arm(args):
         return 0
     if args.config == "path":
         return path_reference_arm(args)
+    if args.config == "cp128k":
+        return cp_reference_arm(args)
     B, H, N, D, _ = CONFIGS[args.config]
     n_cpu = args.cpu_n
     cpu_reference_sample(1024, D)
@@ -392,6 +394,118 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
 
 
 # ---------------------------------------------------------------------------
+# context-parallel forward at 128K
+# ---------------------------------------------------------------------------
+CP_METRIC = "LUCID attention forward TFLOP/s, context-parallel, B1 H32 N131072 D128 (config 5)"
+
+
+def cp_cpu_sample(N: int, seed: int = 0):
+    """Seconds for one (batch, head) of the LUCID attention FORWARD at length N on
+    the host (oracle/torch_ref.py, fp32, correlated keys of config 5)."""
+    import torch
+
+    from oracle import torch_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    D = 128
+    q = torch.randn(1, 1, N, D, generator=g)
+    k = 0.6 * torch.randn(1, 1, 1, D, generator=g) + 0.8 * torch.randn(1, 1, N, D, generator=g)
+    v = torch.randn(1, 1, N, D, generator=g)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        torch_ref.lucid_layer(q, k, v)
+    return time.perf_counter() - t0
+
+
+def cp_reference_arm(args):
+    n_cpu = min(args.cpu_n, 8192)
+    cp_cpu_sample(1024)
+    for _ in range(args.warmup):
+        cp_cpu_sample(n_cpu)
+    times = [cp_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
+    t = sum(times) / len(times)
+    val = 4.0 * n_cpu * n_cpu * 128 / t / 1e12
+    line = {
+        "impl": "reference", "metric": CP_METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"LUCID attention forward B1 H32 N131072 D128 (sampled: 1 head at N={n_cpu})",
+                   "global_batch": 1, "seq_len": 131072, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"1 (batch, head) at N={n_cpu}, fp32 forward, oracle/torch_ref.py"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
+    from lucid_b200.cp import cp_lucid_attention_forward
+    B, H, N, D = 1, 32, 131072, 128
+    C = N // world
+    s = D ** -0.5
+    # K = 0.6 s + 0.8 n with s shared per head (the same on every rank) and n per token
+    gs = torch.Generator(device=dev).manual_seed(5000)
+    shared = torch.randn(B, H, 1, D, generator=gs, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5001 + rank)
+    q = torch.randn(B, H, C, D, generator=g, device=dev).bfloat16()
+    k = (0.6 * shared + 0.8 * torch.randn(B, H, C, D, generator=g, device=dev)).bfloat16()
+    v = torch.randn(B, H, C, D, generator=g, device=dev).bfloat16()
+
+    def step():
+        return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        o = step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    finite = bool(torch.isfinite(o).all().item())
+    fl = 4.0 * N * N * D * B * H   # solve 2 N^2 D + attention 2 N^2 D per (batch, head)
+    tflops = fl / (ms * 1e-3) / 1e12
+    pk_burst, pk_sust, hbm, pk_kind = peaks()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    G = args.head_groups
+    line = {
+        "metric": CP_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"LUCID attention FORWARD B{B} H{H} N{N} D{D}, keys 0.6 s + 0.8 n, sequence split in "
+                               f"{world} contiguous chunks of {C} (one per rank), {G} head groups pipelined",
+                   "global_batch": B, "seq_len": N, "parallelism": f"context parallel x{world} (NCCL send/recv)",
+                   "scope": "forward only: the backward of the context-parallel chain is not built",
+                   "l2": "inputs larger than L2, no flush"},
+        "tokens_per_s": B * N / (ms * 1e-3),
+        "frac_of_bf16_peak": tflops / (pk_sust * world),
+        "output_finite": finite,
+        "clocks": clk,
+        "gpu_launches": (4 * G + G * max(0, world - 1)) * args.steps,
+        "e2e": None, "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def main(argv=None):
@@ -400,7 +514,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path"], default="32k")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k"], default="32k")
+    ap.add_argument("--head-groups", type=int, default=4, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -428,6 +543,8 @@ def main(argv=None):
 
     if args.config == "path":
         return bench_path(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "cp128k":
+        return bench_cp(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
     B, H, N, D, qs = CONFIGS[args.config]
     s = D ** -0.5
