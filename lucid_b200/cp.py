@@ -45,8 +45,9 @@ class ChunkProtocol:
     def __init__(self, backend, group=None):
         self.be = backend
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        # a single process without a process group is a world of one
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
 
     def _peer(self, r):
         return dist.get_global_rank(self.group, r) if self.group is not None else r
@@ -206,7 +207,8 @@ def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_g
     CUDA), the chunks of rank r being rows [r C, (r+1) C) of the sequence.
     Returns this rank's rows of O as [B, C, Hq, D] (the layout of
     eager_lucid_attention_forward, modeling_lucid.py:546)."""
-    W, r = dist.get_world_size(group), dist.get_rank(group)
+    W = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
     B, Hq, C, D = q.shape
     H = k.shape[1]
     s = D ** -0.5 if scale is None else scale
