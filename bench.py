@@ -440,9 +440,10 @@ def cp_reference_arm(args):
 
 
 def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
-    from lucid_b200.cp import cp_lucid_attention_forward
+    from lucid_b200.cp import balanced_bounds, cp_lucid_attention_forward
     B, H, N, D = 1, 32, 131072, 128
-    C = N // world
+    bounds = balanced_bounds(N, world)
+    C = bounds[rank + 1] - bounds[rank]
     s = D ** -0.5
     # K = 0.6 s + 0.8 n with s shared per head (the same on every rank) and n per token
     gs = torch.Generator(device=dev).manual_seed(5000)
@@ -453,7 +454,7 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
     v = torch.randn(B, H, C, D, generator=g, device=dev).bfloat16()
 
     def step():
-        return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups)
+        return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
 
     for _ in range(args.warmup):
         step()
@@ -490,7 +491,8 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"LUCID attention FORWARD B{B} H{H} N{N} D{D}, keys 0.6 s + 0.8 n, sequence split in "
-                               f"{world} contiguous chunks of {C} (one per rank), {G} head groups pipelined",
+                               f"{world} contiguous chunks of equal causal work (bounds {bounds}), {G} head "
+                               f"groups pipelined",
                    "global_batch": B, "seq_len": N, "parallelism": f"context parallel x{world} (NCCL send/recv)",
                    "scope": "forward only: the backward of the context-parallel chain is not built",
                    "l2": "inputs larger than L2, no flush"},
@@ -515,7 +517,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k"], default="32k")
-    ap.add_argument("--head-groups", type=int, default=4, help="cp128k: kv-head groups pipelined across ranks")
+    ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

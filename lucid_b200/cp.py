@@ -25,6 +25,10 @@ Protocol (all point-to-point NCCL send/recv, no collective):
   NCCL receive, and the persistent kernels leave `reserve_sms` SMs free so
   the NCCL kernels of the other groups run alongside.
 
+Chunks may differ in length (balanced_bounds equalises the causal work:
+the solve and the attention of row t cost ~t, so equal chunks leave the
+last rank (2W-1)/W^2 of the work).
+
 Forward only: the backward of the context-parallel chain is not built (the
 single-GPU op `lucid_attention` has the full backward).
 """
@@ -35,7 +39,23 @@ import torch.distributed as dist
 
 from . import _lib
 
-__all__ = ["cp_lucid_attention_forward", "ChunkProtocol", "KernelBackend"]
+__all__ = ["cp_lucid_attention_forward", "ChunkProtocol", "KernelBackend", "balanced_bounds", "even_bounds"]
+
+
+def even_bounds(N: int, world: int):
+    """Chunk boundaries of equal contiguous chunks."""
+    return [r * (N // world) for r in range(world)] + [N]
+
+
+def balanced_bounds(N: int, world: int, align: int = 256):
+    """Contiguous chunks of equal causal work: row r's solve and attention cost
+    grows with r, so the chunk of rank r ends near N sqrt((r+1)/world)
+    (rounded to `align` rows, 256 = one pair of 128-row blocks)."""
+    b = [0]
+    for r in range(1, world):
+        x = int(round(N * (r / world) ** 0.5 / align)) * align
+        b.append(min(max(x, b[-1] + align), N - (world - r) * align))
+    return b + [N]
 
 
 class ChunkProtocol:
@@ -58,7 +78,7 @@ class ChunkProtocol:
         # 1. raw keys flow to every later rank
         reqs, kbuf = [], {}
         for j in range(r):
-            kbuf[j] = be.empty_chunk(heads=be.H)
+            kbuf[j] = be.empty_chunk(be.H, j)
             reqs.append(dist.irecv(kbuf[j], src=self._peer(j), group=self.group))
         ksend = be.own_keys()
         sends = [dist.isend(ksend, dst=self._peer(j), group=self.group) for j in range(r + 1, W)]
@@ -71,7 +91,7 @@ class ChunkProtocol:
         xbuf, xreq = {}, {}
         for g in range(be.G):
             for j in range(r):
-                xbuf[g, j] = be.empty_chunk(heads=be.Hg)
+                xbuf[g, j] = be.empty_chunk(be.Hg, j)
                 xreq[g, j] = dist.irecv(xbuf[g, j], src=self._peer(j), group=self.group)
         for g in range(be.G):
             for j in range(r):
@@ -89,11 +109,13 @@ class ChunkProtocol:
 class KernelBackend:
     """The chunk computations on the B200 kernels (C ABI lucid_cp_*)."""
 
-    def __init__(self, B, H, Hq, N, D, scale, eps, rank, world, head_groups, device, reserve_sms=8):
+    def __init__(self, B, H, Hq, bounds, D, scale, eps, rank, world, head_groups, device, reserve_sms=8):
         if D != 128:
             raise NotImplementedError("head_dim must be 128")
-        if N % world or (N // world) % 256:
-            raise ValueError("the sequence must split into chunks of a multiple of 256 tokens per rank")
+        N = bounds[-1]
+        if len(bounds) != world + 1 or bounds[0] != 0 or any(x % 256 for x in bounds[:-1]) or \
+                any(bounds[j + 1] <= bounds[j] for j in range(world)) or N % 128:
+            raise ValueError("chunk bounds must start at 0, increase, and sit on multiples of 256 rows")
         if H % head_groups or Hq % H:
             raise ValueError("head_groups must divide the kv heads and Hq must be a multiple of H")
         self.lib = _lib.load()
@@ -101,11 +123,12 @@ class KernelBackend:
         self.s, self.eps = float(scale), float(eps)
         self.r, self.W = rank, world
         self.G, self.Hg, self.Gq = head_groups, H // head_groups, Hq // H
-        self.C = N // world
+        self.bounds = list(bounds)
+        self.C = bounds[rank + 1] - bounds[rank]
         self.NB = N // 128
-        self.blk_lo = rank * (self.C // 128)
-        self.blk_hi = self.blk_lo + self.C // 128
-        self.row0 = rank * self.C
+        self.blk_lo = bounds[rank] // 128
+        self.blk_hi = bounds[rank + 1] // 128
+        self.row0 = bounds[rank]
         self.dev = device
         n_sm = torch.cuda.get_device_properties(device).multi_processor_count
         self.max_ctas = max(1, n_sm - reserve_sms) if world > 1 else 0
@@ -128,10 +151,11 @@ class KernelBackend:
         return torch.cuda.current_stream(self.dev).cuda_stream
 
     def _rows(self, j):
-        return slice(j * self.C, (j + 1) * self.C)
+        return slice(self.bounds[j], self.bounds[j + 1])
 
-    def empty_chunk(self, heads):
-        return torch.empty(self.B, heads, self.C, self.D, dtype=torch.bfloat16, device=self.dev)
+    def empty_chunk(self, heads, j):
+        n = self.bounds[j + 1] - self.bounds[j]
+        return torch.empty(self.B, heads, n, self.D, dtype=torch.bfloat16, device=self.dev)
 
     def _hs(self, g):
         return slice(g * self.Hg, (g + 1) * self.Hg)
@@ -148,7 +172,7 @@ class KernelBackend:
         self.Kf[:, :, self._rows(j)] = buf
 
     def prep(self):
-        lib, nb_own = self.lib, self.C // 128
+        lib = self.lib
         for g in range(self.G):
             kv = self.Kf[:, self._hs(g)]
             args = (kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2), self.khat[g].data_ptr(),
@@ -156,13 +180,13 @@ class KernelBackend:
             _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, 0, self.blk_lo, 1,
                                          *args), "lucid_cp_prep")
             _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, self.blk_lo,
-                                         self.blk_lo + nb_own, 0, *args), "lucid_cp_prep")
+                                         self.blk_hi, 0, *args), "lucid_cp_prep")
 
     def store_values(self, g, j, buf):
         self.x[g][:, :, self._rows(j)] = buf
-        nb = self.C // 128
-        _lib.check(self.lib.lucid_cp_publish(self.flags[g].data_ptr(), self.B * self.Hg, self.NB, j * nb,
-                                             (j + 1) * nb, self._st()), "lucid_cp_publish")
+        _lib.check(self.lib.lucid_cp_publish(self.flags[g].data_ptr(), self.B * self.Hg, self.NB,
+                                             self.bounds[j] // 128, self.bounds[j + 1] // 128, self._st()),
+                   "lucid_cp_publish")
 
     def solve(self, g, v):
         vg = v[:, self._hs(g)]
@@ -200,17 +224,23 @@ class KernelBackend:
         return self.o
 
 
-def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_groups=4, reserve_sms=8):
+def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8,
+                               bounds=None):
     """LUCID attention forward over a sequence split across the ranks of ``group``.
 
-    Each rank passes its own chunk: q [B, Hq, C, D], k, v [B, H, C, D] (bf16,
-    CUDA), the chunks of rank r being rows [r C, (r+1) C) of the sequence.
-    Returns this rank's rows of O as [B, C, Hq, D] (the layout of
+    Each rank passes its own chunk: q [B, Hq, C_r, D], k, v [B, H, C_r, D] (bf16,
+    CUDA), rank r holding rows [bounds[r], bounds[r+1]) of the sequence
+    (``bounds`` as from balanced_bounds / even_bounds; None: equal chunks).
+    Returns this rank's rows of O as [B, C_r, Hq, D] (the layout of
     eager_lucid_attention_forward, modeling_lucid.py:546)."""
     W = dist.get_world_size(group) if dist.is_initialized() else 1
     r = dist.get_rank(group) if dist.is_initialized() else 0
     B, Hq, C, D = q.shape
     H = k.shape[1]
     s = D ** -0.5 if scale is None else scale
-    be = KernelBackend(B, H, Hq, C * W, D, s, eps, r, W, head_groups, q.device, reserve_sms)
+    if bounds is None:
+        bounds = even_bounds(C * W, W)
+    if bounds[r + 1] - bounds[r] != C:
+        raise ValueError(f"rank {r} passed {C} rows but owns [{bounds[r]}, {bounds[r + 1]})")
+    be = KernelBackend(B, H, Hq, bounds, D, s, eps, r, W, head_groups, q.device, reserve_sms)
     return ChunkProtocol(be, group).run(q, k, v)

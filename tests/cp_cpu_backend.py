@@ -8,12 +8,14 @@ import torch
 
 
 class CpuBackend:
-    def __init__(self, B, H, Hq, N, D, scale, eps, rank, world, head_groups):
+    def __init__(self, B, H, Hq, bounds, D, scale, eps, rank, world, head_groups):
+        N = bounds[-1]
         self.B, self.H, self.Hq, self.N, self.D = B, H, Hq, N, D
         self.s, self.eps = scale, eps
         self.r, self.W = rank, world
         self.G, self.Hg, self.Gq = head_groups, H // head_groups, Hq // H
-        self.C = N // world
+        self.bounds = bounds
+        self.C = bounds[rank + 1] - bounds[rank]
         f = dict(dtype=torch.float64)
         self.Kf = torch.zeros(B, H, N, D, **f)
         self.Qf = torch.zeros(B, Hq, N, D, **f)
@@ -22,13 +24,13 @@ class CpuBackend:
         self.o = torch.zeros(B, self.C, Hq, D, **f)
 
     def _rows(self, j):
-        return slice(j * self.C, (j + 1) * self.C)
+        return slice(self.bounds[j], self.bounds[j + 1])
 
     def _hs(self, g):
         return slice(g * self.Hg, (g + 1) * self.Hg)
 
-    def empty_chunk(self, heads):
-        return torch.empty(self.B, heads, self.C, self.D, dtype=torch.float64)
+    def empty_chunk(self, heads, j):
+        return torch.empty(self.B, heads, self.bounds[j + 1] - self.bounds[j], self.D, dtype=torch.float64)
 
     def set_local(self, q, k):
         self.Kf[:, :, self._rows(self.r)] = k
@@ -41,7 +43,7 @@ class CpuBackend:
         self.Kf[:, :, self._rows(j)] = buf
 
     def prep(self):
-        k = self.Kf[:, :, : (self.r + 1) * self.C]
+        k = self.Kf[:, :, : self.bounds[self.r + 1]]
         self.khat = k / torch.sqrt((k * k).mean(-1, keepdim=True) + self.eps)
 
     def store_values(self, g, j, buf):
@@ -50,7 +52,7 @@ class CpuBackend:
 
     def solve(self, g, v):
         assert self.solved[g] == set(range(self.r)), "solve before every earlier chunk arrived"
-        c0, c1 = self.r * self.C, (self.r + 1) * self.C
+        c0, c1 = self.bounds[self.r], self.bounds[self.r + 1]
         kh = self.khat[:, self._hs(g)]
         R = v[:, self._hs(g)].clone()
         if c0 > 0:
@@ -63,7 +65,7 @@ class CpuBackend:
         return self.x[g][:, :, self._rows(self.r)].contiguous()
 
     def attend(self, g):
-        c0, c1 = self.r * self.C, (self.r + 1) * self.C
+        c0, c1 = self.bounds[self.r], self.bounds[self.r + 1]
         hq = slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
         q = self.Qf[:, hq, c0:c1]
         k = self.Kf[:, self._hs(g), :c1].repeat_interleave(self.Gq, dim=1)

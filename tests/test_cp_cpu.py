@@ -34,6 +34,12 @@ def _inputs():
     return q, k, v
 
 
+def _bounds(world, mode):
+    from lucid_b200.cp import balanced_bounds, even_bounds
+    N = SEQ["N"]
+    return balanced_bounds(N, world, align=64) if mode == "balanced" else even_bounds(N, world)
+
+
 def _worker(rank, world, port, groups, mode, out_dir):
     import sys
     sys.path.insert(0, ROOT)
@@ -44,9 +50,9 @@ def _worker(rank, world, port, groups, mode, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
     q, k, v = _inputs()
-    C = SEQ["N"] // world
-    rows = slice(rank * C, (rank + 1) * C)
-    be = CpuBackend(SEQ["B"], SEQ["H"], SEQ["Hq"], SEQ["N"], SEQ["D"], SEQ["D"] ** -0.5, 1e-5, rank, world, groups)
+    bounds = _bounds(world, mode)
+    rows = slice(bounds[rank], bounds[rank + 1])
+    be = CpuBackend(SEQ["B"], SEQ["H"], SEQ["Hq"], bounds, SEQ["D"], SEQ["D"] ** -0.5, 1e-5, rank, world, groups)
     try:
         if mode == "die" and rank == 0:
             os._exit(0)   # leaves without sending anything
@@ -56,15 +62,15 @@ def _worker(rank, world, port, groups, mode, out_dir):
         with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as f:
             f.write(repr(e))
     finally:
-        if not (mode == "die"):
+        if mode != "die":
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,groups", [(2, 1), (3, 2)])
-def test_cp_protocol_matches_oracle(tmp_path, world, groups):
+@pytest.mark.parametrize("world,groups,mode", [(2, 1, "even"), (3, 2, "even"), (3, 2, "balanced")])
+def test_cp_protocol_matches_oracle(tmp_path, world, groups, mode):
     from oracle.lucid_oracle import lucid_fwd
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, groups, "ok", str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, port, groups, mode, str(tmp_path)), nprocs=world, start_method="spawn")
     for r in range(world):
         assert not (tmp_path / f"err{r}.txt").exists(), (tmp_path / f"err{r}.txt").read_text()
     o = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=1)
@@ -88,3 +94,12 @@ def test_cp_protocol_reports_a_dead_peer(tmp_path):
         p.kill()
     assert not hung, "a rank hung after its peer died"
     assert (tmp_path / "err1.txt").exists()
+
+
+def test_balanced_bounds_equalise_causal_work():
+    from lucid_b200.cp import balanced_bounds
+    N, W = 131072, 8
+    b = balanced_bounds(N, W)
+    assert b[0] == 0 and b[-1] == N and all(x % 256 == 0 for x in b)
+    work = [(b[r + 1] ** 2 - b[r] ** 2) / N ** 2 for r in range(W)]
+    assert max(work) < 1.02 / W
