@@ -537,7 +537,9 @@ def main(argv=None):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        # a short timeout ends a stuck collective with an error instead of holding all GPUs
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60 if args.config == "cp128k" else 300),
+                                device_id=dev)
 
     def barrier():
         if world > 1:

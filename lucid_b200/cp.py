@@ -58,9 +58,32 @@ def balanced_bounds(N: int, world: int, align: int = 256):
     return b + [N]
 
 
+_PAIR_GROUPS = {}
+
+
+def _pair_groups(group):
+    """One process group per pair of ranks (created once, by every rank in the
+    same order), so that point-to-point traffic between different pairs never
+    queues behind one another (a single communicator runs its send/recv ops
+    in issue order)."""
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+    key = tuple(ranks)
+    if key not in _PAIR_GROUPS:
+        _PAIR_GROUPS[key] = {(a, b): dist.new_group([ranks[a], ranks[b]])
+                             for a in range(len(ranks)) for b in range(a + 1, len(ranks))}
+    return _PAIR_GROUPS[key], ranks
+
+
 class ChunkProtocol:
     """The message schedule of the forward chain, independent of how the
-    chunks are computed (``backend``) and of the process group's device."""
+    chunks are computed (``backend``) and of the process group's device.
+
+    Every message flows from a lower to a higher rank, each pair of ranks has
+    its own communicator, and both ends of a pair exchange their messages in
+    the same order (keys, then the values of head group 0, 1, ...).  Rank r
+    posts the receives of group g only after its sends of group g-1, so even
+    if all of a rank's operations ran in issue order every wait would be on a
+    (group, rank) that comes earlier: the schedule cannot deadlock."""
 
     def __init__(self, backend, group=None):
         self.be = backend
@@ -68,38 +91,39 @@ class ChunkProtocol:
         # a single process without a process group is a world of one
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.pairs, self.ranks = _pair_groups(group) if self.world > 1 else ({}, [0])
 
-    def _peer(self, r):
-        return dist.get_global_rank(self.group, r) if self.group is not None else r
+    def _send(self, t, j):
+        lo, hi = min(self.rank, j), max(self.rank, j)
+        return dist.isend(t, dst=self.ranks[j], group=self.pairs[lo, hi])
+
+    def _recv(self, t, j):
+        lo, hi = min(self.rank, j), max(self.rank, j)
+        return dist.irecv(t, src=self.ranks[j], group=self.pairs[lo, hi])
 
     def run(self, q, k, v):
         be, r, W = self.be, self.rank, self.world
         be.set_local(q, k)
         # 1. raw keys flow to every later rank
-        reqs, kbuf = [], {}
-        for j in range(r):
-            kbuf[j] = be.empty_chunk(be.H, j)
-            reqs.append(dist.irecv(kbuf[j], src=self._peer(j), group=self.group))
+        kbuf = {j: be.empty_chunk(be.H, j) for j in range(r)}
+        reqs = [self._recv(kbuf[j], j) for j in range(r)]
         ksend = be.own_keys()
-        sends = [dist.isend(ksend, dst=self._peer(j), group=self.group) for j in range(r + 1, W)]
+        sends = [self._send(ksend, j) for j in range(r + 1, W)]
         for rq in reqs:
             rq.wait()
         for j in range(r):
             be.store_keys(j, kbuf[j])
         be.prep()
         # 2. solved values, pipelined over head groups
-        xbuf, xreq = {}, {}
         for g in range(be.G):
+            xbuf = {j: be.empty_chunk(be.Hg, j) for j in range(r)}
+            reqs = [self._recv(xbuf[j], j) for j in range(r)]
             for j in range(r):
-                xbuf[g, j] = be.empty_chunk(be.Hg, j)
-                xreq[g, j] = dist.irecv(xbuf[g, j], src=self._peer(j), group=self.group)
-        for g in range(be.G):
-            for j in range(r):
-                xreq[g, j].wait()
-                be.store_values(g, j, xbuf[g, j])
+                reqs[j].wait()
+                be.store_values(g, j, xbuf[j])
             be.solve(g, v)
             xs = be.own_values(g)
-            sends += [dist.isend(xs, dst=self._peer(j), group=self.group) for j in range(r + 1, W)]
+            sends += [self._send(xs, j) for j in range(r + 1, W)]
             be.attend(g)
         for s in sends:
             s.wait()

@@ -103,3 +103,79 @@ def test_balanced_bounds_equalise_causal_work():
     assert b[0] == 0 and b[-1] == N and all(x % 256 == 0 for x in b)
     work = [(b[r + 1] ** 2 - b[r] ** 2) / N ** 2 for r in range(W)]
     assert max(work) < 1.02 / W
+
+
+class _Req:
+    def wait(self):
+        pass
+
+
+class _NullBackend:
+    """Records nothing but shapes: lets ChunkProtocol run without data."""
+
+    def __init__(self, G):
+        self.G, self.H, self.Hg = G, 1, 1
+
+    def set_local(self, q, k):
+        pass
+
+    def empty_chunk(self, heads, j):
+        return None
+
+    def own_keys(self):
+        return None
+
+    def store_keys(self, j, buf):
+        pass
+
+    def prep(self):
+        pass
+
+    def store_values(self, g, j, buf):
+        pass
+
+    def solve(self, g, v):
+        pass
+
+    def own_values(self, g):
+        return None
+
+    def attend(self, g):
+        pass
+
+    def finish(self):
+        return None
+
+
+def _schedule(rank, world, G):
+    """The point-to-point operations rank `rank` issues, in issue order."""
+    from lucid_b200.cp import ChunkProtocol
+    ops = []
+    proto = ChunkProtocol.__new__(ChunkProtocol)
+    proto.be, proto.group, proto.rank, proto.world = _NullBackend(G), None, rank, world
+    proto._send = lambda t, j: (ops.append(("send", j)), _Req())[1]
+    proto._recv = lambda t, j: (ops.append(("recv", j)), _Req())[1]
+    proto.run(None, None, None)
+    return ops
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("G", [1, 2, 8])
+def test_cp_schedule_cannot_deadlock_even_fully_serialised(world, G):
+    """Worst case for NCCL point-to-point: every rank runs all of its sends and
+    receives strictly in issue order (one queue per rank, as a single eager
+    communicator does).  A send and a receive complete together when each is
+    at the head of its rank's queue; the whole schedule must drain."""
+    queues = [list(_schedule(r, world, G)) for r in range(world)]
+    progress = True
+    while progress and any(queues):
+        progress = False
+        for r in range(world):
+            if not queues[r]:
+                continue
+            op, j = queues[r][0]
+            if op == "send" and queues[j] and queues[j][0] == ("recv", r):
+                queues[r].pop(0)
+                queues[j].pop(0)
+                progress = True
+    assert not any(queues), f"deadlock: heads {[q[0] if q else None for q in queues]}"
