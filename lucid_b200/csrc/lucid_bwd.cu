@@ -139,9 +139,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int BHk = p.B * p.Hkv;
   const int G = p.Hq / p.Hkv;
   const int total = p.NB * BHk;
+  // transposed solve: blocks NB-1 .. 0 across heads (wavefront order);
+  // attention: head-major, longest columns first within a head, so the CTAs in
+  // flight share one or two heads whose Q / dO tiles stay resident in L2
   auto decode = [&](int idx, int& i, int& b, int& hk) {
-    i = SOLVE ? (p.NB - 1 - idx / BHk) : (idx / BHk);
-    const int bh = idx % BHk;
+    i = SOLVE ? (p.NB - 1 - idx / BHk) : (idx % p.NB);
+    const int bh = SOLVE ? idx % BHk : idx / p.NB;
     b = bh / p.Hkv;
     hk = bh % p.Hkv;
   };
@@ -593,13 +596,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // items: (row block j, head); longest rows first for balance
+  // items: (row block j, head)
   const int BH = SOLVE ? p.B * p.Hkv : p.B * p.Hq;
   const int G = p.Hq / p.Hkv;
   const int total = p.NB * BH;
   auto decode = [&](int idx, int& j, int& b, int& ha, int& hk) {
-    j = p.NB - 1 - idx / BH;
-    const int bh = idx % BH;
+    // head-major, longest rows first within a head (L2 residency of the head's tiles)
+    j = p.NB - 1 - idx % p.NB;
+    const int bh = idx / p.NB;
     if (SOLVE) {
       b = bh / p.Hkv;
       hk = bh % p.Hkv;

@@ -167,6 +167,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   const int total = (p.NB - 1) * BHQ;
   const long long Npad = (long long)p.NB * 128;
   auto decode = [&](int idx, int& i, int& bhq, int& b, int& h, int& bhk) {
+    // longest rows first across all heads (the chain is latency-bound: balance
+    // matters more here than L2 residency)
     i = p.NB - 1 - idx / BHQ;
     bhq = idx % BHQ;
     b = bhq / p.HQ;
@@ -579,8 +581,10 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   const int total = p.NB * BHQ;
   const long long Npad = (long long)p.NB * 128;
   auto decode = [&](int idx, int& i, int& bhq, int& b, int& h, int& bhk) {
-    i = p.NB - 1 - idx / BHQ;
-    bhq = idx % BHQ;
+    // head-major, longest rows first within a head (L2 residency of the head's
+    // O / K_new / W / W2 tiles across the CTAs in flight)
+    i = p.NB - 1 - idx % p.NB;
+    bhq = idx / p.NB;
     b = bhq / p.HQ;
     h = (bhq % p.HQ) / p.G;
     bhk = b * p.H + h;
@@ -804,7 +808,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   const int total = p.NB * BHQ;
   const long long Npad = (long long)p.NB * 128;
   auto decode = [&](int idx, int& j, int& bhq, int& b, int& h, int& bhk, int& steps) {
-    j = idx / BHQ;
+    j = idx / BHQ;            // longest columns first across all heads
     bhq = idx % BHQ;
     b = bhq / p.HQ;
     h = (bhq % p.HQ) / p.G;
@@ -1058,8 +1062,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   const int total = p.NB * BHQ;
   const long long Npad = (long long)p.NB * 128;
   auto decode = [&](int idx, int& i, int& bhq, int& b, int& hq, int& h, int& bhk) {
-    i = p.NB - 1 - idx / BHQ;
-    bhq = idx % BHQ;
+    i = p.NB - 1 - idx % p.NB;  // head-major, longest rows first within a head
+    bhq = idx / p.NB;
     b = bhq / p.HQ;
     hq = bhq % p.HQ;
     h = hq / p.G;
