@@ -321,8 +321,7 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
         try:
             with open(tpath) as f:
                 tj = json.load(f)
-            if tj.get("config") == "path":
-                roof["traffic"] = tj.get(dom)
+            roof["traffic"] = tj.get("path", {}).get(dom)
         except Exception:
             pass
 
@@ -633,8 +632,7 @@ def main(argv=None):
         try:
             with open(tpath) as f:
                 tj = json.load(f)
-            if tj.get("config") == args.config:
-                traffic = tj.get(dom)
+            traffic = tj.get(args.config, {}).get(dom)
         except Exception:
             traffic = None
 
