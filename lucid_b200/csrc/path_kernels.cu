@@ -110,12 +110,21 @@ struct TileRing {
 // ===========================================================================
 // path_scores_kernel
 // ===========================================================================
+// Warps 4-7 carry the query chain, the critical path of the kernel: they write
+// -S2 back into TMEM as the A operand of the chain GEMM, which accumulates
+// Q~ += (-S2) W2_j in TMEM, then turn Q~ into the bf16 hi / lo operand tiles
+// of the next step and store the snapshot.  Warps 0-3 turn each score tile
+// into L_ij (exp, bf16, to HBM) off the critical path.  Per step the MMA warp
+// issues the chain's S2 before the scores S.
 namespace psc {
 constexpr int kRing = 4;
 constexpr uint32_t kOffQ = 0, kOffQlo = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
-enum { RF0 = 0, RE0 = RF0 + kRing, QOP_FULL = RE0 + kRing, QFREE, QWRITTEN, SS_FULL, NS2_FULL, D_FULL, DRAIN, NBAR };
+enum { RF0 = 0, RE0 = RF0 + kRing, QOP_FULL = RE0 + kRing, QOP_FREE, QFREE, S_FULL, S_FREE, S2_FULL, NS2_FULL,
+       QD_FULL, DRAIN, NBAR };
 constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
-constexpr uint32_t kTmS = 0, kTmS2 = 128;
+constexpr uint32_t kTmS = 0, kTmS2 = 128, kTmQ = 256;
+constexpr int kHalf = 128;
+constexpr int kChainLead = 128;   // thread that stores the snapshots (first of warps 4-7)
 }  // namespace psc
 
 __global__ void __launch_bounds__(pk::kThreads, 1)
@@ -140,12 +149,14 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       mbar_init(bar(RF0 + s), 1);
       mbar_init(bar(RE0 + s), 1);
     }
-    mbar_init(bar(QOP_FULL), 1);
+    mbar_init(bar(QOP_FULL), kHalf);
+    mbar_init(bar(QOP_FREE), 1);
     mbar_init(bar(QFREE), 1);
-    mbar_init(bar(QWRITTEN), pk::kEpi);
-    mbar_init(bar(SS_FULL), 1);
-    mbar_init(bar(NS2_FULL), pk::kEpi);
-    mbar_init(bar(D_FULL), 1);
+    mbar_init(bar(S_FULL), 1);
+    mbar_init(bar(S_FREE), kHalf);
+    mbar_init(bar(S2_FULL), 1);
+    mbar_init(bar(NS2_FULL), kHalf);
+    mbar_init(bar(QD_FULL), 1);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -155,7 +166,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     tma_prefetch_desc(&tmQs);
   }
   if (warp == pk::kWarpMma) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -193,10 +204,11 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     }
   } else if (warp == pk::kWarpMma) {
     if (lane == 0) {
-      uint32_t rc = 0, n_q = 0, n_ns2 = 0;
+      uint32_t rc = 0, n_q = 0, n_ns2 = 0, n_sfree = 0;
       auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
       auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
       auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      const uint32_t tS = tmem + kTmS, tS2 = tmem + kTmS2;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         int i, bhq, b, h, bhk;
@@ -211,107 +223,159 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
             if (!ring_wait(sW)) { ok = false; break; }
           }
           tc_fence_after();
-          umma_tile(tmem + kTmS, sQ, false, ring_slot(sK), false, 0u);
-          umma_tile(tmem + kTmS, sQlo, false, ring_slot(sK), false, 1u);
-          if (j > 0) umma_tile(tmem + kTmS2, sQ, false, ring_slot(sW), false, 0u);
-          umma_commit(bar(SS_FULL));
+          if (j > 0) {  // chain first
+            umma_tile(tS2, sQ, false, ring_slot(sW), false, 0u);
+            umma_commit(bar(S2_FULL));
+          }
+          // the previous score tile has been read by warps 0-3
+          if (!mbar_wait(bar(S_FREE), ((n_sfree++) & 1) ^ 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          umma_tile(tS, sQ, false, ring_slot(sK), false, 0u);
+          umma_tile(tS, sQlo, false, ring_slot(sK), false, 1u);
+          umma_commit(bar(S_FULL));
           ring_free(sK);
-          if (j == 0) break;
+          if (j == 0) {
+            umma_commit(bar(QOP_FREE));  // the operand tiles may be rewritten for the next item
+            break;
+          }
           ring_free(sW);
           if (!mbar_wait(bar(NS2_FULL), (n_ns2++) & 1, ab)) { ok = false; break; }
           const uint32_t sW2 = rc++;
           if (!ring_wait(sW2)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t s2 = tmem + kTmS2;
-          umma_tile_ts(tmem + kTmS, [&](int kk) { return packed_half_kslice(s2, kk); }, ring_slot(sW2), true, 0u);
-          umma_commit(bar(D_FULL));
+          // -S2 was packed by full rows: K-slice kk at column 8 kk; Q~ accumulates in TMEM
+          umma_tile_ts(tmem + kTmQ, [&](int kk) { return tS2 + 8u * (uint32_t)kk; }, ring_slot(sW2), true, 1u);
+          umma_commit(bar(QD_FULL));
           ring_free(sW2);
         }
       }
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
-  } else {
-    const int qd = warp & 3, hf = warp >> 2;
-    const int r = qd * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    const uint32_t tS = tmem + lane_base + kTmS + 64u * hf;
-    const uint32_t tS2 = tmem + lane_base + kTmS2 + 64u * hf;
+  } else if (warp < 4) {
+    // ---------------- score tiles -> L_ij ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16) + kTmS;
     const float c1 = p.s * 1.4426950408889634f, c2 = 1.4426950408889634f / p.s;
-    uint32_t n_ss = 0, n_d = 0, n_qf = 0, n_qw = 0;
-    // Publish the bf16 copy of Q~ as the next MMA operand and as snapshot `pair`.
-    auto write_qop = [&](const float (&q)[64], long long pair, int bhq) -> bool {
-      if (threadIdx.x == 0) {
+    uint32_t n_s = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+      int i, bhq, b, h, bhk;
+      decode(idx, i, bhq, b, h, bhk);
+      for (int j = i - 1; j >= 0; --j) {
+        if (!pwarp_wait(bar(S_FULL), (n_s++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        bf16* dst = p.L + (((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128;
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS + 32u * c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 a = fma2(make_float2(v[e], v[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+            v[e] = fast_exp2(a.x);
+            v[e + 1] = fast_exp2(a.y);
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) st_bf16x8(dst + c * 32 + e * 8, v + e * 8);
+        }
+        tc_fence_before();
+        mbar_arrive(bar(S_FREE));
+      }
+    }
+  } else {
+    // ---------------- query chain ----------------
+    const int wq = warp - 4;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS2 = tmem + lane_base + kTmS2, tQ = tmem + lane_base + kTmQ;
+    uint32_t n_s2 = 0, n_qd = 0, n_qf = 0, n_free = 0, n_full = 0;
+    bool first = true;
+    auto write_op = [&](int c, const float (&v)[32]) {
+      float hi[32], lo[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        hi[e] = __bfloat162float(__float2bfloat16(v[e]));
+        lo[e] = v[e] - hi[e];
+      }
+      tile_store_row32(sQ, r, c, hi);
+      tile_store_row32(sQlo, r, c, lo);
+    };
+    // the snapshot stores of the previous operand have finished reading it
+    auto operand_free = [&]() -> bool {
+      if ((int)threadIdx.x == kChainLead) {
         bulk_wait_read_all();
         mbar_arrive(bar(QFREE));
       }
       __syncwarp();
-      if (!pwarp_wait(bar(QFREE), (n_qf++) & 1, ab)) return false;
-      {  // Q~ = hi + lo (bf16 each): the score GEMM uses both, the chain GEMM and the snapshot hi
-        float hi[64], lo[64];
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          hi[e] = __bfloat162float(__float2bfloat16(q[e]));
-          lo[e] = q[e] - hi[e];
-        }
-        tile_store_row64(sQ, r, hf, hi);
-        tile_store_row64(sQlo, r, hf, lo);
-      }
+      return pwarp_wait(bar(QFREE), (n_qf++) & 1, ab);
+    };
+    // all 128 rows written: hand the operand to the MMA warp and store the snapshot
+    auto publish = [&](long long pair, int bhq) {
       fence_proxy_async_smem();
-      mbar_arrive(bar(QWRITTEN));
-      if (threadIdx.x == 0) {
-        if (mbar_wait(bar(QWRITTEN), n_qw & 1, ab)) {
+      tc_fence_before();
+      mbar_arrive(bar(QOP_FULL));
+      if ((int)threadIdx.x == kChainLead) {
+        if (mbar_wait(bar(QOP_FULL), n_full & 1, ab)) {
           tma_store_tile(&tmQs, sQ, (int)(pair * 128), bhq, 0);
           bulk_commit();
-          mbar_arrive(bar(QOP_FULL));
         }
       }
-      ++n_qw;
+      ++n_full;
       __syncwarp();
-      return true;
     };
     bool ok = true;
     for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
       int i, bhq, b, h, bhk;
       decode(idx, i, bhq, b, h, bhk);
-      float q[64];
+      // the previous item's last score GEMM has finished reading the operand tiles
+      if (!first && !pwarp_wait(bar(QOP_FREE), (n_free++) & 1, ab)) break;
+      first = false;
+      if (!operand_free()) break;
       {
-        const float4* src = reinterpret_cast<const float4*>(p.qn + (((long long)bhq * Npad) + i * 128 + r) * 128 + hf * 64);
+        const float* src = p.qn + (((long long)bhq * Npad) + i * 128 + r) * 128;
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float4 f = src[e];
-          q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
+          for (int e = 0; e < 32; e += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(src + c * 32 + e);
+            v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+          }
+          tmem_st32(tQ + 32u * c, v);
+          write_op(c, v);
         }
+        tmem_st_wait();
+        publish(path_pair(i, i - 1), bhq);
       }
-      if (!write_qop(q, path_pair(i, i - 1), bhq)) break;
-      for (int j = i - 1; j >= 0; --j) {
-        if (!pwarp_wait(bar(SS_FULL), (n_ss++) & 1, ab)) { ok = false; break; }
+      for (int j = i - 1; j >= 1; --j) {
+        if (!pwarp_wait(bar(S2_FULL), (n_s2++) & 1, ab)) { ok = false; break; }
         tc_fence_after();
-        float sv[64];
-        tmem_ld64(tS, sv);
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS2 + 32u * c, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          const float2 a = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
-          sv[e] = fast_exp2(a.x);
-          sv[e + 1] = fast_exp2(a.y);
+          for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(-v[2 * e], -v[2 * e + 1]);
+          // packed columns of chunk c go to [16c, 16c+16): inside chunks already read
+          tmem_st16(tS2 + 16u * (uint32_t)c, pk);
         }
-        st_bf16x64(p.L + ((((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128 + hf * 64), sv);
-        if (j == 0) break;
-        tmem_ld64(tS2, sv);
-        tmem_st_packed64(tS2, sv, -1.f);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(NS2_FULL));
-        if (!pwarp_wait(bar(D_FULL), (n_d++) & 1, ab)) { ok = false; break; }
+        if (!pwarp_wait(bar(QD_FULL), (n_qd++) & 1, ab)) { ok = false; break; }
         tc_fence_after();
-        tmem_ld64(tS, sv);
-#pragma unroll
-        for (int e = 0; e < 64; ++e) q[e] += sv[e];
-        tc_fence_before();
-        if (!write_qop(q, path_pair(i, j - 1), bhq)) { ok = false; break; }
+        if (!operand_free()) { ok = false; break; }
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tQ + 32u * c, v);
+          tmem_ld_wait();
+          write_op(c, v);
+        }
+        publish(path_pair(i, j - 1), bhq);
       }
     }
-    if (threadIdx.x == 0) bulk_wait_all();
+    if ((int)threadIdx.x == kChainLead) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -319,7 +383,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   if (warp == pk::kWarpMma) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -518,13 +582,21 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 // ===========================================================================
 // path_row_kernel
 // ===========================================================================
+// Warps 0-3 produce the dA tiles (P = dV_i O_j^T read from TMEM, the L tile from
+// HBM, dA stored and packed back into TMEM as an A operand); warps 4-7 carry the
+// dQ~ chain, the critical path: -S3 back into TMEM, then dQ~ -- accumulated in
+// TMEM by the chain GEMM dQ~ += dA K_new_j + (-S3) W_j -- into the bf16 operand
+// of the next step and the snapshot.  P is double-buffered in TMEM and issued
+// one step ahead, so dA(j+1) is ready before the chain reaches step j+1.
 namespace prw {
 constexpr int kRing = 4;
 constexpr uint32_t kOffDV = 0, kOffDOP = 32768, kOffRing = 65536, kOffBar = kOffRing + kRing * 32768;
-enum { RF0 = 0, RE0 = RF0 + kRing, DV_FULL = RE0 + kRing, DV_EMPTY, PS_FULL, PK_FULL, D_FULL, DOP_FULL, QFREE,
-       QWRITTEN, DRAIN, NBAR };
+enum { RF0 = 0, RE0 = RF0 + kRing, DV_FULL = RE0 + kRing, DV_EMPTY, P_FULL, PK_FULL, S3_FULL, NS3_FULL, DQ_FULL,
+       DQ_FREE, DOP_FULL, QFREE, DRAIN, NBAR };
 constexpr uint32_t kSmem = kOffBar + NBAR * 8 + 16;
-constexpr uint32_t kTmP = 0, kTmS3 = 128, kTmD = 256;
+constexpr uint32_t kTmP = 0, kTmS3 = 256, kTmDQ = 384;   // P: two 128-column buffers
+constexpr int kHalf = 128;
+constexpr int kChainLead = 128;
 }  // namespace prw
 
 __global__ void __launch_bounds__(pk::kThreads, 1)
@@ -552,12 +624,14 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     }
     mbar_init(bar(DV_FULL), 1);
     mbar_init(bar(DV_EMPTY), 1);
-    mbar_init(bar(PS_FULL), 1);
-    mbar_init(bar(PK_FULL), pk::kEpi);
-    mbar_init(bar(D_FULL), 1);
-    mbar_init(bar(DOP_FULL), 1);
+    mbar_init(bar(P_FULL), 1);
+    mbar_init(bar(PK_FULL), kHalf);
+    mbar_init(bar(S3_FULL), 1);
+    mbar_init(bar(NS3_FULL), kHalf);
+    mbar_init(bar(DQ_FULL), 1);
+    mbar_init(bar(DQ_FREE), kHalf);
+    mbar_init(bar(DOP_FULL), kHalf);
     mbar_init(bar(QFREE), 1);
-    mbar_init(bar(QWRITTEN), pk::kEpi);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -604,6 +678,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         last_dv = (int)(it & 1);
         mbar_arrive_expect_tx(bar(DV_FULL), 32768);
         tma_load_tile(sDV, &tmDV, bar(DV_FULL), i * 128, bhq, 0);
+        // per step: O_j, W2_j, K_new_j, W_j.  The MMA warp takes O_{j+1} before it frees
+        // W2_j, K_new_j and W_j, which is exactly the ring's four slots
         for (int j = 0; j <= i && ok; ++j) {
           ok = ring.load(&tmO, j * 128, bhq, 0, ab);
           if (ok && j >= 1 && j < i) ok = ring.load(&tmW2, j * 128, bhk, 0, ab);
@@ -616,128 +692,199 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     }
   } else if (warp == pk::kWarpMma) {
     if (lane == 0) {
-      uint32_t rc = 0, n_pk = 0, n_dop = 0, it = 0;
+      uint32_t rc = 0, n_pk = 0, n_dop = 0, n_ns3 = 0, n_dqfree = 0, it = 0;
       auto ring_slot = [&](uint32_t idx) { return sbase + kOffRing + (idx % kRing) * 32768u; };
       auto ring_wait = [&](uint32_t idx) { return mbar_wait(bar(RF0 + (int)(idx % kRing)), (idx / kRing) & 1, ab); };
       auto ring_free = [&](uint32_t idx) { umma_commit(bar(RE0 + (int)(idx % kRing))); };
+      const uint32_t tp = tmem + kTmP, ts3 = tmem + kTmS3;
       bool ok = true;
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++it) {
         int i, bhq, b, h, bhk;
         decode(idx, i, bhq, b, h, bhk);
         if (!mbar_wait(bar(DV_FULL), it & 1, ab)) break;
+        // slot index of O_j for step j; the other tiles of the step follow it
+        auto tiles_of = [&](int j) { return 1 + ((j >= 1 && j < i) ? 1 : 0) + (j < i ? 1 : 0) + ((j >= 1 && j < i) ? 1 : 0); };
+        auto issue_p = [&](int j, uint32_t sO) -> bool {  // P_j = dV_i O_j^T into buffer j & 1
+          if (!ring_wait(sO)) return false;
+          tc_fence_after();
+          umma_tile(tp + 128u * (uint32_t)(j & 1), sDV, false, ring_slot(sO), false, 0u);
+          umma_commit(bar(P_FULL));
+          ring_free(sO);
+          return true;
+        };
+        uint32_t base = rc;
+        if (!issue_p(0, base)) break;
         for (int j = 0; j <= i; ++j) {
           const bool has_s3 = (j >= 1 && j < i);
-          const uint32_t sO = rc++;
-          if (!ring_wait(sO)) { ok = false; break; }
-          uint32_t sW2 = 0;
-          if (has_s3) {
+          const uint32_t next = base + (uint32_t)tiles_of(j);
+          // P of the next step goes out first: its buffer's previous dA was read by D(j-1)
+          if (j + 1 <= i && !issue_p(j + 1, next)) { ok = false; break; }
+          uint32_t k = base + 1;
+          if (has_s3) {  // chain: S3 = dQ~^{(j-1)} W2_j^T
             if (!mbar_wait(bar(DOP_FULL), (n_dop++) & 1, ab)) { ok = false; break; }
-            sW2 = rc++;
+            const uint32_t sW2 = k++;
             if (!ring_wait(sW2)) { ok = false; break; }
+            tc_fence_after();
+            umma_tile(ts3, sDOP, false, ring_slot(sW2), false, 0u);
+            umma_commit(bar(S3_FULL));
+            ring_free(sW2);
+          }
+          if (!mbar_wait(bar(PK_FULL), (n_pk++) & 1, ab)) { ok = false; break; }
+          if (j == i) {
+            base = next;
+            break;
+          }
+          const uint32_t sK = k++;
+          if (!ring_wait(sK)) { ok = false; break; }
+          uint32_t sW = 0;
+          if (j >= 1) {
+            sW = k++;
+            if (!ring_wait(sW) || !mbar_wait(bar(NS3_FULL), (n_ns3++) & 1, ab)) { ok = false; break; }
+          } else if (!mbar_wait(bar(DQ_FREE), ((n_dqfree++) & 1) ^ 1, ab)) {
+            ok = false;  // the previous item's dQ~ has been read out
+            break;
           }
           tc_fence_after();
-          umma_tile(tmem + kTmP, sDV, false, ring_slot(sO), false, 0u);
-          if (has_s3) umma_tile(tmem + kTmS3, sDOP, false, ring_slot(sW2), false, 0u);
-          umma_commit(bar(PS_FULL));
-          ring_free(sO);
-          if (has_s3) ring_free(sW2);
-          if (!mbar_wait(bar(PK_FULL), (n_pk++) & 1, ab)) { ok = false; break; }
-          if (j < i) {
-            const uint32_t sK = rc++;
-            if (!ring_wait(sK)) { ok = false; break; }
-            uint32_t sW = 0;
-            if (j >= 1) {
-              sW = rc++;
-              if (!ring_wait(sW)) { ok = false; break; }
-            }
-            tc_fence_after();
-            const uint32_t tp = tmem + kTmP, ts3 = tmem + kTmS3;
-            umma_tile_ts(tmem + kTmD, [&](int kk) { return packed_half_kslice(tp, kk); }, ring_slot(sK), true, 0u);
-            if (j >= 1)
-              umma_tile_ts(tmem + kTmD, [&](int kk) { return packed_half_kslice(ts3, kk); }, ring_slot(sW), true, 1u);
-            umma_commit(bar(D_FULL));
-            ring_free(sK);
-            if (j >= 1) ring_free(sW);
-          }
+          // dQ~ (TMEM) = [dQ~ +] dA K_new_j [+ (-S3) W_j]; packed operands by full rows (slice kk at 8 kk)
+          const uint32_t pj = tp + 128u * (uint32_t)(j & 1);
+          umma_tile_ts(tmem + kTmDQ, [&](int kk) { return pj + 8u * (uint32_t)kk; }, ring_slot(sK), true,
+                       j > 0 ? 1u : 0u);
+          if (j >= 1)
+            umma_tile_ts(tmem + kTmDQ, [&](int kk) { return ts3 + 8u * (uint32_t)kk; }, ring_slot(sW), true, 1u);
+          umma_commit(bar(DQ_FULL));
+          ring_free(sK);
+          if (j >= 1) ring_free(sW);
+          base = next;
         }
+        rc = base;
+        if (!ok) break;
         umma_commit(bar(DV_EMPTY));
       }
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
+  } else if (warp < 4) {
+    // ---------------- dA tiles ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t tP0 = tmem + ((uint32_t)(warp * 32) << 16) + kTmP;
+    uint32_t n_p = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+      int i, bhq, b, h, bhk;
+      decode(idx, i, bhq, b, h, bhk);
+      for (int j = 0; j <= i; ++j) {
+        if (!pwarp_wait(bar(P_FULL), (n_p++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tP = tP0 + 128u * (uint32_t)(j & 1);
+        const long long toff = (j < i) ? ((((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128)
+                                       : ((((long long)bhq * p.NB + i) * 128 + r) * 128);
+        const bf16* lrow = (j < i ? p.L : p.Ld) + toff;
+        bf16* drow = (j < i ? p.dA : p.dAd) + toff;
+        for (int c = 0; c < 4; ++c) {
+          float pv[32], lv[32];
+          tmem_ld32(tP + 32u * c, pv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ld_bf16x8(lrow + c * 32 + e * 8, lv + e * 8);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float v = -p.s * lv[e] * pv[e];
+            if (j == i && c * 32 + e >= r) v = 0.f;
+            pv[e] = v;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) st_bf16x8(drow + c * 32 + e * 8, pv + e * 8);
+          if (j < i) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(pv[2 * e], pv[2 * e + 1]);
+            // packed columns of chunk c go to [16c, 16c+16): inside chunks already read
+            tmem_st16(tP + 16u * (uint32_t)c, pk);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(PK_FULL));
+      }
+    }
   } else {
-    const int qd = warp & 3, hf = warp >> 2;
-    const int r = qd * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    const uint32_t tP = tmem + lane_base + kTmP + 64u * hf;
-    const uint32_t tS3 = tmem + lane_base + kTmS3 + 64u * hf;
-    const uint32_t tD = tmem + lane_base + kTmD + 64u * hf;
-    uint32_t n_ps = 0, n_d = 0, n_qf = 0, n_qw = 0;
-    auto write_dop = [&](const float (&q)[64], long long pair, int bhq) -> bool {
-      if (threadIdx.x == 0) {
+    // ---------------- dQ~ chain ----------------
+    const int wq = warp - 4;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS3 = tmem + lane_base + kTmS3, tDQ = tmem + lane_base + kTmDQ;
+    uint32_t n_s3 = 0, n_dq = 0, n_qf = 0, n_full = 0;
+    auto operand_free = [&]() -> bool {
+      if ((int)threadIdx.x == kChainLead) {
         bulk_wait_read_all();
         mbar_arrive(bar(QFREE));
       }
       __syncwarp();
-      if (!pwarp_wait(bar(QFREE), (n_qf++) & 1, ab)) return false;
-      tile_store_row64(sDOP, r, hf, q);
-      fence_proxy_async_smem();
-      mbar_arrive(bar(QWRITTEN));
-      if (threadIdx.x == 0) {
-        if (mbar_wait(bar(QWRITTEN), n_qw & 1, ab)) {
-          tma_store_tile(&tmDs, sDOP, (int)(pair * 128), bhq, 0);
-          bulk_commit();
-          mbar_arrive(bar(DOP_FULL));
-        }
-      }
-      ++n_qw;
-      __syncwarp();
-      return true;
+      return pwarp_wait(bar(QFREE), (n_qf++) & 1, ab);
     };
     bool ok = true;
     for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
       int i, bhq, b, h, bhk;
       decode(idx, i, bhq, b, h, bhk);
-      float dq[64];
-#pragma unroll
-      for (int e = 0; e < 64; ++e) dq[e] = 0.f;
-      for (int j = 0; j <= i; ++j) {
-        if (!pwarp_wait(bar(PS_FULL), (n_ps++) & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        float pv[64], lv[64];
-        tmem_ld64(tP, pv);
-        const long long toff = (j < i) ? ((((long long)bhq * p.NPAIR + path_pair(i, j)) * 128 + r) * 128 + hf * 64)
-                                       : ((((long long)bhq * p.NB + i) * 128 + r) * 128 + hf * 64);
-        ld_bf16x64((j < i ? p.L : p.Ld) + toff, lv);
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          float v = -p.s * lv[e] * pv[e];
-          if (j == i && hf * 64 + e >= r) v = 0.f;
-          pv[e] = v;
-        }
-        st_bf16x64((j < i ? p.dA : p.dAd) + toff, pv);
-        if (j < i) tmem_st_packed64(tP, pv, 1.f);
-        if (j >= 1 && j < i) {
-          tmem_ld64(tS3, lv);
-          tmem_st_packed64(tS3, lv, -1.f);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(bar(PK_FULL));
-        if (j < i) {
-          if (!pwarp_wait(bar(D_FULL), (n_d++) & 1, ab)) { ok = false; break; }
+      float* dq_row = p.dqn + (((long long)bhq * Npad) + i * 128 + r) * 128;
+      if (i == 0) {  // no off-diagonal block: dQ_new of the first row block is zero
+        for (int e = 0; e < 128; e += 4) *reinterpret_cast<float4*>(dq_row + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      for (int j = 0; j < i; ++j) {
+        if (j >= 1) {
+          if (!pwarp_wait(bar(S3_FULL), (n_s3++) & 1, ab)) { ok = false; break; }
           tc_fence_after();
-          tmem_ld64(tD, pv);
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(tS3 + 32u * c, v);
+            tmem_ld_wait();
+            uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 64; ++e) dq[e] += pv[e];
+            for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(-v[2 * e], -v[2 * e + 1]);
+            tmem_st16(tS3 + 16u * (uint32_t)c, pk);
+          }
+          tmem_st_wait();
           tc_fence_before();
-          if (j + 1 < i && !write_dop(dq, path_pair(i, j + 1), bhq)) { ok = false; break; }
+          mbar_arrive(bar(NS3_FULL));
+        }
+        if (!pwarp_wait(bar(DQ_FULL), (n_dq++) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        if (j + 1 < i) {
+          // dQ~^{(j)}: the operand of step j+1 and the snapshot of pair (i, j+1)
+          if (!operand_free()) { ok = false; break; }
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(tDQ + 32u * c, v);
+            tmem_ld_wait();
+            tile_store_row32(sDOP, r, c, v);
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(bar(DOP_FULL));
+          if ((int)threadIdx.x == kChainLead) {
+            if (mbar_wait(bar(DOP_FULL), n_full & 1, ab)) {
+              tma_store_tile(&tmDs, sDOP, (int)(path_pair(i, j + 1) * 128), bhq, 0);
+              bulk_commit();
+            }
+          }
+          ++n_full;
+          __syncwarp();
+        } else {
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(tDQ + 32u * c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(dq_row + c * 32 + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          }
+          tc_fence_before();
+          mbar_arrive(bar(DQ_FREE));
         }
       }
-      if (!ok) break;
-      st_f32x64(p.dqn + (((long long)bhq * Npad) + i * 128 + r) * 128 + hf * 64, dq);
     }
-    if (threadIdx.x == 0) bulk_wait_all();
+    if ((int)threadIdx.x == kChainLead) bulk_wait_all();
   }
 
   tc_fence_before();
