@@ -293,6 +293,44 @@ int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk
                       void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse, int* status, void* stream);
 
 /*
+ * Context-parallel backward (same chunking; the backward of lucid_attn_fwd /
+ * lucid_solve_fwd, replacing Lucid_Tril_Solver.backward, modeling_lucid.py:314-382,
+ * and the autograd of eager_lucid_attention_forward, :505-549, for one chunk).
+ * A rank computes every gradient of its own rows: the column passes cover its own
+ * column blocks over all later rows (whose q, dO, lse, delta, k^ and dV it holds as
+ * received), the row passes its own row blocks over all earlier columns.
+ *   lucid_cp_delta      delta = rowsum(dO o O) of rows [row_lo, row_hi) into the
+ *                       internal [B*Hq][Npad] fp32 layout (o / dout indexed by
+ *                       global row)
+ *   lucid_cp_attn_bwd   passes & 1: column pass of column blocks [blk_lo, blk_hi)
+ *                       (dk_f32, dx_f32 internal fp32); passes & 2: row pass of
+ *                       row blocks [blk_lo, blk_hi) (dq, indexed by global row)
+ *   lucid_cp_solve_bwd  passes & 1: transposed solve of column blocks [blk_lo, blk_hi)
+ *                       into dv_int (bf16 internal) and dk_col, publishing their flags;
+ *                       every later block's flag must be set beforehand
+ *                       (lucid_cp_publish after its dV arrived); passes & 2: row pass
+ *                       of row blocks [blk_lo, blk_hi) into dk_row, then dK (= RMSNorm
+ *                       backward of dk_col + dk_row + the diagonal term, + dk_add) and
+ *                       dV of those rows (dk / dv indexed by global row)
+ * Same block-range, max_ctas and no-cross-launch-wait rules as the forward blocks.
+ */
+int lucid_cp_delta(int B, int Hq, int N, int D, int row_lo, int row_hi, const void* o, int64_t o_sb, int64_t o_sh,
+                   int64_t o_sn, const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, float* delta,
+                   void* stream);
+int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
+                      int passes, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                      const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x,
+                      const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, const float* lse,
+                      const float* delta, void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn,
+                      float* dk_f32, float* dx_f32, int* status, void* stream);
+int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas, int passes,
+                       const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x, const void* khat,
+                       const void* u, const float* rstd, const float* dinv, const float* dx_f32,
+                       const float* dk_add, void* dv_int, float* dk_col, float* dk_row, int* flags,
+                       void* dk, int64_t dk_sb, int64_t dk_sh, int64_t dk_sn,
+                       void* dv, int64_t dv_sb, int64_t dv_sh, int64_t dv_sn, int* status, void* stream);
+
+/*
  * Kernel timing hook (benchmarks).  While enabled for one kernel family,
  * every launch of that family's main kernel is bracketed by a pair of CUDA
  * events recorded on the launch stream; lucid_profile_read waits for the

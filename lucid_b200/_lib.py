@@ -74,6 +74,11 @@ SIGNATURES = {
                            + [c_void_p] * 6 + [c_void_p]),
     "lucid_cp_attn_fwd": (c_int, [c_int] * 5 + [c_float, c_int, c_int, c_int] + [c_void_p] + S3 + [c_void_p] + S3
                           + [c_void_p] + [c_void_p] + S3 + [c_void_p, c_void_p, c_void_p]),
+    "lucid_cp_delta": (c_int, [c_int] * 6 + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_void_p]),
+    "lucid_cp_attn_bwd": (c_int, [c_int] * 5 + [c_float] + [c_int] * 4 + [c_void_p] + S3 + [c_void_p] + S3
+                          + [c_void_p] + [c_void_p] + S3 + [c_void_p] * 2 + [c_void_p] + S3 + [c_void_p] * 4),
+    "lucid_cp_solve_bwd": (c_int, [c_int] * 4 + [c_float] + [c_int] * 4 + [c_void_p] + S3 + [c_void_p] * 11
+                           + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p] * 2),
     "lucid_selftest_umma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "lucid_profile_enable": (c_int, [c_int]),
     "lucid_profile_read": (c_int, [c_float_p, ctypes.POINTER(c_int)]),

@@ -25,12 +25,24 @@ Protocol (all point-to-point NCCL send/recv, no collective):
   NCCL receive, and the persistent kernels leave `reserve_sms` SMs free so
   the NCCL kernels of the other groups run alongside.
 
-Chunks may differ in length (balanced_bounds equalises the causal work:
-the solve and the attention of row t cost ~t, so equal chunks leave the
-last rank (2W-1)/W^2 of the work).
+Backward (ChunkProtocol.backward, after run): a rank computes every
+gradient of its own rows.  Its column passes (attention dX / dK over its
+own key blocks, the transposed solve dV = P^-T dX and the column part of
+dK^) need the rows after its chunk, its row passes (dQ, the row part of
+dK^) only the rows before it, which the forward already brought in.  So
+the messages mirror the forward's, flowing from higher to lower ranks:
+  1. every rank sends q, dO, its raw keys, lse and delta = rowsum(dO o O)
+     of its rows to every earlier rank (inputs and forward outputs, so
+     this starts at once);
+  2. for each head group in order, rank r waits for dV_j(g) of every
+     j > r, publishes those blocks, runs its transposed solve, sends its
+     dV_r(g) to every earlier rank, then runs the attention column pass of
+     group g+1 and the row passes of group g while rank r-1 solves.
+The chain of the backward runs from the last rank to the first.
 
-Forward only: the backward of the context-parallel chain is not built (the
-single-GPU op `lucid_attention` has the full backward).
+Chunks may differ in length.  balanced_bounds equalises the forward's work
+(the solve and the attention of row t cost ~t); train_bounds equalises the
+forward plus the backward, whose column passes cost ~N-t and row passes ~t.
 """
 from __future__ import annotations
 
@@ -39,7 +51,8 @@ import torch.distributed as dist
 
 from . import _lib
 
-__all__ = ["cp_lucid_attention_forward", "ChunkProtocol", "KernelBackend", "balanced_bounds", "even_bounds"]
+__all__ = ["cp_lucid_attention_forward", "cp_lucid_attention", "ChunkProtocol", "KernelBackend", "balanced_bounds",
+           "even_bounds", "train_bounds"]
 
 
 def even_bounds(N: int, world: int):
@@ -54,6 +67,29 @@ def balanced_bounds(N: int, world: int, align: int = 256):
     b = [0]
     for r in range(1, world):
         x = int(round(N * (r / world) ** 0.5 / align)) * align
+        b.append(min(max(x, b[-1] + align), N - (world - r) * align))
+    return b + [N]
+
+
+def train_bounds(N: int, world: int, align: int = 256, col: float = 1.0, row: float = 1.2, flat: float = 0.05):
+    """Contiguous chunks of equal forward + backward work.  Per row t of an N-row
+    sequence the work is modelled as col (N - t) + row t + flat N: the backward's
+    column passes (attention dX / dK, transposed solve) cost ~N - t, the forward
+    and the backward's row passes ~t, the row statistics a constant.  The default
+    weights are the measured stage times of the single-GPU kernels (column passes
+    34 ms, forward + row passes 42 ms, prep 3.5 ms at N = 32768)."""
+    def work(x):  # cumulative work of rows [0, x), in units of N^2
+        u = x / N
+        return col * (u - u * u / 2) + row * u * u / 2 + flat * u
+    total = work(N)
+    b = [0]
+    for r in range(1, world):
+        target = total * r / world
+        lo, hi = 0.0, float(N)
+        for _ in range(60):
+            mid = (lo + hi) / 2
+            lo, hi = (mid, hi) if work(mid) < target else (lo, mid)
+        x = int(round(lo / align)) * align
         b.append(min(max(x, b[-1] + align), N - (world - r) * align))
     return b + [N]
 
@@ -128,6 +164,43 @@ class ChunkProtocol:
         for s in sends:
             s.wait()
         return be.finish()
+
+    def backward(self, do):
+        """Gradients of this rank's rows after run(): returns what the
+        backend's finish_grad returns (dq, dk, dv of the chunk)."""
+        be, r, W = self.be, self.rank, self.world
+        be.set_grad(do)
+        # 1. q, dO, raw keys, lse and delta flow to every earlier rank; receives
+        #    from later ranks are posted latest-rank first and sends go to the
+        #    nearest earlier rank first (the forward's order under r -> W-1-r)
+        later = list(range(W - 1, r, -1))
+        earlier = list(range(r - 1, -1, -1))
+        bufs = {j: be.empty_grad_inputs(j) for j in later}
+        reqs = {j: [self._recv(t, j) for t in bufs[j]] for j in later}
+        mine = be.own_grad_inputs()
+        sends = [self._send(t, j) for j in earlier for t in mine]
+        for j in later:
+            for rq in reqs[j]:
+                rq.wait()
+            be.store_grad_inputs(j, bufs[j])
+        be.prep_later()
+        # 2. dV flows to earlier ranks, pipelined over head groups
+        be.attn_col(0)
+        for g in range(be.G):
+            dbuf = {j: be.empty_chunk(be.Hg, j) for j in later}
+            reqs = [self._recv(dbuf[j], j) for j in later]
+            for j, rq in zip(later, reqs):
+                rq.wait()
+                be.store_dv(g, j, dbuf[j])
+            be.solve_col(g)
+            dvs = be.own_dv(g)
+            sends += [self._send(dvs, j) for j in earlier]
+            if g + 1 < be.G:
+                be.attn_col(g + 1)
+            be.rows(g)
+        for s in sends:
+            s.wait()
+        return be.finish_grad()
 
 
 class KernelBackend:
@@ -242,10 +315,170 @@ class KernelBackend:
                    "lucid_cp_attn_fwd")
 
     def finish(self):
+        self._check_status()
+        return self.o
+
+    def _check_status(self):
         st = int(self.status[0].item())
         if st != 0:
             raise _lib.LucidError(f"context-parallel kernels reported status {st:#x} (a bounded wait timed out)")
-        return self.o
+
+    # ---- backward ----
+    def _hq(self, g):
+        return slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
+
+    def _shift(self, t, row_dim):
+        """Address of global row 0 of a tensor holding this rank's rows (the
+        kernels index outputs by global row)."""
+        return t.data_ptr() - self.row0 * t.stride(row_dim) * t.element_size()
+
+    def set_grad(self, do):
+        B, N, D, Hq, H = self.B, self.N, self.D, self.Hq, self.H
+        bf = dict(dtype=torch.bfloat16, device=self.dev)
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        self.dOf = torch.zeros(B, Hq, N, D, **bf)
+        self.dOf[:, :, self._rows(self.r)] = do.transpose(1, 2)
+        self.delta = [torch.zeros(B, self.Hg * self.Gq, N, **f32) for _ in range(self.G)]
+        for g in range(self.G):
+            og = self.o[:, :, self._hq(g)].transpose(1, 2)
+            dg = self.dOf[:, self._hq(g)]
+            _lib.check(self.lib.lucid_cp_delta(B, self.Hg * self.Gq, N, D, self.row0, self.row0 + self.C,
+                                               self._shift(og, 2), og.stride(0), og.stride(1), og.stride(2),
+                                               dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2),
+                                               self.delta[g].data_ptr(), self._st()), "lucid_cp_delta")
+        # per-parity scratch of the head group in flight (group g uses g % 2)
+        self.dx32 = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
+        self.dka32 = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
+        self.dkcol = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
+        self.dkrow = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
+        self.dvint = [torch.zeros(B, self.Hg, N, D, **bf) for _ in range(2)]
+        self.bflags = [torch.zeros(B * self.Hg * self.NB, dtype=torch.int32, device=self.dev) for _ in range(self.G)]
+        self.dq = torch.empty(B, Hq, self.C, D, **bf)
+        self.dk = torch.empty(B, H, self.C, D, **bf)
+        self.dv = torch.empty(B, H, self.C, D, **bf)
+
+    def _own_stats(self, lst):
+        return torch.cat([t[:, :, self._rows(self.r)] for t in lst], dim=1)
+
+    def own_grad_inputs(self):
+        rows = self._rows(self.r)
+        packed = torch.cat([self.Qf[:, :, rows], self.dOf[:, :, rows], self.Kf[:, :, rows]], dim=1).contiguous()
+        stats = torch.stack([self._own_stats(self.lse), self._own_stats(self.delta)]).contiguous()
+        return [packed, stats]
+
+    def empty_grad_inputs(self, j):
+        n = self.bounds[j + 1] - self.bounds[j]
+        return [torch.empty(self.B, 2 * self.Hq + self.H, n, self.D, dtype=torch.bfloat16, device=self.dev),
+                torch.empty(2, self.B, self.Hq, n, dtype=torch.float32, device=self.dev)]
+
+    def store_grad_inputs(self, j, bufs):
+        packed, stats = bufs
+        rows, Hq = self._rows(j), self.Hq
+        self.Qf[:, :, rows] = packed[:, :Hq]
+        self.dOf[:, :, rows] = packed[:, Hq:2 * Hq]
+        self.Kf[:, :, rows] = packed[:, 2 * Hq:]
+        for g in range(self.G):
+            self.lse[g][:, :, rows] = stats[0][:, self._hq(g)]
+            self.delta[g][:, :, rows] = stats[1][:, self._hq(g)]
+
+    def prep_later(self):
+        if self.blk_hi >= self.NB:
+            return
+        for g in range(self.G):
+            kv = self.Kf[:, self._hs(g)]
+            _lib.check(self.lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, self.blk_hi,
+                                              self.NB, 1, kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2),
+                                              self.khat[g].data_ptr(), self.u[g].data_ptr(),
+                                              self.rstd[g].data_ptr(), self.dinv[g].data_ptr(), self._st()),
+                       "lucid_cp_prep")
+
+    def _attn_bwd(self, g, passes):
+        hq, pr = self._hq(g), g % 2
+        qg, kg, dg = self.Qf[:, hq], self.Kf[:, self._hs(g)], self.dOf[:, hq]
+        dq = self.dq[:, hq]
+        _lib.check(self.lib.lucid_cp_attn_bwd(
+            self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi, self.max_ctas,
+            passes, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
+            kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2), self.x[g].data_ptr(),
+            dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2), self.lse[g].data_ptr(),
+            self.delta[g].data_ptr(), self._shift(dq, 2), dq.stride(0), dq.stride(1), dq.stride(2),
+            self.dka32[pr].data_ptr(), self.dx32[pr].data_ptr(), self.status.data_ptr(), self._st()),
+            "lucid_cp_attn_bwd")
+
+    def _solve_bwd(self, g, passes):
+        hs, pr = self._hs(g), g % 2
+        kg, dk, dv = self.Kf[:, hs], self.dk[:, hs], self.dv[:, hs]
+        _lib.check(self.lib.lucid_cp_solve_bwd(
+            self.B, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi, self.max_ctas, passes,
+            kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2), self.x[g].data_ptr(),
+            self.khat[g].data_ptr(), self.u[g].data_ptr(), self.rstd[g].data_ptr(), self.dinv[g].data_ptr(),
+            self.dx32[pr].data_ptr(), self.dka32[pr].data_ptr(), self.dvint[pr].data_ptr(),
+            self.dkcol[pr].data_ptr(), self.dkrow[pr].data_ptr(), self.bflags[g].data_ptr(),
+            self._shift(dk, 2), dk.stride(0), dk.stride(1), dk.stride(2),
+            self._shift(dv, 2), dv.stride(0), dv.stride(1), dv.stride(2), self.status.data_ptr(), self._st()),
+            "lucid_cp_solve_bwd")
+
+    def attn_col(self, g):
+        self._attn_bwd(g, 1)
+
+    def store_dv(self, g, j, buf):
+        self.dvint[g % 2][:, :, self._rows(j)] = buf
+        _lib.check(self.lib.lucid_cp_publish(self.bflags[g].data_ptr(), self.B * self.Hg, self.NB,
+                                             self.bounds[j] // 128, self.bounds[j + 1] // 128, self._st()),
+                   "lucid_cp_publish")
+
+    def solve_col(self, g):
+        self._solve_bwd(g, 1)
+
+    def own_dv(self, g):
+        return self.dvint[g % 2][:, :, self._rows(self.r)].contiguous()
+
+    def rows(self, g):
+        self._solve_bwd(g, 2)
+        self._attn_bwd(g, 2)
+
+    def finish_grad(self):
+        self._check_status()
+        return self.dq, self.dk, self.dv
+
+
+class CPLucidAttentionFunction(torch.autograd.Function):
+    """Autograd of the context-parallel op: the forward chain, then the
+    backward chain with the forward's per-rank state (held by the protocol)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, proto):
+        ctx.proto = proto
+        return proto.run(q, k, v)
+
+    @staticmethod
+    def backward(ctx, do):
+        proto, ctx.proto = ctx.proto, None
+        dq, dk, dv = proto.backward(do.contiguous())
+        return dq, dk, dv, None
+
+
+def _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds):
+    W = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
+    B, Hq, C, D = q.shape
+    H = k.shape[1]
+    s = D ** -0.5 if scale is None else scale
+    if bounds is None:
+        bounds = even_bounds(C * W, W)
+    if bounds[r + 1] - bounds[r] != C:
+        raise ValueError(f"rank {r} passed {C} rows but owns [{bounds[r]}, {bounds[r + 1]})")
+    be = KernelBackend(B, H, Hq, bounds, D, s, eps, r, W, head_groups, q.device, reserve_sms)
+    return ChunkProtocol(be, group)
+
+
+def cp_lucid_attention(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8, bounds=None):
+    """LUCID attention over a sequence split across the ranks of ``group``, with
+    autograd: the arguments and the result are those of
+    cp_lucid_attention_forward, and backward() runs the backward chain
+    (every rank must call backward, as every rank called forward)."""
+    proto = _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds)
+    return CPLucidAttentionFunction.apply(q, k, v, proto)
 
 
 def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8,
@@ -257,14 +490,4 @@ def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_g
     (``bounds`` as from balanced_bounds / even_bounds; None: equal chunks).
     Returns this rank's rows of O as [B, C_r, Hq, D] (the layout of
     eager_lucid_attention_forward, modeling_lucid.py:546)."""
-    W = dist.get_world_size(group) if dist.is_initialized() else 1
-    r = dist.get_rank(group) if dist.is_initialized() else 0
-    B, Hq, C, D = q.shape
-    H = k.shape[1]
-    s = D ** -0.5 if scale is None else scale
-    if bounds is None:
-        bounds = even_bounds(C * W, W)
-    if bounds[r + 1] - bounds[r] != C:
-        raise ValueError(f"rank {r} passed {C} rows but owns [{bounds[r]}, {bounds[r + 1]})")
-    be = KernelBackend(B, H, Hq, bounds, D, s, eps, r, W, head_groups, q.device, reserve_sms)
-    return ChunkProtocol(be, group).run(q, k, v)
+    return _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds).run(q, k, v)

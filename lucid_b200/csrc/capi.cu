@@ -16,17 +16,19 @@ cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap
                            const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st);
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
                          long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
-                         long long d_sn, float* delta, cudaStream_t st);
+                         long long d_sn, float* delta, cudaStream_t st, int row0 = 0, int row1 = -1);
 cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const bf16* k, long long k_sb,
                                   long long k_sh, long long k_sn, const float* rstd, const float* dinv,
                                   const bf16* x, const bf16* dv_int, const float* dk_col,
                                   const float* dk_row, const float* dk_add, bf16* dk, long long dk_sb,
                                   long long dk_sh, long long dk_sn, bf16* dv, long long dv_sb,
-                                  long long dv_sh, long long dv_sn, cudaStream_t st);
+                                  long long dv_sh, long long dv_sn, cudaStream_t st, int row0 = 0,
+                                  int row1 = -1);
 }  // namespace lb
 
 using namespace lb;
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -432,6 +434,105 @@ extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float sca
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
   return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
+}
+
+extern "C" int lucid_cp_delta(int B, int Hq, int N, int D, int row_lo, int row_hi, const void* o, int64_t o_sb,
+                              int64_t o_sh, int64_t o_sn, const void* dout, int64_t do_sb, int64_t do_sh,
+                              int64_t do_sn, float* delta, void* stream) {
+  if (!shape_ok(B, Hq, Hq, N, D) || row_lo < 0 || row_hi > N || row_lo > row_hi) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hq, N) || row_lo == row_hi) return LUCID_OK;
+  if (!aligned16(delta) || !strides_ok(o_sb, o_sh, o_sn) || !strides_ok(do_sb, do_sh, do_sn)) return LUCID_ERR_ALIGN;
+  return to_status(launch_delta(B, Hq, N, npad_of(N), static_cast<const bf16*>(o), o_sb, o_sh, o_sn,
+                                static_cast<const bf16*>(dout), do_sb, do_sh, do_sn, delta,
+                                reinterpret_cast<cudaStream_t>(stream), row_lo, row_hi));
+}
+
+extern "C" int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi,
+                                 int max_ctas, int passes, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                                 const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x,
+                                 const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, const float* lse,
+                                 const float* delta, void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn,
+                                 float* dk_f32, float* dx_f32, int* status, void* stream) {
+  if (!shape_ok(B, Hq, Hkv, N, D) || !cp_range_ok(N, blk_lo, blk_hi) || passes < 1 || passes > 3)
+    return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(dout) || !aligned16(lse) ||
+      !aligned16(delta) || !aligned16(dk_f32) || !aligned16(dx_f32) || !strides_ok(q_sb, q_sh, q_sn) ||
+      !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(do_sb, do_sh, do_sn) || !strides_ok(dq_sb, dq_sh, dq_sn) ||
+      status == nullptr)
+    return LUCID_ERR_ALIGN;
+  const int NB = nb_of(N), Npad = npad_of(N);
+  CUtensorMap tK, tX, tQ, tDO;
+  if (!tmap_strided(&tK, k, B, Hkv, N, k_sb, k_sh, k_sn) || !tmap_internal(&tX, x, B, Hkv, Npad) ||
+      !tmap_strided(&tQ, q, B, Hq, N, q_sb, q_sh, q_sn) ||
+      !tmap_strided(&tDO, dout, B, Hq, N, do_sb, do_sh, do_sn))
+    return LUCID_ERR_TENSORMAP;
+  BwdArgs ba{};
+  ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
+  ba.scale = scale;
+  ba.lse = lse; ba.delta = delta;
+  ba.dx = dx_f32; ba.dk_col = dk_f32;
+  ba.dq = static_cast<bf16*>(dq); ba.dq_sb = dq_sb; ba.dq_sh = dq_sh; ba.dq_sn = dq_sn;
+  ba.status = status;
+  ba.blk0 = blk_lo; ba.blk1 = blk_hi; ba.max_ctas = max_ctas;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (passes & 1) {
+    ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
+    if (launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  }
+  if (passes & 2) {
+    ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
+    if (launch_bwd_row(false, tQ, tDO, tK, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  }
+  return LUCID_OK;
+}
+
+extern "C" int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
+                                  int passes, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                                  const void* x, const void* khat, const void* u, const float* rstd,
+                                  const float* dinv, const float* dx_f32, const float* dk_add, void* dv_int,
+                                  float* dk_col, float* dk_row, int* flags, void* dk, int64_t dk_sb,
+                                  int64_t dk_sh, int64_t dk_sn, void* dv, int64_t dv_sb, int64_t dv_sh,
+                                  int64_t dv_sn, int* status, void* stream) {
+  if (!shape_ok(B, H, H, N, D) || !cp_range_ok(N, blk_lo, blk_hi) || passes < 1 || passes > 3)
+    return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  if (!aligned16(x) || !aligned16(khat) || !aligned16(u) || !aligned16(rstd) || !aligned16(dinv) ||
+      !aligned16(dx_f32) || (dk_add && !aligned16(dk_add)) || !aligned16(dv_int) || !aligned16(dk_col) ||
+      !aligned16(dk_row) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(dk_sb, dk_sh, dk_sn) ||
+      !strides_ok(dv_sb, dv_sh, dv_sn) || flags == nullptr || status == nullptr)
+    return LUCID_ERR_ALIGN;
+  const int NB = nb_of(N), Npad = npad_of(N);
+  CUtensorMap tK, tX, tDV, tU;
+  if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
+      !tmap_internal(&tDV, dv_int, B, H, Npad) || !tmap_internal(&tU, u, B, H, Npad))
+    return LUCID_ERR_TENSORMAP;
+  BwdArgs ba{};
+  ba.B = B; ba.Hq = H; ba.Hkv = H; ba.N = N; ba.NB = NB; ba.Npad = Npad;
+  ba.scale = scale;
+  ba.dk_col = dk_col; ba.dk_row = dk_row;
+  ba.dinv = dinv; ba.dx_in = dx_f32; ba.dv = static_cast<bf16*>(dv_int);
+  ba.flags = flags;
+  ba.status = status;
+  ba.blk0 = blk_lo; ba.blk1 = blk_hi; ba.max_ctas = max_ctas;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (passes & 1) {
+    ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
+    if (launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+  }
+  if (passes & 2) {
+    {
+      ProfileScope ps(LUCID_KERNEL_SOLVE_BWD_ROW, st);
+      if (launch_bwd_row(true, tK, tDV, tK, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    }
+    const int row_hi = std::min(N, blk_hi * 128);
+    return to_status(launch_solve_finalize(
+        B, H, N, Npad, scale, static_cast<const bf16*>(k), k_sb, k_sh, k_sn, rstd, dinv,
+        static_cast<const bf16*>(x), static_cast<const bf16*>(dv_int), dk_col, dk_row, dk_add,
+        static_cast<bf16*>(dk), dk_sb, dk_sh, dk_sn, static_cast<bf16*>(dv), dv_sb, dv_sh, dv_sn, st,
+        blk_lo * 128, row_hi));
+  }
+  return LUCID_OK;
 }
 
 extern "C" int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps, const void* k,

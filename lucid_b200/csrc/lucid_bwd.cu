@@ -138,13 +138,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int BHk = p.B * p.Hkv;
   const int G = p.Hq / p.Hkv;
-  const int total = p.NB * BHk;
-  // transposed solve: blocks NB-1 .. 0 across heads (wavefront order);
+  const int blk0 = p.blk0, blk1 = p.blk1 > 0 ? p.blk1 : p.NB, nblk = blk1 - blk0;
+  const int total = nblk * BHk;
+  // transposed solve: blocks blk1-1 .. blk0 across heads (wavefront order);
   // attention: head-major, longest columns first within a head, so the CTAs in
   // flight share one or two heads whose Q / dO tiles stay resident in L2
   auto decode = [&](int idx, int& i, int& b, int& hk) {
-    i = SOLVE ? (p.NB - 1 - idx / BHk) : (idx % p.NB);
-    const int bh = SOLVE ? idx % BHk : idx / p.NB;
+    i = SOLVE ? (blk1 - 1 - idx / BHk) : (blk0 + idx % nblk);
+    const int bh = SOLVE ? idx % BHk : idx / nblk;
     b = bh / p.Hkv;
     hk = bh % p.Hkv;
   };
@@ -599,11 +600,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // items: (row block j, head)
   const int BH = SOLVE ? p.B * p.Hkv : p.B * p.Hq;
   const int G = p.Hq / p.Hkv;
-  const int total = p.NB * BH;
+  const int blk1 = p.blk1 > 0 ? p.blk1 : p.NB, nblk = blk1 - p.blk0;
+  const int total = nblk * BH;
   auto decode = [&](int idx, int& j, int& b, int& ha, int& hk) {
     // head-major, longest rows first within a head (L2 residency of the head's tiles)
-    j = p.NB - 1 - idx % p.NB;
-    const int bh = idx / p.NB;
+    j = blk1 - 1 - idx % nblk;
+    const int bh = idx / nblk;
     if (SOLVE) {
       b = bh / p.Hkv;
       hk = bh % p.Hkv;
@@ -831,14 +833,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // delta[bhq][row] = sum_d dO[row][d] * O[row][d]  (zero on padding rows)
 __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb,
                                    long long o_sh, long long o_sn, const bf16* dout, long long d_sb,
-                                   long long d_sh, long long d_sn, float* delta) {
+                                   long long d_sh, long long d_sn, float* delta, int row0, int nrows) {
   const int warps = blockDim.x >> 5;
   const long long gw = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const long long total = (long long)B * Hq * Npad;
+  const long long total = (long long)B * Hq * nrows;
   if (gw >= total) return;
-  const int row = (int)(gw % Npad);
-  const long long bh = gw / Npad;
+  const int row = row0 + (int)(gw % nrows);
+  const long long bh = gw / nrows;
   const int b = (int)(bh / Hq), h = (int)(bh % Hq);
   float acc = 0.f;
   if (row < N) {
@@ -858,7 +860,7 @@ __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o
   }
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-  if (lane == 0) delta[gw] = acc;
+  if (lane == 0) delta[bh * Npad + row] = acc;
 }
 
 // Solve backward finalize, one warp per row (row < N):
@@ -871,14 +873,15 @@ __global__ void lucid_solve_finalize_kernel(int B, int H, int N, int Npad, float
                                             const bf16* dv_int, const float* dk_col,
                                             const float* dk_row, const float* dk_add, bf16* dk,
                                             long long dk_sb, long long dk_sh, long long dk_sn, bf16* dv,
-                                            long long dv_sb, long long dv_sh, long long dv_sn) {
+                                            long long dv_sb, long long dv_sh, long long dv_sn, int row0,
+                                            int nrows) {
   const int warps = blockDim.x >> 5;
   const long long gw = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const long long total = (long long)B * H * N;
+  const long long total = (long long)B * H * nrows;
   if (gw >= total) return;
-  const int row = (int)(gw % N);
-  const long long bh = gw / N;
+  const int row = row0 + (int)(gw % nrows);
+  const long long bh = gw / nrows;
   const int b = (int)(bh / H), h = (int)(bh % H);
   const long long ir = bh * Npad + row;  // internal row
   const int d0 = lane * 4;
@@ -945,9 +948,10 @@ static cudaError_t set_smem(K kernel, uint32_t bytes) {
 
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a, cudaStream_t st) {
-  const int total = a.NB * a.B * a.Hkv;
-  if (total == 0) return cudaSuccess;
-  const int grid = std::min(total, bwd_num_sms());
+  const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
+  const int total = nblk * a.B * a.Hkv;
+  if (total <= 0) return cudaSuccess;
+  const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, bwd_num_sms()) : bwd_num_sms());
   cudaError_t e;
   if (solve) {
     if ((e = set_smem(lucid_bwd_col_kernel<true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
@@ -961,9 +965,10 @@ cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap
 
 cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st) {
-  const int total = a.NB * a.B * (solve ? a.Hkv : a.Hq);
-  if (total == 0) return cudaSuccess;
-  const int grid = std::min(total, bwd_num_sms());
+  const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
+  const int total = nblk * a.B * (solve ? a.Hkv : a.Hq);
+  if (total <= 0) return cudaSuccess;
+  const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, bwd_num_sms()) : bwd_num_sms());
   cudaError_t e;
   if (solve) {
     if ((e = set_smem(lucid_bwd_row_kernel<true>, bwdr::kSmemBytes)) != cudaSuccess) return e;
@@ -977,12 +982,13 @@ cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap
 
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
                          long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
-                         long long d_sn, float* delta, cudaStream_t st) {
-  const long long warps = (long long)B * Hq * Npad;
-  if (warps == 0) return cudaSuccess;
+                         long long d_sn, float* delta, cudaStream_t st, int row0, int row1) {
+  if (row1 < 0) row1 = Npad;
+  const long long warps = (long long)B * Hq * (row1 - row0);
+  if (warps <= 0) return cudaSuccess;
   const int blocks = (int)((warps + 7) / 8);
   lucid_delta_kernel<<<blocks, 256, 0, st>>>(B, Hq, N, Npad, o, o_sb, o_sh, o_sn, dout, d_sb, d_sh,
-                                             d_sn, delta);
+                                             d_sn, delta, row0, row1 - row0);
   return cudaGetLastError();
 }
 
@@ -991,13 +997,15 @@ cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const 
                                   const bf16* x, const bf16* dv_int, const float* dk_col,
                                   const float* dk_row, const float* dk_add, bf16* dk, long long dk_sb,
                                   long long dk_sh, long long dk_sn, bf16* dv, long long dv_sb,
-                                  long long dv_sh, long long dv_sn, cudaStream_t st) {
-  const long long warps = (long long)B * H * N;
-  if (warps == 0) return cudaSuccess;
+                                  long long dv_sh, long long dv_sn, cudaStream_t st, int row0, int row1) {
+  if (row1 < 0) row1 = N;
+  const long long warps = (long long)B * H * (row1 - row0);
+  if (warps <= 0) return cudaSuccess;
   const int blocks = (int)((warps + 7) / 8);
   lucid_solve_finalize_kernel<<<blocks, 256, 0, st>>>(B, H, N, Npad, s, k, k_sb, k_sh, k_sn, rstd, dinv,
                                                       x, dv_int, dk_col, dk_row, dk_add, dk, dk_sb,
-                                                      dk_sh, dk_sn, dv, dv_sb, dv_sh, dv_sn);
+                                                      dk_sh, dk_sn, dv, dv_sb, dv_sh, dv_sn, row0,
+                                                      row1 - row0);
   return cudaGetLastError();
 }
 

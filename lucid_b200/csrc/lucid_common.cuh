@@ -65,6 +65,11 @@ struct BwdArgs {
   bf16* dv;                  // [B][Hkv][Npad][128] bf16 (MMA operand + output source)
   int* flags;                // [B*Hkv][NB], zero before launch
   int* status;
+  // output blocks [blk0, blk1) (blk1 == 0: NB): column blocks of the column pass, row
+  // blocks of the row pass; the operand blocks on the other side span all of [0, NB)
+  // (context parallel: the rest of the sequence is held as received from other ranks).
+  // max_ctas caps the persistent grid (0: #SMs).
+  int blk0 = 0, blk1 = 0, max_ctas = 0;
 };
 
 // Decode step (get_new_v_prime) and decode attention: one pass over the caches.

@@ -34,9 +34,17 @@ def _inputs():
     return q, k, v
 
 
+def _grad_out():
+    g = torch.Generator().manual_seed(6)
+    B, Hq, N, D = (SEQ[k] for k in ("B", "Hq", "N", "D"))
+    return torch.randn(B, N, Hq, D, generator=g, dtype=torch.float64)
+
+
 def _bounds(world, mode):
-    from lucid_b200.cp import balanced_bounds, even_bounds
+    from lucid_b200.cp import balanced_bounds, even_bounds, train_bounds
     N = SEQ["N"]
+    if mode == "train":
+        return train_bounds(N, world, align=64)
     return balanced_bounds(N, world, align=64) if mode == "balanced" else even_bounds(N, world)
 
 
@@ -56,35 +64,50 @@ def _worker(rank, world, port, groups, mode, out_dir):
     try:
         if mode == "die" and rank == 0:
             os._exit(0)   # leaves without sending anything
-        o = ChunkProtocol(be).run(q[:, :, rows], k[:, :, rows], v[:, :, rows])
+        proto = ChunkProtocol(be)
+        o = proto.run(q[:, :, rows], k[:, :, rows], v[:, :, rows])
         np.save(os.path.join(out_dir, f"o{rank}.npy"), o.numpy())
+        if mode == "die_bwd" and rank == world - 1:
+            os._exit(0)   # finishes the forward, then leaves without sending its backward inputs
+        dq, dk, dv = proto.backward(_grad_out()[:, rows])
+        for nm, t in (("dq", dq), ("dk", dk), ("dv", dv)):
+            np.save(os.path.join(out_dir, f"{nm}{rank}.npy"), t.numpy())
     except Exception as e:  # noqa: BLE001 - the failure test inspects it
         with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as f:
             f.write(repr(e))
     finally:
-        if mode != "die":
+        if not mode.startswith("die"):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,groups,mode", [(2, 1, "even"), (3, 2, "even"), (3, 2, "balanced")])
+@pytest.mark.parametrize("world,groups,mode", [(2, 1, "even"), (3, 2, "even"), (3, 2, "balanced"),
+                                               (4, 2, "train")])
 def test_cp_protocol_matches_oracle(tmp_path, world, groups, mode):
-    from oracle.lucid_oracle import lucid_fwd
+    """Forward and backward chains on gloo ranks: the gathered O, dQ, dK, dV equal
+    the float64 oracle on the whole sequence."""
+    from oracle.lucid_oracle import lucid_bwd, lucid_fwd
     port = _free_port()
     mp.start_processes(_worker, args=(world, port, groups, mode, str(tmp_path)), nprocs=world, start_method="spawn")
     for r in range(world):
         assert not (tmp_path / f"err{r}.txt").exists(), (tmp_path / f"err{r}.txt").read_text()
     o = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=1)
-    q, k, v = _inputs()
-    ref = lucid_fwd(q.numpy(), k.numpy(), v.numpy(), SEQ["D"] ** -0.5, 1e-5)[0]
+    q, k, v = (t.numpy() for t in _inputs())
+    ref = lucid_fwd(q, k, v, SEQ["D"] ** -0.5, 1e-5)[0]
     np.testing.assert_allclose(o, ref, rtol=1e-10, atol=1e-10)
+    dq, dk, dv = lucid_bwd(q, k, v, _grad_out().numpy(), SEQ["D"] ** -0.5, 1e-5)
+    for nm, r_ in (("dq", dq), ("dk", dk), ("dv", dv)):
+        got = np.concatenate([np.load(tmp_path / f"{nm}{r}.npy") for r in range(world)], axis=2)
+        np.testing.assert_allclose(got, r_, rtol=1e-9, atol=1e-9, err_msg=nm)
 
 
-def test_cp_protocol_reports_a_dead_peer(tmp_path):
+@pytest.mark.parametrize("mode,dead,waiting", [("die", 0, 1), ("die_bwd", 1, 0)])
+def test_cp_protocol_reports_a_dead_peer(tmp_path, mode, dead, waiting):
+    """A rank that leaves (before the forward's keys, or after the forward but
+    before the backward's messages) makes its peer's next receive end with an
+    error (the process group timeout is 10 s) instead of hanging."""
     port = _free_port()
-    ctx = mp.start_processes(_worker, args=(2, port, 1, "die", str(tmp_path)), nprocs=2, start_method="spawn",
+    ctx = mp.start_processes(_worker, args=(2, port, 1, mode, str(tmp_path)), nprocs=2, start_method="spawn",
                              join=False)
-    # rank 0 exits at once; rank 1's receive must end with an error (the process
-    # group timeout is 10 s), not hang
     import time
     deadline = time.time() + 120
     while any(p.is_alive() for p in ctx.processes) and time.time() < deadline:
@@ -93,7 +116,7 @@ def test_cp_protocol_reports_a_dead_peer(tmp_path):
     for p in hung:
         p.kill()
     assert not hung, "a rank hung after its peer died"
-    assert (tmp_path / "err1.txt").exists()
+    assert (tmp_path / f"err{waiting}.txt").exists()
 
 
 def test_balanced_bounds_equalise_causal_work():
@@ -146,6 +169,39 @@ class _NullBackend:
     def finish(self):
         return None
 
+    def set_grad(self, do):
+        pass
+
+    def empty_grad_inputs(self, j):
+        return [None, None]
+
+    def own_grad_inputs(self):
+        return [None, None]
+
+    def store_grad_inputs(self, j, bufs):
+        pass
+
+    def prep_later(self):
+        pass
+
+    def attn_col(self, g):
+        pass
+
+    def store_dv(self, g, j, buf):
+        pass
+
+    def solve_col(self, g):
+        pass
+
+    def own_dv(self, g):
+        return None
+
+    def rows(self, g):
+        pass
+
+    def finish_grad(self):
+        return None
+
 
 def _schedule(rank, world, G):
     """The point-to-point operations rank `rank` issues, in issue order."""
@@ -156,13 +212,14 @@ def _schedule(rank, world, G):
     proto._send = lambda t, j: (ops.append(("send", j)), _Req())[1]
     proto._recv = lambda t, j: (ops.append(("recv", j)), _Req())[1]
     proto.run(None, None, None)
+    proto.backward(None)
     return ops
 
 
 @pytest.mark.parametrize("world", [2, 3, 4, 8])
 @pytest.mark.parametrize("G", [1, 2, 8])
 def test_cp_schedule_cannot_deadlock_even_fully_serialised(world, G):
-    """Worst case for NCCL point-to-point: every rank runs all of its sends and
+    """Forward then backward chain.  Worst case for NCCL point-to-point: every rank runs all of its sends and
     receives strictly in issue order (one queue per rank, as a single eager
     communicator does).  A send and a receive complete together when each is
     at the head of its rank's queue; the whole schedule must drain."""

@@ -1,7 +1,15 @@
-"""Context-parallel LUCID forward (lucid_b200/cp.py) on real GPUs over NCCL:
-two ranks each own half of the sequence; the gathered output must match the
-float64 oracle like the single-GPU op does.  Needs at least two GPUs (skipped
-otherwise)."""
+"""Context-parallel LUCID attention (lucid_b200/cp.py) on the B200 kernels.
+
+* loopback (one GPU): W ranks run one after another in one process, the
+  forward in rank order and the backward in reverse rank order, their
+  messages passed through an in-process mailbox.  Every dependency of the
+  chain points from an earlier-run rank to a later-run one, and the kernels
+  never wait on another launch, so this runs the partial-range kernels and
+  the whole protocol without a second GPU.
+* two GPUs over NCCL (skipped with fewer GPUs).
+The gathered output and gradients must match the float64 oracle like the
+single-GPU op does, and the single-GPU op itself closely (same kernels, same
+accumulation order)."""
 import os
 import socket
 
@@ -31,6 +39,82 @@ def _inputs():
     return q, k, v
 
 
+def _grad_out():
+    import torch
+    g = torch.Generator().manual_seed(18)
+    B, Hq, N, D = (CASE[k] for k in ("B", "Hq", "N", "D"))
+    return torch.randn(B, N, Hq, D, generator=g).bfloat16()
+
+
+def _check_against_oracle(o, dq, dk, dv):
+    from oracle.lucid_oracle import lucid_fwd_bwd
+    q, k, v = (t.double().numpy() for t in _inputs())
+    ro, rdq, rdk, rdv = lucid_fwd_bwd(q, k, v, _grad_out().double().numpy(), CASE["D"] ** -0.5, 1e-5)
+    for nm, got, ref in (("o", o, ro), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        assert np.all(np.isfinite(got)), nm
+        err = np.abs(got - ref) - (1e-2 + 2.0 ** -8 * np.abs(ref))
+        assert err.max() <= 0, f"{nm}: max err {np.abs(got - ref).max():.3e}"
+
+
+class _Req:
+    def __init__(self, fn=None):
+        self.fn = fn
+
+    def wait(self):
+        if self.fn:
+            self.fn()
+
+
+def test_cp_loopback_fwd_bwd_matches_oracle_and_single_gpu(cuda_device):
+    """Three ranks with unequal chunks (train_bounds) and two head groups."""
+    import torch
+    from lucid_b200.cp import ChunkProtocol, KernelBackend, train_bounds
+    from lucid_b200.ops import lucid_attention
+    q, k, v = _inputs()
+    do = _grad_out()
+    B, Hq, H, N, D = (CASE[x] for x in ("B", "Hq", "H", "N", "D"))
+    W = 3
+    bounds = train_bounds(N, W)
+    assert len(set(bounds[r + 1] - bounds[r] for r in range(W))) > 1
+    mail = {}
+    protos = []
+    for r in range(W):
+        be = KernelBackend(B, H, Hq, bounds, D, D ** -0.5, 1e-5, r, W, CASE["groups"], cuda_device)
+        pr = ChunkProtocol.__new__(ChunkProtocol)
+        pr.be, pr.group, pr.rank, pr.world = be, None, r, W
+
+        def send(t, j, r=r):
+            mail.setdefault((r, j), []).append(t.clone())
+            return _Req()
+
+        def recv(t, j, r=r):
+            box = mail[(j, r)]   # the sender ran first, so its message is queued
+            return _Req(lambda: t.copy_(box.pop(0)))
+        pr._send, pr._recv = send, recv
+        protos.append(pr)
+    dev = cuda_device
+    outs = {}
+    for r in range(W):
+        rows = slice(bounds[r], bounds[r + 1])
+        outs[r] = protos[r].run(q[:, :, rows].to(dev), k[:, :, rows].to(dev), v[:, :, rows].to(dev))
+    grads = {}
+    for r in reversed(range(W)):
+        rows = slice(bounds[r], bounds[r + 1])
+        grads[r] = protos[r].backward(do[:, rows].to(dev))
+    torch.cuda.synchronize()
+    assert not any(mail.values()), "unconsumed messages"
+    o = torch.cat([outs[r] for r in range(W)], 1).float().cpu().numpy()
+    dq, dk, dv = (torch.cat([grads[r][i] for r in range(W)], 2).float().cpu().numpy() for i in range(3))
+    _check_against_oracle(o, dq, dk, dv)
+    # the single-GPU op: same kernels, same accumulation order per block
+    qs, ks, vs = (t.to(dev).requires_grad_() for t in (q, k, v))
+    os_ = lucid_attention(qs, ks, vs)
+    os_.backward(do.to(dev))
+    for nm, got, ref in (("o", o, os_), ("dq", dq, qs.grad), ("dk", dk, ks.grad), ("dv", dv, vs.grad)):
+        ref = ref.detach().float().cpu().numpy()
+        assert np.abs(got - ref).max() <= 2.0 ** -7 * np.abs(ref).max(), (nm, float(np.abs(got - ref).max()))
+
+
 def _worker(rank, world, port, out_dir):
     import sys
     sys.path.insert(0, ROOT)
@@ -42,14 +126,17 @@ def _worker(rank, world, port, out_dir):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
-        from lucid_b200.cp import cp_lucid_attention_forward
+        from lucid_b200.cp import cp_lucid_attention
         q, k, v = _inputs()
         C = CASE["N"] // world
         rows = slice(rank * C, (rank + 1) * C)
-        o = cp_lucid_attention_forward(q[:, :, rows].to(dev), k[:, :, rows].to(dev), v[:, :, rows].to(dev),
-                                       head_groups=CASE["groups"])
+        qs, ks, vs = (t[:, :, rows].to(dev).requires_grad_() for t in (q, k, v))
+        o = cp_lucid_attention(qs, ks, vs, head_groups=CASE["groups"])
+        o.backward(_grad_out()[:, rows].to(dev))
         torch.cuda.synchronize()
-        np.save(os.path.join(out_dir, f"o{rank}.npy"), o.float().cpu().numpy())
+        np.save(os.path.join(out_dir, f"o{rank}.npy"), o.detach().float().cpu().numpy())
+        for nm, t in (("dq", qs), ("dk", ks), ("dv", vs)):
+            np.save(os.path.join(out_dir, f"{nm}{rank}.npy"), t.grad.float().cpu().numpy())
     except Exception as e:  # noqa: BLE001
         with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as f:
             f.write(repr(e))
@@ -57,19 +144,16 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_cp_forward_two_gpus_matches_oracle(tmp_path):
+def test_cp_fwd_bwd_two_gpus_matches_oracle(tmp_path):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
-    from oracle.lucid_oracle import lucid_fwd
     world = 2
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
     for r in range(world):
         assert not (tmp_path / f"err{r}.txt").exists(), (tmp_path / f"err{r}.txt").read_text()
     o = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=1)
-    q, k, v = (t.double().numpy() for t in _inputs())
-    ref = lucid_fwd(q, k, v, CASE["D"] ** -0.5, 1e-5)[0]
-    assert np.all(np.isfinite(o))
-    err = np.abs(o - ref) - (1e-2 + 2.0 ** -8 * np.abs(ref))
-    assert err.max() <= 0, np.abs(o - ref).max()
+    dq, dk, dv = (np.concatenate([np.load(tmp_path / f"{nm}{r}.npy") for r in range(world)], axis=2)
+                  for nm in ("dq", "dk", "dv"))
+    _check_against_oracle(o, dq, dk, dv)
