@@ -12,7 +12,13 @@
  *   - "Internal" tensors are contiguous [B, H, Npad, D] (or [B, H, Npad])
  *     buffers with Npad = lucid_padded_len(N); the library owns their
  *     contents, the caller owns their memory.
- *   - D must be 128 (the tensor-core head dimension of this build).
+ *   - D is the head dimension, 1 <= D <= 128.  lucid_solve_*, lucid_attn_*
+ *     and lucid_cp_*: every row holds 128 elements (the tensor-core width of
+ *     this build) and a smaller head dimension is zero-padded to 128 by the
+ *     caller (columns D..127 zero); D enters only the RMS mean of K^ (the
+ *     mean over D, not 128).  lucid_decode_*: rows hold D elements, D a
+ *     multiple of 4 (no padding).  lucid_path_*: D = 128 (zero-pad smaller
+ *     head dimensions: the Householder products act as the identity there).
  *   - Hq must be a multiple of Hkv (grouped-query attention).
  *   - Every call is asynchronous on `stream` (a cudaStream_t, 0 = legacy
  *     default stream), performs no host synchronisation and allocates no

@@ -17,7 +17,7 @@ KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bw
               "solve_bwd_row": 7, "path_block": 8, "path_scores": 9, "path_solve": 10, "path_solve_t": 11,
               "path_row": 12, "path_col": 13, "path_attn": 14, "decode": 15}
 ERRORS = {
-    1: "unsupported shape (head_dim must be 128, Hq a multiple of Hkv)",
+    1: "unsupported shape (head_dim at most 128, Hq a multiple of Hkv)",
     2: "pointer or stride not 16-byte aligned",
     3: "workspace missing or too small",
     4: "TMA descriptor creation failed",

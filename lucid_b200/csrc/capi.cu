@@ -23,7 +23,7 @@ cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const 
                                   const float* dk_row, const float* dk_add, bf16* dk, long long dk_sb,
                                   long long dk_sh, long long dk_sn, bf16* dv, long long dv_sb,
                                   long long dv_sh, long long dv_sn, cudaStream_t st, int row0 = 0,
-                                  int row1 = -1);
+                                  int row1 = -1, int D = kHeadDim);
 }  // namespace lb
 
 using namespace lb;
@@ -43,8 +43,10 @@ int nb_of(int N) { return (N + 127) / 128; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool strides_ok(int64_t a, int64_t b, int64_t c) { return (a % 8 == 0) && (b % 8 == 0) && (c % 8 == 0); }
 
+// D is the logical head dimension (1..128); rows always hold 128 elements, the
+// columns from D on zero (a smaller head dimension is zero-padded by the caller).
 bool shape_ok(int B, int Hq, int Hkv, int N, int D) {
-  return B >= 0 && Hq >= 0 && Hkv >= 0 && N >= 0 && D == kHeadDim &&
+  return B >= 0 && Hq >= 0 && Hkv >= 0 && N >= 0 && D >= 1 && D <= kHeadDim &&
          (Hkv == 0 || Hq % Hkv == 0) && (Hkv > 0 || Hq == 0) && N <= (1 << 30);
 }
 bool empty_problem(int B, int Hq, int Hkv, int N) { return B == 0 || Hq == 0 || Hkv == 0 || N == 0; }
@@ -121,7 +123,7 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
 
   PrepArgs pa{};
   pa.B = B; pa.H = H; pa.N = N; pa.NB = NB; pa.Npad = Npad;
-  pa.s = scale; pa.eps = eps;
+  pa.s = scale; pa.eps = eps; pa.D = D;
   pa.k = static_cast<const bf16*>(k); pa.k_sb = k_sb; pa.k_sh = k_sh; pa.k_sn = k_sn;
   pa.khat = static_cast<bf16*>(khat); pa.rstd = rstd; pa.dinv = dinv; pa.u = static_cast<bf16*>(u);
   {
@@ -302,7 +304,7 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   return to_status(launch_solve_finalize(
       B, H, N, Npad, scale, static_cast<const bf16*>(k), k_sb, k_sh, k_sn, rstd, dinv,
       static_cast<const bf16*>(x), dv_int, dk_col, dk_row, dk_add, static_cast<bf16*>(dk), dk_sb, dk_sh,
-      dk_sn, static_cast<bf16*>(dv), dv_sb, dv_sh, dv_sn, st));
+      dk_sn, static_cast<bf16*>(dv), dv_sb, dv_sh, dv_sn, st, 0, -1, D));
 }
 
 }  // extern "C"
@@ -362,7 +364,7 @@ extern "C" int lucid_cp_prep(int B, int H, int N, int D, float scale, float eps,
     return LUCID_ERR_ALIGN;
   PrepArgs pa{};
   pa.B = B; pa.H = H; pa.N = N; pa.NB = NB; pa.Npad = npad_of(N);
-  pa.s = scale; pa.eps = eps;
+  pa.s = scale; pa.eps = eps; pa.D = D;
   pa.k = static_cast<const bf16*>(k); pa.k_sb = k_sb; pa.k_sh = k_sh; pa.k_sn = k_sn;
   pa.khat = static_cast<bf16*>(khat); pa.rstd = rstd; pa.dinv = dinv; pa.u = static_cast<bf16*>(u);
   pa.blk0 = blk_lo; pa.blk1 = blk_hi; pa.khat_only = khat_only;
@@ -530,7 +532,7 @@ extern "C" int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int b
         B, H, N, Npad, scale, static_cast<const bf16*>(k), k_sb, k_sh, k_sn, rstd, dinv,
         static_cast<const bf16*>(x), static_cast<const bf16*>(dv_int), dk_col, dk_row, dk_add,
         static_cast<bf16*>(dk), dk_sb, dk_sh, dk_sn, static_cast<bf16*>(dv), dv_sb, dv_sh, dv_sn, st,
-        blk_lo * 128, row_hi));
+        blk_lo * 128, row_hi, D));
   }
   return LUCID_OK;
 }

@@ -31,7 +31,7 @@ int lucid_decode_update(int B, int H, int Ln, int Nc, int D, float scale, float 
                         const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
                         void* x_new, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                         void* workspace, size_t workspace_bytes, void* stream) {
-  if (B < 0 || H < 0 || Ln < 0 || Nc < 0 || D != kHeadDim) return LUCID_ERR_SHAPE;
+  if (B < 0 || H < 0 || Ln < 0 || Nc < 0 || D < 4 || D > kHeadDim || D % 4) return LUCID_ERR_SHAPE;
   if (B == 0 || H == 0 || Ln == 0) return LUCID_OK;
   if (!a8(k_new) || !a8(k_cache) || !a8(x_cache) || !s4(kn_sb, kn_sh, kn_sn) || !s4(kc_sb, kc_sh, kc_sn) ||
       !s4(xc_sb, xc_sh, xc_sn))
@@ -44,7 +44,7 @@ int lucid_decode_update(int B, int H, int Ln, int Nc, int D, float scale, float 
                static_cast<const bf16*>(k_cache), kc_sb, kc_sh, kc_sn,
                static_cast<const bf16*>(x_cache), xc_sb, xc_sh, xc_sn,
                static_cast<bf16*>(x_new), o_sb, o_sh, o_sn,
-               reinterpret_cast<float*>(static_cast<char*>(workspace) + 256), H};
+               reinterpret_cast<float*>(static_cast<char*>(workspace) + 256), H, D};
   ProfileScope ps(LUCID_KERNEL_DECODE, reinterpret_cast<cudaStream_t>(stream));
   return launch_decode(a, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? LUCID_OK : LUCID_ERR_LAUNCH;
 }
@@ -60,7 +60,8 @@ int lucid_decode_attn(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale
                       const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
                       void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                       void* workspace, size_t workspace_bytes, void* stream) {
-  if (B < 0 || Hq < 0 || Hkv <= 0 || Ln < 0 || Nc < Ln || D != kHeadDim || Hq % Hkv != 0) return LUCID_ERR_SHAPE;
+  if (B < 0 || Hq < 0 || Hkv <= 0 || Ln < 0 || Nc < Ln || D < 4 || D > kHeadDim || D % 4 || Hq % Hkv != 0)
+    return LUCID_ERR_SHAPE;
   if (B == 0 || Hq == 0 || Ln == 0) return LUCID_OK;
   if (!a8(k_cache) || !a8(x_cache) || !s4(kc_sb, kc_sh, kc_sn) || !s4(xc_sb, xc_sh, xc_sn)) return LUCID_ERR_ALIGN;
   if (workspace == nullptr || workspace_bytes < lucid_decode_attn_workspace_bytes(B, Hq, Ln, Nc, D) ||
@@ -72,7 +73,7 @@ int lucid_decode_attn(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale
                static_cast<const bf16*>(k_cache), kc_sb, kc_sh, kc_sn,
                static_cast<const bf16*>(x_cache), xc_sb, xc_sh, xc_sn,
                static_cast<bf16*>(o), o_sb, o_sh, o_sn,
-               reinterpret_cast<float*>(static_cast<char*>(workspace) + 256), Hq};
+               reinterpret_cast<float*>(static_cast<char*>(workspace) + 256), Hq, D};
   ProfileScope ps(LUCID_KERNEL_DECODE, reinterpret_cast<cudaStream_t>(stream));
   return launch_decode_attn(a, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? LUCID_OK : LUCID_ERR_LAUNCH;
 }

@@ -865,7 +865,7 @@ __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o
 
 // Solve backward finalize, one warp per row (row < N):
 //   dk^  = dk_col + dk_row + 2 dG_rr k^_r,  dG_rr = -s P_rr (dV_r . X_r)
-//   dK   = rstd (dk^ - (k^.dk^ / D) k^) + dk_add        (RMSNorm backward)
+//   dK   = rstd (dk^ - (k^.dk^ / D) k^) + dk_add        (RMSNorm backward; D the logical head dim)
 //   dV   = copy of the internal bf16 dV
 __global__ void lucid_solve_finalize_kernel(int B, int H, int N, int Npad, float s, const bf16* k,
                                             long long k_sb, long long k_sh, long long k_sn,
@@ -874,7 +874,7 @@ __global__ void lucid_solve_finalize_kernel(int B, int H, int N, int Npad, float
                                             const float* dk_row, const float* dk_add, bf16* dk,
                                             long long dk_sb, long long dk_sh, long long dk_sn, bf16* dv,
                                             long long dv_sb, long long dv_sh, long long dv_sn, int row0,
-                                            int nrows) {
+                                            int nrows, float inv_d) {
   const int warps = blockDim.x >> 5;
   const long long gw = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -913,7 +913,7 @@ __global__ void lucid_solve_finalize_kernel(int B, int H, int N, int Npad, float
   float proj = kh[0] * g[0] + kh[1] * g[1] + kh[2] * g[2] + kh[3] * g[3];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) proj += __shfl_xor_sync(0xffffffffu, proj, o);
-  proj *= (1.0f / kHeadDim);
+  proj *= inv_d;
   float outk[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) outk[e] = rs * (g[e] - proj * kh[e]);
@@ -997,7 +997,8 @@ cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const 
                                   const bf16* x, const bf16* dv_int, const float* dk_col,
                                   const float* dk_row, const float* dk_add, bf16* dk, long long dk_sb,
                                   long long dk_sh, long long dk_sn, bf16* dv, long long dv_sb,
-                                  long long dv_sh, long long dv_sn, cudaStream_t st, int row0, int row1) {
+                                  long long dv_sh, long long dv_sn, cudaStream_t st, int row0, int row1,
+                                  int D) {
   if (row1 < 0) row1 = N;
   const long long warps = (long long)B * H * (row1 - row0);
   if (warps <= 0) return cudaSuccess;
@@ -1005,7 +1006,7 @@ cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const 
   lucid_solve_finalize_kernel<<<blocks, 256, 0, st>>>(B, H, N, Npad, s, k, k_sb, k_sh, k_sn, rstd, dinv,
                                                       x, dv_int, dk_col, dk_row, dk_add, dk, dk_sb,
                                                       dk_sh, dk_sn, dv, dv_sb, dv_sh, dv_sn, row0,
-                                                      row1 - row0);
+                                                      row1 - row0, 1.0f / (float)D);
   return cudaGetLastError();
 }
 

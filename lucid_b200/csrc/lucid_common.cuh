@@ -24,6 +24,9 @@ struct PrepArgs {
   // block range [blk0, blk1) (blk1 == 0: NB); khat_only: row statistics and k^ only
   // (blocks whose solve runs elsewhere, e.g. another rank's chunk of the sequence)
   int blk0 = 0, blk1 = 0, khat_only = 0;
+  // logical head dimension of the RMS mean (rows hold 128 elements; a smaller head
+  // dimension is zero-padded to 128)
+  int D = kHeadDim;
 };
 
 // Forward tile engine (solve or attention).
@@ -83,6 +86,7 @@ struct DecodeArgs {
   bf16* out; long long o_sb, o_sh, o_st;
   float* part;                                     // per-split partial sums
   int Hq;                                          // attention: query heads (H = kv heads)
+  int D = kHeadDim;                                // logical head dimension of the RMS mean
 };
 
 }  // namespace lb

@@ -27,6 +27,12 @@ __device__ __forceinline__ float4 ld_bf16x4(const bf16* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// four elements of a row whose head dimension is D (a multiple of 4): lanes past
+// D read nothing and return zeros
+__device__ __forceinline__ float4 ld_bf16x4_d(const bf16* p, bool act) {
+  return act ? ld_bf16x4(p) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -44,14 +50,15 @@ __global__ void __launch_bounds__(256) lucid_decode_partial_kernel(const DecodeA
   const int r1 = min(a.Nc, r0 + a.rows_per_split);
   const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh + lane * 4;
   const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh + lane * 4;
+  const bool act = lane * 4 < a.D;
   for (int t0 = 0; t0 < a.Ln; t0 += kDecTok) {
     const int nt = min(kDecTok, a.Ln - t0);
     __syncthreads();
     if (warp < nt) {  // RMSNorm of new token t0 + warp
-      const float4 k4 = ld_bf16x4(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
-                                  (long long)(t0 + warp) * a.kn_st + lane * 4);
+      const float4 k4 = ld_bf16x4_d(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
+                                    (long long)(t0 + warp) * a.kn_st + lane * 4, act);
       const float ss = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
-      const float r = rsqrtf(ss * (1.f / 128.f) + a.eps);
+      const float r = rsqrtf(ss * (1.f / (float)a.D) + a.eps);
       khn[warp][lane * 4 + 0] = k4.x * r;
       khn[warp][lane * 4 + 1] = k4.y * r;
       khn[warp][lane * 4 + 2] = k4.z * r;
@@ -67,9 +74,9 @@ __global__ void __launch_bounds__(256) lucid_decode_partial_kernel(const DecodeA
 #pragma unroll
     for (int t = 0; t < kDecTok; ++t) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int row = r0 + warp; row < r1; row += 8) {
-      const float4 k4 = ld_bf16x4(kbase + (long long)row * a.kc_st);
-      const float4 x4 = ld_bf16x4(xbase + (long long)row * a.xc_st);
-      const float rs = rsqrtf(warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w) * (1.f / 128.f) + a.eps);
+      const float4 k4 = ld_bf16x4_d(kbase + (long long)row * a.kc_st, act);
+      const float4 x4 = ld_bf16x4_d(xbase + (long long)row * a.xc_st, act);
+      const float rs = rsqrtf(warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w) * (1.f / (float)a.D) + a.eps);
 #pragma unroll
       for (int t = 0; t < kDecTok; ++t) {
         if (t < nt) {
@@ -105,6 +112,7 @@ __global__ void lucid_decode_finish_kernel(const DecodeArgs a) {
   const int l = (int)(row % a.Ln);
   const long long bh = row / a.Ln;
   const int b = (int)(bh / a.H), h = (int)(bh % a.H);
+  if (c >= a.D) return;
   float sum = 0.f;
   for (int sp = 0; sp < a.nsplit; ++sp) sum += a.part[(((long long)sp * a.B * a.H + bh) * a.Ln + l) * 128 + c];
   const float v = __bfloat162float(a.vn[(long long)b * a.vn_sb + (long long)h * a.vn_sh + (long long)l * a.vn_st + c]);
@@ -157,13 +165,15 @@ __global__ void __launch_bounds__(256) lucid_decode_attn_partial_kernel(const De
   const int r1 = min(a.Nc, r0 + a.rows_per_split);
   const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh + lane * 4;
   const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh + lane * 4;
+  const bool act = lane * 4 < a.D;
   for (int t0 = 0; t0 < a.Ln; t0 += kDecTok) {
     const int nt = min(kDecTok, a.Ln - t0);
     __syncthreads();
     for (int e = threadIdx.x; e < nt * 128; e += blockDim.x) {
       const int t = e >> 7, c = e & 127;
-      qs[t][c] = __bfloat162float(a.kn[(long long)b * a.kn_sb + (long long)hq * a.kn_sh +
-                                       (long long)(t0 + t) * a.kn_st + c]) * sm;
+      qs[t][c] = c < a.D ? __bfloat162float(a.kn[(long long)b * a.kn_sb + (long long)hq * a.kn_sh +
+                                                 (long long)(t0 + t) * a.kn_st + c]) * sm
+                         : 0.f;
     }
     __syncthreads();
     float4 q[kDecTok], acc[kDecTok];
@@ -177,8 +187,8 @@ __global__ void __launch_bounds__(256) lucid_decode_attn_partial_kernel(const De
       l[t] = 0.f;
     }
     for (int row = r0 + warp; row < r1; row += 8) {
-      const float4 k4 = ld_bf16x4(kbase + (long long)row * a.kc_st);
-      const float4 x4 = ld_bf16x4(xbase + (long long)row * a.xc_st);
+      const float4 k4 = ld_bf16x4_d(kbase + (long long)row * a.kc_st, act);
+      const float4 x4 = ld_bf16x4_d(xbase + (long long)row * a.xc_st, act);
 #pragma unroll
       for (int t = 0; t < kDecTok; ++t) {
         if (t < nt && row <= a.Nc - a.Ln + t0 + t) {
@@ -236,6 +246,7 @@ __global__ void lucid_decode_attn_finish_kernel(const DecodeArgs a) {
   const int l = (int)(row % a.Ln);
   const long long bq = row / a.Ln;
   const int b = (int)(bq / a.Hq), hq = (int)(bq % a.Hq);
+  if (c >= a.D) return;
   float M = -INFINITY;
   for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, a.part[(((long long)sp * a.B * a.Hq + bq) * a.Ln + l) * 130 + 128]);
   float L = 0.f, S = 0.f;

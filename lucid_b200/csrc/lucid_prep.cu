@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) lucid_prep_kernel(PrepArgs p) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const bool valid = row < p.N;
-    const float r = valid ? 1.0f / sqrtf(ss * (1.0f / kHeadDim) + p.eps) : 0.f;
+    const float r = valid ? 1.0f / sqrtf(ss * (1.0f / (float)p.D) + p.eps) : 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) kf[rr * kLD + lane * 4 + e] = v[e] * r;
     uint2 outv;

@@ -16,7 +16,12 @@ Autograd functions:
 
 All tensors are [B, H, N, D] (any strides with a unit innermost stride);
 the attention output is returned as [B, N, Hq, D] like the reference
-(modeling_lucid.py:546).  There is no CPU path: CPU tensors raise.
+(modeling_lucid.py:546).  Head dimensions below 128 (e.g. the 68 of the
+reference's lucid/config) are zero-padded to the kernels' 128 columns inside
+the autograd functions and sliced back; zero columns change neither the
+scores nor the solve, and the kernels take the true D for the RMS mean of
+K^.  The stage functions take padded 128-column tensors and the true head
+dimension as ``d``.  There is no CPU path: CPU tensors raise.
 """
 from __future__ import annotations
 
@@ -50,6 +55,13 @@ def _prep(t: torch.Tensor, name: str) -> torch.Tensor:
     return t if ok else t.contiguous()
 
 
+def _pad128(t: torch.Tensor) -> torch.Tensor:
+    d = t.shape[-1]
+    if d > 128:
+        raise ValueError(f"head dimension {d} > 128 is not supported")
+    return t if d == 128 else torch.nn.functional.pad(t, (0, 128 - d))
+
+
 def _s3(t: torch.Tensor):
     return t.stride(0), t.stride(1), t.stride(2)
 
@@ -61,19 +73,20 @@ def _ws(nbytes: int, device) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 # stages
 # ---------------------------------------------------------------------------
-def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float):
+def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int | None = None):
     """X = P^-1 V.  Returns (x_int, khat, u, rstd, dinv); x_int is
-    [B, H, Npad, D] (rows >= N are padding)."""
+    [B, H, Npad, 128] (rows >= N are padding)."""
     lib = _lib.load()
     k = _prep(k, "key")
     v = _prep(v, "value")
-    B, H, N, D = k.shape
+    B, H, N, W = k.shape
+    D = W if d is None else d
     if v.shape != k.shape:
         raise ValueError(f"key {tuple(k.shape)} and value {tuple(v.shape)} must match")
     Np = padded_len(N)
     dev = k.device
-    x = torch.empty(B, H, Np, D, dtype=torch.bfloat16, device=dev)
-    khat = torch.empty(B, H, Np, D, dtype=torch.bfloat16, device=dev)
+    x = torch.empty(B, H, Np, W, dtype=torch.bfloat16, device=dev)
+    khat = torch.empty(B, H, Np, W, dtype=torch.bfloat16, device=dev)
     u = torch.empty(B, H, Np, 128, dtype=torch.bfloat16, device=dev)
     rstd = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
     dinv = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
@@ -85,18 +98,19 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float):
     return x, khat, u, rstd, dinv
 
 
-def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float):
-    """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,D], lse)."""
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float, d: int | None = None):
+    """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,128], lse)."""
     lib = _lib.load()
     q = _prep(q, "query")
     k = _prep(k, "key")
-    B, Hq, N, D = q.shape
+    B, Hq, N, W = q.shape
+    D = W if d is None else d
     Hkv = k.shape[1]
     Np = padded_len(N)
-    if k.shape != (B, Hkv, N, D) or x_int.shape != (B, Hkv, Np, D) or not x_int.is_contiguous():
+    if k.shape != (B, Hkv, N, W) or x_int.shape != (B, Hkv, Np, W) or not x_int.is_contiguous():
         raise ValueError("attn_fwd: inconsistent shapes")
     dev = q.device
-    o = torch.empty(B, N, Hq, D, dtype=torch.bfloat16, device=dev)
+    o = torch.empty(B, N, Hq, W, dtype=torch.bfloat16, device=dev)
     ot = o.transpose(1, 2)
     lse = torch.empty(B, Hq, Np, dtype=torch.float32, device=dev)
     ws = _ws(lib.lucid_attn_fwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
@@ -107,21 +121,22 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float
     return o, lse
 
 
-def attn_bwd(q, k, x_int, o, do, lse, scale: float):
-    """Backward of attn_fwd.  o, do are [B,N,Hq,D].  Returns
-    (dq [B,Hq,N,D] bf16, dk_f32 [B,Hkv,Npad,D], dx_f32 [B,Hkv,Npad,D])."""
+def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
+    """Backward of attn_fwd.  o, do are [B,N,Hq,128].  Returns
+    (dq [B,Hq,N,128] bf16, dk_f32 [B,Hkv,Npad,128], dx_f32 [B,Hkv,Npad,128])."""
     lib = _lib.load()
     q = _prep(q, "query")
     k = _prep(k, "key")
     ot = _prep(o.transpose(1, 2), "attn_output")
     dot = _prep(do.transpose(1, 2), "grad_output")
-    B, Hq, N, D = q.shape
+    B, Hq, N, W = q.shape
+    D = W if d is None else d
     Hkv = k.shape[1]
     Np = padded_len(N)
     dev = q.device
-    dq = torch.empty(B, Hq, N, D, dtype=torch.bfloat16, device=dev)
-    dk = torch.empty(B, Hkv, Np, D, dtype=torch.float32, device=dev)
-    dx = torch.empty(B, Hkv, Np, D, dtype=torch.float32, device=dev)
+    dq = torch.empty(B, Hq, N, W, dtype=torch.bfloat16, device=dev)
+    dk = torch.empty(B, Hkv, Np, W, dtype=torch.float32, device=dev)
+    dx = torch.empty(B, Hkv, Np, W, dtype=torch.float32, device=dev)
     ws = _ws(lib.lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
     rc = lib.lucid_attn_bwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), dot.data_ptr(),
@@ -131,14 +146,15 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float):
     return dq, dk, dx
 
 
-def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None):
-    """Backward of solve_fwd.  Returns (dk, dv) bf16 [B,H,N,D]."""
+def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None, d: int | None = None):
+    """Backward of solve_fwd.  Returns (dk, dv) bf16 [B,H,N,128]."""
     lib = _lib.load()
     k = _prep(k, "key")
-    B, H, N, D = k.shape
+    B, H, N, W = k.shape
+    D = W if d is None else d
     dev = k.device
-    dk = torch.empty(B, H, N, D, dtype=torch.bfloat16, device=dev)
-    dv = torch.empty(B, H, N, D, dtype=torch.bfloat16, device=dev)
+    dk = torch.empty(B, H, N, W, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty(B, H, N, W, dtype=torch.bfloat16, device=dev)
     ws = _ws(lib.lucid_solve_bwd_workspace_bytes(B, H, N, D), dev)
     rc = lib.lucid_solve_bwd(B, H, N, D, float(scale), k.data_ptr(), *_s3(k), x_int.data_ptr(),
                              khat.data_ptr(), u.data_ptr(), rstd.data_ptr(), dinv.data_ptr(),
@@ -157,20 +173,22 @@ class LucidSolveFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, key, value, scaling: float, eps: float):
-        k = _prep(key, "key")
-        x, khat, u, rstd, dinv = solve_fwd(k, value, scaling, eps)
+        D = key.shape[-1]
+        k = _prep(_pad128(key), "key")
+        x, khat, u, rstd, dinv = solve_fwd(k, _pad128(value), scaling, eps, d=D)
         ctx.save_for_backward(k, x, khat, u, rstd, dinv)
-        ctx.scaling = scaling
-        return x[:, :, : k.shape[2]]
+        ctx.scaling, ctx.d = scaling, D
+        return x[:, :, : k.shape[2], :D]
 
     @staticmethod
     def backward(ctx, gx):
         k, x, khat, u, rstd, dinv = ctx.saved_tensors
-        B, H, N, D = k.shape
-        dx = torch.zeros(B, H, x.shape[2], D, dtype=torch.float32, device=k.device)
-        dx[:, :, :N] = gx.float()
-        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, ctx.scaling)
-        return dk, dv, None, None
+        B, H, N, W = k.shape
+        D = ctx.d
+        dx = torch.zeros(B, H, x.shape[2], W, dtype=torch.float32, device=k.device)
+        dx[:, :, :N, :D] = gx.float()
+        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, ctx.scaling, d=D)
+        return dk[..., :D], dv[..., :D], None, None
 
 
 class LucidAttnFunction(torch.autograd.Function):
@@ -180,19 +198,20 @@ class LucidAttnFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, query, key, v_prime, scaling: float):
         B, Hkv, N, D = key.shape
-        x = torch.zeros(B, Hkv, padded_len(N), D, dtype=torch.bfloat16, device=key.device)
-        x[:, :, :N] = v_prime
-        o, lse = attn_fwd(query, key, x, scaling)
-        ctx.save_for_backward(query, key, x, o, lse)
-        ctx.scaling = scaling
-        return o
+        q, k = _pad128(query), _pad128(key)
+        x = torch.zeros(B, Hkv, padded_len(N), 128, dtype=torch.bfloat16, device=key.device)
+        x[:, :, :N, :D] = v_prime
+        o, lse = attn_fwd(q, k, x, scaling, d=D)
+        ctx.save_for_backward(q, k, x, o, lse)
+        ctx.scaling, ctx.d = scaling, D
+        return o[..., :D]
 
     @staticmethod
     def backward(ctx, do):
         q, k, x, o, lse = ctx.saved_tensors
-        N = k.shape[2]
-        dq, dk, dx = attn_bwd(q, k, x, o, do, lse, ctx.scaling)
-        return dq, dk[:, :, :N].to(torch.bfloat16), dx[:, :, :N].to(torch.bfloat16), None
+        N, D = k.shape[2], ctx.d
+        dq, dk, dx = attn_bwd(q, k, x, o, _pad128(do), lse, ctx.scaling, d=D)
+        return (dq[..., :D], dk[:, :, :N, :D].to(torch.bfloat16), dx[:, :, :N, :D].to(torch.bfloat16), None)
 
 
 class LucidAttentionFunction(torch.autograd.Function):
@@ -201,21 +220,24 @@ class LucidAttentionFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, query, key, value, scaling: float, eps: float):
-        k = _prep(key, "key")
-        q = _prep(query, "query")
-        x, khat, u, rstd, dinv = solve_fwd(k, value, scaling, eps)
-        o, lse = attn_fwd(q, k, x, scaling)
+        D = key.shape[-1]
+        k = _prep(_pad128(key), "key")
+        q = _prep(_pad128(query), "query")
+        x, khat, u, rstd, dinv = solve_fwd(k, _pad128(value), scaling, eps, d=D)
+        o, lse = attn_fwd(q, k, x, scaling, d=D)
         ctx.save_for_backward(q, k, x, khat, u, rstd, dinv, o, lse)
-        ctx.scaling = scaling
-        return o
+        ctx.scaling, ctx.d = scaling, D
+        return o if D == 128 else o[..., :D]
 
     @staticmethod
     def backward(ctx, do):
         q, k, x, khat, u, rstd, dinv, o, lse = ctx.saved_tensors
-        s = ctx.scaling
-        dq, dk_attn, dx = attn_bwd(q, k, x, o, do, lse, s)
-        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, s, dk_add=dk_attn)
-        return dq, dk, dv, None, None
+        s, D = ctx.scaling, ctx.d
+        dq, dk_attn, dx = attn_bwd(q, k, x, o, _pad128(do), lse, s, d=D)
+        dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, s, dk_add=dk_attn, d=D)
+        if D == 128:
+            return dq, dk, dv, None, None
+        return dq[..., :D], dk[..., :D], dv[..., :D], None, None
 
 
 def lucid_attention(query, key, value, scaling: float | None = None, eps: float = 1e-5):
@@ -241,8 +263,9 @@ def _prep_dec(t: torch.Tensor, name: str) -> torch.Tensor:
 def decode_update(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor, x_cache: torch.Tensor,
                   scale: float, eps: float = 1e-5) -> torch.Tensor:
     """get_new_v_prime (modeling_lucid.py:576-598): x_new = value -
-    exp(s k^ K^_cache^T - 1/s) X_cache, key/value [B,H,Ln,128], caches
-    [B,H,Nc,128] (raw keys, solved values).  Returns x_new [B,H,Ln,128]."""
+    exp(s k^ K^_cache^T - 1/s) X_cache, key/value [B,H,Ln,D], caches
+    [B,H,Nc,D] (raw keys, solved values; D <= 128 a multiple of 4, no
+    padding).  Returns x_new [B,H,Ln,D]."""
     lib = _lib.load()
     key, value = _prep_dec(key, "key"), _prep_dec(value, "value")
     key_cache, x_cache = _prep_dec(key_cache, "key_cache"), _prep_dec(x_cache, "value_cache")
@@ -261,9 +284,9 @@ def decode_update(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tenso
 def decode_attention(query: torch.Tensor, key_cache: torch.Tensor, x_cache: torch.Tensor,
                      scale: float) -> torch.Tensor:
     """softmax(s Q K^T + causal) X for Ln new queries at the end of the cache
-    (eager_lucid_attention_forward during decoding).  query [B,Hq,Ln,128],
-    caches [B,Hkv,Nc,128] already holding the new tokens.  Returns O as
-    [B, Ln, Hq, 128] like the reference (modeling_lucid.py:546)."""
+    (eager_lucid_attention_forward during decoding).  query [B,Hq,Ln,D],
+    caches [B,Hkv,Nc,D] already holding the new tokens (D <= 128 a multiple
+    of 4).  Returns O as [B, Ln, Hq, D] like the reference (modeling_lucid.py:546)."""
     lib = _lib.load()
     query = _prep_dec(query, "query")
     key_cache, x_cache = _prep_dec(key_cache, "key_cache"), _prep_dec(x_cache, "value_cache")

@@ -14,11 +14,13 @@ The forward and backward are the C-ABI entry points lucid_path_fwd /
 lucid_path_bwd (include/lucid_b200.h); the forward's workspace is the state
 saved for the backward.  There is no CPU path: CPU tensors raise.
 
-Differences from the reference, all raising instead of computing something
-else: head_dim must be 128 (the reference accepts 16/32/64/128, parallel.py:230);
-``g`` must be None (the reference asserts the same, :235).
-``cu_seqlens`` (packed variable-length batches, B == 1) runs one call per
-sequence.
+Head dimensions: 16, 32, 64 or 128 as in the reference (parallel.py:230-231).
+The kernels are 128 wide; a smaller head dimension is zero-padded to 128 and
+the outputs sliced back, which is exact: with zero columns in w every
+Householder H_t acts as the identity on them, so q, k and v stay zero there
+and the scores are unchanged.  ``g`` must be None (the reference asserts the
+same, :235).  ``cu_seqlens`` (packed variable-length batches, B == 1) runs
+one call per sequence.
 """
 from __future__ import annotations
 
@@ -147,6 +149,13 @@ class ParallelLUCIDPathAttentionFunction(torch.autograd.Function):
         return dq, dk, dv, dw, dbeta, None, None, None, None
 
 
+_HEAD_DIMS = (16, 32, 64, 128)
+
+
+def _pad128(t):
+    return t if t.shape[-1] == 128 else torch.nn.functional.pad(t, (0, 128 - t.shape[-1]))
+
+
 def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_seqlens=None, use_cache=False):
     """Drop-in for lucid_path/triton_code/parallel.py:180-241; returns (o, k_cache).
     k_cache is None unless use_cache (then the keys transformed by every later
@@ -156,6 +165,8 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
         q = k
     if scale is None:
         scale = k.shape[-1] ** -0.5
+    if q.shape[-1] not in _HEAD_DIMS or v.shape[-1] not in _HEAD_DIMS:
+        raise ValueError("only support head_dim in [16, 32, 64, 128]")
     if q.shape[-1] != k.shape[-1]:
         raise ValueError("q, k should have the same head_dim.")
     if k.shape != w.shape:
@@ -166,6 +177,12 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
         raise NotImplementedError("g is not supported")
     if q.shape[-2] % k.shape[-2] != 0:
         raise ValueError("the number of query heads should be divisible by the number of key heads")
+    K, V = k.shape[-1], v.shape[-1]
+    if K < 128 or V < 128:
+        o, kc = parallel_lucid_path_attention(_pad128(k), _pad128(v), _pad128(w), beta,
+                                              q=None if q is k else _pad128(q), scale=scale,
+                                              cu_seqlens=cu_seqlens, use_cache=use_cache)
+        return o[..., :V], (kc[..., :K] if kc is not None else None)
     if cu_seqlens is None:
         return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, bool(use_cache))
     if k.shape[0] != 1:
@@ -188,7 +205,14 @@ def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):
     intra_chunk_preprocess_fwd_fn + parallel_path_fwd_fn
     (intra_chunk_preprocess_fwd.py:124-168, parallel_path_fwd.py:127-170).
     ``q`` may be None (q = k).  Forward only: the reference has no backward
-    kernels for this op."""
+    kernels for this op.  Head dimensions below 128 run zero-padded."""
+    Kd, Vd = k.shape[-1], v.shape[-1]
+    if Kd not in _HEAD_DIMS or Vd not in _HEAD_DIMS:
+        raise ValueError("only support head_dim in [16, 32, 64, 128]")
+    if Kd < 128 or Vd < 128:
+        o, lse = parallel_path_attention_fwd(None if q is None else _pad128(q), _pad128(k), _pad128(v),
+                                             _pad128(w), beta, scale=Kd ** -0.5 if scale is None else scale)
+        return o[..., :Vd], lse
     lib = _lib.load()
     k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
     beta = _prep(beta, "beta", 3)

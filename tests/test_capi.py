@@ -61,9 +61,14 @@ def test_argument_errors_without_launch(lib):
     """Bad shapes / alignment / workspace are rejected before any CUDA call."""
     from lucid_b200 import _lib as L
     null = None
-    # D != 128
-    rc = lib.lucid_solve_fwd(1, 1, 128, 64, 0.125, 1e-5, 16, 64, 64, 64, 16, 64, 64, 64,
-                             16, 16, 16, 16, 16, 16, 4096, null)
+    # head dimension outside 1..128 (smaller ones are zero-padded rows of 128)
+    for d in (0, 129, 256):
+        rc = lib.lucid_solve_fwd(1, 1, 128, d, 0.125, 1e-5, 16, 128, 128, 128, 16, 128, 128, 128,
+                                 16, 16, 16, 16, 16, 16, 4096, null)
+        assert rc == 1
+    # decode reads rows of D elements with 8-byte loads: D must be a multiple of 4
+    rc = lib.lucid_decode_update(1, 1, 1, 16, 66, 0.125, 1e-5, 16, 64, 64, 64, 16, 64, 64, 64, 16, 64, 64, 64,
+                                 16, 64, 64, 64, 16, 64, 64, 64, 16, 4096, null)
     assert rc == 1
     # misaligned pointer
     rc = lib.lucid_solve_fwd(1, 1, 128, 128, 0.088, 1e-5, 18, 128, 128, 128, 16, 128, 128, 128,

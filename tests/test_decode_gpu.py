@@ -26,17 +26,38 @@ def test_decode_update_matches_reference_fixture(cuda_device, name):
     assert err.max() <= 0, np.abs(x - d["x_new"]).max()
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,Ln,Nc", [(1, 4, 2, 1, 1000), (2, 2, 2, 3, 300), (1, 8, 1, 1, 5000)])
-def test_decode_attention_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc):
+@pytest.mark.parametrize("B,H,Ln,Nc,D", [(1, 4, 1, 3000, 68), (2, 2, 3, 500, 68), (1, 2, 2, 700, 32)])
+def test_decode_update_small_head_dim_matches_oracle(cuda_device, B, H, Ln, Nc, D):
+    """Head dimensions below 128 (68: the reference model's) read natively, with
+    the key RMS mean over D."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import decode_update
+    from oracle.lucid_oracle import decode_update as ref_update
+    g = np.random.default_rng(Nc + D)
+    bf = lambda a: (torch.tensor(a, dtype=torch.float32).bfloat16().double().numpy())
+    kn, vn = bf(g.standard_normal((B, H, Ln, D))), bf(g.standard_normal((B, H, Ln, D)))
+    kc = bf(0.6 * g.standard_normal((B, H, 1, D)) + 0.8 * g.standard_normal((B, H, Nc, D)))
+    xc = bf(0.1 * g.standard_normal((B, H, Nc, D)))
+    s = D ** -0.5
+    ref = ref_update(kn, vn, kc, xc, s, 1e-5)
+    x = decode_update(*(_bf(torch, a, cuda_device) for a in (kn, vn, kc, xc)), s, 1e-5).float().cpu().numpy()
+    assert x.shape == ref.shape
+    err = np.abs(x - ref) - (1e-2 + 2.0 ** -8 * np.abs(ref))
+    assert err.max() <= 0, np.abs(x - ref).max()
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Ln,Nc,D", [(1, 4, 2, 1, 1000, 128), (2, 2, 2, 3, 300, 128),
+                                              (1, 8, 1, 1, 5000, 128), (1, 8, 1, 2, 2000, 68)])
+def test_decode_attention_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc, D):
     torch = pytest.importorskip("torch")
     from lucid_b200 import decode_attention
     from oracle.lucid_oracle import decode_attention as ref_attn
     g = np.random.default_rng(Nc + Ln)
     bf = lambda a: (torch.tensor(a, dtype=torch.float32).bfloat16().double().numpy())
-    q = bf(g.standard_normal((B, Hq, Ln, 128)))
-    kc = bf(g.standard_normal((B, Hkv, Nc, 128)))
-    xc = bf(g.standard_normal((B, Hkv, Nc, 128)))
-    s = 128 ** -0.5
+    q = bf(g.standard_normal((B, Hq, Ln, D)))
+    kc = bf(g.standard_normal((B, Hkv, Nc, D)))
+    xc = bf(g.standard_normal((B, Hkv, Nc, D)))
+    s = D ** -0.5
     ref = ref_attn(q, kc, xc, s)
     o = decode_attention(*(_bf(torch, a, cuda_device) for a in (q, kc, xc)), s).float().cpu().numpy()
     assert o.shape == ref.shape
@@ -44,15 +65,17 @@ def test_decode_attention_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc):
     assert err.max() <= 0, np.abs(o - ref).max()
 
 
-def test_layer_prefill_then_decode_matches_ops(cuda_device):
+@pytest.mark.parametrize("hd", [128, 68])
+def test_layer_prefill_then_decode_matches_ops(cuda_device, hd):
     """LucidAttention with a cache: prefill fills (raw keys, solved values) and
-    a decode step equals decode_update + decode_attention on that cache."""
+    a decode step equals decode_update + decode_attention on that cache (head_dim
+    128, and the reference model's 68)."""
     torch = pytest.importorskip("torch")
     from transformers import DynamicCache, LlamaConfig
-    from lucid_b200 import decode_attention, decode_update, solve_fwd
+    from lucid_b200 import LucidSolveFunction, decode_attention, decode_update
     from lucid_b200.layer import LucidAttention
     torch.manual_seed(0)
-    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=hd,
                       rms_norm_eps=1e-5)
     layer = LucidAttention(cfg, 0).to(cuda_device, torch.bfloat16).eval()
     T = 200
@@ -65,16 +88,16 @@ def test_layer_prefill_then_decode_matches_ops(cuda_device):
             (cache.key_cache[0], cache.value_cache[0])
         assert kc.shape[2] == T + 1 and xc.shape[2] == T + 1
         # prefill part of the cache holds the solved values
-        k_pre = layer.k_proj(h[:, :T]).view(1, T, 2, 128).transpose(1, 2)
-        v_pre = layer.v_proj(h[:, :T]).view(1, T, 2, 128).transpose(1, 2)
-        x_pre = solve_fwd(k_pre, v_pre, layer.scaling, 1e-5)[0][:, :, :T]
+        k_pre = layer.k_proj(h[:, :T]).view(1, T, 2, hd).transpose(1, 2)
+        v_pre = layer.v_proj(h[:, :T]).view(1, T, 2, hd).transpose(1, 2)
+        x_pre = LucidSolveFunction.apply(k_pre, v_pre, layer.scaling, 1e-5)
         torch.testing.assert_close(xc[:, :, :T], x_pre, rtol=0, atol=0)
         # decode step = decode_update + decode_attention on the cache
-        k1 = layer.k_proj(h[:, T:]).view(1, 1, 2, 128).transpose(1, 2)
-        v1 = layer.v_proj(h[:, T:]).view(1, 1, 2, 128).transpose(1, 2)
+        k1 = layer.k_proj(h[:, T:]).view(1, 1, 2, hd).transpose(1, 2)
+        v1 = layer.v_proj(h[:, T:]).view(1, 1, 2, hd).transpose(1, 2)
         x1 = decode_update(k1, v1, kc[:, :, :T], xc[:, :, :T], layer.scaling, 1e-5)
         torch.testing.assert_close(xc[:, :, T:], x1, rtol=0, atol=0)
-        q1 = layer.q_proj(h[:, T:]).view(1, 1, 4, 128).transpose(1, 2)
+        q1 = layer.q_proj(h[:, T:]).view(1, 1, 4, hd).transpose(1, 2)
         o1 = decode_attention(q1, kc, xc, layer.scaling)
         ref = layer.o_proj(o1.reshape(1, 1, -1))
         torch.testing.assert_close(out, ref, rtol=0, atol=0)
@@ -88,7 +111,7 @@ def _kc_bar(d_k, d_w, d_beta, ref):
     return max(1e-2, 1.5 * float(np.abs(reference_bf16_k_cache(d_k, d_w, d_beta) - ref).max()))
 
 
-@pytest.mark.parametrize("name", [c for c in PATH_CASES if "k128" in c])
+@pytest.mark.parametrize("name", PATH_CASES)
 def test_path_key_cache_matches_reference_fixture(cuda_device, name):
     torch = pytest.importorskip("torch")
     from lucid_b200.path import parallel_lucid_path_attention

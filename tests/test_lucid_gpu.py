@@ -119,8 +119,9 @@ def test_solve_fwd_diag_block_inverse(cuda_device):
 # ---------------------------------------------------------------------------
 # full op against the reference's own outputs
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("case", [c for c in ATTN_CASES if c.endswith("d128")])
+@pytest.mark.parametrize("case", ATTN_CASES)
 def test_fused_matches_reference_fixture(cuda_device, case):
+    """Every reference fixture, head_dim 128 and the zero-padded head_dim 32."""
     import torch
     from lucid_b200 import lucid_attention
     g = load_golden(case)
@@ -137,17 +138,21 @@ def test_fused_matches_reference_fixture(cuda_device, case):
     assert_bf16_close(_np(v.grad), g["dv"], f"{case} dV", G)
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,N,keys,qs", [
-    (1, 2, 2, 384, "iid", 1.0),
-    (2, 4, 2, 300, "iid", 128 ** -0.5),
-    (1, 1, 1, 1024, "corr", 1.0),
-    (1, 8, 1, 256, "iid", 1.0),
+@pytest.mark.parametrize("B,Hq,Hkv,N,keys,qs,D", [
+    (1, 2, 2, 384, "iid", 1.0, 128),
+    (2, 4, 2, 300, "iid", 128 ** -0.5, 128),
+    (1, 1, 1, 1024, "corr", 1.0, 128),
+    (1, 8, 1, 256, "iid", 1.0, 128),
+    (1, 8, 1, 640, "corr", 1.0, 68),    # the reference model's head_dim (lucid/config), 8 q per kv head
+    (2, 2, 2, 200, "iid", 1.0, 64),
 ])
-def test_fused_fwd_bwd_matches_oracle(cuda_device, B, Hq, Hkv, N, keys, qs):
+def test_fused_fwd_bwd_matches_oracle(cuda_device, B, Hq, Hkv, N, keys, qs, D):
+    """Head dimensions below 128 run zero-padded: the oracle normalises K over
+    the true D and uses s = D^-1/2."""
     import torch
     from lucid_b200 import lucid_attention
-    q_, k_, v_, do_ = _rand_inputs(100 + N, B, Hq, Hkv, N, keys=keys, q_scale=qs)
-    s = 128 ** -0.5
+    q_, k_, v_, do_ = _rand_inputs(100 + N, B, Hq, Hkv, N, D=D, keys=keys, q_scale=qs)
+    s = D ** -0.5
     q = _t(q_, cuda_device).requires_grad_(True)
     k = _t(k_, cuda_device).requires_grad_(True)
     v = _t(v_, cuda_device).requires_grad_(True)

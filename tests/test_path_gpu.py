@@ -64,7 +64,7 @@ def _check(got, ref, label, ref_dev=None):
         assert rel <= 2e-2, f"{label} {nm}: max err {np.abs(g - r).max():.3e} (rel {rel:.3e})"
 
 
-@pytest.mark.parametrize("name", [c for c in PATH_CASES if "k128" in c])
+@pytest.mark.parametrize("name", PATH_CASES)
 def test_path_matches_reference_fixture(cuda_device, name):
     torch = pytest.importorskip("torch")
     d = load_path_golden(name)
