@@ -393,14 +393,15 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
 
 
 # ---------------------------------------------------------------------------
-# context-parallel forward at 128K
+# context-parallel forward + backward at 128K
 # ---------------------------------------------------------------------------
-CP_METRIC = "LUCID attention forward TFLOP/s, context-parallel, B1 H32 N131072 D128 (config 5)"
+CP_METRIC = "LUCID attention fwd+bwd TFLOP/s, context-parallel, B1 H32 N131072 D128 (config 5)"
+CP_METRIC_FWD = "LUCID attention forward TFLOP/s, context-parallel, B1 H32 N131072 D128 (config 5)"
 
 
-def cp_cpu_sample(N: int, seed: int = 0):
-    """Seconds for one (batch, head) of the LUCID attention FORWARD at length N on
-    the host (oracle/torch_ref.py, fp32, correlated keys of config 5)."""
+def cp_cpu_sample(N: int, seed: int = 0, backward: bool = True):
+    """Seconds for one (batch, head) of the LUCID attention forward (+ backward)
+    at length N on the host (oracle/torch_ref.py, fp32, correlated keys of config 5)."""
     import torch
 
     from oracle import torch_ref
@@ -410,28 +411,35 @@ def cp_cpu_sample(N: int, seed: int = 0):
     q = torch.randn(1, 1, N, D, generator=g)
     k = 0.6 * torch.randn(1, 1, 1, D, generator=g) + 0.8 * torch.randn(1, 1, N, D, generator=g)
     v = torch.randn(1, 1, N, D, generator=g)
+    do = torch.randn(1, N, 1, D, generator=g)
     t0 = time.perf_counter()
-    with torch.no_grad():
-        torch_ref.lucid_layer(q, k, v)
+    if backward:
+        torch_ref.lucid_fwd_bwd(q, k, v, do)
+    else:
+        with torch.no_grad():
+            torch_ref.lucid_layer(q, k, v)
     return time.perf_counter() - t0
 
 
 def cp_reference_arm(args):
-    n_cpu = min(args.cpu_n, 8192)
-    cp_cpu_sample(1024)
+    bwd = not args.cp_forward_only
+    n_cpu = min(args.cpu_n, 4096 if bwd else 8192)
+    cp_cpu_sample(1024, backward=bwd)
     for _ in range(args.warmup):
-        cp_cpu_sample(n_cpu)
-    times = [cp_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
+        cp_cpu_sample(n_cpu, backward=bwd)
+    times = [cp_cpu_sample(n_cpu, seed=i, backward=bwd) for i in range(args.steps)]
     t = sum(times) / len(times)
-    val = 4.0 * n_cpu * n_cpu * 128 / t / 1e12
+    val = (14.0 if bwd else 4.0) * n_cpu * n_cpu * 128 / t / 1e12
+    what = "forward + backward" if bwd else "forward"
     line = {
-        "impl": "reference", "metric": CP_METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": CP_METRIC if bwd else CP_METRIC_FWD, "value": val, "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"LUCID attention forward B1 H32 N131072 D128 (sampled: 1 head at N={n_cpu})",
+        "config": {"workload": f"LUCID attention {what} B1 H32 N131072 D128 (sampled: 1 head at N={n_cpu})",
                    "global_batch": 1, "seq_len": 131072, "parallelism": "cpu"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"1 (batch, head) at N={n_cpu}, fp32 forward, oracle/torch_ref.py"},
+                         "sample": f"1 (batch, head) at N={n_cpu}, fp32 {what}, oracle/torch_ref.py"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -439,9 +447,10 @@ def cp_reference_arm(args):
 
 
 def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
-    from lucid_b200.cp import balanced_bounds, cp_lucid_attention_forward
+    from lucid_b200.cp import balanced_bounds, cp_lucid_attention, cp_lucid_attention_forward, train_bounds
     B, H, N, D = 1, 32, 131072, 128
-    bounds = balanced_bounds(N, world)
+    bwd = not args.cp_forward_only
+    bounds = train_bounds(N, world) if bwd else balanced_bounds(N, world)
     C = bounds[rank + 1] - bounds[rank]
     s = D ** -0.5
     # K = 0.6 s + 0.8 n with s shared per head (the same on every rank) and n per token
@@ -451,9 +460,18 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
     q = torch.randn(B, H, C, D, generator=g, device=dev).bfloat16()
     k = (0.6 * shared + 0.8 * torch.randn(B, H, C, D, generator=g, device=dev)).bfloat16()
     v = torch.randn(B, H, C, D, generator=g, device=dev).bfloat16()
+    do = torch.randn(B, C, H, D, generator=g, device=dev).bfloat16()
+    q.requires_grad_(bwd)
+    k.requires_grad_(bwd)
+    v.requires_grad_(bwd)
 
     def step():
-        return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
+        if not bwd:
+            return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
+        q.grad = k.grad = v.grad = None
+        o = cp_lucid_attention(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
+        o.backward(do)
+        return o.detach()
 
     for _ in range(args.warmup):
         step()
@@ -476,7 +494,10 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     finite = bool(torch.isfinite(o).all().item())
-    fl = 4.0 * N * N * D * B * H   # solve 2 N^2 D + attention 2 N^2 D per (batch, head)
+    if bwd:
+        finite = finite and all(bool(torch.isfinite(t.grad).all().item()) for t in (q, k, v))
+    # per (batch, head): forward (solve 2 N^2 D + attention 2 N^2 D), backward 10 N^2 D
+    fl = (14.0 if bwd else 4.0) * N * N * D * B * H
     tflops = fl / (ms * 1e-3) / 1e12
     pk_burst, pk_sust, hbm, pk_kind = peaks()
     if world > 1:
@@ -485,21 +506,26 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
     if rank != 0:
         return 0
     G = args.head_groups
+    # launches of rank 0 per step: forward prep / solve / attention per group; backward delta,
+    # prep of the later rows, flag publishes (one per later rank), attention column pass,
+    # transposed solve, solve row pass + finalize and attention row pass per group
+    launches = 3 * G + ((1 + (1 if world > 1 else 0) + 5) * G + G * (world - 1) if bwd else 0)
+    what = "forward + backward" if bwd else "FORWARD"
     line = {
-        "metric": CP_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "metric": CP_METRIC if bwd else CP_METRIC_FWD, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"LUCID attention FORWARD B{B} H{H} N{N} D{D}, keys 0.6 s + 0.8 n, sequence split in "
-                               f"{world} contiguous chunks of equal causal work (bounds {bounds}), {G} head "
-                               f"groups pipelined",
+        "config": {"workload": f"LUCID attention {what} B{B} H{H} N{N} D{D}, keys 0.6 s + 0.8 n, sequence split "
+                               f"in {world} contiguous chunks ({'train_bounds' if bwd else 'balanced_bounds'} "
+                               f"{bounds}), {G} head groups pipelined",
                    "global_batch": B, "seq_len": N, "parallelism": f"context parallel x{world} (NCCL send/recv)",
-                   "scope": "forward only: the backward of the context-parallel chain is not built",
                    "l2": "inputs larger than L2, no flush"},
         "tokens_per_s": B * N / (ms * 1e-3),
         "frac_of_bf16_peak": tflops / (pk_sust * world),
         "output_finite": finite,
         "clocks": clk,
-        "gpu_launches": (4 * G + G * max(0, world - 1)) * args.steps,
+        "gpu_launches": launches * args.steps,
         "e2e": None, "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)
@@ -517,6 +543,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k"], default="32k")
     ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
+    ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
