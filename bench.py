@@ -167,6 +167,8 @@ def reference_arm(args):
         return path_reference_arm(args)
     if args.config == "cp128k":
         return cp_reference_arm(args)
+    if args.config == "prefill":
+        return prefill_reference_arm(args)
     B, H, N, D, _ = CONFIGS[args.config]
     n_cpu = args.cpu_n
     cpu_reference_sample(1024, D)
@@ -393,6 +395,196 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
 
 
 # ---------------------------------------------------------------------------
+# full-model prefill
+# ---------------------------------------------------------------------------
+PREFILL_METRIC = ("Full-model prefill tokens/s: Llama-architecture decoder with LUCID attention "
+                  "(lucid/config: 22 layers, hidden 2048, 32/4 heads, head_dim 68), 32768 tokens per GPU (config 4)")
+PREFILL_N = 32768
+
+
+def prefill_cpu_sample(N: int, seed: int = 0):
+    """Seconds for ONE decoder layer of the reference model on the host at N
+    tokens, float32: LlamaRMSNorm, q/k/v/o projections, the reference's LUCID
+    attention (oracle/torch_ref.py: get_v_prime + SDPA) and the SiLU MLP."""
+    import torch
+
+    from lucid_b200.decoder import LUCID_CONFIG as C
+    from oracle import torch_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    hs, hd, hq, hk, im = C["hidden_size"], C["head_dim"], C["num_attention_heads"], C["num_key_value_heads"], \
+        C["intermediate_size"]
+    w = lambda *sh: torch.randn(*sh, generator=g) * 0.02
+    Wq, Wk, Wv, Wo = w(hq * hd, hs), w(hk * hd, hs), w(hk * hd, hs), w(hs, hq * hd)
+    Wg, Wu, Wd = w(im, hs), w(im, hs), w(hs, im)
+    x = torch.randn(1, N, hs, generator=g)
+    norm = lambda t: t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-5)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        h = norm(x)
+        q = (h @ Wq.T).view(1, N, hq, hd).transpose(1, 2)
+        k = (h @ Wk.T).view(1, N, hk, hd).transpose(1, 2)
+        v = (h @ Wv.T).view(1, N, hk, hd).transpose(1, 2)
+        x = x + torch_ref.lucid_layer(q, k, v, hd ** -0.5).reshape(1, N, hq * hd) @ Wo.T
+        h = norm(x)
+        x = x + (torch.nn.functional.silu(h @ Wg.T) * (h @ Wu.T)) @ Wd.T
+    return time.perf_counter() - t0
+
+
+def prefill_reference_arm(args):
+    n_cpu = min(args.cpu_n, 4096)
+    layers = 22
+    prefill_cpu_sample(512)
+    for _ in range(args.warmup):
+        prefill_cpu_sample(n_cpu)
+    times = [prefill_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
+    t = sum(times) / len(times) * layers
+    val = n_cpu / t
+    line = {
+        "impl": "reference", "metric": PREFILL_METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decoder prefill, sampled: 1 of {layers} layers at N={n_cpu} (tokens/s = N / "
+                               f"({layers} x layer time); embedding and LM head not timed)",
+                   "global_batch": 1, "seq_len": PREFILL_N, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"1 decoder layer at N={n_cpu}, fp32, attention by oracle/torch_ref.py"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_prefill(args, torch, dist, dev, world, rank, local, barrier):
+    import ctypes as ct
+
+    from transformers import DynamicCache
+
+    from lucid_b200 import _lib
+    from lucid_b200.decoder import LucidForCausalLM, lucid_config
+    lib = _lib.load()
+    cfg = lucid_config()
+    L, N = cfg.num_hidden_layers, PREFILL_N
+    hd, hq, hk = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+    with torch.device(dev):
+        model = LucidForCausalLM(cfg)
+    model = model.to(torch.bfloat16).init_weights(seed=4000 + rank).eval()
+    g = torch.Generator().manual_seed(4100 + rank)
+    ids_host = torch.randint(0, cfg.vocab_size, (1, N), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+
+    def step(inp, events=None):
+        with torch.no_grad():
+            # the reference's prefill: use_cache=True fills (raw keys, solved values)
+            return model(inp, past_key_values=DynamicCache(), logits_to_keep=1, attn_events=events)
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    mkev = lambda: torch.cuda.Event(enable_timing=True)
+    events = [[(mkev(), mkev()) for _ in range(L)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = mkev(), mkev()
+    ev0.record()
+    for i in range(args.steps):
+        logits = step(ids, events[i])
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    attn_ms = sum(a.elapsed_time(b) for evs in events for a, b in evs) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tok_s = world * N / (ms * 1e-3)
+    finite = bool(torch.isfinite(logits).all().item())
+
+    # ---- the LUCID kernels alone (profile hook) and the dominant one's roofline ----
+    pk_burst, pk_sust, hbm, pk_kind = peaks()
+    stage_ms, stage_n = {}, {}
+    for name in ("prep", "solve_fwd", "attn_fwd"):
+        lib.lucid_profile_enable(_lib.KERNEL_IDS[name])
+        step(ids)
+        torch.cuda.synchronize()
+        tot, n = ct.c_float(), ct.c_int()
+        lib.lucid_profile_read(ct.byref(tot), ct.byref(n))
+        stage_ms[name], stage_n[name] = tot.value, n.value
+    lib.lucid_profile_enable(0)
+    # algorithmic flops per layer at the model's head_dim (the kernels run 128 columns):
+    # causal attention 2 N^2 D per query head, the solve 2 N^2 D per kv head
+    alg = {"attn_fwd": 2.0 * N * N * hd * hq, "solve_fwd": 2.0 * N * N * hd * hk}
+    dom = max(alg, key=lambda n_: stage_ms[n_])
+    per_launch_ms = stage_ms[dom] / max(1, stage_n[dom])
+    ach = alg[dom] / (per_launch_ms * 1e-3) / 1e12
+    roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": pk_burst, "unit": "TFLOP/s",
+            "frac": ach / pk_burst, "peak_kind": f"{pk_kind} burst bf16",
+            "executed_tflops": ach * 128 / hd, "note": f"algorithmic flops at head_dim {hd}; the kernels "
+                                                          f"compute 128 zero-padded columns"}
+    roof["traffic"] = None
+
+    # ---- end to end: token ids from pinned host memory, last logits back to the host ----
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty(1, 1, cfg.vocab_size, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            lg = step(ids_host.to(dev, non_blocking=True))
+            out_host.copy_(lg, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = mkev(), mkev()
+        ne = max(1, min(args.steps, 3))
+        a0.record()
+        for _ in range(ne):
+            e2e_step()
+        a1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = a0.elapsed_time(a1) / ne
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": world * N / (ems * 1e-3), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": N * 8, "d2h_bytes_per_step": cfg.vocab_size * 2}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n_cpu = min(args.cpu_n, 4096)
+        prefill_cpu_sample(512)
+        tc = min(prefill_cpu_sample(n_cpu, seed=i) for i in range(2))
+        cpu = {"value": n_cpu / (L * tc), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"1 of {L} decoder layers at N={n_cpu}, fp32 (attention by oracle/torch_ref.py), best "
+                         f"of 2; tokens/s = N / ({L} x layer time)", "seconds_per_layer": tc}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": PREFILL_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform token ids, random N(0, 0.02) weights)",
+        "config": {"workload": f"prefill forward of the {L}-layer LUCID decoder (lucid/config), batch 1 x {N} "
+                               f"tokens per GPU, use_cache=True (cache filled), logits of the last position",
+                   "global_batch": world, "seq_len": N, "parallelism": f"data parallel replicas x{world}",
+                   "l2": "activations and weights larger than L2, no flush"},
+        "attention_ms": attn_ms, "attention_share": attn_ms / ms,
+        "stage_ms": stage_ms, "roofline": roof, "clocks": clk, "output_finite": finite,
+        "gpu_launches": 3 * L * args.steps, "e2e": e2e, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # context-parallel forward + backward at 128K (BASELINE config 5)
 # ---------------------------------------------------------------------------
 CP_METRIC = "LUCID attention fwd+bwd TFLOP/s, context-parallel, B1 H32 N131072 D128 (config 5)"
@@ -541,7 +733,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k"], default="32k")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill"], default="32k")
     ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
@@ -575,6 +767,8 @@ def main(argv=None):
         return bench_path(args, torch, dist, dev, world, rank, local, barrier)
     if args.config == "cp128k":
         return bench_cp(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "prefill":
+        return bench_prefill(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
     B, H, N, D, qs = CONFIGS[args.config]
     s = D ** -0.5
