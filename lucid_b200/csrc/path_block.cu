@@ -32,12 +32,13 @@ __device__ __forceinline__ float pvec_at(const PVec& v, int b, int h, long long 
   return __bfloat162float(reinterpret_cast<const bf16*>(v.ptr)[off]);
 }
 
-// 64 consecutive elements [c0, c0+64) of stored row r of matrix (b, h, blk).
-__device__ __forceinline__ bool pmat_load64(const PMat& m, int b, int h, int blk, int r, int c0, float (&v)[64]) {
+// W consecutive elements [c0, c0+W) of stored row r of matrix (b, h, blk), W = 32 or 64.
+template <int W>
+__device__ __forceinline__ bool pmat_load(const PMat& m, int b, int h, int blk, int r, int c0, float (&v)[W]) {
   const bool valid = (long long)blk * 128 + r < m.rows;
   if (!valid) {
 #pragma unroll
-    for (int e = 0; e < 64; ++e) v[e] = 0.f;
+    for (int e = 0; e < W; ++e) v[e] = 0.f;
     return false;
   }
   const long long off = (long long)b * m.s_b + (long long)(h / m.hdiv) * m.s_h + (long long)blk * m.s_blk +
@@ -45,44 +46,57 @@ __device__ __forceinline__ bool pmat_load64(const PMat& m, int b, int h, int blk
   if (m.fp32) {
     const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(m.ptr) + off);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
+    for (int e = 0; e < W / 4; ++e) {
       const float4 f = p[e];
       v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
     }
   } else {
     const bf16* p = reinterpret_cast<const bf16*>(m.ptr) + off;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ld_bf16x8(p + 8 * e, v + 8 * e);
+    for (int e = 0; e < W / 8; ++e) ld_bf16x8(p + 8 * e, v + 8 * e);
   }
   return true;
 }
 
-__device__ __forceinline__ void pmat_store64(const PMat& m, int b, int h, int blk, int r, int c0, const float (&v)[64]) {
+template <int W>
+__device__ __forceinline__ void pmat_store(const PMat& m, int b, int h, int blk, int r, int c0, const float (&v)[W]) {
   if ((long long)blk * 128 + r >= m.rows) return;
   const long long off = (long long)b * m.s_b + (long long)(h / m.hdiv) * m.s_h + (long long)blk * m.s_blk +
                         (long long)r * m.s_row + c0;
   if (m.fp32) {
     float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(m.ptr) + off);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) p[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    for (int e = 0; e < W / 4; ++e) p[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
   } else {
     bf16* p = reinterpret_cast<bf16*>(m.ptr) + off;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) st_bf16x8(p + 8 * e, v + 8 * e);
+    for (int e = 0; e < W / 8; ++e) st_bf16x8(p + 8 * e, v + 8 * e);
   }
 }
 
-__device__ __forceinline__ void apply_mask64(int mask, int r, int c0, float (&v)[64]) {
+template <int W>
+__device__ __forceinline__ void apply_mask(int mask, int r, int c0, float (&v)[W]) {
   if (mask == kMaskNone) return;
 #pragma unroll
-  for (int e = 0; e < 64; ++e) {
+  for (int e = 0; e < W; ++e) {
     const int c = c0 + e;
     const bool keep = (mask == kMaskTril) ? (c <= r) : (c < r);
     if (!keep) v[e] = 0.f;
   }
 }
 
-__global__ void __launch_bounds__(pblk::kThreads) path_bgemm_kernel(const __grid_constant__ BGemmArgs a) {
+__device__ __forceinline__ bool pmat_load64(const PMat& m, int b, int h, int blk, int r, int c0, float (&v)[64]) {
+  return pmat_load<64>(m, b, h, blk, r, c0, v);
+}
+__device__ __forceinline__ void pmat_store64(const PMat& m, int b, int h, int blk, int r, int c0, const float (&v)[64]) {
+  pmat_store<64>(m, b, h, blk, r, c0, v);
+}
+__device__ __forceinline__ void apply_mask64(int mask, int r, int c0, float (&v)[64]) { apply_mask<64>(mask, r, c0, v); }
+
+// 32-column chunks keep the register footprint under 85 per thread, so that
+// three CTAs (one output block each) share an SM: a CTA spends most of its
+// life waiting on its operand loads, and the other two fill that time.
+__global__ void __launch_bounds__(pblk::kThreads, 3) path_bgemm_kernel(const __grid_constant__ BGemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const int ntile = 2 * a.nprod;
@@ -117,21 +131,22 @@ __global__ void __launch_bounds__(pblk::kThreads) path_bgemm_kernel(const __grid
   for (int p = 0; p < a.nprod; ++p) {
     for (int side = 0; side < 2; ++side) {
       const POperand& op = side == 0 ? a.A[p] : a.B[p];
-      float v[64];
-      pmat_load64(op.m, b, h, blk, r, c0, v);
-      if (op.lo) {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) v[e] -= __bfloat162float(__float2bfloat16(v[e]));
-      }
       float sc = op.scale;
       if (op.rsc.ptr != nullptr) sc *= pvec_at(op.rsc, b, h, t);
-#pragma unroll
-      for (int e = 0; e < 64; ++e) v[e] *= sc;
-      apply_mask64(op.mask, r, c0, v);
       const uint32_t tile = sbase + (uint32_t)(2 * p + side) * 32768u;
-      float* v0 = v;
-      tile_store_row32(tile, r, 2 * hf, *reinterpret_cast<float(*)[32]>(v0));
-      tile_store_row32(tile, r, 2 * hf + 1, *reinterpret_cast<float(*)[32]>(v0 + 32));
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float v[32];
+        pmat_load<32>(op.m, b, h, blk, r, c0 + 32 * q, v);
+        if (op.lo) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] -= __bfloat162float(__float2bfloat16(v[e]));
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= sc;
+        apply_mask<32>(op.mask, r, c0 + 32 * q, v);
+        tile_store_row32(tile, r, 2 * hf + q, v);
+      }
     }
   }
   fence_proxy_async_smem();
@@ -149,32 +164,37 @@ __global__ void __launch_bounds__(pblk::kThreads) path_bgemm_kernel(const __grid
   const bool ok = mbar_wait(bar, 0, ab);
   tc_fence_after();
   if (ok) {
-    float acc[64];
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    tmem_ld32(tmem + lane_base + (uint32_t)c0, *reinterpret_cast<float(*)[32]>(acc));
-    tmem_ld32(tmem + lane_base + (uint32_t)c0 + 32u, *reinterpret_cast<float(*)[32]>(acc + 32));
-    tmem_ld_wait();
-    if (a.orsc.ptr != nullptr) {
-      const float f = pvec_at(a.orsc, b, h, t);
+    const float fo = a.orsc.ptr != nullptr ? pvec_at(a.orsc, b, h, t) : 1.f;
+    float fc[2];
 #pragma unroll
-      for (int e = 0; e < 64; ++e) acc[e] *= f;
-    }
-    for (int c = 0; c < a.nc; ++c) {
-      float cv[64];
-      pmat_load64(a.C[c], b, h, blk, r, c0, cv);
-      float f = a.cbeta[c];
-      if (a.crsc[c].ptr != nullptr) f *= pvec_at(a.crsc[c], b, h, t);
+    for (int c = 0; c < 2; ++c)
+      fc[c] = (c < a.nc && a.crsc[c].ptr != nullptr) ? a.cbeta[c] * pvec_at(a.crsc[c], b, h, t) : a.cbeta[c];
 #pragma unroll
-      for (int e = 0; e < 64; ++e) acc[e] = fmaf(f, cv[e], acc[e]);
-    }
-    if (a.epi == kEpiPathExp) {
-      const float c1 = a.s * 1.4426950408889634f, c2 = 1.4426950408889634f / a.s;
+    for (int q = 0; q < 2; ++q) {
+      const int cq = c0 + 32 * q;
+      float acc[32];
+      tmem_ld32(tmem + lane_base + (uint32_t)cq, acc);
+      tmem_ld_wait();
 #pragma unroll
-      for (int e = 0; e < 64; ++e) acc[e] = exp2f(fmaf(acc[e], c1, -c2));
+      for (int e = 0; e < 32; ++e) acc[e] *= fo;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c >= a.nc) break;
+        float cv[32];
+        pmat_load<32>(a.C[c], b, h, blk, r, cq, cv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = fmaf(fc[c], cv[e], acc[e]);
+      }
+      if (a.epi == kEpiPathExp) {
+        const float c1 = a.s * 1.4426950408889634f, c2 = 1.4426950408889634f / a.s;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = exp2f(fmaf(acc[e], c1, -c2));
+      }
+      apply_mask<32>(a.out_mask, r, cq, acc);
+      pmat_store<32>(a.O, b, h, blk, r, cq, acc);
+      if (a.O2.ptr != nullptr) pmat_store<32>(a.O2, b, h, blk, r, cq, acc);
     }
-    apply_mask64(a.out_mask, r, c0, acc);
-    pmat_store64(a.O, b, h, blk, r, c0, acc);
-    if (a.O2.ptr != nullptr) pmat_store64(a.O2, b, h, blk, r, c0, acc);
   }
   tc_fence_before();
   __syncthreads();
