@@ -99,10 +99,10 @@ __device__ __forceinline__ void apply_mask64(int mask, int r, int c0, float (&v)
 __global__ void __launch_bounds__(pblk::kThreads, 3) path_bgemm_kernel(const __grid_constant__ BGemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
-  const int ntile = 2 * a.nprod;
-  const uint32_t bar = sbase + (uint32_t)ntile * 32768u;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + ntile * 32768 + 8);
-  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + ntile * 32768 + 12);
+  // one (A, B) tile pair, reused by every product: 64 KB per CTA whatever nprod
+  const uint32_t bar = sbase + 2u * 32768u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 2 * 32768 + 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + 2 * 32768 + 12);
   const Abort ab{abort_cta, a.status, kTagPathGemm};
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {
@@ -127,13 +127,24 @@ __global__ void __launch_bounds__(pblk::kThreads, 3) path_bgemm_kernel(const __g
     tmem_alloc(smem_u32(tmem_slot), 128);
     tmem_relinquish();
   }
-  // ---- stage operands ----
+  // ---- per product: stage (A_p, B_p) into the tile pair, then one MMA batch; the
+  // next product overwrites the tiles once this MMA's commit has landed ----
+  bool ok = true;
+  uint32_t tmem = 0;
   for (int p = 0; p < a.nprod; ++p) {
+    if (p > 0) {
+      const bool w = mbar_wait(bar, (uint32_t)((p - 1) & 1), ab);
+      if (!__syncthreads_and(w ? 1 : 0)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+    }
     for (int side = 0; side < 2; ++side) {
       const POperand& op = side == 0 ? a.A[p] : a.B[p];
       float sc = op.scale;
       if (op.rsc.ptr != nullptr) sc *= pvec_at(op.rsc, b, h, t);
-      const uint32_t tile = sbase + (uint32_t)(2 * p + side) * 32768u;
+      const uint32_t tile = sbase + (uint32_t)side * 32768u;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         float v[32];
@@ -148,20 +159,17 @@ __global__ void __launch_bounds__(pblk::kThreads, 3) path_bgemm_kernel(const __g
         tile_store_row32(tile, r, 2 * hf + q, v);
       }
     }
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < a.nprod; ++p) {
-      const uint32_t ta = sbase + (uint32_t)(2 * p) * 32768u, tb = ta + 32768u;
-      umma_tile(tmem, ta, a.A[p].trans != 0, tb, a.B[p].trans == 0, p > 0 ? 1u : 0u);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem = *tmem_slot;
+    if (threadIdx.x == 0) {
+      umma_tile(tmem, sbase, a.A[p].trans != 0, sbase + 32768u, a.B[p].trans == 0, p > 0 ? 1u : 0u);
+      umma_commit(bar);
     }
-    umma_commit(bar);
   }
-  const bool ok = mbar_wait(bar, 0, ab);
+  if (ok) ok = mbar_wait(bar, (uint32_t)((a.nprod - 1) & 1), ab);
   tc_fence_after();
   if (ok) {
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
@@ -252,13 +260,26 @@ __global__ void __launch_bounds__(256) path_triinv_kernel(const __grid_constant_
   {
     const int rr = tid >> 4, c = tid & 15;
     for (int I = 1; I < 8; ++I) {
-      // tt_J = L[I, J16:I16] Z[J16:I16, J]   (row block I still holds L)
-      for (int J = 0; J < I; ++J) {
-        float acc = 0.f;
-        for (int col = J * 16; col < I * 16; ++col)
-          acc = fmaf(z[(I * 16 + rr) * kInvLD + col], z[col * kInvLD + J * 16 + c], acc);
-        tt[J * 256 + rr * 16 + c] = acc;
+      // tt_J = L[I, J16:I16] Z[J16:I16, J]   (row block I still holds L): one pass over
+      // the columns loads each L entry once for every J it feeds
+      float acc[7];
+#pragma unroll
+      for (int J = 0; J < 7; ++J) acc[J] = 0.f;
+#pragma unroll
+      for (int K = 0; K < 7; ++K) {   // column block K of L's row block I feeds Z_IJ, J <= K
+        if (K >= I) break;
+        const float* lrow = z + (I * 16 + rr) * kInvLD + K * 16;
+        const float* zrow = z + (K * 16) * kInvLD + c;
+#pragma unroll 4
+        for (int m = 0; m < 16; ++m) {
+          const float l = lrow[m];
+#pragma unroll
+          for (int J = 0; J <= K; ++J) acc[J] = fmaf(l, zrow[m * kInvLD + J * 16], acc[J]);
+        }
       }
+#pragma unroll
+      for (int J = 0; J < 7; ++J)
+        if (J < I) tt[J * 256 + rr * 16 + c] = acc[J];
       __syncthreads();
       for (int J = 0; J < I; ++J) {
         float acc = 0.f;
@@ -279,7 +300,8 @@ __global__ void __launch_bounds__(256) path_triinv_kernel(const __grid_constant_
     }
     if (a.Z.ptr != nullptr) pmat_store64(a.Z, b, h, blk, r, c0, v);
     if (a.U.ptr != nullptr) {
-      if (r >= c0 && r < c0 + 64) v[r - c0] -= 1.f;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) v[e] -= (c0 + e == r) ? 1.f : 0.f;
       pmat_store64(a.U, b, h, blk, r, c0, v);
     }
   }
@@ -377,8 +399,8 @@ __global__ void path_eye_kernel(float* out, long long head_stride) {
 cudaError_t launch_path_bgemm(const BGemmArgs& a, cudaStream_t st) {
   const long long n = (long long)a.Bn * a.Hx * a.NB;
   if (n == 0) return cudaSuccess;
-  const size_t smem = (size_t)2 * a.nprod * 32768 + 64;
-  cudaError_t e = cudaFuncSetAttribute(path_bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(3 * 2 * 32768 + 64));
+  const size_t smem = (size_t)2 * 32768 + 64;
+  cudaError_t e = cudaFuncSetAttribute(path_bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   path_bgemm_kernel<<<(unsigned)n, pblk::kThreads, smem, st>>>(a);
   return cudaGetLastError();
