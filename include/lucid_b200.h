@@ -158,6 +158,10 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
  *      dx_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dX)
  */
 size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
+/* Workspace of the stored-tile schedule: with at least this many bytes the column pass
+ * also stores every bf16 dS^T tile (B*Hq*ceil(N/128)*(ceil(N/128)+1)/2 tiles of 32 KB)
+ * and the row pass streams them instead of recomputing S and dP; same results. */
+size_t lucid_attn_bwd_fast_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
 int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale,
                    const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,

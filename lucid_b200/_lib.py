@@ -45,6 +45,7 @@ SIGNATURES = {
     "lucid_attn_fwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
                        + [c_void_p] + S3 + [c_void_p] + [c_void_p, c_size_t, c_void_p]),
     "lucid_attn_bwd_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_attn_bwd_fast_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_bwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
                        + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p] + [c_void_p] + S3
                        + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),

@@ -11,7 +11,10 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
-                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a, cudaStream_t st);
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const CUtensorMap& tS, const BwdArgs& a,
+                           cudaStream_t st);
+cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUtensorMap& tB, const BwdArgs& a,
+                                  cudaStream_t st);
 cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st);
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
@@ -194,6 +197,13 @@ size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
   return kStatusRegion + align256(rows * sizeof(float));
 }
 
+// Stored-tile schedule: one bf16 dS^T tile per (batch, query head, key block i <= query block j).
+size_t lucid_attn_bwd_fast_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
+  const size_t nb = (size_t)nb_of(N);
+  return lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D) +
+         align256((size_t)B * Hq * (nb * (nb + 1) / 2) * kTileBytes);
+}
+
 int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
                    int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                    const void* x, const void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
@@ -223,6 +233,13 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
       !tmap_strided(&tQ, q, B, Hq, N, q_sb, q_sh, q_sn) ||
       !tmap_strided(&tDO, dout, B, Hq, N, do_sb, do_sh, do_sn))
     return LUCID_ERR_TENSORMAP;
+  // a workspace large enough for the dS^T tiles selects the stored-tile schedule
+  const size_t npair = (size_t)NB * (NB + 1) / 2;
+  const bool stored = workspace_bytes >= lucid_attn_bwd_fast_workspace_bytes(B, Hq, Hkv, N, D) &&
+                      npair * 128 < (size_t)1 << 31;
+  bf16* tiles = stored ? reinterpret_cast<bf16*>(ws + lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D)) : nullptr;
+  CUtensorMap tS = tX;
+  if (stored && !tmap_internal(&tS, tiles, B, Hq, (int)(npair * 128))) return LUCID_ERR_TENSORMAP;
   BwdArgs ba{};
   ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
@@ -230,12 +247,14 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   ba.dx = dx_f32; ba.dk_col = dk_f32;
   ba.dq = static_cast<bf16*>(dq); ba.dq_sb = dq_sb; ba.dq_sh = dq_sh; ba.dq_sn = dq_sn;
   ba.status = status;
+  ba.store_tiles = stored ? 1 : 0;
   {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
-    e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st);
+    e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, tS, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
+  if (stored) return to_status(launch_bwd_row_stored(false, tS, tK, ba, st));
   return to_status(launch_bwd_row(false, tQ, tDO, tK, tX, ba, st));
 }
 
@@ -293,7 +312,7 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   cudaError_t e;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st);
+    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, tU, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   {
@@ -480,7 +499,7 @@ extern "C" int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float sca
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (passes & 1) {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
-    if (launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    if (launch_bwd_col(false, tK, tX, tQ, tDO, tX, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
   if (passes & 2) {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
@@ -520,7 +539,7 @@ extern "C" int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int b
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (passes & 1) {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    if (launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    if (launch_bwd_col(true, tK, tX, tK, tDV, tU, tU, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
   if (passes & 2) {
     {

@@ -58,7 +58,7 @@ __device__ __forceinline__ uint32_t packed_kslice(uint32_t region, int kk) {
 constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdEpiThreads = kBwdEpiWarps * 32;
 constexpr int kBwdThreads = kBwdEpiThreads + 128;  // + control warpgroup (TMA, MMA, 2 idle warps)
-constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1;
+constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1, kBwdWarpStore = kBwdEpiWarps + 2;
 // register split: 384 x 168 at launch >= 256 x 192 + 128 x 120
 constexpr int kBwdRegsEpi = 192, kBwdRegsCtl = 120;
 
@@ -73,7 +73,7 @@ constexpr uint32_t kOffVec = 229376;         // stage s: lse[128], delta[128] at
 constexpr uint32_t kOffBar = kOffVec + 2048;
 enum {
   A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_READ, PD_FULL, DS_FREE,
-  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, NBAR
+  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, STG_READY, STG_FREE, NBAR
 };
 constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
@@ -83,7 +83,8 @@ template <bool SOLVE>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     lucid_bwd_col_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
                          const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
-                         const __grid_constant__ CUtensorMap tmU, BwdArgs p) {
+                         const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmS,
+                         BwdArgs p) {
   using namespace bwdc;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -119,6 +120,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(bar(ACC_FREE), kBwdEpiThreads);
     mbar_init(bar(EPI_DONE), kBwdEpiThreads);
     mbar_init(bar(DRAIN), 1);
+    mbar_init(bar(STG_READY), kBwdEpiThreads);
+    mbar_init(bar(STG_FREE), 1);
     *abort_cta = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA1);
@@ -311,6 +314,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
+  } else if (warp == kBwdWarpStore && !SOLVE && p.store_tiles != 0) {
+    // ============ tile store (attention, stored-tile schedule) ============
+    // per tile: once the 256 epilogue threads staged the packed dS^T tile, store it to
+    // pair j (j + 1) / 2 + i of query head hk G + g (evict-first: it is read once), and
+    // free the staging tile as soon as the store has read it
+    if (lane == 0) {
+      Ph stg_ready;
+      bool ok = true;
+      const uint64_t pol = l2_policy_evict_first();
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int i, b, hk;
+        decode(idx, i, b, hk);
+        const int T = ntiles(i);
+        for (int t = 0; t < T; ++t) {
+          int g, j;
+          tile_at(i, t, g, j);
+          if (!mbar_wait(bar(STG_READY), stg_ready.full(), ab)) { ok = false; break; }
+          tma_store_tile_hint(&tmS, sDS, (j * (j + 1) / 2 + i) * 128, hk * G + g, b, pol);
+          bulk_commit();
+          bulk_wait_read_all();
+          mbar_arrive(bar(STG_FREE));
+        }
+      }
+      bulk_wait_all();
+    }
   }
   } else {
     regs_inc<kBwdRegsEpi>();
@@ -322,8 +350,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float kLog2e = 1.4426950408889634f;
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
-    Ph sd_full, ds_free, t_full, acc_full, acc2_full;
+    Ph sd_full, ds_free, t_full, acc_full, acc2_full, stg_free;
     uint32_t n_kv = 0, item = 0;
+    // attention, stored-tile schedule: every packed dS^T tile also goes to global
+    // memory through the (otherwise unused) sDS tile, stored by warp kBwdWarpStore
+    const bool stage = !SOLVE && p.store_tiles != 0;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
       int i, b, hk;
       decode(idx, i, b, hk);
@@ -349,6 +380,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
         const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
                                 : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
+        // the staging tile is free once the store warp saw the previous tile's store read it
+        if (stage && !warp_wait_b(bar(STG_FREE), stg_free.empty(), ab)) { ok = false; break; }
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const int cb = (int)c0 + 32 * q;
@@ -390,10 +423,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q + 16u, dk);
+          if (stage) tile_store_row32_packed(sDS, r, 2 * h + q, dk);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(PD_FULL));
+        if (stage) {
+          fence_proxy_async_smem();
+          mbar_arrive(bar(STG_READY));
+        }
       }
       if (!ok) break;
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
@@ -826,6 +864,183 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ===========================================================================
+// row pass, stored-tile schedule
+// ===========================================================================
+// The column pass stored every packed dS^T (attention) / dG^T (solve) tile, tile
+// (key block i, row block j) at pair index j (j + 1) / 2 + i (attention, i <= j)
+// or j (j - 1) / 2 + i (solve, i < j).  The row pass is then a streamed GEMM:
+//   dQ_j = s sum_{i <= j} (dS^T_ij)^T K_i        dK^row_j = sum_{i < j} (dG^T_ij)^T K^_i
+// with the stored tile as the MN-major A operand, in the same key-block order
+// (and so with the same fp32 accumulation order) as the recomputing row pass.
+// Warps 0-3 epilogue (TMEM lane = tile row), warp 4 TMA, warp 5 MMA; three
+// stages of (stored tile, K tile), accumulator double-buffered in TMEM.
+namespace bwds {
+constexpr int kStages = 3;
+constexpr int kThreads = 192;
+constexpr uint32_t kOffBar = kStages * 65536u;
+enum { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, ACC_FREE0 = ACC_FULL0 + 2,
+       DRAIN = ACC_FREE0 + 2, NBAR };
+constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
+}  // namespace bwds
+
+template <bool SOLVE>
+__global__ void __launch_bounds__(bwds::kThreads, 1)
+    lucid_bwd_row_stored_kernel(const __grid_constant__ CUtensorMap tmT, const __grid_constant__ CUtensorMap tmB,
+                                BwdArgs p) {
+  using namespace bwds;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + kOffBar;
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + kOffBar + NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagBwdRowStored};
+  auto sT = [&](uint32_t n) { return sbase + (n % kStages) * 65536u; };
+  auto sB = [&](uint32_t n) { return sbase + (n % kStages) * 65536u + 32768u; };
+  const int warp = warp_id(), lane = lane_id();
+  if ((sbase & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (kTagBwdRowStored << 20));
+    return;
+  }
+  if (threadIdx.x == 128) {
+    for (int s2 = 0; s2 < kStages; ++s2) {
+      mbar_init(bar(FULL0 + s2), 1);
+      mbar_init(bar(EMPTY0 + s2), 1);
+    }
+    for (int a2 = 0; a2 < 2; ++a2) {
+      mbar_init(bar(ACC_FULL0 + a2), 1);
+      mbar_init(bar(ACC_FREE0 + a2), 128);
+    }
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmT);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int BH = SOLVE ? p.B * p.Hkv : p.B * p.Hq;
+  const int G = p.Hq / p.Hkv;
+  const int blk1 = p.blk1 > 0 ? p.blk1 : p.NB, nblk = blk1 - p.blk0;
+  const int total = nblk * BH;
+  auto decode = [&](int idx, int& j, int& b, int& ha, int& hk) {
+    j = blk1 - 1 - idx % nblk;   // head-major, longest rows first (as the recomputing row pass)
+    const int bh = idx / nblk;
+    b = bh / (SOLVE ? p.Hkv : p.Hq);
+    ha = bh % (SOLVE ? p.Hkv : p.Hq);
+    hk = SOLVE ? ha : ha / G;
+  };
+  auto ntiles = [&](int j) { return SOLVE ? j : j + 1; };
+  auto pair0 = [&](int j) { return SOLVE ? j * (j - 1) / 2 : j * (j + 1) / 2; };
+
+  if (warp == 4) {
+    // ======================= TMA producer =======================
+    if (lane == 0) {
+      uint32_t n = 0;
+      int last[kStages];
+      for (int s2 = 0; s2 < kStages; ++s2) last[s2] = -1;
+      bool ok = true;
+      const uint64_t pol = l2_policy_evict_first();   // each stored tile is read once
+      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
+        int j, b, ha, hk;
+        decode(idx, j, b, ha, hk);
+        const int T = ntiles(j), base = pair0(j);
+        for (int t = 0; t < T; ++t, ++n) {
+          const uint32_t st = n % kStages, use = n / kStages;
+          if (!mbar_wait(bar(EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
+          last[st] = use & 1;
+          mbar_arrive_expect_tx(bar(FULL0 + st), 65536);
+          tma_load_tile_hint(sT(n), &tmT, bar(FULL0 + st), (base + t) * 128, ha, b, pol);
+          tma_load_tile(sB(n), &tmB, bar(FULL0 + st), t * 128, hk, b);
+        }
+      }
+      for (int s2 = 0; s2 < kStages; ++s2)
+        if (last[s2] >= 0) mbar_wait_timed(bar(FULL0 + s2), (uint32_t)last[s2], kDrainNs);
+    }
+  } else if (warp == 5) {
+    // ======================= MMA issuer =======================
+    if (lane == 0) {
+      uint32_t n = 0, item = 0;
+      for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+        int j, b, ha, hk;
+        decode(idx, j, b, ha, hk);
+        const int T = ntiles(j);
+        const uint32_t ab2 = item & 1u, use2 = item >> 1;
+        if (!mbar_wait(bar(ACC_FREE0 + ab2), (use2 & 1) ^ 1, ab)) break;
+        tc_fence_after();
+        bool ok = true;
+        for (int t = 0; t < T; ++t, ++n) {
+          const uint32_t st = n % kStages;
+          if (!mbar_wait(bar(FULL0 + st), (n / kStages) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          umma_tile(tmem + 128u * ab2, sT(n), true, sB(n), true, t > 0 ? 1u : 0u);
+          umma_commit(bar(EMPTY0 + st));
+        }
+        if (!ok) break;
+        umma_commit(bar(ACC_FULL0 + ab2));
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    }
+  } else {
+    // ======================= epilogue warps 0-3 =======================
+    const int r = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    uint32_t item = 0;
+    for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+      int j, b, ha, hk;
+      decode(idx, j, b, ha, hk);
+      const int T = ntiles(j);
+      const uint32_t ab2 = item & 1u, use2 = item >> 1;
+      if (!warp_wait_b(bar(ACC_FULL0 + ab2), use2 & 1, ab)) break;
+      tc_fence_after();
+      const int row = j * 128 + r;
+      const long long bha = (long long)b * (SOLVE ? p.Hkv : p.Hq) + ha;
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        float av[32];
+        if (T > 0) {
+          tmem_ld32(tmem + 128u * ab2 + lane_base + 32u * (uint32_t)q, av);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) av[e] = 0.f;
+        }
+        if (SOLVE) {
+          float* dst = p.dk_row + (bha * p.Npad + row) * kHeadDim + 32 * q;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            reinterpret_cast<float4*>(dst)[c] = make_float4(av[4 * c], av[4 * c + 1], av[4 * c + 2], av[4 * c + 3]);
+        } else if (row < p.N) {
+          bf16* dst = p.dq + (long long)b * p.dq_sb + (long long)ha * p.dq_sh + (long long)row * p.dq_sn + 32 * q;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) av[e] *= p.scale;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) st_bf16x8(dst + c * 8, av + c * 8);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar(ACC_FREE0 + ab2));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 // --------------------------------------------------------------------------
 // elementwise helpers of the backward
 // --------------------------------------------------------------------------
@@ -947,7 +1162,8 @@ static cudaError_t set_smem(K kernel, uint32_t bytes) {
 }
 
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
-                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a, cudaStream_t st) {
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const CUtensorMap& tS, const BwdArgs& a,
+                           cudaStream_t st) {
   const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
   const int total = nblk * a.B * a.Hkv;
   if (total <= 0) return cudaSuccess;
@@ -955,10 +1171,10 @@ cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap
   cudaError_t e;
   if (solve) {
     if ((e = set_smem(lucid_bwd_col_kernel<true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
+    lucid_bwd_col_kernel<true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
   } else {
     if ((e = set_smem(lucid_bwd_col_kernel<false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
+    lucid_bwd_col_kernel<false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
   }
   return cudaGetLastError();
 }
@@ -976,6 +1192,24 @@ cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap
   } else {
     if ((e = set_smem(lucid_bwd_row_kernel<false>, bwdr::kSmemBytes)) != cudaSuccess) return e;
     lucid_bwd_row_kernel<false><<<grid, kBwdThreads, bwdr::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, a);
+  }
+  return cudaGetLastError();
+}
+
+// Row pass of the stored-tile schedule: tT = the stored tiles, tB = K (attention) / K^ (solve).
+cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUtensorMap& tB, const BwdArgs& a,
+                                  cudaStream_t st) {
+  const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
+  const int total = nblk * a.B * (solve ? a.Hkv : a.Hq);
+  if (total <= 0) return cudaSuccess;
+  const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, bwd_num_sms()) : bwd_num_sms());
+  cudaError_t e;
+  if (solve) {
+    if ((e = set_smem(lucid_bwd_row_stored_kernel<true>, bwds::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_row_stored_kernel<true><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tT, tB, a);
+  } else {
+    if ((e = set_smem(lucid_bwd_row_stored_kernel<false>, bwds::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_row_stored_kernel<false><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tT, tB, a);
   }
   return cudaGetLastError();
 }

@@ -73,6 +73,10 @@ struct BwdArgs {
   // (context parallel: the rest of the sequence is held as received from other ranks).
   // max_ctas caps the persistent grid (0: #SMs).
   int blk0 = 0, blk1 = 0, max_ctas = 0;
+  // stored-tile schedule: the column pass also stores every packed dS^T (attention) /
+  // dG^T (solve) tile it computes, and the row pass streams them instead of
+  // recomputing S and dP (tensor map passed to both kernels)
+  int store_tiles = 0;
 };
 
 // Decode step (get_new_v_prime) and decode attention: one pass over the caches.

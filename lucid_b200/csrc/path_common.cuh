@@ -142,18 +142,6 @@ enum : int { kTagPathGemm = 8, kTagPathScores = 9, kTagPathSolve = 10, kTagPathS
 // 128-thread named barrier helpers for the 256 epilogue threads.
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// TMA tile store (two 64-column boxes) from a swizzled shared-memory tile.
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(m)),
-      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-__device__ __forceinline__ void tma_store_tile(const CUtensorMap* m, uint32_t src, int row0, int c2, int c3) {
-  tma_store_4d(m, src, 0, row0, c2, c3);
-  tma_store_4d(m, src + 16384, 64, row0, c2, c3);
-}
 
 // Packed bf16 A-operand address in TMEM of K-slice kk when each 64-column
 // half hf of a 128-column fp32 region was rewritten in place as 32 columns

@@ -34,7 +34,7 @@ enum : int {
 };
 // kernel tags
 enum : int { kTagFwdSolve = 1, kTagFwdAttn = 2, kTagBwdColAttn = 3, kTagBwdColSolve = 4,
-             kTagBwdRowAttn = 5, kTagBwdRowSolve = 6, kTagSelftest = 7 };
+             kTagBwdRowAttn = 5, kTagBwdRowSolve = 6, kTagSelftest = 7, kTagBwdRowStored = 15 };
 
 // Wall-clock bound for any spin wait inside a kernel.  A correct launch never
 // comes close (the longest legitimate wait is one work item, milliseconds);
@@ -207,6 +207,54 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 }
 // wait until all committed bulk groups completed (global writes included)
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// TMA tile store (two 64-column boxes) from a swizzled shared-memory tile,
+// tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_tile(const CUtensorMap* m, uint32_t src, int row0, int c2, int c3) {
+  tma_store_4d(m, src, 0, row0, c2, c3);
+  tma_store_4d(m, src + 16384, 64, row0, c2, c3);
+}
+
+// L2 policy for data streamed once (written or read a single time): evicted first,
+// so that it does not push the reused tiles of the current head out of L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_store_4d_hint(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3,
+                                                  uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4, %5}], [%1], %6;" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_tile_hint(const CUtensorMap* m, uint32_t src, int row0, int c2, int c3,
+                                                    uint64_t pol) {
+  tma_store_4d_hint(m, src, 0, row0, c2, c3, pol);
+  tma_store_4d_hint(m, src + 16384, 64, row0, c2, c3, pol);
+}
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1,
+                                                 int c2, int c3, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_tile_hint(uint32_t dst, const CUtensorMap* m, uint32_t bar, int row0, int c2,
+                                                   int c3, uint64_t pol) {
+  tma_load_4d_hint(dst, m, bar, 0, row0, c2, c3, pol);
+  tma_load_4d_hint(dst + 16384, m, bar, 64, row0, c2, c3, pol);
+}
 
 // Load one [128 x 128] bf16 tile (two 64-column boxes) whose rows start at
 // `row0` of matrix (c2, c3).  Box k of the tile lands at dst + k*16 KB.

@@ -25,6 +25,8 @@ dimension as ``d``.  There is no CPU path: CPU tensors raise.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
@@ -68,6 +70,20 @@ def _s3(t: torch.Tensor):
 
 def _ws(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _stored_tiles_fit(nbytes: int, device) -> bool:
+    """The stored-tile backward schedule (the column pass stores its packed dS^T tiles,
+    the row pass streams them instead of recomputing S and dP) trades O(N^2) memory
+    for a third of the row pass's tensor work; take it when its workspace fits in
+    half of what this process can still allocate.  LUCID_B200_STORED_TILES=0 / 1
+    forces the choice."""
+    env = os.environ.get("LUCID_B200_STORED_TILES")
+    if env is not None:
+        return env != "0"
+    free, _ = torch.cuda.mem_get_info(device)
+    avail = free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+    return nbytes <= 0.5 * avail
 
 
 # ---------------------------------------------------------------------------
@@ -137,7 +153,9 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
     dq = torch.empty(B, Hq, N, W, dtype=torch.bfloat16, device=dev)
     dk = torch.empty(B, Hkv, Np, W, dtype=torch.float32, device=dev)
     dx = torch.empty(B, Hkv, Np, W, dtype=torch.float32, device=dev)
-    ws = _ws(lib.lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
+    nbytes = lib.lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D)
+    fast = lib.lucid_attn_bwd_fast_workspace_bytes(B, Hq, Hkv, N, D)
+    ws = _ws(fast if _stored_tiles_fit(fast, dev) else nbytes, dev)
     rc = lib.lucid_attn_bwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), dot.data_ptr(),
                             *_s3(dot), lse.data_ptr(), dq.data_ptr(), *_s3(dq), dk.data_ptr(),

@@ -167,6 +167,26 @@ def test_fused_fwd_bwd_matches_oracle(cuda_device, B, Hq, Hkv, N, keys, qs, D):
     assert_bf16_close(_np(v.grad), dv_ref, "dV", G)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 2, 2, 1000), (2, 4, 1, 384)])
+def test_attn_bwd_stored_tiles_equal_recompute(cuda_device, monkeypatch, B, Hq, Hkv, N):
+    """The stored-tile schedule streams the column pass's own bf16 dS^T tiles through
+    the row pass in the recomputing pass's key-block order: bit-identical results."""
+    import torch
+    from lucid_b200 import attn_bwd, attn_fwd, solve_fwd
+    q_, k_, v_, do_ = _rand_inputs(31 + N, B, Hq, Hkv, N)
+    q, k, v, do = (_t(a, cuda_device) for a in (q_, k_, v_, do_))
+    s = 128 ** -0.5
+    x = solve_fwd(k, v, s, 1e-5)[0]
+    o, lse = attn_fwd(q, k, x, s)
+    out = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("LUCID_B200_STORED_TILES", mode)
+        out[mode] = attn_bwd(q, k, x, o, do, lse, s)
+        torch.cuda.synchronize()
+    for a, b in zip(out["0"], out["1"]):
+        assert torch.equal(a, b)
+
+
 def test_separate_functions_compose(cuda_device):
     """get_v_prime (LucidSolveFunction) followed by the attention function
     (LucidAttnFunction) gives the same result as the fused op."""
