@@ -183,6 +183,10 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale,
  * Out: dk, dv strided bf16 [B,H,N,D].
  */
 size_t lucid_solve_bwd_workspace_bytes(int B, int H, int N, int D);
+/* Workspace of the stored-tile schedule: with at least this many bytes the transposed
+ * solve also stores every bf16 dG^T tile (B*H*ceil(N/128)*(ceil(N/128)-1)/2 tiles of
+ * 32 KB) and the row pass streams them instead of recomputing E and D; same results. */
+size_t lucid_solve_bwd_fast_workspace_bytes(int B, int H, int N, int D);
 int lucid_solve_bwd(int B, int H, int N, int D, float scale,
                     const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                     const void* x, const void* khat, const void* u,

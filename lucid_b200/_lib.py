@@ -50,6 +50,7 @@ SIGNATURES = {
                        + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p] + [c_void_p] + S3
                        + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),
     "lucid_solve_bwd_workspace_bytes": (c_size_t, [c_int] * 4),
+    "lucid_solve_bwd_fast_workspace_bytes": (c_size_t, [c_int] * 4),
     "lucid_solve_bwd": (c_int, [c_int] * 4 + [c_float] + [c_void_p] + S3 + [c_void_p] * 5
                         + [c_void_p, c_void_p] + [c_void_p] + S3 + [c_void_p] + S3
                         + [c_void_p, c_size_t, c_void_p]),

@@ -268,6 +268,12 @@ size_t lucid_solve_bwd_workspace_bytes(int B, int H, int N, int D) {
          align256(rows * kHeadDim * sizeof(bf16)) + 2 * align256(rows * kHeadDim * sizeof(float));
 }
 
+// Stored-tile schedule: one bf16 dG^T tile per (batch, head, column block i < row block j).
+size_t lucid_solve_bwd_fast_workspace_bytes(int B, int H, int N, int D) {
+  const size_t nb = (size_t)nb_of(N);
+  return lucid_solve_bwd_workspace_bytes(B, H, N, D) + align256((size_t)B * H * (nb * (nb - 1) / 2) * kTileBytes);
+}
+
 int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int64_t k_sb, int64_t k_sh,
                     int64_t k_sn, const void* x, const void* khat, const void* u, const float* rstd,
                     const float* dinv, const float* dx_f32, const float* dk_add, void* dk, int64_t dk_sb,
@@ -302,6 +308,13 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   if (!tmap_internal(&tK, khat, B, H, Npad) || !tmap_internal(&tX, x, B, H, Npad) ||
       !tmap_internal(&tDV, dv_int, B, H, Npad) || !tmap_internal(&tU, u, B, H, Npad))
     return LUCID_ERR_TENSORMAP;
+  // a workspace large enough for the dG^T tiles selects the stored-tile schedule
+  const size_t npair = (size_t)NB * (NB - 1) / 2;
+  const bool stored = npair > 0 && workspace_bytes >= lucid_solve_bwd_fast_workspace_bytes(B, H, N, D) &&
+                      npair * 128 < (size_t)1 << 31;
+  CUtensorMap tS = tU;
+  if (stored && !tmap_internal(&tS, ws + lucid_solve_bwd_workspace_bytes(B, H, N, D), B, H, (int)(npair * 128)))
+    return LUCID_ERR_TENSORMAP;
   BwdArgs ba{};
   ba.B = B; ba.Hq = H; ba.Hkv = H; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
@@ -309,15 +322,16 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   ba.dinv = dinv; ba.dx_in = dx_f32; ba.dv = dv_int;
   ba.flags = flags;
   ba.status = status;
+  ba.store_tiles = stored ? 1 : 0;
   cudaError_t e;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, tU, ba, st);
+    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, tS, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD_ROW, st);
-    e = launch_bwd_row(true, tK, tDV, tK, tX, ba, st);
+    e = stored ? launch_bwd_row_stored(true, tS, tK, ba, st) : launch_bwd_row(true, tK, tDV, tK, tX, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   return to_status(launch_solve_finalize(

@@ -314,11 +314,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
-  } else if (warp == kBwdWarpStore && !SOLVE && p.store_tiles != 0) {
-    // ============ tile store (attention, stored-tile schedule) ============
-    // per tile: once the 256 epilogue threads staged the packed dS^T tile, store it to
-    // pair j (j + 1) / 2 + i of query head hk G + g (evict-first: it is read once), and
-    // free the staging tile as soon as the store has read it
+  } else if (warp == kBwdWarpStore && p.store_tiles != 0) {
+    // ============ tile store (stored-tile schedule) ============
+    // per tile: once the 256 epilogue threads staged the packed tile (attention dS^T of
+    // key block i, query block j >= i: pair j (j + 1) / 2 + i of query head hk G + g;
+    // solve dG^T of column block i, row block j > i: pair j (j - 1) / 2 + i of head hk),
+    // store it (evict-first: it is read once) and free the staging tile as soon as the
+    // store has read it
     if (lane == 0) {
       Ph stg_ready;
       bool ok = true;
@@ -331,7 +333,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           int g, j;
           tile_at(i, t, g, j);
           if (!mbar_wait(bar(STG_READY), stg_ready.full(), ab)) { ok = false; break; }
-          tma_store_tile_hint(&tmS, sDS, (j * (j + 1) / 2 + i) * 128, hk * G + g, b, pol);
+          if (SOLVE)
+            tma_store_tile_hint(&tmS, sDS, (j * (j - 1) / 2 + i) * 128, hk, b, pol);
+          else
+            tma_store_tile_hint(&tmS, sDS, (j * (j + 1) / 2 + i) * 128, hk * G + g, b, pol);
           bulk_commit();
           bulk_wait_read_all();
           mbar_arrive(bar(STG_FREE));
@@ -350,11 +355,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float kLog2e = 1.4426950408889634f;
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
-    Ph sd_full, ds_free, t_full, acc_full, acc2_full, stg_free;
+    Ph sd_full, ds_free, t_full, acc_full, acc2_full;
     uint32_t n_kv = 0, item = 0;
-    // attention, stored-tile schedule: every packed dS^T tile also goes to global
-    // memory through the (otherwise unused) sDS tile, stored by warp kBwdWarpStore
-    const bool stage = !SOLVE && p.store_tiles != 0;
+    // stored-tile schedule: every packed dS^T (attention) / dG^T (solve) tile also goes
+    // to global memory through the sDS tile, stored by warp kBwdWarpStore.  n_st counts
+    // the tiles staged so far; the staging tile is free for tile n_st once STG_FREE has
+    // completed n_st times (the solve's diagonal steps also use sDS: they wait for the
+    // item's last store, and an item's first staged tile waits for the previous item's
+    // last diagonal MMA in place of its first diagonal step)
+    const bool stage = p.store_tiles != 0;
+    uint32_t n_st = 0;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
       int i, b, hk;
       decode(idx, i, b, hk);
@@ -380,8 +390,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
         const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
                                 : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
-        // the staging tile is free once the store warp saw the previous tile's store read it
-        if (stage && !warp_wait_b(bar(STG_FREE), stg_free.empty(), ab)) { ok = false; break; }
+        if (stage) {
+          if (n_st > 0 && !warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) { ok = false; break; }
+          if (SOLVE && t == 0 && !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) { ok = false; break; }
+        }
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const int cb = (int)c0 + 32 * q;
@@ -431,6 +443,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (stage) {
           fence_proxy_async_smem();
           mbar_arrive(bar(STG_READY));
+          ++n_st;
         }
       }
       if (!ok) break;
@@ -482,7 +495,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           rr[q][4 * c + 3] = x4.w - a1[4 * c + 3];
         }
       }
-      if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) break;
+      if (stage && T > 0) {
+        // the item's staged tiles: wait for the last store's read of sDS
+        if (!warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) break;
+      } else if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) {
+        break;
+      }
 #pragma unroll
       for (int q = 0; q < 2; ++q) tile_store_row32(sDS, r, 2 * h + q, rr[q]);
       fence_proxy_async_smem();

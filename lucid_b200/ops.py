@@ -173,7 +173,9 @@ def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None, 
     dev = k.device
     dk = torch.empty(B, H, N, W, dtype=torch.bfloat16, device=dev)
     dv = torch.empty(B, H, N, W, dtype=torch.bfloat16, device=dev)
-    ws = _ws(lib.lucid_solve_bwd_workspace_bytes(B, H, N, D), dev)
+    nbytes = lib.lucid_solve_bwd_workspace_bytes(B, H, N, D)
+    fast = lib.lucid_solve_bwd_fast_workspace_bytes(B, H, N, D)
+    ws = _ws(fast if _stored_tiles_fit(fast, dev) else nbytes, dev)
     rc = lib.lucid_solve_bwd(B, H, N, D, float(scale), k.data_ptr(), *_s3(k), x_int.data_ptr(),
                              khat.data_ptr(), u.data_ptr(), rstd.data_ptr(), dinv.data_ptr(),
                              dx_f32.data_ptr(), dk_add.data_ptr() if dk_add is not None else None,

@@ -187,6 +187,27 @@ def test_attn_bwd_stored_tiles_equal_recompute(cuda_device, monkeypatch, B, Hq, 
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("B,H,N,keys", [(1, 2, 1000, "corr"), (2, 1, 384, "iid"), (1, 1, 128, "iid")])
+def test_solve_bwd_stored_tiles_equal_recompute(cuda_device, monkeypatch, B, H, N, keys):
+    """Solve backward: the stored dG^T tiles streamed through the row pass give the
+    recomputing schedule's results bit for bit (N = 128: a single block, no tiles)."""
+    import torch
+    from lucid_b200 import solve_bwd, solve_fwd
+    _, k_, v_, _ = _rand_inputs(47 + N, B, H, H, N, keys=keys)
+    k, v = _t(k_, cuda_device), _t(v_, cuda_device)
+    s = 128 ** -0.5
+    x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
+    g = torch.Generator(device="cpu").manual_seed(N)
+    dx = torch.randn(x.shape, generator=g).to(cuda_device)
+    out = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("LUCID_B200_STORED_TILES", mode)
+        out[mode] = solve_bwd(k, x, khat, u, rstd, dinv, dx, s)
+        torch.cuda.synchronize()
+    for a, b in zip(out["0"], out["1"]):
+        assert torch.equal(a, b)
+
+
 def test_separate_functions_compose(cuda_device):
     """get_v_prime (LucidSolveFunction) followed by the attention function
     (LucidAttnFunction) gives the same result as the fused op."""
