@@ -814,8 +814,13 @@ def main(argv=None):
     pk_burst, pk_sust, hbm, pk_kind = peaks()
     per_stage_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": 1,
                        "solve_bwd": 4, "solve_bwd_row": 1}
-    executed_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": 3,
-                      "solve_bwd": 4, "solve_bwd_row": 3}
+    # the stored-tile schedule (chosen by the ops when its workspace fits) streams the
+    # column passes' tiles through the row passes: one GEMM per tile, no recompute
+    from lucid_b200.ops import stored_tiles_fit
+    stored = stored_tiles_fit(lib.lucid_attn_bwd_fast_workspace_bytes(B, H, H, N, D), dev)
+    row_exec = 1 if stored else 3
+    executed_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": row_exec,
+                      "solve_bwd": 4, "solve_bwd_row": row_exec}
     stage_ms = {}
     with torch.no_grad():
         x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
@@ -953,6 +958,7 @@ def main(argv=None):
                                     "ratio_vs_our_attention": ms / our_attn_ms},
         "stage_ms": stage_ms,
         "stage_tflops": stage_tflops,
+        "backward_schedule": "stored tiles" if stored else "recompute",
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": pk_burst,
                      "unit": "TFLOP/s", "frac": achieved / pk_burst, "traffic": traffic,
                      "peak_kind": f"{pk_kind} burst bf16 (kernel timed alone)"},

@@ -34,7 +34,7 @@ from . import _lib
 __all__ = [
     "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
     "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
-    "lucid_attention", "padded_len", "decode_update", "decode_attention",
+    "lucid_attention", "padded_len", "decode_update", "decode_attention", "stored_tiles_fit",
 ]
 
 
@@ -72,7 +72,7 @@ def _ws(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
-def _stored_tiles_fit(nbytes: int, device) -> bool:
+def stored_tiles_fit(nbytes: int, device) -> bool:
     """The stored-tile backward schedule (the column pass stores its packed dS^T tiles,
     the row pass streams them instead of recomputing S and dP) trades O(N^2) memory
     for a third of the row pass's tensor work; take it when its workspace fits in
@@ -155,7 +155,7 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
     dx = torch.empty(B, Hkv, Np, W, dtype=torch.float32, device=dev)
     nbytes = lib.lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D)
     fast = lib.lucid_attn_bwd_fast_workspace_bytes(B, Hq, Hkv, N, D)
-    ws = _ws(fast if _stored_tiles_fit(fast, dev) else nbytes, dev)
+    ws = _ws(fast if stored_tiles_fit(fast, dev) else nbytes, dev)
     rc = lib.lucid_attn_bwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), dot.data_ptr(),
                             *_s3(dot), lse.data_ptr(), dq.data_ptr(), *_s3(dq), dk.data_ptr(),
@@ -175,7 +175,7 @@ def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None, 
     dv = torch.empty(B, H, N, W, dtype=torch.bfloat16, device=dev)
     nbytes = lib.lucid_solve_bwd_workspace_bytes(B, H, N, D)
     fast = lib.lucid_solve_bwd_fast_workspace_bytes(B, H, N, D)
-    ws = _ws(fast if _stored_tiles_fit(fast, dev) else nbytes, dev)
+    ws = _ws(fast if stored_tiles_fit(fast, dev) else nbytes, dev)
     rc = lib.lucid_solve_bwd(B, H, N, D, float(scale), k.data_ptr(), *_s3(k), x_int.data_ptr(),
                              khat.data_ptr(), u.data_ptr(), rstd.data_ptr(), dinv.data_ptr(),
                              dx_f32.data_ptr(), dk_add.data_ptr() if dk_add is not None else None,
