@@ -639,11 +639,18 @@ def cp_reference_arm(args):
 
 
 def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
-    from lucid_b200.cp import balanced_bounds, cp_lucid_attention, cp_lucid_attention_forward, train_bounds
+    from lucid_b200.cp import (Layout, balanced_bounds, cp_lucid_attention, cp_lucid_attention_forward,
+                               train_bounds, zigzag_layout)
     B, H, N, D = 1, 32, 131072, 128
     bwd = not args.cp_forward_only
-    bounds = train_bounds(N, world) if bwd else balanced_bounds(N, world)
-    C = bounds[rank + 1] - bounds[rank]
+    if args.cp_layout == "zigzag":
+        layout = zigzag_layout(N, world)
+        layout_desc = f"zigzag: {2 * world} segments, rank r owning r and {2 * world - 1}-r"
+    else:
+        bounds = train_bounds(N, world) if bwd else balanced_bounds(N, world)
+        layout = Layout.contiguous(bounds)
+        layout_desc = f"contiguous chunks ({'train_bounds' if bwd else 'balanced_bounds'} {bounds})"
+    C = layout.local_rows(rank)
     s = D ** -0.5
     # K = 0.6 s + 0.8 n with s shared per head (the same on every rank) and n per token
     gs = torch.Generator(device=dev).manual_seed(5000)
@@ -659,9 +666,9 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
 
     def step():
         if not bwd:
-            return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
+            return cp_lucid_attention_forward(q, k, v, scale=s, head_groups=args.head_groups, layout=layout)
         q.grad = k.grad = v.grad = None
-        o = cp_lucid_attention(q, k, v, scale=s, head_groups=args.head_groups, bounds=bounds)
+        o = cp_lucid_attention(q, k, v, scale=s, head_groups=args.head_groups, layout=layout)
         o.backward(do)
         return o.detach()
 
@@ -701,7 +708,17 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
     # launches of rank 0 per step: forward prep / solve / attention per group; backward delta,
     # prep of the later rows, flag publishes (one per later rank), attention column pass,
     # transposed solve, solve row pass + finalize and attention row pass per group
-    launches = 3 * G + ((1 + (1 if world > 1 else 0) + 5) * G + G * (world - 1) if bwd else 0)
+    mine = layout.mine(rank)
+    first, last = mine[0], mine[-1]
+    foreign_before = sum(1 for x in range(last) if layout.owner(x) != rank)
+    foreign_after = sum(1 for x in range(first + 1, layout.n) if layout.owner(x) != rank)
+    # rank 0 per step: forward prep of every segment up to its last, solve + attention per own
+    # segment, one flag publish per received segment (all per head group); backward delta,
+    # prep of the later segments, attention column, transposed solve, solve row + finalize and
+    # attention row per own segment, one publish per received dV segment
+    launches = G * ((last + 1) + 2 * len(mine) + foreign_before)
+    if bwd:
+        launches += G * (len(mine) + (layout.n - 1 - last) + 5 * len(mine) + foreign_after)
     what = "forward + backward" if bwd else "FORWARD"
     line = {
         "metric": CP_METRIC if bwd else CP_METRIC_FWD, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
@@ -709,8 +726,7 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"LUCID attention {what} B{B} H{H} N{N} D{D}, keys 0.6 s + 0.8 n, sequence split "
-                               f"in {world} contiguous chunks ({'train_bounds' if bwd else 'balanced_bounds'} "
-                               f"{bounds}), {G} head groups pipelined",
+                               f"over {world} ranks, {layout_desc}, {G} head groups pipelined",
                    "global_batch": B, "seq_len": N, "parallelism": f"context parallel x{world} (NCCL send/recv)",
                    "l2": "inputs larger than L2, no flush"},
         "tokens_per_s": B * N / (ms * 1e-3),
@@ -736,6 +752,8 @@ def main(argv=None):
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill"], default="32k")
     ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
+    ap.add_argument("--cp-layout", choices=["zigzag", "contiguous"], default="zigzag",
+                    help="cp128k: rows per rank (zigzag: segments r and 2W-1-r; contiguous: one chunk)")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

@@ -1,48 +1,53 @@
-"""Context-parallel LUCID attention forward for long sequences (the 128K
-configuration): one process per GPU, each rank owning a contiguous chunk of
-C = N / world tokens of every (batch, head).
+"""Context-parallel LUCID attention for long sequences (the 128K
+configuration): one process per GPU, the sequence cut into row segments each
+owned by one rank, forward and backward.
 
 The reference runs long sequences on one GPU (the blockwise solver of
 modeling_lucid.py:285-312 under gradient checkpointing); this module spreads
-one sequence over the GPUs of a node:
+one sequence over the GPUs of a node.
 
-  X = P^-1 V is a forward substitution, so chunk r needs the solved values
-  X_j and the keys K_j of every earlier chunk j < r:
-    R_r = V_r - sum_{j<r} exp(s K^_r K^_j^T - 1/s) X_j ,  X_r = P_rr^-1 R_r
-  and the attention of chunk r's queries needs K_j and X_j of every j <= r.
+Math.  X = P^-1 V is a forward substitution, so segment t needs the solved
+values X_s and the keys K_s of every earlier segment s < t:
+    R_t = V_t - sum_{s<t} exp(s K^_t K^_s^T - 1/s) X_s ,  X_t = P_tt^-1 R_t
+and the attention of segment t's queries needs K_s and X_s of every s <= t.
+In the backward a rank computes every gradient of its own rows: its column
+passes (attention dX / dK over its own key blocks, the transposed solve
+dV = P^-T dX and the column part of dK^) need the rows after each of its
+segments; its row passes (dQ, the row part of dK^) only the rows before,
+which the forward brought in.  No partial sums cross ranks.
 
-Protocol (all point-to-point NCCL send/recv, no collective):
-  1. every rank sends its raw keys to every later rank (they are an input,
-     so this starts at once); a receiver normalises them (k^ only);
-  2. the kv heads are split into head groups; for each group g in order,
-     rank r waits for X_j(g) of every j < r, marks those row blocks solved
-     (the wavefront solve's per-block flags), solves its own row blocks,
-     sends its X_r(g) to every later rank and runs the attention of its own
-     queries for the group.  Rank r solves group g while rank r-1 already
-     works on group g+1, so the serial chain across ranks is pipelined over
-     the head groups.
-  Kernels never wait on another launch: every dependency is a stream-ordered
-  NCCL receive, and the persistent kernels leave `reserve_sms` SMs free so
-  the NCCL kernels of the other groups run alongside.
+Layouts (Layout): contiguous chunks (one segment per rank; even_bounds,
+balanced_bounds, train_bounds) or zigzag (zigzag_layout: 2W equal segments,
+rank r owning segments r and 2W-1-r).  With contiguous chunks the forward's
+work (growing with the row) and the backward's column passes (shrinking with
+it) cannot both be balanced; the zigzag pairs an early and a late segment on
+every rank and balances each phase on its own.
 
-Backward (ChunkProtocol.backward, after run): a rank computes every
-gradient of its own rows.  Its column passes (attention dX / dK over its
-own key blocks, the transposed solve dV = P^-T dX and the column part of
-dK^) need the rows after its chunk, its row passes (dQ, the row part of
-dK^) only the rows before it, which the forward already brought in.  So
-the messages mirror the forward's, flowing from higher to lower ranks:
-  1. every rank sends q, dO, its raw keys, lse and delta = rowsum(dO o O)
-     of its rows to every earlier rank (inputs and forward outputs, so
-     this starts at once);
-  2. for each head group in order, rank r waits for dV_j(g) of every
-     j > r, publishes those blocks, runs its transposed solve, sends its
-     dV_r(g) to every earlier rank, then runs the attention column pass of
-     group g+1 and the row passes of group g while rank r-1 solves.
-The chain of the backward runs from the last rank to the first.
-
-Chunks may differ in length.  balanced_bounds equalises the forward's work
-(the solve and the attention of row t cost ~t); train_bounds equalises the
-forward plus the backward, whose column passes cost ~N-t and row passes ~t.
+Protocol (all point-to-point NCCL send/recv on one communicator per pair of
+ranks, no collective):
+  forward   1. every rank sends the raw keys of each of its segments to every
+               rank owning a later segment (inputs: this starts at once);
+            2. for each own segment t in sequence order and each kv-head group
+               g in order, a rank receives X_s(g) of every foreign s < t,
+               marks those row blocks solved (the wavefront solve's per-block
+               flags), solves segment t, sends X_t(g) to every rank owning a
+               later segment and runs the attention of t's queries for g;
+  backward  the mirror image: q, dO, raw keys, lse and delta = rowsum(dO o O)
+            of each own segment go to every rank owning an earlier segment;
+            then for each own segment t in reverse sequence order and each
+            group, dV_s(g) of every foreign s > t is received, the transposed
+            solve of t runs, dV_t(g) goes to the ranks owning earlier
+            segments, and t's row passes run.
+NCCL matches a pair's sends and receives per direction in issue order, so on
+every pair both ends keep one order: forward messages by (source segment,
+group) ascending, backward messages by source segment descending then group
+ascending.  A rank sends in that order by construction (it walks its own
+segments and groups in that order) and posts each receive at its
+segment's turn in the same walk, ahead of need.  Kernels
+never wait on another launch: every cross-rank dependency is a stream-ordered
+NCCL receive, and the persistent kernels leave `reserve_sms` SMs free so the
+NCCL kernels run alongside.  The schedule is checked for deadlock freedom
+with every rank's operations fully serialised (tests/test_cp_cpu.py).
 """
 from __future__ import annotations
 
@@ -51,8 +56,8 @@ import torch.distributed as dist
 
 from . import _lib
 
-__all__ = ["cp_lucid_attention_forward", "cp_lucid_attention", "ChunkProtocol", "KernelBackend", "balanced_bounds",
-           "even_bounds", "train_bounds"]
+__all__ = ["cp_lucid_attention_forward", "cp_lucid_attention", "ChunkProtocol", "KernelBackend", "Layout",
+           "balanced_bounds", "even_bounds", "train_bounds", "zigzag_layout"]
 
 
 def even_bounds(N: int, world: int):
@@ -94,6 +99,72 @@ def train_bounds(N: int, world: int, align: int = 256, col: float = 1.0, row: fl
     return b + [N]
 
 
+class Layout:
+    """The sequence rows [0, N) as segments in sequence order, segment s =
+    rows [lo_s, hi_s) owned by rank owner_s.  A rank's local tensors hold its
+    segments' rows concatenated in sequence order."""
+
+    def __init__(self, segs):
+        self.segs = [(int(lo), int(hi), int(o)) for lo, hi, o in segs]
+        if not self.segs or self.segs[0][0] != 0 or any(
+                self.segs[i][1] != self.segs[i + 1][0] for i in range(len(self.segs) - 1)):
+            raise ValueError("segments must cover [0, N) in order")
+        if any(hi <= lo for lo, hi, _ in self.segs):
+            raise ValueError("empty segment")
+        self.N = self.segs[-1][1]
+        self.n = len(self.segs)
+
+    @classmethod
+    def contiguous(cls, bounds):
+        return cls([(bounds[r], bounds[r + 1], r) for r in range(len(bounds) - 1)])
+
+    def lo(self, s):
+        return self.segs[s][0]
+
+    def hi(self, s):
+        return self.segs[s][1]
+
+    def owner(self, s):
+        return self.segs[s][2]
+
+    def mine(self, r):
+        return [s for s in range(self.n) if self.segs[s][2] == r]
+
+    def local_rows(self, r):
+        return sum(self.hi(s) - self.lo(s) for s in self.mine(r))
+
+    def local_offset(self, s):
+        """Row of segment s's first row in its owner's local tensors."""
+        o = self.owner(s)
+        return sum(self.hi(t) - self.lo(t) for t in range(s) if self.owner(t) == o)
+
+    def later_owners(self, s, r):
+        """Ranks other than r owning a segment after s (they need segment s's
+        forward messages)."""
+        return sorted({self.owner(t) for t in range(s + 1, self.n)} - {r})
+
+    def earlier_owners(self, s, r):
+        return sorted({self.owner(t) for t in range(s)} - {r})
+
+    def check(self, align=256, world=None):
+        if any(lo % align for lo, _, _ in self.segs) or self.N % 128:
+            raise ValueError(f"segment bounds must sit on multiples of {align} rows (N a multiple of 128)")
+        if world is not None and sorted({o for _, _, o in self.segs}) != list(range(world)):
+            raise ValueError("every rank must own at least one segment")
+
+
+def zigzag_layout(N: int, world: int, align: int = 256):
+    """2W segments of (nearly) equal length, rank r owning segments r and
+    2W-1-r: an early and a late segment per rank, so the forward's work
+    (growing with the row) and the backward's column passes (shrinking with
+    it) are both balanced."""
+    n = 2 * world
+    b = [int(round(N * i / n / align)) * align for i in range(n)] + [N]
+    for i in range(1, n):
+        b[i] = min(max(b[i], b[i - 1] + align), N - (n - i) * align)
+    return Layout([(b[i], b[i + 1], i if i < world else n - 1 - i) for i in range(n)])
+
+
 _PAIR_GROUPS = {}
 
 
@@ -111,15 +182,9 @@ def _pair_groups(group):
 
 
 class ChunkProtocol:
-    """The message schedule of the forward chain, independent of how the
-    chunks are computed (``backend``) and of the process group's device.
-
-    Every message flows from a lower to a higher rank, each pair of ranks has
-    its own communicator, and both ends of a pair exchange their messages in
-    the same order (keys, then the values of head group 0, 1, ...).  Rank r
-    posts the receives of group g only after its sends of group g-1, so even
-    if all of a rank's operations ran in issue order every wait would be on a
-    (group, rank) that comes earlier: the schedule cannot deadlock."""
+    """The message schedule of the forward and backward chains, independent of
+    how the segments are computed (``backend``) and of the process group's
+    device.  ``backend.layout`` is the Layout."""
 
     def __init__(self, backend, group=None):
         self.be = backend
@@ -137,95 +202,138 @@ class ChunkProtocol:
         lo, hi = min(self.rank, j), max(self.rank, j)
         return dist.irecv(t, src=self.ranks[j], group=self.pairs[lo, hi])
 
+    def _post(self, buf, src):
+        if isinstance(buf, list):   # a message of several tensors, sent in list order
+            return buf, _MultiReq([self._recv(b, src) for b in buf])
+        return buf, self._recv(buf, src)
+
     def run(self, q, k, v):
-        be, r, W = self.be, self.rank, self.world
+        be, r = self.be, self.rank
+        L = be.layout
+        mine = L.mine(r)
+        last = mine[-1]
         be.set_local(q, k)
-        # 1. raw keys flow to every later rank
-        kbuf = {j: be.empty_chunk(be.H, j) for j in range(r)}
-        reqs = [self._recv(kbuf[j], j) for j in range(r)]
-        ksend = be.own_keys()
-        sends = [self._send(ksend, j) for j in range(r + 1, W)]
-        for rq in reqs:
+        # Messages are issued in one global order, segment by segment in sequence
+        # order: a rank sends its own segment's messages and posts the receives of a
+        # foreign segment it needs (every segment before its last one) at that
+        # segment's turn, so both ends of every pair issue their common messages in
+        # the same order, whichever direction they flow.
+        # 1. raw keys: segment s goes to every other rank owning a later segment
+        sends, keys = [], {}
+        for s in range(L.n):
+            if L.owner(s) == r:
+                for d in L.later_owners(s, r):
+                    sends.append(self._send(be.keys(s), d))
+            elif s < last:
+                keys[s] = self._post(be.empty_chunk(be.H, s), L.owner(s))
+        for s, (buf, rq) in keys.items():
             rq.wait()
-        for j in range(r):
-            be.store_keys(j, kbuf[j])
+            be.store_keys(s, buf)
         be.prep()
-        # 2. solved values, pipelined over head groups
-        for g in range(be.G):
-            xbuf = {j: be.empty_chunk(be.Hg, j) for j in range(r)}
-            reqs = [self._recv(xbuf[j], j) for j in range(r)]
-            for j in range(r):
-                reqs[j].wait()
-                be.store_values(g, j, xbuf[j])
-            be.solve(g, v)
-            xs = be.own_values(g)
-            sends += [self._send(xs, j) for j in range(r + 1, W)]
-            be.attend(g)
-        for s in sends:
-            s.wait()
+        # 2. solved values: an own segment is solved group by group, each X_t(g) sent
+        #    to the ranks owning later segments; a foreign segment's X_s(g) receives
+        #    are posted at its turn and waited right before the first solve needing them
+        posted, stored = {}, set()
+        for t in range(L.n):
+            if L.owner(t) != r:
+                if t < last:
+                    for g in range(be.G):
+                        posted[t, g] = self._post(be.empty_chunk(be.Hg, t), L.owner(t))
+                continue
+            for g in range(be.G):
+                for s in range(t):
+                    if L.owner(s) == r or (s, g) in stored:
+                        continue
+                    buf, rq = posted[s, g]
+                    rq.wait()
+                    be.store_values(g, s, buf)
+                    stored.add((s, g))
+                be.solve(t, g, v)
+                xs = be.own_values(t, g)
+                sends += [self._send(xs, d) for d in L.later_owners(t, r)]
+                be.attend(t, g)
+        for s_ in sends:
+            s_.wait()
         return be.finish()
 
     def backward(self, do):
         """Gradients of this rank's rows after run(): returns what the
-        backend's finish_grad returns (dq, dk, dv of the chunk)."""
-        be, r, W = self.be, self.rank, self.world
+        backend's finish_grad returns (dq, dk, dv of the rank's rows).  The
+        mirror image of run: segments walked from the last one down."""
+        be, r = self.be, self.rank
+        L = be.layout
+        first = L.mine(r)[0]
         be.set_grad(do)
-        # 1. q, dO, raw keys, lse and delta flow to every earlier rank; receives
-        #    from later ranks are posted latest-rank first and sends go to the
-        #    nearest earlier rank first (the forward's order under r -> W-1-r)
-        later = list(range(W - 1, r, -1))
-        earlier = list(range(r - 1, -1, -1))
-        bufs = {j: be.empty_grad_inputs(j) for j in later}
-        reqs = {j: [self._recv(t, j) for t in bufs[j]] for j in later}
-        mine = be.own_grad_inputs()
-        sends = [self._send(t, j) for j in earlier for t in mine]
-        for j in later:
-            for rq in reqs[j]:
-                rq.wait()
-            be.store_grad_inputs(j, bufs[j])
+        # 1. q, dO, raw keys, lse and delta: segment s goes to every other rank
+        #    owning an earlier segment
+        sends, ins = [], {}
+        for s in range(L.n - 1, -1, -1):
+            if L.owner(s) == r:
+                for d in L.earlier_owners(s, r):
+                    sends += [self._send(t_, d) for t_ in be.grad_inputs(s)]
+            elif s > first:
+                ins[s] = self._post(be.empty_grad_inputs(s), L.owner(s))
+        for s, (bufs, rq) in ins.items():
+            rq.wait()
+            be.store_grad_inputs(s, bufs)
         be.prep_later()
-        # 2. dV flows to earlier ranks, pipelined over head groups
-        be.attn_col(0)
-        for g in range(be.G):
-            dbuf = {j: be.empty_chunk(be.Hg, j) for j in later}
-            reqs = [self._recv(dbuf[j], j) for j in later]
-            for j, rq in zip(later, reqs):
-                rq.wait()
-                be.store_dv(g, j, dbuf[j])
-            be.solve_col(g)
-            dvs = be.own_dv(g)
-            sends += [self._send(dvs, j) for j in earlier]
-            if g + 1 < be.G:
-                be.attn_col(g + 1)
-            be.rows(g)
-        for s in sends:
-            s.wait()
+        # 2. dV, per own segment from the last one down and head group in order
+        posted, stored = {}, set()
+        for t in range(L.n - 1, -1, -1):
+            if L.owner(t) != r:
+                if t > first:
+                    for g in range(be.G):
+                        posted[t, g] = self._post(be.empty_chunk(be.Hg, t), L.owner(t))
+                continue
+            be.attn_col(t, 0)
+            for g in range(be.G):
+                for s in range(L.n - 1, t, -1):
+                    if L.owner(s) == r or (s, g) in stored:
+                        continue
+                    buf, rq = posted[s, g]
+                    rq.wait()
+                    be.store_dv(g, s, buf)
+                    stored.add((s, g))
+                be.solve_col(t, g)
+                dv = be.own_dv(t, g)
+                sends += [self._send(dv, d) for d in L.earlier_owners(t, r)]
+                if g + 1 < be.G:
+                    be.attn_col(t, g + 1)
+                be.rows(t, g)
+        for s_ in sends:
+            s_.wait()
         return be.finish_grad()
 
 
-class KernelBackend:
-    """The chunk computations on the B200 kernels (C ABI lucid_cp_*)."""
+class _MultiReq:
+    """Several receives waited as one (a message made of several tensors)."""
 
-    def __init__(self, B, H, Hq, bounds, D, scale, eps, rank, world, head_groups, device, reserve_sms=8):
+    def __init__(self, reqs):
+        self.reqs = reqs
+
+    def wait(self):
+        for rq in self.reqs:
+            rq.wait()
+
+
+class KernelBackend:
+    """The segment computations on the B200 kernels (C ABI lucid_cp_*)."""
+
+    def __init__(self, B, H, Hq, layout, D, scale, eps, rank, world, head_groups, device, reserve_sms=8):
         if D != 128:
             raise NotImplementedError("head_dim must be 128")
-        N = bounds[-1]
-        if len(bounds) != world + 1 or bounds[0] != 0 or any(x % 256 for x in bounds[:-1]) or \
-                any(bounds[j + 1] <= bounds[j] for j in range(world)) or N % 128:
-            raise ValueError("chunk bounds must start at 0, increase, and sit on multiples of 256 rows")
+        layout.check(256, world)
         if H % head_groups or Hq % H:
             raise ValueError("head_groups must divide the kv heads and Hq must be a multiple of H")
+        N = layout.N
+        self.layout = layout
         self.lib = _lib.load()
         self.B, self.H, self.Hq, self.N, self.D = B, H, Hq, N, D
         self.s, self.eps = float(scale), float(eps)
         self.r, self.W = rank, world
         self.G, self.Hg, self.Gq = head_groups, H // head_groups, Hq // H
-        self.bounds = list(bounds)
-        self.C = bounds[rank + 1] - bounds[rank]
+        self.C = layout.local_rows(rank)
         self.NB = N // 128
-        self.blk_lo = bounds[rank] // 128
-        self.blk_hi = bounds[rank + 1] // 128
-        self.row0 = bounds[rank]
         self.dev = device
         n_sm = torch.cuda.get_device_properties(device).multi_processor_count
         self.max_ctas = max(1, n_sm - reserve_sms) if world > 1 else 0
@@ -247,133 +355,150 @@ class KernelBackend:
     def _st(self):
         return torch.cuda.current_stream(self.dev).cuda_stream
 
-    def _rows(self, j):
-        return slice(self.bounds[j], self.bounds[j + 1])
+    def _rows(self, s):
+        return slice(self.layout.lo(s), self.layout.hi(s))
 
-    def empty_chunk(self, heads, j):
-        n = self.bounds[j + 1] - self.bounds[j]
+    def _local(self, s):
+        off = self.layout.local_offset(s)
+        return slice(off, off + self.layout.hi(s) - self.layout.lo(s))
+
+    def _blk(self, s):
+        return self.layout.lo(s) // 128, self.layout.hi(s) // 128
+
+    def _shift(self, t, s, row_dim):
+        """Address of global row 0 of a local tensor (this rank's rows in
+        segment order) for the rows of segment s: the kernels index by global row."""
+        delta = self.layout.local_offset(s) - self.layout.lo(s)
+        return t.data_ptr() + delta * t.stride(row_dim) * t.element_size()
+
+    def empty_chunk(self, heads, s):
+        n = self.layout.hi(s) - self.layout.lo(s)
         return torch.empty(self.B, heads, n, self.D, dtype=torch.bfloat16, device=self.dev)
 
     def _hs(self, g):
         return slice(g * self.Hg, (g + 1) * self.Hg)
 
-    # ---- protocol steps ----
-    def set_local(self, q, k):
-        self.Kf[:, :, self._rows(self.r)] = k
-        self.Qf[:, :, self._rows(self.r)] = q
-
-    def own_keys(self):
-        return self.Kf[:, :, self._rows(self.r)].contiguous()
-
-    def store_keys(self, j, buf):
-        self.Kf[:, :, self._rows(j)] = buf
-
-    def prep(self):
-        lib = self.lib
-        for g in range(self.G):
-            kv = self.Kf[:, self._hs(g)]
-            args = (kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2), self.khat[g].data_ptr(),
-                    self.u[g].data_ptr(), self.rstd[g].data_ptr(), self.dinv[g].data_ptr(), self._st())
-            _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, 0, self.blk_lo, 1,
-                                         *args), "lucid_cp_prep")
-            _lib.check(lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, self.blk_lo,
-                                         self.blk_hi, 0, *args), "lucid_cp_prep")
-
-    def store_values(self, g, j, buf):
-        self.x[g][:, :, self._rows(j)] = buf
-        _lib.check(self.lib.lucid_cp_publish(self.flags[g].data_ptr(), self.B * self.Hg, self.NB,
-                                             self.bounds[j] // 128, self.bounds[j + 1] // 128, self._st()),
-                   "lucid_cp_publish")
-
-    def solve(self, g, v):
-        vg = v[:, self._hs(g)]
-        if vg.stride(-1) != 1:
-            vg = vg.contiguous()
-        # the kernel indexes V by global row: shift the pointer back by this rank's first row
-        vptr = vg.data_ptr() - self.row0 * vg.stride(2) * vg.element_size()
-        _lib.check(self.lib.lucid_cp_solve_fwd(self.B, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi,
-                                               self.max_ctas,
-                                               vptr, vg.stride(0), vg.stride(1), vg.stride(2), self.x[g].data_ptr(),
-                                               self.khat[g].data_ptr(), self.u[g].data_ptr(),
-                                               self.dinv[g].data_ptr(), self.flags[g].data_ptr(),
-                                               self.status.data_ptr(), self._st()), "lucid_cp_solve_fwd")
-        self._vg = vg  # keep a contiguous copy alive until the kernel has run
-
-    def own_values(self, g):
-        return self.x[g][:, :, self._rows(self.r)].contiguous()
-
-    def attend(self, g):
-        hq = slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
-        qg, kg = self.Qf[:, hq], self.Kf[:, self._hs(g)]
-        og = self.o[:, :, hq].transpose(1, 2)   # [B, Hq_g, C, D] view of [B, C, Hq, D]
-        optr = og.data_ptr() - self.row0 * og.stride(2) * og.element_size()
-        _lib.check(self.lib.lucid_cp_attn_fwd(self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, self.blk_lo,
-                                              self.blk_hi, self.max_ctas, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
-                                              kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2),
-                                              self.x[g].data_ptr(), optr, og.stride(0), og.stride(1), og.stride(2),
-                                              self.lse[g].data_ptr(), self.status.data_ptr(), self._st()),
-                   "lucid_cp_attn_fwd")
-
-    def finish(self):
-        self._check_status()
-        return self.o
+    def _hq(self, g):
+        return slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
 
     def _check_status(self):
         st = int(self.status[0].item())
         if st != 0:
             raise _lib.LucidError(f"context-parallel kernels reported status {st:#x} (a bounded wait timed out)")
 
+    # ---- forward ----
+    def set_local(self, q, k):
+        for s in self.layout.mine(self.r):
+            self.Kf[:, :, self._rows(s)] = k[:, :, self._local(s)]
+            self.Qf[:, :, self._rows(s)] = q[:, :, self._local(s)]
+
+    def keys(self, s):
+        return self.Kf[:, :, self._rows(s)].contiguous()
+
+    def store_keys(self, s, buf):
+        self.Kf[:, :, self._rows(s)] = buf
+
+    def _prep(self, s, khat_only):
+        lo, hi = self._blk(s)
+        for g in range(self.G):
+            kv = self.Kf[:, self._hs(g)]
+            _lib.check(self.lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, lo, hi, khat_only,
+                                              kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2),
+                                              self.khat[g].data_ptr(), self.u[g].data_ptr(), self.rstd[g].data_ptr(),
+                                              self.dinv[g].data_ptr(), self._st()), "lucid_cp_prep")
+
+    def prep(self):
+        L, mine = self.layout, self.layout.mine(self.r)
+        for s in range(mine[-1] + 1):
+            if L.owner(s) == self.r:
+                self._prep(s, 0)
+            else:
+                self._prep(s, 1)   # received keys: k^ only
+
+    def store_values(self, g, s, buf):
+        self.x[g][:, :, self._rows(s)] = buf
+        lo, hi = self._blk(s)
+        _lib.check(self.lib.lucid_cp_publish(self.flags[g].data_ptr(), self.B * self.Hg, self.NB, lo, hi,
+                                             self._st()), "lucid_cp_publish")
+
+    def solve(self, t, g, v):
+        vg = v[:, self._hs(g)]
+        if vg.stride(-1) != 1:
+            vg = vg.contiguous()
+        lo, hi = self._blk(t)
+        _lib.check(self.lib.lucid_cp_solve_fwd(self.B, self.Hg, self.N, self.D, self.s, lo, hi, self.max_ctas,
+                                               self._shift(vg, t, 2), vg.stride(0), vg.stride(1), vg.stride(2),
+                                               self.x[g].data_ptr(), self.khat[g].data_ptr(), self.u[g].data_ptr(),
+                                               self.dinv[g].data_ptr(), self.flags[g].data_ptr(),
+                                               self.status.data_ptr(), self._st()), "lucid_cp_solve_fwd")
+        self._vg = vg  # keep a contiguous copy alive until the kernel has run
+
+    def own_values(self, t, g):
+        return self.x[g][:, :, self._rows(t)].contiguous()
+
+    def attend(self, t, g):
+        hq = self._hq(g)
+        qg, kg = self.Qf[:, hq], self.Kf[:, self._hs(g)]
+        og = self.o[:, :, hq].transpose(1, 2)   # [B, Hq_g, C, D] view of [B, C, Hq, D]
+        lo, hi = self._blk(t)
+        _lib.check(self.lib.lucid_cp_attn_fwd(self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, lo, hi,
+                                              self.max_ctas, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
+                                              kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2),
+                                              self.x[g].data_ptr(), self._shift(og, t, 2), og.stride(0), og.stride(1),
+                                              og.stride(2), self.lse[g].data_ptr(), self.status.data_ptr(),
+                                              self._st()), "lucid_cp_attn_fwd")
+
+    def finish(self):
+        self._check_status()
+        return self.o
+
     # ---- backward ----
-    def _hq(self, g):
-        return slice(g * self.Hg * self.Gq, (g + 1) * self.Hg * self.Gq)
-
-    def _shift(self, t, row_dim):
-        """Address of global row 0 of a tensor holding this rank's rows (the
-        kernels index outputs by global row)."""
-        return t.data_ptr() - self.row0 * t.stride(row_dim) * t.element_size()
-
     def set_grad(self, do):
         B, N, D, Hq, H = self.B, self.N, self.D, self.Hq, self.H
         bf = dict(dtype=torch.bfloat16, device=self.dev)
         f32 = dict(dtype=torch.float32, device=self.dev)
+        mine = self.layout.mine(self.r)
         self.dOf = torch.zeros(B, Hq, N, D, **bf)
-        self.dOf[:, :, self._rows(self.r)] = do.transpose(1, 2)
+        for s in mine:
+            self.dOf[:, :, self._rows(s)] = do[:, self._local(s)].transpose(1, 2)
         self.delta = [torch.zeros(B, self.Hg * self.Gq, N, **f32) for _ in range(self.G)]
         for g in range(self.G):
             og = self.o[:, :, self._hq(g)].transpose(1, 2)
             dg = self.dOf[:, self._hq(g)]
-            _lib.check(self.lib.lucid_cp_delta(B, self.Hg * self.Gq, N, D, self.row0, self.row0 + self.C,
-                                               self._shift(og, 2), og.stride(0), og.stride(1), og.stride(2),
-                                               dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2),
-                                               self.delta[g].data_ptr(), self._st()), "lucid_cp_delta")
-        # per-parity scratch of the head group in flight (group g uses g % 2)
+            for s in mine:
+                _lib.check(self.lib.lucid_cp_delta(B, self.Hg * self.Gq, N, D, self.layout.lo(s), self.layout.hi(s),
+                                                   self._shift(og, s, 2), og.stride(0), og.stride(1), og.stride(2),
+                                                   dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2),
+                                                   self.delta[g].data_ptr(), self._st()), "lucid_cp_delta")
+        # per-parity scratch of the head group in flight (group g uses g % 2); dV is kept
+        # per group: a rank's earlier segment needs the dV its later segment solved
         self.dx32 = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
         self.dka32 = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
         self.dkcol = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
         self.dkrow = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]
-        self.dvint = [torch.zeros(B, self.Hg, N, D, **bf) for _ in range(2)]
+        self.dvint = [torch.zeros(B, self.Hg, N, D, **bf) for _ in range(self.G)]
         self.bflags = [torch.zeros(B * self.Hg * self.NB, dtype=torch.int32, device=self.dev) for _ in range(self.G)]
         self.dq = torch.empty(B, Hq, self.C, D, **bf)
         self.dk = torch.empty(B, H, self.C, D, **bf)
         self.dv = torch.empty(B, H, self.C, D, **bf)
 
-    def _own_stats(self, lst):
-        return torch.cat([t[:, :, self._rows(self.r)] for t in lst], dim=1)
+    def _stats(self, lst, s):
+        return torch.cat([t[:, :, self._rows(s)] for t in lst], dim=1)
 
-    def own_grad_inputs(self):
-        rows = self._rows(self.r)
+    def grad_inputs(self, s):
+        rows = self._rows(s)
         packed = torch.cat([self.Qf[:, :, rows], self.dOf[:, :, rows], self.Kf[:, :, rows]], dim=1).contiguous()
-        stats = torch.stack([self._own_stats(self.lse), self._own_stats(self.delta)]).contiguous()
+        stats = torch.stack([self._stats(self.lse, s), self._stats(self.delta, s)]).contiguous()
         return [packed, stats]
 
-    def empty_grad_inputs(self, j):
-        n = self.bounds[j + 1] - self.bounds[j]
+    def empty_grad_inputs(self, s):
+        n = self.layout.hi(s) - self.layout.lo(s)
         return [torch.empty(self.B, 2 * self.Hq + self.H, n, self.D, dtype=torch.bfloat16, device=self.dev),
                 torch.empty(2, self.B, self.Hq, n, dtype=torch.float32, device=self.dev)]
 
-    def store_grad_inputs(self, j, bufs):
+    def store_grad_inputs(self, s, bufs):
         packed, stats = bufs
-        rows, Hq = self._rows(j), self.Hq
+        rows, Hq = self._rows(s), self.Hq
         self.Qf[:, :, rows] = packed[:, :Hq]
         self.dOf[:, :, rows] = packed[:, Hq:2 * Hq]
         self.Kf[:, :, rows] = packed[:, 2 * Hq:]
@@ -382,60 +507,57 @@ class KernelBackend:
             self.delta[g][:, :, rows] = stats[1][:, self._hq(g)]
 
     def prep_later(self):
-        if self.blk_hi >= self.NB:
-            return
-        for g in range(self.G):
-            kv = self.Kf[:, self._hs(g)]
-            _lib.check(self.lib.lucid_cp_prep(self.B, self.Hg, self.N, self.D, self.s, self.eps, self.blk_hi,
-                                              self.NB, 1, kv.data_ptr(), kv.stride(0), kv.stride(1), kv.stride(2),
-                                              self.khat[g].data_ptr(), self.u[g].data_ptr(),
-                                              self.rstd[g].data_ptr(), self.dinv[g].data_ptr(), self._st()),
-                       "lucid_cp_prep")
+        # the forward prepared every segment up to this rank's last one; the later
+        # (foreign) segments' keys arrived with the backward's inputs: k^ only
+        for s in range(self.layout.mine(self.r)[-1] + 1, self.layout.n):
+            self._prep(s, 1)
 
-    def _attn_bwd(self, g, passes):
+    def _attn_bwd(self, t, g, passes):
         hq, pr = self._hq(g), g % 2
         qg, kg, dg = self.Qf[:, hq], self.Kf[:, self._hs(g)], self.dOf[:, hq]
         dq = self.dq[:, hq]
+        lo, hi = self._blk(t)
         _lib.check(self.lib.lucid_cp_attn_bwd(
-            self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi, self.max_ctas,
+            self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, lo, hi, self.max_ctas,
             passes, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
             kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2), self.x[g].data_ptr(),
             dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2), self.lse[g].data_ptr(),
-            self.delta[g].data_ptr(), self._shift(dq, 2), dq.stride(0), dq.stride(1), dq.stride(2),
+            self.delta[g].data_ptr(), self._shift(dq, t, 2), dq.stride(0), dq.stride(1), dq.stride(2),
             self.dka32[pr].data_ptr(), self.dx32[pr].data_ptr(), self.status.data_ptr(), self._st()),
             "lucid_cp_attn_bwd")
 
-    def _solve_bwd(self, g, passes):
+    def _solve_bwd(self, t, g, passes):
         hs, pr = self._hs(g), g % 2
         kg, dk, dv = self.Kf[:, hs], self.dk[:, hs], self.dv[:, hs]
+        lo, hi = self._blk(t)
         _lib.check(self.lib.lucid_cp_solve_bwd(
-            self.B, self.Hg, self.N, self.D, self.s, self.blk_lo, self.blk_hi, self.max_ctas, passes,
+            self.B, self.Hg, self.N, self.D, self.s, lo, hi, self.max_ctas, passes,
             kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2), self.x[g].data_ptr(),
             self.khat[g].data_ptr(), self.u[g].data_ptr(), self.rstd[g].data_ptr(), self.dinv[g].data_ptr(),
-            self.dx32[pr].data_ptr(), self.dka32[pr].data_ptr(), self.dvint[pr].data_ptr(),
+            self.dx32[pr].data_ptr(), self.dka32[pr].data_ptr(), self.dvint[g].data_ptr(),
             self.dkcol[pr].data_ptr(), self.dkrow[pr].data_ptr(), self.bflags[g].data_ptr(),
-            self._shift(dk, 2), dk.stride(0), dk.stride(1), dk.stride(2),
-            self._shift(dv, 2), dv.stride(0), dv.stride(1), dv.stride(2), self.status.data_ptr(), self._st()),
+            self._shift(dk, t, 2), dk.stride(0), dk.stride(1), dk.stride(2),
+            self._shift(dv, t, 2), dv.stride(0), dv.stride(1), dv.stride(2), self.status.data_ptr(), self._st()),
             "lucid_cp_solve_bwd")
 
-    def attn_col(self, g):
-        self._attn_bwd(g, 1)
+    def attn_col(self, t, g):
+        self._attn_bwd(t, g, 1)
 
-    def store_dv(self, g, j, buf):
-        self.dvint[g % 2][:, :, self._rows(j)] = buf
-        _lib.check(self.lib.lucid_cp_publish(self.bflags[g].data_ptr(), self.B * self.Hg, self.NB,
-                                             self.bounds[j] // 128, self.bounds[j + 1] // 128, self._st()),
-                   "lucid_cp_publish")
+    def store_dv(self, g, s, buf):
+        self.dvint[g][:, :, self._rows(s)] = buf
+        lo, hi = self._blk(s)
+        _lib.check(self.lib.lucid_cp_publish(self.bflags[g].data_ptr(), self.B * self.Hg, self.NB, lo, hi,
+                                             self._st()), "lucid_cp_publish")
 
-    def solve_col(self, g):
-        self._solve_bwd(g, 1)
+    def solve_col(self, t, g):
+        self._solve_bwd(t, g, 1)
 
-    def own_dv(self, g):
-        return self.dvint[g % 2][:, :, self._rows(self.r)].contiguous()
+    def own_dv(self, t, g):
+        return self.dvint[g][:, :, self._rows(t)].contiguous()
 
-    def rows(self, g):
-        self._solve_bwd(g, 2)
-        self._attn_bwd(g, 2)
+    def rows(self, t, g):
+        self._solve_bwd(t, g, 2)
+        self._attn_bwd(t, g, 2)
 
     def finish_grad(self):
         self._check_status()
@@ -458,36 +580,43 @@ class CPLucidAttentionFunction(torch.autograd.Function):
         return dq, dk, dv, None
 
 
-def _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds):
+def _layout_of(bounds, layout, C, W):
+    if layout is not None:
+        return layout
+    return Layout.contiguous(bounds if bounds is not None else even_bounds(C * W, W))
+
+
+def _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds, layout):
     W = dist.get_world_size(group) if dist.is_initialized() else 1
     r = dist.get_rank(group) if dist.is_initialized() else 0
     B, Hq, C, D = q.shape
     H = k.shape[1]
     s = D ** -0.5 if scale is None else scale
-    if bounds is None:
-        bounds = even_bounds(C * W, W)
-    if bounds[r + 1] - bounds[r] != C:
-        raise ValueError(f"rank {r} passed {C} rows but owns [{bounds[r]}, {bounds[r + 1]})")
-    be = KernelBackend(B, H, Hq, bounds, D, s, eps, r, W, head_groups, q.device, reserve_sms)
+    L = _layout_of(bounds, layout, C, W)
+    if L.local_rows(r) != C:
+        raise ValueError(f"rank {r} passed {C} rows but owns {L.local_rows(r)} (segments {L.mine(r)})")
+    be = KernelBackend(B, H, Hq, L, D, s, eps, r, W, head_groups, q.device, reserve_sms)
     return ChunkProtocol(be, group)
 
 
-def cp_lucid_attention(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8, bounds=None):
+def cp_lucid_attention(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8, bounds=None,
+                       layout=None):
     """LUCID attention over a sequence split across the ranks of ``group``, with
     autograd: the arguments and the result are those of
     cp_lucid_attention_forward, and backward() runs the backward chain
     (every rank must call backward, as every rank called forward)."""
-    proto = _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds)
+    proto = _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds, layout)
     return CPLucidAttentionFunction.apply(q, k, v, proto)
 
 
 def cp_lucid_attention_forward(q, k, v, group=None, scale=None, eps=1e-5, head_groups=8, reserve_sms=8,
-                               bounds=None):
+                               bounds=None, layout=None):
     """LUCID attention forward over a sequence split across the ranks of ``group``.
 
-    Each rank passes its own chunk: q [B, Hq, C_r, D], k, v [B, H, C_r, D] (bf16,
-    CUDA), rank r holding rows [bounds[r], bounds[r+1]) of the sequence
-    (``bounds`` as from balanced_bounds / even_bounds; None: equal chunks).
-    Returns this rank's rows of O as [B, C_r, Hq, D] (the layout of
-    eager_lucid_attention_forward, modeling_lucid.py:546)."""
-    return _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds).run(q, k, v)
+    Each rank passes its own rows: q [B, Hq, C_r, D], k, v [B, H, C_r, D] (bf16,
+    CUDA), the rows of its segments concatenated in sequence order.  ``layout``
+    (a Layout, e.g. zigzag_layout) or ``bounds`` (contiguous chunk bounds as from
+    balanced_bounds / train_bounds / even_bounds; default equal chunks) says which
+    rows a rank owns.  Returns this rank's rows of O as [B, C_r, Hq, D] (the
+    layout of eager_lucid_attention_forward, modeling_lucid.py:546)."""
+    return _protocol(q, k, v, group, scale, eps, head_groups, reserve_sms, bounds, layout).run(q, k, v)
