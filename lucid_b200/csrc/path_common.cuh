@@ -139,8 +139,6 @@ enum : int { kTagPathAttn = 14 };
 enum : int { kTagPathGemm = 8, kTagPathScores = 9, kTagPathSolve = 10, kTagPathSolveT = 11,
              kTagPathRow = 12, kTagPathCol = 13 };
 
-// 128-thread named barrier helpers for the 256 epilogue threads.
-__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 
 // Packed bf16 A-operand address in TMEM of K-slice kk when each 64-column
