@@ -128,12 +128,27 @@ __global__ void __launch_bounds__(256) lucid_prep_kernel(PrepArgs p) {
   {
     const int r = tid >> 4, c = tid & 15;
     for (int I = 1; I < 8; ++I) {
-      for (int J = 0; J < I; ++J) {
-        float a = 0.f;
-        for (int col = J * 16; col < I * 16; ++col)
-          a = fmaf(lt[(I * 16 + r) * kLD + col], z[col * kLD + J * 16 + c], a);
-        tt[J * 256 + r * 16 + c] = a;
+      // tt_J = L~[I, 16J:16I] Z[16J:16I, J] for every J < I in one pass over the
+      // columns: each L~ entry is loaded once for all the blocks it feeds (same
+      // per-J accumulation order as a loop per J)
+      float acc[7];
+#pragma unroll
+      for (int J = 0; J < 7; ++J) acc[J] = 0.f;
+#pragma unroll
+      for (int K = 0; K < 7; ++K) {
+        if (K >= I) break;
+        const float* lrow = lt + (I * 16 + r) * kLD + K * 16;
+        const float* zrow = z + (K * 16) * kLD + c;
+#pragma unroll 4
+        for (int m = 0; m < 16; ++m) {
+          const float l = lrow[m];
+#pragma unroll
+          for (int J = 0; J <= K; ++J) acc[J] = fmaf(l, zrow[m * kLD + J * 16], acc[J]);
+        }
       }
+#pragma unroll
+      for (int J = 0; J < 7; ++J)
+        if (J < I) tt[J * 256 + r * 16 + c] = acc[J];
       __syncthreads();
       for (int J = 0; J < I; ++J) {
         float a = 0.f;
