@@ -238,6 +238,8 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
     from lucid_b200.path import parallel_lucid_path_attention, path_bwd, path_fwd
     lib = _lib.load()
     B, H, T, K = PATH_CONFIG
+    if args.path_seq:   # a shorter sequence (profiling cases); the metric is quoted at T = 16384
+        T = args.path_seq
     g = torch.Generator(device=dev).manual_seed(3000 + rank)
     k = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
     v = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
@@ -753,6 +755,8 @@ def main(argv=None):
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill"], default="32k")
     ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
+    ap.add_argument("--path-seq", type=int, default=0,
+                    help="path: sequence length instead of config 3's 16384 (smaller profiling cases)")
     ap.add_argument("--cp-layout", choices=["auto", "zigzag", "contiguous"], default="auto",
                     help="cp128k: rows per rank (zigzag: segments r and 2W-1-r; contiguous: one chunk; "
                          "auto: contiguous below 4 ranks, where its balanced chunks are as good, else zigzag)")
