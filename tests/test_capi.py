@@ -55,6 +55,15 @@ def test_host_helpers(lib):
     assert ws_b >= B * H * 1024 * 128 * (2 + 4 + 4)
     # attention backward scratch: status word + delta rows (no dQ accumulator: the row pass owns dQ)
     assert lib.lucid_attn_bwd_workspace_bytes(B, 8, H, N, D) >= 256 + B * 8 * 1024 * 4
+    # stored-tile schedule: one 32 KB bf16 tile per block pair on top of the base workspace
+    nb = 8  # ceil(1000 / 128)
+    extra_attn = lib.lucid_attn_bwd_fast_workspace_bytes(B, 8, H, N, D) - lib.lucid_attn_bwd_workspace_bytes(
+        B, 8, H, N, D)
+    assert extra_attn == B * 8 * (nb * (nb + 1) // 2) * 32768
+    extra_solve = lib.lucid_solve_bwd_fast_workspace_bytes(B, H, N, D) - ws_b
+    assert extra_solve == B * H * (nb * (nb - 1) // 2) * 32768
+    # a single block has no off-diagonal pair: the solve needs nothing extra
+    assert lib.lucid_solve_bwd_fast_workspace_bytes(1, 1, 100, D) == lib.lucid_solve_bwd_workspace_bytes(1, 1, 100, D)
 
 
 def test_argument_errors_without_launch(lib):
