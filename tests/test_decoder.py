@@ -4,8 +4,9 @@ the reference model of lucid/config/config.json, for the full-model prefill.
 CPU: the configuration and the parameter count of the full model (built on
 the meta device).  GPU: a small model with the reference's head_dim 68 and
 8 query heads per kv head against a float32 torch restatement of the same
-model (attention by oracle/torch_ref.py, the reference's own torch path), and
-the cache-filling prefill against the fused one."""
+model (attention by oracle/torch_ref.py, the reference's own torch path): the
+prefill logits, the cache-filling prefill against the fused one, and one
+training step's parameter gradients (the LUCID backward inside the model)."""
 import pytest
 import torch
 
@@ -31,7 +32,9 @@ def _ref_forward(model, ids, eps=1e-5):
     from oracle import torch_ref
     cfg = model.config
     hd, hq, hk = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-    W = {n: p.detach().float() for n, p in model.named_parameters()}
+    # float32 parameters are used as they are (a training-step reference differentiates
+    # through them); the bf16 model's are copied to float32
+    W = {n: p if p.dtype == torch.float32 else p.detach().float() for n, p in model.named_parameters()}
 
     def norm(x, w):
         return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
@@ -75,3 +78,37 @@ def test_small_decoder_matches_torch_restatement(cuda_device):
     assert (cached - fused).abs().max().item() <= 1e-2 * scale
     torch.testing.assert_close(last, fused[:, -1:], rtol=0, atol=0)
     assert cache.get_seq_length(0) == 384
+
+
+@pytest.mark.gpu
+def test_small_decoder_training_step_gradients(cuda_device):
+    """Next-token cross-entropy through the whole model; every parameter gradient
+    against autograd through the float32 restatement (relative L2 error)."""
+    from lucid_b200.decoder import LucidForCausalLM, lucid_config
+    cfg = lucid_config(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                       num_key_value_heads=1, head_dim=68, vocab_size=1000)
+    model = LucidForCausalLM(cfg).to(cuda_device, torch.bfloat16).init_weights(seed=5, std=0.05).train()
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(0, cfg.vocab_size, (2, 300), generator=g).to(cuda_device)
+    logits = model(ids)
+    loss = torch.nn.functional.cross_entropy(logits[:, :-1].float().reshape(-1, cfg.vocab_size),
+                                             ids[:, 1:].reshape(-1))
+    loss.backward()
+    ref_params = {n: p.detach().float().clone().requires_grad_(True) for n, p in model.named_parameters()}
+
+    class _View:   # the restatement reads weights by name
+        config = cfg
+
+        def named_parameters(self):
+            return ref_params.items()
+    ref_logits = _ref_forward(_View(), ids)
+    ref_loss = torch.nn.functional.cross_entropy(ref_logits[:, :-1].reshape(-1, cfg.vocab_size), ids[:, 1:].reshape(-1))
+    ref_loss.backward()
+    assert abs(loss.item() - ref_loss.item()) < 1e-2 * abs(ref_loss.item())
+    worst = {}
+    for n, p in model.named_parameters():
+        gr = ref_params[n].grad
+        assert p.grad is not None and torch.isfinite(p.grad).all(), n
+        worst[n] = ((p.grad.float() - gr).norm() / gr.norm().clamp_min(1e-30)).item()
+    bad = {n: e for n, e in worst.items() if e > 5e-2}
+    assert not bad, bad
