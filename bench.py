@@ -169,6 +169,8 @@ def reference_arm(args):
         return cp_reference_arm(args)
     if args.config == "prefill":
         return prefill_reference_arm(args)
+    if args.config == "decode":
+        return decode_reference_arm(args)
     B, H, N, D, _ = CONFIGS[args.config]
     n_cpu = args.cpu_n
     cpu_reference_sample(1024, D)
@@ -452,6 +454,154 @@ def prefill_reference_arm(args):
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"1 decoder layer at N={n_cpu}, fp32, attention by oracle/torch_ref.py"},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+DECODE_METRIC = ("LUCID decode step tokens/s (get_new_v_prime + cache append + decode attention), "
+                 "B4 H32 D128, 32768-token cache")
+
+
+def decode_cpu_sample(Nc: int, seed: int = 0):
+    """Seconds for one decode step of one (batch, head) on the host: the
+    reference's get_new_v_prime (modeling_lucid.py:576-598) and the attention of
+    the new query over the cache, float32 (oracle/torch_ref.py's formulas)."""
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    D = 128
+    kc, xc = torch.randn(1, 1, Nc, D, generator=g), torch.randn(1, 1, Nc, D, generator=g)
+    q, kn, vn = (torch.randn(1, 1, 1, D, generator=g) for _ in range(3))
+    s = D ** -0.5
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        nk = torch.nn.functional.rms_norm(kn, (D,), eps=1e-5)
+        nc = torch.nn.functional.rms_norm(kc, (D,), eps=1e-5)
+        x_new = vn - torch.exp(s * nk @ nc.transpose(-1, -2) - 1 / s) @ xc
+        k_all, x_all = torch.cat([kc, kn], 2), torch.cat([xc, x_new], 2)
+        torch.nn.functional.scaled_dot_product_attention(q, k_all, x_all, scale=s)
+    return time.perf_counter() - t0
+
+
+def decode_reference_arm(args):
+    n_cpu = min(args.cpu_n, 32768)
+    decode_cpu_sample(1024)
+    for _ in range(args.warmup):
+        decode_cpu_sample(n_cpu)
+    times = [decode_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
+    t = sum(times) / len(times) * 4 * 32   # B4 x H32 (batch, head) pairs per step
+    val = 4 / t
+    line = {
+        "impl": "reference", "metric": DECODE_METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode step B4 H32 D128 cache {n_cpu} (sampled: one (batch, head), x 128)",
+                   "global_batch": 4, "seq_len": n_cpu, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"1 (batch, head) decode step, cache {n_cpu}, fp32 torch"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_decode(args, torch, dist, dev, world, rank, local, barrier):
+    """One decode step per iteration: x_new = get_new_v_prime(k_new, v_new) over the
+    cache (raw keys, solved values), the new token appended, then the new query's
+    attention over the cache.  Both passes read the whole cache (HBM-bound); the
+    comparison is PyTorch SDPA decoding one query over a plain KV cache of the same
+    size (one pass)."""
+    import torch.nn.functional as F
+
+    from lucid_b200 import decode_attention, decode_update
+    B, H, Nc, D = 4, 32, 32768, 128
+    s = D ** -0.5
+    g = torch.Generator(device=dev).manual_seed(6000 + rank)
+    bf = dict(dtype=torch.bfloat16, device=dev)
+    kc = torch.randn(B, H, Nc + 1, D, generator=g, device=dev).to(torch.bfloat16)
+    xc = (0.1 * torch.randn(B, H, Nc + 1, D, generator=g, device=dev)).to(torch.bfloat16)
+    q, kn, vn = (torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+
+    def step():
+        x_new = decode_update(kn, vn, kc[:, :, :Nc], xc[:, :, :Nc], s, 1e-5)
+        kc[:, :, Nc:] = kn
+        xc[:, :, Nc:] = x_new
+        return decode_attention(q, kc, xc, s)
+
+    def sdpa_step():
+        return F.scaled_dot_product_attention(q, kc, xc, scale=s)
+
+    mkev = lambda: torch.cuda.Event(enable_timing=True)
+    reps = max(args.steps, 20)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = mkev(), mkev()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = timed(step)
+    clk = clocks.stop()
+    sdpa_ms = timed(sdpa_step)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # the update reads K and X of the cache, the attention reads them again
+    cache_bytes = 2 * B * H * Nc * D * 2
+    gbs = 2 * cache_bytes / (ms * 1e-3) / 1e9
+    _, _, hbm, pk_kind = peaks()
+
+    # end to end: the new token's q / k / v from pinned host memory, the output back
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, kn, vn))
+        out = torch.empty(B, 1, H, D, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            q_, k_, v_ = (h.to(dev, non_blocking=True) for h in (hq, hk, hv))
+            x_new = decode_update(k_, v_, kc[:, :, :Nc], xc[:, :, :Nc], s, 1e-5)
+            kc[:, :, Nc:] = k_
+            xc[:, :, Nc:] = x_new
+            out.copy_(decode_attention(q_, kc, xc, s), non_blocking=True)
+
+        ems = timed(e2e_step)
+        e2e = {"value": world * B / (ems * 1e-3), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": 3 * B * H * D * 2, "d2h_bytes_per_step": B * H * D * 2}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        decode_cpu_sample(1024)
+        tc = min(decode_cpu_sample(Nc, seed=i) for i in range(3))
+        cpu = {"value": B / (tc * B * H), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"1 (batch, head) decode step at cache {Nc}, fp32 torch, best of 3, x {B * H}"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": DECODE_METRIC, "value": world * B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": reps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"decode step B{B} H{H} D{D}, cache {Nc} tokens (raw keys, solved values), one new "
+                               f"token per sequence", "global_batch": B * world, "seq_len": Nc,
+                   "parallelism": f"data parallel replicas x{world}",
+                   "l2": "cache (2 GiB of K and X) larger than L2, no flush"},
+        "roofline": {"bound": "hbm", "kernel": "decode update + decode attention", "achieved": gbs, "peak": hbm,
+                     "unit": "GB/s", "frac": gbs / hbm, "peak_kind": f"{pk_kind} HBM copy bandwidth",
+                     "traffic": None},
+        "sdpa_decode_ms": sdpa_ms, "overhead_vs_sdpa_decode": ms / sdpa_ms,
+        "clocks": clk, "gpu_launches": 4 * reps, "e2e": e2e, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -752,7 +902,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill"], default="32k")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill", "decode"], default="32k")
     ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
     ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
     ap.add_argument("--path-seq", type=int, default=0,
@@ -793,6 +943,8 @@ def main(argv=None):
         return bench_cp(args, torch, dist, dev, world, rank, local, barrier)
     if args.config == "prefill":
         return bench_prefill(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "decode":
+        return bench_decode(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
     B, H, N, D, qs = CONFIGS[args.config]
     s = D ** -0.5
