@@ -18,7 +18,6 @@
 namespace lb {
 
 
-constexpr int kDecTok = 8;  // new tokens per pass
 
 __device__ __forceinline__ float4 ld_bf16x4(const bf16* p) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);
@@ -39,59 +38,128 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(256) lucid_decode_partial_kernel(const DecodeArgs a) {
-  __shared__ __align__(16) float khn[kDecTok][128];        // normalised new keys of this pass
-  __shared__ __align__(16) float red[8][kDecTok][128];     // per-warp partials
+// The cache passes give each cache row to a group of 8 lanes (4 rows per warp at a
+// time, lane l holding elements [16 (l % 8), +16) of its group's row): the row's dot
+// products need 3 shuffle levels, each shuffle instruction serving 4 rows, and each
+// warp keeps kGrpRows rows in flight per group.
+constexpr int kGrpTok = 2;   // new tokens per pass of the grouped kernels
+constexpr int kGrpRows = 2;  // row iterations in flight per group
+
+// 16 elements [e0, e0 + 16) of a row with head dimension D (a multiple of 4); the
+// 4-element chunks at or past D read nothing and are zero
+__device__ __forceinline__ void ld_row16(const bf16* row, int e0, int D, float (&v)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 f = ld_bf16x4_d(row + e0 + 4 * c, e0 + 4 * c < D);
+    v[4 * c] = f.x; v[4 * c + 1] = f.y; v[4 * c + 2] = f.z; v[4 * c + 3] = f.w;
+  }
+}
+
+// sum over the 8 lanes of a lane group
+__device__ __forceinline__ float grp_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+
+__device__ __forceinline__ float dot16_smem(const float* q, const float (&k)[16]) {
+  float d = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * c);
+    d = fmaf(q4.x, k[4 * c], d);
+    d = fmaf(q4.y, k[4 * c + 1], d);
+    d = fmaf(q4.z, k[4 * c + 2], d);
+    d = fmaf(q4.w, k[4 * c + 3], d);
+  }
+  return d;
+}
+
+__global__ void __launch_bounds__(256, 2) lucid_decode_partial_kernel(const DecodeArgs a) {
+  __shared__ __align__(16) float khn[kGrpTok][128];        // normalised new keys of this pass
+  __shared__ __align__(16) float red[8][kGrpTok][128];     // per-warp partials
   const int split = blockIdx.x, bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, e0 = (lane & 7) * 16;
   const float c1 = a.s * 1.4426950408889634f, c2 = 1.4426950408889634f / a.s;
+  const float inv_d = 1.f / (float)a.D;
   const int r0 = split * a.rows_per_split;
   const int r1 = min(a.Nc, r0 + a.rows_per_split);
-  const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh + lane * 4;
-  const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh + lane * 4;
+  const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh;
+  const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh;
   const bool act = lane * 4 < a.D;
-  for (int t0 = 0; t0 < a.Ln; t0 += kDecTok) {
-    const int nt = min(kDecTok, a.Ln - t0);
+  for (int t0 = 0; t0 < a.Ln; t0 += kGrpTok) {
+    const int nt = min(kGrpTok, a.Ln - t0);
     __syncthreads();
-    if (warp < nt) {  // RMSNorm of new token t0 + warp
+    if (warp < nt) {  // RMSNorm of new token t0 + warp (a whole warp per token)
       const float4 k4 = ld_bf16x4_d(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
                                     (long long)(t0 + warp) * a.kn_st + lane * 4, act);
       const float ss = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
-      const float r = rsqrtf(ss * (1.f / (float)a.D) + a.eps);
+      const float r = rsqrtf(ss * inv_d + a.eps);
       khn[warp][lane * 4 + 0] = k4.x * r;
       khn[warp][lane * 4 + 1] = k4.y * r;
       khn[warp][lane * 4 + 2] = k4.z * r;
       khn[warp][lane * 4 + 3] = k4.w * r;
     }
     __syncthreads();
-    float4 q[kDecTok];
+    float acc[kGrpTok][16];
 #pragma unroll
-    for (int t = 0; t < kDecTok; ++t)
-      q[t] = t < nt ? make_float4(khn[t][lane * 4], khn[t][lane * 4 + 1], khn[t][lane * 4 + 2], khn[t][lane * 4 + 3])
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 acc[kDecTok];
+    for (int t = 0; t < kGrpTok; ++t)
 #pragma unroll
-    for (int t = 0; t < kDecTok; ++t) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int row = r0 + warp; row < r1; row += 8) {
-      const float4 k4 = ld_bf16x4_d(kbase + (long long)row * a.kc_st, act);
-      const float4 x4 = ld_bf16x4_d(xbase + (long long)row * a.xc_st, act);
-      const float rs = rsqrtf(warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w) * (1.f / (float)a.D) + a.eps);
+      for (int i = 0; i < 16; ++i) acc[t][i] = 0.f;
+    // rows base + 32 u + 4 warp + grp; every lane runs every iteration (the shuffles
+    // span the warp), rows past r1 load nothing and add nothing
+    for (int base = r0; base < r1; base += 32 * kGrpRows) {
+      float k[kGrpRows][16], x[kGrpRows][16];
 #pragma unroll
-      for (int t = 0; t < kDecTok; ++t) {
-        if (t < nt) {
-          const float d = warp_sum(q[t].x * k4.x + q[t].y * k4.y + q[t].z * k4.z + q[t].w * k4.w) * rs;
-          const float e = exp2f(fmaf(d, c1, -c2));
-          acc[t].x = fmaf(e, x4.x, acc[t].x);
-          acc[t].y = fmaf(e, x4.y, acc[t].y);
-          acc[t].z = fmaf(e, x4.z, acc[t].z);
-          acc[t].w = fmaf(e, x4.w, acc[t].w);
+      for (int u = 0; u < kGrpRows; ++u) {
+        const int row = base + 32 * u + 4 * warp + grp;
+        if (row < r1) {
+          ld_row16(kbase + (long long)row * a.kc_st, e0, a.D, k[u]);
+          ld_row16(xbase + (long long)row * a.xc_st, e0, a.D, x[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) k[u][i] = x[u][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kGrpRows; ++u) {
+        const bool valid = base + 32 * u + 4 * warp + grp < r1;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ss = fmaf(k[u][i], k[u][i], ss);
+        const float rs = rsqrtf(grp_sum(ss) * inv_d + a.eps);
+#pragma unroll
+        for (int t = 0; t < kGrpTok; ++t) {
+          if (t < nt) {
+            const float d = grp_sum(dot16_smem(&khn[t][e0], k[u])) * rs;
+            const float e = valid ? exp2f(fmaf(d, c1, -c2)) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(e, x[u][i], acc[t][i]);
+          }
         }
       }
     }
+    // the 4 groups summed different rows into the same output elements
 #pragma unroll
-    for (int t = 0; t < kDecTok; ++t)
-      if (t < nt) *reinterpret_cast<float4*>(&red[warp][t][lane * 4]) = acc[t];
+    for (int t = 0; t < kGrpTok; ++t)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        acc[t][i] += __shfl_xor_sync(0xffffffffu, acc[t][i], 8);
+        acc[t][i] += __shfl_xor_sync(0xffffffffu, acc[t][i], 16);
+      }
+    if (grp == 0) {
+#pragma unroll
+      for (int t = 0; t < kGrpTok; ++t)
+        if (t < nt) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<float4*>(&red[warp][t][e0 + 4 * c]) =
+                make_float4(acc[t][4 * c], acc[t][4 * c + 1], acc[t][4 * c + 2], acc[t][4 * c + 3]);
+        }
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < nt * 128; e += blockDim.x) {
       const int t = e >> 7, c = e & 127;
@@ -151,23 +219,23 @@ cudaError_t launch_decode(DecodeArgs a, cudaStream_t st) {
 // ===========================================================================
 namespace lb {
 
-__global__ void __launch_bounds__(256) lucid_decode_attn_partial_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(256, 2) lucid_decode_attn_partial_kernel(const DecodeArgs a) {
   // rows of 132 floats: 128 partial values, the running maximum and the
   // denominator, padded so that every row starts on a 16-byte boundary
   constexpr int kRow = 132;
-  __shared__ __align__(16) float qs[kDecTok][128];
-  __shared__ __align__(16) float red[8][kDecTok][kRow];
+  __shared__ __align__(16) float qs[kGrpTok][128];
+  __shared__ __align__(16) float red[8][kGrpTok][kRow];
   const int split = blockIdx.x, bq = blockIdx.y;
   const int b = bq / a.Hq, hq = bq % a.Hq, h = hq / (a.Hq / a.H);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, e0 = (lane & 7) * 16;
   const float sm = a.s * 1.4426950408889634f;
   const int r0 = split * a.rows_per_split;
   const int r1 = min(a.Nc, r0 + a.rows_per_split);
-  const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh + lane * 4;
-  const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh + lane * 4;
-  const bool act = lane * 4 < a.D;
-  for (int t0 = 0; t0 < a.Ln; t0 += kDecTok) {
-    const int nt = min(kDecTok, a.Ln - t0);
+  const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh;
+  const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh;
+  for (int t0 = 0; t0 < a.Ln; t0 += kGrpTok) {
+    const int nt = min(kGrpTok, a.Ln - t0);
     __syncthreads();
     for (int e = threadIdx.x; e < nt * 128; e += blockDim.x) {
       const int t = e >> 7, c = e & 127;
@@ -176,41 +244,78 @@ __global__ void __launch_bounds__(256) lucid_decode_attn_partial_kernel(const De
                          : 0.f;
     }
     __syncthreads();
-    float4 q[kDecTok], acc[kDecTok];
-    float m[kDecTok], l[kDecTok];
+    float acc[kGrpTok][16], m[kGrpTok], l[kGrpTok];
 #pragma unroll
-    for (int t = 0; t < kDecTok; ++t) {
-      q[t] = t < nt ? make_float4(qs[t][lane * 4], qs[t][lane * 4 + 1], qs[t][lane * 4 + 2], qs[t][lane * 4 + 3])
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-      acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < kGrpTok; ++t) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[t][i] = 0.f;
       m[t] = -INFINITY;
       l[t] = 0.f;
     }
-    for (int row = r0 + warp; row < r1; row += 8) {
-      const float4 k4 = ld_bf16x4_d(kbase + (long long)row * a.kc_st, act);
-      const float4 x4 = ld_bf16x4_d(xbase + (long long)row * a.xc_st, act);
+    for (int base = r0; base < r1; base += 32 * kGrpRows) {
+      float k[kGrpRows][16], x[kGrpRows][16];
 #pragma unroll
-      for (int t = 0; t < kDecTok; ++t) {
-        if (t < nt && row <= a.Nc - a.Ln + t0 + t) {
-          const float z = warp_sum(q[t].x * k4.x + q[t].y * k4.y + q[t].z * k4.z + q[t].w * k4.w);
-          const float mn = fmaxf(m[t], z);
-          const float al = exp2f(m[t] - mn), p = exp2f(z - mn);
-          l[t] = l[t] * al + p;
-          acc[t].x = fmaf(p, x4.x, acc[t].x * al);
-          acc[t].y = fmaf(p, x4.y, acc[t].y * al);
-          acc[t].z = fmaf(p, x4.z, acc[t].z * al);
-          acc[t].w = fmaf(p, x4.w, acc[t].w * al);
-          m[t] = mn;
+      for (int u = 0; u < kGrpRows; ++u) {
+        const int row = base + 32 * u + 4 * warp + grp;
+        if (row < r1) {
+          ld_row16(kbase + (long long)row * a.kc_st, e0, a.D, k[u]);
+          ld_row16(xbase + (long long)row * a.xc_st, e0, a.D, x[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) k[u][i] = x[u][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kGrpRows; ++u) {
+        const int row = base + 32 * u + 4 * warp + grp;
+#pragma unroll
+        for (int t = 0; t < kGrpTok; ++t) {
+          if (t < nt) {
+            const float z = grp_sum(dot16_smem(&qs[t][e0], k[u]));
+            // the new query t0 + t sits at cache position Nc - Ln + t0 + t (causal)
+            if (row < r1 && row <= a.Nc - a.Ln + t0 + t) {   // uniform within the group
+              const float mn = fmaxf(m[t], z);
+              const float al = exp2f(m[t] - mn), p = exp2f(z - mn);
+              l[t] = l[t] * al + p;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(p, x[u][i], acc[t][i] * al);
+              m[t] = mn;
+            }
+          }
         }
       }
     }
+    // merge the 4 groups' running (max, sum, weighted sum) of each token
 #pragma unroll
-    for (int t = 0; t < kDecTok; ++t) {
-      if (t < nt) {
-        *reinterpret_cast<float4*>(&red[warp][t][lane * 4]) = acc[t];
-        if (lane == 0) {
-          red[warp][t][128] = m[t];
-          red[warp][t][129] = l[t];
+    for (int t = 0; t < kGrpTok; ++t) {
+      float M = fmaxf(m[t], __shfl_xor_sync(0xffffffffu, m[t], 8));
+      M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+      const float f = (m[t] == -INFINITY) ? 0.f : exp2f(m[t] - M);
+      float L = l[t] * f;
+      L += __shfl_xor_sync(0xffffffffu, L, 8);
+      L += __shfl_xor_sync(0xffffffffu, L, 16);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float v = acc[t][i] * f;
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        acc[t][i] = v;
+      }
+      m[t] = M;
+      l[t] = L;
+    }
+    if (grp == 0) {
+#pragma unroll
+      for (int t = 0; t < kGrpTok; ++t) {
+        if (t < nt) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<float4*>(&red[warp][t][e0 + 4 * c]) =
+                make_float4(acc[t][4 * c], acc[t][4 * c + 1], acc[t][4 * c + 2], acc[t][4 * c + 3]);
+          if (lane == 0) {
+            red[warp][t][128] = m[t];
+            red[warp][t][129] = l[t];
+          }
         }
       }
     }
