@@ -533,7 +533,7 @@ def bench_decode(args, torch, dist, dev, world, rank, local, barrier):
         return F.scaled_dot_product_attention(q, kc, xc, scale=s)
 
     mkev = lambda: torch.cuda.Event(enable_timing=True)
-    reps = max(args.steps, 20)
+    reps = args.steps
 
     def timed(fn):
         for _ in range(args.warmup):
