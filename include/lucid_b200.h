@@ -133,6 +133,32 @@ int lucid_decode_attn(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Fused decode step: lucid_decode_update and the new queries' attention in one
+ * pass over the cache (the reference's decoding forward, modeling_lucid.py:467-481
+ * then :505-549, reads the cache in get_new_v_prime and again in the attention).
+ * k_cache / x_cache [B, Hkv, Nc, D] hold the tokens BEFORE this step; the step
+ * writes x_new [B, Hkv, Ln, D] (the solved values of the new tokens, as the cache
+ * update of :479-481 stores them) and o [B, Hq, Ln, D] = softmax(scale q [K_cache;
+ * k_new]^T + causal) [X_cache; x_new], query l at position Nc + l (pass the strides
+ * of a [B, Ln, Hq, D] tensor for the reference's layout).  The caller appends
+ * k_new / x_new to its cache.  lucid_decode_step_fused(Hq, Hkv, Ln) is 1 for the
+ * shapes with a single-pass kernel (Ln 1 with Hq/Hkv 1 or 2, Ln 2 with Hq = Hkv);
+ * any other shape returns LUCID_ERR_SHAPE (use lucid_decode_update, the cache
+ * append and lucid_decode_attn).  Alignment as lucid_decode_update, q included.
+ */
+int lucid_decode_step_fused(int Hq, int Hkv, int Ln);
+size_t lucid_decode_step_workspace_bytes(int B, int Hq, int Hkv, int Ln, int Nc, int D);
+int lucid_decode_step(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale, float eps,
+                      const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                      const void* k_new, int64_t kn_sb, int64_t kn_sh, int64_t kn_sn,
+                      const void* v_new, int64_t vn_sb, int64_t vn_sh, int64_t vn_sn,
+                      const void* k_cache, int64_t kc_sb, int64_t kc_sh, int64_t kc_sn,
+                      const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
+                      void* x_new, int64_t xn_sb, int64_t xn_sh, int64_t xn_sn,
+                      void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Attention forward: O = softmax(scale Q K^T + causal) X.
  * Replaces LucidAttention.eager_lucid_attention_forward
  * (modeling_lucid.py:505-549; SDPA with repeat_kv, is_causal=True).

@@ -12,6 +12,8 @@ from .ops import (  # noqa: F401
     attn_bwd,
     attn_fwd,
     decode_attention,
+    decode_step,
+    decode_step_fused,
     decode_update,
     lucid_attention,
     padded_len,

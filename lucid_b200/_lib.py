@@ -69,6 +69,10 @@ SIGNATURES = {
                             + [c_void_p, c_size_t, c_void_p]),
     "lucid_decode_attn_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_decode_attn": (c_int, [c_int] * 6 + [c_float] + ([c_void_p] + S3) * 4 + [c_void_p, c_size_t, c_void_p]),
+    "lucid_decode_step_fused": (c_int, [c_int] * 3),
+    "lucid_decode_step_workspace_bytes": (c_size_t, [c_int] * 6),
+    "lucid_decode_step": (c_int, [c_int] * 6 + [c_float, c_float] + ([c_void_p] + S3) * 7
+                          + [c_void_p, c_size_t, c_void_p]),
     "lucid_cp_prep": (c_int, [c_int] * 4 + [c_float, c_float] + [c_int] * 3 + [c_void_p] + S3
                       + [c_void_p] * 4 + [c_void_p]),
     "lucid_cp_publish": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),

@@ -93,4 +93,20 @@ struct DecodeArgs {
   int D = kHeadDim;                                // logical head dimension of the RMS mean
 };
 
+// Fused decode step: get_new_v_prime and the new queries' attention in one pass
+// over the cache (csrc/lucid_decode.cu)
+struct DecodeStepArgs {
+  int B, H, Hq, Ln, Nc, D, nsplit, rows_per_split;
+  float s, eps;
+  const bf16* q; long long q_sb, q_sh, q_st;       // new queries [B,Hq,Ln,D]
+  const bf16* kn; long long kn_sb, kn_sh, kn_st;   // new keys [B,H,Ln,D]
+  const bf16* vn; long long vn_sb, vn_sh, vn_st;   // new values [B,H,Ln,D]
+  const bf16* kc; long long kc_sb, kc_sh, kc_st;   // cached keys [B,H,Nc,D]
+  const bf16* xc; long long xc_sb, xc_sh, xc_st;   // cached solved values [B,H,Nc,D]
+  bf16* xo; long long xo_sb, xo_sh, xo_st;         // solved new values [B,H,Ln,D]
+  bf16* o; long long o_sb, o_sh, o_st;             // attention output [B,Hq,Ln,D]
+  float* part_u;                                   // [nsplit][B*H][Ln][128] cache sums
+  float* part_a;                                   // [nsplit][B*H][Hq/H*Ln][130] softmax partials
+};
+
 }  // namespace lb

@@ -7,17 +7,17 @@
 // divided out.
 //
 // Memory-bound (one pass over K_cache and X_cache): the cache rows are split
-// over CTAs (grid = splits x heads), each warp walks rows with one 8-byte
-// load per lane per tensor, normalises the cached key on the fly and
-// accumulates up to 8 new tokens at a time in registers; a second kernel sums
-// the per-split partials and writes x_new.
+// over CTAs (grid = splits x heads), each cache row goes to a group of 8 lanes
+// (16 elements per lane), the cached key is normalised on the fly and 2 new
+// tokens at a time accumulate in registers; a second kernel sums the
+// per-split partials and writes x_new.  The fused decode step at the end of
+// the file computes the update and the new queries' attention in one pass.
 #include "lucid_common.cuh"
 
 #include <algorithm>
+#include <climits>
 
 namespace lb {
-
-
 
 __device__ __forceinline__ float4 ld_bf16x4(const bf16* p) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);
@@ -188,11 +188,24 @@ __global__ void lucid_decode_finish_kernel(const DecodeArgs a) {
 }
 
 int decode_splits(int B, int H, int Nc) {
-  // about 4 CTAs per SM over all heads, at least 256 cache rows per CTA
-  const int bh = std::max(1, B * H);
-  int n = (4 * 148 + bh - 1) / bh;
-  n = std::min(n, std::max(1, (Nc + 255) / 256));
-  return std::max(1, std::min(n, 1024));
+  // Splits of each (batch, head)'s cache over CTAs for the partial kernels (two
+  // resident CTAs per SM on 148 SMs): the count that minimises the modelled time,
+  // waves x (cache rows per CTA + 64 rows' worth of fixed cost for the CTA's setup
+  // and merges), with at least 128 cache rows per CTA.
+  constexpr long long kSlots = 2 * 148, kFixedRows = 64;
+  const long long bh = std::max(1, B * H);
+  const int nmax = std::max(1, std::min(1024, (Nc + 127) / 128));
+  int best = 1;
+  long long best_t = LLONG_MAX;
+  for (int n = 1; n <= nmax; ++n) {
+    const long long waves = (bh * n + kSlots - 1) / kSlots;
+    const long long t = waves * ((Nc + n - 1) / n + kFixedRows);
+    if (t < best_t) {
+      best_t = t;
+      best = n;
+    }
+  }
+  return best;
 }
 
 cudaError_t launch_decode(DecodeArgs a, cudaStream_t st) {
@@ -374,6 +387,287 @@ cudaError_t launch_decode_attn(DecodeArgs a, cudaStream_t st) {
   const long long total = (long long)a.B * a.Hq * a.Ln * 128;
   lucid_decode_attn_finish_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(a);
   return cudaGetLastError();
+}
+
+
+// ===========================================================================
+// Fused decode step: the reference's decoding forward (modeling_lucid.py:467-481
+// then :505-549) reads the cache twice, once in get_new_v_prime and once in the
+// attention over the updated cache.  Here one pass over the Nc cached rows
+// computes both: NU = Ln update slots (normalised new keys) and NA = (Hq/H) x Ln
+// attention slots (scaled new queries; every cached row is visible to every new
+// query).  The finish kernel forms x_new = v_new - sum, rounds it to bf16 as the
+// cache stores it, and adds the Ln new rows (keys k_new, values x_new; query l
+// sees new rows i <= l) to the attention.  Each slot keeps 16 accumulators per
+// lane, so only small slot counts have an instance; decode_step_fused says which.
+// ===========================================================================
+
+template <int NU, int NA, int ROWS>
+__global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const DecodeStepArgs a) {
+  constexpr int NS = NU + NA;
+  constexpr int kRow = 132;  // 128 values, the running maximum and the denominator, padded
+  __shared__ __align__(16) float kq[NS][128];  // normalised new keys, then scaled queries
+  __shared__ __align__(16) float red[8][NS][kRow];
+  const int split = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H, gq = a.Hq / a.H;
+  const long long BH = (long long)a.B * a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, e0 = (lane & 7) * 16;
+  const float c1 = a.s * 1.4426950408889634f, c2 = 1.4426950408889634f / a.s;
+  const float inv_d = 1.f / (float)a.D;
+  const int r0 = split * a.rows_per_split;
+  const int r1 = min(a.Nc, r0 + a.rows_per_split);
+  const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh;
+  const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh;
+  if (warp < NU) {  // RMSNorm of new key `warp` (a whole warp per key)
+    const bool act = lane * 4 < a.D;
+    const float4 k4 = ld_bf16x4_d(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
+                                  (long long)warp * a.kn_st + lane * 4, act);
+    const float r = rsqrtf(warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w) * inv_d + a.eps);
+    kq[warp][lane * 4 + 0] = k4.x * r;
+    kq[warp][lane * 4 + 1] = k4.y * r;
+    kq[warp][lane * 4 + 2] = k4.z * r;
+    kq[warp][lane * 4 + 3] = k4.w * r;
+  }
+  for (int e = threadIdx.x; e < NA * 128; e += blockDim.x) {
+    const int sl = e >> 7, c = e & 127, j = sl / NU, l = sl % NU;  // query head h*gq + j, token l
+    kq[NU + sl][c] = c < a.D ? __bfloat162float(a.q[(long long)b * a.q_sb + (long long)(h * gq + j) * a.q_sh +
+                                                    (long long)l * a.q_st + c]) * c1
+                             : 0.f;
+  }
+  __syncthreads();
+  float acc[NS][16], m[NA], l[NA];
+#pragma unroll
+  for (int t = 0; t < NS; ++t)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[t][i] = 0.f;
+#pragma unroll
+  for (int t = 0; t < NA; ++t) {
+    m[t] = -INFINITY;
+    l[t] = 0.f;
+  }
+  for (int base = r0; base < r1; base += 32 * ROWS) {
+    float k[ROWS][16], x[ROWS][16];
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+      const int row = base + 32 * u + 4 * warp + grp;
+      if (row < r1) {
+        ld_row16(kbase + (long long)row * a.kc_st, e0, a.D, k[u]);
+        ld_row16(xbase + (long long)row * a.xc_st, e0, a.D, x[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) k[u][i] = x[u][i] = 0.f;
+      }
+    }
+    // every row's weights first (the keys die here), then one accumulation step
+    // per slot for all ROWS rows
+    float ev[NU][ROWS], zv[NA][ROWS];
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+      const bool valid = base + 32 * u + 4 * warp + grp < r1;  // uniform within the group
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ss = fmaf(k[u][i], k[u][i], ss);
+      const float rs = rsqrtf(grp_sum(ss) * inv_d + a.eps);
+#pragma unroll
+      for (int t = 0; t < NU; ++t) {
+        const float d = grp_sum(dot16_smem(&kq[t][e0], k[u])) * rs;
+        ev[t][u] = valid ? exp2f(fmaf(d, c1, -c2)) : 0.f;
+      }
+#pragma unroll
+      for (int t = 0; t < NA; ++t) {
+        const float z = grp_sum(dot16_smem(&kq[NU + t][e0], k[u]));
+        zv[t][u] = valid ? z : -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NU; ++t)
+#pragma unroll
+      for (int u = 0; u < ROWS; ++u)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(ev[t][u], x[u][i], acc[t][i]);
+#pragma unroll
+    for (int t = 0; t < NA; ++t) {
+      float mn = m[t];
+#pragma unroll
+      for (int u = 0; u < ROWS; ++u) mn = fmaxf(mn, zv[t][u]);
+      if (mn != -INFINITY) {  // some row of the group valid so far
+        const float al = exp2f(m[t] - mn);  // 0 while m is still -inf
+        float p[ROWS], psum = 0.f;
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) {
+          p[u] = exp2f(zv[t][u] - mn);  // 0 for the invalid rows
+          psum += p[u];
+        }
+        l[t] = l[t] * al + psum;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v = acc[NU + t][i] * al;
+#pragma unroll
+          for (int u = 0; u < ROWS; ++u) v = fmaf(p[u], x[u][i], v);
+          acc[NU + t][i] = v;
+        }
+        m[t] = mn;
+      }
+    }
+  }
+  // merge the 4 lane groups of the warp: sums for the update, (max, sum) for the attention
+#pragma unroll
+  for (int t = 0; t < NU; ++t)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      acc[t][i] += __shfl_xor_sync(0xffffffffu, acc[t][i], 8);
+      acc[t][i] += __shfl_xor_sync(0xffffffffu, acc[t][i], 16);
+    }
+#pragma unroll
+  for (int t = 0; t < NA; ++t) {
+    float M = fmaxf(m[t], __shfl_xor_sync(0xffffffffu, m[t], 8));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+    const float f = (m[t] == -INFINITY) ? 0.f : exp2f(m[t] - M);
+    float L = l[t] * f;
+    L += __shfl_xor_sync(0xffffffffu, L, 8);
+    L += __shfl_xor_sync(0xffffffffu, L, 16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float v = acc[NU + t][i] * f;
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      acc[NU + t][i] = v;
+    }
+    m[t] = M;
+    l[t] = L;
+  }
+  if (grp == 0) {
+#pragma unroll
+    for (int t = 0; t < NS; ++t)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<float4*>(&red[warp][t][e0 + 4 * c]) =
+            make_float4(acc[t][4 * c], acc[t][4 * c + 1], acc[t][4 * c + 2], acc[t][4 * c + 3]);
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < NA; ++t) {
+        red[warp][NU + t][128] = m[t];
+        red[warp][NU + t][129] = l[t];
+      }
+    }
+  }
+  __syncthreads();
+  // merge the 8 warps into this split's partials
+  for (int e = threadIdx.x; e < NS * 128; e += blockDim.x) {
+    const int sl = e >> 7, c = e & 127;
+    if (sl < NU) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += red[w][sl][c];
+      a.part_u[(((long long)split * BH + bh) * NU + sl) * 128 + c] = sum;
+    } else {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) M = fmaxf(M, red[w][sl][128]);
+      float L = 0.f, S = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float f = (red[w][sl][128] == -INFINITY) ? 0.f : exp2f(red[w][sl][128] - M);
+        L += f * red[w][sl][129];
+        S += f * red[w][sl][c];
+      }
+      float* dst = a.part_a + (((long long)split * BH + bh) * NA + (sl - NU)) * 130;
+      dst[c] = S;
+      if (c == 0) {
+        dst[128] = M;
+        dst[129] = L;
+      }
+    }
+  }
+}
+
+template <int NU, int NA>
+__global__ void __launch_bounds__(256) lucid_decode_step_finish_kernel(const DecodeStepArgs a) {
+  __shared__ __align__(16) float xs[NU][128];  // x_new as the cache holds it (bf16 values)
+  __shared__ float zs[NA][NU];                 // new query x new key scores (log2 domain)
+  const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, gq = a.Hq / a.H;
+  const long long BH = (long long)a.B * a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float sm = a.s * 1.4426950408889634f;
+  for (int e = threadIdx.x; e < NU * 128; e += blockDim.x) {
+    const int l = e >> 7, c = e & 127;
+    float xv = 0.f;
+    if (c < a.D) {
+      float sum = 0.f;
+      for (int sp = 0; sp < a.nsplit; ++sp) sum += a.part_u[(((long long)sp * BH + bh) * NU + l) * 128 + c];
+      const float v = __bfloat162float(a.vn[(long long)b * a.vn_sb + (long long)h * a.vn_sh +
+                                            (long long)l * a.vn_st + c]);
+      const bf16 xb = __float2bfloat16(v - sum);
+      a.xo[(long long)b * a.xo_sb + (long long)h * a.xo_sh + (long long)l * a.xo_st + c] = xb;
+      xv = __bfloat162float(xb);
+    }
+    xs[l][c] = xv;
+  }
+  for (int p = warp; p < NA * NU; p += 8) {  // one warp per (slot, new key) pair
+    const int sl = p / NU, i = p % NU, j = sl / NU, l = sl % NU;
+    float z = -INFINITY;
+    if (i <= l) {  // causal among the new tokens (uniform within the warp)
+      const bool act = lane * 4 < a.D;
+      const float4 q4 = ld_bf16x4_d(a.q + (long long)b * a.q_sb + (long long)(h * gq + j) * a.q_sh +
+                                    (long long)l * a.q_st + lane * 4, act);
+      const float4 k4 = ld_bf16x4_d(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
+                                    (long long)i * a.kn_st + lane * 4, act);
+      z = warp_sum(q4.x * sm * k4.x + q4.y * sm * k4.y + q4.z * sm * k4.z + q4.w * sm * k4.w);
+    }
+    if (lane == 0) zs[sl][i] = z;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < NA * 128; e += blockDim.x) {
+    const int sl = e >> 7, c = e & 127, j = sl / NU, l = sl % NU;
+    if (c >= a.D) continue;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.nsplit; ++sp)
+      M = fmaxf(M, a.part_a[(((long long)sp * BH + bh) * NA + sl) * 130 + 128]);
+#pragma unroll
+    for (int i = 0; i < NU; ++i) M = fmaxf(M, zs[sl][i]);
+    float L = 0.f, S = 0.f;
+    for (int sp = 0; sp < a.nsplit; ++sp) {
+      const float* pp = a.part_a + (((long long)sp * BH + bh) * NA + sl) * 130;
+      const float f = (pp[128] == -INFINITY) ? 0.f : exp2f(pp[128] - M);
+      L += f * pp[129];
+      S += f * pp[c];
+    }
+#pragma unroll
+    for (int i = 0; i < NU; ++i) {
+      if (i <= l) {
+        const float p = exp2f(zs[sl][i] - M);
+        L += p;
+        S += p * xs[i][c];
+      }
+    }
+    a.o[(long long)b * a.o_sb + (long long)(h * gq + j) * a.o_sh + (long long)l * a.o_st + c] =
+        __float2bfloat16(S / L);
+  }
+}
+
+template <int NU, int NA, int ROWS>
+static cudaError_t launch_decode_step_t(const DecodeStepArgs& a, cudaStream_t st) {
+  lucid_decode_step_partial_kernel<NU, NA, ROWS><<<dim3(a.nsplit, a.B * a.H), 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  lucid_decode_step_finish_kernel<NU, NA><<<a.B * a.H, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+bool decode_step_fused(int gq, int Ln) {
+  return (Ln == 1 && (gq == 1 || gq == 2)) || (Ln == 2 && gq == 1);
+}
+
+cudaError_t launch_decode_step(DecodeStepArgs a, cudaStream_t st) {
+  if (a.B == 0 || a.H == 0 || a.Ln == 0) return cudaSuccess;
+  a.nsplit = decode_splits(a.B, a.H, a.Nc);
+  a.rows_per_split = (a.Nc + a.nsplit - 1) / a.nsplit;
+  const int gq = a.Hq / a.H;
+  if (a.Ln == 1 && gq == 1) return launch_decode_step_t<1, 1, 2>(a, st);
+  if (a.Ln == 1 && gq == 2) return launch_decode_step_t<1, 2, 1>(a, st);
+  if (a.Ln == 2 && gq == 1) return launch_decode_step_t<2, 2, 1>(a, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace lb

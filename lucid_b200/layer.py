@@ -13,13 +13,18 @@ kernels, leaving everything else of the reference model untouched.
 Training / prefill (past_seq_len == 0) and incremental decoding
 (get_new_v_prime, :576-598, then attention over the cache) are both covered;
 the cache keeps raw keys and solved values like the reference (:479-481).
+Where a single-pass kernel covers the step's shape (ops.decode_step_fused),
+``LucidAttention.forward`` computes get_new_v_prime and the attention in one
+pass over the cache and then appends to it; the three methods above keep the
+reference's separate calls for code that calls or patches them.
 """
 from __future__ import annotations
 
 import torch
 from torch import nn
 
-from .ops import LucidAttentionFunction, LucidAttnFunction, LucidSolveFunction, decode_attention, decode_update
+from .ops import (LucidAttentionFunction, LucidAttnFunction, LucidSolveFunction, decode_attention, decode_step,
+                  decode_step_fused, decode_update)
 
 __all__ = ["LucidAttention", "patch_reference", "get_v_prime", "get_new_v_prime", "eager_lucid_attention_forward"]
 
@@ -33,6 +38,11 @@ def _cache_layer(past_key_value, layer_idx):
     return layer.keys, layer.values
 
 
+def _k_norm_eps(self) -> float:
+    eps = getattr(self.k_norm, "eps", None)
+    return float(eps) if eps is not None else 1e-5
+
+
 def get_v_prime(self, key: torch.Tensor, value: torch.Tensor, scaling: float,
                 attention_mask: torch.Tensor | None = None) -> torch.Tensor:
     """X = P^-1 V with P = tril(exp(s k_norm(K) k_norm(K)^T - 1/s))
@@ -43,8 +53,7 @@ def get_v_prime(self, key: torch.Tensor, value: torch.Tensor, scaling: float,
     which = getattr(self, "which_rmsnorm", "exp_k_norm")
     if which != "exp_k_norm":
         raise NotImplementedError(f"{which} not implemented")
-    eps = self.k_norm.eps if getattr(self.k_norm, "eps", None) is not None else 1e-5
-    return LucidSolveFunction.apply(key, value, float(scaling), float(eps))
+    return LucidSolveFunction.apply(key, value, float(scaling), _k_norm_eps(self))
 
 
 def get_new_v_prime(self, key: torch.Tensor, value: torch.Tensor, attention_mask: torch.Tensor | None,
@@ -55,9 +64,8 @@ def get_new_v_prime(self, key: torch.Tensor, value: torch.Tensor, attention_mask
     which = getattr(self, "which_rmsnorm", "exp_k_norm")
     if which != "exp_k_norm":
         raise NotImplementedError(f"{which} not implemented")
-    eps = self.k_norm.eps if getattr(self.k_norm, "eps", None) is not None else 1e-5
     k_cache, x_cache = _cache_layer(past_key_value, self.layer_idx)
-    return decode_update(key, value, k_cache, x_cache, float(scaling), float(eps))
+    return decode_update(key, value, k_cache, x_cache, float(scaling), _k_norm_eps(self))
 
 
 def eager_lucid_attention_forward(self, query: torch.Tensor, key: torch.Tensor, v_prime: torch.Tensor,
@@ -129,13 +137,19 @@ class LucidAttention(nn.Module):
             o = LucidAttentionFunction.apply(q, k, v, float(self.scaling), float(self.k_norm.eps or 1e-5))
         else:
             past = past_key_value.get_seq_length(self.layer_idx)
+            o = None
             if past == 0:
                 x = self.get_v_prime(k, v, self.scaling, None)
+            elif decode_step_fused(q.shape[1], k.shape[1], k.shape[2]):
+                # get_new_v_prime and the attention in one pass over the cache
+                k_cache, x_cache = _cache_layer(past_key_value, self.layer_idx)
+                o, x = decode_step(q, k, v, k_cache, x_cache, float(self.scaling), _k_norm_eps(self))
             else:
                 x = self.get_new_v_prime(k, v, None, self.scaling, past_key_value)
             k_all, x_all = past_key_value.update(k, x, self.layer_idx,
                                                  {"cache_position": cache_position})
-            o, _ = self.eager_lucid_attention_forward(q, k_all, x_all, self.scaling, None)
+            if o is None:
+                o, _ = self.eager_lucid_attention_forward(q, k_all, x_all, self.scaling, None)
         o = o.reshape(*input_shape, -1).contiguous()
         return self.o_proj(o), None
 

@@ -34,7 +34,8 @@ from . import _lib
 __all__ = [
     "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
     "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
-    "lucid_attention", "padded_len", "decode_update", "decode_attention", "stored_tiles_fit",
+    "lucid_attention", "padded_len", "decode_update", "decode_attention", "decode_step", "decode_step_fused",
+    "stored_tiles_fit",
 ]
 
 
@@ -320,3 +321,36 @@ def decode_attention(query: torch.Tensor, key_cache: torch.Tensor, x_cache: torc
                                ov.data_ptr(), *_s3(ov), ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_decode_attn")
     return o
+
+
+def decode_step_fused(num_heads: int, num_kv_heads: int, new_tokens: int) -> bool:
+    """True when decode_step has a single-pass kernel for this shape (one new token
+    with 1 or 2 query heads per kv head, or two new tokens without grouping)."""
+    return bool(_lib.load().lucid_decode_step_fused(num_heads, num_kv_heads, new_tokens))
+
+
+def decode_step(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
+                x_cache: torch.Tensor, scale: float, eps: float = 1e-5):
+    """One decoding step of LucidAttention.forward (modeling_lucid.py:467-481, then
+    :505-549) in one pass over the cache: x_new = get_new_v_prime(key, value) against
+    the cache and the attention of the new queries over [cache; new tokens].
+    query [B,Hq,Ln,D], key / value [B,Hkv,Ln,D], caches [B,Hkv,Nc,D] holding the
+    tokens before this step (raw keys, solved values).  Returns (O [B,Ln,Hq,D],
+    x_new [B,Hkv,Ln,D]); the caller appends (key, x_new) to its cache.  Shapes
+    without a fused kernel (decode_step_fused false) raise."""
+    lib = _lib.load()
+    query, key, value = _prep_dec(query, "query"), _prep_dec(key, "key"), _prep_dec(value, "value")
+    key_cache, x_cache = _prep_dec(key_cache, "key_cache"), _prep_dec(x_cache, "value_cache")
+    B, Hq, Ln, D = query.shape
+    Hkv, Nc = key_cache.shape[1], key_cache.shape[2]
+    x_new = torch.empty(B, Hkv, Ln, D, dtype=torch.bfloat16, device=query.device)
+    o = torch.empty(B, Ln, Hq, D, dtype=torch.bfloat16, device=query.device)
+    ov = o.transpose(1, 2)
+    ws = _ws(lib.lucid_decode_step_workspace_bytes(B, Hq, Hkv, Ln, Nc, D), query.device)
+    rc = lib.lucid_decode_step(B, Hq, Hkv, Ln, Nc, D, float(scale), float(eps), query.data_ptr(), *_s3(query),
+                               key.data_ptr(), *_s3(key), value.data_ptr(), *_s3(value),
+                               key_cache.data_ptr(), *_s3(key_cache), x_cache.data_ptr(), *_s3(x_cache),
+                               x_new.data_ptr(), *_s3(x_new), ov.data_ptr(), *_s3(ov),
+                               ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_decode_step")
+    return o, x_new

@@ -66,6 +66,21 @@ def test_host_helpers(lib):
     assert lib.lucid_solve_bwd_fast_workspace_bytes(1, 1, 100, D) == lib.lucid_solve_bwd_workspace_bytes(1, 1, 100, D)
 
 
+def test_decode_step_shapes(lib):
+    """The fused decode step covers one new token with 1 or 2 query heads per kv
+    head and two new tokens without grouping; its workspace holds per-split sums
+    (128 floats per new token) and softmax partials (130 per query slot)."""
+    for (hq, hkv, ln), want in {(8, 8, 1): 1, (4, 2, 1): 1, (4, 4, 2): 1, (8, 1, 1): 0, (4, 4, 3): 0,
+                                (4, 2, 2): 0, (3, 2, 1): 0, (4, 0, 1): 0}.items():
+        assert lib.lucid_decode_step_fused(hq, hkv, ln) == want, (hq, hkv, ln)
+    a = lib.lucid_decode_step_workspace_bytes(4, 8, 4, 1, 5000, 128) - 256
+    b = lib.lucid_decode_step_workspace_bytes(4, 8, 4, 2, 5000, 128) - 256
+    assert a > 0 and a % ((128 + 2 * 130) * 4) == 0 and b == 2 * a
+    # a shape without a single-pass kernel is refused before any launch
+    rc = lib.lucid_decode_step(1, 8, 1, 1, 16, 128, 0.088, 1e-5, *([16, 128, 128, 128] * 7), 16, 4096, None)
+    assert rc == 1
+
+
 def test_argument_errors_without_launch(lib):
     """Bad shapes / alignment / workspace are rejected before any CUDA call."""
     from lucid_b200 import _lib as L

@@ -65,17 +65,76 @@ def test_decode_attention_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc, D):
     assert err.max() <= 0, np.abs(o - ref).max()
 
 
-@pytest.mark.parametrize("hd", [128, 68])
-def test_layer_prefill_then_decode_matches_ops(cuda_device, hd):
+def _bf16_close(torch, got, ref):
+    """|got - ref| <= 1e-2 + 2^-7 |ref|: one bf16 rounding of either side apart."""
+    err = (got.float() - ref.float()).abs() - (1e-2 + 2.0 ** -7 * ref.float().abs())
+    assert err.max().item() <= 0, (got.float() - ref.float()).abs().max().item()
+
+
+STEP_CASES = [(4, 8, 8, 1, 5000, 128), (2, 4, 2, 1, 3000, 68), (1, 2, 2, 2, 700, 128), (2, 4, 4, 1, 37, 64),
+              (1, 2, 1, 1, 40000, 128)]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Ln,Nc,D", STEP_CASES)
+def test_decode_step_matches_two_pass(cuda_device, B, Hq, Hkv, Ln, Nc, D):
+    """The fused step (one pass over the cache) against decode_update, the cache
+    append and decode_attention (two passes)."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import decode_attention, decode_step, decode_step_fused, decode_update
+    assert decode_step_fused(Hq, Hkv, Ln)
+    g = torch.Generator(device=cuda_device).manual_seed(Nc + D)
+    rn = lambda *sh, sc=1.0: (sc * torch.randn(*sh, generator=g, device=cuda_device)).to(torch.bfloat16)
+    q, kn, vn = rn(B, Hq, Ln, D), rn(B, Hkv, Ln, D), rn(B, Hkv, Ln, D)
+    kc, xc = rn(B, Hkv, Nc, D), rn(B, Hkv, Nc, D, sc=0.1)
+    s = D ** -0.5
+    o, x = decode_step(q, kn, vn, kc, xc, s, 1e-5)
+    x2 = decode_update(kn, vn, kc, xc, s, 1e-5)
+    o2 = decode_attention(q, torch.cat([kc, kn], 2), torch.cat([xc, x2], 2), s)
+    assert o.shape == o2.shape == (B, Ln, Hq, D) and x.shape == x2.shape == (B, Hkv, Ln, D)
+    _bf16_close(torch, x, x2)
+    _bf16_close(torch, o, o2)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Ln,Nc,D", STEP_CASES[:4] + [(1, 2, 2, 2, 0, 128)])
+def test_decode_step_matches_oracle(cuda_device, B, Hq, Hkv, Ln, Nc, D):
+    """x_new against the oracle's get_new_v_prime and the attention against the
+    oracle over the cache with the new tokens appended (x_new rounded to bf16 as
+    the cache stores it); an empty cache included."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import decode_step
+    from oracle.lucid_oracle import decode_attention as ref_attn
+    from oracle.lucid_oracle import decode_update as ref_update
+    g = np.random.default_rng(Nc + 7 * Ln)
+    bf = lambda a: (torch.tensor(a, dtype=torch.float32).bfloat16().double().numpy())
+    q, kn, vn = bf(g.standard_normal((B, Hq, Ln, D))), bf(g.standard_normal((B, Hkv, Ln, D))), \
+        bf(g.standard_normal((B, Hkv, Ln, D)))
+    kc = bf(0.6 * g.standard_normal((B, Hkv, 1, D)) + 0.8 * g.standard_normal((B, Hkv, Nc, D)))
+    xc = bf(0.1 * g.standard_normal((B, Hkv, Nc, D)))
+    s = D ** -0.5
+    x_ref = ref_update(kn, vn, kc, xc, s, 1e-5)
+    o_ref = ref_attn(q, np.concatenate([kc, kn], 2), np.concatenate([xc, bf(x_ref)], 2), s)
+    o, x = decode_step(*(_bf(torch, a, cuda_device) for a in (q, kn, vn, kc, xc)), s, 1e-5)
+    for got, ref in ((x, x_ref), (o, o_ref)):
+        got = got.float().cpu().numpy()
+        assert got.shape == ref.shape
+        err = np.abs(got - ref) - (1e-2 + 2.0 ** -8 * np.abs(ref))
+        assert err.max() <= 0, np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("hd,heads,kv", [(128, 4, 2), (68, 4, 2), (68, 8, 1)])
+def test_layer_prefill_then_decode_matches_ops(cuda_device, hd, heads, kv):
     """LucidAttention with a cache: prefill fills (raw keys, solved values) and
     a decode step equals decode_update + decode_attention on that cache (head_dim
-    128, and the reference model's 68)."""
+    128, and the reference model's 68): through the fused step where its shape has
+    one (2 query heads per kv head), through the two calls otherwise (8)."""
     torch = pytest.importorskip("torch")
     from transformers import DynamicCache, LlamaConfig
-    from lucid_b200 import LucidSolveFunction, decode_attention, decode_update
+    from lucid_b200 import LucidSolveFunction, decode_attention, decode_step_fused, decode_update
     from lucid_b200.layer import LucidAttention
     torch.manual_seed(0)
-    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=hd,
+    fused = decode_step_fused(heads, kv, 1)
+    assert fused == (heads // kv == 2)
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=heads, num_key_value_heads=kv, head_dim=hd,
                       rms_norm_eps=1e-5)
     layer = LucidAttention(cfg, 0).to(cuda_device, torch.bfloat16).eval()
     T = 200
@@ -88,20 +147,25 @@ def test_layer_prefill_then_decode_matches_ops(cuda_device, hd):
             (cache.key_cache[0], cache.value_cache[0])
         assert kc.shape[2] == T + 1 and xc.shape[2] == T + 1
         # prefill part of the cache holds the solved values
-        k_pre = layer.k_proj(h[:, :T]).view(1, T, 2, hd).transpose(1, 2)
-        v_pre = layer.v_proj(h[:, :T]).view(1, T, 2, hd).transpose(1, 2)
+        k_pre = layer.k_proj(h[:, :T]).view(1, T, kv, hd).transpose(1, 2)
+        v_pre = layer.v_proj(h[:, :T]).view(1, T, kv, hd).transpose(1, 2)
         x_pre = LucidSolveFunction.apply(k_pre, v_pre, layer.scaling, 1e-5)
         torch.testing.assert_close(xc[:, :, :T], x_pre, rtol=0, atol=0)
         # decode step = decode_update + decode_attention on the cache
-        k1 = layer.k_proj(h[:, T:]).view(1, 1, 2, hd).transpose(1, 2)
-        v1 = layer.v_proj(h[:, T:]).view(1, 1, 2, hd).transpose(1, 2)
+        k1 = layer.k_proj(h[:, T:]).view(1, 1, kv, hd).transpose(1, 2)
+        v1 = layer.v_proj(h[:, T:]).view(1, 1, kv, hd).transpose(1, 2)
         x1 = decode_update(k1, v1, kc[:, :, :T], xc[:, :, :T], layer.scaling, 1e-5)
-        torch.testing.assert_close(xc[:, :, T:], x1, rtol=0, atol=0)
-        q1 = layer.q_proj(h[:, T:]).view(1, 1, 4, hd).transpose(1, 2)
+        q1 = layer.q_proj(h[:, T:]).view(1, 1, heads, hd).transpose(1, 2)
         o1 = decode_attention(q1, kc, xc, layer.scaling)
         ref = layer.o_proj(o1.reshape(1, 1, -1))
-        torch.testing.assert_close(out, ref, rtol=0, atol=0)
         assert torch.isfinite(out).all()
+        if fused:   # one pass, merged in another order: within a bf16 rounding
+            _bf16_close(torch, xc[:, :, T:], x1)
+            scale = ref.float().abs().max().item()
+            assert (out.float() - ref.float()).abs().max().item() <= 1e-2 * scale
+        else:       # the same two calls
+            torch.testing.assert_close(xc[:, :, T:], x1, rtol=0, atol=0)
+            torch.testing.assert_close(out, ref, rtol=0, atol=0)
 
 
 def _kc_bar(d_k, d_w, d_beta, ref):
