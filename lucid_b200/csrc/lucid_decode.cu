@@ -402,23 +402,103 @@ cudaError_t launch_decode_attn(DecodeArgs a, cudaStream_t st) {
 // lane, so only small slot counts have an instance; decode_step_fused says which.
 // ===========================================================================
 
-template <int NU, int NA, int ROWS>
-__global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const DecodeStepArgs a) {
+// The cache rows stream through a per-thread ring of kStepStages stages in shared
+// memory filled by cp.async: each lane copies exactly the 16 elements of K and of X
+// it later reads, so a stage needs no synchronisation beyond the thread's own
+// cp.async.wait_group, and kStepStages - 1 row iterations stay in flight while the
+// current one computes.  Chunks are CB bytes (16 when every row start is 16-byte
+// aligned, else 8) of CE = CB / 2 elements; lane j of a quarter-warp group holds
+// chunks q at elements CE j + 8 CE q, so one copy instruction of the group covers
+// 8 CB contiguous bytes of its row (whole sectors).  The bytes of a chunk at or past
+// D, and whole chunks of rows past the split, are zero-filled (cp.async with a
+// smaller source size) and read no memory.
+constexpr int kStepStages = 5;
+constexpr int kStepThreads = 256;
+constexpr int kStepSmem = kStepStages * 2 * 32 * kStepThreads;  // bytes of the ring
+
+template <int CB>
+__device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void* src, int bytes) {
+  if constexpr (CB == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// dot product of a lane's 16 elements (chunks of CE at ej + 8 CE q) with a row of
+// 128 floats in shared memory
+template <int CE>
+__device__ __forceinline__ float dot_chunks(const float* row, int ej, const float (&k)[16]) {
+  float d = 0.f;
+#pragma unroll
+  for (int q = 0; q < 16 / CE; ++q)
+#pragma unroll
+    for (int c = 0; c < CE / 4; ++c) {
+      const float4 r4 = *reinterpret_cast<const float4*>(row + ej + 8 * CE * q + 4 * c);
+      const float* kk = k + q * CE + 4 * c;
+      d = fmaf(r4.x, kk[0], d);
+      d = fmaf(r4.y, kk[1], d);
+      d = fmaf(r4.z, kk[2], d);
+      d = fmaf(r4.w, kk[3], d);
+    }
+  return d;
+}
+
+template <int NU, int NA, int CB>
+__global__ void __launch_bounds__(kStepThreads, 2) lucid_decode_step_partial_kernel(const DecodeStepArgs a) {
   constexpr int NS = NU + NA;
-  constexpr int kRow = 132;  // 128 values, the running maximum and the denominator, padded
+  constexpr int NQ = 32 / CB;    // chunks per lane per tensor row
+  constexpr int CE = CB / 2;     // elements per chunk
+  constexpr int kRow = 132;      // 128 values, the running maximum and the denominator, padded
+  extern __shared__ __align__(16) unsigned char ring[];  // [stage][tensor][chunk][thread][CB]
   __shared__ __align__(16) float kq[NS][128];  // normalised new keys, then scaled queries
   __shared__ __align__(16) float red[8][NS][kRow];
   const int split = blockIdx.x, bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H, gq = a.Hq / a.H;
   const long long BH = (long long)a.B * a.H;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = lane >> 3, e0 = (lane & 7) * 16;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = lane >> 3, ej = (lane & 7) * CE;  // chunk q of this lane: elements ej + 8 CE q
   const float c1 = a.s * 1.4426950408889634f, c2 = 1.4426950408889634f / a.s;
   const float inv_d = 1.f / (float)a.D;
   const int r0 = split * a.rows_per_split;
   const int r1 = min(a.Nc, r0 + a.rows_per_split);
+  const int nit = r1 > r0 ? (r1 - r0 + 31) / 32 : 0;  // row iterations (32 rows of the CTA each)
   const bf16* kbase = a.kc + (long long)b * a.kc_sb + (long long)h * a.kc_sh;
   const bf16* xbase = a.xc + (long long)b * a.xc_sb + (long long)h * a.xc_sh;
+  const uint32_t ring0 = (uint32_t)__cvta_generic_to_shared(ring);
+  // iteration `it` -> stage `st`: this thread's row r0 + 32 it + 4 warp + grp
+  auto issue = [&](int it, int st) {
+    const int row = r0 + 32 * it + 4 * warp + grp;
+    const bool ok = row < r1;
+    const bf16* kp = kbase + (long long)(ok ? row : r0) * a.kc_st;
+    const bf16* xp = xbase + (long long)(ok ? row : r0) * a.xc_st;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int el = ej + 8 * CE * q;
+      const int bytes = ok ? max(0, min(CB, (a.D - el) * 2)) : 0;
+      const uint32_t dk = ring0 + (uint32_t)((((st * 2 + 0) * NQ + q) * kStepThreads + tid) * CB);
+      const uint32_t dx = ring0 + (uint32_t)((((st * 2 + 1) * NQ + q) * kStepThreads + tid) * CB);
+      cp_async_zfill<CB>(dk, bytes ? (const void*)(kp + el) : (const void*)kbase, bytes);
+      cp_async_zfill<CB>(dx, bytes ? (const void*)(xp + el) : (const void*)xbase, bytes);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kStepStages - 1; ++i) {
+    if (i < nit) issue(i, i);
+    cp_async_commit();
+  }
   if (warp < NU) {  // RMSNorm of new key `warp` (a whole warp per key)
     const bool act = lane * 4 < a.D;
     const float4 k4 = ld_bf16x4_d(a.kn + (long long)b * a.kn_sb + (long long)h * a.kn_sh +
@@ -429,7 +509,7 @@ __global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const
     kq[warp][lane * 4 + 2] = k4.z * r;
     kq[warp][lane * 4 + 3] = k4.w * r;
   }
-  for (int e = threadIdx.x; e < NA * 128; e += blockDim.x) {
+  for (int e = tid; e < NA * 128; e += blockDim.x) {
     const int sl = e >> 7, c = e & 127, j = sl / NU, l = sl % NU;  // query head h*gq + j, token l
     kq[NU + sl][c] = c < a.D ? __bfloat162float(a.q[(long long)b * a.q_sb + (long long)(h * gq + j) * a.q_sh +
                                                     (long long)l * a.q_st + c]) * c1
@@ -446,71 +526,63 @@ __global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const
     m[t] = -INFINITY;
     l[t] = 0.f;
   }
-  for (int base = r0; base < r1; base += 32 * ROWS) {
-    float k[ROWS][16], x[ROWS][16];
+  int st = 0;
+  for (int it = 0; it < nit; ++it) {
+    {
+      const int nx = it + kStepStages - 1;
+      if (nx < nit) issue(nx, nx % kStepStages);
+      cp_async_commit();
+    }
+    cp_async_wait<kStepStages - 1>();  // this thread's copies of iteration `it` have landed
+    float k[16], x[16];
 #pragma unroll
-    for (int u = 0; u < ROWS; ++u) {
-      const int row = base + 32 * u + 4 * warp + grp;
-      if (row < r1) {
-        ld_row16(kbase + (long long)row * a.kc_st, e0, a.D, k[u]);
-        ld_row16(xbase + (long long)row * a.xc_st, e0, a.D, x[u]);
+    for (int q = 0; q < NQ; ++q) {
+      const unsigned char* pk = ring + (((st * 2 + 0) * NQ + q) * kStepThreads + tid) * CB;
+      const unsigned char* px = ring + (((st * 2 + 1) * NQ + q) * kStepThreads + tid) * CB;
+      if constexpr (CB == 16) {
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(pk), k + q * CE);
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(px), x + q * CE);
       } else {
+        const uint2 uk = *reinterpret_cast<const uint2*>(pk), ux = *reinterpret_cast<const uint2*>(px);
+        const __nv_bfloat162* hk = reinterpret_cast<const __nv_bfloat162*>(&uk);
+        const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&ux);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) k[u][i] = x[u][i] = 0.f;
+        for (int i = 0; i < 2; ++i) {
+          const float2 fk = __bfloat1622float2(hk[i]), fx = __bfloat1622float2(hx[i]);
+          k[q * CE + 2 * i] = fk.x;
+          k[q * CE + 2 * i + 1] = fk.y;
+          x[q * CE + 2 * i] = fx.x;
+          x[q * CE + 2 * i + 1] = fx.y;
+        }
       }
     }
-    // every row's weights first (the keys die here), then one accumulation step
-    // per slot for all ROWS rows
-    float ev[NU][ROWS], zv[NA][ROWS];
+    st = (st + 1 == kStepStages) ? 0 : st + 1;
+    const bool valid = r0 + 32 * it + 4 * warp + grp < r1;  // uniform within the group
+    float ss = 0.f;
 #pragma unroll
-    for (int u = 0; u < ROWS; ++u) {
-      const bool valid = base + 32 * u + 4 * warp + grp < r1;  // uniform within the group
-      float ss = 0.f;
+    for (int i = 0; i < 16; ++i) ss = fmaf(k[i], k[i], ss);
+    const float rs = rsqrtf(grp_sum(ss) * inv_d + a.eps);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ss = fmaf(k[u][i], k[u][i], ss);
-      const float rs = rsqrtf(grp_sum(ss) * inv_d + a.eps);
+    for (int t = 0; t < NU; ++t) {
+      const float d = grp_sum(dot_chunks<CE>(kq[t], ej, k)) * rs;
+      const float e = valid ? exp2f(fmaf(d, c1, -c2)) : 0.f;
 #pragma unroll
-      for (int t = 0; t < NU; ++t) {
-        const float d = grp_sum(dot16_smem(&kq[t][e0], k[u])) * rs;
-        ev[t][u] = valid ? exp2f(fmaf(d, c1, -c2)) : 0.f;
-      }
-#pragma unroll
-      for (int t = 0; t < NA; ++t) {
-        const float z = grp_sum(dot16_smem(&kq[NU + t][e0], k[u]));
-        zv[t][u] = valid ? z : -INFINITY;
-      }
+      for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(e, x[i], acc[t][i]);
     }
-#pragma unroll
-    for (int t = 0; t < NU; ++t)
-#pragma unroll
-      for (int u = 0; u < ROWS; ++u)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(ev[t][u], x[u][i], acc[t][i]);
 #pragma unroll
     for (int t = 0; t < NA; ++t) {
-      float mn = m[t];
+      const float z = grp_sum(dot_chunks<CE>(kq[NU + t], ej, k));
+      if (valid) {
+        const float mn = fmaxf(m[t], z);
+        const float al = exp2f(m[t] - mn), p = exp2f(z - mn);  // al = 0 while m is -inf
+        l[t] = l[t] * al + p;
 #pragma unroll
-      for (int u = 0; u < ROWS; ++u) mn = fmaxf(mn, zv[t][u]);
-      if (mn != -INFINITY) {  // some row of the group valid so far
-        const float al = exp2f(m[t] - mn);  // 0 while m is still -inf
-        float p[ROWS], psum = 0.f;
-#pragma unroll
-        for (int u = 0; u < ROWS; ++u) {
-          p[u] = exp2f(zv[t][u] - mn);  // 0 for the invalid rows
-          psum += p[u];
-        }
-        l[t] = l[t] * al + psum;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v = acc[NU + t][i] * al;
-#pragma unroll
-          for (int u = 0; u < ROWS; ++u) v = fmaf(p[u], x[u][i], v);
-          acc[NU + t][i] = v;
-        }
+        for (int i = 0; i < 16; ++i) acc[NU + t][i] = fmaf(p, x[i], acc[NU + t][i] * al);
         m[t] = mn;
       }
     }
   }
+  cp_async_wait<0>();  // nothing of this thread's stays in flight past the loop
   // merge the 4 lane groups of the warp: sums for the update, (max, sum) for the attention
 #pragma unroll
   for (int t = 0; t < NU; ++t)
@@ -541,9 +613,11 @@ __global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const
 #pragma unroll
     for (int t = 0; t < NS; ++t)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<float4*>(&red[warp][t][e0 + 4 * c]) =
+      for (int c = 0; c < 4; ++c) {  // accumulators 4c..4c+3: chunk 4c / CE, offset 4c % CE
+        const int col = ej + 8 * CE * (4 * c / CE) + (4 * c) % CE;
+        *reinterpret_cast<float4*>(&red[warp][t][col]) =
             make_float4(acc[t][4 * c], acc[t][4 * c + 1], acc[t][4 * c + 2], acc[t][4 * c + 3]);
+      }
     if (lane == 0) {
 #pragma unroll
       for (int t = 0; t < NA; ++t) {
@@ -554,7 +628,7 @@ __global__ void __launch_bounds__(256, 2) lucid_decode_step_partial_kernel(const
   }
   __syncthreads();
   // merge the 8 warps into this split's partials
-  for (int e = threadIdx.x; e < NS * 128; e += blockDim.x) {
+  for (int e = tid; e < NS * 128; e += blockDim.x) {
     const int sl = e >> 7, c = e & 127;
     if (sl < NU) {
       float sum = 0.f;
@@ -646,13 +720,24 @@ __global__ void __launch_bounds__(256) lucid_decode_step_finish_kernel(const Dec
   }
 }
 
-template <int NU, int NA, int ROWS>
-static cudaError_t launch_decode_step_t(const DecodeStepArgs& a, cudaStream_t st) {
-  lucid_decode_step_partial_kernel<NU, NA, ROWS><<<dim3(a.nsplit, a.B * a.H), 256, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+template <int NU, int NA, int CB>
+static cudaError_t launch_decode_step_cb(const DecodeStepArgs& a, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(lucid_decode_step_partial_kernel<NU, NA, CB>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem);
+  if (e != cudaSuccess) return e;
+  lucid_decode_step_partial_kernel<NU, NA, CB><<<dim3(a.nsplit, a.B * a.H), kStepThreads, kStepSmem, st>>>(a);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   lucid_decode_step_finish_kernel<NU, NA><<<a.B * a.H, 256, 0, st>>>(a);
   return cudaGetLastError();
+}
+
+// 16-byte chunks when every row of both caches starts on a 16-byte boundary
+template <int NU, int NA>
+static cudaError_t launch_decode_step_t(const DecodeStepArgs& a, cudaStream_t st) {
+  const bool a16 = ((reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.xc)) & 15u) == 0 &&
+                   ((a.kc_sb | a.kc_sh | a.kc_st | a.xc_sb | a.xc_sh | a.xc_st) & 7) == 0;
+  return a16 ? launch_decode_step_cb<NU, NA, 16>(a, st) : launch_decode_step_cb<NU, NA, 8>(a, st);
 }
 
 bool decode_step_fused(int gq, int Ln) {
@@ -664,9 +749,9 @@ cudaError_t launch_decode_step(DecodeStepArgs a, cudaStream_t st) {
   a.nsplit = decode_splits(a.B, a.H, a.Nc);
   a.rows_per_split = (a.Nc + a.nsplit - 1) / a.nsplit;
   const int gq = a.Hq / a.H;
-  if (a.Ln == 1 && gq == 1) return launch_decode_step_t<1, 1, 2>(a, st);
-  if (a.Ln == 1 && gq == 2) return launch_decode_step_t<1, 2, 1>(a, st);
-  if (a.Ln == 2 && gq == 1) return launch_decode_step_t<2, 2, 1>(a, st);
+  if (a.Ln == 1 && gq == 1) return launch_decode_step_t<1, 1>(a, st);
+  if (a.Ln == 1 && gq == 2) return launch_decode_step_t<1, 2>(a, st);
+  if (a.Ln == 2 && gq == 1) return launch_decode_step_t<2, 2>(a, st);
   return cudaErrorInvalidValue;
 }
 
