@@ -47,11 +47,26 @@ CONFIGS = {
     "cfg2": (4, 32, 4096, 128, 128 ** -0.5),
     "small": (1, 8, 4096, 128, 128 ** -0.5),
     "8k": (1, 32, 8192, 128, 128 ** -0.5),   # profiling case (about 1.5 GB on the device)
+    "32k-gqa": (1, 32, 32768, 128, 128 ** -0.5),
 }
+# kv heads of the grouped-query configurations (the others are MHA)
+KV_HEADS = {"32k-gqa": 4}
 
 
-def flops_per_step(B, H, N, D):
-    return 14.0 * N * N * D * B * H
+def flops_per_step(B, H, N, D, Hkv=None):
+    """Algorithmic flops of one LUCID fwd+bwd: the attention's 7 N^2 D per query head
+    and the solve's 7 N^2 D per kv head (14 N^2 D per head without grouping)."""
+    Hkv = H if Hkv is None else Hkv
+    return 7.0 * N * N * D * B * (H + Hkv)
+
+
+def stage_units(H, Hkv):
+    """Per stage: its algorithmic GEMM work in units of N^2 D per batch element (a causal
+    GEMM over the lower triangle is N^2 D flops per head).  The attention stages run per
+    query head, the solve stages per kv head; the row passes' 1 excludes the S and dP
+    recomputation of the recomputing schedule, which is executed but not algorithmic."""
+    return {"solve_fwd": 2 * Hkv, "attn_fwd": 2 * H, "attn_bwd": 4 * H, "attn_bwd_row": 1 * H,
+            "solve_bwd": 4 * Hkv, "solve_bwd_row": 1 * Hkv}
 
 
 def peaks():
@@ -172,6 +187,8 @@ def reference_arm(args):
     if args.config == "decode":
         return decode_reference_arm(args)
     B, H, N, D, _ = CONFIGS[args.config]
+    Hkv = KV_HEADS.get(args.config, H)
+    heads = f"H{H}" if Hkv == H else f"Hq{H} Hkv{Hkv}"
     n_cpu = args.cpu_n
     cpu_reference_sample(1024, D)
     for _ in range(args.warmup):
@@ -183,7 +200,7 @@ def reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} (sampled: 1 head at N={n_cpu})",
+        "config": {"workload": f"LUCID attention fwd+bwd B{B} {heads} N{N} D{D} (sampled: 1 head at N={n_cpu})",
                    "global_batch": B, "seq_len": N, "parallelism": "cpu"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"1 (batch, head) at N={n_cpu}, D={D}, fp32, oracle/torch_ref.py"},
@@ -951,12 +968,13 @@ def main(argv=None):
         return bench_decode(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
     B, H, N, D, qs = CONFIGS[args.config]
+    Hkv = KV_HEADS.get(args.config, H)
     s = D ** -0.5
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     mk = lambda *shape, sc=1.0: (torch.randn(*shape, generator=g, device=dev) * sc).to(torch.bfloat16)
     q = mk(B, H, N, D, sc=qs).requires_grad_(True)
-    k = mk(B, H, N, D).requires_grad_(True)
-    v = mk(B, H, N, D).requires_grad_(True)
+    k = mk(B, Hkv, N, D).requires_grad_(True)
+    v = mk(B, Hkv, N, D).requires_grad_(True)
     do = mk(B, N, H, D)
 
     def step():
@@ -984,23 +1002,18 @@ def main(argv=None):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    fl = flops_per_step(B, H, N, D) * world
+    fl = flops_per_step(B, H, N, D, Hkv) * world
     tflops = fl / (ms * 1e-3) / 1e12
 
     # ---- per-kernel timing (dominant kernel -> roofline) ----
-    # algorithmic GEMM work of each kernel in units of N^2 D per (batch, head)
-    # (causal: each GEMM over the lower triangle is N^2 D flops); the row
-    # passes recompute S and dP, which is executed but not algorithmic work.
     pk_burst, pk_sust, hbm, pk_kind = peaks()
-    per_stage_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": 1,
-                       "solve_bwd": 4, "solve_bwd_row": 1}
+    per_stage_flops = stage_units(H, Hkv)
     # the stored-tile schedule (chosen by the ops when its workspace fits) streams the
     # column passes' tiles through the row passes: one GEMM per tile, no recompute
     from lucid_b200.ops import stored_tiles_fit
-    stored = stored_tiles_fit(lib.lucid_attn_bwd_fast_workspace_bytes(B, H, H, N, D), dev)
+    stored = stored_tiles_fit(lib.lucid_attn_bwd_fast_workspace_bytes(B, H, Hkv, N, D), dev)
     row_exec = 1 if stored else 3
-    executed_flops = {"solve_fwd": 2, "attn_fwd": 2, "attn_bwd": 4, "attn_bwd_row": row_exec,
-                      "solve_bwd": 4, "solve_bwd_row": row_exec}
+    executed_flops = dict(per_stage_flops, attn_bwd_row=row_exec * H, solve_bwd_row=row_exec * Hkv)
     stage_ms = {}
     with torch.no_grad():
         x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
@@ -1026,7 +1039,7 @@ def main(argv=None):
             stage_ms[name] = tot.value / max(n.value, 1)
         lib.lucid_profile_enable(0)
         del x, khat, u, rstd, dinv, o, lse, dq, dkf, dxf
-    unit_flops = float(N) * N * D * B * H
+    unit_flops = float(N) * N * D * B
     stage_tflops = {n: {"alg": per_stage_flops[n] * unit_flops / (stage_ms[n] * 1e-3) / 1e12,
                         "executed": executed_flops[n] * unit_flops / (stage_ms[n] * 1e-3) / 1e12}
                     for n in per_stage_flops}
@@ -1048,7 +1061,8 @@ def main(argv=None):
     dot = do.transpose(1, 2)
     def sdpa_step():
         qd.grad = kd.grad = vd.grad = None
-        F.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=s).backward(dot)
+        F.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=s,
+                                       enable_gqa=Hkv != H).backward(dot)
     for _ in range(2):
         sdpa_step()
     torch.cuda.synchronize()
@@ -1069,8 +1083,9 @@ def main(argv=None):
         hk = k.detach().cpu().pin_memory()
         hv = v.detach().cpu().pin_memory()
         hdo = do.cpu().pin_memory()
-        outs = [torch.empty(B, N, H, D, dtype=torch.bfloat16).pin_memory()] + \
-               [torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+        outs = [torch.empty(B, N, H, D, dtype=torch.bfloat16).pin_memory(),
+                torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory()] + \
+               [torch.empty(B, Hkv, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
         def e2e_step():
             qq = hq.to(dev, non_blocking=True).requires_grad_(True)
@@ -1098,9 +1113,10 @@ def main(argv=None):
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = float(t.item())
-        nbytes = B * H * N * D * 2
+        # q, dO (o, dq) per query head; k, v (dk, dv) per kv head
+        nbytes = 2 * B * N * D * 2 * (H + Hkv)
         e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
-               "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes}
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1126,8 +1142,9 @@ def main(argv=None):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} causal MHA per GPU",
-                   "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D,
+        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} causal MHA per GPU" if Hkv == H else
+                               f"LUCID attention fwd+bwd B{B} Hq{H} Hkv{Hkv} N{N} D{D} causal GQA per GPU",
+                   "global_batch": B * world, "seq_len": N, "heads": H, "kv_heads": Hkv, "head_dim": D,
                    "parallelism": f"(batch,head) shards x{world}, no collective",
                    "l2": "inputs larger than L2 (268 MB per tensor), no flush"},
         "tokens_per_s": B * N * world / (ms * 1e-3),
