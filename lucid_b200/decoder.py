@@ -123,6 +123,20 @@ class LucidForCausalLM(nn.Module):
                 m.weight.fill_(1.0)
         return self
 
+    def load_reference_state_dict(self, state_dict, strict: bool = True):
+        """Load a state dict of the reference's LlamaForCausalLM (modeling_lucid.py:847-968:
+        ``model.embed_tokens.weight``, ``model.layers.{i}.self_attn.q_proj.weight`` …,
+        ``model.norm.weight``, ``lm_head.weight``).  The submodule names are the
+        reference's, so only the ``model.`` prefix goes; rotary ``inv_freq`` buffers
+        (non-persistent in the reference, unused by this NoPE model) are skipped if a
+        checkpoint carries them."""
+        sd = {}
+        for k, v in state_dict.items():
+            if k.endswith("rotary_emb.inv_freq"):
+                continue
+            sd[k[len("model."):] if k.startswith("model.") else k] = v
+        return self.load_state_dict(sd, strict=strict)
+
     def forward(self, input_ids, past_key_values=None, logits_to_keep: int = 0, attn_events=None):
         """Logits of the last ``logits_to_keep`` positions (0: all).  With a
         transformers Cache, the prefill fills it (raw keys, solved values) as

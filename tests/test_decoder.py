@@ -2,7 +2,7 @@
 the reference model of lucid/config/config.json, for the full-model prefill.
 
 CPU: the configuration and the parameter count of the full model (built on
-the meta device).  GPU: a small model with the reference's head_dim 68 and
+the meta device), and loading a reference checkpoint's state dict.  GPU: a small model with the reference's head_dim 68 and
 8 query heads per kv head against a float32 torch restatement of the same
 model (attention by oracle/torch_ref.py, the reference's own torch path): the
 prefill logits, the cache-filling prefill against the fused one, and one
@@ -24,6 +24,22 @@ def test_config_matches_reference_model():
     per_layer = (2048 * 32 * 68 + 2 * 2048 * 4 * 68 + 32 * 68 * 2048) + 3 * 2048 * 5632 + 2 * 2048
     expect = 2 * 32000 * 2048 + 22 * per_layer + 2048
     assert sum(p.numel() for p in m.parameters()) == expect
+
+
+def test_reference_state_dict_loads():
+    """A checkpoint saved from the reference's LlamaForCausalLM (``model.`` prefix,
+    lm_head at the top) loads with every parameter in place."""
+    from lucid_b200.decoder import LucidForCausalLM, lucid_config
+    cfg = lucid_config(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                       num_key_value_heads=2, head_dim=16, vocab_size=50)
+    src = LucidForCausalLM(cfg).init_weights(seed=1)
+    ref_sd = {(k if k.startswith("lm_head.") else "model." + k): v for k, v in src.state_dict().items()}
+    ref_sd["model.rotary_emb.inv_freq"] = torch.ones(8)
+    assert "model.layers.1.self_attn.k_proj.weight" in ref_sd and "model.norm.weight" in ref_sd
+    dst = LucidForCausalLM(cfg).init_weights(seed=2)
+    dst.load_reference_state_dict(ref_sd)
+    for (n, a), (_, b) in zip(src.named_parameters(), dst.named_parameters()):
+        assert torch.equal(a, b), n
 
 
 def _ref_forward(model, ids, eps=1e-5):
