@@ -76,8 +76,9 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Solve forward that allocates nothing and takes no workspace.
- * No counterpart in the reference: it exists for callers that cannot call
+ * Solve forward that allocates nothing and takes no workspace: the computation
+ * of lucid_solve_fwd (LucidAttention.get_v_prime, modeling_lucid.py:551-574).
+ * The allocation-free form has no counterpart in the reference: it exists for callers that cannot call
  * cudaMalloc, e.g. a plugin hosted by an engine that owns all device memory
  * and forbids allocations after start-up, or a code path that cannot afford
  * the implicit device synchronisation of an allocation.
@@ -177,7 +178,9 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
                    float* lse, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Attention backward (autograd of eager_lucid_attention_forward).
+ * Attention backward: what torch autograd derives for the SDPA call of
+ * eager_lucid_attention_forward (modeling_lucid.py:505-549, causal, repeat_kv'd X),
+ * with the grouped-query sums over the query heads of each kv head done in-kernel.
  * In : q, k, o, dout strided; x internal; lse from lucid_attn_fwd.
  * Out: dq strided bf16 [B,Hq,N,D];
  *      dk_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dK through Q K^T)
@@ -301,10 +304,14 @@ int lucid_path_attn_fwd(int B, int T, int H, int HQ, int D, float scale,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Context-parallel building blocks (one process per GPU, each owning a contiguous
- * chunk of the sequence; no counterpart in the reference, which runs long
- * sequences on one GPU).  Buffers are full-length ([B, H, N, D] / internal
- * [B, H, Npad, D]); a rank fills the rows it owns and the chunks it receives.
+ * Context-parallel building blocks (one process per GPU, each owning one or more
+ * segments, i.e. contiguous row ranges, of the sequence; no counterpart in the
+ * reference, which runs long sequences on one GPU).  They are block-range forms of
+ * the prep and solve of get_v_prime (modeling_lucid.py:551-574; the blockwise
+ * Lucid_Tril_Solver.forward, :285-312, runs the same recurrence over row blocks) and
+ * of eager_lucid_attention_forward (:505-549).  Buffers are full-length ([B, H, N, D]
+ * / internal [B, H, Npad, D]); a rank fills the rows it owns and the segments it
+ * receives.
  *   lucid_cp_prep       prep of row blocks [blk_lo, blk_hi): khat_only = 1 computes
  *                       rstd and k^ only (received chunks), 0 also the diagonal
  *                       inverses (own chunk)
