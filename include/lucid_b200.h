@@ -108,6 +108,7 @@ int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps,
  * divided out.  k^ = RMSNorm(k) without affine (eps), computed on the fly for the
  * cache.  All tensors bf16 [B, H, L, D] strided (sb, sh, sn), strides multiples of
  * 4 elements; k_new / v_new / x_new have L = Ln, k_cache / x_cache L = Nc.
+ * The decode entry points take B x (query) heads <= 65535 (one grid row each).
  */
 size_t lucid_decode_workspace_bytes(int B, int H, int Ln, int Nc, int D);
 int lucid_decode_update(int B, int H, int Ln, int Nc, int D, float scale, float eps,

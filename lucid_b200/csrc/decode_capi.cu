@@ -33,7 +33,8 @@ int lucid_decode_update(int B, int H, int Ln, int Nc, int D, float scale, float 
                         const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
                         void* x_new, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                         void* workspace, size_t workspace_bytes, void* stream) {
-  if (B < 0 || H < 0 || Ln < 0 || Nc < 0 || D < 4 || D > kHeadDim || D % 4) return LUCID_ERR_SHAPE;
+  if (B < 0 || H < 0 || Ln < 0 || Nc < 0 || D < 4 || D > kHeadDim || D % 4 || (long long)B * H > 65535)
+    return LUCID_ERR_SHAPE;
   if (B == 0 || H == 0 || Ln == 0) return LUCID_OK;
   if (!a8(k_new) || !a8(k_cache) || !a8(x_cache) || !s4(kn_sb, kn_sh, kn_sn) || !s4(kc_sb, kc_sh, kc_sn) ||
       !s4(xc_sb, xc_sh, xc_sn))
@@ -62,7 +63,8 @@ int lucid_decode_attn(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale
                       const void* x_cache, int64_t xc_sb, int64_t xc_sh, int64_t xc_sn,
                       void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                       void* workspace, size_t workspace_bytes, void* stream) {
-  if (B < 0 || Hq < 0 || Hkv <= 0 || Ln < 0 || Nc < Ln || D < 4 || D > kHeadDim || D % 4 || Hq % Hkv != 0)
+  if (B < 0 || Hq < 0 || Hkv <= 0 || Ln < 0 || Nc < Ln || D < 4 || D > kHeadDim || D % 4 || Hq % Hkv != 0 ||
+      (long long)B * Hq > 65535)
     return LUCID_ERR_SHAPE;
   if (B == 0 || Hq == 0 || Ln == 0) return LUCID_OK;
   if (!a8(k_cache) || !a8(x_cache) || !s4(kc_sb, kc_sh, kc_sn) || !s4(xc_sb, xc_sh, xc_sn)) return LUCID_ERR_ALIGN;

@@ -94,6 +94,13 @@ def test_argument_errors_without_launch(lib):
     rc = lib.lucid_decode_update(1, 1, 1, 16, 66, 0.125, 1e-5, 16, 64, 64, 64, 16, 64, 64, 64, 16, 64, 64, 64,
                                  16, 64, 64, 64, 16, 64, 64, 64, 16, 4096, null)
     assert rc == 1
+    # more than 65535 (batch, head) rows in a decode grid
+    rc = lib.lucid_decode_update(256, 256, 1, 16, 64, 0.125, 1e-5, 16, 64, 64, 64, 16, 64, 64, 64, 16, 64, 64, 64,
+                                 16, 64, 64, 64, 16, 64, 64, 64, 16, 4096, null)
+    assert rc == 1
+    rc = lib.lucid_decode_attn(256, 256, 1, 1, 16, 64, 0.125, 16, 64, 64, 64, 16, 64, 64, 64, 16, 64, 64, 64,
+                               16, 64, 64, 64, 16, 4096, null)
+    assert rc == 1
     # misaligned pointer
     rc = lib.lucid_solve_fwd(1, 1, 128, 128, 0.088, 1e-5, 18, 128, 128, 128, 16, 128, 128, 128,
                              16, 16, 16, 16, 16, 16, 4096, null)
