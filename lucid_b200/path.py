@@ -29,7 +29,13 @@ import torch
 from . import _lib
 
 __all__ = ["parallel_lucid_path_attention", "ParallelLUCIDPathAttentionFunction", "path_fwd", "path_bwd",
-           "parallel_path_attention_fwd"]
+           "parallel_path_attention_fwd", "PathArgumentError"]
+
+
+class PathArgumentError(ValueError, AssertionError):
+    """An argument the reference op rejects.  The reference checks its arguments with
+    ``assert`` (parallel.py:230-239), so this is an AssertionError for callers written
+    against it, and a ValueError for everyone else."""
 
 
 def _stream() -> int:
@@ -166,17 +172,17 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
     if scale is None:
         scale = k.shape[-1] ** -0.5
     if q.shape[-1] not in _HEAD_DIMS or v.shape[-1] not in _HEAD_DIMS:
-        raise ValueError("only support head_dim in [16, 32, 64, 128]")
+        raise PathArgumentError("only support head_dim in [16, 32, 64, 128]")
     if q.shape[-1] != k.shape[-1]:
-        raise ValueError("q, k should have the same head_dim.")
+        raise PathArgumentError("q, k should have the same head_dim.")
     if k.shape != w.shape:
-        raise ValueError("k, w should have the same shape.")
+        raise PathArgumentError("k, w should have the same shape.")
     if beta.shape[:3] != k.shape[:3]:
-        raise ValueError("beta should have the same number of heads as k")
+        raise PathArgumentError("beta should have the same number of heads as k")
     if g is not None:
-        raise NotImplementedError("g is not supported")
+        raise PathArgumentError("g is not supported")
     if q.shape[-2] % k.shape[-2] != 0:
-        raise ValueError("the number of query heads should be divisible by the number of key heads")
+        raise PathArgumentError("the number of query heads should be divisible by the number of key heads")
     K, V = k.shape[-1], v.shape[-1]
     if K < 128 or V < 128:
         o, kc = parallel_lucid_path_attention(_pad128(k), _pad128(v), _pad128(w), beta,
@@ -186,7 +192,7 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
     if cu_seqlens is None:
         return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, bool(use_cache))
     if k.shape[0] != 1:
-        raise ValueError("cu_seqlens requires a packed batch of size 1")
+        raise PathArgumentError("cu_seqlens requires a packed batch of size 1")
     bounds = [int(x) for x in cu_seqlens.tolist()]
     outs, caches = [], []
     for a, b in zip(bounds[:-1], bounds[1:]):
@@ -208,7 +214,7 @@ def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):
     kernels for this op.  Head dimensions below 128 run zero-padded."""
     Kd, Vd = k.shape[-1], v.shape[-1]
     if Kd not in _HEAD_DIMS or Vd not in _HEAD_DIMS:
-        raise ValueError("only support head_dim in [16, 32, 64, 128]")
+        raise PathArgumentError("only support head_dim in [16, 32, 64, 128]")
     if Kd < 128 or Vd < 128:
         o, lse = parallel_path_attention_fwd(None if q is None else _pad128(q), _pad128(k), _pad128(v),
                                              _pad128(w), beta, scale=Kd ** -0.5 if scale is None else scale)
