@@ -16,6 +16,14 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU (sm_100a)")
 
 
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """List the deviations every parity check measured (tests/parity.py)."""
+    import parity
+
+    for line in parity.summary_lines():
+        terminalreporter.write_line(line)
+
+
 def from_bf16_bits(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << 16).view(np.float32)
 
