@@ -76,22 +76,24 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Solve forward that allocates nothing and takes no workspace: the computation
- * of lucid_solve_fwd (LucidAttention.get_v_prime, modeling_lucid.py:551-574).
- * The allocation-free form has no counterpart in the reference: it exists for callers that cannot call
+ * Solve forward that allocates nothing and takes no workspace.
+ * It has no counterpart in the reference: it exists for callers that cannot call
  * cudaMalloc, e.g. a plugin hosted by an engine that owns all device memory
  * and forbids allocations after start-up, or a code path that cannot afford
  * the implicit device synchronisation of an allocation.
- * Same arguments and results as lucid_solve_fwd minus the workspace.  Its
- * scratch (the per-block dependency flags and the status word) is a fixed
- * static device array of LUCID_NOALLOC_SCRATCH_BYTES bytes that every GPU
- * loading the library holds until the process exits:
+ * Same arguments as lucid_solve_fwd minus the workspace, and the same x, khat, u,
+ * rstd and dinv.  Its scratch (the per-block dependency flags and the run-time
+ * status word) is a fixed static device array of LUCID_NOALLOC_SCRATCH_BYTES bytes
+ * that every GPU loading the library holds until the process exits:
  *   - B * H * ceil(N / 128) must not exceed LUCID_NOALLOC_MAX_BLOCKS, else the
  *     call returns LUCID_ERR_TOO_LARGE and launches nothing;
  *   - the first call on each device looks up the array's device address, so
  *     make that first call before any stream capture;
  *   - every call clears and reuses the same array: calls whose execution
- *     overlaps on the GPU (e.g. on two streams) race, so serialise them.
+ *     overlaps on the GPU (e.g. on two streams) race, so serialise them;
+ *   - the status word of the last call (0, or a bounded wait that ran out, as
+ *     in every workspace) stays in the array until the next call clears it:
+ *     lucid_solve_fwd_noalloc_status reads it.
  */
 #define LUCID_NOALLOC_MAX_BLOCKS 16384
 #define LUCID_NOALLOC_SCRATCH_BYTES (256 + 4 * LUCID_NOALLOC_MAX_BLOCKS)
@@ -99,6 +101,12 @@ int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, float eps,
                             const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                             const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
                             void* x, void* khat, void* u, float* rstd, float* dinv, void* stream);
+/* Copy the run-time status word of the last lucid_solve_fwd_noalloc call on the
+ * current device into *status (host memory), ordered on `stream` after the work
+ * queued there before it: with pinned memory the value is valid once the stream
+ * has reached this point (synchronise it), with pageable memory when the call
+ * returns.  No allocation; LUCID_ERR_LAUNCH if the copy cannot be queued. */
+int lucid_solve_fwd_noalloc_status(int* status, void* stream);
 
 /*
  * Decode step of the solve: x_new = v_new - exp(scale k^_new K^_cache^T - 1/scale) X_cache.

@@ -584,6 +584,16 @@ extern "C" int lucid_solve_fwd_noalloc(int B, int H, int N, int D, float scale, 
                          dinv, ws, LUCID_NOALLOC_SCRATCH_BYTES, stream);
 }
 
+extern "C" int lucid_solve_fwd_noalloc_status(int* status, void* stream) {
+  if (!status) return LUCID_ERR_SHAPE;
+  void* ws = noalloc_scratch_ptr();
+  if (!ws) return LUCID_ERR_LAUNCH;
+  // the status word sits at lucid_workspace_status_offset() of the scratch, as in every workspace
+  const char* word = static_cast<const char*>(ws) + lucid_workspace_status_offset();
+  return to_status(cudaMemcpyAsync(status, word, sizeof(int), cudaMemcpyDeviceToHost,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
 // ---------------------------------------------------------------------------
 // tensor-core self test
 // ---------------------------------------------------------------------------

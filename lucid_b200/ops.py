@@ -22,6 +22,10 @@ the autograd functions and sliced back; zero columns change neither the
 scores nor the solve, and the kernels take the true D for the RMS mean of
 K^.  The stage functions take padded 128-column tensors and the true head
 dimension as ``d``.  There is no CPU path: CPU tensors raise.
+
+Run-time failures (a bounded wait inside a kernel that ran out) are read back from
+each call's status word without stalling the stream and raised as LucidError at the
+next call or by ``check_status()`` (_lib._StatusWatch).
 """
 from __future__ import annotations
 
@@ -35,8 +39,10 @@ __all__ = [
     "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
     "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
     "lucid_attention", "padded_len", "decode_update", "decode_attention", "decode_step", "decode_step_fused",
-    "stored_tiles_fit",
+    "stored_tiles_fit", "check_status",
 ]
+
+check_status = _lib.check_status
 
 
 def padded_len(n: int) -> int:
@@ -94,6 +100,7 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int
     """X = P^-1 V.  Returns (x_int, khat, u, rstd, dinv); x_int is
     [B, H, Npad, 128] (rows >= N are padding)."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     k = _prep(k, "key")
     v = _prep(v, "value")
     B, H, N, W = k.shape
@@ -112,12 +119,14 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int
                              v.data_ptr(), *_s3(v), x.data_ptr(), khat.data_ptr(), u.data_ptr(),
                              rstd.data_ptr(), dinv.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_solve_fwd")
+    _lib.STATUS.watch(ws, "lucid_solve_fwd")
     return x, khat, u, rstd, dinv
 
 
 def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float, d: int | None = None):
     """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,128], lse)."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     q = _prep(q, "query")
     k = _prep(k, "key")
     B, Hq, N, W = q.shape
@@ -135,6 +144,7 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), lse.data_ptr(),
                             ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_attn_fwd")
+    _lib.STATUS.watch(ws, "lucid_attn_fwd")
     return o, lse
 
 
@@ -142,6 +152,7 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
     """Backward of attn_fwd.  o, do are [B,N,Hq,128].  Returns
     (dq [B,Hq,N,128] bf16, dk_f32 [B,Hkv,Npad,128], dx_f32 [B,Hkv,Npad,128])."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     q = _prep(q, "query")
     k = _prep(k, "key")
     ot = _prep(o.transpose(1, 2), "attn_output")
@@ -162,12 +173,14 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
                             *_s3(dot), lse.data_ptr(), dq.data_ptr(), *_s3(dq), dk.data_ptr(),
                             dx.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_attn_bwd")
+    _lib.STATUS.watch(ws, "lucid_attn_bwd")
     return dq, dk, dx
 
 
 def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None, d: int | None = None):
     """Backward of solve_fwd.  Returns (dk, dv) bf16 [B,H,N,128]."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     k = _prep(k, "key")
     B, H, N, W = k.shape
     D = W if d is None else d
@@ -183,6 +196,7 @@ def solve_bwd(k, x_int, khat, u, rstd, dinv, dx_f32, scale: float, dk_add=None, 
                              dk.data_ptr(), *_s3(dk), dv.data_ptr(), *_s3(dv), ws.data_ptr(), ws.numel(),
                              _stream())
     _lib.check(rc, "lucid_solve_bwd")
+    _lib.STATUS.watch(ws, "lucid_solve_bwd")
     return dk, dv
 
 

@@ -70,6 +70,7 @@ def path_fwd(k, v, w, beta, q=None, scale=None, use_cache=False):
     forward workspace the backward reads; ``k_cache`` ([B,T,H,K], the keys
     transformed by every later Householder, prepare_k_cache.py) or None."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
     beta = _prep(beta, "beta", 3)
     B, T, H, K = k.shape
@@ -93,6 +94,7 @@ def path_fwd(k, v, w, beta, q=None, scale=None, use_cache=False):
                             w.data_ptr(), *_s3(w), beta.data_ptr(), int(beta.dtype == torch.float32), *beta.stride(),
                             o.data_ptr(), *_s3(o), kcp, *kcs, ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_path_fwd")
+    _lib.STATUS.watch(ws, "lucid_path_fwd")
     return o, ws, kc
 
 
@@ -100,6 +102,7 @@ def path_bwd(state, do, k, w, beta, q=None, scale=None):
     """Backward stage.  Returns (dq or None, dk, dv, dw, dbeta); with q None
     the query gradient is folded into dk (q = k)."""
     lib = _lib.load()
+    _lib.STATUS.poll()
     k, w, do = _prep(k, "k"), _prep(w, "w"), _prep(do, "do")
     beta = _prep(beta, "beta", 3)
     B, T, H, K = k.shape
@@ -124,6 +127,7 @@ def path_bwd(state, do, k, w, beta, q=None, scale=None):
                             dbeta.data_ptr(), int(dbeta.dtype == torch.float32), *dbeta.stride(),
                             ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_path_bwd")
+    _lib.STATUS.watch(ws, "lucid_path_bwd")
     return dq, dk, dv, dw, dbeta
 
 
@@ -220,6 +224,7 @@ def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):
                                              _pad128(w), beta, scale=Kd ** -0.5 if scale is None else scale)
         return o[..., :Vd], lse
     lib = _lib.load()
+    _lib.STATUS.poll()
     k, v, w = _prep(k, "k"), _prep(v, "v"), _prep(w, "w")
     beta = _prep(beta, "beta", 3)
     B, T, H, K = k.shape
@@ -243,4 +248,5 @@ def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):
                                  *beta.stride(), o.data_ptr(), *_s3(o), lse.data_ptr(), *lse.stride(),
                                  ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_path_attn_fwd")
+    _lib.STATUS.watch(ws, "lucid_path_attn_fwd")
     return o, lse

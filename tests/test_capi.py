@@ -127,3 +127,11 @@ def test_ops_refuse_cpu_tensors():
     q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         lucid_attention(q, q, q)
+
+
+def test_status_words_decode():
+    from lucid_b200 import _lib
+    assert _lib.decode_status(2 | (1 << 20)).startswith("solve forward: a cross-CTA dependency flag never arrived")
+    msg = _lib.decode_status(1 | (0x12 << 8) | (4 << 20))
+    assert msg.startswith("transposed-solve column pass: an mbarrier wait timed out")
+    assert "0x90" in msg

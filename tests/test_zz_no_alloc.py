@@ -3,7 +3,8 @@ cudaMalloc (for example a plugin inside an engine that owns all device
 memory, or a path that cannot afford an allocation's implicit device
 synchronisation).  It takes no workspace; its scratch is a fixed static
 device array.  Its results must equal those of lucid_solve_fwd, which takes
-a caller-allocated workspace, on consecutive calls that reuse the array.
+a caller-allocated workspace, on consecutive calls that reuse the array, and
+its status word (read back by lucid_solve_fwd_noalloc_status) must be clear.
 
 This file is collected last so that a failure here never hides another test."""
 import numpy as np
@@ -28,6 +29,12 @@ def _solve(lib, torch, k, v, noalloc):
             x.data_ptr(), khat.data_ptr(), u.data_ptr(), rstd.data_ptr(), dinv.data_ptr())
     if noalloc:
         rc = lib.lucid_solve_fwd_noalloc(*args, st)
+        assert rc == 0
+        # the call's run-time status word, kept in the static array until the next call
+        word = torch.full((1,), -1, dtype=torch.int32, pin_memory=True)
+        assert lib.lucid_solve_fwd_noalloc_status(word.data_ptr(), st) == 0
+        torch.cuda.synchronize()
+        assert int(word[0]) == 0
     else:
         ws = torch.empty(lib.lucid_solve_fwd_workspace_bytes(B, H, N, D), dtype=torch.uint8, device=dev)
         rc = lib.lucid_solve_fwd(*args, ws.data_ptr(), ws.numel(), st)
@@ -48,8 +55,9 @@ def test_noalloc_solve_matches_workspace_solve_on_consecutive_calls(cuda_device)
         x_ref, d_ref = _solve(lib, torch, k, v, noalloc=False)
         x_na, d_na = _solve(lib, torch, k, v, noalloc=True)
         assert np.all(np.isfinite(x_na))
-        # same kernels on the same inputs: the bf16 tolerance of the other tests is met exactly
+        # the bf16 tolerance of the other tests, and (same kernels, same inputs) equality
         assert np.max(np.abs(x_na - x_ref) - (1e-2 + 2.0 ** -8 * np.abs(x_ref))) <= 0
+        np.testing.assert_array_equal(x_na, x_ref)
         np.testing.assert_array_equal(d_na, d_ref)
 
 
