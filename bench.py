@@ -13,9 +13,12 @@ K, V, dO ~ N(0,1) (seeded synthetic data, per rank).  Every input tensor is
 Algorithmic FLOPs per (batch, head): 14 N^2 D
   attention fwd 2 N^2 D + bwd 5 N^2 D, LUCID solve fwd 2 N^2 D + bwd 5 N^2 D.
 
-Multi-GPU (torchrun): (batch, head) sharding with no data-path collective;
-every rank runs its own batch element (weak scaling); the step time is the
-max over ranks.
+Multi-GPU (torchrun): the workload is the whole job and is split, not
+replicated: rank r of W takes the contiguous (batch, kv head) pairs
+[r B Hkv / W, (r + 1) B Hkv / W) (all query heads of those kv heads), with no
+data-path collective; the step time is the max over ranks and `value` the whole
+job's algorithmic work over it (strong scaling).  Every (batch, head) slice is
+drawn from its own seeded generator, so the data do not depend on the GPU count.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -194,13 +197,14 @@ def reference_arm(args):
     for _ in range(args.warmup):
         cpu_reference_sample(n_cpu, D)
     times = [cpu_reference_sample(n_cpu, D, seed=i) for i in range(args.steps)]
-    t = sum(times) / len(times)
+    t = statistics.median(times)
     val = flops_per_step(1, 1, n_cpu, D) / t / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"LUCID attention fwd+bwd B{B} {heads} N{N} D{D} (sampled: 1 head at N={n_cpu})",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"LUCID attention fwd+bwd B{B} {heads} N{N} D{D} causal (whole job; sampled: "
+                               f"1 head at N={n_cpu})",
                    "global_batch": B, "seq_len": N, "parallelism": "cpu"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"1 (batch, head) at N={n_cpu}, D={D}, fp32, oracle/torch_ref.py"},
@@ -235,13 +239,13 @@ def path_reference_arm(args):
     for _ in range(args.warmup):
         path_cpu_sample(n_cpu)
     times = [path_cpu_sample(n_cpu, seed=i) for i in range(args.steps)]
-    t = sum(times) / len(times)
+    t = statistics.median(times)
     val = 14.0 * n_cpu * n_cpu * K / t / 1e12
     line = {
         "impl": "reference", "metric": PATH_METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"LUCID-Path fwd+bwd B{B} H{H} T{T} K{K} (sampled: 1 head at T={n_cpu})",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"LUCID-Path fwd+bwd B{B} H{H} T{T} K{K} (whole job; sampled: 1 head at T={n_cpu})",
                    "global_batch": B, "seq_len": T, "parallelism": "cpu"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"1 (batch, head) at T={n_cpu}, float64 numpy, oracle/path_oracle.py"},
@@ -256,16 +260,23 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
     from lucid_b200 import _lib
     from lucid_b200.path import parallel_lucid_path_attention, path_bwd, path_fwd
     lib = _lib.load()
-    B, H, T, K = PATH_CONFIG
+    Bg, Hg, T, K = PATH_CONFIG
     if args.path_seq:   # a shorter sequence (profiling cases); the metric is quoted at T = 16384
         T = args.path_seq
-    g = torch.Generator(device=dev).manual_seed(3000 + rank)
-    k = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
-    v = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16().requires_grad_(True)
-    w = torch.nn.functional.normalize(torch.randn(B, T, H, K, generator=g, device=dev), dim=-1).bfloat16()
-    w.requires_grad_(True)
-    beta = (2 * torch.sigmoid(torch.randn(B, T, H, generator=g, device=dev))).bfloat16().requires_grad_(True)
-    do = torch.randn(B, T, H, K, generator=g, device=dev).bfloat16()
+    b0, B, h0, H = shard(Bg, Hg, world, rank)
+    k, v, w, do = (torch.empty(B, T, H, K, dtype=torch.bfloat16, device=dev) for _ in range(4))
+    beta = torch.empty(B, T, H, dtype=torch.bfloat16, device=dev)
+    for bi in range(B):
+        for hi in range(H):
+            # every (batch, head) slice from its own generator: independent of the GPU count
+            g = torch.Generator(device=dev).manual_seed(3000 + 8 * ((b0 + bi) * 4096 + h0 + hi))
+            k[bi, :, hi] = torch.randn(T, K, generator=g, device=dev).bfloat16()
+            v[bi, :, hi] = torch.randn(T, K, generator=g, device=dev).bfloat16()
+            w[bi, :, hi] = torch.nn.functional.normalize(torch.randn(T, K, generator=g, device=dev), dim=-1).bfloat16()
+            beta[bi, :, hi] = (2 * torch.sigmoid(torch.randn(T, generator=g, device=dev))).bfloat16()
+            do[bi, :, hi] = torch.randn(T, K, generator=g, device=dev).bfloat16()
+    for t in (k, v, w, beta):
+        t.requires_grad_(True)
 
     def step():
         k.grad = v.grad = w.grad = beta.grad = None
@@ -292,7 +303,7 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    fl = 14.0 * T * T * K * B * H * world
+    fl = 14.0 * T * T * K * Bg * Hg      # the whole job's work, fixed as the GPU count grows
     tflops = fl / (ms * 1e-3) / 1e12
 
     # ---- per kernel family (profile hook), dominant kernel -> roofline ----
@@ -400,14 +411,15 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
     launches = sum(stage_n.values()) - 1 + 4
     line = {
         "metric": PATH_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"LUCID-Path fwd+bwd B{B} H{H} T{T} K{K} per GPU, q = k",
-                   "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": K,
-                   "parallelism": f"(batch,head) shards x{world}, no collective",
+        "config": {"workload": f"LUCID-Path fwd+bwd B{Bg} H{Hg} T{T} K{K} (whole job), q = k",
+                   "global_batch": Bg, "seq_len": T, "heads": Hg, "head_dim": K,
+                   "parallelism": f"(batch, head) shards: {B * H} of {Bg * Hg} pairs per rank x{world}, "
+                                  f"no collective",
                    "l2": "inputs and path tiles larger than L2, no flush"},
-        "tokens_per_s": B * T * world / (ms * 1e-3),
-        "frac_of_bf16_peak": tflops / pk_sust,
+        "tokens_per_s": Bg * T / (ms * 1e-3),
+        "frac_of_bf16_peak": tflops / (pk_sust * world),
         "stage": stage, "stage_ms": stage_ms, "roofline": roof, "clocks": clk,
         "gpu_launches": launches * args.steps, "e2e": e2e, "cpu_baseline": cpu,
     }
@@ -917,65 +929,114 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def main(argv=None):
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill", "decode"], default="32k")
-    ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
-    ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
-    ap.add_argument("--path-seq", type=int, default=0,
-                    help="path: sequence length instead of config 3's 16384 (smaller profiling cases)")
-    ap.add_argument("--cp-layout", choices=["auto", "zigzag", "contiguous"], default="auto",
-                    help="cp128k: rows per rank (zigzag: segments r and 2W-1-r; contiguous: one chunk; "
-                         "auto: contiguous below 4 ranks, where its balanced chunks are as good, else zigzag)")
-    ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
-    ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args(argv)
-    if args.impl == "reference":
-        return reference_arm(args)
+# ---------------------------------------------------------------------------
+# LUCID attention (the metric's configuration and config 2)
+# ---------------------------------------------------------------------------
+def shard(B, Hkv, world, rank):
+    """(batch, kv head) pairs of a B x Hkv workload split into `world` contiguous equal
+    shards (GPU g gets pairs [g B Hkv / W, (g + 1) B Hkv / W)).  Returns (b0, nb, kv0, nkv):
+    rank `rank` owns batch elements [b0, b0 + nb) x kv heads [kv0, kv0 + nkv) (with all
+    query heads of those kv heads).  Raises ValueError when the pairs do not split into
+    such rectangles."""
+    pairs = B * Hkv
+    if world < 1 or pairs % world:
+        raise ValueError(f"{pairs} (batch, kv head) pairs do not split over {world} ranks")
+    per = pairs // world
+    start = rank * per
+    if per % Hkv == 0:
+        return start // Hkv, per // Hkv, 0, Hkv
+    if Hkv % per == 0:
+        return start // Hkv, 1, start % Hkv, per
+    raise ValueError(f"{per} pairs per rank do not tile batch x {Hkv} kv heads")
 
-    import torch
-    import torch.distributed as dist
 
+def shard_inputs(torch, dev, B0, nb, kv0, nkv, G, N, D, qs, seed=1000):
+    """This rank's slice of the global inputs: every (batch, head) slice is drawn from its
+    own generator seeded by its global index, so the data do not depend on the GPU count."""
+    def head(seed_, sc=1.0):
+        g = torch.Generator(device=dev).manual_seed(seed_)
+        return (torch.randn(N, D, generator=g, device=dev) * sc).to(torch.bfloat16)
+    q = torch.empty(nb, nkv * G, N, D, dtype=torch.bfloat16, device=dev)
+    do = torch.empty(nb, N, nkv * G, D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(nb, nkv, N, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(nb, nkv, N, D, dtype=torch.bfloat16, device=dev)
+    for bi in range(nb):
+        b = B0 + bi
+        for hi in range(nkv):
+            kvh = kv0 + hi
+            k[bi, hi] = head(seed + 4 * (b * 4096 + kvh))
+            v[bi, hi] = head(seed + 4 * (b * 4096 + kvh) + 1)
+            for gi in range(G):
+                hq = kvh * G + gi
+                q[bi, hi * G + gi] = head(seed + 4 * (b * 4096 + hq) + 2, qs)
+                do[bi, :, hi * G + gi] = head(seed + 4 * (b * 4096 + hq) + 3)
+    return q, k, v, do
+
+
+def pipelined_e2e(torch, dev, steps, h_in, make_outs, run):
+    """End-to-end time per step through the public API with host buffers: every step
+    copies its inputs from pinned host memory (h_in) to the device, runs `run(*inputs)`
+    (returning the device results) and copies the results back into pinned host memory.
+    Copies in, compute and copies out run on three streams, double-buffered, so step i's
+    compute overlaps the copies of steps i - 1 and i + 1.  Returns ms per step (device
+    events from the first copy in to the last copy out)."""
+    comp = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    d_in = [[torch.empty_like(t, device=dev) for t in h_in] for _ in range(2)]
+    h_out = [make_outs() for _ in range(2)]
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def copy_in(i):
+        s = i & 1
+        with torch.cuda.stream(h2d):
+            if i >= 2:
+                h2d.wait_event(in_free[s])       # step i - 2 is done with these buffers
+            for d, h in zip(d_in[s], h_in):
+                d.copy_(h, non_blocking=True)
+            in_ready[s].record(h2d)
+
+    torch.cuda.synchronize()
+    t0.record(h2d)
+    copy_in(0)
+    for i in range(steps):
+        s = i & 1
+        if i + 1 < steps:
+            copy_in(i + 1)
+        comp.wait_event(in_ready[s])
+        outs = run(*d_in[s])
+        in_free[s].record(comp)
+        out_ready[s].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(out_ready[s])
+            if i >= 2:
+                d2h.wait_event(out_free[s])
+            for h, t in zip(h_out[s], outs):
+                t.record_stream(d2h)
+                h.copy_(t.detach(), non_blocking=True)
+            out_free[s].record(d2h)
+        del outs
+    t1.record(d2h)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
     from lucid_b200 import _lib, attn_bwd, attn_fwd, lucid_attention, solve_bwd, solve_fwd
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        # a short timeout ends a stuck collective with an error instead of holding all GPUs
-        dist.init_process_group("nccl", timeout=timedelta(seconds=60 if args.config == "cp128k" else 300),
-                                device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    if args.config == "path":
-        return bench_path(args, torch, dist, dev, world, rank, local, barrier)
-    if args.config == "cp128k":
-        return bench_cp(args, torch, dist, dev, world, rank, local, barrier)
-    if args.config == "prefill":
-        return bench_prefill(args, torch, dist, dev, world, rank, local, barrier)
-    if args.config == "decode":
-        return bench_decode(args, torch, dist, dev, world, rank, local, barrier)
     lib = _lib.load()
-    B, H, N, D, qs = CONFIGS[args.config]
-    Hkv = KV_HEADS.get(args.config, H)
+    Bg, Hg, N, D, qs = CONFIGS[args.config]
+    Hkvg = KV_HEADS.get(args.config, Hg)
+    G = Hg // Hkvg
+    b0, B, kv0, Hkv = shard(Bg, Hkvg, world, rank)
+    H = Hkv * G
     s = D ** -0.5
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    mk = lambda *shape, sc=1.0: (torch.randn(*shape, generator=g, device=dev) * sc).to(torch.bfloat16)
-    q = mk(B, H, N, D, sc=qs).requires_grad_(True)
-    k = mk(B, Hkv, N, D).requires_grad_(True)
-    v = mk(B, Hkv, N, D).requires_grad_(True)
-    do = mk(B, N, H, D)
+    q, k, v, do = shard_inputs(torch, dev, b0, B, kv0, Hkv, G, N, D, qs)
+    q.requires_grad_(True)
+    k.requires_grad_(True)
+    v.requires_grad_(True)
 
     def step():
         q.grad = k.grad = v.grad = None
@@ -985,6 +1046,7 @@ def main(argv=None):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    _lib.check_status()
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
@@ -997,15 +1059,17 @@ def main(argv=None):
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1) / args.steps
+    _lib.check_status()
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = ms_local
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    fl = flops_per_step(B, H, N, D, Hkv) * world
+    fl = flops_per_step(Bg, Hg, N, D, Hkvg)          # the whole job's work, fixed as N grows
     tflops = fl / (ms * 1e-3) / 1e12
 
-    # ---- per-kernel timing (dominant kernel -> roofline) ----
+    # ---- per-kernel timing on this rank's shard (dominant kernel -> roofline) ----
     pk_burst, pk_sust, hbm, pk_kind = peaks()
     per_stage_flops = stage_units(H, Hkv)
     # the stored-tile schedule (chosen by the ops when its workspace fits) streams the
@@ -1047,7 +1111,7 @@ def main(argv=None):
     achieved = stage_tflops[dom]["alg"]
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
+    if os.path.exists(tpath) and world == 1:
         try:
             with open(tpath) as f:
                 tj = json.load(f)
@@ -1056,71 +1120,51 @@ def main(argv=None):
             traffic = None
 
     # ---- causal attention of the same shape (overhead reference) ----
-    import torch.nn.functional as F
-    qd, kd, vd = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
-    dot = do.transpose(1, 2)
-    def sdpa_step():
-        qd.grad = kd.grad = vd.grad = None
-        F.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=s,
-                                       enable_gqa=Hkv != H).backward(dot)
-    for _ in range(2):
-        sdpa_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(3):
-        sdpa_step()
-    e1.record()
-    torch.cuda.synchronize()
-    sdpa_ms = e0.elapsed_time(e1) / 3
+    sdpa_ms = sdpa_fwd_bwd_ms(torch, q, k, v, do, s)
     our_attn_ms = stage_ms["attn_fwd"] + stage_ms["attn_bwd"] + stage_ms["attn_bwd_row"]
-    del qd, kd, vd
 
     # ---- end to end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
-        hq = q.detach().cpu().pin_memory()
-        hk = k.detach().cpu().pin_memory()
-        hv = v.detach().cpu().pin_memory()
-        hdo = do.cpu().pin_memory()
-        outs = [torch.empty(B, N, H, D, dtype=torch.bfloat16).pin_memory(),
-                torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory()] + \
-               [torch.empty(B, Hkv, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        h_in = [t.detach().cpu().pin_memory() for t in (q, k, v, do)]
 
-        def e2e_step():
-            qq = hq.to(dev, non_blocking=True).requires_grad_(True)
-            kk = hk.to(dev, non_blocking=True).requires_grad_(True)
-            vv = hv.to(dev, non_blocking=True).requires_grad_(True)
-            dd = hdo.to(dev, non_blocking=True)
+        def make_outs():
+            return [torch.empty(B, N, H, D, dtype=torch.bfloat16).pin_memory(),
+                    torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory()] + \
+                   [torch.empty(B, Hkv, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+
+        def run(qq, kk, vv, dd):
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (qq, kk, vv))
             oo = lucid_attention(qq, kk, vv, s)
             oo.backward(dd)
-            for h, t in zip(outs, (oo, qq.grad, kk.grad, vv.grad)):
-                h.copy_(t.detach(), non_blocking=True)
+            return oo, qq.grad, kk.grad, vv.grad
 
-        e2e_step()
-        torch.cuda.synchronize()
+        pipelined_e2e(torch, dev, 2, h_in, make_outs, run)      # warm-up
         barrier()
-        ne = max(1, min(args.steps, 3))
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record()
-        for _ in range(ne):
-            e2e_step()
-        a1.record()
-        torch.cuda.synchronize()
+        ems = pipelined_e2e(torch, dev, max(2, min(args.steps, 6)), h_in, make_outs, run)
         barrier()
-        ems = a0.elapsed_time(a1) / ne
+        _lib.check_status()
         if world > 1:
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = float(t.item())
-        # q, dO (o, dq) per query head; k, v (dk, dv) per kv head
+        # q, dO (o, dq) per query head; k, v (dk, dv) per kv head: this rank's bytes
         nbytes = 2 * B * N * D * 2 * (H + Hkv)
         e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
-               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes}
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+               "schedule": "copies in / compute / copies out on three streams, double-buffered"}
+        del h_in
+
+    # ---- the grouped-query layout of the reference model (Hq 32, Hkv 4) beside it ----
+    gqa = None
+    if world == 1 and args.config == "32k" and not args.no_gqa:
+        del q, k, v, do
+        torch.cuda.empty_cache()
+        gqa = gqa_overhead(torch, dev, lucid_attention, _lib, N, D, qs)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(args.cpu_n, D)
+        cpu = cpu_baseline(args.cpu_n, D, reps=10)
 
     if world > 1:
         dist.barrier()
@@ -1129,6 +1173,7 @@ def main(argv=None):
         return 0
     # prep, solve, attn fwd, delta, attn bwd col + row, solve bwd col + row, finalize
     launches_per_step = 9
+    heads = f"H{Hg}" if Hkvg == Hg else f"Hq{Hg} Hkv{Hkvg}"
     line = {
         "metric": METRIC,
         "value": tflops,
@@ -1138,21 +1183,26 @@ def main(argv=None):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"LUCID attention fwd+bwd B{B} H{H} N{N} D{D} causal MHA per GPU" if Hkv == H else
-                               f"LUCID attention fwd+bwd B{B} Hq{H} Hkv{Hkv} N{N} D{D} causal GQA per GPU",
-                   "global_batch": B * world, "seq_len": N, "heads": H, "kv_heads": Hkv, "head_dim": D,
-                   "parallelism": f"(batch,head) shards x{world}, no collective",
-                   "l2": "inputs larger than L2 (268 MB per tensor), no flush"},
-        "tokens_per_s": B * N * world / (ms * 1e-3),
-        "frac_of_bf16_peak": tflops / pk_sust,
-        "peak_used": {"bf16_tflops_sustained": pk_sust, "bf16_tflops_burst": pk_burst, "kind": pk_kind},
-        "overhead_vs_causal_attn": {"sdpa_fwd_bwd_ms": sdpa_ms, "lucid_fwd_bwd_ms": ms,
-                                    "ratio_vs_sdpa": ms / sdpa_ms, "our_attention_only_ms": our_attn_ms,
-                                    "ratio_vs_our_attention": ms / our_attn_ms},
+        "config": {"workload": f"LUCID attention fwd+bwd B{Bg} {heads} N{N} D{D} causal "
+                               f"{'MHA' if Hkvg == Hg else 'GQA'} (whole job)",
+                   "global_batch": Bg, "seq_len": N, "heads": Hg, "kv_heads": Hkvg, "head_dim": D,
+                   "parallelism": f"(batch, kv head) shards: {B * Hkv} of {Bg * Hkvg} pairs per rank x{world}, "
+                                  f"no collective",
+                   "l2": "inputs larger than L2 (268 MB per tensor at one GPU), no flush"},
+        "tokens_per_s": Bg * N / (ms * 1e-3),
+        "frac_of_bf16_peak": tflops / (pk_sust * world),
+        "peak_used": {"bf16_tflops_sustained": pk_sust, "bf16_tflops_burst": pk_burst, "kind": pk_kind,
+                      "note": "frac_of_bf16_peak divides by the peak of all GPUs of the run"},
+        "rank0_ms_per_step": ms_local,
+        "overhead_vs_causal_attn": {"sdpa_fwd_bwd_ms": sdpa_ms, "lucid_fwd_bwd_ms": ms_local,
+                                    "ratio_vs_sdpa": ms_local / sdpa_ms, "our_attention_only_ms": our_attn_ms,
+                                    "ratio_vs_our_attention": ms_local / our_attn_ms,
+                                    "shape": f"rank 0 shard B{B} Hq{H} Hkv{Hkv} N{N}"},
+        "gqa_overhead_vs_causal_attn": gqa,
         "stage_ms": stage_ms,
         "stage_tflops": stage_tflops,
         "backward_schedule": "stored tiles" if stored else "recompute",
@@ -1167,6 +1217,108 @@ def main(argv=None):
     print(json.dumps(line), flush=True)
     return 0
 
+
+def sdpa_fwd_bwd_ms(torch, q, k, v, do, s, reps=3):
+    """PyTorch SDPA (cuDNN on B200) causal fwd+bwd of the same shape, ms per step."""
+    import torch.nn.functional as F
+    G = q.shape[1] // k.shape[1]
+    qd, kd, vd = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    dot = do.transpose(1, 2)
+
+    def sdpa_step():
+        qd.grad = kd.grad = vd.grad = None
+        F.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=s, enable_gqa=G > 1).backward(dot)
+    for _ in range(2):
+        sdpa_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        sdpa_step()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gqa_overhead(torch, dev, lucid_attention, _lib, N, D, qs, Hq=32, Hkv=4, reps=3):
+    """LUCID fwd+bwd against causal SDPA fwd+bwd at the reference model's grouped-query
+    layout (Hq 32 query heads over Hkv 4 kv heads, modeling_lucid.py:523-524), B1 N D."""
+    q, k, v, do = shard_inputs(torch, dev, 0, 1, 0, Hkv, Hq // Hkv, N, D, qs, seed=5000)
+    q.requires_grad_(True)
+    k.requires_grad_(True)
+    v.requires_grad_(True)
+    s = D ** -0.5
+
+    def step():
+        q.grad = k.grad = v.grad = None
+        lucid_attention(q, k, v, s).backward(do)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    _lib.check_status()
+    ms = e0.elapsed_time(e1) / reps
+    sdpa = sdpa_fwd_bwd_ms(torch, q, k, v, do, s, reps)
+    fl = flops_per_step(1, Hq, N, D, Hkv)
+    return {"shape": f"B1 Hq{Hq} Hkv{Hkv} N{N} D{D}", "lucid_fwd_bwd_ms": ms, "sdpa_fwd_bwd_ms": sdpa,
+            "ratio_vs_sdpa": ms / sdpa, "lucid_tflops": fl / (ms * 1e-3) / 1e12,
+            "arithmetic_ratio": (Hq + Hkv) / Hq}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["path", "cp128k", "prefill", "decode"], default="32k")
+    ap.add_argument("--head-groups", type=int, default=8, help="cp128k: kv-head groups pipelined across ranks")
+    ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
+    ap.add_argument("--path-seq", type=int, default=0,
+                    help="path: sequence length instead of config 3's 16384 (smaller profiling cases)")
+    ap.add_argument("--cp-layout", choices=["auto", "zigzag", "contiguous"], default="auto",
+                    help="cp128k: rows per rank (zigzag: segments r and 2W-1-r; contiguous: one chunk; "
+                         "auto: contiguous below 4 ranks, where its balanced chunks are as good, else zigzag)")
+    ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-gqa", action="store_true", help="skip the grouped-query overhead measurement")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        # a short timeout ends a stuck collective with an error instead of holding all GPUs
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60 if args.config == "cp128k" else 300),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    if args.config == "path":
+        return bench_path(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "cp128k":
+        return bench_cp(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "prefill":
+        return bench_prefill(args, torch, dist, dev, world, rank, local, barrier)
+    if args.config == "decode":
+        return bench_decode(args, torch, dist, dev, world, rank, local, barrier)
+    return bench_lucid(args, torch, dist, dev, world, rank, local, barrier)
 
 if __name__ == "__main__":
     sys.exit(main())

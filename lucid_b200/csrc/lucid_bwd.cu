@@ -72,8 +72,8 @@ constexpr uint32_t kOffDS = 196608;          // R / dV / dG^T tile of the diagon
 constexpr uint32_t kOffVec = 229376;         // stage s: lse[128], delta[128] at +s*1024
 constexpr uint32_t kOffBar = kOffVec + 2048;
 enum {
-  A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_READ, PD_FULL, DS_FREE,
-  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, STG_READY, STG_FREE, NBAR
+  A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_FULL, PD_FULL, DS_FREE,
+  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, STG_READY, STG_FREE, DSP_FULL, NBAR
 };
 constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {  // the tile layout needs a 1024-byte aligned window
-    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | ((SOLVE ? 1 : 0) << 20));
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
     return;
   }
   if (threadIdx.x == kBwdWarpTma * 32) {
@@ -110,8 +110,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(bar(KV_EMPTY0 + s2), 1);
     }
     mbar_init(bar(SD_FULL), 1);
-    mbar_init(bar(DP_READ), kBwdEpiThreads);
+    mbar_init(bar(DP_FULL), 1);
     mbar_init(bar(PD_FULL), kBwdEpiThreads);
+    mbar_init(bar(DSP_FULL), kBwdEpiThreads);
     mbar_init(bar(DS_FREE), 1);
     mbar_init(bar(T_FULL), 1);
     mbar_init(bar(S_FREE), kBwdEpiThreads);
@@ -224,9 +225,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == kBwdWarpMma) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      Ph a_full, dp_read, pd_full, acc_free, s_free;
+      Ph a_full, pd_full, dsp_full, acc_free, s_free;
       uint32_t n_kv = 0;
-      bool pending_dp_read = false;  // a dP read whose release the next dP write must await
       bool first_item = true;
       const uint32_t tS = tmem + kTmS, tDP = tmem + kTmDP;
       for (int idx = blockIdx.x; idx < total; idx += gridDim.x) {
@@ -239,40 +239,46 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (SOLVE && !first_item && !mbar_wait(bar(S_FREE), s_free.full(), ab)) break;
         first_item = false;
         bool ok = true;
-        // tile t: dP(t) = A2 B2^T is issued as soon as dP(t-1) was read by the
-        // epilogue (P / dS live in the S region); S(t) = A1 B1^T after the
-        // GEMMs that read P(t-1) / dS(t-1).
+        // tile t: S(t) = A1 B1^T (SD_FULL) and dP(t) = A2 B2^T (DP_FULL).  The epilogue
+        // packs P(t) into the S region (PD_FULL), then dS(t) into the dP region
+        // (DSP_FULL).  acc1 += P B2 and S(t+1) follow P(t); acc2 += dS B1 and dP(t+1)
+        // follow dS(t), so the epilogue computes P(t+1) while the tensor core runs
+        // acc2(t) and dP(t+1).  A region's next write is issued after the GEMM that
+        // reads its packed operand (the MMAs of one issuer run in order) and after the
+        // epilogue arrival that ends the epilogue's reads of it.
         if (T > 0) {
           const int st = n_kv & 1;
           if (!mbar_wait(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) break;
-          if (pending_dp_read && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) break;
           tc_fence_after();
-          umma_tile(tDP, sA2, false, sB2(st), false, 0u);
           umma_tile(tS, sA1, false, sB1(st), false, 0u);
           umma_commit(bar(SD_FULL));
-          pending_dp_read = true;
+          umma_tile(tDP, sA2, false, sB2(st), false, 0u);
+          umma_commit(bar(DP_FULL));
         }
         for (int t = 0; t < T; ++t, ++n_kv) {
           const int st = n_kv & 1;
           const int st2 = (n_kv + 1) & 1;
           const bool has_next = t + 1 < T;
-          if (has_next) {
-            if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab) ||
-                !mbar_wait(bar(DP_READ), dp_read.full(), ab)) { ok = false; break; }
-            tc_fence_after();
-            umma_tile(tDP, sA2, false, sB2(st2), false, 0u);  // dP(t+1)
-          }
           if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab)) { ok = false; break; }
           if (t == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
           tc_fence_after();
           const uint32_t acc = t > 0 ? 1u : 0u;
-          // acc1 += P B2, acc2 += dS B1 (P, dS packed in the S region)
+          // acc1 += P B2 (P packed in the S region), then S(t+1) over it
           umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk); }, sB2(st), true, acc);
-          umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tS, kk) + 16u; }, sB1(st), true, acc);
-          umma_commit(bar(KV_EMPTY0 + st));
           if (has_next) {
+            if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab)) { ok = false; break; }
+            tc_fence_after();
             umma_tile(tS, sA1, false, sB1(st2), false, 0u);    // S(t+1)
             umma_commit(bar(SD_FULL));
+          }
+          // acc2 += dS B1 (dS packed in the dP region), then dP(t+1) over it
+          if (!mbar_wait(bar(DSP_FULL), dsp_full.full(), ab)) { ok = false; break; }
+          tc_fence_after();
+          umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tDP, kk); }, sB1(st), true, acc);
+          umma_commit(bar(KV_EMPTY0 + st));
+          if (has_next) {
+            umma_tile(tDP, sA2, false, sB2(st2), false, 0u);  // dP(t+1)
+            umma_commit(bar(DP_FULL));
           }
         }
         if (!ok) break;
@@ -293,9 +299,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(bar(DS_FREE));
         umma_commit(bar(KV_EMPTY0 + st));
         // D4: S' = K^_i K^_i^T ; D' = X_i dV_i^T
+        // (the last tile's readers of the dP region: the epilogue, done at its DSP_FULL,
+        // and acc2, issued earlier)
         if (!mbar_wait(bar(PD_FULL), pd_full.full(), ab) || !mbar_wait(bar(S_FREE), s_free.full(), ab)) break;
-        if (pending_dp_read && T > 0 && !mbar_wait(bar(DP_READ), dp_read.full(), ab)) break;
-        pending_dp_read = false;
         tc_fence_after();
         umma_tile(tS, sA1, false, sA1, false, 0u);
         umma_tile(tDP, sA2, false, sDS, false, 0u);
@@ -355,7 +361,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const float kLog2e = 1.4426950408889634f;
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
-    Ph sd_full, ds_free, t_full, acc_full, acc2_full;
+    Ph sd_full, dp_full, ds_free, t_full, acc_full, acc2_full;
     uint32_t n_kv = 0, item = 0;
     // stored-tile schedule: every packed dS^T (attention) / dG^T (solve) tile also goes
     // to global memory through the sDS tile, stored by warp kBwdWarpStore.  n_st counts
@@ -379,17 +385,61 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!SOLVE && !warp_wait_b(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) { ok = false; break; }
         if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
-        float dv[2][32], sv[2][32];
-        tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
-        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
-        tmem_ld32(tmem + lane_base + kTmS + c0, sv[0]);
-        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u, sv[1]);
+        // phase 1: P (attention) / E (solve) from S alone, packed into the S region
+        float pv[2][32];
+        tmem_ld32(tmem + lane_base + kTmS + c0, pv[0]);
+        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u, pv[1]);
         tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(bar(DP_READ));
         const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
         const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
                                 : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int cb = (int)c0 + 32 * q;
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 ls4;
+            if (!SOLVE) ls4 = *reinterpret_cast<const float4*>(vec + cb + e);
+#pragma unroll
+            for (int hh = 0; hh < 4; hh += 2) {
+              const int c = cb + e + hh;
+              float2 arg, pe;
+              if (SOLVE) {
+                arg = fma2(make_float2(pv[q][e + hh], pv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+                if (!full) {
+                  if (j * 128 + c >= p.N) pe.x = 0.f;
+                  if (j * 128 + c + 1 >= p.N) pe.y = 0.f;
+                }
+              } else {
+                const float2 ls = hh == 0 ? make_float2(ls4.x, ls4.y) : make_float2(ls4.z, ls4.w);
+                arg = fma2(make_float2(pv[q][e + hh], pv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-ls.x, -ls.y));
+                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+                if (!full) {
+                  const int q0 = j * 128 + c;
+                  if (!(q0 < p.N && row_i < p.N && q0 >= row_i)) pe.x = 0.f;
+                  if (!(q0 + 1 < p.N && row_i < p.N && q0 + 1 >= row_i)) pe.y = 0.f;
+                }
+              }
+              pv[q][e + hh] = pe.x;
+              pv[q][e + hh + 1] = pe.y;
+              pk[(e + hh) >> 1] = pack_bf16(pe.x, pe.y);
+            }
+          }
+          tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(PD_FULL));
+        // phase 2: dS (attention) / dG^T (solve) from dP and the P kept in registers,
+        // packed into the dP region (and staged for the tile store)
+        if (!warp_wait_b(bar(DP_FULL), dp_full.full(), ab)) { ok = false; break; }
+        tc_fence_after();
+        float dv[2][32];
+        tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
+        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        tmem_ld_wait();
         if (stage) {
           if (n_st > 0 && !warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) { ok = false; break; }
           if (SOLVE && t == 0 && !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) { ok = false; break; }
@@ -397,49 +447,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const int cb = (int)c0 + 32 * q;
-          uint32_t pk[16], dk[16];
+          uint32_t dk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            float4 ls4, dl4;
-            if (!SOLVE) {
-              ls4 = *reinterpret_cast<const float4*>(vec + cb + e);
-              dl4 = *reinterpret_cast<const float4*>(vec + 128 + cb + e);
-            }
+            float4 dl4;
+            if (!SOLVE) dl4 = *reinterpret_cast<const float4*>(vec + 128 + cb + e);
 #pragma unroll
             for (int hh = 0; hh < 4; hh += 2) {
-              const int c = cb + e + hh;
-              float2 arg, pe, ds;
+              const float2 pe = make_float2(pv[q][e + hh], pv[q][e + hh + 1]);
+              float2 ds;
               if (SOLVE) {
-                arg = fma2(make_float2(sv[q][e + hh], sv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
-                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
-                if (!full) {
-                  if (j * 128 + c >= p.N) pe.x = 0.f;
-                  if (j * 128 + c + 1 >= p.N) pe.y = 0.f;
-                }
                 ds = mul2(pe, mul2(make_float2(dv[q][e + hh], dv[q][e + hh + 1]), make_float2(-p.scale, -p.scale)));
               } else {
-                const float2 ls = hh == 0 ? make_float2(ls4.x, ls4.y) : make_float2(ls4.z, ls4.w);
                 const float2 dl = hh == 0 ? make_float2(dl4.x, dl4.y) : make_float2(dl4.z, dl4.w);
-                arg = fma2(make_float2(sv[q][e + hh], sv[q][e + hh + 1]), make_float2(c1, c1), make_float2(-ls.x, -ls.y));
-                pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
-                if (!full) {
-                  const int q0 = j * 128 + c;
-                  if (!(q0 < p.N && row_i < p.N && q0 >= row_i)) pe.x = 0.f;
-                  if (!(q0 + 1 < p.N && row_i < p.N && q0 + 1 >= row_i)) pe.y = 0.f;
-                }
                 ds = mul2(pe, add2(make_float2(dv[q][e + hh], dv[q][e + hh + 1]), make_float2(-dl.x, -dl.y)));
               }
-              pk[(e + hh) >> 1] = pack_bf16(pe.x, pe.y);
               dk[(e + hh) >> 1] = pack_bf16(ds.x, ds.y);
             }
           }
-          tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
-          tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q + 16u, dk);
+          tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q, dk);
           if (stage) tile_store_row32_packed(sDS, r, 2 * h + q, dk);
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(PD_FULL));
+        mbar_arrive(bar(DSP_FULL));
         if (stage) {
           fence_proxy_async_smem();
           mbar_arrive(bar(STG_READY));
@@ -617,7 +648,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   if ((sbase & 1023u) != 0) {
-    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | ((SOLVE ? 1 : 0) << 20));
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
     return;
   }
   if (threadIdx.x == kBwdWarpTma * 32) {
