@@ -393,6 +393,21 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
         e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
                "h2d_bytes_per_step": 4 * nb4 + B * T * H * 2, "d2h_bytes_per_step": 4 * nb4 + B * T * H * 2}
 
+    # ---- the reference Triton op on the same inputs, and both deviations from float64 ----
+    ref_gpu = None
+    if world == 1 and not args.no_ref_gpu:
+        lv = [t.detach().requires_grad_(True) for t in (k, v, w, beta)]
+        oo, _ = parallel_lucid_path_attention(*lv)
+        oo.backward(do)
+        ours = (oo.detach(), lv[0].grad, lv[1].grad, lv[2].grad, lv[3].grad)
+        torch.cuda.synchronize()
+        del lv, oo
+        torch.cuda.empty_cache()
+        ref_gpu = reference_gpu_bar(lambda rg: rg.triton_path(torch, k, v, w, beta, do, ours=ours,
+                                                              steps=max(1, min(args.steps, 3)),
+                                                              check=T <= 16384), ms)
+        del ours
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_cpu = min(args.cpu_n, 4096)
@@ -420,7 +435,7 @@ def bench_path(args, torch, dist, dev, world, rank, local, barrier):
                    "l2": "inputs and path tiles larger than L2, no flush"},
         "tokens_per_s": Bg * T / (ms * 1e-3),
         "frac_of_bf16_peak": tflops / (pk_sust * world),
-        "stage": stage, "stage_ms": stage_ms, "roofline": roof, "clocks": clk,
+        "stage": stage, "stage_ms": stage_ms, "roofline": roof, "clocks": clk, "reference_gpu": ref_gpu,
         "gpu_launches": launches * args.steps, "e2e": e2e, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
@@ -1081,15 +1096,15 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
     stage_ms = {}
     with torch.no_grad():
         x, khat, u, rstd, dinv = solve_fwd(k, v, s, 1e-5)
-        o, lse = attn_fwd(q, k, x, s)
-        dq, dkf, dxf = attn_bwd(q, k, x, o, do, lse, s)
+        o, lse, o_res = attn_fwd(q, k, x, s, residual=True)
+        dq, dkf, dxf = attn_bwd(q, k, x, o, do, lse, s, o_res=o_res)
         torch.cuda.synchronize()
         runs = {
             "prep": lambda: solve_fwd(k, v, s, 1e-5),
             "solve_fwd": lambda: solve_fwd(k, v, s, 1e-5),
-            "attn_fwd": lambda: attn_fwd(q, k, x, s),
-            "attn_bwd": lambda: attn_bwd(q, k, x, o, do, lse, s),
-            "attn_bwd_row": lambda: attn_bwd(q, k, x, o, do, lse, s),
+            "attn_fwd": lambda: attn_fwd(q, k, x, s, residual=True),
+            "attn_bwd": lambda: attn_bwd(q, k, x, o, do, lse, s, o_res=o_res),
+            "attn_bwd_row": lambda: attn_bwd(q, k, x, o, do, lse, s, o_res=o_res),
             "solve_bwd": lambda: solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf),
             "solve_bwd_row": lambda: solve_bwd(k, x, khat, u, rstd, dinv, dxf, s, dk_add=dkf),
         }
@@ -1155,6 +1170,12 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
                "schedule": "copies in / compute / copies out on three streams, double-buffered"}
         del h_in
 
+    # ---- the reference's own GPU path on the same inputs (config 2: it fits one GPU) ----
+    ref_gpu = None
+    if world == 1 and args.config == "cfg2" and not args.no_ref_gpu:
+        ref_gpu = reference_gpu_bar(lambda rg: rg.torch_path_cfg2(torch, q, k, v, do, ours_outputs(
+            torch, lucid_attention, q, k, v, do, s), steps=max(1, min(args.steps, 3))), ms)
+
     # ---- the grouped-query layout of the reference model (Hq 32, Hkv 4) beside it ----
     gqa = None
     if world == 1 and args.config == "32k" and not args.no_gqa:
@@ -1203,6 +1224,7 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
                                     "ratio_vs_our_attention": ms_local / our_attn_ms,
                                     "shape": f"rank 0 shard B{B} Hq{H} Hkv{Hkv} N{N}"},
         "gqa_overhead_vs_causal_attn": gqa,
+        "reference_gpu": ref_gpu,
         "stage_ms": stage_ms,
         "stage_tflops": stage_tflops,
         "backward_schedule": "stored tiles" if stored else "recompute",
@@ -1216,6 +1238,30 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def ours_outputs(torch, lucid_attention, q, k, v, do, s):
+    """(o, dq, dk, dv) of one fwd+bwd of our op on the benchmark's inputs."""
+    qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+    o = lucid_attention(qq, kk, vv, s)
+    o.backward(do)
+    return o.detach(), qq.grad, kk.grad, vv.grad
+
+
+def reference_gpu_bar(run, our_ms):
+    """Run one reference-GPU comparison (baseline/reference_gpu.py) and add our speed-up
+    over it; a missing or failing reference copy is reported, not fatal."""
+    import torch
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import reference_gpu as rg
+        out = run(rg)
+        out["our_speedup"] = out["ms_per_step"] / our_ms
+        return out
+    except Exception as e:   # the comparator is optional: report why it did not run
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
+    finally:
+        torch.cuda.empty_cache()
 
 
 def sdpa_fwd_bwd_ms(torch, q, k, v, do, s, reps=3):
@@ -1288,6 +1334,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-gqa", action="store_true", help="skip the grouped-query overhead measurement")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="cfg2 / path: skip timing the reference's own GPU code (baseline/_ref) beside ours")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)

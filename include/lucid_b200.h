@@ -176,7 +176,12 @@ int lucid_decode_step(int B, int Hq, int Hkv, int Ln, int Nc, int D, float scale
  *      x internal bf16 [B,Hkv,Npad,D].
  * Out: o strided [B,Hq,N,D] (pass the strides of the caller's output, e.g.
  *      the [B,N,Hq,D] layout the reference returns); lse internal fp32
- *      [B,Hq,Npad] (log2 domain, saved for the backward).
+ *      [B,Hq,Npad] (log2 domain, saved for the backward); o_res optional (NULL:
+ *      not written), a bf16 buffer with o's strides that receives the rounding
+ *      residual bf16(O - bf16(O)) of the fp32 output.  Passed on to lucid_attn_bwd
+ *      it makes the backward's rowsum(dO o O) use O to about 16 significant bits
+ *      instead of bf16's 8 (the dominant term of dQ's deviation from a float32
+ *      reference when attention is spread over many keys).
  */
 size_t lucid_attn_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
 int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
@@ -184,20 +189,22 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                    const void* x,
                    void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
-                   float* lse, void* workspace, size_t workspace_bytes, void* stream);
+                   float* lse, void* o_res, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Attention backward: what torch autograd derives for the SDPA call of
  * eager_lucid_attention_forward (modeling_lucid.py:505-549, causal, repeat_kv'd X),
  * with the grouped-query sums over the query heads of each kv head done in-kernel.
- * In : q, k, o, dout strided; x internal; lse from lucid_attn_fwd.
+ * In : q, k, o, dout strided; x internal; lse and (optional, may be NULL) o_res from
+ *      lucid_attn_fwd.
  * Out: dq strided bf16 [B,Hq,N,D];
  *      dk_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dK through Q K^T)
  *      dx_f32 internal fp32 [B,Hkv,Npad,D]  (dL/dX)
  */
 size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
 /* Workspace of the stored-tile schedule: with at least this many bytes the column pass
- * also stores every bf16 dS^T tile (B*Hq*ceil(N/128)*(ceil(N/128)+1)/2 tiles of 32 KB)
+ * also stores every bf16 dS^T tile (B*Hq*ceil(N/128)*(ceil(N/128)+1)/2 tiles of 32 KB,
+ * plus B*Hq*ceil(N/128) tiles holding the bf16 residual of the diagonal blocks' dS^T)
  * and the row pass streams them instead of recomputing S and dP; same results. */
 size_t lucid_attn_bwd_fast_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
 int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale,
@@ -206,7 +213,7 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale,
                    const void* x,
                    const void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                    const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn,
-                   const float* lse,
+                   const float* lse, const void* o_res,
                    void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn,
                    float* dk_f32, float* dx_f32,
                    void* workspace, size_t workspace_bytes, void* stream);
@@ -346,7 +353,8 @@ int lucid_cp_solve_fwd(int B, int H, int N, int D, float scale, int blk_lo, int 
 int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
                       const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
                       const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x,
-                      void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse, int* status, void* stream);
+                      void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse, void* o_res, int* status,
+                      void* stream);
 
 /*
  * Context-parallel backward (same chunking; the backward of lucid_attn_fwd /
@@ -357,7 +365,8 @@ int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk
  * received), the row passes its own row blocks over all earlier columns.
  *   lucid_cp_delta      delta = rowsum(dO o O) of rows [row_lo, row_hi) into the
  *                       internal [B*Hq][Npad] fp32 layout (o / dout indexed by
- *                       global row)
+ *                       global row; o_res, o's rounding residual from
+ *                       lucid_cp_attn_fwd with o's strides, may be NULL)
  *   lucid_cp_attn_bwd   passes & 1: column pass of column blocks [blk_lo, blk_hi)
  *                       (dk_f32, dx_f32 internal fp32); passes & 2: row pass of
  *                       row blocks [blk_lo, blk_hi) (dq, indexed by global row)
@@ -371,8 +380,8 @@ int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk
  * Same block-range, max_ctas and no-cross-launch-wait rules as the forward blocks.
  */
 int lucid_cp_delta(int B, int Hq, int N, int D, int row_lo, int row_hi, const void* o, int64_t o_sb, int64_t o_sh,
-                   int64_t o_sn, const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, float* delta,
-                   void* stream);
+                   int64_t o_sn, const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn,
+                   const void* o_res, float* delta, void* stream);
 int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi, int max_ctas,
                       int passes, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
                       const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x,

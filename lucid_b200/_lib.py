@@ -44,11 +44,11 @@ SIGNATURES = {
     "lucid_solve_fwd_noalloc_status": (c_int, [c_void_p, c_void_p]),
     "lucid_attn_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_fwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
-                       + [c_void_p] + S3 + [c_void_p] + [c_void_p, c_size_t, c_void_p]),
+                       + [c_void_p] + S3 + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),
     "lucid_attn_bwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_bwd_fast_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_bwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
-                       + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p] + [c_void_p] + S3
+                       + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_void_p] + [c_void_p] + S3
                        + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),
     "lucid_solve_bwd_workspace_bytes": (c_size_t, [c_int] * 4),
     "lucid_solve_bwd_fast_workspace_bytes": (c_size_t, [c_int] * 4),
@@ -80,8 +80,8 @@ SIGNATURES = {
     "lucid_cp_solve_fwd": (c_int, [c_int] * 4 + [c_float, c_int, c_int, c_int] + [c_void_p] + S3
                            + [c_void_p] * 6 + [c_void_p]),
     "lucid_cp_attn_fwd": (c_int, [c_int] * 5 + [c_float, c_int, c_int, c_int] + [c_void_p] + S3 + [c_void_p] + S3
-                          + [c_void_p] + [c_void_p] + S3 + [c_void_p, c_void_p, c_void_p]),
-    "lucid_cp_delta": (c_int, [c_int] * 6 + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_void_p]),
+                          + [c_void_p] + [c_void_p] + S3 + [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "lucid_cp_delta": (c_int, [c_int] * 6 + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p, c_void_p, c_void_p]),
     "lucid_cp_attn_bwd": (c_int, [c_int] * 5 + [c_float] + [c_int] * 4 + [c_void_p] + S3 + [c_void_p] + S3
                           + [c_void_p] + [c_void_p] + S3 + [c_void_p] * 2 + [c_void_p] + S3 + [c_void_p] * 4),
     "lucid_cp_solve_bwd": (c_int, [c_int] * 4 + [c_float] + [c_int] * 4 + [c_void_p] + S3 + [c_void_p] * 11

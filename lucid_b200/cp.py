@@ -350,6 +350,7 @@ class KernelBackend:
         self.flags = [torch.zeros(B * self.Hg * self.NB, dtype=torch.int32, device=device) for _ in range(self.G)]
         self.status = torch.zeros(64, dtype=torch.int32, device=device)
         self.o = torch.empty(B, self.C, Hq, D, **bf)
+        self.o_res = torch.empty_like(self.o)   # bf16 rounding residual of O (for rowsum(dO * O))
 
     # ---- helpers ----
     def _st(self):
@@ -440,13 +441,14 @@ class KernelBackend:
         hq = self._hq(g)
         qg, kg = self.Qf[:, hq], self.Kf[:, self._hs(g)]
         og = self.o[:, :, hq].transpose(1, 2)   # [B, Hq_g, C, D] view of [B, C, Hq, D]
+        orr = self.o_res[:, :, hq].transpose(1, 2)
         lo, hi = self._blk(t)
         _lib.check(self.lib.lucid_cp_attn_fwd(self.B, self.Hg * self.Gq, self.Hg, self.N, self.D, self.s, lo, hi,
                                               self.max_ctas, qg.data_ptr(), qg.stride(0), qg.stride(1), qg.stride(2),
                                               kg.data_ptr(), kg.stride(0), kg.stride(1), kg.stride(2),
                                               self.x[g].data_ptr(), self._shift(og, t, 2), og.stride(0), og.stride(1),
-                                              og.stride(2), self.lse[g].data_ptr(), self.status.data_ptr(),
-                                              self._st()), "lucid_cp_attn_fwd")
+                                              og.stride(2), self.lse[g].data_ptr(), self._shift(orr, t, 2),
+                                              self.status.data_ptr(), self._st()), "lucid_cp_attn_fwd")
 
     def finish(self):
         self._check_status()
@@ -464,12 +466,14 @@ class KernelBackend:
         self.delta = [torch.zeros(B, self.Hg * self.Gq, N, **f32) for _ in range(self.G)]
         for g in range(self.G):
             og = self.o[:, :, self._hq(g)].transpose(1, 2)
+            orr = self.o_res[:, :, self._hq(g)].transpose(1, 2)
             dg = self.dOf[:, self._hq(g)]
             for s in mine:
                 _lib.check(self.lib.lucid_cp_delta(B, self.Hg * self.Gq, N, D, self.layout.lo(s), self.layout.hi(s),
                                                    self._shift(og, s, 2), og.stride(0), og.stride(1), og.stride(2),
                                                    dg.data_ptr(), dg.stride(0), dg.stride(1), dg.stride(2),
-                                                   self.delta[g].data_ptr(), self._st()), "lucid_cp_delta")
+                                                   self._shift(orr, s, 2), self.delta[g].data_ptr(), self._st()),
+                           "lucid_cp_delta")
         # per-parity scratch of the head group in flight (group g uses g % 2); dV is kept
         # per group: a rank's earlier segment needs the dV its later segment solved
         self.dx32 = [torch.empty(B, self.Hg, N, D, **f32) for _ in range(2)]

@@ -19,7 +19,8 @@ cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap
                            const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st);
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
                          long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
-                         long long d_sn, float* delta, cudaStream_t st, int row0 = 0, int row1 = -1);
+                         long long d_sn, const bf16* o_res, float* delta, cudaStream_t st, int row0 = 0,
+                         int row1 = -1);
 cudaError_t launch_solve_finalize(int B, int H, int N, int Npad, float s, const bf16* k, long long k_sb,
                                   long long k_sh, long long k_sn, const float* rstd, const float* dinv,
                                   const bf16* x, const bf16* dv_int, const float* dk_col,
@@ -162,10 +163,11 @@ size_t lucid_attn_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
 int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
                    int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                    const void* x, void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse,
-                   void* workspace, size_t workspace_bytes, void* stream) {
+                   void* o_res, void* workspace, size_t workspace_bytes, void* stream) {
   if (!shape_ok(B, Hq, Hkv, N, D)) return LUCID_ERR_SHAPE;
   if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
   if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(o) || !aligned16(lse) ||
+      (o_res && !aligned16(o_res)) ||
       !strides_ok(q_sb, q_sh, q_sn) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn))
     return LUCID_ERR_ALIGN;
   if (!workspace || workspace_bytes < lucid_attn_fwd_workspace_bytes(B, Hq, Hkv, N, D))
@@ -183,6 +185,7 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   fa.scale = scale;
   fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
   fa.lse = lse;
+  fa.o_res = static_cast<bf16*>(o_res);
   fa.status = status;
   ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
   return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
@@ -197,22 +200,24 @@ size_t lucid_attn_bwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
   return kStatusRegion + align256(rows * sizeof(float));
 }
 
-// Stored-tile schedule: one bf16 dS^T tile per (batch, query head, key block i <= query block j).
+// Stored-tile schedule: one bf16 dS^T tile per (batch, query head, key block i <= query block j),
+// plus the bf16 residual (lo) tile of each diagonal block.
 size_t lucid_attn_bwd_fast_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
   const size_t nb = (size_t)nb_of(N);
   return lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D) +
-         align256((size_t)B * Hq * (nb * (nb + 1) / 2) * kTileBytes);
+         align256((size_t)B * Hq * (nb * (nb + 1) / 2 + nb) * kTileBytes);
 }
 
 int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void* q, int64_t q_sb,
                    int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                    const void* x, const void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
                    const void* dout, int64_t do_sb, int64_t do_sh, int64_t do_sn, const float* lse,
-                   void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn, float* dk_f32, float* dx_f32,
-                   void* workspace, size_t workspace_bytes, void* stream) {
+                   const void* o_res, void* dq, int64_t dq_sb, int64_t dq_sh, int64_t dq_sn, float* dk_f32,
+                   float* dx_f32, void* workspace, size_t workspace_bytes, void* stream) {
   if (!shape_ok(B, Hq, Hkv, N, D)) return LUCID_ERR_SHAPE;
   if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
   if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(o) || !aligned16(dout) ||
+      (o_res && !aligned16(o_res)) ||
       !aligned16(lse) || !aligned16(dq) || !aligned16(dk_f32) || !aligned16(dx_f32) ||
       !strides_ok(q_sb, q_sh, q_sn) || !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn) ||
       !strides_ok(do_sb, do_sh, do_sn) || !strides_ok(dq_sb, dq_sh, dq_sn))
@@ -226,7 +231,8 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   float* delta = reinterpret_cast<float*>(ws + kStatusRegion);
   if (cudaMemsetAsync(ws, 0, kStatusRegion, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   cudaError_t e = launch_delta(B, Hq, N, Npad, static_cast<const bf16*>(o), o_sb, o_sh, o_sn,
-                               static_cast<const bf16*>(dout), do_sb, do_sh, do_sn, delta, st);
+                               static_cast<const bf16*>(dout), do_sb, do_sh, do_sn,
+                               static_cast<const bf16*>(o_res), delta, st);
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   CUtensorMap tK, tX, tQ, tDO;
   if (!tmap_strided(&tK, k, B, Hkv, N, k_sb, k_sh, k_sn) || !tmap_internal(&tX, x, B, Hkv, Npad) ||
@@ -234,12 +240,12 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
       !tmap_strided(&tDO, dout, B, Hq, N, do_sb, do_sh, do_sn))
     return LUCID_ERR_TENSORMAP;
   // a workspace large enough for the dS^T tiles selects the stored-tile schedule
-  const size_t npair = (size_t)NB * (NB + 1) / 2;
+  const size_t ntile = (size_t)NB * (NB + 1) / 2 + NB;   // pair tiles + diagonal residual tiles
   const bool stored = workspace_bytes >= lucid_attn_bwd_fast_workspace_bytes(B, Hq, Hkv, N, D) &&
-                      npair * 128 < (size_t)1 << 31;
+                      ntile * 128 < (size_t)1 << 31;
   bf16* tiles = stored ? reinterpret_cast<bf16*>(ws + lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D)) : nullptr;
   CUtensorMap tS = tX;
-  if (stored && !tmap_internal(&tS, tiles, B, Hq, (int)(npair * 128))) return LUCID_ERR_TENSORMAP;
+  if (stored && !tmap_internal(&tS, tiles, B, Hq, (int)(ntile * 128))) return LUCID_ERR_TENSORMAP;
   BwdArgs ba{};
   ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
@@ -248,6 +254,7 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   ba.dq = static_cast<bf16*>(dq); ba.dq_sb = dq_sb; ba.dq_sh = dq_sh; ba.dq_sn = dq_sn;
   ba.status = status;
   ba.store_tiles = stored ? 1 : 0;
+  ba.tiles = tiles;
   {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
     e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, tS, ba, st);
@@ -446,10 +453,11 @@ extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float sca
                                  int max_ctas,
                                  const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn, const void* k,
                                  int64_t k_sb, int64_t k_sh, int64_t k_sn, const void* x, void* o, int64_t o_sb,
-                                 int64_t o_sh, int64_t o_sn, float* lse, int* status, void* stream) {
+                                 int64_t o_sh, int64_t o_sn, float* lse, void* o_res, int* status, void* stream) {
   if (!shape_ok(B, Hq, Hkv, N, D) || !cp_range_ok(N, blk_lo, blk_hi)) return LUCID_ERR_SHAPE;
   if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(lse) || !strides_ok(q_sb, q_sh, q_sn) ||
+  if (!aligned16(q) || !aligned16(k) || !aligned16(x) || !aligned16(lse) || (o_res && !aligned16(o_res)) ||
+      !strides_ok(q_sb, q_sh, q_sn) ||
       !strides_ok(k_sb, k_sh, k_sn) || !strides_ok(o_sb, o_sh, o_sn) || status == nullptr)
     return LUCID_ERR_ALIGN;
   const int NB = nb_of(N), Npad = npad_of(N);
@@ -462,6 +470,7 @@ extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float sca
   fa.scale = scale;
   fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
   fa.lse = lse;
+  fa.o_res = static_cast<bf16*>(o_res);
   fa.status = status;
   fa.pp0 = blk_lo / 2;
   fa.pp1 = (blk_hi + 1) / 2;
@@ -473,13 +482,14 @@ extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float sca
 
 extern "C" int lucid_cp_delta(int B, int Hq, int N, int D, int row_lo, int row_hi, const void* o, int64_t o_sb,
                               int64_t o_sh, int64_t o_sn, const void* dout, int64_t do_sb, int64_t do_sh,
-                              int64_t do_sn, float* delta, void* stream) {
+                              int64_t do_sn, const void* o_res, float* delta, void* stream) {
   if (!shape_ok(B, Hq, Hq, N, D) || row_lo < 0 || row_hi > N || row_lo > row_hi) return LUCID_ERR_SHAPE;
   if (empty_problem(B, Hq, Hq, N) || row_lo == row_hi) return LUCID_OK;
   if (!aligned16(delta) || !strides_ok(o_sb, o_sh, o_sn) || !strides_ok(do_sb, do_sh, do_sn)) return LUCID_ERR_ALIGN;
   return to_status(launch_delta(B, Hq, N, npad_of(N), static_cast<const bf16*>(o), o_sb, o_sh, o_sn,
-                                static_cast<const bf16*>(dout), do_sb, do_sh, do_sn, delta,
-                                reinterpret_cast<cudaStream_t>(stream), row_lo, row_hi));
+                                static_cast<const bf16*>(dout), do_sb, do_sh, do_sn,
+                                static_cast<const bf16*>(o_res), delta, reinterpret_cast<cudaStream_t>(stream),
+                                row_lo, row_hi));
 }
 
 extern "C" int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, int blk_lo, int blk_hi,

@@ -21,6 +21,13 @@
 //     E = exp(s K^_j K^_i^T - 1/s),  D = dV_j X_i^T,  dG = -s E o D,  dK^row_j += dG K^_i
 //   The diagonal entries P_rr enter exactly in fp32 in the finalize kernel.
 //
+// Diagonal tiles of the attention (key block i = query block j): P and dS are split
+// into bf16 hi + lo parts (lo = bf16(v - hi)) and both enter the GEMMs, so the rows
+// whose softmax sits on a few keys (the first rows of a sequence, where P and dS are
+// O(1)) do not lose bf16's half-ulp in dX, dK and dQ.  The row passes add the lo
+// tile right after the hi tile of the diagonal in both schedules (same order, same
+// results).
+//
 // Both passes: warps 0-7 are the epilogue (warp w reads TMEM lanes of
 // sub-partition w%4 = tile rows 32(w%4).., column half w/4); in the control
 // warpgroup warp 8 issues TMA and warp 9 issues tcgen05.mma (registers are
@@ -43,6 +50,47 @@ struct Ph {
 __device__ __forceinline__ bool warp_wait_b(uint32_t bar, uint32_t parity, const Abort& ab) {
   const bool ok = mbar_wait(bar, parity, ab);
   return __all_sync(0xffffffffu, ok);
+}
+
+// bf16 residuals of a pair: (a - bf16(a), b - bf16(b)) packed as bf16.
+__device__ __forceinline__ uint32_t pack_bf16_lo(float a, float b) {
+  return pack_bf16(a - __bfloat162float(__float2bfloat16_rn(a)), b - __bfloat162float(__float2bfloat16_rn(b)));
+}
+
+// Residual (lo) operands of a diagonal attention tile, kept out of line so that the
+// per-tile epilogue code stays small: v holds one thread's 64 values (its row, tile
+// columns [c0, c0 + 64)), staged in local memory by the caller.  Writes the packed
+// residuals into the second-operand columns (+16 of each 32-column chunk) at tcol.
+__device__ __noinline__ void diag_lo_to_tmem(uint32_t tcol, const float* v) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t pl[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) pl[e >> 1] = pack_bf16_lo(v[32 * q + e], v[32 * q + e + 1]);
+    tmem_st16(tcol + 32u * q + 16u, pl);
+  }
+}
+// dS = P (dP - delta) of the same 64 values, its residual into TMEM as above and, when
+// lo_row is given, into the stored residual tile's row (plain 16-byte stores).
+__device__ __noinline__ void diag_lo_ds(uint32_t tcol, const float* pv, const float* dv, const float* dlt,
+                                        __nv_bfloat16* lo_row) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t dl[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const float2 ds = mul2(make_float2(pv[32 * q + e], pv[32 * q + e + 1]),
+                             add2(make_float2(dv[32 * q + e], dv[32 * q + e + 1]),
+                                  make_float2(-dlt[32 * q + e], -dlt[32 * q + e + 1])));
+      dl[e >> 1] = pack_bf16_lo(ds.x, ds.y);
+    }
+    tmem_st16(tcol + 32u * q + 16u, dl);
+    if (lo_row) {
+      uint4* d4 = reinterpret_cast<uint4*>(lo_row + 32 * q);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) d4[c] = make_uint4(dl[4 * c], dl[4 * c + 1], dl[4 * c + 2], dl[4 * c + 3]);
+    }
+  }
 }
 
 // Packed bf16 operands written back into a 128-column TMEM region by the
@@ -263,8 +311,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (t == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
           tc_fence_after();
           const uint32_t acc = t > 0 ? 1u : 0u;
+          int g_, j_;
+          tile_at(i, t, g_, j_);
+          const bool diag = !SOLVE && j_ == i;   // P and dS also carry a bf16 lo part
           // acc1 += P B2 (P packed in the S region), then S(t+1) over it
           umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk); }, sB2(st), true, acc);
+          if (diag)
+            umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk) + 16u; }, sB2(st), true, 1u);
           if (has_next) {
             if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab)) { ok = false; break; }
             tc_fence_after();
@@ -275,6 +328,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!mbar_wait(bar(DSP_FULL), dsp_full.full(), ab)) { ok = false; break; }
           tc_fence_after();
           umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tDP, kk); }, sB1(st), true, acc);
+          if (diag)
+            umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tDP, kk) + 16u; }, sB1(st), true, 1u);
           umma_commit(bar(KV_EMPTY0 + st));
           if (has_next) {
             umma_tile(tDP, sA2, false, sB2(st2), false, 0u);  // dP(t+1)
@@ -429,6 +484,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
         }
+        const bool diag = !SOLVE && j == i;
+        if (diag) {
+          float tmp[64];
+#pragma unroll
+          for (int e = 0; e < 64; ++e) tmp[e] = pv[e >> 5][e & 31];
+          diag_lo_to_tmem(tmem + lane_base + kTmS + c0, tmp);
+        }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(PD_FULL));
@@ -467,6 +529,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q, dk);
           if (stage) tile_store_row32_packed(sDS, r, 2 * h + q, dk);
+        }
+        if (diag) {
+          // lo part of dS: into the dP region's second-operand columns and, in the
+          // stored-tile schedule, straight to its residual tile (row r of key block i)
+          const long long npair = (long long)p.NB * (p.NB + 1) / 2;
+          bf16* lo_row = stage ? p.tiles + (((long long)b * p.Hq + hk * G + g) * (npair + p.NB) * 128 +
+                                            (npair + i) * 128 + r) * kHeadDim + c0
+                               : nullptr;
+          float tp[64], td[64];
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            tp[e] = pv[e >> 5][e & 31];
+            td[e] = dv[e >> 5][e & 31];
+          }
+          diag_lo_ds(tmem + lane_base + kTmDP + c0, tp, td, vec + 128 + c0, lo_row);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -784,6 +861,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const uint32_t sreg = tS(n_s + tt);
             umma_tile_ts(tmem + kTmAcc, [&](int kk) { return packed_kslice(sreg, kk); }, sK(ki), true,
                          tt > 0 ? 1u : 0u);
+            if (!SOLVE && tt == T - 1)   // diagonal tile: the lo part of dS
+              umma_tile_ts(tmem + kTmAcc, [&](int kk) { return packed_kslice(sreg, kk) + 16u; }, sK(ki), true, 1u);
             umma_commit(bar(K_EMPTY0 + ki % 3u));
           }
         }
@@ -862,6 +941,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             dk[e >> 1] = pack_bf16(ds.x, ds.y);
           }
           tmem_st16(sreg + c0 + 32u * q, dk);
+        }
+        if (!SOLVE && i == j) {
+          // diagonal tile: the lo part of dS into the second-operand columns
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float (&sv)[32] = svv[q];
+            const int cb = (int)c0 + 32 * q;
+            uint32_t dl[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 arg = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-lse_r, -lse_r));
+              float2 pe = make_float2(fast_exp2(arg.x), fast_exp2(arg.y));
+              const int k0 = i * 128 + cb + e;
+              if (!(k0 <= row && k0 < p.N && row < p.N)) pe.x = 0.f;
+              if (!(k0 + 1 <= row && k0 + 1 < p.N && row < p.N)) pe.y = 0.f;
+              const float2 ds = mul2(pe, add2(make_float2(dv[q][e], dv[q][e + 1]), make_float2(-dl_r, -dl_r)));
+              dl[e >> 1] = pack_bf16_lo(ds.x, ds.y);
+            }
+            tmem_st16(sreg + c0 + 32u * q + 16u, dl);
+          }
         }
         tmem_st_wait();
         tc_fence_before();
@@ -987,8 +1086,12 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
     ha = bh % (SOLVE ? p.Hkv : p.Hq);
     hk = SOLVE ? ha : ha / G;
   };
-  auto ntiles = [&](int j) { return SOLVE ? j : j + 1; };
+  // attention: the dS^T tiles of key blocks 0..j, then the residual (lo) tile of the
+  // diagonal block j, stored after all pair tiles at index NB (NB + 1) / 2 + j
+  auto ntiles = [&](int j) { return SOLVE ? j : j + 2; };
   auto pair0 = [&](int j) { return SOLVE ? j * (j - 1) / 2 : j * (j + 1) / 2; };
+  auto tile_idx = [&](int j, int t) { return (SOLVE || t <= j) ? pair0(j) + t : p.NB * (p.NB + 1) / 2 + j; };
+  auto key_blk = [&](int j, int t) { return (SOLVE || t <= j) ? t : j; };
 
   if (warp == 4) {
     // ======================= TMA producer =======================
@@ -1001,14 +1104,14 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         int j, b, ha, hk;
         decode(idx, j, b, ha, hk);
-        const int T = ntiles(j), base = pair0(j);
+        const int T = ntiles(j);
         for (int t = 0; t < T; ++t, ++n) {
           const uint32_t st = n % kStages, use = n / kStages;
           if (!mbar_wait(bar(EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
           last[st] = use & 1;
           mbar_arrive_expect_tx(bar(FULL0 + st), 65536);
-          tma_load_tile_hint(sT(n), &tmT, bar(FULL0 + st), (base + t) * 128, ha, b, pol);
-          tma_load_tile(sB(n), &tmB, bar(FULL0 + st), t * 128, hk, b);
+          tma_load_tile_hint(sT(n), &tmT, bar(FULL0 + st), tile_idx(j, t) * 128, ha, b, pol);
+          tma_load_tile(sB(n), &tmB, bar(FULL0 + st), key_blk(j, t) * 128, hk, b);
         }
       }
       for (int s2 = 0; s2 < kStages; ++s2)
@@ -1094,10 +1197,12 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
 // elementwise helpers of the backward
 // --------------------------------------------------------------------------
 
-// delta[bhq][row] = sum_d dO[row][d] * O[row][d]  (zero on padding rows)
+// delta[bhq][row] = sum_d dO[row][d] * O[row][d]  (zero on padding rows); with the forward's
+// rounding residual o_res (O's strides, nullable) O is taken as o + o_res
 __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb,
                                    long long o_sh, long long o_sn, const bf16* dout, long long d_sb,
-                                   long long d_sh, long long d_sn, float* delta, int row0, int nrows) {
+                                   long long d_sh, long long d_sn, const bf16* o_res, float* delta,
+                                   int row0, int nrows) {
   const int warps = blockDim.x >> 5;
   const long long gw = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -1120,6 +1225,12 @@ __global__ void lucid_delta_kernel(int B, int Hq, int N, int Npad, const bf16* o
     f = __bfloat1622float2(ha[1]); a[2] = f.x; a[3] = f.y;
     f = __bfloat1622float2(hc[0]); c[0] = f.x; c[1] = f.y;
     f = __bfloat1622float2(hc[1]); c[2] = f.x; c[3] = f.y;
+    if (o_res) {
+      const uint2 ur = *reinterpret_cast<const uint2*>(o_res + (op - o));
+      const __nv_bfloat162* hr = reinterpret_cast<const __nv_bfloat162*>(&ur);
+      f = __bfloat1622float2(hr[0]); a[0] += f.x; a[1] += f.y;
+      f = __bfloat1622float2(hr[1]); a[2] += f.x; a[3] += f.y;
+    }
     acc = a[0] * c[0] + a[1] * c[1] + a[2] * c[2] + a[3] * c[3];
   }
 #pragma unroll
@@ -1265,13 +1376,14 @@ cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUten
 
 cudaError_t launch_delta(int B, int Hq, int N, int Npad, const bf16* o, long long o_sb, long long o_sh,
                          long long o_sn, const bf16* dout, long long d_sb, long long d_sh,
-                         long long d_sn, float* delta, cudaStream_t st, int row0, int row1) {
+                         long long d_sn, const bf16* o_res, float* delta, cudaStream_t st, int row0,
+                         int row1) {
   if (row1 < 0) row1 = Npad;
   const long long warps = (long long)B * Hq * (row1 - row0);
   if (warps <= 0) return cudaSuccess;
   const int blocks = (int)((warps + 7) / 8);
   lucid_delta_kernel<<<blocks, 256, 0, st>>>(B, Hq, N, Npad, o, o_sb, o_sh, o_sn, dout, d_sb, d_sh,
-                                             d_sn, delta, row0, row1 - row0);
+                                             d_sn, o_res, delta, row0, row1 - row0);
   return cudaGetLastError();
 }
 

@@ -43,6 +43,8 @@ struct FwdArgs {
   bf16* o;
   long long o_sb, o_sh, o_sn;
   float* lse;                // [B*Hq][Npad], log2 domain
+  bf16* o_res = nullptr;     // optional, O's strides: bf16(O_fp32 - bf16(O_fp32)), the rounding
+                             // residual of O, so the backward's rowsum(dO * O) sees O to ~16 bits
   int* status;
   // row-block pairs [pp0, pp1) processed (pp1 == 0: all; earlier blocks are solved
   // elsewhere and their flags already set) and an optional cap on the persistent
@@ -77,6 +79,10 @@ struct BwdArgs {
   // dG^T (solve) tile it computes, and the row pass streams them instead of
   // recomputing S and dP (tensor map passed to both kernels)
   int store_tiles = 0;
+  // attention, stored-tile schedule: the tiles' base address, [B*Hq][tile_rows][128] bf16
+  // (tile_rows = (NB (NB + 1) / 2 + NB) * 128: the dS^T tiles, then one bf16 residual tile
+  // per diagonal block, written by the column pass with plain stores)
+  bf16* tiles = nullptr;
 };
 
 // Decode step (get_new_v_prime) and decode attention: one pass over the caches.

@@ -427,6 +427,21 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) st_bf16x8(orow + q * 32 + c * 8, acc[q] + c * 8);
           }
+          if (p.o_res) {
+            bf16* rrow = p.o_res + (orow - p.o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float res[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float v = acc[q][c * 8 + e];
+                  res[e] = v - __bfloat162float(__float2bfloat16_rn(v));
+                }
+                st_bf16x8(rrow + q * 32 + c * 8, res);
+              }
+          }
         }
         p.lse[((long long)b * p.Hq + ha) * p.Npad + row] = m_run + __log2f(l_run);
         continue;

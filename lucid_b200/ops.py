@@ -123,8 +123,11 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int
     return x, khat, u, rstd, dinv
 
 
-def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float, d: int | None = None):
-    """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,128], lse)."""
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float, d: int | None = None,
+             residual: bool = False):
+    """O = softmax(scale Q K^T + causal) X.  Returns (o [B,N,Hq,128], lse), and with
+    ``residual`` also o_res (o's shape): the bf16 rounding residual of the fp32 output,
+    which attn_bwd adds back to O for rowsum(dO * O)."""
     lib = _lib.load()
     _lib.STATUS.poll()
     q = _prep(q, "query")
@@ -139,24 +142,28 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float
     o = torch.empty(B, N, Hq, W, dtype=torch.bfloat16, device=dev)
     ot = o.transpose(1, 2)
     lse = torch.empty(B, Hq, Np, dtype=torch.float32, device=dev)
+    o_res = torch.empty_like(o) if residual else None
     ws = _ws(lib.lucid_attn_fwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
     rc = lib.lucid_attn_fwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), lse.data_ptr(),
-                            ws.data_ptr(), ws.numel(), _stream())
+                            o_res.data_ptr() if residual else None, ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_attn_fwd")
     _lib.STATUS.watch(ws, "lucid_attn_fwd")
-    return o, lse
+    return (o, lse, o_res) if residual else (o, lse)
 
 
-def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
-    """Backward of attn_fwd.  o, do are [B,N,Hq,128].  Returns
-    (dq [B,Hq,N,128] bf16, dk_f32 [B,Hkv,Npad,128], dx_f32 [B,Hkv,Npad,128])."""
+def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None, o_res=None):
+    """Backward of attn_fwd.  o, do (and o_res, attn_fwd's residual, if given) are
+    [B,N,Hq,128].  Returns (dq [B,Hq,N,128] bf16, dk_f32 [B,Hkv,Npad,128],
+    dx_f32 [B,Hkv,Npad,128])."""
     lib = _lib.load()
     _lib.STATUS.poll()
     q = _prep(q, "query")
     k = _prep(k, "key")
     ot = _prep(o.transpose(1, 2), "attn_output")
     dot = _prep(do.transpose(1, 2), "grad_output")
+    if o_res is not None and o_res.stride() != o.stride():
+        raise ValueError("attn_bwd: o_res must have o's layout")
     B, Hq, N, W = q.shape
     D = W if d is None else d
     Hkv = k.shape[1]
@@ -170,7 +177,8 @@ def attn_bwd(q, k, x_int, o, do, lse, scale: float, d: int | None = None):
     ws = _ws(fast if stored_tiles_fit(fast, dev) else nbytes, dev)
     rc = lib.lucid_attn_bwd(B, Hq, Hkv, N, D, float(scale), q.data_ptr(), *_s3(q), k.data_ptr(),
                             *_s3(k), x_int.data_ptr(), ot.data_ptr(), *_s3(ot), dot.data_ptr(),
-                            *_s3(dot), lse.data_ptr(), dq.data_ptr(), *_s3(dq), dk.data_ptr(),
+                            *_s3(dot), lse.data_ptr(), o_res.data_ptr() if o_res is not None else None,
+                            dq.data_ptr(), *_s3(dq), dk.data_ptr(),
                             dx.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     _lib.check(rc, "lucid_attn_bwd")
     _lib.STATUS.watch(ws, "lucid_attn_bwd")
@@ -236,16 +244,16 @@ class LucidAttnFunction(torch.autograd.Function):
         q, k = _pad128(query), _pad128(key)
         x = torch.zeros(B, Hkv, padded_len(N), 128, dtype=torch.bfloat16, device=key.device)
         x[:, :, :N, :D] = v_prime
-        o, lse = attn_fwd(q, k, x, scaling, d=D)
-        ctx.save_for_backward(q, k, x, o, lse)
+        o, lse, o_res = attn_fwd(q, k, x, scaling, d=D, residual=True)
+        ctx.save_for_backward(q, k, x, o, lse, o_res)
         ctx.scaling, ctx.d = scaling, D
         return o[..., :D]
 
     @staticmethod
     def backward(ctx, do):
-        q, k, x, o, lse = ctx.saved_tensors
+        q, k, x, o, lse, o_res = ctx.saved_tensors
         N, D = k.shape[2], ctx.d
-        dq, dk, dx = attn_bwd(q, k, x, o, _pad128(do), lse, ctx.scaling, d=D)
+        dq, dk, dx = attn_bwd(q, k, x, o, _pad128(do), lse, ctx.scaling, d=D, o_res=o_res)
         return (dq[..., :D], dk[:, :, :N, :D].to(torch.bfloat16), dx[:, :, :N, :D].to(torch.bfloat16), None)
 
 
@@ -259,16 +267,16 @@ class LucidAttentionFunction(torch.autograd.Function):
         k = _prep(_pad128(key), "key")
         q = _prep(_pad128(query), "query")
         x, khat, u, rstd, dinv = solve_fwd(k, _pad128(value), scaling, eps, d=D)
-        o, lse = attn_fwd(q, k, x, scaling, d=D)
-        ctx.save_for_backward(q, k, x, khat, u, rstd, dinv, o, lse)
+        o, lse, o_res = attn_fwd(q, k, x, scaling, d=D, residual=True)
+        ctx.save_for_backward(q, k, x, khat, u, rstd, dinv, o, lse, o_res)
         ctx.scaling, ctx.d = scaling, D
         return o if D == 128 else o[..., :D]
 
     @staticmethod
     def backward(ctx, do):
-        q, k, x, khat, u, rstd, dinv, o, lse = ctx.saved_tensors
+        q, k, x, khat, u, rstd, dinv, o, lse, o_res = ctx.saved_tensors
         s, D = ctx.scaling, ctx.d
-        dq, dk_attn, dx = attn_bwd(q, k, x, o, _pad128(do), lse, s, d=D)
+        dq, dk_attn, dx = attn_bwd(q, k, x, o, _pad128(do), lse, s, d=D, o_res=o_res)
         dk, dv = solve_bwd(k, x, khat, u, rstd, dinv, dx, s, dk_add=dk_attn, d=D)
         if D == 128:
             return dq, dk, dv, None, None

@@ -56,10 +56,11 @@ def test_host_helpers(lib):
     # attention backward scratch: status word + delta rows (no dQ accumulator: the row pass owns dQ)
     assert lib.lucid_attn_bwd_workspace_bytes(B, 8, H, N, D) >= 256 + B * 8 * 1024 * 4
     # stored-tile schedule: one 32 KB bf16 tile per block pair on top of the base workspace
+    # (attention: plus the residual tile of each diagonal block)
     nb = 8  # ceil(1000 / 128)
     extra_attn = lib.lucid_attn_bwd_fast_workspace_bytes(B, 8, H, N, D) - lib.lucid_attn_bwd_workspace_bytes(
         B, 8, H, N, D)
-    assert extra_attn == B * 8 * (nb * (nb + 1) // 2) * 32768
+    assert extra_attn == B * 8 * (nb * (nb + 1) // 2 + nb) * 32768
     extra_solve = lib.lucid_solve_bwd_fast_workspace_bytes(B, H, N, D) - ws_b
     assert extra_solve == B * H * (nb * (nb - 1) // 2) * 32768
     # a single block has no off-diagonal pair: the solve needs nothing extra
@@ -111,7 +112,7 @@ def test_argument_errors_without_launch(lib):
     assert rc == 3
     # Hq not a multiple of Hkv
     rc = lib.lucid_attn_fwd(1, 3, 2, 128, 128, 0.088, 16, 128, 128, 128, 16, 128, 128, 128, 16,
-                            16, 128, 128, 128, 16, 16, 4096, null)
+                            16, 128, 128, 128, 16, None, 16, 4096, null)
     assert rc == 1
     # empty problems are a no-op
     rc = lib.lucid_solve_fwd(1, 1, 0, 128, 0.088, 1e-5, 16, 128, 128, 128, 16, 128, 128, 128,

@@ -285,8 +285,8 @@ def test_attn_bwd_stage(cuda_device, B, Hq, Hkv, N, keys):
     xp[:, :, :N] = x_
     q, k, do = _t(q_, cuda_device), _t(k_, cuda_device), _t(do_, cuda_device)
     x = _t(xp, cuda_device)
-    o, lse = attn_fwd(q, k, x, s)
-    dq, dk, dx = attn_bwd(q, k, x, o, do, lse, s)
+    o, lse, o_res = attn_fwd(q, k, x, s, residual=True)
+    dq, dk, dx = attn_bwd(q, k, x, o, do, lse, s, o_res=o_res)
     torch.cuda.synchronize()
     dq_r, dk_r, dx_r = _attn_bwd_oracle(q_, k_, x_, do_, s)
     G = Hq // Hkv
