@@ -1258,8 +1258,11 @@ def reference_gpu_bar(run, our_ms):
         out = run(rg)
         out["our_speedup"] = out["ms_per_step"] / our_ms
         return out
-    except Exception as e:   # the comparator is optional: report why it did not run
-        return {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
+    except Exception as e:   # the comparator is optional: report why it did not run (and where)
+        import traceback
+        frames = [f"{os.path.basename(fr.filename)}:{fr.lineno} {fr.name}" for fr in traceback.extract_tb(e.__traceback__)
+                  if "_ref" in fr.filename]
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:300]}", "where": frames[-3:]}
     finally:
         torch.cuda.empty_cache()
 

@@ -24,9 +24,11 @@
 // Diagonal tiles of the attention (key block i = query block j): P and dS are split
 // into bf16 hi + lo parts (lo = bf16(v - hi)) and both enter the GEMMs, so the rows
 // whose softmax sits on a few keys (the first rows of a sequence, where P and dS are
-// O(1)) do not lose bf16's half-ulp in dX, dK and dQ.  The row passes add the lo
-// tile right after the hi tile of the diagonal in both schedules (same order, same
-// results).
+// O(1)) do not lose bf16's half-ulp in dX, dK and dQ.  The attention column pass runs
+// as two launches of one template: the off-diagonal tiles (j > i), then the diagonal
+// tiles (DIAG), which add their hi + lo products to dX / dK; the main launch's code
+// carries none of the residual work.  The row passes add the lo tile right after the
+// hi tile of the diagonal in both schedules (same order, same results).
 //
 // Both passes: warps 0-7 are the epilogue (warp w reads TMEM lanes of
 // sub-partition w%4 = tile rows 32(w%4).., column half w/4); in the control
@@ -55,42 +57,6 @@ __device__ __forceinline__ bool warp_wait_b(uint32_t bar, uint32_t parity, const
 // bf16 residuals of a pair: (a - bf16(a), b - bf16(b)) packed as bf16.
 __device__ __forceinline__ uint32_t pack_bf16_lo(float a, float b) {
   return pack_bf16(a - __bfloat162float(__float2bfloat16_rn(a)), b - __bfloat162float(__float2bfloat16_rn(b)));
-}
-
-// Residual (lo) operands of a diagonal attention tile, kept out of line so that the
-// per-tile epilogue code stays small: v holds one thread's 64 values (its row, tile
-// columns [c0, c0 + 64)), staged in local memory by the caller.  Writes the packed
-// residuals into the second-operand columns (+16 of each 32-column chunk) at tcol.
-__device__ __noinline__ void diag_lo_to_tmem(uint32_t tcol, const float* v) {
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    uint32_t pl[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) pl[e >> 1] = pack_bf16_lo(v[32 * q + e], v[32 * q + e + 1]);
-    tmem_st16(tcol + 32u * q + 16u, pl);
-  }
-}
-// dS = P (dP - delta) of the same 64 values, its residual into TMEM as above and, when
-// lo_row is given, into the stored residual tile's row (plain 16-byte stores).
-__device__ __noinline__ void diag_lo_ds(uint32_t tcol, const float* pv, const float* dv, const float* dlt,
-                                        __nv_bfloat16* lo_row) {
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    uint32_t dl[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      const float2 ds = mul2(make_float2(pv[32 * q + e], pv[32 * q + e + 1]),
-                             add2(make_float2(dv[32 * q + e], dv[32 * q + e + 1]),
-                                  make_float2(-dlt[32 * q + e], -dlt[32 * q + e + 1])));
-      dl[e >> 1] = pack_bf16_lo(ds.x, ds.y);
-    }
-    tmem_st16(tcol + 32u * q + 16u, dl);
-    if (lo_row) {
-      uint4* d4 = reinterpret_cast<uint4*>(lo_row + 32 * q);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) d4[c] = make_uint4(dl[4 * c], dl[4 * c + 1], dl[4 * c + 2], dl[4 * c + 3]);
-    }
-  }
 }
 
 // Packed bf16 operands written back into a 128-column TMEM region by the
@@ -127,13 +93,14 @@ constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
 }  // namespace bwdc
 
-template <bool SOLVE>
+template <bool SOLVE, bool DIAG>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     lucid_bwd_col_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
                          const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
                          const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmS,
                          BwdArgs p) {
   using namespace bwdc;
+  static_assert(!(SOLVE && DIAG), "the diagonal launch is the attention's");
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
@@ -201,15 +168,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     b = bh / p.Hkv;
     hk = bh % p.Hkv;
   };
-  auto ntiles = [&](int i) { return SOLVE ? (p.NB - 1 - i) : G * (p.NB - i); };
+  // attention: the main launch takes the tiles j > i (query head g, block j), the
+  // diagonal launch the tiles j = i of each query head of the group
+  auto ntiles = [&](int i) { return SOLVE ? (p.NB - 1 - i) : (DIAG ? G : G * (p.NB - 1 - i)); };
   auto tile_at = [&](int i, int t, int& g, int& j) {
     if (SOLVE) {
       g = 0;
       j = p.NB - 1 - t;
+    } else if (DIAG) {
+      g = t;
+      j = i;
     } else {
-      const int per = p.NB - i;
+      const int per = p.NB - 1 - i;
       g = t / per;
-      j = i + t % per;
+      j = i + 1 + t % per;
     }
   };
 
@@ -311,12 +283,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (t == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) { ok = false; break; }
           tc_fence_after();
           const uint32_t acc = t > 0 ? 1u : 0u;
-          int g_, j_;
-          tile_at(i, t, g_, j_);
-          const bool diag = !SOLVE && j_ == i;   // P and dS also carry a bf16 lo part
-          // acc1 += P B2 (P packed in the S region), then S(t+1) over it
+          // acc1 += P B2 (P packed in the S region; diagonal: its lo part too), then S(t+1) over it
           umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk); }, sB2(st), true, acc);
-          if (diag)
+          if constexpr (DIAG)
             umma_tile_ts(tmem + kTmAcc1, [&](int kk) { return packed_kslice(tS, kk) + 16u; }, sB2(st), true, 1u);
           if (has_next) {
             if (!mbar_wait(bar(KV_FULL0 + st2), ((n_kv + 1) >> 1) & 1, ab)) { ok = false; break; }
@@ -328,7 +297,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!mbar_wait(bar(DSP_FULL), dsp_full.full(), ab)) { ok = false; break; }
           tc_fence_after();
           umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tDP, kk); }, sB1(st), true, acc);
-          if (diag)
+          if constexpr (DIAG)
             umma_tile_ts(tmem + kTmAcc2, [&](int kk) { return packed_kslice(tDP, kk) + 16u; }, sB1(st), true, 1u);
           umma_commit(bar(KV_EMPTY0 + st));
           if (has_next) {
@@ -337,6 +306,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
         if (!ok) break;
+        // an item without tiles (the last key block of the off-diagonal launch) still
+        // takes its turn on the accumulator barriers (the epilogue writes zeros)
+        if (!SOLVE && T == 0 && !mbar_wait(bar(ACC_FREE), acc_free.empty(), ab)) break;
         umma_commit(bar(ACC_FULL));
         if (!SOLVE) {
           umma_commit(bar(A_EMPTY));
@@ -447,7 +419,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld_wait();
         const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
         const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
-                                : (j > i && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
+                                : (!DIAG && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const int cb = (int)c0 + 32 * q;
@@ -484,12 +456,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q, pk);
         }
-        const bool diag = !SOLVE && j == i;
-        if (diag) {
-          float tmp[64];
+        if constexpr (DIAG) {   // lo part of P into the second-operand columns
 #pragma unroll
-          for (int e = 0; e < 64; ++e) tmp[e] = pv[e >> 5][e & 31];
-          diag_lo_to_tmem(tmem + lane_base + kTmS + c0, tmp);
+          for (int q = 0; q < 2; ++q) {
+            uint32_t pl[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) pl[e >> 1] = pack_bf16_lo(pv[q][e], pv[q][e + 1]);
+            tmem_st16(tmem + lane_base + kTmS + c0 + 32u * q + 16u, pl);
+          }
         }
         tmem_st_wait();
         tc_fence_before();
@@ -530,20 +504,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q, dk);
           if (stage) tile_store_row32_packed(sDS, r, 2 * h + q, dk);
         }
-        if (diag) {
+        if constexpr (DIAG) {
           // lo part of dS: into the dP region's second-operand columns and, in the
           // stored-tile schedule, straight to its residual tile (row r of key block i)
           const long long npair = (long long)p.NB * (p.NB + 1) / 2;
-          bf16* lo_row = stage ? p.tiles + (((long long)b * p.Hq + hk * G + g) * (npair + p.NB) * 128 +
-                                            (npair + i) * 128 + r) * kHeadDim + c0
-                               : nullptr;
-          float tp[64], td[64];
+          bf16* lo_row = p.tiles + (((long long)b * p.Hq + hk * G + g) * (npair + p.NB) * 128 + (npair + i) * 128 + r) *
+                                       kHeadDim;
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            tp[e] = pv[e >> 5][e & 31];
-            td[e] = dv[e >> 5][e & 31];
+          for (int q = 0; q < 2; ++q) {
+            const int cb = (int)c0 + 32 * q;
+            uint32_t dl[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 ds = mul2(make_float2(pv[q][e], pv[q][e + 1]),
+                                     add2(make_float2(dv[q][e], dv[q][e + 1]),
+                                          make_float2(-vec[128 + cb + e], -vec[128 + cb + e + 1])));
+              dl[e >> 1] = pack_bf16_lo(ds.x, ds.y);
+            }
+            tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q + 16u, dl);
+            if (stage) {
+              uint4* d4 = reinterpret_cast<uint4*>(lo_row + cb);
+#pragma unroll
+              for (int c = 0; c < 4; ++c) d4[c] = make_uint4(dl[4 * c], dl[4 * c + 1], dl[4 * c + 2], dl[4 * c + 3]);
+            }
           }
-          diag_lo_ds(tmem + lane_base + kTmDP + c0, tp, td, vec + 128 + c0, lo_row);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -558,21 +542,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
       tc_fence_after();
       if (!SOLVE) {
+        // dX_i, s dK_i: stored by the off-diagonal launch (zeros for an item without
+        // tiles), added to by the diagonal launch, which runs after it
         float* dxr = p.dx + (bhk * p.Npad + row_i) * kHeadDim + c0;
         float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           float a1[32], a2[32];
-          tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
-          tmem_ld32(tmem + lane_base + kTmAcc2 + c0 + 32u * q, a2);
-          tmem_ld_wait();
+          if (T > 0) {
+            tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
+            tmem_ld32(tmem + lane_base + kTmAcc2 + c0 + 32u * q, a2);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) a1[e] = a2[e] = 0.f;
+          }
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            reinterpret_cast<float4*>(dxr)[q * 8 + c] =
-                make_float4(a1[4 * c], a1[4 * c + 1], a1[4 * c + 2], a1[4 * c + 3]);
-            reinterpret_cast<float4*>(dkr)[q * 8 + c] =
-                make_float4(a2[4 * c] * p.scale, a2[4 * c + 1] * p.scale, a2[4 * c + 2] * p.scale,
-                            a2[4 * c + 3] * p.scale);
+            float4 x4 = make_float4(a1[4 * c], a1[4 * c + 1], a1[4 * c + 2], a1[4 * c + 3]);
+            float4 k4 = make_float4(a2[4 * c] * p.scale, a2[4 * c + 1] * p.scale, a2[4 * c + 2] * p.scale,
+                                    a2[4 * c + 3] * p.scale);
+            if constexpr (DIAG) {
+              const float4 ox = reinterpret_cast<const float4*>(dxr)[q * 8 + c];
+              const float4 ok4 = reinterpret_cast<const float4*>(dkr)[q * 8 + c];
+              x4 = make_float4(ox.x + x4.x, ox.y + x4.y, ox.z + x4.z, ox.w + x4.w);
+              k4 = make_float4(ok4.x + k4.x, ok4.y + k4.y, ok4.z + k4.z, ok4.w + k4.w);
+            }
+            reinterpret_cast<float4*>(dxr)[q * 8 + c] = x4;
+            reinterpret_cast<float4*>(dkr)[q * 8 + c] = k4;
           }
         }
         tc_fence_before();
@@ -1330,11 +1327,15 @@ cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap
   const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, bwd_num_sms()) : bwd_num_sms());
   cudaError_t e;
   if (solve) {
-    if ((e = set_smem(lucid_bwd_col_kernel<true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    if ((e = set_smem(lucid_bwd_col_kernel<true, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_col_kernel<true, false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
   } else {
-    if ((e = set_smem(lucid_bwd_col_kernel<false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    // off-diagonal tiles, then the diagonal tiles (which add to dX, dK)
+    if ((e = set_smem(lucid_bwd_col_kernel<false, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_col_kernel<false, false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = set_smem(lucid_bwd_col_kernel<false, true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
+    lucid_bwd_col_kernel<false, true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
   }
   return cudaGetLastError();
 }
