@@ -843,7 +843,7 @@ def bench_cp(args, torch, dist, dev, world, rank, local, barrier):
                                train_bounds, zigzag_layout)
     B, H, N, D = 1, 32, 131072, 128
     bwd = not args.cp_forward_only
-    lay = args.cp_layout if args.cp_layout != "auto" else ("zigzag" if world >= 4 else "contiguous")
+    lay = args.cp_layout   # contiguous chunks unless zigzag is asked for by name
     if lay == "zigzag":
         layout = zigzag_layout(N, world)
         layout_desc = f"zigzag: {2 * world} segments, rank r owning r and {2 * world - 1}-r"
@@ -1330,9 +1330,9 @@ def main(argv=None):
     ap.add_argument("--cp-forward-only", action="store_true", help="cp128k: time the forward chain alone")
     ap.add_argument("--path-seq", type=int, default=0,
                     help="path: sequence length instead of config 3's 16384 (smaller profiling cases)")
-    ap.add_argument("--cp-layout", choices=["auto", "zigzag", "contiguous"], default="auto",
-                    help="cp128k: rows per rank (zigzag: segments r and 2W-1-r; contiguous: one chunk; "
-                         "auto: contiguous below 4 ranks, where its balanced chunks are as good, else zigzag)")
+    ap.add_argument("--cp-layout", choices=["zigzag", "contiguous"], default="contiguous",
+                    help="cp128k: rows per rank (contiguous: one chunk per rank, solved X chunks flowing "
+                         "rank to rank, the default; zigzag: segments r and 2W-1-r, a non-default variant)")
     ap.add_argument("--cpu-n", type=int, default=8192, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t packed_kslice(uint32_t region, int kk) {
 constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdEpiThreads = kBwdEpiWarps * 32;
 constexpr int kBwdThreads = kBwdEpiThreads + 128;  // + control warpgroup (TMA, MMA, 2 idle warps)
-constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1, kBwdWarpStore = kBwdEpiWarps + 2;
+constexpr int kBwdWarpTma = kBwdEpiWarps, kBwdWarpMma = kBwdEpiWarps + 1;
 // register split: 384 x 168 at launch >= 256 x 192 + 128 x 120
 constexpr int kBwdRegsEpi = 192, kBwdRegsCtl = 120;
 
@@ -91,10 +91,21 @@ enum {
 };
 constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
+// 16 epilogue warps (four per TMEM sub-partition, one 32-column chunk of the tile
+// each) so that every scheduler has four epilogue warps to hide the latencies of the
+// TMEM loads, exponentials and stores; warps 16-19: TMA, MMA, tile store, idle.
+constexpr int kColEpiWarps = 16, kColQ = 4 * 4 / kColEpiWarps;
+constexpr int kColEpiThreads = kColEpiWarps * 32;
+constexpr int kColThreads = kColEpiThreads + 128;
+constexpr int kColWarpTma = kColEpiWarps, kColWarpMma = kColEpiWarps + 1, kColWarpStore = kColEpiWarps + 2;
+// register split: 640 x 96 at launch >= 512 x 96 + 128 x 88
+constexpr int kColRegsEpi = 96, kColRegsCtl = 88;
+static_assert(kColEpiThreads * kColRegsEpi + 128 * kColRegsCtl <= kColThreads * (65536 / kColThreads / 8 * 8),
+              "register split exceeds the launch allocation");
 }  // namespace bwdc
 
 template <bool SOLVE, bool DIAG>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(bwdc::kColThreads, 1)
     lucid_bwd_col_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
                          const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
                          const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmS,
@@ -117,7 +128,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
     return;
   }
-  if (threadIdx.x == kBwdWarpTma * 32) {
+  if (threadIdx.x == kColWarpTma * 32) {
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
     for (int s2 = 0; s2 < 2; ++s2) {
@@ -126,17 +137,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(bar(SD_FULL), 1);
     mbar_init(bar(DP_FULL), 1);
-    mbar_init(bar(PD_FULL), kBwdEpiThreads);
-    mbar_init(bar(DSP_FULL), kBwdEpiThreads);
+    mbar_init(bar(PD_FULL), kColEpiThreads);
+    mbar_init(bar(DSP_FULL), kColEpiThreads);
     mbar_init(bar(DS_FREE), 1);
     mbar_init(bar(T_FULL), 1);
-    mbar_init(bar(S_FREE), kBwdEpiThreads);
+    mbar_init(bar(S_FREE), kColEpiThreads);
     mbar_init(bar(ACC_FULL), 1);
     mbar_init(bar(ACC2_FULL), 1);
-    mbar_init(bar(ACC_FREE), kBwdEpiThreads);
-    mbar_init(bar(EPI_DONE), kBwdEpiThreads);
+    mbar_init(bar(ACC_FREE), kColEpiThreads);
+    mbar_init(bar(EPI_DONE), kColEpiThreads);
     mbar_init(bar(DRAIN), 1);
-    mbar_init(bar(STG_READY), kBwdEpiThreads);
+    mbar_init(bar(STG_READY), kColEpiThreads);
     mbar_init(bar(STG_FREE), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -146,7 +157,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tmB2);
     if (SOLVE) tma_prefetch_desc(&tmU);
   }
-  if (warp == kBwdWarpMma) {
+  if (warp == kColWarpMma) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -185,9 +196,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   };
 
-  if (warp >= kBwdWarpTma) {
-  regs_dec<kBwdRegsCtl>();
-  if (warp == kBwdWarpTma) {
+  if (warp >= kColWarpTma) {
+  regs_dec<kColRegsCtl>();
+  if (warp == kColWarpTma) {
     // ======================= TMA producer =======================
     if (lane == 0) {
       Ph a_empty;
@@ -242,7 +253,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int s2 = 0; s2 < 2; ++s2)
         if (last_kv[s2] >= 0) mbar_wait_timed(bar(KV_FULL0 + s2), (uint32_t)last_kv[s2], kDrainNs);
     }
-  } else if (warp == kBwdWarpMma) {
+  } else if (warp == kColWarpMma) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
       Ph a_full, pd_full, dsp_full, acc_free, s_free;
@@ -347,7 +358,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
-  } else if (warp == kBwdWarpStore && p.store_tiles != 0) {
+  } else if (warp == kColWarpStore && p.store_tiles != 0) {
     // ============ tile store (stored-tile schedule) ============
     // per tile: once the 256 epilogue threads staged the packed tile (attention dS^T of
     // key block i, query block j >= i: pair j (j + 1) / 2 + i of query head hk G + g;
@@ -379,19 +390,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   }
   } else {
-    regs_inc<kBwdRegsEpi>();
+    regs_inc<kColRegsEpi>();
     // ======================= epilogue warps 0-7 =======================
-    const int sp = warp & 3, h = warp >> 2;
+    // warp w: TMEM lanes of sub-partition w % 4 (tile rows 32 (w % 4) ..) and the
+    // kColQ 32-column chunks from chunk ch0 = (w / 4) kColQ
+    const int sp = warp & 3, ch0 = (warp >> 2) * kColQ;
     const int r = sp * 32 + lane;
     const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
-    const uint32_t c0 = 64u * (uint32_t)h;
+    const uint32_t c0 = 32u * (uint32_t)ch0;
     const float kLog2e = 1.4426950408889634f;
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
     Ph sd_full, dp_full, ds_free, t_full, acc_full, acc2_full;
     uint32_t n_kv = 0, item = 0;
     // stored-tile schedule: every packed dS^T (attention) / dG^T (solve) tile also goes
-    // to global memory through the sDS tile, stored by warp kBwdWarpStore.  n_st counts
+    // to global memory through the sDS tile, stored by warp kColWarpStore.  n_st counts
     // the tiles staged so far; the staging tile is free for tile n_st once STG_FREE has
     // completed n_st times (the solve's diagonal steps also use sDS: they wait for the
     // item's last store, and an item's first staged tile waits for the previous item's
@@ -413,15 +426,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
         // phase 1: P (attention) / E (solve) from S alone, packed into the S region
-        float pv[2][32];
-        tmem_ld32(tmem + lane_base + kTmS + c0, pv[0]);
-        tmem_ld32(tmem + lane_base + kTmS + c0 + 32u, pv[1]);
+        float pv[kColQ][32];
+#pragma unroll
+        for (int q = 0; q < kColQ; ++q) tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, pv[q]);
         tmem_ld_wait();
         const float* vec = reinterpret_cast<const float*>(smem + kOffVec + st * 1024);
         const bool full = SOLVE ? ((j + 1) * 128 <= p.N)
                                 : (!DIAG && (j + 1) * 128 <= p.N && (i + 1) * 128 <= p.N);
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < kColQ; ++q) {
           const int cb = (int)c0 + 32 * q;
           uint32_t pk[16];
 #pragma unroll
@@ -458,7 +471,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         if constexpr (DIAG) {   // lo part of P into the second-operand columns
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
+          for (int q = 0; q < kColQ; ++q) {
             uint32_t pl[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) pl[e >> 1] = pack_bf16_lo(pv[q][e], pv[q][e + 1]);
@@ -472,16 +485,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // packed into the dP region (and staged for the tile store)
         if (!warp_wait_b(bar(DP_FULL), dp_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
-        float dv[2][32];
-        tmem_ld32(tmem + lane_base + kTmDP + c0, dv[0]);
-        tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u, dv[1]);
+        float dv[kColQ][32];
+#pragma unroll
+        for (int q = 0; q < kColQ; ++q) tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u * q, dv[q]);
         tmem_ld_wait();
         if (stage) {
           if (n_st > 0 && !warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) { ok = false; break; }
           if (SOLVE && t == 0 && !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) { ok = false; break; }
         }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < kColQ; ++q) {
           const int cb = (int)c0 + 32 * q;
           uint32_t dk[16];
 #pragma unroll
@@ -502,7 +515,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
           tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q, dk);
-          if (stage) tile_store_row32_packed(sDS, r, 2 * h + q, dk);
+          if (stage) tile_store_row32_packed(sDS, r, ch0 + q, dk);
         }
         if constexpr (DIAG) {
           // lo part of dS: into the dP region's second-operand columns and, in the
@@ -511,7 +524,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           bf16* lo_row = p.tiles + (((long long)b * p.Hq + hk * G + g) * (npair + p.NB) * 128 + (npair + i) * 128 + r) *
                                        kHeadDim;
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
+          for (int q = 0; q < kColQ; ++q) {
             const int cb = (int)c0 + 32 * q;
             uint32_t dl[16];
 #pragma unroll
@@ -547,7 +560,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         float* dxr = p.dx + (bhk * p.Npad + row_i) * kHeadDim + c0;
         float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < kColQ; ++q) {
           float a1[32], a2[32];
           if (T > 0) {
             tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
@@ -579,10 +592,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       ++n_kv;  // the U_i load
       // ---------------- solve: diagonal block ----------------
       // D1: R = dX_i - acc1 (this warp's column half), staged as bf16 for U^T R
-      float rr[2][32];
+      float rr[kColQ][32];
       const float* dxr = p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kColQ; ++q) {
         float a1[32];
         if (T > 0) {
           tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
@@ -607,7 +620,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
 #pragma unroll
-      for (int q = 0; q < 2; ++q) tile_store_row32(sDS, r, 2 * h + q, rr[q]);
+      for (int q = 0; q < kColQ; ++q) tile_store_row32(sDS, r, ch0 + q, rr[q]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar(PD_FULL));
@@ -618,7 +631,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float di = p.dinv[bhk * p.Npad + row_i];
       bf16* dvr = p.dv + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kColQ; ++q) {
         float tv[32];
         tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, tv);
         tmem_ld_wait();
@@ -626,7 +639,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int e = 0; e < 32; ++e) tv[e] = (rr[q][e] + tv[e]) * di;
 #pragma unroll
         for (int c = 0; c < 4; ++c) st_bf16x8(dvr + q * 32 + c * 8, tv + c * 8);
-        tile_store_row32(sDS, r, 2 * h + q, tv);
+        tile_store_row32(sDS, r, ch0 + q, tv);
       }
       tc_fence_before();
       mbar_arrive(bar(S_FREE));
@@ -644,7 +657,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       tc_fence_after();
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kColQ; ++q) {
         float sv[32], dv[32];
         tmem_ld32(tmem + lane_base + kTmS + c0 + 32u * q, sv);
         tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u * q, dv);
@@ -655,7 +668,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const bool valid = (c > r) && (i * 128 + c < p.N);
           sv[e] = valid ? -p.scale * fast_exp2(fmaf(sv[e], c1, -c2)) * dv[e] : 0.f;
         }
-        tile_store_row32(sDS, r, 2 * h + q, sv);
+        tile_store_row32(sDS, r, ch0 + q, sv);
       }
       tc_fence_before();
       mbar_arrive(bar(S_FREE));
@@ -666,7 +679,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       float* dkr = p.dk_col + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kColQ; ++q) {
         float a2[32];
         tmem_ld32(tmem + lane_base + kTmAcc2 + c0 + 32u * q, a2);
         tmem_ld_wait();
@@ -682,7 +695,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kBwdWarpMma) {
+  if (warp == kColWarpMma) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1328,14 +1341,16 @@ cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap
   cudaError_t e;
   if (solve) {
     if ((e = set_smem(lucid_bwd_col_kernel<true, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<true, false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    // the transposed solve's CTAs wait on one another's flags: all of them must be resident
+    return launch_cooperative(lucid_bwd_col_kernel<true, false>, grid, bwdc::kColThreads, bwdc::kSmemBytes, st, tA1,
+                              tA2, tB1, tB2, tU, tS, a);
   } else {
     // off-diagonal tiles, then the diagonal tiles (which add to dX, dK)
     if ((e = set_smem(lucid_bwd_col_kernel<false, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false, false><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    lucid_bwd_col_kernel<false, false><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(lucid_bwd_col_kernel<false, true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false, true><<<grid, kBwdThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    lucid_bwd_col_kernel<false, true><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
   }
   return cudaGetLastError();
 }

@@ -528,7 +528,8 @@ cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB,
     e = cudaFuncSetAttribute(lucid_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
-    lucid_fwd_kernel<true><<<grid, fwd::kThreads, fwd::kSmemBytes, st>>>(tA, tB, tC, tU, a);
+    // the wavefront's CTAs wait on one another's flags: all of them must be resident
+    return launch_cooperative(lucid_fwd_kernel<true>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
   } else {
     e = cudaFuncSetAttribute(lucid_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);

@@ -1104,37 +1104,41 @@ static int path_num_sms() {
   return n > 0 ? n : 148;
 }
 
+// cooperative: the grid's CTAs wait on flags published by other CTAs of the grid (the
+// wavefront solves), so the launch must place all of them at once
 template <typename K, typename... Args>
-static cudaError_t launch_persistent(K kernel, uint32_t smem, int total, cudaStream_t st, Args... args) {
+static cudaError_t launch_persistent(K kernel, uint32_t smem, int total, cudaStream_t st, bool cooperative,
+                                     Args... args) {
   if (total <= 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::min(total, path_num_sms());
+  if (cooperative) return launch_cooperative(kernel, grid, pk::kThreads, smem, st, args...);
   kernel<<<grid, pk::kThreads, smem, st>>>(args...);
   return cudaGetLastError();
 }
 
 cudaError_t launch_path_scores(const CUtensorMap& tmKn, const CUtensorMap& tmW, const CUtensorMap& tmW2,
                                const CUtensorMap& tmQs, const PathScoresArgs& a, cudaStream_t st) {
-  return launch_persistent(path_scores_kernel, psc::kSmem, (a.NB - 1) * a.B * a.HQ, st, tmKn, tmW, tmW2, tmQs, a);
+  return launch_persistent(path_scores_kernel, psc::kSmem, (a.NB - 1) * a.B * a.HQ, st, false, tmKn, tmW, tmW2, tmQs, a);
 }
 
 cudaError_t launch_path_solve(bool transposed, const CUtensorMap& tmL, const CUtensorMap& tmX, const CUtensorMap& tmU,
                               const PathSolveArgs& a, cudaStream_t st) {
   const int total = a.NB * a.B * a.HQ;
-  if (transposed) return launch_persistent(path_solve_kernel<true>, psv::kSmem, total, st, tmL, tmX, tmU, a);
-  return launch_persistent(path_solve_kernel<false>, psv::kSmem, total, st, tmL, tmX, tmU, a);
+  if (transposed) return launch_persistent(path_solve_kernel<true>, psv::kSmem, total, st, true, tmL, tmX, tmU, a);
+  return launch_persistent(path_solve_kernel<false>, psv::kSmem, total, st, true, tmL, tmX, tmU, a);
 }
 
 cudaError_t launch_path_row(const CUtensorMap& tmDV, const CUtensorMap& tmO, const CUtensorMap& tmKn,
                             const CUtensorMap& tmW, const CUtensorMap& tmW2, const CUtensorMap& tmDs,
                             const PathRowArgs& a, cudaStream_t st) {
-  return launch_persistent(path_row_kernel, prw::kSmem, a.NB * a.B * a.HQ, st, tmDV, tmO, tmKn, tmW, tmW2, tmDs, a);
+  return launch_persistent(path_row_kernel, prw::kSmem, a.NB * a.B * a.HQ, st, false, tmDV, tmO, tmKn, tmW, tmW2, tmDs, a);
 }
 
 cudaError_t launch_path_col(const CUtensorMap& tmDA, const CUtensorMap& tmQs, const CUtensorMap& tmDs,
                             const CUtensorMap& tmW, const CUtensorMap& tmW2, const PathColArgs& a, cudaStream_t st) {
-  return launch_persistent(path_col_kernel, pcl::kSmem, a.NB * a.B * a.HQ, st, tmDA, tmQs, tmDs, tmW, tmW2, a);
+  return launch_persistent(path_col_kernel, pcl::kSmem, a.NB * a.B * a.HQ, st, false, tmDA, tmQs, tmDs, tmW, tmW2, a);
 }
 
 // ===========================================================================
@@ -1483,7 +1487,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 
 cudaError_t launch_path_attn(const CUtensorMap& tmKn, const CUtensorMap& tmW, const CUtensorMap& tmW2,
                              const CUtensorMap& tmV, const PathAttnArgs& a, cudaStream_t st) {
-  return launch_persistent(path_attn_kernel, pat::kSmem, a.NB * a.B * a.HQ, st, tmKn, tmW, tmW2, tmV, a);
+  return launch_persistent(path_attn_kernel, pat::kSmem, a.NB * a.B * a.HQ, st, false, tmKn, tmW, tmW2, tmV, a);
 }
 
 }  // namespace lb

@@ -15,6 +15,7 @@
 // without any data movement.
 #pragma once
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -552,6 +553,27 @@ __device__ __forceinline__ void st_bf16x8(__nv_bfloat16* p, const float* in) {
   u.z = pack_bf16(in[4], in[5]);
   u.w = pack_bf16(in[6], in[7]);
   *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Host: launch `kernel` as a cooperative grid, for the wavefront kernels whose CTAs
+// wait on flags other CTAs of the same grid publish.  A cooperative launch either
+// places every CTA of the grid on the GPU at once or fails with an error
+// (cudaErrorCooperativeLaunchTooLarge), so a CTA never waits on a CTA that cannot
+// start while it occupies an SM (other streams or processes holding SMs included).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_cooperative(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cudaStream_t st,
+                                      Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace lb
