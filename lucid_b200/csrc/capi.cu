@@ -11,9 +11,9 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
-                           const CUtensorMap& tB2, const CUtensorMap& tU, const CUtensorMap& tS, const BwdArgs& a,
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a,
                            cudaStream_t st);
-cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUtensorMap& tB, const BwdArgs& a,
+cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tB, const BwdArgs& a,
                                   cudaStream_t st);
 cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const BwdArgs& a, cudaStream_t st);
@@ -244,8 +244,6 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   const bool stored = workspace_bytes >= lucid_attn_bwd_fast_workspace_bytes(B, Hq, Hkv, N, D) &&
                       ntile * 128 < (size_t)1 << 31;
   bf16* tiles = stored ? reinterpret_cast<bf16*>(ws + lucid_attn_bwd_workspace_bytes(B, Hq, Hkv, N, D)) : nullptr;
-  CUtensorMap tS = tX;
-  if (stored && !tmap_internal(&tS, tiles, B, Hq, (int)(ntile * 128))) return LUCID_ERR_TENSORMAP;
   BwdArgs ba{};
   ba.B = B; ba.Hq = Hq; ba.Hkv = Hkv; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
@@ -257,11 +255,11 @@ int lucid_attn_bwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   ba.tiles = tiles;
   {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
-    e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, tS, ba, st);
+    e = launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
-  if (stored) return to_status(launch_bwd_row_stored(false, tS, tK, ba, st));
+  if (stored) return to_status(launch_bwd_row_stored(false, tK, ba, st));
   return to_status(launch_bwd_row(false, tQ, tDO, tK, tX, ba, st));
 }
 
@@ -319,9 +317,6 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   const size_t npair = (size_t)NB * (NB - 1) / 2;
   const bool stored = npair > 0 && workspace_bytes >= lucid_solve_bwd_fast_workspace_bytes(B, H, N, D) &&
                       npair * 128 < (size_t)1 << 31;
-  CUtensorMap tS = tU;
-  if (stored && !tmap_internal(&tS, ws + lucid_solve_bwd_workspace_bytes(B, H, N, D), B, H, (int)(npair * 128)))
-    return LUCID_ERR_TENSORMAP;
   BwdArgs ba{};
   ba.B = B; ba.Hq = H; ba.Hkv = H; ba.N = N; ba.NB = NB; ba.Npad = Npad;
   ba.scale = scale;
@@ -330,15 +325,16 @@ int lucid_solve_bwd(int B, int H, int N, int D, float scale, const void* k, int6
   ba.flags = flags;
   ba.status = status;
   ba.store_tiles = stored ? 1 : 0;
+  ba.tiles = stored ? reinterpret_cast<bf16*>(ws + lucid_solve_bwd_workspace_bytes(B, H, N, D)) : nullptr;
   cudaError_t e;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, tS, ba, st);
+    e = launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD_ROW, st);
-    e = stored ? launch_bwd_row_stored(true, tS, tK, ba, st) : launch_bwd_row(true, tK, tDV, tK, tX, ba, st);
+    e = stored ? launch_bwd_row_stored(true, tK, ba, st) : launch_bwd_row(true, tK, tDV, tK, tX, ba, st);
   }
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
   return to_status(launch_solve_finalize(
@@ -523,7 +519,7 @@ extern "C" int lucid_cp_attn_bwd(int B, int Hq, int Hkv, int N, int D, float sca
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (passes & 1) {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD, st);
-    if (launch_bwd_col(false, tK, tX, tQ, tDO, tX, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    if (launch_bwd_col(false, tK, tX, tQ, tDO, tX, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
   if (passes & 2) {
     ProfileScope ps(LUCID_KERNEL_ATTN_BWD_ROW, st);
@@ -563,7 +559,7 @@ extern "C" int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int b
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (passes & 1) {
     ProfileScope ps(LUCID_KERNEL_SOLVE_BWD, st);
-    if (launch_bwd_col(true, tK, tX, tK, tDV, tU, tU, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
+    if (launch_bwd_col(true, tK, tX, tK, tDV, tU, ba, st) != cudaSuccess) return LUCID_ERR_LAUNCH;
   }
   if (passes & 2) {
     {

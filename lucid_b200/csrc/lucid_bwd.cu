@@ -69,6 +69,40 @@ __device__ __forceinline__ uint32_t packed_kslice(uint32_t region, int kk) {
   return region + 64u * (uint32_t)(kk >> 2) + 32u * (uint32_t)((kk >> 1) & 1) + 8u * (uint32_t)(kk & 1);
 }
 
+// Stored-tile layout (the stored-tile schedule): a packed bf16 dS^T / dG^T tile (rows =
+// keys / column block, columns = queries / row block) is 16 "pieces" of 8 columns; piece
+// p holds its 8 columns of all 128 rows as 16-byte rows, so element (r, c) sits at
+// ((c / 8) * 128 + r) * 8 + c % 8.  The column pass writes it straight from registers:
+// for one piece, the 32 threads of a warp (consecutive rows) store 512 contiguous bytes.
+// The row pass copies a tile into shared memory unchanged (one bulk copy) and reads it
+// as a non-swizzled MN-major operand: 8-row x 16-byte core matrices, 128 bytes apart
+// along K (rows), 2048 bytes apart along M (pieces).
+constexpr int kPieceElems = 128 * 8;
+__device__ __forceinline__ void store_tile_pieces(bf16* tile, int r, int chunk, const uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    __stcs(reinterpret_cast<uint4*>(tile + (4 * chunk + c) * kPieceElems + r * 8),
+           make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
+}
+__device__ __forceinline__ uint64_t desc_pieces(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(128u >> 4) << 16;   // leading byte offset: next 8 rows (K)
+  d |= (uint64_t)(2048u >> 4) << 32;  // stride byte offset: next piece (M)
+  d |= (uint64_t)1u << 46;            // descriptor version; no swizzle
+  return d;
+}
+// D (+)= A B over a 128x128x128 product, A a stored tile in the piece layout (MN-major,
+// K-slice kk = rows 16 kk .. 16 kk + 15) and B a swizzled MN-major tile.
+__device__ __forceinline__ void umma_tile_pieces(uint32_t d_tmem, uint32_t a_tile, uint32_t b_tile,
+                                                 uint32_t accumulate_first) {
+  const uint32_t idesc = idesc_bf16(128, 128, true, true);
+  const uint64_t a0 = desc_pieces(a_tile), b0 = desc_tile(b_tile, true);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_ss(d_tmem, a0 + (uint64_t)(kk * 16), desc_slice(b0, true, kk), idesc, (kk > 0) ? 1u : accumulate_first);
+}
+
 constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdEpiThreads = kBwdEpiWarps * 32;
 constexpr int kBwdThreads = kBwdEpiThreads + 128;  // + control warpgroup (TMA, MMA, 2 idle warps)
@@ -87,17 +121,17 @@ constexpr uint32_t kOffVec = 229376;         // stage s: lse[128], delta[128] at
 constexpr uint32_t kOffBar = kOffVec + 2048;
 enum {
   A_FULL = 0, A_EMPTY, KV_FULL0, KV_FULL1, KV_EMPTY0, KV_EMPTY1, SD_FULL, DP_FULL, PD_FULL, DS_FREE,
-  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, STG_READY, STG_FREE, DSP_FULL, NBAR
+  T_FULL, S_FREE, ACC_FULL, ACC2_FULL, ACC_FREE, EPI_DONE, DRAIN, DSP_FULL, NBAR
 };
 constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS = 0, kTmDP = 128, kTmAcc1 = 256, kTmAcc2 = 384;
 // 16 epilogue warps (four per TMEM sub-partition, one 32-column chunk of the tile
 // each) so that every scheduler has four epilogue warps to hide the latencies of the
-// TMEM loads, exponentials and stores; warps 16-19: TMA, MMA, tile store, idle.
+// TMEM loads, exponentials and stores; warps 16-19: TMA, MMA, two idle.
 constexpr int kColEpiWarps = 16, kColQ = 4 * 4 / kColEpiWarps;
 constexpr int kColEpiThreads = kColEpiWarps * 32;
 constexpr int kColThreads = kColEpiThreads + 128;
-constexpr int kColWarpTma = kColEpiWarps, kColWarpMma = kColEpiWarps + 1, kColWarpStore = kColEpiWarps + 2;
+constexpr int kColWarpTma = kColEpiWarps, kColWarpMma = kColEpiWarps + 1;
 // register split: 640 x 96 at launch >= 512 x 96 + 128 x 88
 constexpr int kColRegsEpi = 96, kColRegsCtl = 88;
 static_assert(kColEpiThreads * kColRegsEpi + 128 * kColRegsCtl <= kColThreads * (65536 / kColThreads / 8 * 8),
@@ -108,8 +142,7 @@ template <bool SOLVE, bool DIAG>
 __global__ void __launch_bounds__(bwdc::kColThreads, 1)
     lucid_bwd_col_kernel(const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmA2,
                          const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
-                         const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmS,
-                         BwdArgs p) {
+                         const __grid_constant__ CUtensorMap tmU, BwdArgs p) {
   using namespace bwdc;
   static_assert(!(SOLVE && DIAG), "the diagonal launch is the attention's");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -147,8 +180,6 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
     mbar_init(bar(ACC_FREE), kColEpiThreads);
     mbar_init(bar(EPI_DONE), kColEpiThreads);
     mbar_init(bar(DRAIN), 1);
-    mbar_init(bar(STG_READY), kColEpiThreads);
-    mbar_init(bar(STG_FREE), 1);
     *abort_cta = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA1);
@@ -358,36 +389,6 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       umma_commit(bar(DRAIN));
       mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
     }
-  } else if (warp == kColWarpStore && p.store_tiles != 0) {
-    // ============ tile store (stored-tile schedule) ============
-    // per tile: once the 256 epilogue threads staged the packed tile (attention dS^T of
-    // key block i, query block j >= i: pair j (j + 1) / 2 + i of query head hk G + g;
-    // solve dG^T of column block i, row block j > i: pair j (j - 1) / 2 + i of head hk),
-    // store it (evict-first: it is read once) and free the staging tile as soon as the
-    // store has read it
-    if (lane == 0) {
-      Ph stg_ready;
-      bool ok = true;
-      const uint64_t pol = l2_policy_evict_first();
-      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
-        int i, b, hk;
-        decode(idx, i, b, hk);
-        const int T = ntiles(i);
-        for (int t = 0; t < T; ++t) {
-          int g, j;
-          tile_at(i, t, g, j);
-          if (!mbar_wait(bar(STG_READY), stg_ready.full(), ab)) { ok = false; break; }
-          if (SOLVE)
-            tma_store_tile_hint(&tmS, sDS, (j * (j - 1) / 2 + i) * 128, hk, b, pol);
-          else
-            tma_store_tile_hint(&tmS, sDS, (j * (j + 1) / 2 + i) * 128, hk * G + g, b, pol);
-          bulk_commit();
-          bulk_wait_read_all();
-          mbar_arrive(bar(STG_FREE));
-        }
-      }
-      bulk_wait_all();
-    }
   }
   } else {
     regs_inc<kColRegsEpi>();
@@ -404,13 +405,14 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
     Ph sd_full, dp_full, ds_free, t_full, acc_full, acc2_full;
     uint32_t n_kv = 0, item = 0;
     // stored-tile schedule: every packed dS^T (attention) / dG^T (solve) tile also goes
-    // to global memory through the sDS tile, stored by warp kColWarpStore.  n_st counts
-    // the tiles staged so far; the staging tile is free for tile n_st once STG_FREE has
-    // completed n_st times (the solve's diagonal steps also use sDS: they wait for the
-    // item's last store, and an item's first staged tile waits for the previous item's
-    // last diagonal MMA in place of its first diagonal step)
+    // to global memory, straight from the registers, in the piece layout: attention
+    // tile (key block i, query block j >= i) of query head hq at pair j (j + 1) / 2 + i
+    // of that head's NB (NB + 1) / 2 + NB tiles (the last NB: the diagonal blocks' lo
+    // parts); solve tile (column block i, row block j > i) at j (j - 1) / 2 + i of the
+    // head's NB (NB - 1) / 2
     const bool stage = p.store_tiles != 0;
-    uint32_t n_st = 0;
+    const long long tiles_per_head = SOLVE ? (long long)p.NB * (p.NB - 1) / 2
+                                           : (long long)p.NB * (p.NB + 1) / 2 + p.NB;
     for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
       int i, b, hk;
       decode(idx, i, b, hk);
@@ -489,9 +491,11 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
 #pragma unroll
         for (int q = 0; q < kColQ; ++q) tmem_ld32(tmem + lane_base + kTmDP + c0 + 32u * q, dv[q]);
         tmem_ld_wait();
+        bf16* tile_out = nullptr;
         if (stage) {
-          if (n_st > 0 && !warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) { ok = false; break; }
-          if (SOLVE && t == 0 && !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) { ok = false; break; }
+          const long long head = SOLVE ? (long long)b * p.Hkv + hk : (long long)b * p.Hq + hk * G + g;
+          const long long pair = SOLVE ? (long long)j * (j - 1) / 2 + i : (long long)j * (j + 1) / 2 + i;
+          tile_out = p.tiles + (head * tiles_per_head + pair) * (long long)kTileBytes / 2;
         }
 #pragma unroll
         for (int q = 0; q < kColQ; ++q) {
@@ -515,14 +519,14 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
             }
           }
           tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q, dk);
-          if (stage) tile_store_row32_packed(sDS, r, ch0 + q, dk);
+          if (stage) store_tile_pieces(tile_out, r, ch0 + q, dk);
         }
         if constexpr (DIAG) {
           // lo part of dS: into the dP region's second-operand columns and, in the
           // stored-tile schedule, straight to its residual tile (row r of key block i)
-          const long long npair = (long long)p.NB * (p.NB + 1) / 2;
-          bf16* lo_row = p.tiles + (((long long)b * p.Hq + hk * G + g) * (npair + p.NB) * 128 + (npair + i) * 128 + r) *
-                                       kHeadDim;
+          bf16* lo_tile = stage ? tile_out + ((long long)p.NB * (p.NB + 1) / 2 + i - ((long long)j * (j + 1) / 2 + i)) *
+                                                (long long)kTileBytes / 2
+                                : nullptr;
 #pragma unroll
           for (int q = 0; q < kColQ; ++q) {
             const int cb = (int)c0 + 32 * q;
@@ -535,21 +539,12 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
               dl[e >> 1] = pack_bf16_lo(ds.x, ds.y);
             }
             tmem_st16(tmem + lane_base + kTmDP + c0 + 32u * q + 16u, dl);
-            if (stage) {
-              uint4* d4 = reinterpret_cast<uint4*>(lo_row + cb);
-#pragma unroll
-              for (int c = 0; c < 4; ++c) d4[c] = make_uint4(dl[4 * c], dl[4 * c + 1], dl[4 * c + 2], dl[4 * c + 3]);
-            }
+            if (stage) store_tile_pieces(lo_tile, r, ch0 + q, dl);
           }
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(DSP_FULL));
-        if (stage) {
-          fence_proxy_async_smem();
-          mbar_arrive(bar(STG_READY));
-          ++n_st;
-        }
       }
       if (!ok) break;
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
@@ -613,12 +608,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
           rr[q][4 * c + 3] = x4.w - a1[4 * c + 3];
         }
       }
-      if (stage && T > 0) {
-        // the item's staged tiles: wait for the last store's read of sDS
-        if (!warp_wait_b(bar(STG_FREE), (n_st - 1) & 1, ab)) break;
-      } else if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) {
-        break;
-      }
+      if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) break;
 #pragma unroll
       for (int q = 0; q < kColQ; ++q) tile_store_row32(sDS, r, ch0 + q, rr[q]);
       fence_proxy_async_smem();
@@ -1044,8 +1034,7 @@ constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 
 template <bool SOLVE>
 __global__ void __launch_bounds__(bwds::kThreads, 1)
-    lucid_bwd_row_stored_kernel(const __grid_constant__ CUtensorMap tmT, const __grid_constant__ CUtensorMap tmB,
-                                BwdArgs p) {
+    lucid_bwd_row_stored_kernel(const __grid_constant__ CUtensorMap tmB, BwdArgs p) {
   using namespace bwds;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -1073,7 +1062,6 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmT);
     tma_prefetch_desc(&tmB);
   }
   if (warp == 5) {
@@ -1102,6 +1090,8 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
   auto pair0 = [&](int j) { return SOLVE ? j * (j - 1) / 2 : j * (j + 1) / 2; };
   auto tile_idx = [&](int j, int t) { return (SOLVE || t <= j) ? pair0(j) + t : p.NB * (p.NB + 1) / 2 + j; };
   auto key_blk = [&](int j, int t) { return (SOLVE || t <= j) ? t : j; };
+  const long long tiles_per_head = SOLVE ? (long long)p.NB * (p.NB - 1) / 2 : (long long)p.NB * (p.NB + 1) / 2 + p.NB;
+  auto bha_of = [&](int b, int ha) { return (long long)b * (SOLVE ? p.Hkv : p.Hq) + ha; };
 
   if (warp == 4) {
     // ======================= TMA producer =======================
@@ -1110,7 +1100,6 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
       int last[kStages];
       for (int s2 = 0; s2 < kStages; ++s2) last[s2] = -1;
       bool ok = true;
-      const uint64_t pol = l2_policy_evict_first();   // each stored tile is read once
       for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x) {
         int j, b, ha, hk;
         decode(idx, j, b, ha, hk);
@@ -1120,7 +1109,8 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
           if (!mbar_wait(bar(EMPTY0 + st), (use & 1) ^ 1, ab)) { ok = false; break; }
           last[st] = use & 1;
           mbar_arrive_expect_tx(bar(FULL0 + st), 65536);
-          tma_load_tile_hint(sT(n), &tmT, bar(FULL0 + st), tile_idx(j, t) * 128, ha, b, pol);
+          bulk_load(sT(n), p.tiles + (bha_of(b, ha) * tiles_per_head + tile_idx(j, t)) * (long long)kTileBytes / 2,
+                    (uint32_t)kTileBytes, bar(FULL0 + st));
           tma_load_tile(sB(n), &tmB, bar(FULL0 + st), key_blk(j, t) * 128, hk, b);
         }
       }
@@ -1143,7 +1133,7 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
           const uint32_t st = n % kStages;
           if (!mbar_wait(bar(FULL0 + st), (n / kStages) & 1, ab)) { ok = false; break; }
           tc_fence_after();
-          umma_tile(tmem + 128u * ab2, sT(n), true, sB(n), true, t > 0 ? 1u : 0u);
+          umma_tile_pieces(tmem + 128u * ab2, sT(n), sB(n), t > 0 ? 1u : 0u);
           umma_commit(bar(EMPTY0 + st));
         }
         if (!ok) break;
@@ -1332,7 +1322,7 @@ static cudaError_t set_smem(K kernel, uint32_t bytes) {
 }
 
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
-                           const CUtensorMap& tB2, const CUtensorMap& tU, const CUtensorMap& tS, const BwdArgs& a,
+                           const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a,
                            cudaStream_t st) {
   const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
   const int total = nblk * a.B * a.Hkv;
@@ -1343,14 +1333,14 @@ cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap
     if ((e = set_smem(lucid_bwd_col_kernel<true, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
     // the transposed solve's CTAs wait on one another's flags: all of them must be resident
     return launch_cooperative(lucid_bwd_col_kernel<true, false>, grid, bwdc::kColThreads, bwdc::kSmemBytes, st, tA1,
-                              tA2, tB1, tB2, tU, tS, a);
+                              tA2, tB1, tB2, tU, a);
   } else {
     // off-diagonal tiles, then the diagonal tiles (which add to dX, dK)
     if ((e = set_smem(lucid_bwd_col_kernel<false, false>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false, false><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    lucid_bwd_col_kernel<false, false><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = set_smem(lucid_bwd_col_kernel<false, true>, bwdc::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_col_kernel<false, true><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, tS, a);
+    lucid_bwd_col_kernel<false, true><<<grid, bwdc::kColThreads, bwdc::kSmemBytes, st>>>(tA1, tA2, tB1, tB2, tU, a);
   }
   return cudaGetLastError();
 }
@@ -1373,7 +1363,7 @@ cudaError_t launch_bwd_row(bool solve, const CUtensorMap& tA1, const CUtensorMap
 }
 
 // Row pass of the stored-tile schedule: tT = the stored tiles, tB = K (attention) / K^ (solve).
-cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUtensorMap& tB, const BwdArgs& a,
+cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tB, const BwdArgs& a,
                                   cudaStream_t st) {
   const int nblk = (a.blk1 > 0 ? a.blk1 : a.NB) - a.blk0;
   const int total = nblk * a.B * (solve ? a.Hkv : a.Hq);
@@ -1382,10 +1372,10 @@ cudaError_t launch_bwd_row_stored(bool solve, const CUtensorMap& tT, const CUten
   cudaError_t e;
   if (solve) {
     if ((e = set_smem(lucid_bwd_row_stored_kernel<true>, bwds::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_row_stored_kernel<true><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tT, tB, a);
+    lucid_bwd_row_stored_kernel<true><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tB, a);
   } else {
     if ((e = set_smem(lucid_bwd_row_stored_kernel<false>, bwds::kSmemBytes)) != cudaSuccess) return e;
-    lucid_bwd_row_stored_kernel<false><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tT, tB, a);
+    lucid_bwd_row_stored_kernel<false><<<grid, bwds::kThreads, bwds::kSmemBytes, st>>>(tB, a);
   }
   return cudaGetLastError();
 }

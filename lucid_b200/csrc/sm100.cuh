@@ -407,16 +407,26 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool 
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Descriptor of K-slice kk from the slice-0 descriptor of the same tile: only the
+// start-address field (bits 0-13, byte address >> 4) moves, by the slice's byte offset
+// >> 4.  Tiles are 1024-byte aligned and shared memory ends below 256 KB, so the field
+// never carries into the next one.  One add per slice keeps the single MMA-issuing
+// thread's instruction count low (it shares its scheduler with epilogue warps).
+__device__ __forceinline__ uint64_t desc_slice(uint64_t d0, bool mn, int kk) {
+  return d0 + (uint64_t)(mn ? kk * 128 : (kk >> 2) * 1024 + (kk & 3) * 2);
+}
+__device__ __forceinline__ uint64_t desc_tile(uint32_t tile, bool mn) {
+  return mn ? desc_mnmajor(tile, 0) : desc_kmajor(tile, 0);
+}
+
 // Issue the 8 K-slices of a 128x128x128 product.
 __device__ __forceinline__ void umma_tile(uint32_t d_tmem, uint32_t a_tile, bool a_mn,
                                           uint32_t b_tile, bool b_mn, uint32_t accumulate_first) {
   const uint32_t idesc = idesc_bf16(128, 128, a_mn, b_mn);
+  const uint64_t a0 = desc_tile(a_tile, a_mn), b0 = desc_tile(b_tile, b_mn);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint64_t ad = a_mn ? desc_mnmajor(a_tile, kk) : desc_kmajor(a_tile, kk);
-    const uint64_t bd = b_mn ? desc_mnmajor(b_tile, kk) : desc_kmajor(b_tile, kk);
-    umma_ss(d_tmem, ad, bd, idesc, (kk > 0) ? 1u : accumulate_first);
-  }
+  for (int kk = 0; kk < 8; ++kk)
+    umma_ss(d_tmem, desc_slice(a0, a_mn, kk), desc_slice(b0, b_mn, kk), idesc, (kk > 0) ? 1u : accumulate_first);
 }
 
 // The 8 K-slices of a 128x128x128 product whose A operand lives in TMEM.
@@ -425,11 +435,10 @@ template <typename AddrFn>
 __device__ __forceinline__ void umma_tile_ts(uint32_t d_tmem, AddrFn a_tmem, uint32_t b_tile, bool b_mn,
                                              uint32_t accumulate_first) {
   const uint32_t idesc = idesc_bf16(128, 128, false, b_mn);
+  const uint64_t b0 = desc_tile(b_tile, b_mn);
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint64_t bd = b_mn ? desc_mnmajor(b_tile, kk) : desc_kmajor(b_tile, kk);
-    umma_ts(d_tmem, a_tmem(kk), bd, idesc, (kk > 0) ? 1u : accumulate_first);
-  }
+  for (int kk = 0; kk < 8; ++kk)
+    umma_ts(d_tmem, a_tmem(kk), desc_slice(b0, b_mn, kk), idesc, (kk > 0) ? 1u : accumulate_first);
 }
 
 // ---------------------------------------------------------------------------
