@@ -19,8 +19,9 @@ The kernels are 128 wide; a smaller head dimension is zero-padded to 128 and
 the outputs sliced back, which is exact: with zero columns in w every
 Householder H_t acts as the identity on them, so q, k and v stay zero there
 and the scores are unchanged.  ``g`` must be None (the reference asserts the
-same, :235).  ``cu_seqlens`` (packed variable-length batches, B == 1) runs
-one call per sequence.
+same, :235).  ``cu_seqlens`` (packed variable-length batches, B == 1) runs the
+sequences with the same number of 128-token blocks as one batch, each zero-padded
+at its end (exact for the real tokens; see _varlen).
 """
 from __future__ import annotations
 
@@ -197,16 +198,50 @@ def parallel_lucid_path_attention(k, v, w, beta, q=None, g=None, scale=None, cu_
         return ParallelLUCIDPathAttentionFunction.apply(q, k, v, w, beta, None, float(scale), None, bool(use_cache))
     if k.shape[0] != 1:
         raise PathArgumentError("cu_seqlens requires a packed batch of size 1")
-    bounds = [int(x) for x in cu_seqlens.tolist()]
-    outs, caches = [], []
-    for a, b in zip(bounds[:-1], bounds[1:]):
-        qa = q[:, a:b] if q is not k else None
-        ka = k[:, a:b]
-        o, kc = ParallelLUCIDPathAttentionFunction.apply(qa if qa is not None else ka, ka, v[:, a:b], w[:, a:b],
-                                                         beta[:, a:b], None, float(scale), None, bool(use_cache))
-        outs.append(o)
-        caches.append(kc)
-    return torch.cat(outs, dim=1), (torch.cat(caches, dim=1) if use_cache else None)
+    return _varlen(q, k, v, w, beta, float(scale), [int(x) for x in cu_seqlens.tolist()], bool(use_cache))
+
+
+def _varlen(q, k, v, w, beta, scale, bounds, use_cache):
+    """Packed variable-length sequences (cu_seqlens = bounds): the sequences with the
+    same number of 128-token blocks run as one batch, each zero-padded at its end to
+    that block count (one kernel chain per distinct block count instead of one per
+    sequence).  Zero padding is exact for the real tokens: a padded token has w = 0 and
+    beta = 0 (its Householder is the identity) and comes after every real token of its
+    sequence, so causality keeps it out of their outputs, and with dO = 0 there its dV,
+    and so its share of every gradient, is zero."""
+    T = k.shape[1]
+    dev = k.device
+    lens = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
+    if bounds[0] != 0 or bounds[-1] != T or any(n < 0 for n in lens):
+        raise PathArgumentError("cu_seqlens must rise from 0 to the packed length")
+    groups = {}
+    for s_, n in enumerate(lens):
+        if n > 0:
+            groups.setdefault((n + 127) // 128, []).append(s_)
+    zero_row = lambda t: torch.cat([t[0], t.new_zeros((1,) + tuple(t.shape[2:]))], 0)   # [T + 1, ...]
+    qz = zero_row(q) if q is not k else None
+    kz, vz, wz, bz = zero_row(k), zero_row(v), zero_row(w), zero_row(beta)
+    o_parts, kc_parts, pos = [], [], torch.empty(T, dtype=torch.long)
+    base = 0
+    for nb, seqs in sorted(groups.items()):
+        Tp = nb * 128
+        idx = torch.full((len(seqs), Tp), T, dtype=torch.long)   # T: the appended zero row
+        for r_, s_ in enumerate(seqs):
+            a, n = bounds[s_], lens[s_]
+            idx[r_, :n] = torch.arange(a, a + n)
+            pos[a:a + n] = base + r_ * Tp + torch.arange(n)
+        base += len(seqs) * Tp
+        idx = idx.to(dev)
+        kk = kz[idx]
+        o, kc = ParallelLUCIDPathAttentionFunction.apply(qz[idx] if qz is not None else kk, kk, vz[idx], wz[idx],
+                                                         bz[idx], None, scale, None, use_cache)
+        o_parts.append(o.reshape((-1,) + tuple(o.shape[2:])))
+        if use_cache:
+            kc_parts.append(kc.reshape((-1,) + tuple(kc.shape[2:])))
+    pos = pos.to(dev)
+    o = torch.cat(o_parts, 0)[pos].unsqueeze(0)
+    kc = torch.cat(kc_parts, 0)[pos].unsqueeze(0) if use_cache else None
+    return o, kc
 
 
 def parallel_path_attention_fwd(q, k, v, w, beta, scale=None):

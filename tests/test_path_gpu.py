@@ -142,18 +142,34 @@ def test_path_deterministic(cuda_device):
 
 
 def test_path_varlen_matches_separate_sequences(cuda_device):
+    """cu_seqlens: sequences of 150, 250, 100, 300 and 10 tokens (block counts 2, 2, 1, 3
+    and 1, so three batched groups) against one call per sequence: o, the key cache and
+    every gradient."""
     torch = pytest.importorskip("torch")
     from lucid_b200.path import parallel_lucid_path_attention
     from oracle.path_oracle import make_path_inputs
-    d = make_path_inputs(21, 1, 400, 1, 128)
+    bounds = [0, 150, 400, 500, 800, 810]
+    d = make_path_inputs(21, 1, bounds[-1], 2, 128)
     dev = cuda_device
-    k, v, w, beta = (_to(torch, d[n], dev) for n in ("k", "v", "w", "beta"))
-    cu = torch.tensor([0, 150, 400], dtype=torch.int32, device=dev)
-    with torch.no_grad():
-        o, _ = parallel_lucid_path_attention(k, v, w, beta, cu_seqlens=cu, scale=0.15)
-        o_a, _ = parallel_lucid_path_attention(k[:, :150], v[:, :150], w[:, :150], beta[:, :150], scale=0.15)
-        o_b, _ = parallel_lucid_path_attention(k[:, 150:], v[:, 150:], w[:, 150:], beta[:, 150:], scale=0.15)
-    torch.testing.assert_close(o, torch.cat([o_a, o_b], 1), rtol=0, atol=0)
+    base = [_to(torch, d[n], dev) for n in ("k", "v", "w", "beta")]
+    do = _to(torch, d["do"], dev)
+
+    def run(sl):
+        leaves = [t[:, sl].clone().requires_grad_(True) for t in base]
+        return leaves
+
+    cu = torch.tensor(bounds, dtype=torch.int32, device=dev)
+    packed = run(slice(None))
+    o, kc = parallel_lucid_path_attention(*packed, cu_seqlens=cu, scale=0.15, use_cache=True)
+    o.backward(do)
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        sep = run(slice(a, b))
+        o_s, kc_s = parallel_lucid_path_attention(*sep, scale=0.15, use_cache=True)
+        o_s.backward(do[:, a:b])
+        torch.testing.assert_close(o[:, a:b], o_s, rtol=0, atol=0)
+        torch.testing.assert_close(kc[:, a:b], kc_s, rtol=0, atol=0)
+        for t_p, t_s in zip(packed, sep):
+            torch.testing.assert_close(t_p.grad[:, a:b], t_s.grad, rtol=0, atol=0)
 
 
 def _attn(torch, d, dev, scale=None):
