@@ -25,12 +25,14 @@ at its end (exact for the real tokens; see _varlen).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
 
 __all__ = ["parallel_lucid_path_attention", "ParallelLUCIDPathAttentionFunction", "path_fwd", "path_bwd",
-           "parallel_path_attention_fwd", "PathArgumentError"]
+           "parallel_path_attention_fwd", "path_memory_groups", "PathArgumentError"]
 
 
 class PathArgumentError(ValueError, AssertionError):
@@ -132,27 +134,92 @@ def path_bwd(state, do, k, w, beta, q=None, scale=None):
     return dq, dk, dv, dw, dbeta
 
 
+def path_memory_groups(B: int, T: int, H: int, HQ: int, device, budget: int | None = None):
+    """The (batch, kv-head) slices the op runs at once.  The forward's saved state and the
+    backward's workspace hold O(T^2) block-pair tiles per (batch, query head) (about
+    4 x 32 KB per pair of 128-row blocks); when the whole batch's tiles do not fit in
+    ``budget`` bytes (default: half of what this process can still allocate;
+    LUCID_B200_PATH_MAX_BYTES overrides), the op runs kv-head groups one after another
+    and the backward recomputes each group's forward, so memory is bounded by one
+    group.  Returns a list of (b0, b1, h0, h1) kv-head slices; raises if a single kv
+    head does not fit."""
+    lib = _lib.load()
+    per = lambda b, h: (lib.lucid_path_fwd_workspace_bytes(b, T, h, h * (HQ // H), 128) +
+                        lib.lucid_path_bwd_workspace_bytes(b, T, h, h * (HQ // H), 128))
+    if budget is None:
+        env = os.environ.get("LUCID_B200_PATH_MAX_BYTES")
+        if env is not None:
+            budget = int(env)
+        else:
+            free, _ = torch.cuda.mem_get_info(device)
+            budget = int(0.5 * (free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)))
+    if per(B, H) <= budget:
+        return [(0, B, 0, H)]
+    if per(1, 1) > budget:
+        raise _lib.LucidError(f"LUCID-Path at T={T}: one head needs {per(1, 1) / 2**30:.1f} GiB of block-pair "
+                              f"workspace, more than the {budget / 2**30:.1f} GiB available")
+    hg = max(h for h in range(1, H + 1) if H % h == 0 and per(1, h) <= budget)
+    return [(b, b + 1, h0, h0 + hg) for b in range(B) for h0 in range(0, H, hg)]
+
+
 class ParallelLUCIDPathAttentionFunction(torch.autograd.Function):
-    """Autograd mirror of parallel.py:27-177 (same positional arguments)."""
+    """Autograd mirror of parallel.py:27-177 (same positional arguments).  When the
+    block-pair workspace of the whole batch does not fit (path_memory_groups), kv-head
+    groups run one after another and the backward recomputes each group's forward."""
 
     @staticmethod
     def forward(ctx, q, k, v, w, beta, g, scale, cu_seqlens, use_cache=False):
         if g is not None:
             raise NotImplementedError("g is not supported (the reference asserts g is None)")
         q_given = q is not None and q is not k
-        o, state, kc = path_fwd(k, v, w, beta, q=q if q_given else None, scale=scale, use_cache=use_cache)
-        ctx.save_for_backward(q if q_given else None, k, w, beta, state)
+        _prep(k, "k")   # CPU tensors raise here, before any device query
+        B, T, H, _ = k.shape
+        HQ = q.shape[2] if q_given else H
+        groups = path_memory_groups(B, T, H, HQ, k.device)
         ctx.q_given = q_given
         ctx.q_is_k = q is k
         ctx.scale = scale
+        ctx.groups = groups
+        if len(groups) == 1:
+            o, state, kc = path_fwd(k, v, w, beta, q=q if q_given else None, scale=scale, use_cache=use_cache)
+            ctx.save_for_backward(q if q_given else None, k, v, w, beta, state)
+        else:
+            G = HQ // H
+            o = torch.empty(B, T, HQ, v.shape[-1], dtype=v.dtype, device=k.device)
+            kc = torch.empty_like(k) if use_cache else None
+            for b0, b1, h0, h1 in groups:
+                sl, slq = (slice(b0, b1), slice(None), slice(h0, h1)), (slice(b0, b1), slice(None), slice(h0 * G, h1 * G))
+                og, _, kcg = path_fwd(k[sl], v[sl], w[sl], beta[sl], q=q[slq] if q_given else None, scale=scale,
+                                      use_cache=use_cache)
+                o[slq] = og
+                if use_cache:
+                    kc[sl] = kcg
+                del og, kcg
+            ctx.save_for_backward(q if q_given else None, k, v, w, beta, None)
         if kc is not None:
             ctx.mark_non_differentiable(kc)
         return o, kc
 
     @staticmethod
     def backward(ctx, do, dk_cache):
-        q, k, w, beta, state = ctx.saved_tensors
-        dq, dk, dv, dw, dbeta = path_bwd(state, do, k, w, beta, q=q, scale=ctx.scale)
+        q, k, v, w, beta, state = ctx.saved_tensors
+        if len(ctx.groups) == 1:
+            dq, dk, dv, dw, dbeta = path_bwd(state, do, k, w, beta, q=q, scale=ctx.scale)
+        else:
+            H, HQ = k.shape[2], (q.shape[2] if q is not None else k.shape[2])
+            G = HQ // H
+            dq = torch.empty_like(q) if q is not None else None
+            dk, dv, dw = torch.empty_like(k), torch.empty_like(v), torch.empty_like(w)
+            dbeta = torch.empty_like(beta)
+            for b0, b1, h0, h1 in ctx.groups:
+                sl, slq = (slice(b0, b1), slice(None), slice(h0, h1)), (slice(b0, b1), slice(None), slice(h0 * G, h1 * G))
+                qg = q[slq] if q is not None else None
+                _, st, _ = path_fwd(k[sl], v[sl], w[sl], beta[sl], q=qg, scale=ctx.scale)   # recompute the state
+                r = path_bwd(st, do[slq], k[sl], w[sl], beta[sl], q=qg, scale=ctx.scale)
+                del st
+                if dq is not None:
+                    dq[slq] = r[0]
+                dk[sl], dv[sl], dw[sl], dbeta[sl] = r[1], r[2], r[3], r[4]
         if ctx.q_is_k:
             # q and k are the same tensor: the reference returns dq and dk
             # separately and autograd sums them; dk already holds the sum.

@@ -58,3 +58,21 @@ def test_cpu_tensors_raise_without_fallback(K):
         parallel_lucid_path_attention(k, v, w, beta)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         parallel_path_attention_fwd(None, k, v, w, beta)
+
+
+def test_path_memory_groups_split_by_kv_head():
+    """Group selection of the bounded-memory LUCID-Path schedule (workspace sizes from
+    the C ABI, no GPU needed): the whole batch when it fits, else the largest kv-head
+    group that fits, and a clear error when one head does not."""
+    pytest.importorskip("torch")
+    from lucid_b200 import _lib
+    from lucid_b200.path import path_memory_groups
+    lib = _lib.load()
+    per = lambda b, h: (lib.lucid_path_fwd_workspace_bytes(b, 1000, h, 2 * h, 128)
+                        + lib.lucid_path_bwd_workspace_bytes(b, 1000, h, 2 * h, 128))
+    assert path_memory_groups(2, 1000, 4, 8, None, budget=per(2, 4)) == [(0, 2, 0, 4)]
+    assert path_memory_groups(2, 1000, 4, 8, None, budget=per(1, 2)) == [(0, 1, 0, 2), (0, 1, 2, 4),
+                                                                         (1, 2, 0, 2), (1, 2, 2, 4)]
+    assert len(path_memory_groups(2, 1000, 4, 8, None, budget=per(1, 1))) == 8
+    with pytest.raises(_lib.LucidError):
+        path_memory_groups(2, 1000, 4, 8, None, budget=per(1, 1) - 1)

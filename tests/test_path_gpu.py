@@ -211,3 +211,34 @@ def test_path_attention_matches_oracle(cuda_device, B, T, H, HQ, with_q, scale):
     assert np.all(np.isfinite(o))
     assert dev <= max(1.5 * ref_dev, 1e-2), (dev, ref_dev)
     assert np.abs(lse - rl).max() < 2e-2
+
+
+def test_path_head_groups_match_whole_batch(cuda_device, monkeypatch):
+    """The bounded-memory schedule (kv-head groups one after another, the backward
+    recomputing each group's forward) against the whole-batch call: o, the key cache
+    and every gradient bit-identical (B2, 2 kv heads, 4 query heads, explicit q)."""
+    torch = pytest.importorskip("torch")
+    from lucid_b200 import _lib
+    from lucid_b200.path import parallel_lucid_path_attention, path_memory_groups
+    from oracle.path_oracle import make_path_inputs
+    d = make_path_inputs(33, 2, 300, 2, 128, 4, True)
+    dev = cuda_device
+    base = [_to(torch, d[n], dev) for n in ("q", "k", "v", "w", "beta")]
+    do = _to(torch, d["do"], dev)
+
+    def run():
+        leaves = [t.clone().requires_grad_(True) for t in base]
+        o, kc = parallel_lucid_path_attention(leaves[1], leaves[2], leaves[3], leaves[4], q=leaves[0],
+                                              use_cache=True)
+        o.backward(do)
+        torch.cuda.synchronize()
+        return [o, kc] + [t.grad for t in leaves]
+
+    whole = run()
+    lib = _lib.load()
+    one_head = lib.lucid_path_fwd_workspace_bytes(1, 300, 1, 2, 128) + lib.lucid_path_bwd_workspace_bytes(1, 300, 1, 2, 128)
+    monkeypatch.setenv("LUCID_B200_PATH_MAX_BYTES", str(one_head))
+    assert len(path_memory_groups(2, 300, 2, 4, dev)) == 4
+    grouped = run()
+    for a, b in zip(whole, grouped):
+        torch.testing.assert_close(a, b, rtol=0, atol=0)
