@@ -420,6 +420,11 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       const long long bhk = (long long)b * p.Hkv + hk;
       const int row_i = i * 128 + r;
       bool ok = true;
+      if (SOLVE) {
+        // the diagonal step reads this row's dX (fp32, this warp's 32 columns) on the
+        // wavefront's critical path: fetch it into L2 while the column's tiles run
+        prefetch_l2(p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0);
+      }
       for (int t = 0; t < T; ++t, ++n_kv) {
         int g, j;
         tile_at(i, t, g, j);
@@ -636,10 +641,12 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(bar(PD_FULL));
       fence_proxy_async_global();
-      __threadfence();
       mbar_arrive(bar(EPI_DONE));
-      if (threadIdx.x == 0) {
-        if (mbar_wait(bar(EPI_DONE), item & 1, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+      if (threadIdx.x == 0) {   // publish: the CTA's dV rows, then the flag (one fence, cumulative)
+        if (mbar_wait(bar(EPI_DONE), item & 1, ab)) {
+          __threadfence();
+          st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+        }
       }
       __syncwarp();
       // D5: dG^T of the strictly-lower part of P_ii -> smem tile

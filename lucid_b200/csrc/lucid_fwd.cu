@@ -321,6 +321,13 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       const int row = i * 128 + r;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
+      if (SOLVE && row < p.N) {
+        // the diagonal step reads this row of V on the wavefront's critical path: fetch
+        // it into L2 while the row's streaming tiles run
+        const bf16* vrow = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh + (long long)row * p.v_sn;
+        prefetch_l2(vrow);
+        prefetch_l2(vrow + 64);
+      }
       for (int t = 0; t < nk; ++t, ++n_p) {
         if (!warp_wait(bar(S_FULL0 + k), (n_sfull++) & 1, ab)) { ok = false; break; }
         tc_fence_after();
@@ -486,10 +493,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       }
       tc_fence_before();
       fence_proxy_async_global();
-      __threadfence();
       mbar_arrive(bar(EPI_DONE0 + k));
-      if ((int)threadIdx.x == wg_thread0) {
-        if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+      if ((int)threadIdx.x == wg_thread0) {   // publish: the rows of X, then the flag (one fence, cumulative)
+        if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) {
+          __threadfence();
+          st_release_gpu(&p.flags[bhk * p.NB + i], 1);
+        }
       }
       ++n_epi;
       __syncwarp();

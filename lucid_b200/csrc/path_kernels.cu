@@ -560,10 +560,12 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       if (!TR && p.out != nullptr && t < p.T)
         st_bf16x64(p.out + (long long)b * p.o_sb + (long long)hq * p.o_sh + t * p.o_st + hf * 64, X);
       fence_proxy_async_global();
-      __threadfence();
       mbar_arrive(bar(EPI_DONE));
-      if (threadIdx.x == 0) {
-        if (mbar_wait(bar(EPI_DONE), n_epi & 1, ab)) st_release_gpu(&p.flags[(long long)bhq * p.NB + blk], 1);
+      if (threadIdx.x == 0) {   // publish: the block's rows, then the flag (one fence, cumulative)
+        if (mbar_wait(bar(EPI_DONE), n_epi & 1, ab)) {
+          __threadfence();
+          st_release_gpu(&p.flags[(long long)bhq * p.NB + blk], 1);
+        }
       }
       ++n_epi;
       __syncwarp();

@@ -150,12 +150,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Spin until *flag >= want.  Returns false on timeout / abort.
+// Spin until *flag >= want (one polling thread per CTA; the wavefronts' critical path
+// runs through these waits, so they poll without sleeping).  Returns false on timeout /
+// abort.
 __device__ __forceinline__ bool wait_flag_geq(const int* flag, int want, const Abort& ab) {
   if (ld_acquire_gpu(flag) >= want) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    __nanosleep(64);
     if (ld_acquire_gpu(flag) >= want) return true;
     if (*ab.cta) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -542,6 +543,11 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
   for (int k = DEG - 1; k >= 0; --k) p = fma2(p, f, make_float2(C[k], C[k]));
   return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// Ask L2 to fetch a global line early (no data returned, no register written).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // Load 8 bf16 (16 bytes) from global and widen to fp32.
