@@ -51,6 +51,9 @@ CONFIGS = {
     "small": (1, 8, 4096, 128, 128 ** -0.5),
     "8k": (1, 32, 8192, 128, 128 ** -0.5),   # profiling case (about 1.5 GB on the device)
     "32k-gqa": (1, 32, 32768, 128, 128 ** -0.5),
+    # one rank's share of the 32K job at 8 GPUs (4 of its 32 heads), measured on one GPU:
+    # the stages whose per-head dependency chains set the 8-GPU step time
+    "32k-r8": (1, 4, 32768, 128, 128 ** -0.5),
 }
 # kv heads of the grouped-query configurations (the others are MHA)
 KV_HEADS = {"32k-gqa": 4}

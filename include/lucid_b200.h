@@ -69,6 +69,15 @@ size_t lucid_workspace_status_offset(void);
  *      rstd, dinv internal fp32 [B,H,Npad]                         (saved)
  */
 size_t lucid_solve_fwd_workspace_bytes(int B, int H, int N, int D);
+/* Workspace of the chain schedule: with at least this many bytes (16-byte aligned) the
+ * solve runs each head's diagonal steps in one CTA that keeps its X tiles in shared
+ * memory, while the other CTAs publish the partial row sums, whenever that is faster
+ * on this device (few heads per GPU: their dependency chains, not the GEMM work, set
+ * the time).  Equals lucid_solve_fwd_workspace_bytes when the wavefront schedule is
+ * faster.  Same results up to the fp32 summation order of the row sums.
+ * LUCID_B200_SOLVE_SCHEDULE=chain or =wavefront in the environment forces a schedule
+ * (the size follows). */
+size_t lucid_solve_fwd_fast_workspace_bytes(int B, int H, int N, int D);
 int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps,
                     const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
                     const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,

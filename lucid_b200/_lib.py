@@ -37,6 +37,7 @@ SIGNATURES = {
     "lucid_padded_len": (c_int, [c_int]),
     "lucid_workspace_status_offset": (c_size_t, []),
     "lucid_solve_fwd_workspace_bytes": (c_size_t, [c_int] * 4),
+    "lucid_solve_fwd_fast_workspace_bytes": (c_size_t, [c_int] * 4),
     "lucid_solve_fwd": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3
                         + [c_void_p] * 5 + [c_void_p, c_size_t, c_void_p]),
     "lucid_solve_fwd_noalloc": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3

@@ -10,6 +10,7 @@ namespace lb {
 cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
+int solve_chain_ctas(int BH, int NB);
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a,
                            cudaStream_t st);
@@ -106,6 +107,19 @@ size_t lucid_solve_fwd_workspace_bytes(int B, int H, int N, int D) {
   return kStatusRegion + align256((size_t)B * H * nb_of(N) * sizeof(int));
 }
 
+// Chain schedule's workspace after the minimal one: chain flags, W ring, E tiles.
+static size_t chain_extra_bytes(int B, int H, int N) {
+  const size_t bh = (size_t)B * H, nb = nb_of(N);
+  return align256(bh * nb * sizeof(int)) + bh * kChainWRing * kBlock * kHeadDim * sizeof(float) +
+         bh * nb * kChainLook * (size_t)kTileBytes;
+}
+
+size_t lucid_solve_fwd_fast_workspace_bytes(int B, int H, int N, int D) {
+  const size_t base = lucid_solve_fwd_workspace_bytes(B, H, N, D);
+  if (B <= 0 || H <= 0 || N <= 0 || solve_chain_ctas(B * H, nb_of(N)) == 0) return base;
+  return base + chain_extra_bytes(B, H, N);
+}
+
 int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const void* k, int64_t k_sb,
                     int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
                     void* x, void* khat, void* u, float* rstd, float* dinv, void* workspace,
@@ -122,7 +136,13 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
   const int NB = nb_of(N), Npad = npad_of(N);
   int* status = reinterpret_cast<int*>(workspace);
   int* flags = reinterpret_cast<int*>(static_cast<char*>(workspace) + kStatusRegion);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, lucid_solve_fwd_workspace_bytes(B, H, N, D), st);
+  // chain schedule when the model picks it and the (16-byte aligned) workspace holds its buffers
+  const size_t base = lucid_solve_fwd_workspace_bytes(B, H, N, D);
+  const int nchain = (workspace_bytes >= base + chain_extra_bytes(B, H, N) && aligned16(workspace))
+                         ? solve_chain_ctas(B * H, NB) : 0;
+  char* extra = static_cast<char*>(workspace) + base;
+  const size_t cflag_bytes = align256((size_t)B * H * NB * sizeof(int));
+  cudaError_t e = cudaMemsetAsync(workspace, 0, base + (nchain > 0 ? cflag_bytes : 0), st);
   if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
 
   PrepArgs pa{};
@@ -148,6 +168,13 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
   fa.x = static_cast<bf16*>(x);
   fa.flags = flags;
   fa.status = status;
+  if (nchain > 0) {
+    fa.nchain = nchain;
+    fa.cflags = reinterpret_cast<int*>(extra);
+    fa.wring = reinterpret_cast<float*>(extra + cflag_bytes);
+    fa.etiles = reinterpret_cast<bf16*>(extra + cflag_bytes +
+                                        (size_t)B * H * kChainWRing * kBlock * kHeadDim * sizeof(float));
+  }
   ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
   return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
 }

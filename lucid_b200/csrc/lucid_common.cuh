@@ -50,7 +50,26 @@ struct FwdArgs {
   // elsewhere and their flags already set) and an optional cap on the persistent
   // grid (0: #SMs)
   int pp0 = 0, pp1 = 0, max_ctas = 0;
+  // solve, chain schedule (nchain > 0): CTAs [0, nchain) each run the diagonal steps of
+  // one (batch, kv head); the other CTAs stream row-block pairs and hand each row
+  // block i to its chain as the partial sum W_i = V_i - sum_{j < i-kChainLook} E_ij X_j
+  // (fp32, in a ring of kChainWRing slots per head) plus the kChainLook tiles
+  // E_{i,i-kChainLook} .. E_{i,i-1} (bf16, in the shared-memory image of a K-major
+  // operand tile)
+  int nchain = 0;
+  int* cflags = nullptr;     // [B*Hkv][NB]: 1 = E tiles of row block i written, 2 = W_i too
+  float* wring = nullptr;    // [B*Hkv][kChainWRing][32][128][4] fp32
+  bf16* etiles = nullptr;    // [B*Hkv][NB][kChainLook][128*128] bf16
 };
+// Chain schedule: key blocks i-kChainLook .. i-1 of row block i are multiplied by the
+// chain CTA, the rest by the workers, so a worker has kChainLook + 1 chain steps to
+// turn X_{i-kChainLook-1} into W_i.
+constexpr int kChainLook = 3;
+// W slots per head.  The worker writes W_i only after X_{i-kChainLook-1} is published,
+// i.e. after the chain finished step i-kChainLook-1; a ring of kChainLook + 1 slots or
+// more never overwrites a W that the chain has not read.
+constexpr int kChainWRing = 8;
+static_assert(kChainWRing >= kChainLook + 1, "W ring too small");
 
 // Backward tile engines (column pass and row pass; attention or solve).
 struct BwdArgs {

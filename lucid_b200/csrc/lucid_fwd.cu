@@ -8,6 +8,17 @@
 //     Blocks are processed as a wavefront: a work item waits on a global flag
 //     for every X_j it consumes and publishes its own X_i.
 //
+//     Chain schedule (few heads per GPU): the chain X_0 -> X_1 -> ... of one head
+//     is its critical path, and in the wavefront every step crosses CTAs (publish,
+//     poll, reload X through L2).  Here CTA c < nchain owns the diagonal steps of
+//     head c and keeps the X tiles it produces in shared memory (L = kChainLook):
+//       X_i = Y + U_i Y,  Y = D_i^-1 (W_i - sum_{j=i-L}^{i-1} E_ij X_j)
+//     while the other CTAs (workers) stream row-block pairs and publish, per row
+//     block, the tiles E_{i,i-L} .. E_{i,i-1} first and the partial sum
+//     W_i = V_i - sum_{j < i-L} E_ij X_j when its last X_j has arrived.  A chain
+//     step is L + 1 GEMMs and two epilogues on one SM, and only one GEMM of it
+//     waits for the previous step.
+//
 //   ATTN   (modeling_lucid.py:505-549)
 //     O = softmax(scale Q K^T + causal) X   (raw K, X from SOLVE), keeping the
 //     row log-sum-exp for the backward.  Grouped-query heads index kv head =
@@ -27,6 +38,8 @@
 #include "lucid_common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 namespace lb {
 
@@ -54,12 +67,232 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
   return __all_sync(0xffffffffu, ok);
 }
 
-template <bool SOLVE>
+// ---------------------------------------------------------------------------
+// Chain CTA of the chain schedule: the diagonal steps of head blockIdx.x.
+//   acc_i = sum_{e < kChainLook} E_{i,i-kChainLook+e} X_{i-kChainLook+e}
+//   Y_i   = D_i^-1 (W_i - acc_i),  X_i = Y_i + U_i Y_i
+// Shared memory: E ring (kChainLook tiles) | X ring (kChainLook tiles; Y_i is staged
+// in the slot X_i will take, that of X_{i-kChainLook}) | U (one tile).  TMEM: two
+// 128-column accumulators (step parity); the accumulator of step i holds acc_i,
+// then T_i = U_i Y_i.  Warps 0-7: epilogue (warp w: rows 32 (w % 4).., columns
+// 64 (w / 4)..), warp 8: loads, warp 9: MMA, warp 10: publishes X flags.
+// ---------------------------------------------------------------------------
+namespace chain {
+constexpr uint32_t kOffE = 0, kOffX = kChainLook * 32768, kOffU = 2 * kChainLook * 32768;
+static_assert(kOffU + 32768 <= fwd::kOffBar, "chain tiles exceed the engine's tile area");
+constexpr int kEpiRing = kChainLook + 1;  // publisher barriers (see the publisher)
+enum { EFULL0 = 0, EEMPTY0 = kChainLook, UFULL = 2 * kChainLook, UEMPTY, ACC, YF, TF, XR, EPI0,
+       DRAIN = EPI0 + kEpiRing, NBAR };
+static_assert((int)NBAR <= (int)fwd::NBAR, "chain barriers exceed the engine's barrier area");
+constexpr int kEpiThreads = 256;
+}  // namespace chain
+
+__device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const FwdArgs& p, uint8_t* smem) {
+  using namespace chain;
+  constexpr int L = kChainLook;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + fwd::kOffBar;
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + fwd::kOffBar + fwd::NBAR * 8);
+  volatile int* abort_cta = reinterpret_cast<volatile int*>(smem + fwd::kOffBar + fwd::NBAR * 8 + 4);
+  const Abort ab{abort_cta, p.status, kTagFwdSolve};
+  auto sE = [&](uint32_t s) { return sbase + kOffE + s * 32768u; };
+  auto sX = [&](int j) { return sbase + kOffX + (uint32_t)(j % L) * 32768u; };  // slot of block j
+  const uint32_t sU = sbase + kOffU;
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == fwd::kWarpTma * 32) {
+    for (int s = 0; s < L; ++s) {
+      mbar_init(bar(EFULL0 + s), 1);
+      mbar_init(bar(EEMPTY0 + s), 1);
+    }
+    mbar_init(bar(UFULL), 1);
+    mbar_init(bar(UEMPTY), 1);
+    mbar_init(bar(ACC), 1);
+    mbar_init(bar(YF), kEpiThreads);
+    mbar_init(bar(TF), 1);
+    mbar_init(bar(XR), kEpiThreads);
+    for (int s = 0; s < kEpiRing; ++s) mbar_init(bar(EPI0 + s), kEpiThreads);
+    mbar_init(bar(DRAIN), 1);
+    *abort_cta = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(tmU);
+  }
+  if (warp == fwd::kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int NB = p.NB;
+  const long long bhk = blockIdx.x;
+  const int b = (int)bhk / p.Hkv, hk = (int)bhk % p.Hkv;
+  const int* cflag = p.cflags + bhk * NB;
+  int* xflag = p.flags + bhk * NB;
+
+  if (warp >= fwd::kWarpTma) {
+    regs_dec<fwd::kRegsCtl>();
+    if (warp == fwd::kWarpTma && lane == 0) {
+      // ---- loads: U_i by TMA; the E tiles of row block i by bulk copy once the
+      // worker flagged them (tile e of row i: key block i - L + e)
+      const bf16* et = p.etiles + bhk * NB * L * (long long)(kTileBytes / 2);
+      uint32_t e_idx = 0;
+      int last_e[L], last_u = -1;
+      for (int s = 0; s < L; ++s) last_e[s] = -1;
+      for (int i = 0; i < NB; ++i) {
+        if (!mbar_wait(bar(UEMPTY), ((uint32_t)i & 1) ^ 1, ab)) break;
+        last_u = i & 1;
+        mbar_arrive_expect_tx(bar(UFULL), 32768);
+        tma_load_tile(sU, tmU, bar(UFULL), i * 128, hk, b);
+        if (i == 0) continue;
+        if (!wait_flag_geq(&cflag[i], 1, ab)) break;
+        fence_proxy_async_global();
+        bool ok = true;
+        for (int e = (i >= L ? 0 : L - i); e < L; ++e) {
+          const uint32_t se = e_idx % L, euse = e_idx / L;
+          if (!mbar_wait(bar(EEMPTY0 + se), (euse & 1) ^ 1, ab)) { ok = false; break; }
+          last_e[se] = (int)(euse & 1);
+          mbar_arrive_expect_tx(bar(EFULL0 + se), 32768);
+          bulk_load(sE(se), et + ((long long)i * L + e) * (kTileBytes / 2), 32768, bar(EFULL0 + se));
+          ++e_idx;
+        }
+        if (!ok) break;
+      }
+      if (last_u >= 0) mbar_wait_timed(bar(UFULL), (uint32_t)last_u, kDrainNs);
+      for (int s = 0; s < L; ++s)
+        if (last_e[s] >= 0) mbar_wait_timed(bar(EFULL0 + s), (uint32_t)last_e[s], kDrainNs);
+    } else if (warp == fwd::kWarpMma && lane == 0) {
+      // ---- MMA: acc_i = sum_e E_{i,j} X_j (j = i-L+e), then T_i = U_i Y_i over it.  Only
+      // the last product waits for the epilogue (X_{i-1}); the others read X blocks
+      // the epilogue wrote one or more steps earlier.
+      uint32_t e_idx = 0;
+      for (int i = 0; i < NB; ++i) {
+        const uint32_t acc = tmem + 128u * (uint32_t)(i & 1);
+        bool ok = true, first = true;
+        for (int e = (i >= L ? 0 : L - i); e < L; ++e) {
+          const int j = i - L + e;
+          const uint32_t se = e_idx % L;
+          if (!mbar_wait(bar(EFULL0 + se), (e_idx / L) & 1, ab)) { ok = false; break; }
+          if (e == L - 1 && !mbar_wait(bar(XR), (uint32_t)(i - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          umma_tile(acc, sE(se), false, sX(j), true, first ? 0u : 1u);
+          umma_commit(bar(EEMPTY0 + se));
+          first = false;
+          ++e_idx;
+        }
+        if (!ok) break;
+        umma_commit(bar(ACC));
+        if (!mbar_wait(bar(UFULL), (uint32_t)i & 1, ab) || !mbar_wait(bar(YF), (uint32_t)i & 1, ab)) break;
+        tc_fence_after();
+        umma_tile(acc, sU, false, sX(i), true, 0u);
+        umma_commit(bar(TF));
+        umma_commit(bar(UEMPTY));
+      }
+      umma_commit(bar(DRAIN));
+      mbar_wait_timed(bar(DRAIN), 0, kDrainNs);
+    } else if (warp == fwd::kWarpMma + 1 && lane == 0) {
+      // ---- publisher: X_i rows are in global memory -> release the flag.  The
+      // epilogue can finish steps i+1 .. i+L before this thread sees step i (W_{i+L+1}
+      // waits for X_i), never step i+L+1: kEpiRing = L+1 barriers in rotation keep
+      // every wait unambiguous.
+      for (int i = 0; i < NB; ++i) {
+        if (!mbar_wait(bar(EPI0 + i % kEpiRing), ((uint32_t)(i / kEpiRing)) & 1, ab)) break;
+        __threadfence();
+        st_release_gpu(&xflag[i], 1);
+      }
+    }
+  } else {
+    regs_inc<fwd::kRegsEpi>();
+    // ---- epilogue: thread = (row r, column half h)
+    const int sp = warp & 3, h = warp >> 2;
+    const int r = sp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    const float* wslots = p.wring + bhk * kChainWRing * (long long)(kBlock * kHeadDim);
+    for (int i = 0; i < NB; ++i) {
+      const int row = i * 128 + r;
+      // W_i (fp32, this thread's 64 columns): chunk c4 of row r at (c4 * 128 + r) * 4,
+      // read through L2 (the slot is rewritten every kChainWRing steps by other CTAs)
+      bool ok = true;
+      if (lane == 0) ok = wait_flag_geq(&cflag[i], 2, ab);
+      if (!__all_sync(0xffffffffu, __shfl_sync(0xffffffffu, (int)ok, 0) != 0)) break;
+      const float4* ws = reinterpret_cast<const float4*>(wslots + (long long)(i % kChainWRing) * (kBlock * kHeadDim));
+      float y[2][32];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 w4 = __ldcg(ws + (16 * h + 8 * q + m) * 128 + r);
+          y[q][4 * m] = w4.x;
+          y[q][4 * m + 1] = w4.y;
+          y[q][4 * m + 2] = w4.z;
+          y[q][4 * m + 3] = w4.w;
+        }
+      const float di = p.dinv[bhk * p.Npad + row];
+      const uint32_t tacc = tmem + lane_base + 128u * (uint32_t)(i & 1) + 64u * (uint32_t)h;
+      if (!warp_wait(bar(ACC), (uint32_t)i & 1, ab)) break;
+      tc_fence_after();
+      if (i > 0) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float a[32];
+          tmem_ld32(tacc + 32u * q, a);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) y[q][e] -= a[e];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) y[q][e] *= di;
+        tile_store_row32(sX(i), r, 2 * h + q, y[q]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(YF));
+      // X_i = Y + U_i Y: into the slot (operand of steps i+1 .. i+L) and to global memory
+      if (!warp_wait(bar(TF), (uint32_t)i & 1, ab)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float t[32];
+        tmem_ld32(tacc + 32u * q, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) y[q][e] += t[e];
+        tile_store_row32(sX(i), r, 2 * h + q, y[q]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(XR));
+      bf16* xrow = p.x + (bhk * p.Npad + row) * kHeadDim + 64 * h;
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) st_bf16x8(xrow + q * 32 + c * 8, y[q] + c * 8);
+      fence_proxy_async_global();
+      mbar_arrive(bar(EPI0 + i % kEpiRing));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == fwd::kWarpMma) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int MODE>
 __global__ void __launch_bounds__(fwd::kThreads, 1)
     lucid_fwd_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmU,
                      FwdArgs p) {
   using namespace fwd;
+  // MODE 0: attention; 1: solve, wavefront schedule; 2: solve, chain schedule
+  constexpr bool SOLVE = MODE != 0, CHAIN = MODE == 2;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
@@ -76,6 +309,15 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     if (threadIdx.x == 0) atomicCAS(p.status, 0, kStatusMisaligned | (ab.tag << 20));
     return;
   }
+  if constexpr (CHAIN) {
+    if ((int)blockIdx.x < p.nchain) {
+      solve_chain_cta(&tmU, p, smem);
+      return;
+    }
+  }
+  // this CTA's share of the work items (chain schedule: the CTAs after the chains)
+  const int cta0 = CHAIN ? (int)blockIdx.x - p.nchain : (int)blockIdx.x;
+  const int ncta = CHAIN ? (int)gridDim.x - p.nchain : (int)gridDim.x;
   if (threadIdx.x == kWarpTma * 32) {
     mbar_init(bar(Q_FULL), 1);
     mbar_init(bar(Q_EMPTY), 1);
@@ -136,10 +378,19 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   // Streaming tiles of row k: attention row block i has tiles j = 0..i;
   // the solve streams the shared tiles j < 2pp (row 1's tile 2pp is part of
   // its tail).
+  // Chain schedule: row block i = 2pp + k streams the tiles j < i - kChainLook (its
+  // chain multiplies the blocks i - kChainLook .. i - 1).
   auto nrow = [&](int pp, int k) -> int {
     const bool r1 = (2 * pp + 1) < p.NB;
     if (k == 1 && !r1) return 0;
+    if (CHAIN) return 2 * pp - kChainLook + k > 0 ? 2 * pp - kChainLook + k : 0;
     return SOLVE ? 2 * pp : 2 * pp + 1 + k;
+  };
+  // Chain schedule: the E tiles of both rows come from the key blocks
+  // j = 2pp - kChainLook + e (e = 0 .. kChainLook); row k uses them as its tile e - k.
+  auto etile_used = [&](int pp, int e, int k) -> bool {
+    const int j = 2 * pp - kChainLook + e, s2 = e - k;
+    return j >= 0 && s2 >= 0 && s2 < kChainLook && (k == 0 || 2 * pp + 1 < p.NB);
   };
 
   if (warp >= kWarpTma) {
@@ -168,7 +419,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         ++xidx;
         return true;
       };
-      for (int idx = blockIdx.x; idx < total && ok; idx += gridDim.x, ++item) {
+      for (int idx = cta0; idx < total && ok; idx += ncta, ++item) {
         int pp, b, ha, hk;
         decode(idx, pp, b, ha, hk);
         const int i0 = 2 * pp;
@@ -178,6 +429,13 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         mbar_arrive_expect_tx(bar(Q_FULL), r1 ? 65536 : 32768);
         tma_load_tile(sQ(0), &tmA, bar(Q_FULL), i0 * 128, ha, b);
         if (r1) tma_load_tile(sQ(1), &tmA, bar(Q_FULL), (i0 + 1) * 128, ha, b);
+        if (CHAIN) {
+          // the key blocks of the tiles handed to the chain (no X needed)
+          for (int e = 0; e <= kChainLook && ok; ++e)
+            if (etile_used(pp, e, 0) || etile_used(pp, e, 1))
+              ok = loadK(&tmB, (2 * pp - kChainLook + e) * 128, hk, b);
+          if (!ok) break;
+        }
         const int nt = nrow(pp, 0) > nrow(pp, 1) ? nrow(pp, 0) : nrow(pp, 1);
         for (int j = 0; j < nt; ++j) {
           if (!loadK(&tmB, j * 128, hk, b)) { ok = false; break; }
@@ -187,7 +445,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
           }
           if (!loadX(j * 128, hk, b)) { ok = false; break; }
         }
-        if (!ok || !SOLVE) continue;
+        if (!ok || !SOLVE || CHAIN) continue;
         // solve tail: K^_{2pp} for row 1, U_i0, U_i1, then X_{2pp} (made by row 0 of this item)
         if (r1 && !loadK(&tmB, i0 * 128, hk, b)) break;
         if (!loadK(&tmU, i0 * 128, hk, b)) break;
@@ -227,7 +485,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         umma_commit(bar(O_DONE0 + k));
         return true;
       };
-      for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+      for (int idx = cta0; idx < total; idx += ncta, ++item) {
         int pp, b, ha, hk;
         decode(idx, pp, b, ha, hk);
         const int i0 = 2 * pp;
@@ -236,6 +494,28 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         if (!mbar_wait(bar(Q_FULL), item & 1, ab)) break;
         tc_fence_after();
         bool ok = true;
+        if (CHAIN) {
+          // S of the tiles handed to the chain; the epilogue reads each S_k before the
+          // next GEMM into that region (P_FULL, with no PV in between)
+          bool busy[2] = {false, false};
+          for (int e = 0; e <= kChainLook && ok; ++e) {
+            const bool u0 = etile_used(pp, e, 0), u1 = etile_used(pp, e, 1);
+            if (!u0 && !u1) continue;
+            if (!waitK(kidx)) { ok = false; break; }
+            for (int k2 = 0; k2 < 2; ++k2) {
+              if (!(k2 == 0 ? u0 : u1)) continue;
+              if (busy[k2] && !mbar_wait(bar(P_FULL0 + k2), (n_pfull[k2]++) & 1, ab)) { ok = false; break; }
+              tc_fence_after();
+              issue_s(k2, kidx);
+              busy[k2] = true;
+            }
+            umma_commit(bar(K_EMPTY0 + kidx % 3u));
+            ++kidx;
+          }
+          for (int k2 = 0; k2 < 2 && ok; ++k2)
+            if (busy[k2] && !mbar_wait(bar(P_FULL0 + k2), (n_pfull[k2]++) & 1, ab)) ok = false;
+          if (!ok) break;
+        }
         const uint32_t kb = kidx, xb = xidx;
         // S for the first tile of each row
         if (nt > 0) {
@@ -264,7 +544,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         if (!ok) break;
         kidx = kb + nt;
         xidx = xb + nt;
-        if (SOLVE) {
+        if (SOLVE && !CHAIN) {
           // tail: S1(2pp), DIAG0, PV1(2pp), DIAG1
           if (r1) {
             if (!waitK(kidx)) break;
@@ -312,15 +592,60 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     const float c1 = p.scale * kLog2e;
     const float c2 = kLog2e / p.scale;
     uint32_t n_sfull = 0, n_p = 0, n_epi = 0, item = 0;
-    for (int idx = blockIdx.x; idx < total; idx += gridDim.x, ++item) {
+    for (int idx = cta0; idx < total; idx += ncta, ++item) {
       int pp, b, ha, hk;
       decode(idx, pp, b, ha, hk);
       const int i = 2 * pp + k;         // this warpgroup's row block
       if (i >= p.NB) continue;
-      const int nk = nrow(pp, k) + ((SOLVE && k == 1) ? 1 : 0);  // solve row 1 adds tile 2pp
+      const int nk = nrow(pp, k) + ((SOLVE && !CHAIN && k == 1) ? 1 : 0);  // wavefront row 1 adds tile 2pp
       const int row = i * 128 + r;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
+      // chain schedule: make this row's writes visible, then release its chain flag
+      auto publish = [&](int* flag, int value) {
+        fence_proxy_async_global();
+        mbar_arrive(bar(EPI_DONE0 + k));
+        if ((int)threadIdx.x == wg_thread0) {
+          if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) {
+            __threadfence();
+            st_release_gpu(flag, value);
+          }
+        }
+        ++n_epi;
+        __syncwarp();
+      };
+      if (CHAIN) {
+        // E_{i,i-kChainLook} .. E_{i,i-1} (row r) -> global, in the shared-memory image of
+        // a K-major operand tile, which the chain copies unchanged
+        const long long bhk = (long long)b * p.Hkv + hk;
+        for (int s2 = 0; s2 < kChainLook && ok; ++s2) {
+          if (i - kChainLook + s2 < 0) continue;
+          if (!warp_wait(bar(S_FULL0 + k), (n_sfull++) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* et = reinterpret_cast<uint8_t*>(p.etiles + ((bhk * p.NB + i) * kChainLook + s2) *
+                                                                  (long long)(kTileBytes / 2));
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float sv[32];
+            tmem_ld32(tSk + 32u * q, sv);
+            tmem_ld_wait();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 a = fma2(make_float2(sv[e], sv[e + 1]), make_float2(c1, c1), make_float2(-c2, -c2));
+              pk[e >> 1] = pack_bf16(fast_exp2(a.x), fast_exp2(a.y));
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(et + tile_chunk_off(r, 4 * q + c)) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          }
+          tc_fence_before();
+          mbar_arrive(bar(P_FULL0 + k));
+        }
+        if (!ok) break;
+        publish(&p.cflags[bhk * p.NB + i], 1);
+      }
       if (SOLVE && row < p.N) {
         // the diagonal step reads this row of V on the wavefront's critical path: fetch
         // it into L2 while the row's streaming tiles run
@@ -453,6 +778,31 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         p.lse[((long long)b * p.Hq + ha) * p.Npad + row] = m_run + __log2f(l_run);
         continue;
       }
+      if (CHAIN) {
+        // W_i = V_i - acc (fp32) into the head's ring slot: chunk c4 (4 columns) of row r
+        // at (c4 * 128 + r) * 4 floats, so one warp store covers 512 contiguous bytes
+        const long long bhk = (long long)b * p.Hkv + hk;
+        const bf16* vrow = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh + (long long)row * p.v_sn;
+        float4* ws = reinterpret_cast<float4*>(p.wring + (bhk * kChainWRing + i % kChainWRing) *
+                                                             (long long)(kBlock * kHeadDim));
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float vv[8];
+            if (row < p.N) {
+              ld_bf16x8(vrow + q * 32 + c * 8, vv);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) vv[e] = 0.f;
+            }
+            const float* a = acc[q] + c * 8;
+            ws[(8 * q + 2 * c) * 128 + r] = make_float4(vv[0] - a[0], vv[1] - a[1], vv[2] - a[2], vv[3] - a[3]);
+            ws[(8 * q + 2 * c + 1) * 128 + r] = make_float4(vv[4] - a[4], vv[5] - a[5], vv[6] - a[6], vv[7] - a[7]);
+          }
+        publish(&p.cflags[bhk * p.NB + i], 2);
+        continue;
+      }
       // ---- solve: diagonal block.  Y = D^-1 (V - acc) -> A buffer of this row ----
       const long long bhk = (long long)b * p.Hkv + hk;
       const float di = p.dinv[bhk * p.Npad + row];
@@ -531,21 +881,49 @@ cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB,
   const int pairs = (a.pp1 > 0 ? a.pp1 : (a.NB + 1) / 2) - a.pp0;
   const int total = solve ? pairs * a.B * a.Hkv : pairs * a.B * a.Hq;
   if (total <= 0) return cudaSuccess;
-  const int grid = std::min(total, a.max_ctas > 0 ? std::min(a.max_ctas, num_sms()) : num_sms());
+  const int cap = a.max_ctas > 0 ? std::min(a.max_ctas, num_sms()) : num_sms();
   cudaError_t e;
+  if (solve && a.nchain > 0) {
+    // chain schedule: the chains plus at least one worker CTA, all resident
+    if (a.pp0 != 0 || a.pp1 != 0 || a.nchain != a.B * a.Hkv || a.nchain >= cap) return cudaErrorInvalidValue;
+    const int grid = std::min(a.nchain + total, cap);
+    e = cudaFuncSetAttribute(lucid_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fwd::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    return launch_cooperative(lucid_fwd_kernel<2>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
+  }
+  const int grid = std::min(total, cap);
   if (solve) {
-    e = cudaFuncSetAttribute(lucid_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(lucid_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
     // the wavefront's CTAs wait on one another's flags: all of them must be resident
-    return launch_cooperative(lucid_fwd_kernel<true>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
+    return launch_cooperative(lucid_fwd_kernel<1>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
   } else {
-    e = cudaFuncSetAttribute(lucid_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(lucid_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
-    lucid_fwd_kernel<false><<<grid, fwd::kThreads, fwd::kSmemBytes, st>>>(tA, tB, tC, tU, a);
+    lucid_fwd_kernel<0><<<grid, fwd::kThreads, fwd::kSmemBytes, st>>>(tA, tB, tC, tU, a);
   }
   return cudaGetLastError();
+}
+
+// Schedule of the solve forward for B*H heads of NB row blocks on this device: the
+// number of chain CTAs (the chain schedule, one per head) or 0 (the wavefront).  Model
+// (one B200, 32K rows): a tile of the row sums costs ~1.2 us of one SM; a diagonal step
+// ~10 us in the wavefront (it crosses CTAs through L2) and ~4 us in a chain CTA, which
+// waits for the workers' partial sums.  LUCID_B200_SOLVE_SCHEDULE=chain / wavefront
+// overrides the choice.
+int solve_chain_ctas(int BH, int NB) {
+  const int sms = num_sms();
+  if (BH <= 0 || NB <= 0 || BH + 4 > sms) return 0;
+  const char* env = getenv("LUCID_B200_SOLVE_SCHEDULE");
+  if (env && strcmp(env, "wavefront") == 0) return 0;
+  if (env && strcmp(env, "chain") == 0) return BH;
+  const double work = (double)BH * NB * (NB + 1) / 2.0 * 1.2;  // SM-microseconds
+  const double t_wave = std::max(work / sms, NB * 10.0);
+  const double t_chain = std::max(work / (sms - BH), NB * 4.0);
+  return t_chain < 0.9 * t_wave ? BH : 0;
 }
 
 }  // namespace lb

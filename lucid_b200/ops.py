@@ -114,7 +114,8 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int
     u = torch.empty(B, H, Np, 128, dtype=torch.bfloat16, device=dev)
     rstd = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
     dinv = torch.empty(B, H, Np, dtype=torch.float32, device=dev)
-    ws = _ws(lib.lucid_solve_fwd_workspace_bytes(B, H, N, D), dev)
+    # the chain schedule's buffers when the library picks it (few heads), else the flags
+    ws = _ws(lib.lucid_solve_fwd_fast_workspace_bytes(B, H, N, D), dev)
     rc = lib.lucid_solve_fwd(B, H, N, D, float(scale), float(eps), k.data_ptr(), *_s3(k),
                              v.data_ptr(), *_s3(v), x.data_ptr(), khat.data_ptr(), u.data_ptr(),
                              rstd.data_ptr(), dinv.data_ptr(), ws.data_ptr(), ws.numel(), _stream())

@@ -94,6 +94,31 @@ def test_solve_fwd_matches_oracle(cuda_device, B, H, N, keys):
     assert np.all(np.isfinite(_np(x)))
 
 
+@pytest.mark.parametrize("B,H,N,keys", [(1, 1, 1, "iid"), (1, 1, 128, "iid"), (1, 2, 257, "corr"),
+                                        (2, 3, 1000, "iid"), (1, 2, 4096, "corr")])
+def test_solve_fwd_chain_and_wavefront_schedules(cuda_device, monkeypatch, B, H, N, keys):
+    """Both schedules of the solve forward against the oracle, and against each other
+    (the chain schedule only regroups the fp32 row sums)."""
+    from lucid_b200 import _lib, solve_fwd
+    lib = _lib.load()
+    _, k, v, _ = _rand_inputs(20 + N, B, H, H, N, keys=keys)
+    s = 128 ** -0.5
+    ref = orc.solve(k, v, s, 1e-5)
+    xs = {}
+    for sched in ("chain", "wavefront"):
+        monkeypatch.setenv("LUCID_B200_SOLVE_SCHEDULE", sched)
+        base = lib.lucid_solve_fwd_workspace_bytes(B, H, N, 128)
+        fast = lib.lucid_solve_fwd_fast_workspace_bytes(B, H, N, 128)
+        assert (fast > base) == (sched == "chain")
+        x = solve_fwd(_t(k, cuda_device), _t(v, cuda_device), s, 1e-5)[0]
+        _lib.check_status()
+        xs[sched] = _np(x)[:, :, :N]
+        assert np.all(np.isfinite(xs[sched]))
+        assert_bf16_close(xs[sched], ref, f"X ({sched})")
+    diff = np.abs(xs["chain"] - xs["wavefront"])
+    assert float(diff.max()) <= 2e-2 * max(1.0, float(np.abs(ref).max()))
+
+
 def test_solve_fwd_diag_block_inverse(cuda_device):
     """U = (I + L~)^-1 - I of every diagonal block, against numpy."""
     from lucid_b200 import solve_fwd
