@@ -75,7 +75,8 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
 // in the slot X_i will take, that of X_{i-kChainLook}) | U (one tile).  TMEM: two
 // 128-column accumulators (step parity); the accumulator of step i holds acc_i,
 // then T_i = U_i Y_i.  Warps 0-7: epilogue (warp w: rows 32 (w % 4).., columns
-// 64 (w / 4)..), warp 8: loads, warp 9: MMA, warp 10: publishes X flags.
+// 64 (w / 4)..), warp 8: E loads, warp 9: MMA, warp 10: publishes X flags, warp 11:
+// U loads.
 // ---------------------------------------------------------------------------
 namespace chain {
 constexpr uint32_t kOffE = 0, kOffX = kChainLook * 32768, kOffU = 2 * kChainLook * 32768;
@@ -135,18 +136,13 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
   if (warp >= fwd::kWarpTma) {
     regs_dec<fwd::kRegsCtl>();
     if (warp == fwd::kWarpTma && lane == 0) {
-      // ---- loads: U_i by TMA; the E tiles of row block i by bulk copy once the
-      // worker flagged them (tile e of row i: key block i - L + e)
+      // ---- E loads: the tiles of row block i by bulk copy once the worker flagged them
+      // (tile e of row i: key block i - L + e), each as soon as its slot is free
       const bf16* et = p.etiles + bhk * NB * L * (long long)(kTileBytes / 2);
       uint32_t e_idx = 0;
-      int last_e[L], last_u = -1;
+      int last_e[L];
       for (int s = 0; s < L; ++s) last_e[s] = -1;
-      for (int i = 0; i < NB; ++i) {
-        if (!mbar_wait(bar(UEMPTY), ((uint32_t)i & 1) ^ 1, ab)) break;
-        last_u = i & 1;
-        mbar_arrive_expect_tx(bar(UFULL), 32768);
-        tma_load_tile(sU, tmU, bar(UFULL), i * 128, hk, b);
-        if (i == 0) continue;
+      for (int i = 1; i < NB; ++i) {
         if (!wait_flag_geq(&cflag[i], 1, ab)) break;
         fence_proxy_async_global();
         bool ok = true;
@@ -160,33 +156,51 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
         }
         if (!ok) break;
       }
-      if (last_u >= 0) mbar_wait_timed(bar(UFULL), (uint32_t)last_u, kDrainNs);
       for (int s = 0; s < L; ++s)
         if (last_e[s] >= 0) mbar_wait_timed(bar(EFULL0 + s), (uint32_t)last_e[s], kDrainNs);
-    } else if (warp == fwd::kWarpMma && lane == 0) {
-      // ---- MMA: acc_i = sum_e E_{i,j} X_j (j = i-L+e), then T_i = U_i Y_i over it.  Only
-      // the last product waits for the epilogue (X_{i-1}); the others read X blocks
-      // the epilogue wrote one or more steps earlier.
-      uint32_t e_idx = 0;
+    } else if (warp == fwd::kWarpMma + 2 && lane == 0) {
+      // ---- U loads (own thread, so that a U slot still in use never holds back an E load)
+      int last_u = -1;
       for (int i = 0; i < NB; ++i) {
-        const uint32_t acc = tmem + 128u * (uint32_t)(i & 1);
-        bool ok = true, first = true;
-        for (int e = (i >= L ? 0 : L - i); e < L; ++e) {
-          const int j = i - L + e;
-          const uint32_t se = e_idx % L;
-          if (!mbar_wait(bar(EFULL0 + se), (e_idx / L) & 1, ab)) { ok = false; break; }
-          if (e == L - 1 && !mbar_wait(bar(XR), (uint32_t)(i - 1) & 1, ab)) { ok = false; break; }
-          tc_fence_after();
-          umma_tile(acc, sE(se), false, sX(j), true, first ? 0u : 1u);
-          umma_commit(bar(EEMPTY0 + se));
-          first = false;
-          ++e_idx;
-        }
+        if (!mbar_wait(bar(UEMPTY), ((uint32_t)i & 1) ^ 1, ab)) break;
+        last_u = i & 1;
+        mbar_arrive_expect_tx(bar(UFULL), 32768);
+        tma_load_tile(sU, tmU, bar(UFULL), i * 128, hk, b);
+      }
+      if (last_u >= 0) mbar_wait_timed(bar(UFULL), (uint32_t)last_u, kDrainNs);
+    } else if (warp == fwd::kWarpMma && lane == 0) {
+      // ---- MMA.  Step i: acc_i = sum_e E_{i,j} X_j (j = i-L+e), then T_i = U_i Y_i over
+      // it.  Only the last product (e = L-1, X_{i-1}) waits for the epilogue; the
+      // lookahead products of step i+1 (e < L-1) are issued around T_i (one before it
+      // when its tile is already loaded, the rest after), so that the tensor core runs
+      // them while the epilogue works on step i.
+      uint32_t e_idx = 0;  // next E tile (the loads run in the same order)
+      auto e_first = [&](int i) { return i >= L ? 0 : L - i; };
+      auto issue_e = [&](int i, int e) -> bool {
+        const uint32_t se = e_idx % L;
+        if (!mbar_wait(bar(EFULL0 + se), (e_idx / L) & 1, ab)) return false;
+        if (e == L - 1 && !mbar_wait(bar(XR), (uint32_t)(i - 1) & 1, ab)) return false;
+        tc_fence_after();
+        umma_tile(tmem + 128u * (uint32_t)(i & 1), sE(se), false, sX(i - L + e), true, e > e_first(i) ? 1u : 0u);
+        umma_commit(bar(EEMPTY0 + se));
+        ++e_idx;
+        return true;
+      };
+      int e_next = L - 1;  // first lookahead product of the current step still to issue
+      for (int i = 0; i < NB; ++i) {
+        bool ok = true;
+        for (int e = e_next; e < L - 1 && ok; ++e) ok = issue_e(i, e);
+        if (ok && i >= 1) ok = issue_e(i, L - 1);
         if (!ok) break;
         umma_commit(bar(ACC));
+        e_next = i + 1 < NB ? e_first(i + 1) : L - 1;
+        if (e_next < L - 1 && mbar_try_wait(bar(EFULL0 + e_idx % L), (e_idx / L) & 1)) {
+          if (!issue_e(i + 1, e_next)) break;
+          ++e_next;
+        }
         if (!mbar_wait(bar(UFULL), (uint32_t)i & 1, ab) || !mbar_wait(bar(YF), (uint32_t)i & 1, ab)) break;
         tc_fence_after();
-        umma_tile(acc, sU, false, sX(i), true, 0u);
+        umma_tile(tmem + 128u * (uint32_t)(i & 1), sU, false, sX(i), true, 0u);
         umma_commit(bar(TF));
         umma_commit(bar(UEMPTY));
       }
