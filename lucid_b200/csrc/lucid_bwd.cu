@@ -429,6 +429,12 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         int g, j;
         tile_at(i, t, g, j);
         const int st = n_kv & 1;
+        if (SOLVE && t == T - 1) {
+          // the column's tiles ran long enough for other traffic to evict the row's dX
+          // and 1 / P_rr from L2: fetch them again while the last tile waits for its dV
+          prefetch_l2(p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0);
+          prefetch_l2(p.dinv + bhk * p.Npad + row_i);
+        }
         if (!SOLVE && !warp_wait_b(bar(KV_FULL0 + st), (n_kv >> 1) & 1, ab)) { ok = false; break; }
         if (!warp_wait_b(bar(SD_FULL), sd_full.full(), ab)) { ok = false; break; }
         tc_fence_after();
@@ -552,6 +558,24 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         mbar_arrive(bar(DSP_FULL));
       }
       if (!ok) break;
+      // solve: the diagonal step's dX row (this warp's columns) and 1 / P_rr, loaded while
+      // the last tile's GEMMs finish (they sit on the wavefront's critical path)
+      float dxv[kColQ][32];
+      float di = 0.f;
+      if constexpr (SOLVE) {
+        const float4* dx4 = reinterpret_cast<const float4*>(p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0);
+#pragma unroll
+        for (int q = 0; q < kColQ; ++q)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 x4 = dx4[q * 8 + c];
+            dxv[q][4 * c] = x4.x;
+            dxv[q][4 * c + 1] = x4.y;
+            dxv[q][4 * c + 2] = x4.z;
+            dxv[q][4 * c + 3] = x4.w;
+          }
+        di = p.dinv[bhk * p.Npad + row_i];
+      }
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
       tc_fence_after();
       if (!SOLVE) {
@@ -592,25 +616,15 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       ++n_kv;  // the U_i load
       // ---------------- solve: diagonal block ----------------
       // D1: R = dX_i - acc1 (this warp's column half), staged as bf16 for U^T R
-      float rr[kColQ][32];
-      const float* dxr = p.dx_in + (bhk * p.Npad + row_i) * kHeadDim + c0;
+      float (&rr)[kColQ][32] = dxv;
 #pragma unroll
       for (int q = 0; q < kColQ; ++q) {
-        float a1[32];
         if (T > 0) {
+          float a1[32];
           tmem_ld32(tmem + lane_base + kTmAcc1 + c0 + 32u * q, a1);
           tmem_ld_wait();
-        } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) a1[e] = 0.f;
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float4 x4 = reinterpret_cast<const float4*>(dxr)[q * 8 + c];
-          rr[q][4 * c + 0] = x4.x - a1[4 * c + 0];
-          rr[q][4 * c + 1] = x4.y - a1[4 * c + 1];
-          rr[q][4 * c + 2] = x4.z - a1[4 * c + 2];
-          rr[q][4 * c + 3] = x4.w - a1[4 * c + 3];
+          for (int e = 0; e < 32; ++e) rr[q][e] -= a1[e];
         }
       }
       if (!warp_wait_b(bar(DS_FREE), ds_free.empty(), ab)) break;
@@ -623,7 +637,6 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       if (!warp_wait_b(bar(T_FULL), t_full.full(), ab) || !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab))
         break;
       tc_fence_after();
-      const float di = p.dinv[bhk * p.Npad + row_i];
       bf16* dvr = p.dv + (bhk * p.Npad + row_i) * kHeadDim + c0;
 #pragma unroll
       for (int q = 0; q < kColQ; ++q) {
@@ -640,7 +653,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       mbar_arrive(bar(S_FREE));
       fence_proxy_async_smem();
       mbar_arrive(bar(PD_FULL));
-      fence_proxy_async_global();
+      // (the readers fence the async proxy after acquiring the flag, before their TMA loads)
       mbar_arrive(bar(EPI_DONE));
       if (threadIdx.x == 0) {   // publish: the CTA's dV rows, then the flag (one fence, cumulative)
         if (mbar_wait(bar(EPI_DONE), item & 1, ab)) {
