@@ -201,6 +201,28 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale,
                    float* lse, void* o_res, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Layer forward: lucid_solve_fwd then lucid_attn_fwd in one call, with the same
+ * arguments and outputs as the two (one scale for both, as LucidAttention uses
+ * self.scaling for get_v_prime and for the attention).
+ * Replaces LucidAttention.get_v_prime followed by eager_lucid_attention_forward
+ * (modeling_lucid.py:463 and :489, the two halves of LucidAttention.forward).
+ * With the chain schedule (workspace of lucid_fused_fwd_workspace_bytes, few heads per
+ * GPU) the solve and the attention run as ONE launch: the attention's row-block pairs
+ * start as soon as the X blocks they read are published.  Otherwise the two stages run
+ * as two launches.  Same results either way.
+ * In : q strided [B,Hq,N,D]; k, v strided [B,Hkv,N,D]; scale = s; eps.
+ * Out: x, khat, u, rstd, dinv as lucid_solve_fwd; o, lse, o_res as lucid_attn_fwd.
+ */
+size_t lucid_fused_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D);
+int lucid_fused_fwd(int B, int Hq, int Hkv, int N, int D, float scale, float eps,
+                    const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sn,
+                    const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                    const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                    void* x, void* khat, void* u, float* rstd, float* dinv,
+                    void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                    float* lse, void* o_res, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Attention backward: what torch autograd derives for the SDPA call of
  * eager_lucid_attention_forward (modeling_lucid.py:505-549, causal, repeat_kv'd X),
  * with the grouped-query sums over the query heads of each kv head done in-kernel.
@@ -427,6 +449,7 @@ int lucid_cp_solve_bwd(int B, int H, int N, int D, float scale, int blk_lo, int 
 #define LUCID_KERNEL_PATH_COL 13      /* LUCID-Path backward column pass (dK_new, dW, dW2) */
 #define LUCID_KERNEL_PATH_ATTN 14     /* PaTH softmax attention forward */
 #define LUCID_KERNEL_DECODE 15        /* LUCID decode step (get_new_v_prime) */
+#define LUCID_KERNEL_FWD_FUSED 16     /* chain-schedule solve + attention forward in one launch */
 int lucid_profile_enable(int kernel);
 int lucid_profile_read(float* total_ms, int* launches);
 

@@ -11,6 +11,7 @@ from .ops import (  # noqa: F401
     LucidSolveFunction,
     attn_bwd,
     attn_fwd,
+    fused_fwd,
     decode_attention,
     decode_step,
     decode_step_fused,

@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "liblucid_b200.so")
 LUCID_OK = 0
 KERNEL_IDS = {"prep": 1, "solve_fwd": 2, "attn_fwd": 3, "attn_bwd": 4, "solve_bwd": 5, "attn_bwd_row": 6,
               "solve_bwd_row": 7, "path_block": 8, "path_scores": 9, "path_solve": 10, "path_solve_t": 11,
-              "path_row": 12, "path_col": 13, "path_attn": 14, "decode": 15}
+              "path_row": 12, "path_col": 13, "path_attn": 14, "decode": 15, "fwd_fused": 16}
 ERRORS = {
     1: "unsupported shape (head_dim at most 128, Hq a multiple of Hkv)",
     2: "pointer or stride not 16-byte aligned",
@@ -43,6 +43,10 @@ SIGNATURES = {
     "lucid_solve_fwd_noalloc": (c_int, [c_int] * 4 + [c_float, c_float] + [c_void_p] + S3 + [c_void_p] + S3
                                 + [c_void_p] * 5 + [c_void_p]),
     "lucid_solve_fwd_noalloc_status": (c_int, [c_void_p, c_void_p]),
+    "lucid_fused_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
+    "lucid_fused_fwd": (c_int, [c_int] * 5 + [c_float, c_float] + ([c_void_p] + S3) * 3 + [c_void_p] * 3
+                        + [c_void_p, c_void_p] + [c_void_p] + S3 + [c_void_p, c_void_p]
+                        + [c_void_p, c_size_t, c_void_p]),
     "lucid_attn_fwd_workspace_bytes": (c_size_t, [c_int] * 5),
     "lucid_attn_fwd": (c_int, [c_int] * 5 + [c_float] + [c_void_p] + S3 + [c_void_p] + S3 + [c_void_p]
                        + [c_void_p] + S3 + [c_void_p, c_void_p] + [c_void_p, c_size_t, c_void_p]),

@@ -11,6 +11,8 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t st);
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st);
 int solve_chain_ctas(int BH, int NB);
+cudaError_t launch_fwd_fused(const CUtensorMap& tKhat, const CUtensorMap& tX, const CUtensorMap& tU,
+                             const CUtensorMap& tQ, const CUtensorMap& tK, const FwdArgs& a, cudaStream_t st);
 cudaError_t launch_bwd_col(bool solve, const CUtensorMap& tA1, const CUtensorMap& tA2, const CUtensorMap& tB1,
                            const CUtensorMap& tB2, const CUtensorMap& tU, const BwdArgs& a,
                            cudaStream_t st);
@@ -120,12 +122,27 @@ size_t lucid_solve_fwd_fast_workspace_bytes(int B, int H, int N, int D) {
   return base + chain_extra_bytes(B, H, N);
 }
 
-int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const void* k, int64_t k_sb,
-                    int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
-                    void* x, void* khat, void* u, float* rstd, float* dinv, void* workspace,
-                    size_t workspace_bytes, void* stream) {
-  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
-  if (empty_problem(B, H, H, N)) return LUCID_OK;
+}  // extern "C"
+
+namespace {
+// The attention half of lucid_fused_fwd (q, o, lse, o_res of Hq query heads).
+struct AttnPart {
+  int Hq;
+  const void* q;
+  int64_t q_sb, q_sh, q_sn;
+  void* o;
+  int64_t o_sb, o_sh, o_sn;
+  float* lse;
+  void* o_res;
+};
+
+// lucid_solve_fwd, and with `at` the attention after it: fused into the chain
+// schedule's launch when that schedule runs, else a second launch on the same
+// status word.
+int solve_fwd_impl(int B, int H, int N, int D, float scale, float eps, const void* k, int64_t k_sb, int64_t k_sh,
+                   int64_t k_sn, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn, void* x, void* khat,
+                   void* u, float* rstd, float* dinv, void* workspace, size_t workspace_bytes, void* stream,
+                   const AttnPart* at) {
   if (!aligned16(k) || !aligned16(v) || !aligned16(x) || !aligned16(khat) || !aligned16(u) ||
       !aligned16(rstd) || !aligned16(dinv) || !strides_ok(k_sb, k_sh, k_sn) ||
       !strides_ok(v_sb, v_sh, v_sn))
@@ -175,8 +192,71 @@ int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const vo
     fa.etiles = reinterpret_cast<bf16*>(extra + cflag_bytes +
                                         (size_t)B * H * kChainWRing * kBlock * kHeadDim * sizeof(float));
   }
-  ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
-  return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
+  if (!at) {
+    ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
+    return to_status(launch_fwd(true, tK, tK, tX, tU, fa, st));
+  }
+  CUtensorMap tQ, tKr;
+  if (!tmap_strided(&tQ, at->q, B, at->Hq, N, at->q_sb, at->q_sh, at->q_sn) ||
+      !tmap_strided(&tKr, k, B, H, N, k_sb, k_sh, k_sn))
+    return LUCID_ERR_TENSORMAP;
+  FwdArgs fb = fa;
+  fb.Hq = at->Hq;
+  fb.o = static_cast<bf16*>(at->o); fb.o_sb = at->o_sb; fb.o_sh = at->o_sh; fb.o_sn = at->o_sn;
+  fb.lse = at->lse;
+  fb.o_res = static_cast<bf16*>(at->o_res);
+  if (nchain > 0) {
+    fb.attn_scale = scale;  // the layer uses one scale for both (modeling_lucid.py:204)
+    ProfileScope ps(LUCID_KERNEL_FWD_FUSED, st);
+    return to_status(launch_fwd_fused(tK, tX, tU, tQ, tKr, fb, st));
+  }
+  {
+    ProfileScope ps(LUCID_KERNEL_SOLVE_FWD, st);
+    e = launch_fwd(true, tK, tK, tX, tU, fa, st);
+  }
+  if (e != cudaSuccess) return LUCID_ERR_LAUNCH;
+  FwdArgs fc{};
+  fc.B = B; fc.Hq = at->Hq; fc.Hkv = H; fc.N = N; fc.NB = NB; fc.Npad = Npad;
+  fc.scale = scale;
+  fc.o = fb.o; fc.o_sb = fb.o_sb; fc.o_sh = fb.o_sh; fc.o_sn = fb.o_sn;
+  fc.lse = fb.lse;
+  fc.o_res = fb.o_res;
+  fc.status = status;
+  ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
+  return to_status(launch_fwd(false, tQ, tKr, tX, tX, fc, st));
+}
+}  // namespace
+
+extern "C" {
+
+int lucid_solve_fwd(int B, int H, int N, int D, float scale, float eps, const void* k, int64_t k_sb,
+                    int64_t k_sh, int64_t k_sn, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                    void* x, void* khat, void* u, float* rstd, float* dinv, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, H, H, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, H, H, N)) return LUCID_OK;
+  return solve_fwd_impl(B, H, N, D, scale, eps, k, k_sb, k_sh, k_sn, v, v_sb, v_sh, v_sn, x, khat, u, rstd, dinv,
+                        workspace, workspace_bytes, stream, nullptr);
+}
+
+size_t lucid_fused_fwd_workspace_bytes(int B, int Hq, int Hkv, int N, int D) {
+  (void)Hq;
+  return lucid_solve_fwd_fast_workspace_bytes(B, Hkv, N, D);
+}
+
+int lucid_fused_fwd(int B, int Hq, int Hkv, int N, int D, float scale, float eps, const void* q, int64_t q_sb,
+                    int64_t q_sh, int64_t q_sn, const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                    const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sn, void* x, void* khat, void* u,
+                    float* rstd, float* dinv, void* o, int64_t o_sb, int64_t o_sh, int64_t o_sn, float* lse,
+                    void* o_res, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!shape_ok(B, Hq, Hkv, N, D)) return LUCID_ERR_SHAPE;
+  if (empty_problem(B, Hq, Hkv, N)) return LUCID_OK;
+  if (!aligned16(q) || !aligned16(o) || !aligned16(lse) || (o_res && !aligned16(o_res)) ||
+      !strides_ok(q_sb, q_sh, q_sn) || !strides_ok(o_sb, o_sh, o_sn))
+    return LUCID_ERR_ALIGN;
+  const AttnPart at{Hq, q, q_sb, q_sh, q_sn, o, o_sb, o_sh, o_sn, lse, o_res};
+  return solve_fwd_impl(B, Hkv, N, D, scale, eps, k, k_sb, k_sh, k_sn, v, v_sb, v_sh, v_sn, x, khat, u, rstd, dinv,
+                        workspace, workspace_bytes, stream, &at);
 }
 
 // ---------------------------------------------------------------------------

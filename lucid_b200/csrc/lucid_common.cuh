@@ -57,6 +57,8 @@ struct FwdArgs {
   // E_{i,i-kChainLook} .. E_{i,i-1} (bf16, in the shared-memory image of a K-major
   // operand tile)
   int nchain = 0;
+  float attn_scale = 0.f;    // fused launch: the attention items' softmax scale
+  int fuse_lag = 2;          // fused launch: attention pair p follows the solve items of pair p + fuse_lag
   int* cflags = nullptr;     // [B*Hkv][NB]: 1 = E tiles of row block i written, 2 = W_i too
   float* wring = nullptr;    // [B*Hkv][kChainWRing][32][128][4] fp32
   bf16* etiles = nullptr;    // [B*Hkv][NB][kChainLook][128*128] bf16

@@ -24,6 +24,12 @@
 //     row log-sum-exp for the backward.  Grouped-query heads index kv head =
 //     q head / (Hq / Hkv)  (repeat_kv, modeling_lucid.py:523-524).
 //
+//   FUSED  (the layer's forward, modeling_lucid.py:463 then :489): the chain
+//     schedule's solve and the attention in one launch.  The workers take the
+//     attention row-block pairs after their solve items, in increasing pair order,
+//     and wait per tile for the X block's flag, so the attention of early rows runs
+//     while the chains still produce later X blocks.
+//
 // A work item is a PAIR of consecutive row blocks (i0 = 2p, i1 = 2p+1) of one
 // head: both rows share every K / X tile load, which halves the L2->SM
 // traffic per FLOP.  Warp roles (320 threads): warpgroup 0 (warps 0-3) owns
@@ -299,14 +305,22 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
   }
 }
 
+// Tensor maps: solve items read their rows' normalised keys through tmA, the key tiles
+// through tmB, X through tmC and the diagonal-block inverses through tmU; attention
+// items read Q through tmQ, the raw keys through tmK and X through tmC.
 template <int MODE>
 __global__ void __launch_bounds__(fwd::kThreads, 1)
     lucid_fwd_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmU,
+                     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      FwdArgs p) {
   using namespace fwd;
-  // MODE 0: attention; 1: solve, wavefront schedule; 2: solve, chain schedule
-  constexpr bool SOLVE = MODE != 0, CHAIN = MODE == 2;
+  // MODE 0: attention; 1: solve, wavefront schedule; 2: solve, chain schedule;
+  // 3: chain-schedule solve, then attention (fused)
+  constexpr bool SOLVE = MODE != 0;              // the launch has solve items
+  constexpr bool CHAIN = MODE == 2 || MODE == 3;
+  constexpr bool FUSED = MODE == 3;
+  constexpr bool ATTN = MODE == 0 || FUSED;      // the launch has attention items
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + kOffBar;
@@ -356,6 +370,10 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
     if (SOLVE) tma_prefetch_desc(&tmU);
+    if (ATTN) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+    }
   }
   if (warp == kWarpMma) {
     tmem_alloc(smem_u32(tmem_slot), 512);
@@ -370,20 +388,55 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   const int G = p.Hq / p.Hkv;
   const int NP = (p.NB + 1) / 2;
   const int NPe = p.pp1 > 0 ? p.pp1 : NP;  // one past the last pair processed
-  const int total = SOLVE ? (NPe - p.pp0) * BHk : (NPe - p.pp0) * BHq;
+  const int n_solve = SOLVE ? (NPe - p.pp0) * BHk : 0;
+  const int total = n_solve + (ATTN ? (NPe - p.pp0) * BHq : 0);
+  // Fused item order: the solve items of pairs 0 .. lag-1, then per pair p >= lag the
+  // solve items of pair p followed by the attention items of pair p - lag, then the
+  // attention items of the last lag pairs.  Every item depends only on items before
+  // it in this order (attention pair q reads X up to block 2q+1, which the chains
+  // produce from the solve items of pairs <= q), and every CTA takes its items in
+  // this order, so the earliest unfinished item can always progress.
+  const int lag = FUSED ? (p.fuse_lag < NP ? p.fuse_lag : NP) : 0;
+  const int mid = (NP - lag) * (BHk + BHq);
+  // -> (solve item?, pair, (batch, head) index)
+  auto locate = [&](int idx, bool& sv, int& pp, int& bh) {
+    if (!FUSED) {
+      sv = SOLVE;
+      pp = SOLVE ? p.pp0 + idx / BHk : NPe - 1 - idx / BHq;  // solve: wavefront order; attention: longest first
+      bh = SOLVE ? idx % BHk : idx % BHq;
+      return;
+    }
+    int r = idx;
+    if (r < lag * BHk) {
+      sv = true; pp = r / BHk; bh = r % BHk;
+      return;
+    }
+    r -= lag * BHk;
+    if (r < mid) {
+      const int blk = r / (BHk + BHq), off = r % (BHk + BHq);
+      sv = off < BHk;
+      pp = sv ? lag + blk : blk;
+      bh = sv ? off : off - BHk;
+      return;
+    }
+    r -= mid;
+    sv = false; pp = NP - lag + r / BHq; bh = r % BHq;
+  };
+  auto is_solve = [&](int idx) {
+    bool sv; int pp, bh;
+    locate(idx, sv, pp, bh);
+    return sv;
+  };
 
   // Work item -> (pair pp, batch b, A-operand head ha, kv head hk).
-  // Solve: increasing pair index (wavefront).  Attention: longest pairs first.
   auto decode = [&](int idx, int& pp, int& b, int& ha, int& hk) {
-    if (SOLVE) {
-      pp = p.pp0 + idx / BHk;
-      const int bh = idx % BHk;
+    bool sv; int bh;
+    locate(idx, sv, pp, bh);
+    if (sv) {
       b = bh / p.Hkv;
       hk = bh % p.Hkv;
       ha = hk;
     } else {
-      pp = NPe - 1 - idx / BHq;
-      const int bh = idx % BHq;
       b = bh / p.Hq;
       ha = bh % p.Hq;
       hk = ha / G;
@@ -394,11 +447,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
   // its tail).
   // Chain schedule: row block i = 2pp + k streams the tiles j < i - kChainLook (its
   // chain multiplies the blocks i - kChainLook .. i - 1).
-  auto nrow = [&](int pp, int k) -> int {
+  auto nrow = [&](int pp, int k, bool sv) -> int {
     const bool r1 = (2 * pp + 1) < p.NB;
     if (k == 1 && !r1) return 0;
+    if (!sv) return 2 * pp + 1 + k;
     if (CHAIN) return 2 * pp - kChainLook + k > 0 ? 2 * pp - kChainLook + k : 0;
-    return SOLVE ? 2 * pp : 2 * pp + 1 + k;
+    return 2 * pp;
   };
   // Chain schedule: the E tiles of both rows come from the key blocks
   // j = 2pp - kChainLook + e (e = 0 .. kChainLook); row k uses them as its tile e - k.
@@ -436,30 +490,33 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       for (int idx = cta0; idx < total && ok; idx += ncta, ++item) {
         int pp, b, ha, hk;
         decode(idx, pp, b, ha, hk);
+        const bool solve_item = is_solve(idx);
         const int i0 = 2 * pp;
         const bool r1 = i0 + 1 < p.NB;
         if (!mbar_wait(bar(Q_EMPTY), (item & 1) ^ 1, ab)) break;
         last_q = item & 1;
         mbar_arrive_expect_tx(bar(Q_FULL), r1 ? 65536 : 32768);
-        tma_load_tile(sQ(0), &tmA, bar(Q_FULL), i0 * 128, ha, b);
-        if (r1) tma_load_tile(sQ(1), &tmA, bar(Q_FULL), (i0 + 1) * 128, ha, b);
-        if (CHAIN) {
+        const CUtensorMap* mA = solve_item ? &tmA : &tmQ;
+        const CUtensorMap* mB = solve_item ? &tmB : &tmK;
+        tma_load_tile(sQ(0), mA, bar(Q_FULL), i0 * 128, ha, b);
+        if (r1) tma_load_tile(sQ(1), mA, bar(Q_FULL), (i0 + 1) * 128, ha, b);
+        if (CHAIN && solve_item) {
           // the key blocks of the tiles handed to the chain (no X needed)
           for (int e = 0; e <= kChainLook && ok; ++e)
             if (etile_used(pp, e, 0) || etile_used(pp, e, 1))
               ok = loadK(&tmB, (2 * pp - kChainLook + e) * 128, hk, b);
           if (!ok) break;
         }
-        const int nt = nrow(pp, 0) > nrow(pp, 1) ? nrow(pp, 0) : nrow(pp, 1);
+        const int nt = nrow(pp, 0, solve_item) > nrow(pp, 1, solve_item) ? nrow(pp, 0, solve_item) : nrow(pp, 1, solve_item);
         for (int j = 0; j < nt; ++j) {
-          if (!loadK(&tmB, j * 128, hk, b)) { ok = false; break; }
-          if (SOLVE) {
+          if (!loadK(mB, j * 128, hk, b)) { ok = false; break; }
+          if (solve_item || FUSED) {  // X_j is still being produced
             if (!wait_flag_geq(&p.flags[(b * p.Hkv + hk) * p.NB + j], 1, ab)) { ok = false; break; }
             fence_proxy_async_global();
           }
           if (!loadX(j * 128, hk, b)) { ok = false; break; }
         }
-        if (!ok || !SOLVE || CHAIN) continue;
+        if (!ok || !solve_item || CHAIN) continue;
         // solve tail: K^_{2pp} for row 1, U_i0, U_i1, then X_{2pp} (made by row 0 of this item)
         if (r1 && !loadK(&tmB, i0 * 128, hk, b)) break;
         if (!loadK(&tmU, i0 * 128, hk, b)) break;
@@ -502,13 +559,14 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       for (int idx = cta0; idx < total; idx += ncta, ++item) {
         int pp, b, ha, hk;
         decode(idx, pp, b, ha, hk);
+        const bool solve_item = is_solve(idx);
         const int i0 = 2 * pp;
         const bool r1 = i0 + 1 < p.NB;
-        const int n0 = nrow(pp, 0), n1 = nrow(pp, 1), nt = n0 > n1 ? n0 : n1;
+        const int n0 = nrow(pp, 0, solve_item), n1 = nrow(pp, 1, solve_item), nt = n0 > n1 ? n0 : n1;
         if (!mbar_wait(bar(Q_FULL), item & 1, ab)) break;
         tc_fence_after();
         bool ok = true;
-        if (CHAIN) {
+        if (CHAIN && solve_item) {
           // S of the tiles handed to the chain; the epilogue reads each S_k before the
           // next GEMM into that region (P_FULL, with no PV in between)
           bool busy[2] = {false, false};
@@ -558,7 +616,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         if (!ok) break;
         kidx = kb + nt;
         xidx = xb + nt;
-        if (SOLVE && !CHAIN) {
+        if (solve_item && !CHAIN) {
           // tail: S1(2pp), DIAG0, PV1(2pp), DIAG1
           if (r1) {
             if (!waitK(kidx)) break;
@@ -603,15 +661,18 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
     const uint32_t tOk = tmem + lane_base + fwd::kTmO0 + 128u * (uint32_t)k;
     const int wg_thread0 = k * 128;     // publishes this warpgroup's flags
     const float kLog2e = 1.4426950408889634f;
-    const float c1 = p.scale * kLog2e;
-    const float c2 = kLog2e / p.scale;
+    const float ascale = FUSED ? p.attn_scale : p.scale;  // softmax scale of attention items
     uint32_t n_sfull = 0, n_p = 0, n_epi = 0, item = 0;
     for (int idx = cta0; idx < total; idx += ncta, ++item) {
       int pp, b, ha, hk;
       decode(idx, pp, b, ha, hk);
+      const bool solve_item = is_solve(idx);
       const int i = 2 * pp + k;         // this warpgroup's row block
       if (i >= p.NB) continue;
-      const int nk = nrow(pp, k) + ((SOLVE && !CHAIN && k == 1) ? 1 : 0);  // wavefront row 1 adds tile 2pp
+      const float sc = solve_item ? p.scale : ascale;
+      const float c1 = sc * kLog2e;
+      const float c2 = kLog2e / sc;
+      const int nk = nrow(pp, k, solve_item) + ((solve_item && !CHAIN && k == 1) ? 1 : 0);  // wavefront row 1 adds tile 2pp
       const int row = i * 128 + r;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
@@ -628,7 +689,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         ++n_epi;
         __syncwarp();
       };
-      if (CHAIN) {
+      if (CHAIN && solve_item) {
         // E_{i,i-kChainLook} .. E_{i,i-1} (row r) -> global, in the shared-memory image of
         // a K-major operand tile, which the chain copies unchanged
         const long long bhk = (long long)b * p.Hkv + hk;
@@ -660,7 +721,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         if (!ok) break;
         publish(&p.cflags[bhk * p.NB + i], 1);
       }
-      if (SOLVE && row < p.N) {
+      if (solve_item && row < p.N) {
         // the diagonal step reads this row of V on the wavefront's critical path: fetch
         // it into L2 while the row's streaming tiles run
         const bf16* vrow = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh + (long long)row * p.v_sn;
@@ -674,7 +735,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld32(tSk + 32u * q, sv[q]);
         tmem_ld_wait();
-        if (SOLVE) {
+        if (solve_item) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
@@ -762,7 +823,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[q][e] = 0.f;
       }
-      if (!SOLVE) {
+      if (!solve_item) {
         const float inv_l = 1.f / l_run;
         if (row < p.N) {
           bf16* orow = p.o + (long long)b * p.o_sb + (long long)ha * p.o_sh + (long long)row * p.o_sn;
@@ -892,6 +953,7 @@ static int num_sms() {
 
 cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                        const CUtensorMap& tU, const FwdArgs& a, cudaStream_t st) {
+  // attention alone: Q and K come through tmQ / tmK (passed as tA / tB)
   const int pairs = (a.pp1 > 0 ? a.pp1 : (a.NB + 1) / 2) - a.pp0;
   const int total = solve ? pairs * a.B * a.Hkv : pairs * a.B * a.Hq;
   if (total <= 0) return cudaSuccess;
@@ -904,7 +966,8 @@ cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB,
     e = cudaFuncSetAttribute(lucid_fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
-    return launch_cooperative(lucid_fwd_kernel<2>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
+    return launch_cooperative(lucid_fwd_kernel<2>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, tA, tB,
+                              a);
   }
   const int grid = std::min(total, cap);
   if (solve) {
@@ -912,14 +975,32 @@ cudaError_t launch_fwd(bool solve, const CUtensorMap& tA, const CUtensorMap& tB,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
     // the wavefront's CTAs wait on one another's flags: all of them must be resident
-    return launch_cooperative(lucid_fwd_kernel<1>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, a);
+    return launch_cooperative(lucid_fwd_kernel<1>, grid, fwd::kThreads, fwd::kSmemBytes, st, tA, tB, tC, tU, tA, tB,
+                              a);
   } else {
     e = cudaFuncSetAttribute(lucid_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)fwd::kSmemBytes);
     if (e != cudaSuccess) return e;
-    lucid_fwd_kernel<0><<<grid, fwd::kThreads, fwd::kSmemBytes, st>>>(tA, tB, tC, tU, a);
+    lucid_fwd_kernel<0><<<grid, fwd::kThreads, fwd::kSmemBytes, st>>>(tA, tB, tC, tU, tA, tB, a);
   }
   return cudaGetLastError();
+}
+
+// Fused forward (chain schedule, a.nchain = B*Hkv chains): the solve's items, then the
+// attention's, in one cooperative launch.
+cudaError_t launch_fwd_fused(const CUtensorMap& tKhat, const CUtensorMap& tX,
+                             const CUtensorMap& tU, const CUtensorMap& tQ, const CUtensorMap& tK,
+                             const FwdArgs& a, cudaStream_t st) {
+  const int pairs = (a.NB + 1) / 2;
+  const int total = pairs * a.B * (a.Hkv + a.Hq);
+  const int cap = num_sms();
+  if (a.pp0 != 0 || a.pp1 != 0 || a.nchain != a.B * a.Hkv || a.nchain >= cap) return cudaErrorInvalidValue;
+  const int grid = std::min(a.nchain + total, cap);
+  cudaError_t e = cudaFuncSetAttribute(lucid_fwd_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)fwd::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return launch_cooperative(lucid_fwd_kernel<3>, grid, fwd::kThreads, fwd::kSmemBytes, st, tKhat, tKhat, tX, tU, tQ, tK,
+                            a);
 }
 
 // Schedule of the solve forward for B*H heads of NB row blocks on this device: the

@@ -36,7 +36,7 @@ import torch
 from . import _lib
 
 __all__ = [
-    "solve_fwd", "attn_fwd", "attn_bwd", "solve_bwd",
+    "solve_fwd", "attn_fwd", "fused_fwd", "attn_bwd", "solve_bwd",
     "LucidSolveFunction", "LucidAttnFunction", "LucidAttentionFunction",
     "lucid_attention", "padded_len", "decode_update", "decode_attention", "decode_step", "decode_step_fused",
     "stored_tiles_fit", "check_status",
@@ -122,6 +122,41 @@ def solve_fwd(k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int
     _lib.check(rc, "lucid_solve_fwd")
     _lib.STATUS.watch(ws, "lucid_solve_fwd")
     return x, khat, u, rstd, dinv
+
+
+def fused_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, eps: float, d: int | None = None):
+    """solve_fwd then attn_fwd (with the residual) in one library call, which runs them
+    as one launch under the solve's chain schedule.  Returns
+    (x_int, khat, u, rstd, dinv, o, lse, o_res) as the two stages do."""
+    lib = _lib.load()
+    _lib.STATUS.poll()
+    q = _prep(q, "query")
+    k = _prep(k, "key")
+    v = _prep(v, "value")
+    B, Hq, N, W = q.shape
+    Hkv = k.shape[1]
+    D = W if d is None else d
+    if k.shape != (B, Hkv, N, W) or v.shape != k.shape:
+        raise ValueError(f"query {tuple(q.shape)}, key {tuple(k.shape)} and value {tuple(v.shape)} do not match")
+    Np = padded_len(N)
+    dev = k.device
+    x = torch.empty(B, Hkv, Np, W, dtype=torch.bfloat16, device=dev)
+    khat = torch.empty(B, Hkv, Np, W, dtype=torch.bfloat16, device=dev)
+    u = torch.empty(B, Hkv, Np, 128, dtype=torch.bfloat16, device=dev)
+    rstd = torch.empty(B, Hkv, Np, dtype=torch.float32, device=dev)
+    dinv = torch.empty(B, Hkv, Np, dtype=torch.float32, device=dev)
+    o = torch.empty(B, N, Hq, W, dtype=torch.bfloat16, device=dev)
+    ot = o.transpose(1, 2)
+    lse = torch.empty(B, Hq, Np, dtype=torch.float32, device=dev)
+    o_res = torch.empty_like(o)
+    ws = _ws(lib.lucid_fused_fwd_workspace_bytes(B, Hq, Hkv, N, D), dev)
+    rc = lib.lucid_fused_fwd(B, Hq, Hkv, N, D, float(scale), float(eps), q.data_ptr(), *_s3(q), k.data_ptr(),
+                             *_s3(k), v.data_ptr(), *_s3(v), x.data_ptr(), khat.data_ptr(), u.data_ptr(),
+                             rstd.data_ptr(), dinv.data_ptr(), ot.data_ptr(), *_s3(ot), lse.data_ptr(),
+                             o_res.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "lucid_fused_fwd")
+    _lib.STATUS.watch(ws, "lucid_fused_fwd")
+    return x, khat, u, rstd, dinv, o, lse, o_res
 
 
 def attn_fwd(q: torch.Tensor, k: torch.Tensor, x_int: torch.Tensor, scale: float, d: int | None = None,
@@ -267,8 +302,7 @@ class LucidAttentionFunction(torch.autograd.Function):
         D = key.shape[-1]
         k = _prep(_pad128(key), "key")
         q = _prep(_pad128(query), "query")
-        x, khat, u, rstd, dinv = solve_fwd(k, _pad128(value), scaling, eps, d=D)
-        o, lse, o_res = attn_fwd(q, k, x, scaling, d=D, residual=True)
+        x, khat, u, rstd, dinv, o, lse, o_res = fused_fwd(q, k, _pad128(value), scaling, eps, d=D)
         ctx.save_for_backward(q, k, x, khat, u, rstd, dinv, o, lse, o_res)
         ctx.scaling, ctx.d = scaling, D
         return o if D == 128 else o[..., :D]

@@ -119,6 +119,32 @@ def test_solve_fwd_chain_and_wavefront_schedules(cuda_device, monkeypatch, B, H,
     assert float(diff.max()) <= 2e-2 * max(1.0, float(np.abs(ref).max()))
 
 
+@pytest.mark.parametrize("sched", ["chain", "wavefront"])
+@pytest.mark.parametrize("B,Hq,Hkv,N", [(1, 2, 2, 1000), (2, 4, 2, 300), (1, 8, 2, 2048), (1, 1, 1, 128)])
+def test_fused_fwd_equals_two_stages(cuda_device, monkeypatch, sched, B, Hq, Hkv, N):
+    """lucid_fused_fwd (one launch under the chain schedule, two under the wavefront) gives
+    exactly the solve's and the attention's outputs of the separate calls."""
+    import torch
+    from lucid_b200 import _lib, attn_fwd, fused_fwd, solve_fwd
+    monkeypatch.setenv("LUCID_B200_SOLVE_SCHEDULE", sched)
+    q, k, v, _ = _rand_inputs(30 + N, B, Hq, Hkv, N, q_scale=128 ** -0.5)
+    qd, kd, vd = _t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device)
+    s = 128 ** -0.5
+    x1, kh1, u1, r1, d1 = solve_fwd(kd, vd, s, 1e-5)
+    o1, lse1, res1 = attn_fwd(qd, kd, x1, s, residual=True)
+    x2, kh2, u2, r2, d2, o2, lse2, res2 = fused_fwd(qd, kd, vd, s, 1e-5)
+    _lib.check_status()
+    Np = x1.shape[2]
+    # rows from N on are padding, not written
+    for name, a, b_ in (("x", x1, x2), ("khat", kh1, kh2), ("u", u1, u2), ("rstd", r1, r2), ("dinv", d1, d2),
+                        ("lse", lse1, lse2)):
+        assert torch.equal(a[:, :, :N], b_[:, :, :N]), name
+    assert torch.equal(o1, o2) and torch.equal(res1, res2)
+    assert Np == x2.shape[2]
+    ref = orc.lucid_fwd(q, k, v, s, 1e-5)[0]
+    assert_bf16_close(_np(o2), ref, f"O (fused, {sched})")
+
+
 def test_solve_fwd_diag_block_inverse(cuda_device):
     """U = (I + L~)^-1 - I of every diagonal block, against numpy."""
     from lucid_b200 import solve_fwd
