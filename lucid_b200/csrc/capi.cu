@@ -46,6 +46,8 @@ constexpr size_t kStatusRegion = 256;
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 int npad_of(int N) { return ((N + 127) / 128) * 128; }
 int nb_of(int N) { return (N + 127) / 128; }
+// head dimension rounded up to the 16 columns of one MMA K-slice
+int d16_of(int D) { return D >= kHeadDim ? kHeadDim : ((D + 15) / 16) * 16; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool strides_ok(int64_t a, int64_t b, int64_t c) { return (a % 8 == 0) && (b % 8 == 0) && (c % 8 == 0); }
@@ -205,6 +207,7 @@ int solve_fwd_impl(int B, int H, int N, int D, float scale, float eps, const voi
   fb.o = static_cast<bf16*>(at->o); fb.o_sb = at->o_sb; fb.o_sh = at->o_sh; fb.o_sn = at->o_sn;
   fb.lse = at->lse;
   fb.o_res = static_cast<bf16*>(at->o_res);
+  fb.attn_d16 = d16_of(D);
   if (nchain > 0) {
     fb.attn_scale = scale;  // the layer uses one scale for both (modeling_lucid.py:204)
     ProfileScope ps(LUCID_KERNEL_FWD_FUSED, st);
@@ -221,6 +224,7 @@ int solve_fwd_impl(int B, int H, int N, int D, float scale, float eps, const voi
   fc.o = fb.o; fc.o_sb = fb.o_sb; fc.o_sh = fb.o_sh; fc.o_sn = fb.o_sn;
   fc.lse = fb.lse;
   fc.o_res = fb.o_res;
+  fc.attn_d16 = fb.attn_d16;
   fc.status = status;
   ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
   return to_status(launch_fwd(false, tQ, tKr, tX, tX, fc, st));
@@ -293,6 +297,7 @@ int lucid_attn_fwd(int B, int Hq, int Hkv, int N, int D, float scale, const void
   fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
   fa.lse = lse;
   fa.o_res = static_cast<bf16*>(o_res);
+  fa.attn_d16 = d16_of(D);
   fa.status = status;
   ProfileScope ps(LUCID_KERNEL_ATTN_FWD, st);
   return to_status(launch_fwd(false, tQ, tK, tX, tX, fa, st));
@@ -574,6 +579,7 @@ extern "C" int lucid_cp_attn_fwd(int B, int Hq, int Hkv, int N, int D, float sca
   fa.o = static_cast<bf16*>(o); fa.o_sb = o_sb; fa.o_sh = o_sh; fa.o_sn = o_sn;
   fa.lse = lse;
   fa.o_res = static_cast<bf16*>(o_res);
+  fa.attn_d16 = d16_of(D);
   fa.status = status;
   fa.pp0 = blk_lo / 2;
   fa.pp1 = (blk_hi + 1) / 2;

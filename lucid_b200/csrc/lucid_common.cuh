@@ -59,6 +59,10 @@ struct FwdArgs {
   int nchain = 0;
   float attn_scale = 0.f;    // fused launch: the attention items' softmax scale
   int fuse_lag = 2;          // fused launch: attention pair p follows the solve items of pair p + fuse_lag
+  // attention items: the head dimension rounded up to 16 (rows hold 128 elements, zero
+  // from D on): the K extent of Q K^T and the N extent of P X, and O's columns from it
+  // on are written as zeros
+  int attn_d16 = kHeadDim;
   int* cflags = nullptr;     // [B*Hkv][NB]: 1 = E tiles of row block i written, 2 = W_i too
   float* wring = nullptr;    // [B*Hkv][kChainWRing][32][128][4] fp32
   bf16* etiles = nullptr;    // [B*Hkv][NB][kChainLook][128*128] bf16

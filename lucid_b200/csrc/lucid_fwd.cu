@@ -542,8 +542,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       auto waitX = [&](uint32_t idx) { return mbar_wait(bar(X_FULL0 + (idx & 1u)), (idx >> 1) & 1, ab); };
       auto tS = [&](int k) { return tmem + kTmS0 + 128u * (uint32_t)k; };
       auto tO = [&](int k) { return tmem + kTmO0 + 128u * (uint32_t)k; };
+      int cur_d = kHeadDim;  // attention items: K extent of S and N extent of PV (head dimension)
       auto issue_s = [&](int k, uint32_t kslot) {
-        umma_tile(tS(k), sQ(k), false, sK(kslot), false, 0u);
+        if (cur_d == kHeadDim)
+          umma_tile(tS(k), sQ(k), false, sK(kslot), false, 0u);
+        else
+          umma_tile_part(tS(k), sQ(k), false, sK(kslot), false, 0u, cur_d / 16, 128);
         umma_commit(bar(S_FULL0 + k));
       };
       // PV_k of streaming tile t (x slot xs); first_pv: overwrite O_k
@@ -552,7 +556,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         if (first_pv && !mbar_wait(bar(O_FREE0 + k), ((n_ofree[k]++) & 1) ^ 1, ab)) return false;
         tc_fence_after();
         const uint32_t sreg = tS(k);
-        umma_tile_ts(tO(k), [&](int kk) { return sreg + 8u * (uint32_t)kk; }, sX(xs), true, first_pv ? 0u : 1u);
+        umma_tile_ts(tO(k), [&](int kk) { return sreg + 8u * (uint32_t)kk; }, sX(xs), true, first_pv ? 0u : 1u,
+                     cur_d);
         umma_commit(bar(O_DONE0 + k));
         return true;
       };
@@ -563,6 +568,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         const int i0 = 2 * pp;
         const bool r1 = i0 + 1 < p.NB;
         const int n0 = nrow(pp, 0, solve_item), n1 = nrow(pp, 1, solve_item), nt = n0 > n1 ? n0 : n1;
+        cur_d = solve_item ? kHeadDim : p.attn_d16;
         if (!mbar_wait(bar(Q_FULL), item & 1, ab)) break;
         tc_fence_after();
         bool ok = true;
@@ -825,6 +831,13 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       }
       if (!solve_item) {
         const float inv_l = 1.f / l_run;
+        if (p.attn_d16 < kHeadDim) {  // columns the P X product did not write
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (q * 32 + e >= p.attn_d16) acc[q][e] = 0.f;
+        }
         if (row < p.N) {
           bf16* orow = p.o + (long long)b * p.o_sb + (long long)ha * p.o_sh + (long long)row * p.o_sn;
 #pragma unroll

@@ -430,12 +430,24 @@ __device__ __forceinline__ void umma_tile(uint32_t d_tmem, uint32_t a_tile, bool
     umma_ss(d_tmem, desc_slice(a0, a_mn, kk), desc_slice(b0, b_mn, kk), idesc, (kk > 0) ? 1u : accumulate_first);
 }
 
-// The 8 K-slices of a 128x128x128 product whose A operand lives in TMEM.
+// The first nks K-slices (16 each) of a 128 x n product of two 128 x 128 tiles, n a
+// multiple of 16 up to 128: the product of operands whose columns from 16 nks (K) and
+// rows from n (B's N) on are zero, e.g. a head dimension below 128 zero-padded.
+__device__ __forceinline__ void umma_tile_part(uint32_t d_tmem, uint32_t a_tile, bool a_mn, uint32_t b_tile,
+                                               bool b_mn, uint32_t accumulate_first, int nks, int n) {
+  const uint32_t idesc = idesc_bf16(128, n, a_mn, b_mn);
+  const uint64_t a0 = desc_tile(a_tile, a_mn), b0 = desc_tile(b_tile, b_mn);
+  for (int kk = 0; kk < nks; ++kk)
+    umma_ss(d_tmem, desc_slice(a0, a_mn, kk), desc_slice(b0, b_mn, kk), idesc, (kk > 0) ? 1u : accumulate_first);
+}
+
+// The 8 K-slices of a 128x128x128 product whose A operand lives in TMEM (n < 128:
+// only the first n columns of B and of the product).
 // a_tmem(kk) gives the TMEM address of K-slice kk (8 columns of packed bf16).
 template <typename AddrFn>
 __device__ __forceinline__ void umma_tile_ts(uint32_t d_tmem, AddrFn a_tmem, uint32_t b_tile, bool b_mn,
-                                             uint32_t accumulate_first) {
-  const uint32_t idesc = idesc_bf16(128, 128, false, b_mn);
+                                             uint32_t accumulate_first, int n = 128) {
+  const uint32_t idesc = idesc_bf16(128, n, false, b_mn);
   const uint64_t b0 = desc_tile(b_tile, b_mn);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
