@@ -751,17 +751,23 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               sv[q][e + 1] = fast_exp2(a.y);
             }
         } else {
-          const bool diag = (t == i);
+          // Few instructions per score (the epilogue of two warpgroups issues as many
+          // instructions per tile as the tensor core needs cycles): the causal mask on the
+          // diagonal tile only, the max on the raw scores (the scale c1 > 0 is monotone),
+          // and the scale folded into one packed FMA ahead of the exponential.
+          if (t == i) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if ((q * 32 + e) > r) sv[q][e] = -INFINITY;
+          }
           float mx = -INFINITY;
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              float v = sv[q][e] * c1;
-              if (diag && (q * 32 + e) > r) v = -INFINITY;
-              sv[q][e] = v;
-              mx = fmaxf(mx, v);
-            }
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[q][e]);
+          mx *= c1;
           // lazy rescale: keep the running reference unless it grows by > 8 (log2)
           bool need = false;
           float alpha = 1.f;
@@ -788,17 +794,19 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
             tmem_st_wait();
           }
           l_run *= alpha;
-          float sum = 0.f;
+          const float2 cc = make_float2(c1, c1), nm = make_float2(-m_run, -m_run);
+          float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float2 a = add2(make_float2(sv[q][e], sv[q][e + 1]), make_float2(-m_run, -m_run));
-              sv[q][e] = fast_exp2(a.x);
-              sv[q][e + 1] = fast_exp2(a.y);
-              sum += sv[q][e] + sv[q][e + 1];
+              const float2 a = fma2(make_float2(sv[q][e], sv[q][e + 1]), cc, nm);
+              const float2 ex = make_float2(fast_exp2(a.x), fast_exp2(a.y));
+              sv[q][e] = ex.x;
+              sv[q][e + 1] = ex.y;
+              sum2 = add2(sum2, ex);
             }
-          l_run += sum;
+          l_run += sum2.x + sum2.y;
         }
         // P back into tensor memory over S_k (this lane's own columns)
 #pragma unroll
