@@ -49,6 +49,14 @@ struct Ph {
   __device__ __forceinline__ uint32_t empty() { return ((n++) & 1u) ^ 1u; }  // (k-1)-th completion
 };
 
+// One arrival per warp, after every lane's preceding stores and fences: a barrier that
+// counts warps completes after 16 arrivals instead of one per epilogue thread (the
+// arrivals are shared-memory atomics and serialise).
+__device__ __forceinline__ void warp_arrive(uint32_t bar) {
+  __syncwarp();
+  if (lane_id() == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ bool warp_wait_b(uint32_t bar, uint32_t parity, const Abort& ab) {
   const bool ok = mbar_wait(bar, parity, ab);
   return __all_sync(0xffffffffu, ok);
@@ -170,15 +178,15 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
     }
     mbar_init(bar(SD_FULL), 1);
     mbar_init(bar(DP_FULL), 1);
-    mbar_init(bar(PD_FULL), kColEpiThreads);
-    mbar_init(bar(DSP_FULL), kColEpiThreads);
+    mbar_init(bar(PD_FULL), kColEpiWarps);
+    mbar_init(bar(DSP_FULL), kColEpiWarps);
     mbar_init(bar(DS_FREE), 1);
     mbar_init(bar(T_FULL), 1);
-    mbar_init(bar(S_FREE), kColEpiThreads);
+    mbar_init(bar(S_FREE), kColEpiWarps);
     mbar_init(bar(ACC_FULL), 1);
     mbar_init(bar(ACC2_FULL), 1);
-    mbar_init(bar(ACC_FREE), kColEpiThreads);
-    mbar_init(bar(EPI_DONE), kColEpiThreads);
+    mbar_init(bar(ACC_FREE), kColEpiWarps);
+    mbar_init(bar(EPI_DONE), kColEpiWarps);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -493,7 +501,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(PD_FULL));
+        warp_arrive(bar(PD_FULL));
         // phase 2: dS (attention) / dG^T (solve) from dP and the P kept in registers,
         // packed into the dP region (and staged for the tile store)
         if (!warp_wait_b(bar(DP_FULL), dp_full.full(), ab)) { ok = false; break; }
@@ -555,7 +563,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(DSP_FULL));
+        warp_arrive(bar(DSP_FULL));
       }
       if (!ok) break;
       // solve: the diagonal step's dX row (this warp's columns) and 1 / P_rr, loaded while
@@ -610,7 +618,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(bar(ACC_FREE));
+        warp_arrive(bar(ACC_FREE));
         continue;
       }
       ++n_kv;  // the U_i load
@@ -632,7 +640,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
       for (int q = 0; q < kColQ; ++q) tile_store_row32(sDS, r, ch0 + q, rr[q]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar(PD_FULL));
+      warp_arrive(bar(PD_FULL));
       // D3: dV_i = D^-1 (R + U^T R) -> global bf16 and the smem tile; publish
       if (!warp_wait_b(bar(T_FULL), t_full.full(), ab) || !warp_wait_b(bar(DS_FREE), ds_free.empty(), ab))
         break;
@@ -650,11 +658,11 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         tile_store_row32(sDS, r, ch0 + q, tv);
       }
       tc_fence_before();
-      mbar_arrive(bar(S_FREE));
+      warp_arrive(bar(S_FREE));
       fence_proxy_async_smem();
-      mbar_arrive(bar(PD_FULL));
+      warp_arrive(bar(PD_FULL));
       // (the readers fence the async proxy after acquiring the flag, before their TMA loads)
-      mbar_arrive(bar(EPI_DONE));
+      warp_arrive(bar(EPI_DONE));
       if (threadIdx.x == 0) {   // publish: the CTA's dV rows, then the flag (one fence, cumulative)
         if (mbar_wait(bar(EPI_DONE), item & 1, ab)) {
           __threadfence();
@@ -681,9 +689,9 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
         tile_store_row32(sDS, r, ch0 + q, sv);
       }
       tc_fence_before();
-      mbar_arrive(bar(S_FREE));
+      warp_arrive(bar(S_FREE));
       fence_proxy_async_smem();
-      mbar_arrive(bar(PD_FULL));
+      warp_arrive(bar(PD_FULL));
       // D7: column part of dK^_i
       if (!warp_wait_b(bar(ACC2_FULL), acc2_full.full(), ab)) break;
       tc_fence_after();
@@ -699,7 +707,7 @@ __global__ void __launch_bounds__(bwdc::kColThreads, 1)
               make_float4(a2[4 * c], a2[4 * c + 1], a2[4 * c + 2], a2[4 * c + 3]);
       }
       tc_fence_before();
-      mbar_arrive(bar(ACC_FREE));
+      warp_arrive(bar(ACC_FREE));
     }
   }
 
@@ -760,10 +768,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(bar(X_EMPTY0 + s2), 1);
     }
     mbar_init(bar(SD_FULL), 1);
-    mbar_init(bar(DP_READ), kBwdEpiThreads);
-    mbar_init(bar(PD_FULL), kBwdEpiThreads);
+    mbar_init(bar(DP_READ), kBwdEpiWarps);
+    mbar_init(bar(PD_FULL), kBwdEpiWarps);
     mbar_init(bar(ACC_FULL), 1);
-    mbar_init(bar(ACC_FREE), kBwdEpiThreads);
+    mbar_init(bar(ACC_FREE), kBwdEpiWarps);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -933,7 +941,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld32(sreg + c0 + 32u, svv[1]);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(bar(DP_READ));
+        warp_arrive(bar(DP_READ));
         const bool full = SOLVE ? true : (i < j && (j + 1) * 128 <= p.N);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -984,7 +992,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(PD_FULL));
+        warp_arrive(bar(PD_FULL));
       }
       if (!ok) break;
       if (!warp_wait_b(bar(ACC_FULL), acc_full.full(), ab)) break;
@@ -1001,7 +1009,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int e = 0; e < 32; ++e) av[q][e] = 0.f;
       }
       tc_fence_before();
-      mbar_arrive(bar(ACC_FREE));
+      warp_arrive(bar(ACC_FREE));
       if (SOLVE) {
         float* dst = p.dk_row + (bha * p.Npad + row) * kHeadDim + c0;
 #pragma unroll
@@ -1077,7 +1085,7 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
     }
     for (int a2 = 0; a2 < 2; ++a2) {
       mbar_init(bar(ACC_FULL0 + a2), 1);
-      mbar_init(bar(ACC_FREE0 + a2), 128);
+      mbar_init(bar(ACC_FREE0 + a2), 4);  // one arrival per warp
     }
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
@@ -1200,7 +1208,7 @@ __global__ void __launch_bounds__(bwds::kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(bar(ACC_FREE0 + ab2));
+      warp_arrive(bar(ACC_FREE0 + ab2));
     }
   }
 

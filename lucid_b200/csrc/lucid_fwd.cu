@@ -68,6 +68,13 @@ constexpr uint32_t kSmemBytes = kOffBar + NBAR * 8 + 16;
 constexpr uint32_t kTmS0 = 0, kTmO0 = 256;
 }  // namespace fwd
 
+// One arrival per warp, after every lane's preceding stores and fences: the epilogue
+// barriers count warps (the arrivals are shared-memory atomics and serialise).
+__device__ __forceinline__ void warp_arrive(uint32_t bar) {
+  __syncwarp();
+  if (lane_id() == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
   const bool ok = mbar_wait(bar, parity, ab);
   return __all_sync(0xffffffffu, ok);
@@ -115,10 +122,10 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
     mbar_init(bar(UFULL), 1);
     mbar_init(bar(UEMPTY), 1);
     mbar_init(bar(ACC), 1);
-    mbar_init(bar(YF), kEpiThreads);
+    mbar_init(bar(YF), kEpiThreads / 32);
     mbar_init(bar(TF), 1);
-    mbar_init(bar(XR), kEpiThreads);
-    for (int s = 0; s < kEpiRing; ++s) mbar_init(bar(EPI0 + s), kEpiThreads);
+    mbar_init(bar(XR), kEpiThreads / 32);
+    for (int s = 0; s < kEpiRing; ++s) mbar_init(bar(EPI0 + s), kEpiThreads / 32);
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
     fence_mbar_init();
@@ -271,7 +278,7 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar(YF));
+      warp_arrive(bar(YF));
       // X_i = Y + U_i Y: into the slot (operand of steps i+1 .. i+L) and to global memory
       if (!warp_wait(bar(TF), (uint32_t)i & 1, ab)) break;
       tc_fence_after();
@@ -286,14 +293,14 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar(XR));
+      warp_arrive(bar(XR));
       bf16* xrow = p.x + (bhk * p.Npad + row) * kHeadDim + 64 * h;
 #pragma unroll
       for (int q = 0; q < 2; ++q)
 #pragma unroll
         for (int c = 0; c < 4; ++c) st_bf16x8(xrow + q * 32 + c * 8, y[q] + c * 8);
       fence_proxy_async_global();
-      mbar_arrive(bar(EPI0 + i % kEpiRing));
+      warp_arrive(bar(EPI0 + i % kEpiRing));
     }
   }
   tc_fence_before();
@@ -357,11 +364,11 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       mbar_init(bar(X_FULL0 + s2), 1);
       mbar_init(bar(X_EMPTY0 + s2), 1);
       mbar_init(bar(S_FULL0 + s2), 1);
-      mbar_init(bar(P_FULL0 + s2), 128);
+      mbar_init(bar(P_FULL0 + s2), 4);  // one arrival per warp of the warpgroup
       mbar_init(bar(O_DONE0 + s2), 1);
-      mbar_init(bar(O_FREE0 + s2), 128);
-      mbar_init(bar(Y_FULL0 + s2), 128);
-      mbar_init(bar(EPI_DONE0 + s2), 128);
+      mbar_init(bar(O_FREE0 + s2), 4);  // one arrival per warp of the warpgroup
+      mbar_init(bar(Y_FULL0 + s2), 4);  // one arrival per warp of the warpgroup
+      mbar_init(bar(EPI_DONE0 + s2), 4);  // one arrival per warp of the warpgroup
     }
     mbar_init(bar(DRAIN), 1);
     *abort_cta = 0;
@@ -685,7 +692,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       // chain schedule: make this row's writes visible, then release its chain flag
       auto publish = [&](int* flag, int value) {
         fence_proxy_async_global();
-        mbar_arrive(bar(EPI_DONE0 + k));
+        warp_arrive(bar(EPI_DONE0 + k));
         if ((int)threadIdx.x == wg_thread0) {
           if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) {
             __threadfence();
@@ -722,7 +729,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
                   make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
           }
           tc_fence_before();
-          mbar_arrive(bar(P_FULL0 + k));
+          warp_arrive(bar(P_FULL0 + k));
         }
         if (!ok) break;
         publish(&p.cflags[bhk * p.NB + i], 1);
@@ -818,7 +825,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(P_FULL0 + k));
+        warp_arrive(bar(P_FULL0 + k));
       }
       if (!ok) break;
       // O_k is final once the PV of the last tile of this row is done
@@ -830,7 +837,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
         for (int q = 0; q < 4; ++q) tmem_ld32(tOk + 32u * q, acc[q]);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(bar(O_FREE0 + k));
+        warp_arrive(bar(O_FREE0 + k));
       } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -923,7 +930,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
 #pragma unroll
       for (int q = 0; q < 4; ++q) tile_store_row32(sQ(k), r, q, acc[q]);
       fence_proxy_async_smem();
-      mbar_arrive(bar(Y_FULL0 + k));
+      warp_arrive(bar(Y_FULL0 + k));
       if (!warp_wait(bar(S_FULL0 + k), (n_sfull++) & 1, ab)) break;
       tc_fence_after();
       bf16* xrow = p.x + (bhk * p.Npad + row) * kHeadDim;
@@ -939,7 +946,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
       }
       tc_fence_before();
       fence_proxy_async_global();
-      mbar_arrive(bar(EPI_DONE0 + k));
+      warp_arrive(bar(EPI_DONE0 + k));
       if ((int)threadIdx.x == wg_thread0) {   // publish: the rows of X, then the flag (one fence, cumulative)
         if (mbar_wait(bar(EPI_DONE0 + k), n_epi & 1, ab)) {
           __threadfence();
