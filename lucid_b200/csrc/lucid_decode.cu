@@ -456,6 +456,19 @@ __device__ __forceinline__ float dot_chunks(const float* row, int ej, const floa
   return d;
 }
 
+// dot product of two lanes' 16-element registers, four partial sums
+__device__ __forceinline__ float dot16(const float (&a)[16], const float (&b)[16]) {
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    d0 = fmaf(a[i], b[i], d0);
+    d1 = fmaf(a[i + 1], b[i + 1], d1);
+    d2 = fmaf(a[i + 2], b[i + 2], d2);
+    d3 = fmaf(a[i + 3], b[i + 3], d3);
+  }
+  return (d0 + d1) + (d2 + d3);
+}
+
 template <int NU, int NA, int CB>
 __global__ void __launch_bounds__(kStepThreads, 2) lucid_decode_step_partial_kernel(const DecodeStepArgs a) {
   constexpr int NS = NU + NA;
@@ -516,6 +529,17 @@ __global__ void __launch_bounds__(kStepThreads, 2) lucid_decode_step_partial_ker
                              : 0.f;
   }
   __syncthreads();
+  // this lane's 16 elements of every slot's vector (normalised new key / scaled query),
+  // constant over the rows: held in registers instead of re-read from shared memory
+  // for every row (the ring's writes and reads already keep the shared-memory pipe
+  // busier than DRAM)
+  float kr[NS][16];
+#pragma unroll
+  for (int t = 0; t < NS; ++t)
+#pragma unroll
+    for (int q = 0; q < 16 / CE; ++q)
+#pragma unroll
+      for (int c = 0; c < CE; ++c) kr[t][q * CE + c] = kq[t][ej + 8 * CE * q + c];
   float acc[NS][16], m[NA], l[NA];
 #pragma unroll
   for (int t = 0; t < NS; ++t)
@@ -564,14 +588,14 @@ __global__ void __launch_bounds__(kStepThreads, 2) lucid_decode_step_partial_ker
     const float rs = rsqrtf(grp_sum(ss) * inv_d + a.eps);
 #pragma unroll
     for (int t = 0; t < NU; ++t) {
-      const float d = grp_sum(dot_chunks<CE>(kq[t], ej, k)) * rs;
+      const float d = grp_sum(dot16(kr[t], k)) * rs;
       const float e = valid ? exp2f(fmaf(d, c1, -c2)) : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[t][i] = fmaf(e, x[i], acc[t][i]);
     }
 #pragma unroll
     for (int t = 0; t < NA; ++t) {
-      const float z = grp_sum(dot_chunks<CE>(kq[NU + t], ej, k));
+      const float z = grp_sum(dot16(kr[NU + t], k));
       if (valid) {
         const float mn = fmaxf(m[t], z);
         const float al = exp2f(m[t] - mn), p = exp2f(z - mn);  // al = 0 while m is -inf
