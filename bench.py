@@ -718,16 +718,18 @@ def bench_prefill(args, torch, dist, dev, world, rank, local, barrier):
         lib.lucid_profile_read(ct.byref(tot), ct.byref(n))
         stage_ms[name], stage_n[name] = tot.value, n.value
     lib.lucid_profile_enable(0)
-    # algorithmic flops per layer at the model's head_dim (the kernels run 128 columns):
-    # causal attention 2 N^2 D per query head, the solve 2 N^2 D per kv head
+    # algorithmic flops per layer at the model's head_dim: causal attention 2 N^2 D per
+    # query head, the solve 2 N^2 D per kv head.  Executed: the attention forward runs
+    # its GEMMs over the head_dim rounded up to 16 columns, the solve over all 128
     alg = {"attn_fwd": 2.0 * N * N * hd * hq, "solve_fwd": 2.0 * N * N * hd * hk}
+    exec_d = {"attn_fwd": -(-hd // 16) * 16, "solve_fwd": 128}
     dom = max(alg, key=lambda n_: stage_ms[n_])
     per_launch_ms = stage_ms[dom] / max(1, stage_n[dom])
     ach = alg[dom] / (per_launch_ms * 1e-3) / 1e12
     roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": pk_burst, "unit": "TFLOP/s",
             "frac": ach / pk_burst, "peak_kind": f"{pk_kind} burst bf16",
-            "executed_tflops": ach * 128 / hd, "note": f"algorithmic flops at head_dim {hd}; the kernels "
-                                                          f"compute 128 zero-padded columns"}
+            "executed_tflops": ach * exec_d[dom] / hd,
+            "note": f"algorithmic flops at head_dim {hd}; the kernel computes {exec_d[dom]} zero-padded columns"}
     roof["traffic"] = None
 
     # ---- end to end: token ids from pinned host memory, last logits back to the host ----
