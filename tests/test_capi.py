@@ -136,3 +136,45 @@ def test_status_words_decode():
     msg = _lib.decode_status(1 | (0x12 << 8) | (4 << 20))
     assert msg.startswith("transposed-solve column pass: an mbarrier wait timed out")
     assert "0x90" in msg
+
+
+def test_solve_fwd_chain_schedule_workspace(lib, monkeypatch):
+    """The chain schedule's workspace (flags, 8 W slots of 64 KB, 3 E tiles of 32 KB per
+    row block, per head) is asked for only when the library would run that schedule:
+    few heads per GPU (here a CPU process, which models a 148-SM B200), or when forced."""
+    monkeypatch.delenv("LUCID_B200_SOLVE_SCHEDULE", raising=False)
+    N, D = 32768, 128
+    nb = N // 128
+
+    def extra(B, H):
+        return (-(-(B * H * nb * 4) // 256) * 256 + B * H * 8 * 128 * 128 * 4 + B * H * nb * 3 * 128 * 128 * 2)
+
+    base4 = lib.lucid_solve_fwd_workspace_bytes(1, 4, N, D)
+    assert lib.lucid_solve_fwd_fast_workspace_bytes(1, 4, N, D) == base4 + extra(1, 4)   # 4 heads: chains
+    base32 = lib.lucid_solve_fwd_workspace_bytes(1, 32, N, D)
+    assert lib.lucid_solve_fwd_fast_workspace_bytes(1, 32, N, D) == base32              # 32 heads: wavefront
+    # the layer forward sizes its workspace by the kv heads
+    assert lib.lucid_fused_fwd_workspace_bytes(1, 32, 4, N, D) == base4 + extra(1, 4)
+    monkeypatch.setenv("LUCID_B200_SOLVE_SCHEDULE", "wavefront")
+    assert lib.lucid_solve_fwd_fast_workspace_bytes(1, 4, N, D) == base4
+    monkeypatch.setenv("LUCID_B200_SOLVE_SCHEDULE", "chain")
+    assert lib.lucid_solve_fwd_fast_workspace_bytes(1, 32, N, D) == base32 + extra(1, 32)
+    # never more chains than the grid leaves room for workers
+    assert lib.lucid_solve_fwd_fast_workspace_bytes(1, 200, 1024, D) == lib.lucid_solve_fwd_workspace_bytes(
+        1, 200, 1024, D)
+
+
+def test_fused_fwd_argument_errors(lib):
+    """Shape and alignment errors come back before any CUDA call (no GPU needed)."""
+    ok = ctypes.c_void_p(4096)   # 16-byte aligned dummies, never dereferenced
+    bad = ctypes.c_void_p(4098)
+    args = lambda q, o: (1, 4, 2, 256, 128, 0.1, 1e-5, q, 0, 0, 128, ok, 0, 0, 128, ok, 0, 0, 128,
+                         ok, ok, ok, ok, ok, o, 0, 0, 128, ok, None, ok, 1 << 20, None)
+    assert lib.lucid_fused_fwd(*args(bad, ok)) == 2            # LUCID_ERR_ALIGN
+    assert lib.lucid_fused_fwd(*args(ok, bad)) == 2
+    a = list(args(ok, ok))
+    a[1], a[2] = 3, 2                                           # Hq not a multiple of Hkv
+    assert lib.lucid_fused_fwd(*a) == 1                         # LUCID_ERR_SHAPE
+    a = list(args(ok, ok))
+    a[4] = 129                                                  # head_dim above 128
+    assert lib.lucid_fused_fwd(*a) == 1
