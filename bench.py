@@ -995,18 +995,19 @@ def shard_inputs(torch, dev, B0, nb, kv0, nkv, G, N, D, qs, seed=1000):
 
 def pipelined_e2e(torch, dev, steps, h_in, make_outs, run):
     """End-to-end time per step through the public API with host buffers: every step
-    copies its inputs from pinned host memory (h_in) to the device, runs `run(*inputs)`
-    (returning the device results) and copies the results back into pinned host memory.
-    Copies in, compute and copies out run on three streams, double-buffered, so step i's
-    compute overlaps the copies of steps i - 1 and i + 1.  Returns ms per step (device
-    events from the first copy in to the last copy out)."""
+    copies its inputs from pinned host memory (h_in) to the device, computes, and copies
+    its results back into pinned host memory.  Copies in, compute and copies out run on
+    three streams, double-buffered, so step i's compute overlaps the copies of steps
+    i - 1 and i + 1.  `run(inputs, wait_in, emit)` does the compute: `wait_in(j)` makes it
+    wait for input j's copy only where it first needs it, and `emit(j, t)` queues the copy
+    of result j as soon as it is computed (every result of the step must be emitted).
+    Returns ms per step (device events from the first copy in to the last copy out)."""
     comp = torch.cuda.current_stream(dev)
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     d_in = [[torch.empty_like(t, device=dev) for t in h_in] for _ in range(2)]
     h_out = [make_outs() for _ in range(2)]
-    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_ready = [[torch.cuda.Event() for _ in h_in] for _ in range(2)]
     in_free = [torch.cuda.Event() for _ in range(2)]
-    out_ready = [torch.cuda.Event() for _ in range(2)]
     out_free = [torch.cuda.Event() for _ in range(2)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
@@ -1015,9 +1016,9 @@ def pipelined_e2e(torch, dev, steps, h_in, make_outs, run):
         with torch.cuda.stream(h2d):
             if i >= 2:
                 h2d.wait_event(in_free[s])       # step i - 2 is done with these buffers
-            for d, h in zip(d_in[s], h_in):
+            for j, (d, h) in enumerate(zip(d_in[s], h_in)):
                 d.copy_(h, non_blocking=True)
-            in_ready[s].record(h2d)
+                in_ready[s][j].record(h2d)
 
     torch.cuda.synchronize()
     t0.record(h2d)
@@ -1026,19 +1027,25 @@ def pipelined_e2e(torch, dev, steps, h_in, make_outs, run):
         s = i & 1
         if i + 1 < steps:
             copy_in(i + 1)
-        comp.wait_event(in_ready[s])
-        outs = run(*d_in[s])
-        in_free[s].record(comp)
-        out_ready[s].record(comp)
-        with torch.cuda.stream(d2h):
-            d2h.wait_event(out_ready[s])
-            if i >= 2:
-                d2h.wait_event(out_free[s])
-            for h, t in zip(h_out[s], outs):
+        first = [True]
+
+        def wait_in(j, s=s):
+            comp.wait_event(in_ready[s][j])
+
+        def emit(j, t, s=s, i=i, first=first):
+            ready = torch.cuda.Event()
+            ready.record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ready)
+                if i >= 2 and first[0]:
+                    d2h.wait_event(out_free[s])  # step i - 2's host buffers were read
+                first[0] = False
                 t.record_stream(d2h)
-                h.copy_(t.detach(), non_blocking=True)
-            out_free[s].record(d2h)
-        del outs
+                h_out[s][j].copy_(t.detach(), non_blocking=True)
+
+        run(d_in[s], wait_in, emit)
+        in_free[s].record(comp)
+        out_free[s].record(d2h)
     t1.record(d2h)
     torch.cuda.synchronize()
     return t0.elapsed_time(t1) / steps
@@ -1153,11 +1160,19 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
                     torch.empty(B, H, N, D, dtype=torch.bfloat16).pin_memory()] + \
                    [torch.empty(B, Hkv, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
-        def run(qq, kk, vv, dd):
-            qq, kk, vv = (t.detach().requires_grad_(True) for t in (qq, kk, vv))
+        def run(d, wait_in, emit):
+            # the forward starts once q, k, v are in; dO's copy overlaps it, and O's copy
+            # back overlaps the backward
+            for j in range(3):
+                wait_in(j)
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in d[:3])
             oo = lucid_attention(qq, kk, vv, s)
-            oo.backward(dd)
-            return oo, qq.grad, kk.grad, vv.grad
+            emit(0, oo)
+            wait_in(3)
+            oo.backward(d[3])
+            emit(1, qq.grad)
+            emit(2, kk.grad)
+            emit(3, vv.grad)
 
         pipelined_e2e(torch, dev, 2, h_in, make_outs, run)      # warm-up
         barrier()
@@ -1172,7 +1187,8 @@ def bench_lucid(args, torch, dist, dev, world, rank, local, barrier):
         nbytes = 2 * B * N * D * 2 * (H + Hkv)
         e2e = {"value": fl / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
-               "schedule": "copies in / compute / copies out on three streams, double-buffered"}
+               "schedule": "copies in / compute / copies out on three streams, double-buffered; the "
+                           "forward waits for q, k, v only and O is copied back during the backward"}
         del h_in
 
     # ---- the reference's own GPU path on the same inputs (config 2: it fits one GPU) ----
