@@ -72,6 +72,14 @@ bool tmap_strided(CUtensorMap* m, const void* p, int B, int H, int N, int64_t sb
   return make_tmap_bf16(m, p, kHeadDim, N, H, B, sn, sh, sb);
 }
 
+// The solve forward's chain-schedule workspace after the minimal one: chain flags, the
+// W ring, the E tiles.
+size_t chain_extra_bytes(int B, int H, int N) {
+  const size_t bh = (size_t)B * H, nb = nb_of(N);
+  return align256(bh * nb * sizeof(int)) + bh * kChainWRing * kBlock * kHeadDim * sizeof(float) +
+         bh * nb * kChainLook * (size_t)kTileBytes;
+}
+
 }  // namespace
 
 extern "C" {
@@ -109,13 +117,6 @@ size_t lucid_workspace_status_offset(void) { return 0; }
 size_t lucid_solve_fwd_workspace_bytes(int B, int H, int N, int D) {
   (void)D;
   return kStatusRegion + align256((size_t)B * H * nb_of(N) * sizeof(int));
-}
-
-// Chain schedule's workspace after the minimal one: chain flags, W ring, E tiles.
-static size_t chain_extra_bytes(int B, int H, int N) {
-  const size_t bh = (size_t)B * H, nb = nb_of(N);
-  return align256(bh * nb * sizeof(int)) + bh * kChainWRing * kBlock * kHeadDim * sizeof(float) +
-         bh * nb * kChainLook * (size_t)kTileBytes;
 }
 
 size_t lucid_solve_fwd_fast_workspace_bytes(int B, int H, int N, int D) {
