@@ -769,11 +769,17 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               for (int e = 0; e < 32; ++e)
                 if ((q * 32 + e) > r) sv[q][e] = -INFINITY;
           }
-          float mx = -INFINITY;
+          // four independent partial maxima, two scores per three-input max: 16-deep
+          // dependency chains instead of one of 128
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[q][e]);
+            for (int e = 0; e < 32; e += 2) {
+              float& mj = m4[((q * 32 + e) >> 1) & 3];
+              mj = fmax3(mj, sv[q][e], sv[q][e + 1]);
+            }
+          float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
           mx *= c1;
           // lazy rescale: keep the running reference unless it grows by > 8 (log2)
           bool need = false;
@@ -802,7 +808,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
           }
           l_run *= alpha;
           const float2 cc = make_float2(c1, c1), nm = make_float2(-m_run, -m_run);
-          float2 sum2 = make_float2(0.f, 0.f);
+          float2 s4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};
 #pragma unroll
           for (int q = 0; q < 4; ++q)
 #pragma unroll
@@ -811,9 +818,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 1)
               const float2 ex = make_float2(fast_exp2(a.x), fast_exp2(a.y));
               sv[q][e] = ex.x;
               sv[q][e + 1] = ex.y;
-              sum2 = add2(sum2, ex);
+              float2& sj = s4[((q * 32 + e) >> 1) & 3];
+              sj = add2(sj, ex);
             }
-          l_run += sum2.x + sum2.y;
+          const float2 s01 = add2(s4[0], s4[1]), s23 = add2(s4[2], s4[3]);
+          const float2 st = add2(s01, s23);
+          l_run += st.x + st.y;
         }
         // P back into tensor memory over S_k (this lane's own columns)
 #pragma unroll
