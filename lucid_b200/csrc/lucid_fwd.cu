@@ -244,6 +244,7 @@ __device__ __forceinline__ void solve_chain_cta(const CUtensorMap* tmU, const Fw
       bool ok = true;
       if (lane == 0) ok = wait_flag_geq(&cflag[i], 2, ab);
       if (!__all_sync(0xffffffffu, __shfl_sync(0xffffffffu, (int)ok, 0) != 0)) break;
+      __syncwarp();  // the lanes' loads below are ordered after lane 0's acquire of the flag
       const float4* ws = reinterpret_cast<const float4*>(wslots + (long long)(i % kChainWRing) * (kBlock * kHeadDim));
       float y[2][32];
 #pragma unroll
